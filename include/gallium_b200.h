@@ -1,0 +1,206 @@
+/*
+ * gallium_b200.h -- C ABI of the B200 (sm_100a) mixture-of-experts FFN block.
+ *
+ * This library replaces the MoE FFN blocks of rs-gallium:
+ *   - OssMoEFFN::forward  (crates/gallium-models/src/gpt_oss.rs:166-231, safetensors GPT-OSS)
+ *   - QMoEFFN::forward    (crates/gallium-models/src/gpt_oss_q.rs:165-269, GGUF GPT-OSS)
+ *   - QMoEFFN::forward    (crates/gallium-models/src/lfm2moe_q.rs:234-313, LFM2.5)
+ * whose common shape is `fn forward(&self, x: &Tensor) -> Result<Tensor>` with
+ * x of shape (batch, seq, hidden) (gallium-core FfnImpl::forward,
+ * crates/gallium-core/src/ffn.rs:175-181).  The weights those structs load in
+ * `load` (gpt_oss.rs:115-142, gpt_oss_q.rs:135-163, lfm2moe_q.rs:214-232) are
+ * handed to gb_moe_create as host buffers; the library copies and repacks them
+ * into its own device layout once.
+ *
+ * Conventions:
+ *   - Every function returns a gb_status; on failure gb_last_error() (per
+ *     thread) holds a message.  Nothing aborts and no kernel traps.
+ *   - Pointers named *_dev are device pointers on the handle's device; all
+ *     other buffer pointers are host pointers.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - A handle is not re-entrant: one forward at a time per handle, like the
+ *     reference, where the model is borrowed mutably per generation
+ *     (crates/gallium-agent/src/llm_candle.rs:199).
+ */
+#ifndef GALLIUM_B200_H
+#define GALLIUM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GB_ABI_VERSION 1
+
+typedef enum gb_status {
+  GB_OK = 0,
+  GB_ERR_INVALID_ARG = 1, /* null pointer, bad enum, top_k > experts, ...   */
+  GB_ERR_SHAPE = 2,       /* ragged quant blocks (quantized.rs:417-425), ... */
+  GB_ERR_CUDA = 3,        /* a CUDA runtime call failed                       */
+  GB_ERR_NCCL = 4,        /* an NCCL call failed (expert parallel only)       */
+  GB_ERR_TIMEOUT = 5,     /* a bounded device or host wait ran out            */
+  GB_ERR_UNSUPPORTED = 6, /* valid request this build does not implement      */
+  GB_ERR_NO_MEMORY = 7    /* host or device allocation failed                 */
+} gb_status;
+
+/* Router: GPT-OSS softmax over the top-k logits (gpt_oss.rs:172-182), or the
+ * LFM2.5 sigmoid router whose selection bias steers selection only
+ * (lfm2moe_q.rs:241-258). */
+typedef enum { GB_ROUTER_SOFTMAX_TOPK = 0, GB_ROUTER_SIGMOID_TOPK = 1 } gb_router_kind;
+
+/* Expert activation: GPT-OSS clamped SwiGLU (gpt_oss.rs:202-212) or plain
+ * SiLU-gated (lfm2moe_q.rs:287-290, ffn.rs:56-66 without clamp). */
+typedef enum { GB_ACT_GPTOSS_CLAMP = 0, GB_ACT_SILU = 1 } gb_act_kind;
+
+/* Expert weight format as the caller holds it. */
+typedef enum {
+  /* Safetensors MXFP4 (gpt_oss.rs:96-164): fused gate_up with interleaved
+   * rows (row 2i = gate_i, 2i+1 = up_i).  *_blocks [E, rows, K/32, 16] u8,
+   * byte j holding elements 2j (low nibble) and 2j+1 (high nibble);
+   * *_scales [E, rows, K/32] u8, value 2^(s-127), s == 0 -> 0. */
+  GB_FMT_MXFP4_SPLIT = 0,
+  /* GGUF type 39 (quantized.rs:361-449): separate gate/up [E, I, H] and down
+   * [E, H, I] tensors of 17-byte blocks [e8m0, 16 bytes]; low nibble of byte
+   * j -> element j, high nibble -> j+16. */
+  GB_FMT_MXFP4_GGUF = 1,
+  /* GGML Q4_K (144-byte, 256-element super-blocks), separate gate/up/down
+   * like GGUF (quantized.rs:139-178).  Not implemented yet: create returns
+   * GB_ERR_UNSUPPORTED. */
+  GB_FMT_Q4_K = 2
+} gb_weight_format;
+
+typedef enum { GB_DTYPE_F32 = 0, GB_DTYPE_BF16 = 1 } gb_dtype;
+
+/* Everything gb_moe_create needs.  Zero-initialise, set struct_size =
+ * sizeof(gb_moe_desc), then fill in.  Host pointers; the library copies what
+ * it needs and keeps no reference after create returns. */
+typedef struct gb_moe_desc {
+  uint32_t struct_size;
+  int32_t hidden;        /* H (multiple of 32; 256 for Q4_K)               */
+  int32_t inter;         /* I, expert intermediate size (same rule)         */
+  int32_t n_experts;     /* E (<= 256)                                       */
+  int32_t top_k;         /* k (1..8, <= E)                                   */
+  int32_t router_kind;   /* gb_router_kind                                   */
+  int32_t act_kind;      /* gb_act_kind                                      */
+  int32_t weight_format; /* gb_weight_format                                 */
+  float swiglu_limit;    /* GPT-OSS clamp limit (config swiglu_limit, 7.0)   */
+  int32_t device;        /* CUDA device ordinal                              */
+  int32_t max_tokens;    /* workspace is sized for this many tokens; a
+                            forward with more tokens grows it (synchronously) */
+
+  /* Router: weight [E, H], bias [E] (NULL = none), in router_dtype. */
+  const void* router_weight;
+  const void* router_bias;
+  int32_t router_dtype; /* gb_dtype */
+  /* Sigmoid router selection bias [E] f32 (exp_probs_b, lfm2moe_q.rs:216-221);
+   * NULL = zeros. */
+  const float* selection_bias;
+
+  /* GB_FMT_MXFP4_SPLIT */
+  const uint8_t* gate_up_blocks; /* [E, 2I, H/32, 16] */
+  const uint8_t* gate_up_scales; /* [E, 2I, H/32]     */
+  const uint8_t* down_blocks;    /* [E, H, I/32, 16]  */
+  const uint8_t* down_scales;    /* [E, H, I/32]      */
+
+  /* GB_FMT_MXFP4_GGUF / GB_FMT_Q4_K: raw block bytes */
+  const uint8_t* gate_raw; /* [E, I, H] */
+  const uint8_t* up_raw;   /* [E, I, H] */
+  const uint8_t* down_raw; /* [E, H, I] */
+
+  /* Biases in bias_dtype, NULL = none.  SPLIT: gate_up_bias [E, 2I]
+   * (interleaved like the rows).  GGUF: gate_bias, up_bias [E, I].
+   * down_bias [E, H] for both. */
+  const void* gate_up_bias;
+  const void* gate_bias;
+  const void* up_bias;
+  const void* down_bias;
+  int32_t bias_dtype; /* gb_dtype */
+
+  /* Expert parallelism (one process per GPU).  ep_size 1 = single GPU.
+   * For ep_size > 1 every rank passes the same full [E, ...] weight arrays
+   * (or at least valid pointers covering its own experts); rank r keeps
+   * experts [r*E/ep_size, (r+1)*E/ep_size).  nccl_id is the 128-byte
+   * ncclUniqueId from gb_nccl_unique_id() on rank 0, shared out of band. */
+  int32_t ep_rank;
+  int32_t ep_size;
+  const uint8_t* nccl_id;
+} gb_moe_desc;
+
+typedef struct gb_moe gb_moe;
+
+/* Information about a created handle. */
+typedef struct gb_moe_info {
+  uint32_t struct_size;
+  int32_t local_expert_begin, local_expert_end;
+  int64_t weight_bytes;    /* device bytes of the repacked expert weights  */
+  int64_t workspace_bytes; /* device bytes of the current workspace        */
+  int32_t workspace_tokens;
+  int32_t sm_count;
+  int64_t kernel_launches;  /* kernels this handle has launched so far */
+} gb_moe_info;
+
+/* Create: validates the descriptor, uploads and repacks the weights.
+ * Replaces OssMoEFFN::load (gpt_oss.rs:115-142), QMoEFFN::load
+ * (gpt_oss_q.rs:135-163) and QMoEFFN::load (lfm2moe_q.rs:214-232). */
+int gb_moe_create(const gb_moe_desc* desc, gb_moe** out);
+
+/* Forward: x_dev [T, H] f32 row-major -> out_dev [T, H] f32.  Asynchronous on
+ * `stream`.  Replaces the forward methods listed at the top of this file;
+ * the caller flattens (batch, seq) into T and adds the residual itself, as
+ * gpt_oss.rs:385 and gpt_oss_q.rs:296 do.  T == 0 is a no-op. */
+int gb_moe_forward(gb_moe* m, const float* x_dev, int64_t T, float* out_dev, void* stream);
+
+/* Same with host buffers: copies x in, runs, copies out, and synchronises
+ * the stream before returning (the path a candle CPU tensor takes). */
+int gb_moe_forward_host(gb_moe* m, const float* x_host, int64_t T, float* out_host,
+                        void* stream);
+
+/* Routing only, for parity checks (gpt_oss.rs:172-182 / lfm2moe_q.rs:241-264
+ * and the grouping of gpt_oss_q.rs:175-192).  Device outputs, any may be NULL:
+ *   idx_dev [T, k] i32, expert per rank, ranks in descending router order;
+ *   w_dev [T, k] f32, combine weights;
+ *   counts_dev [E] i32, offsets_dev [E+1] i32 (exclusive prefix);
+ *   perm_dev [T*k] i32, entry t*k+r at each sorted position (expert
+ *   ascending, then token ascending).
+ * Synchronises the stream. */
+int gb_moe_route(gb_moe* m, const float* x_dev, int64_t T, int32_t* idx_dev, float* w_dev,
+                 int32_t* counts_dev, int32_t* offsets_dev, int32_t* perm_dev, void* stream);
+
+/* Dequantise one local expert's matrix from the repacked device layout to
+ * f32, for parity checks of the repack and the in-kernel decoder.
+ * which: 0 = gate (gate rows of the fused gate_up), 1 = up, 2 = down.
+ * out_dev [rows, K] f32 (gate/up: [I, H]; down: [H, I]). Synchronises. */
+int gb_moe_dequant_expert(gb_moe* m, int32_t which, int32_t expert, float* out_dev,
+                          void* stream);
+
+int gb_moe_get_info(const gb_moe* m, gb_moe_info* info);
+
+/* Stage timing for profiling (no counterpart in the reference, whose timing
+ * is per generated token, crates/gallium-agent/src/llm_candle.rs:302-345).
+ * When enabled, each forward records a CUDA event at every stage boundary on
+ * its stream.  gb_moe_stage_times synchronises on the last forward's final
+ * event and writes up to `capacity` per-stage durations in milliseconds
+ * (stage names from gb_moe_stage_name) and the stage count. */
+int gb_moe_set_profiling(gb_moe* m, int enable);
+int gb_moe_stage_times(gb_moe* m, float* ms_out, int32_t capacity, int32_t* n_stages);
+const char* gb_moe_stage_name(int32_t stage);
+
+/* Releases device memory, streams and (expert parallel) the communicator. */
+int gb_moe_destroy(gb_moe* m);
+
+/* Expert parallel: a fresh 128-byte ncclUniqueId (rank 0 calls this and
+ * shares the bytes with the other ranks). */
+int gb_nccl_unique_id(uint8_t out[128]);
+
+/* Last error message of the calling thread ("" if none). */
+const char* gb_last_error(void);
+
+/* ABI version this library was built with (GB_ABI_VERSION). */
+int gb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GALLIUM_B200_H */

@@ -1,0 +1,570 @@
+// moe_api.cu -- the C ABI (include/gallium_b200.h): handle lifetime, weight
+// upload and repack, workspace, and the forward pipeline
+//   router + top-k -> grouping -> expert products -> combine.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <new>
+#include <vector>
+
+#include "moe_internal.h"
+
+namespace {
+
+thread_local char g_err[1024] = "";
+
+int set_err(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+  return set_err(GB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define GB_CUDA(call, what)                    \
+  do {                                         \
+    cudaError_t _e = (call);                   \
+    if (_e != cudaSuccess) return cuda_err(_e, what); \
+  } while (0)
+
+// Makes `dev` current for the scope and restores the caller's device.
+struct DeviceScope {
+  int prev = -1;
+  bool ok = false;
+  explicit DeviceScope(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceScope() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+float bf16_to_f32(uint16_t b) {
+  uint32_t bits = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+// Widen a [n] vector of f32 or bf16 host values to f32.
+std::vector<float> widen(const void* src, int64_t n, int dtype) {
+  std::vector<float> out((size_t)n);
+  if (dtype == GB_DTYPE_BF16) {
+    const uint16_t* s = static_cast<const uint16_t*>(src);
+    for (int64_t i = 0; i < n; ++i) out[(size_t)i] = bf16_to_f32(s[i]);
+  } else {
+    memcpy(out.data(), src, sizeof(float) * (size_t)n);
+  }
+  return out;
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+int validate(const gb_moe_desc* d) {
+  if (!d) return set_err(GB_ERR_INVALID_ARG, "descriptor is null");
+  if (d->struct_size < sizeof(gb_moe_desc))
+    return set_err(GB_ERR_INVALID_ARG, "descriptor struct_size %u < %zu (header mismatch)",
+                   d->struct_size, sizeof(gb_moe_desc));
+  if (d->hidden <= 0 || d->inter <= 0 || d->n_experts <= 0 || d->top_k <= 0)
+    return set_err(GB_ERR_INVALID_ARG, "non-positive shape H=%d I=%d E=%d k=%d", d->hidden,
+                   d->inter, d->n_experts, d->top_k);
+  if (d->n_experts > 256)
+    return set_err(GB_ERR_UNSUPPORTED, "n_experts %d > 256", d->n_experts);
+  if (d->top_k > d->n_experts || d->top_k > 8)
+    return set_err(GB_ERR_INVALID_ARG, "top_k %d must be <= n_experts (%d) and <= 8", d->top_k,
+                   d->n_experts);
+  if (d->router_kind != GB_ROUTER_SOFTMAX_TOPK && d->router_kind != GB_ROUTER_SIGMOID_TOPK)
+    return set_err(GB_ERR_INVALID_ARG, "unknown router_kind %d", d->router_kind);
+  if (d->act_kind != GB_ACT_GPTOSS_CLAMP && d->act_kind != GB_ACT_SILU)
+    return set_err(GB_ERR_INVALID_ARG, "unknown act_kind %d", d->act_kind);
+  if (d->router_dtype != GB_DTYPE_F32 && d->router_dtype != GB_DTYPE_BF16)
+    return set_err(GB_ERR_INVALID_ARG, "unknown router_dtype %d", d->router_dtype);
+  if (d->bias_dtype != GB_DTYPE_F32 && d->bias_dtype != GB_DTYPE_BF16)
+    return set_err(GB_ERR_INVALID_ARG, "unknown bias_dtype %d", d->bias_dtype);
+  if (!d->router_weight) return set_err(GB_ERR_INVALID_ARG, "router_weight is null");
+  switch (d->weight_format) {
+    case GB_FMT_MXFP4_SPLIT:
+      if (!d->gate_up_blocks || !d->gate_up_scales || !d->down_blocks || !d->down_scales)
+        return set_err(GB_ERR_INVALID_ARG, "MXFP4_SPLIT needs gate_up/down blocks and scales");
+      break;
+    case GB_FMT_MXFP4_GGUF:
+      if (!d->gate_raw || !d->up_raw || !d->down_raw)
+        return set_err(GB_ERR_INVALID_ARG, "MXFP4_GGUF needs gate_raw, up_raw and down_raw");
+      break;
+    case GB_FMT_Q4_K:
+      return set_err(GB_ERR_UNSUPPORTED, "Q4_K experts are not implemented in this build");
+    default:
+      return set_err(GB_ERR_INVALID_ARG, "unknown weight_format %d", d->weight_format);
+  }
+  // quantized.rs:417-425: a ragged expert is an error naming the count and block size.
+  const int64_t elems_gu = (int64_t)d->hidden, elems_dn = (int64_t)d->inter;
+  if (elems_gu % 32 != 0 || elems_dn % 32 != 0)
+    return set_err(GB_ERR_SHAPE,
+                   "MXFP4 expert rows of %lld (hidden) / %lld (inter) elements are not a whole "
+                   "number of 32-element blocks",
+                   (long long)elems_gu, (long long)elems_dn);
+  if (d->hidden / 32 > 128 || d->inter / 32 > 128)
+    return set_err(GB_ERR_UNSUPPORTED, "hidden/inter above 4096 are not supported");
+  if (d->ep_size < 0 || (d->ep_size > 1 && (d->ep_rank < 0 || d->ep_rank >= d->ep_size)))
+    return set_err(GB_ERR_INVALID_ARG, "bad ep_rank %d / ep_size %d", d->ep_rank, d->ep_size);
+  if (d->ep_size > 1) {
+    if (d->n_experts % d->ep_size != 0)
+      return set_err(GB_ERR_INVALID_ARG, "n_experts %d not divisible by ep_size %d", d->n_experts,
+                     d->ep_size);
+    return set_err(GB_ERR_UNSUPPORTED, "expert parallelism is not implemented in this build");
+  }
+  if (d->max_tokens < 0) return set_err(GB_ERR_INVALID_ARG, "max_tokens %d < 0", d->max_tokens);
+  return GB_OK;
+}
+
+void free_ws(gb::Workspace& ws) {
+  if (ws.base) cudaFree(ws.base);
+  ws = gb::Workspace{};
+}
+
+// Carve the workspace for T tokens out of one allocation (256-byte aligned pieces).
+int alloc_ws(gb::Moe& m, int64_t T) {
+  const gb_moe_desc& d = m.desc;
+  const int64_t E = d.n_experts, K = d.top_k, H = d.hidden, I = d.inter;
+  T = std::max<int64_t>(T, 1);
+  struct Piece {
+    void** ptr;
+    size_t bytes;
+  };
+  gb::Workspace ws;
+  ws.tokens = T;
+  Piece pieces[] = {
+      {(void**)&ws.logits, sizeof(float) * (size_t)(T * E)},
+      {(void**)&ws.tickets, sizeof(unsigned) * (size_t)T},
+      {(void**)&ws.idx, sizeof(int32_t) * (size_t)(T * K)},
+      {(void**)&ws.wts, sizeof(float) * (size_t)(T * K)},
+      {(void**)&ws.counts, sizeof(int32_t) * (size_t)E},
+      {(void**)&ws.offsets, sizeof(int32_t) * (size_t)(E + 1)},
+      {(void**)&ws.active, sizeof(int32_t) * (size_t)E},
+      {(void**)&ws.meta, sizeof(int32_t) * 4},
+      {(void**)&ws.perm, sizeof(int32_t) * (size_t)(T * K)},
+      {(void**)&ws.inv, sizeof(int32_t) * (size_t)(T * K)},
+      {(void**)&ws.h, sizeof(float) * (size_t)(T * K * I)},
+      {(void**)&ws.y, sizeof(float) * (size_t)(T * K * H)},
+      {(void**)&ws.x_stage, sizeof(float) * (size_t)(T * H)},
+      {(void**)&ws.out_stage, sizeof(float) * (size_t)(T * H)},
+  };
+  size_t total = 0;
+  for (auto& p : pieces) total += (size_t)round_up((int64_t)p.bytes, 256);
+  void* base = nullptr;
+  cudaError_t e = cudaMalloc(&base, total);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(GB_ERR_NO_MEMORY, "workspace of %zu bytes for %lld tokens: %s", total,
+                   (long long)T, cudaGetErrorString(e));
+  }
+  e = cudaMemset(base, 0, total);
+  if (e != cudaSuccess) {
+    cudaFree(base);
+    return cuda_err(e, "workspace memset");
+  }
+  size_t off = 0;
+  for (auto& p : pieces) {
+    *p.ptr = static_cast<char*>(base) + off;
+    off += (size_t)round_up((int64_t)p.bytes, 256);
+  }
+  ws.base = base;
+  ws.bytes = total;
+  free_ws(m.ws);
+  m.ws = ws;
+  return GB_OK;
+}
+
+int ensure_ws(gb::Moe& m, int64_t T, cudaStream_t st) {
+  if (T <= m.ws.tokens) return GB_OK;
+  GB_CUDA(cudaStreamSynchronize(st), "synchronise before workspace growth");
+  return alloc_ws(m, T);
+}
+
+template <typename Tp>
+int dev_alloc(Tp** p, size_t bytes, const char* what) {
+  cudaError_t e = cudaMalloc((void**)p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(GB_ERR_NO_MEMORY, "cudaMalloc %s (%zu bytes): %s", what, bytes,
+                   cudaGetErrorString(e));
+  }
+  return GB_OK;
+}
+
+// Frees the device memory of a handle (the handle object itself stays).
+void release_moe(gb::Moe& m) {
+  DeviceScope ds(m.device);
+  for (auto& e : m.ev)
+    if (e) cudaEventDestroy(e);
+  cudaFree(m.router_w);
+  cudaFree(m.router_b);
+  cudaFree(m.sel_bias);
+  cudaFree(m.w.gu_blocks);
+  cudaFree(m.w.gu_scales);
+  cudaFree(m.w.dn_blocks);
+  cudaFree(m.w.dn_scales);
+  cudaFree(m.w.gu_bias);
+  cudaFree(m.w.dn_bias);
+  free_ws(m.ws);
+  m = gb::Moe{};
+}
+
+int upload_weights(gb::Moe& m) {
+  const gb_moe_desc& d = m.desc;
+  const int64_t H = d.hidden, I = d.inter, E = d.n_experts;
+  const int64_t nloc = m.e_end - m.e_begin;
+  const int64_t nbh = H / 32, nbi = I / 32;
+  m.w.sp_h = (int)round_up(nbh, 16);
+  m.w.sp_i = (int)round_up(nbi, 16);
+  m.w.zero_scale = d.weight_format == GB_FMT_MXFP4_GGUF ? 0x1p-127f : 0.0f;
+
+  const size_t gu_blocks = (size_t)(nloc * 2 * I * nbh * 16);
+  const size_t gu_scales = (size_t)(nloc * 2 * I * m.w.sp_h);
+  const size_t dn_blocks = (size_t)(nloc * H * nbi * 16);
+  const size_t dn_scales = (size_t)(nloc * H * m.w.sp_i);
+  int rc;
+  if ((rc = dev_alloc(&m.w.gu_blocks, gu_blocks, "gate_up blocks"))) return rc;
+  if ((rc = dev_alloc(&m.w.gu_scales, gu_scales, "gate_up scales"))) return rc;
+  if ((rc = dev_alloc(&m.w.dn_blocks, dn_blocks, "down blocks"))) return rc;
+  if ((rc = dev_alloc(&m.w.dn_scales, dn_scales, "down scales"))) return rc;
+  GB_CUDA(cudaMemset(m.w.gu_scales, 0, gu_scales), "memset scales");
+  GB_CUDA(cudaMemset(m.w.dn_scales, 0, dn_scales), "memset scales");
+  m.weight_bytes = (int64_t)(gu_blocks + gu_scales + dn_blocks + dn_scales);
+
+  if (d.weight_format == GB_FMT_MXFP4_SPLIT) {
+    const int64_t e0 = m.e_begin;
+    GB_CUDA(cudaMemcpy(m.w.gu_blocks, d.gate_up_blocks + e0 * 2 * I * nbh * 16, gu_blocks,
+                       cudaMemcpyHostToDevice),
+            "upload gate_up blocks");
+    GB_CUDA(cudaMemcpy2D(m.w.gu_scales, (size_t)m.w.sp_h, d.gate_up_scales + e0 * 2 * I * nbh,
+                         (size_t)nbh, (size_t)nbh, (size_t)(nloc * 2 * I), cudaMemcpyHostToDevice),
+            "upload gate_up scales");
+    GB_CUDA(cudaMemcpy(m.w.dn_blocks, d.down_blocks + e0 * H * nbi * 16, dn_blocks,
+                       cudaMemcpyHostToDevice),
+            "upload down blocks");
+    GB_CUDA(cudaMemcpy2D(m.w.dn_scales, (size_t)m.w.sp_i, d.down_scales + e0 * H * nbi,
+                         (size_t)nbi, (size_t)nbi, (size_t)(nloc * H), cudaMemcpyHostToDevice),
+            "upload down scales");
+  } else {
+    // GGUF: per expert, upload the raw 17-byte blocks and convert on the device.
+    const size_t raw_gate = (size_t)(I * nbh * 17), raw_down = (size_t)(H * nbi * 17);
+    uint8_t* tmp = nullptr;
+    if ((rc = dev_alloc(&tmp, std::max(raw_gate, raw_down), "GGUF staging"))) return rc;
+    for (int64_t le = 0; le < nloc && rc == GB_OK; ++le) {
+      const int64_t e = m.e_begin + le;
+      for (int which = 0; which < 3 && rc == GB_OK; ++which) {
+        const uint8_t* src = which == 0 ? d.gate_raw : which == 1 ? d.up_raw : d.down_raw;
+        const size_t bytes = which == 2 ? raw_down : raw_gate;
+        cudaError_t ce = cudaMemcpy(tmp, src + (size_t)e * bytes, bytes, cudaMemcpyHostToDevice);
+        if (ce == cudaSuccess) {
+          if (which < 2) {
+            // gate row i -> fused row 2i, up row i -> 2i+1
+            ce = gb::launch_gguf_to_split(
+                tmp, I, (int)H, m.w.gu_blocks + ((le * 2 * I + which) * nbh) * 16, 2 * nbh,
+                m.w.gu_scales + (le * 2 * I + which) * m.w.sp_h, 2 * (int64_t)m.w.sp_h, 0);
+          } else {
+            ce = gb::launch_gguf_to_split(tmp, H, (int)I, m.w.dn_blocks + (le * H * nbi) * 16, nbi,
+                                          m.w.dn_scales + le * H * m.w.sp_i, m.w.sp_i, 0);
+          }
+        }
+        if (ce == cudaSuccess) ce = cudaDeviceSynchronize();
+        if (ce != cudaSuccess) rc = cuda_err(ce, "GGUF expert upload");
+      }
+    }
+    cudaFree(tmp);
+    if (rc) return rc;
+  }
+
+  // Biases -> f32, fused gate_up order.
+  if (d.weight_format == GB_FMT_MXFP4_SPLIT ? d.gate_up_bias != nullptr
+                                            : (d.gate_bias != nullptr || d.up_bias != nullptr)) {
+    std::vector<float> gub((size_t)(nloc * 2 * I), 0.0f);
+    if (d.weight_format == GB_FMT_MXFP4_SPLIT) {
+      const size_t esz = d.bias_dtype == GB_DTYPE_BF16 ? 2 : 4;
+      gub = widen(static_cast<const char*>(d.gate_up_bias) + (size_t)(m.e_begin * 2 * I) * esz,
+                  nloc * 2 * I, d.bias_dtype);
+    } else {
+      const size_t esz = d.bias_dtype == GB_DTYPE_BF16 ? 2 : 4;
+      std::vector<float> g, u;
+      if (d.gate_bias)
+        g = widen(static_cast<const char*>(d.gate_bias) + (size_t)(m.e_begin * I) * esz, nloc * I,
+                  d.bias_dtype);
+      if (d.up_bias)
+        u = widen(static_cast<const char*>(d.up_bias) + (size_t)(m.e_begin * I) * esz, nloc * I,
+                  d.bias_dtype);
+      for (int64_t le = 0; le < nloc; ++le)
+        for (int64_t i = 0; i < I; ++i) {
+          gub[(size_t)(le * 2 * I + 2 * i)] = g.empty() ? 0.0f : g[(size_t)(le * I + i)];
+          gub[(size_t)(le * 2 * I + 2 * i + 1)] = u.empty() ? 0.0f : u[(size_t)(le * I + i)];
+        }
+    }
+    if ((rc = dev_alloc(&m.w.gu_bias, gub.size() * 4, "gate_up bias"))) return rc;
+    GB_CUDA(cudaMemcpy(m.w.gu_bias, gub.data(), gub.size() * 4, cudaMemcpyHostToDevice),
+            "upload gate_up bias");
+  }
+  if (d.down_bias) {
+    const size_t esz = d.bias_dtype == GB_DTYPE_BF16 ? 2 : 4;
+    std::vector<float> db = widen(
+        static_cast<const char*>(d.down_bias) + (size_t)(m.e_begin * H) * esz, nloc * H, d.bias_dtype);
+    if ((rc = dev_alloc(&m.w.dn_bias, db.size() * 4, "down bias"))) return rc;
+    GB_CUDA(cudaMemcpy(m.w.dn_bias, db.data(), db.size() * 4, cudaMemcpyHostToDevice),
+            "upload down bias");
+  }
+
+  // Router (replicated).
+  std::vector<float> rw = widen(d.router_weight, E * H, d.router_dtype);
+  if ((rc = dev_alloc(&m.router_w, rw.size() * 4, "router weight"))) return rc;
+  GB_CUDA(cudaMemcpy(m.router_w, rw.data(), rw.size() * 4, cudaMemcpyHostToDevice),
+          "upload router weight");
+  if (d.router_bias) {
+    std::vector<float> rb = widen(d.router_bias, E, d.router_dtype);
+    if ((rc = dev_alloc(&m.router_b, rb.size() * 4, "router bias"))) return rc;
+    GB_CUDA(cudaMemcpy(m.router_b, rb.data(), rb.size() * 4, cudaMemcpyHostToDevice),
+            "upload router bias");
+  }
+  if (d.selection_bias) {
+    if ((rc = dev_alloc(&m.sel_bias, (size_t)E * 4, "selection bias"))) return rc;
+    GB_CUDA(cudaMemcpy(m.sel_bias, d.selection_bias, (size_t)E * 4, cudaMemcpyHostToDevice),
+            "upload selection bias");
+  }
+  return GB_OK;
+}
+
+// Stage boundary: record event i when profiling.
+int mark(gb::Moe& m, int i, cudaStream_t st) {
+  if (m.profiling) GB_CUDA(cudaEventRecord(m.ev[i], st), "record stage event");
+  return GB_OK;
+}
+
+int run_route(gb::Moe& m, const float* x, int64_t T, cudaStream_t st) {
+  int rc;
+  if ((rc = mark(m, 0, st))) return rc;
+  GB_CUDA(gb::launch_router_topk(m, x, T, m.ws.idx, m.ws.wts, st), "router kernel launch");
+  if ((rc = mark(m, 1, st))) return rc;
+  GB_CUDA(gb::launch_permute(m, m.ws.idx, T, m.ws, st), "permute kernel launch");
+  m.launches += 2;
+  return mark(m, 2, st);
+}
+
+int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
+  int rc = run_route(m, x, T, st);
+  if (rc) return rc;
+  GB_CUDA(gb::launch_gate_up(m, x, T, m.ws, st), "gate_up kernel launch");
+  if ((rc = mark(m, 3, st))) return rc;
+  GB_CUDA(gb::launch_down(m, T, m.ws, st), "down kernel launch");
+  if ((rc = mark(m, 4, st))) return rc;
+  GB_CUDA(gb::launch_combine(m, T, m.ws, out, st), "combine kernel launch");
+  m.launches += 3;
+  if ((rc = mark(m, 5, st))) return rc;
+  m.profiled_once = m.profiling;
+  return GB_OK;
+}
+
+int check_handle(gb_moe* h) {
+  if (!h) return set_err(GB_ERR_INVALID_ARG, "handle is null");
+  return GB_OK;
+}
+
+}  // namespace
+
+struct gb_moe {
+  gb::Moe m;
+};
+
+extern "C" {
+
+int gb_abi_version(void) { return GB_ABI_VERSION; }
+
+const char* gb_last_error(void) { return g_err; }
+
+int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
+  g_err[0] = 0;
+  if (!out) return set_err(GB_ERR_INVALID_ARG, "out is null");
+  *out = nullptr;
+  int rc = validate(desc);
+  if (rc) return rc;
+  int ndev = 0;
+  GB_CUDA(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (desc->device < 0 || desc->device >= ndev)
+    return set_err(GB_ERR_INVALID_ARG, "device %d does not exist (%d visible)", desc->device, ndev);
+  DeviceScope ds(desc->device);
+  if (!ds.ok) return set_err(GB_ERR_CUDA, "cannot make device %d current", desc->device);
+  gb_moe* h = new (std::nothrow) gb_moe();
+  if (!h) return set_err(GB_ERR_NO_MEMORY, "host allocation failed");
+  gb::Moe& m = h->m;
+  m.desc = *desc;
+  m.device = desc->device;
+  m.ep_size = std::max(1, desc->ep_size);
+  m.ep_rank = m.ep_size > 1 ? desc->ep_rank : 0;
+  const int per = desc->n_experts / m.ep_size;
+  m.e_begin = m.ep_rank * per;
+  m.e_end = m.e_begin + per;
+  cudaError_t ce = cudaDeviceGetAttribute(&m.sm_count, cudaDevAttrMultiProcessorCount, m.device);
+  if (ce != cudaSuccess) {
+    delete h;
+    return cuda_err(ce, "query SM count");
+  }
+  rc = upload_weights(m);
+  if (!rc) rc = alloc_ws(m, std::max(1, desc->max_tokens));
+  if (rc) {
+    release_moe(h->m);
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return GB_OK;
+}
+
+int gb_moe_forward(gb_moe* h, const float* x_dev, int64_t T, float* out_dev, void* stream) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  if (T < 0) return set_err(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
+  if (T == 0) return GB_OK;
+  if (!x_dev || !out_dev) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
+  if (T > (int64_t)1 << 24) return set_err(GB_ERR_UNSUPPORTED, "T = %lld too large", (long long)T);
+  gb::Moe& m = h->m;
+  DeviceScope ds(m.device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = ensure_ws(m, T, st))) return rc;
+  return run_forward(m, x_dev, T, out_dev, st);
+}
+
+int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_host,
+                        void* stream) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  if (T < 0) return set_err(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
+  if (T == 0) return GB_OK;
+  if (!x_host || !out_host) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
+  gb::Moe& m = h->m;
+  DeviceScope ds(m.device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = ensure_ws(m, T, st))) return rc;
+  const size_t bytes = sizeof(float) * (size_t)(T * m.desc.hidden);
+  GB_CUDA(cudaMemcpyAsync(m.ws.x_stage, x_host, bytes, cudaMemcpyHostToDevice, st), "copy x in");
+  if ((rc = run_forward(m, m.ws.x_stage, T, m.ws.out_stage, st))) return rc;
+  GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
+          "copy out");
+  GB_CUDA(cudaStreamSynchronize(st), "synchronise forward");
+  return GB_OK;
+}
+
+int gb_moe_route(gb_moe* h, const float* x_dev, int64_t T, int32_t* idx_dev, float* w_dev,
+                 int32_t* counts_dev, int32_t* offsets_dev, int32_t* perm_dev, void* stream) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  if (T < 0) return set_err(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
+  if (T > 0 && !x_dev) return set_err(GB_ERR_INVALID_ARG, "x is null");
+  gb::Moe& m = h->m;
+  DeviceScope ds(m.device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if ((rc = ensure_ws(m, T, st))) return rc;
+  const int64_t E = m.desc.n_experts, K = m.desc.top_k;
+  if (T > 0 && (rc = run_route(m, x_dev, T, st))) return rc;
+  if (T == 0) {
+    GB_CUDA(cudaMemsetAsync(m.ws.counts, 0, sizeof(int32_t) * E, st), "clear counts");
+    GB_CUDA(cudaMemsetAsync(m.ws.offsets, 0, sizeof(int32_t) * (E + 1), st), "clear offsets");
+  }
+  auto cp = [&](void* dst, const void* src, size_t bytes) -> int {
+    if (!dst || bytes == 0) return GB_OK;
+    GB_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, st), "copy routing out");
+    return GB_OK;
+  };
+  if ((rc = cp(idx_dev, m.ws.idx, sizeof(int32_t) * (size_t)(T * K)))) return rc;
+  if ((rc = cp(w_dev, m.ws.wts, sizeof(float) * (size_t)(T * K)))) return rc;
+  if ((rc = cp(counts_dev, m.ws.counts, sizeof(int32_t) * (size_t)E))) return rc;
+  if ((rc = cp(offsets_dev, m.ws.offsets, sizeof(int32_t) * (size_t)(E + 1)))) return rc;
+  if ((rc = cp(perm_dev, m.ws.perm, sizeof(int32_t) * (size_t)(T * K)))) return rc;
+  GB_CUDA(cudaStreamSynchronize(st), "synchronise route");
+  return GB_OK;
+}
+
+int gb_moe_dequant_expert(gb_moe* h, int32_t which, int32_t expert, float* out_dev,
+                          void* stream) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  gb::Moe& m = h->m;
+  if (which < 0 || which > 2) return set_err(GB_ERR_INVALID_ARG, "which = %d not in 0..2", which);
+  if (expert < m.e_begin || expert >= m.e_end)
+    return set_err(GB_ERR_INVALID_ARG, "expert %d is not local ([%d, %d))", expert, m.e_begin,
+                   m.e_end);
+  if (!out_dev) return set_err(GB_ERR_INVALID_ARG, "out is null");
+  DeviceScope ds(m.device);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GB_CUDA(gb::launch_dequant_expert(m, which, expert - m.e_begin, out_dev, st), "dequant launch");
+  GB_CUDA(cudaStreamSynchronize(st), "synchronise dequant");
+  return GB_OK;
+}
+
+int gb_moe_get_info(const gb_moe* h, gb_moe_info* info) {
+  if (!h || !info) return set_err(GB_ERR_INVALID_ARG, "null argument");
+  if (info->struct_size < sizeof(gb_moe_info))
+    return set_err(GB_ERR_INVALID_ARG, "info struct_size %u < %zu", info->struct_size,
+                   sizeof(gb_moe_info));
+  const gb::Moe& m = h->m;
+  info->local_expert_begin = m.e_begin;
+  info->local_expert_end = m.e_end;
+  info->weight_bytes = m.weight_bytes;
+  info->workspace_bytes = (int64_t)m.ws.bytes;
+  info->workspace_tokens = (int32_t)m.ws.tokens;
+  info->sm_count = m.sm_count;
+  info->kernel_launches = m.launches;
+  return GB_OK;
+}
+
+static const char* kStageNames[gb::Moe::kStages] = {"router", "permute", "gate_up", "down",
+                                                     "combine"};
+
+const char* gb_moe_stage_name(int32_t stage) {
+  return stage >= 0 && stage < gb::Moe::kStages ? kStageNames[stage] : "";
+}
+
+int gb_moe_set_profiling(gb_moe* h, int enable) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  gb::Moe& m = h->m;
+  DeviceScope ds(m.device);
+  if (enable && !m.ev[0])
+    for (auto& e : m.ev) GB_CUDA(cudaEventCreate(&e), "create stage event");
+  m.profiling = enable != 0;
+  m.profiled_once = false;
+  return GB_OK;
+}
+
+int gb_moe_stage_times(gb_moe* h, float* ms_out, int32_t capacity, int32_t* n_stages) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  gb::Moe& m = h->m;
+  if (!m.profiled_once)
+    return set_err(GB_ERR_INVALID_ARG, "no profiled forward yet (call gb_moe_set_profiling)");
+  DeviceScope ds(m.device);
+  GB_CUDA(cudaEventSynchronize(m.ev[gb::Moe::kStages]), "wait for the profiled forward");
+  const int n = std::min<int>(gb::Moe::kStages, std::max<int32_t>(capacity, 0));
+  for (int i = 0; i < n && ms_out; ++i)
+    GB_CUDA(cudaEventElapsedTime(&ms_out[i], m.ev[i], m.ev[i + 1]), "stage elapsed time");
+  if (n_stages) *n_stages = gb::Moe::kStages;
+  return GB_OK;
+}
+
+int gb_moe_destroy(gb_moe* h) {
+  if (!h) return GB_OK;
+  release_moe(h->m);
+  delete h;
+  return GB_OK;
+}
+
+int gb_nccl_unique_id(uint8_t out[128]) {
+  (void)out;
+  return set_err(GB_ERR_UNSUPPORTED, "expert parallelism is not implemented in this build");
+}
+
+}  // extern "C"

@@ -1,0 +1,95 @@
+// moe_internal.h -- state of a gb_moe handle and the kernel launchers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/gallium_b200.h"
+
+namespace gb {
+
+// Repacked expert weights of the local experts (device memory).
+//
+// Layout (MXFP4, one layout for both caller formats):
+//   gu_blocks [E_loc][2I][H/32][16]  fused gate_up, row 2i = gate_i, 2i+1 = up_i;
+//                                    byte j of a block = elements 2j (low
+//                                    nibble) and 2j+1 (high nibble)
+//   gu_scales [E_loc][2I][SP_H]      E8M0 bytes, rows padded to SP_H =
+//                                    roundup(H/32, 16) so a row's scales start
+//                                    16-byte aligned
+//   dn_blocks [E_loc][H][I/32][16], dn_scales [E_loc][H][SP_I]
+//   gu_bias [E_loc][2I], dn_bias [E_loc][H] f32 (or null)
+// zero_scale is the value of an E8M0 byte 0: 0 for safetensors, 2^-127 for
+// GGUF (quantized.rs:375-383).
+struct ExpertWeights {
+  uint8_t* gu_blocks = nullptr;
+  uint8_t* gu_scales = nullptr;
+  uint8_t* dn_blocks = nullptr;
+  uint8_t* dn_scales = nullptr;
+  float* gu_bias = nullptr;
+  float* dn_bias = nullptr;
+  float zero_scale = 0.0f;
+  int sp_h = 0, sp_i = 0;  // padded scale row strides
+};
+
+// Per-forward scratch, sized for `tokens` tokens.
+struct Workspace {
+  int64_t tokens = 0;
+  size_t bytes = 0;
+  void* base = nullptr;
+  float* logits = nullptr;     // [T, E] router logits
+  unsigned* tickets = nullptr; // [T] per token tile, zero between forwards
+  int32_t* idx = nullptr;      // [T*k]
+  float* wts = nullptr;        // [T*k]
+  int32_t* counts = nullptr;   // [E]
+  int32_t* offsets = nullptr;  // [E+1]
+  int32_t* active = nullptr;   // [E] active expert ids, ascending
+  int32_t* meta = nullptr;     // [0] = number of active experts, [1] = error flags
+  int32_t* perm = nullptr;     // [T*k]
+  int32_t* inv = nullptr;      // [T*k]
+  float* h = nullptr;          // [T*k, I]
+  float* y = nullptr;          // [T*k, H]
+  float* x_stage = nullptr;    // [T, H] host-path staging
+  float* out_stage = nullptr;  // [T, H]
+};
+
+struct Moe {
+  gb_moe_desc desc{};  // copy; host pointers inside are not kept valid
+  int device = 0;
+  int sm_count = 0;
+  int e_begin = 0, e_end = 0;  // local experts
+  int ep_rank = 0, ep_size = 1;
+  // router, replicated on every rank
+  float* router_w = nullptr;  // [E][H] f32 (bf16 widened exactly)
+  float* router_b = nullptr;  // [E] or null
+  float* sel_bias = nullptr;  // [E] or null
+  ExpertWeights w;
+  int64_t weight_bytes = 0;
+  Workspace ws;
+  // profiling: events at the stage boundaries of the last forward
+  static constexpr int kStages = 5;  // router, permute, gate_up, down, combine
+  bool profiling = false;
+  bool profiled_once = false;
+  cudaEvent_t ev[kStages + 1] = {};
+  int64_t launches = 0;
+};
+
+// Launchers (router.cu, permute.cu, expert_gemv.cu).  All asynchronous.
+cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
+                               cudaStream_t st);
+cudaError_t launch_permute(const Moe& m, const int32_t* idx, int64_t T, Workspace& ws,
+                           cudaStream_t st);
+cudaError_t launch_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+                           cudaStream_t st);
+cudaError_t launch_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, float* out,
+                           cudaStream_t st);
+cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
+                                  cudaStream_t st);
+cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,
+                                 int64_t row_stride_blocks, uint8_t* scales_dev,
+                                 int64_t row_stride_scales, cudaStream_t st);
+
+}  // namespace gb

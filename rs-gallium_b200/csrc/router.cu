@@ -1,0 +1,208 @@
+// router.cu -- router projection + top-k selection + combine weights.
+//
+// Reference: gpt_oss.rs:172-182 (softmax router), lfm2moe_q.rs:241-258
+// (sigmoid router with selection bias), docs/gpt-oss.md:83-93.
+//
+// logits[t, e] = dot(x[t, :], W[e, :]) + b[e], reduced in a fixed order: lane l
+// of a warp accumulates k = l, l+32, l+64, ... with FMAs, then a butterfly over
+// the 32 lanes (xor 16, 8, 4, 2, 1), then the bias add.  The oracle restates
+// the same order, so expert indices compare bit for bit.
+//
+// Grid: (token tiles of TT, expert groups).  Each warp computes EPW experts'
+// logits for the TT tokens of its tile; the last CTA of a tile to finish
+// (threadfence + per-tile ticket, no waiting) runs the top-k for that tile.
+#include <math.h>
+
+#include "common.cuh"
+#include "moe_internal.h"
+
+namespace gb {
+namespace {
+
+constexpr int kRouterWarps = 8;
+
+template <int TT, int EPW>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+    router_kernel(const float* __restrict__ x, int T, int H, const float* __restrict__ rw,
+                  const float* __restrict__ rb, int E, int K, int kind,
+                  const float* __restrict__ sel_bias, float* __restrict__ logits,
+                  unsigned* __restrict__ tickets, int32_t* __restrict__ idx_out,
+                  float* __restrict__ w_out) {
+  extern __shared__ float xs[];  // [TT][H]
+  __shared__ unsigned s_ticket;
+  const int t0 = blockIdx.x * TT;
+  const int nt = min(TT, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  {
+    const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t0 * H);
+    float4* dst = reinterpret_cast<float4*>(xs);
+    const int n4 = nt * H / 4;
+    for (int i = threadIdx.x; i < TT * H / 4; i += blockDim.x)
+      dst[i] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+
+  const int e0 = (blockIdx.y * kRouterWarps + warp) * EPW;
+  if (e0 < E) {
+    float acc[EPW][TT];
+#pragma unroll
+    for (int q = 0; q < EPW; ++q)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[q][t] = 0.0f;
+    const float* wrow[EPW];
+#pragma unroll
+    for (int q = 0; q < EPW; ++q) wrow[q] = rw + (int64_t)min(e0 + q, E - 1) * H;
+    const int nb = H >> 5;
+#pragma unroll 6
+    for (int j = 0; j < nb; ++j) {
+      const int kk = lane + (j << 5);
+      float wv[EPW];
+#pragma unroll
+      for (int q = 0; q < EPW; ++q) wv[q] = __ldg(wrow[q] + kk);
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        const float xv = xs[t * H + kk];
+#pragma unroll
+        for (int q = 0; q < EPW; ++q) acc[q][t] = __fmaf_rn(xv, wv[q], acc[q][t]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < EPW; ++q) {
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        const float v = warp_sum_butterfly(acc[q][t]);
+        const int e = e0 + q;
+        if (lane == 0 && e < E && t < nt)
+          logits[(int64_t)(t0 + t) * E + e] = rb ? __fadd_rn(v, rb[e]) : v;
+      }
+    }
+  }
+
+  // Last CTA of this token tile runs the top-k.
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_ticket = atomicAdd(&tickets[blockIdx.x], 1u);
+  __syncthreads();
+  if (s_ticket != gridDim.y - 1) return;
+  __threadfence();
+  if (threadIdx.x == 0) tickets[blockIdx.x] = 0;  // ready for the next forward
+
+  for (int t = warp; t < nt; t += kRouterWarps) {
+    const float* lg = logits + (int64_t)(t0 + t) * E;
+    constexpr int kMaxPerLane = 8;  // E <= 256
+    float key[kMaxPerLane];
+    float raw[kMaxPerLane];
+    unsigned taken = 0;
+#pragma unroll
+    for (int q = 0; q < kMaxPerLane; ++q) {
+      const int e = lane + 32 * q;
+      float l = e < E ? __ldcg(lg + e) : -INFINITY;
+      raw[q] = l;
+      if (kind == GB_ROUTER_SIGMOID_TOPK && e < E) {
+        const float p = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l)));
+        raw[q] = p;
+        key[q] = __fadd_rn(p, sel_bias ? sel_bias[e] : 0.0f);
+      } else {
+        key[q] = l;
+      }
+    }
+    float sel_raw[8];
+    int sel_idx[8];
+    for (int r = 0; r < K; ++r) {
+      float best = -INFINITY, braw = 0.0f;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int q = 0; q < kMaxPerLane; ++q) {
+        const int e = lane + 32 * q;
+        if (e < E && !((taken >> q) & 1u) &&
+            (key[q] > best || (key[q] == best && e < bi))) {
+          best = key[q];
+          bi = e;
+          braw = raw[q];
+        }
+      }
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) {
+        const float ob = __shfl_xor_sync(kFullMask, best, s);
+        const int oi = __shfl_xor_sync(kFullMask, bi, s);
+        const float orw = __shfl_xor_sync(kFullMask, braw, s);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+          braw = orw;
+        }
+      }
+      if (bi >= E) {  // only NaN keys left: take the lowest free index
+        bi = 0;
+        for (int e = 0; e < E; ++e) {
+          bool used = false;
+          for (int rr = 0; rr < r; ++rr) used |= sel_idx[rr] == e;
+          if (!used) {
+            bi = e;
+            break;
+          }
+        }
+        braw = kind == GB_ROUTER_SIGMOID_TOPK ? 0.0f : lg[bi];
+      }
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      sel_idx[r] = bi;
+      sel_raw[r] = braw;
+    }
+    if (lane == 0) {
+      int32_t* io = idx_out + (int64_t)(t0 + t) * K;
+      float* wo = w_out + (int64_t)(t0 + t) * K;
+      if (kind == GB_ROUTER_SIGMOID_TOPK) {
+        float total = 0.0f;
+        for (int r = 0; r < K; ++r) total = __fadd_rn(total, sel_raw[r]);
+        total = fmaxf(total, 1e-20f);
+        for (int r = 0; r < K; ++r) {
+          io[r] = sel_idx[r];
+          wo[r] = __fdiv_rn(sel_raw[r], total);
+        }
+      } else {
+        // softmax over the k selected logits (docs/gpt-oss.md:88-93)
+        const float m = sel_raw[0];
+        float ex[8];
+        float total = 0.0f;
+        for (int r = 0; r < K; ++r) {
+          ex[r] = expf(__fsub_rn(sel_raw[r], m));
+          total = __fadd_rn(total, ex[r]);
+        }
+        total = fmaxf(total, 1e-9f);
+        for (int r = 0; r < K; ++r) {
+          io[r] = sel_idx[r];
+          wo[r] = __fdiv_rn(ex[r], total);
+        }
+      }
+    }
+  }
+}
+
+template <int TT, int EPW>
+cudaError_t launch(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
+                   cudaStream_t st) {
+  const gb_moe_desc& d = m.desc;
+  const int H = d.hidden, E = d.n_experts;
+  dim3 grid((unsigned)((T + TT - 1) / TT), (unsigned)((E + kRouterWarps * EPW - 1) / (kRouterWarps * EPW)));
+  const size_t smem = (size_t)TT * H * sizeof(float);
+  auto kern = router_kernel<TT, EPW>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  kern<<<grid, kRouterWarps * 32, smem, st>>>(x, (int)T, H, m.router_w, m.router_b, E, d.top_k,
+                                              d.router_kind, m.sel_bias, m.ws.logits,
+                                              m.ws.tickets, idx, wts);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
+                               cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  if (T <= 4) return launch<1, 1>(m, x, T, idx, wts, st);
+  if (T <= 64) return launch<4, 1>(m, x, T, idx, wts, st);
+  return launch<8, 4>(m, x, T, idx, wts, st);
+}
+
+}  // namespace gb

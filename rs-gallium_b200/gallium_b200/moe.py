@@ -1,0 +1,200 @@
+"""Host-side mirror of rs-gallium's MoE FFN blocks over the C ABI.
+
+The reference's blocks all expose ``forward(&self, x: &Tensor) -> Result<Tensor>``
+with x of shape (batch, seq, hidden):
+
+* ``OssMoEFFN``      crates/gallium-models/src/gpt_oss.rs:97-231 (safetensors MXFP4)
+* ``GptOssQMoEFFN``  the ``QMoEFFN`` of crates/gallium-models/src/gpt_oss_q.rs:119-269
+                     (GGUF MXFP4, separate gate/up tensors)
+
+``load`` mirrors the reference's ``load`` (weights handed over once, repacked
+on the device); ``forward`` keeps the reference's shape and dtype contract
+(f32 compute, result in x's dtype, gpt_oss.rs:169 and :230).  Errors raise
+GalliumError carrying the library's status, where the reference returns a
+candle error.  A CUDA tensor runs through gb_moe_forward on torch's current
+stream; a CPU tensor goes through gb_moe_forward_host (copies in and out).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from ._lib import MoeDesc, MoeInfo, check, load_library
+from .synth import GptOssGgufLayer, GptOssLayer, bf16_bits_to_f32
+
+
+def _ptr(a: Optional[np.ndarray]) -> Optional[int]:
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+class MoEBlock:
+    """Owns one gb_moe handle.  Not re-entrant (one forward at a time)."""
+
+    def __init__(self, desc: MoeDesc, keepalive: list):
+        self._lib = load_library()
+        self._keepalive = keepalive  # host arrays stay alive until create returns
+        h = ctypes.c_void_p()
+        check(self._lib.gb_moe_create(ctypes.byref(desc), ctypes.byref(h)))
+        self._h = h
+        self._keepalive = None
+        self.hidden = desc.hidden
+        self.inter = desc.inter
+        self.n_experts = desc.n_experts
+        self.top_k = desc.top_k
+        self.device = desc.device
+
+    # -- lifetime ------------------------------------------------------------
+    def close(self) -> None:
+        if getattr(self, "_h", None) and self._h.value:
+            check(self._lib.gb_moe_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    @property
+    def handle(self) -> ctypes.c_void_p:
+        return self._h
+
+    def info(self) -> dict:
+        inf = MoeInfo()
+        inf.struct_size = ctypes.sizeof(MoeInfo)
+        check(self._lib.gb_moe_get_info(self._h, ctypes.byref(inf)))
+        return {f: getattr(inf, f) for f, _ in MoeInfo._fields_ if f != "struct_size"}
+
+    # -- forward -------------------------------------------------------------
+    def forward(self, x):
+        """x: torch.Tensor (batch, seq, hidden) or (tokens, hidden)."""
+        import torch
+
+        shape = x.shape
+        if shape[-1] != self.hidden:
+            raise _lib.GalliumError(_lib.GB_ERR_SHAPE,
+                                    f"last dim {shape[-1]} != hidden {self.hidden}")
+        xf = x.reshape(-1, self.hidden).to(torch.float32).contiguous()
+        T = xf.shape[0]
+        if x.is_cuda:
+            out = torch.empty_like(xf)
+            stream = torch.cuda.current_stream(xf.device).cuda_stream
+            check(self._lib.gb_moe_forward(self._h, xf.data_ptr(), T, out.data_ptr(), stream))
+        else:
+            out = torch.empty_like(xf)
+            check(self._lib.gb_moe_forward_host(self._h, xf.data_ptr(), T, out.data_ptr(), None))
+        return out.reshape(shape).to(x.dtype)
+
+    __call__ = forward
+
+    def forward_raw(self, x_ptr: int, T: int, out_ptr: int, stream: int = 0) -> None:
+        """Device pointers straight through to gb_moe_forward (no checks)."""
+        check(self._lib.gb_moe_forward(self._h, x_ptr, T, out_ptr, stream))
+
+    def set_profiling(self, enable: bool = True) -> None:
+        check(self._lib.gb_moe_set_profiling(self._h, 1 if enable else 0))
+
+    def stage_times(self) -> dict:
+        """Per-stage milliseconds of the last profiled forward."""
+        buf = (ctypes.c_float * 16)()
+        n = ctypes.c_int32()
+        check(self._lib.gb_moe_stage_times(self._h, buf, 16, ctypes.byref(n)))
+        return {self._lib.gb_moe_stage_name(i).decode(): buf[i] for i in range(n.value)}
+
+    def route(self, x) -> dict:
+        """Routing of x (CUDA tensor [T, H] f32) as torch tensors on its device."""
+        import torch
+
+        xf = x.reshape(-1, self.hidden).to(torch.float32).contiguous()
+        T = xf.shape[0]
+        dev = xf.device
+        k, E = self.top_k, self.n_experts
+        idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        w = torch.empty((T, k), dtype=torch.float32, device=dev)
+        counts = torch.empty((E,), dtype=torch.int32, device=dev)
+        offsets = torch.empty((E + 1,), dtype=torch.int32, device=dev)
+        perm = torch.empty((T * k,), dtype=torch.int32, device=dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        check(self._lib.gb_moe_route(self._h, xf.data_ptr(), T, idx.data_ptr(), w.data_ptr(),
+                                     counts.data_ptr(), offsets.data_ptr(), perm.data_ptr(),
+                                     stream))
+        return {"idx": idx, "w": w, "counts": counts, "offsets": offsets, "perm": perm}
+
+    def dequant_expert(self, which: int, expert: int):
+        """f32 matrix of a local expert from the repacked device layout:
+        which 0 = gate [I, H], 1 = up [I, H], 2 = down [H, I]."""
+        import torch
+
+        rows, cols = (self.hidden, self.inter) if which == 2 else (self.inter, self.hidden)
+        out = torch.empty((rows, cols), dtype=torch.float32, device=f"cuda:{self.device}")
+        stream = torch.cuda.current_stream(out.device).cuda_stream
+        check(self._lib.gb_moe_dequant_expert(self._h, which, expert, out.data_ptr(), stream))
+        return out
+
+
+def _base_desc(hidden, inter, n_experts, top_k, device, max_tokens) -> MoeDesc:
+    d = MoeDesc()
+    d.struct_size = ctypes.sizeof(MoeDesc)
+    d.hidden, d.inter, d.n_experts, d.top_k = hidden, inter, n_experts, top_k
+    d.device = device
+    d.max_tokens = max_tokens
+    d.ep_size = 1
+    return d
+
+
+class OssMoEFFN(MoEBlock):
+    """Safetensors GPT-OSS MoE block (gpt_oss.rs:97-231)."""
+
+    @classmethod
+    def load(cls, layer: GptOssLayer, device: int = 0, max_tokens: int = 64) -> "OssMoEFFN":
+        d = _base_desc(layer.hidden, layer.inter, layer.n_experts, layer.top_k, device, max_tokens)
+        d.router_kind = _lib.GB_ROUTER_SOFTMAX_TOPK
+        d.act_kind = _lib.GB_ACT_GPTOSS_CLAMP
+        d.weight_format = _lib.GB_FMT_MXFP4_SPLIT
+        d.swiglu_limit = layer.swiglu_limit
+        arrs = [np.ascontiguousarray(a) for a in (
+            layer.router_w, layer.router_b, layer.gu_blocks, layer.gu_scales, layer.dn_blocks,
+            layer.dn_scales, layer.gu_bias, layer.dn_bias)]
+        (d.router_weight, d.router_bias, d.gate_up_blocks, d.gate_up_scales, d.down_blocks,
+         d.down_scales, d.gate_up_bias, d.down_bias) = [_ptr(a) for a in arrs]
+        d.router_dtype = _lib.GB_DTYPE_BF16
+        d.bias_dtype = _lib.GB_DTYPE_BF16
+        return cls(d, arrs)
+
+
+class GptOssQMoEFFN(MoEBlock):
+    """GGUF GPT-OSS MoE block (QMoEFFN, gpt_oss_q.rs:119-269)."""
+
+    @classmethod
+    def load(cls, layer: GptOssGgufLayer, device: int = 0,
+             max_tokens: int = 64) -> "GptOssQMoEFFN":
+        b = layer.base
+        d = _base_desc(b.hidden, b.inter, b.n_experts, b.top_k, device, max_tokens)
+        d.router_kind = _lib.GB_ROUTER_SOFTMAX_TOPK
+        d.act_kind = _lib.GB_ACT_GPTOSS_CLAMP
+        d.weight_format = _lib.GB_FMT_MXFP4_GGUF
+        d.swiglu_limit = b.swiglu_limit
+        rw = bf16_bits_to_f32(b.router_w)
+        rb = bf16_bits_to_f32(b.router_b)
+        gb_ = bf16_bits_to_f32(layer.gate_bias)
+        ub = bf16_bits_to_f32(layer.up_bias)
+        db = bf16_bits_to_f32(layer.down_bias)
+        arrs = [np.ascontiguousarray(a) for a in (
+            rw, rb, layer.gate_raw, layer.up_raw, layer.down_raw, gb_, ub, db)]
+        (d.router_weight, d.router_bias, d.gate_raw, d.up_raw, d.down_raw, d.gate_bias,
+         d.up_bias, d.down_bias) = [_ptr(a) for a in arrs]
+        d.router_dtype = _lib.GB_DTYPE_F32
+        d.bias_dtype = _lib.GB_DTYPE_F32
+        return cls(d, arrs)

@@ -1,0 +1,150 @@
+"""Seeded synthetic MoE layers and inputs (no checkpoints are available).
+
+Shapes and value distributions follow the workloads this path is measured on:
+
+* GPT-OSS-shaped block: hidden 2880, intermediate 2880, top-4, E = 32 (20B
+  shape) or 128 (120B shape).  Router weight bf16 ~ N(0, 0.02), bias 0.
+  Expert weights MXFP4 in the safetensors layout: E2M1 nibbles uniform over
+  the 16 codes, one E8M0 scale per 32 elements uniform over exponents
+  -8..-2 (bytes 119..125).  Expert biases bf16 ~ N(0, 0.01).
+  Activation: clamped SwiGLU, limit 7.
+* Skewed routing: router bias_e = 2 * ln(p_e), p_e proportional to
+  (e + 1)^-1.2 (Zipf, s = 1.2), so a few experts take most tokens.
+* x ~ N(0, 1) f32.
+
+Everything is generated with numpy's PCG64 from an explicit seed, so the
+same call gives the same bytes on every machine.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+
+
+def f32_to_bf16_bits(a) -> np.ndarray:
+    """Round f32 to bf16 (nearest, ties to even); returns the uint16 bits."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    r = ((u >> 16) & 1) + 0x7FFF
+    return ((u + r) >> 16).astype(np.uint16)
+
+
+def bf16_bits_to_f32(b) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint16)
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+@dataclass
+class GptOssLayer:
+    """One GPT-OSS MoE block in the safetensors MXFP4 layout (gpt_oss.rs:96-142)."""
+    hidden: int
+    inter: int
+    n_experts: int
+    top_k: int
+    swiglu_limit: float
+    router_w: np.ndarray        # [E, H] bf16 bits (uint16)
+    router_b: np.ndarray        # [E] bf16 bits
+    gu_blocks: np.ndarray       # [E, 2I, H/32, 16] uint8
+    gu_scales: np.ndarray       # [E, 2I, H/32] uint8
+    gu_bias: np.ndarray         # [E, 2I] bf16 bits
+    dn_blocks: np.ndarray       # [E, H, I/32, 16] uint8
+    dn_scales: np.ndarray       # [E, H, I/32] uint8
+    dn_bias: np.ndarray         # [E, H] bf16 bits
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def expert_bytes(self) -> int:
+        """MXFP4 bytes of one expert (nibbles + scales), 13,219,200 at 2880/2880."""
+        H, I = self.hidden, self.inter
+        return (2 * I * H + H * I) // 2 + (2 * I * H + H * I) // 32
+
+    @property
+    def expert_bias_bytes(self) -> int:
+        return 2 * (2 * self.inter + self.hidden)  # bf16
+
+
+def zipf_router_bias(n_experts: int, s: float = 1.2) -> np.ndarray:
+    p = (np.arange(n_experts, dtype=np.float64) + 1.0) ** (-s)
+    p /= p.sum()
+    return (2.0 * np.log(p)).astype(np.float32)
+
+
+def gptoss_layer(n_experts: int = 32, hidden: int = 2880, inter: int = 2880, top_k: int = 4,
+                 seed: int = 0, skewed: bool = False, scale_lo: int = 119,
+                 scale_hi: int = 125) -> GptOssLayer:
+    rng = np.random.default_rng(seed)
+    E, H, I = n_experts, hidden, inter
+    router_w = f32_to_bf16_bits(rng.normal(0.0, 0.02, (E, H)).astype(np.float32))
+    rb = zipf_router_bias(E) if skewed else np.zeros(E, np.float32)
+    router_b = f32_to_bf16_bits(rb)
+    gu_blocks = rng.integers(0, 256, (E, 2 * I, H // 32, 16), dtype=np.uint8)
+    gu_scales = rng.integers(scale_lo, scale_hi + 1, (E, 2 * I, H // 32), dtype=np.uint8)
+    gu_bias = f32_to_bf16_bits(rng.normal(0.0, 0.01, (E, 2 * I)).astype(np.float32))
+    dn_blocks = rng.integers(0, 256, (E, H, I // 32, 16), dtype=np.uint8)
+    dn_scales = rng.integers(scale_lo, scale_hi + 1, (E, H, I // 32), dtype=np.uint8)
+    dn_bias = f32_to_bf16_bits(rng.normal(0.0, 0.01, (E, H)).astype(np.float32))
+    return GptOssLayer(H, I, E, top_k, 7.0, router_w, router_b, gu_blocks, gu_scales, gu_bias,
+                       dn_blocks, dn_scales, dn_bias,
+                       meta={"seed": seed, "skewed": skewed})
+
+
+def tokens(T: int, hidden: int, seed: int = 0) -> np.ndarray:
+    """x ~ N(0, 1), f32 [T, hidden]; seed 0 stream is independent of the weights'."""
+    rng = np.random.default_rng([seed, 0x5EED])
+    return rng.standard_normal((T, hidden), dtype=np.float32)
+
+
+# ---- GGUF MXFP4 (type 39) views of a safetensors layer ---------------------
+
+def split_to_gguf_blocks(blocks: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """Safetensors blocks [..., nb, 16] + scales [..., nb] -> GGUF 17-byte
+    blocks [..., nb * 17] holding the same values (quantized.rs:386-392: low
+    nibble of byte j = element j, high nibble = element j + 16; the E8M0 byte
+    means the same power of two for bytes >= 1 because the GGUF LUT is the
+    E2M1 table doubled and its scale is halved)."""
+    lo = blocks & 0x0F
+    hi = blocks >> 4
+    el = np.empty(blocks.shape[:-1] + (32,), np.uint8)
+    el[..., 0::2] = lo
+    el[..., 1::2] = hi
+    qs = (el[..., :16] | (el[..., 16:] << 4)).astype(np.uint8)
+    out = np.concatenate([scales[..., None].astype(np.uint8), qs], axis=-1)
+    return np.ascontiguousarray(out.reshape(blocks.shape[:-2] + (blocks.shape[-2] * 17,)))
+
+
+@dataclass
+class GptOssGgufLayer:
+    """The same layer as GGUF tensors: separate gate/up [E, I, H] and down
+    [E, H, I] (gpt_oss_q.rs:110-163)."""
+    base: GptOssLayer
+    gate_raw: np.ndarray
+    up_raw: np.ndarray
+    down_raw: np.ndarray
+    gate_bias: np.ndarray  # bf16 bits [E, I]
+    up_bias: np.ndarray
+    down_bias: np.ndarray
+
+
+def gptoss_gguf_from_split(layer: GptOssLayer) -> GptOssGgufLayer:
+    g = split_to_gguf_blocks(layer.gu_blocks[:, 0::2], layer.gu_scales[:, 0::2])
+    u = split_to_gguf_blocks(layer.gu_blocks[:, 1::2], layer.gu_scales[:, 1::2])
+    d = split_to_gguf_blocks(layer.dn_blocks, layer.dn_scales)
+    return GptOssGgufLayer(layer, g, u, d, np.ascontiguousarray(layer.gu_bias[:, 0::2]),
+                           np.ascontiguousarray(layer.gu_bias[:, 1::2]), layer.dn_bias)
+
+
+def algorithmic_bytes(layer: GptOssLayer, T: int, n_touched: int) -> int:
+    """Bytes one forward must move at minimum: touched experts' MXFP4 weights
+    and biases, the router weight and bias, x in and out (f32), and the
+    routing indices and weights."""
+    E, H = layer.n_experts, layer.hidden
+    return (n_touched * (layer.expert_bytes + layer.expert_bias_bytes) + E * H * 2 + E * 2
+            + 2 * T * H * 4 + T * layer.top_k * 8)
+
+
+def algorithmic_flops(layer: GptOssLayer, T: int) -> int:
+    """Expert GEMM FLOPs (2 * (2I*H + H*I) per token-expert) plus the router."""
+    H, I, E, k = layer.hidden, layer.inter, layer.n_experts, layer.top_k
+    return T * k * 6 * H * I + 2 * T * H * E

@@ -1,0 +1,139 @@
+"""The C ABI surface, checked without a GPU: the library loads, exports every
+function include/gallium_b200.h declares, the ctypes mirrors of the structs
+match the C layout, and descriptor validation answers with status codes
+(INVALID_ARG / SHAPE / UNSUPPORTED) before any device work."""
+import ctypes
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from gallium_b200 import _lib, synth
+from gallium_b200._lib import MoeDesc, MoeInfo
+
+HEADER = _lib.HEADER_PATH
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(gb_[a-z_0-9]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load_library()
+    names = _declared_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in the header but not exported"
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+    assert lib.gb_abi_version() == 1
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    fields_d = [f for f, _ in MoeDesc._fields_]
+    fields_i = [f for f, _ in MoeInfo._fields_]
+    src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', 'int main(void){']
+    src.append('printf("%zu\\n", sizeof(gb_moe_desc));')
+    for f in fields_d:
+        src.append(f'printf("%zu\\n", offsetof(gb_moe_desc, {f}));')
+    src.append('printf("%zu\\n", sizeof(gb_moe_info));')
+    for f in fields_i:
+        src.append(f'printf("%zu\\n", offsetof(gb_moe_info, {f}));')
+    src.append("return 0;}")
+    c = tmp_path / "layout.c"
+    c.write_text("\n".join(src))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", str(c), "-o", str(exe)], check=True)
+    vals = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                           check=True).stdout.split()]
+    want = [ctypes.sizeof(MoeDesc)] + [getattr(MoeDesc, f).offset for f in fields_d]
+    want += [ctypes.sizeof(MoeInfo)] + [getattr(MoeInfo, f).offset for f in fields_i]
+    assert vals == want
+
+
+def _desc(**kw):
+    d = MoeDesc()
+    d.struct_size = ctypes.sizeof(MoeDesc)
+    d.hidden, d.inter, d.n_experts, d.top_k = 64, 64, 4, 2
+    d.weight_format = _lib.GB_FMT_MXFP4_SPLIT
+    d.swiglu_limit = 7.0
+    d.ep_size = 1
+    d.max_tokens = 4
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d
+
+
+def _create(d):
+    lib = _lib.load_library()
+    h = ctypes.c_void_p()
+    rc = lib.gb_moe_create(ctypes.byref(d), ctypes.byref(h))
+    return rc, lib.gb_last_error().decode(), h
+
+
+BUF = np.zeros(1 << 16, np.uint8)
+P = BUF.ctypes.data
+
+
+def _full(**kw):
+    base = dict(router_weight=P, gate_up_blocks=P, gate_up_scales=P, down_blocks=P,
+                down_scales=P)
+    base.update(kw)
+    return _desc(**base)
+
+
+@pytest.mark.parametrize("kw,status,needle", [
+    (dict(struct_size=8), _lib.GB_ERR_INVALID_ARG, "struct_size"),
+    (dict(hidden=0), _lib.GB_ERR_INVALID_ARG, "shape"),
+    (dict(top_k=5), _lib.GB_ERR_INVALID_ARG, "top_k"),
+    (dict(top_k=9, n_experts=16), _lib.GB_ERR_INVALID_ARG, "top_k"),
+    (dict(router_kind=7), _lib.GB_ERR_INVALID_ARG, "router_kind"),
+    (dict(act_kind=7), _lib.GB_ERR_INVALID_ARG, "act_kind"),
+    (dict(weight_format=9), _lib.GB_ERR_INVALID_ARG, "weight_format"),
+    (dict(router_weight=None), _lib.GB_ERR_INVALID_ARG, "router_weight"),
+    (dict(down_scales=None), _lib.GB_ERR_INVALID_ARG, "MXFP4_SPLIT"),
+    (dict(hidden=100), _lib.GB_ERR_SHAPE, "100"),
+    (dict(inter=48), _lib.GB_ERR_SHAPE, "32-element"),
+    (dict(n_experts=300, top_k=2), _lib.GB_ERR_UNSUPPORTED, "256"),
+    (dict(weight_format=_lib.GB_FMT_Q4_K), _lib.GB_ERR_UNSUPPORTED, "Q4_K"),
+    (dict(ep_size=2, ep_rank=3), _lib.GB_ERR_INVALID_ARG, "ep_rank"),
+    (dict(max_tokens=-1), _lib.GB_ERR_INVALID_ARG, "max_tokens"),
+])
+def test_create_rejects_bad_descriptors(kw, status, needle):
+    rc, msg, h = _create(_full(**kw))
+    assert rc == status, msg
+    assert needle in msg
+    assert not h.value
+
+
+def test_gguf_format_needs_raw_tensors():
+    rc, msg, _ = _create(_desc(router_weight=P, weight_format=_lib.GB_FMT_MXFP4_GGUF))
+    assert rc == _lib.GB_ERR_INVALID_ARG and "gate_raw" in msg
+
+
+def test_null_handle_calls_are_errors_not_crashes():
+    lib = _lib.load_library()
+    assert lib.gb_moe_forward(None, None, 1, None, None) == _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_moe_route(None, None, 1, None, None, None, None, None, None) == \
+        _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_moe_destroy(None) == _lib.GB_OK
+    info = MoeInfo()
+    info.struct_size = ctypes.sizeof(MoeInfo)
+    assert lib.gb_moe_get_info(None, ctypes.byref(info)) == _lib.GB_ERR_INVALID_ARG
+
+
+def test_python_errors_carry_status_and_message():
+    with pytest.raises(_lib.GalliumError) as ei:
+        _lib.check(_create(_full(hidden=100))[0])
+    assert ei.value.status == _lib.GB_ERR_SHAPE
+    assert "100" in str(ei.value)
+
+
+def test_gguf_repack_helper_round_trips_values():
+    layer = synth.gptoss_layer(n_experts=1, hidden=64, inter=32, seed=4)
+    gg = synth.gptoss_gguf_from_split(layer)
+    assert gg.gate_raw.shape == (1, 32, 2 * 17)
+    assert gg.down_raw.shape == (1, 64, 1 * 17)

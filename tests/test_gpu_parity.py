@@ -1,0 +1,254 @@
+"""CUDA path vs the CPU oracle, through the C ABI (needs a B200).
+
+Bar (from the path's contract): expert indices and the grouping permutation
+bit-exact; outputs within max-abs 2e-2 and mean-rel 1e-3 after f32
+accumulation, where mean-rel = sum|gpu - oracle| / sum|oracle|.  Dequantised
+weights are compared bit for bit.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from gallium_b200 import GalliumError, GptOssQMoEFFN, OssMoEFFN, synth
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+MEAN_REL = 1e-3
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def assert_parity(got, want, what=""):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape
+    assert np.all(np.isfinite(got)), what
+    err = np.abs(got - want)
+    max_abs = float(err.max()) if err.size else 0.0
+    mean_rel = float(err.sum() / max(np.abs(want).sum(), 1e-30))
+    assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (
+        f"{what}: max_abs {max_abs:.3e} (<= {MAX_ABS}), mean_rel {mean_rel:.3e} (<= {MEAN_REL})")
+    return max_abs, mean_rel
+
+
+@pytest.fixture(scope="module")
+def layer32():
+    return synth.gptoss_layer(n_experts=32, seed=0)
+
+
+@pytest.fixture(scope="module")
+def moe32(layer32):
+    m = OssMoEFFN.load(layer32, device=0, max_tokens=64)
+    yield m
+    m.close()
+
+
+@pytest.fixture(scope="module")
+def layer32_skew():
+    return synth.gptoss_layer(n_experts=32, seed=1, skewed=True)
+
+
+@pytest.fixture(scope="module")
+def moe32_skew(layer32_skew):
+    m = OssMoEFFN.load(layer32_skew, device=0, max_tokens=64)
+    yield m
+    m.close()
+
+
+def _route_oracle(layer, x):
+    rw = synth.bf16_bits_to_f32(layer.router_w)
+    rb = synth.bf16_bits_to_f32(layer.router_b)
+    logits = oracle.router_logits(x, rw, rb)
+    idx, w = oracle.route_softmax_topk(logits, layer.top_k)
+    counts, offsets, perm, inv = oracle.permute(idx, layer.n_experts)
+    return logits, idx, w, counts, offsets, perm
+
+
+def _cuda(a):
+    return _torch().from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+# ---- decoders ---------------------------------------------------------------
+
+@pytest.mark.parametrize("expert", [0, 17, 31])
+def test_device_dequant_is_bit_exact(moe32, layer32, expert):
+    gu = oracle.mxfp4_split_dequant(layer32.gu_blocks[expert], layer32.gu_scales[expert])
+    dn = oracle.mxfp4_split_dequant(layer32.dn_blocks[expert], layer32.dn_scales[expert])
+    for which, want in ((0, gu[0::2]), (1, gu[1::2]), (2, dn)):
+        got = moe32.dequant_expert(which, expert).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), np.ascontiguousarray(want).view(np.uint32))
+
+
+def test_gguf_upload_repacks_to_the_same_values():
+    layer = synth.gptoss_layer(n_experts=4, hidden=256, inter=192, seed=6)
+    # exercise scale byte 0 (GGUF: 2^-127 per quantized.rs:375-383)
+    layer.gu_scales[1, 3, 2] = 0
+    gg = synth.gptoss_gguf_from_split(layer)
+    m = GptOssQMoEFFN.load(gg, device=0, max_tokens=8)
+    try:
+        for e in range(4):
+            g = oracle.mxfp4_gguf_dequant(gg.gate_raw[e], 192 * 256).reshape(192, 256)
+            u = oracle.mxfp4_gguf_dequant(gg.up_raw[e], 192 * 256).reshape(192, 256)
+            d = oracle.mxfp4_gguf_dequant(gg.down_raw[e], 256 * 192).reshape(256, 192)
+            for which, want in ((0, g), (1, u), (2, d)):
+                got = m.dequant_expert(which, e).cpu().numpy()
+                assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (e, which)
+    finally:
+        m.close()
+
+
+# ---- routing ----------------------------------------------------------------
+
+@pytest.mark.parametrize("T", [1, 3, 8, 64, 512])
+def test_routing_is_bit_exact(moe32, layer32, T):
+    x = synth.tokens(T, 2880, seed=T)
+    r = moe32.route(_cuda(x))
+    logits, idx, w, counts, offsets, perm = _route_oracle(layer32, x)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx)
+    assert np.array_equal(r["counts"].cpu().numpy(), counts)
+    assert np.array_equal(r["offsets"].cpu().numpy(), offsets)
+    assert np.array_equal(r["perm"].cpu().numpy(), perm)
+    np.testing.assert_allclose(r["w"].cpu().numpy(), w, rtol=2e-6, atol=1e-7)
+
+
+def test_routing_skewed_and_128_experts(moe32_skew, layer32_skew):
+    x = synth.tokens(256, 2880, seed=77)
+    r = moe32_skew.route(_cuda(x))
+    _, idx, w, counts, offsets, perm = _route_oracle(layer32_skew, x)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx)
+    assert np.array_equal(r["perm"].cpu().numpy(), perm)
+    assert counts[0] > counts[-1]  # skew is visible
+
+
+def test_routing_ties_take_the_lower_index():
+    layer = synth.gptoss_layer(n_experts=8, hidden=64, inter=64, top_k=2, seed=0)
+    layer.router_w[:] = 0
+    layer.router_b[:] = synth.f32_to_bf16_bits(np.array([0, 1, 1, 0, 1, 0, 0, 0], np.float32))
+    m = OssMoEFFN.load(layer, device=0, max_tokens=4)
+    try:
+        r = m.route(_cuda(synth.tokens(3, 64, seed=1)))
+        assert r["idx"].cpu().numpy().tolist() == [[1, 2]] * 3
+        np.testing.assert_allclose(r["w"].cpu().numpy(), 0.5)
+    finally:
+        m.close()
+
+
+# ---- whole block ------------------------------------------------------------
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_forward_matches_oracle_20b_balanced(moe32, layer32, T):
+    x = synth.tokens(T, 2880, seed=100 + T)
+    got = moe32.forward(_cuda(x)).cpu().numpy()
+    want, idx, _ = oracle.OracleMoe(layer32).forward(x)
+    assert_parity(got, want, f"T={T}")
+
+
+@pytest.mark.parametrize("T", [1, 64])
+def test_forward_matches_oracle_20b_skewed(moe32_skew, layer32_skew, T):
+    x = synth.tokens(T, 2880, seed=200 + T)
+    got = moe32_skew.forward(_cuda(x)).cpu().numpy()
+    want, _, _ = oracle.OracleMoe(layer32_skew).forward(x)
+    assert_parity(got, want, f"skewed T={T}")
+
+
+def test_forward_matches_oracle_120b_shape():
+    layer = synth.gptoss_layer(n_experts=128, seed=0)
+    m = OssMoEFFN.load(layer, device=0, max_tokens=32)
+    try:
+        for T in (1, 32):
+            x = synth.tokens(T, 2880, seed=300 + T)
+            got = m.forward(_cuda(x)).cpu().numpy()
+            want, _, _ = oracle.OracleMoe(layer).forward(x)
+            assert_parity(got, want, f"E=128 T={T}")
+    finally:
+        m.close()
+
+
+def test_gguf_format_forward_matches_oracle(layer32):
+    gg = synth.gptoss_gguf_from_split(layer32)
+    m = GptOssQMoEFFN.load(gg, device=0, max_tokens=16)
+    try:
+        x = synth.tokens(16, 2880, seed=5)
+        got = m.forward(_cuda(x)).cpu().numpy()
+        want, _, _ = oracle.OracleMoe(layer32, gguf=gg).forward(x)
+        assert_parity(got, want, "gguf")
+    finally:
+        m.close()
+
+
+def test_host_path_equals_device_path(moe32):
+    torch = _torch()
+    x = synth.tokens(5, 2880, seed=9)
+    dev = moe32.forward(_cuda(x)).cpu().numpy()
+    host = moe32.forward(torch.from_numpy(x)).numpy()
+    assert np.array_equal(dev, host)
+
+
+def test_batch_shape_and_dtype_contract(moe32):
+    torch = _torch()
+    x = torch.from_numpy(synth.tokens(6, 2880, seed=10)).cuda()
+    flat = moe32.forward(x)
+    b = moe32.forward(x.reshape(2, 3, 2880))
+    assert b.shape == (2, 3, 2880)
+    assert torch.equal(b.reshape(6, 2880), flat)
+    xb = x.to(torch.bfloat16)
+    ob = moe32.forward(xb)
+    assert ob.dtype == torch.bfloat16  # cast back to x's dtype (gpt_oss.rs:230)
+
+
+def test_zero_tokens_is_a_no_op(moe32):
+    torch = _torch()
+    out = moe32.forward(torch.empty((0, 2880), device="cuda"))
+    assert out.shape == (0, 2880)
+
+
+def test_wrong_hidden_is_an_error(moe32):
+    torch = _torch()
+    with pytest.raises(GalliumError):
+        moe32.forward(torch.zeros((2, 100), device="cuda"))
+
+
+# ---- full-size properties (T = 4096, 20B shape) ------------------------------
+
+@pytest.fixture(scope="module")
+def big_run(moe32, layer32):
+    torch = _torch()
+    T = 4096
+    x = synth.tokens(T, 2880, seed=4096)
+    xc = _cuda(x)
+    out1 = moe32.forward(xc)
+    out2 = moe32.forward(xc)
+    torch.cuda.synchronize()
+    return x, xc, out1.cpu().numpy(), out2.cpu().numpy()
+
+
+def test_full_size_is_deterministic(big_run):
+    _, _, a, b = big_run
+    assert np.array_equal(a, b)
+
+
+def test_full_size_routing_bit_exact(moe32, layer32, big_run):
+    x, xc, _, _ = big_run
+    r = moe32.route(xc)
+    _, idx, _, counts, offsets, perm = _route_oracle(layer32, x)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx)
+    assert np.array_equal(r["perm"].cpu().numpy(), perm)
+    assert int(r["counts"].sum()) == 4096 * 4
+
+
+def test_full_size_sampled_rows_match_oracle(layer32, big_run):
+    x, _, out, _ = big_run
+    rows = np.random.default_rng(0).choice(4096, 24, replace=False)
+    want, _, _ = oracle.OracleMoe(layer32).forward(x[rows])
+    assert_parity(out[rows], want, "T=4096 sampled rows")
+
+
+def test_full_size_rows_do_not_depend_on_the_batch(moe32, big_run):
+    torch = _torch()
+    _, xc, out, _ = big_run
+    part = moe32.forward(xc[1000:1037]).cpu().numpy()
+    assert_parity(part, out[1000:1037], "sub-batch vs full batch")
