@@ -250,11 +250,14 @@ __global__ void gguf_to_split_kernel(const uint8_t* __restrict__ raw, int64_t ro
   const int64_t r = i / NB;
   const int b = (int)(i % NB);
   const uint8_t* src = raw + i * 17;
+  // The GGUF table has +0 for code 8 (quantized.rs:370, i8 zero), where E2M1
+  // reads it as -0: store code 0 instead so the decode is bit-identical.
   uint8_t el[32];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    el[j] = src[1 + j] & 0xF;
-    el[j + 16] = src[1 + j] >> 4;
+    const uint8_t lo = src[1 + j] & 0xF, hi = src[1 + j] >> 4;
+    el[j] = lo == 8 ? 0 : lo;
+    el[j + 16] = hi == 8 ? 0 : hi;
   }
   uint8_t* dst = blocks + (r * row_stride_blocks + b) * 16;
 #pragma unroll
