@@ -190,6 +190,30 @@ const char* gb_moe_stage_name(int32_t stage);
 /* Releases device memory, streams and (expert parallel) the communicator. */
 int gb_moe_destroy(gb_moe* m);
 
+/* Routing that allocates nothing.  No counterpart in the reference: it is
+ * the router projection, top-k and combine weights of gb_moe_route (the
+ * routing of gpt_oss.rs:172-182 / lfm2moe_q.rs:241-258), for callers that
+ * cannot call cudaMalloc when they route -- a candle custom op whose device
+ * buffers must all come from candle's allocator, or a serving process that
+ * has reserved the device's memory up front.  The caller passes every input
+ * and output as device pointers on the current device: x_dev [T, hidden] f32,
+ * router_weight_dev [n_experts, hidden] f32, router_bias_dev [n_experts] f32
+ * (NULL = none), selection_bias_dev [n_experts] f32 (sigmoid router only,
+ * NULL = zeros), idx_dev [T, top_k] i32, w_dev [T, top_k] f32.  Results equal
+ * gb_moe_route's idx / w for the same inputs.
+ * Scratch (router logits and per-tile tickets) is a fixed 272 KiB array inside
+ * the library, held on every GPU that loads the library until the process
+ * exits; requests with T * n_experts > 65536 or T > 4096 are rejected with
+ * GB_ERR_INVALID_ARG.  The first call on each device looks up that array's
+ * device address (cudaGetSymbolAddress); make that first call before any
+ * stream capture.  Every call shares the one array and each call overwrites
+ * it: calls that overlap on the GPU (other streams, other threads) race, so
+ * serialise them.  Asynchronous on `stream`; calls no cudaMalloc or cudaFree. */
+int gb_route_noalloc(const float* x_dev, const float* router_weight_dev,
+                     const float* router_bias_dev, const float* selection_bias_dev, int64_t T,
+                     int32_t hidden, int32_t n_experts, int32_t top_k, int32_t router_kind,
+                     int32_t* idx_dev, float* w_dev, void* stream);
+
 /* Expert parallel: a fresh 128-byte ncclUniqueId (rank 0 calls this and
  * shares the bytes with the other ranks). */
 int gb_nccl_unique_id(uint8_t out[128]);

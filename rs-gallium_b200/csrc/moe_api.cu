@@ -376,6 +376,16 @@ int check_handle(gb_moe* h) {
 
 }  // namespace
 
+namespace gb {
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof g_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace gb
+
 struct gb_moe {
   gb::Moe m;
 };

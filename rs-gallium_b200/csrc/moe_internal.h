@@ -76,6 +76,9 @@ struct Moe {
   int64_t launches = 0;
 };
 
+// Records an error message for gb_last_error() and returns `code`.
+int set_error(int code, const char* fmt, ...);
+
 // Launchers (router.cu, permute.cu, expert_gemv.cu).  All asynchronous.
 cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
                                cudaStream_t st);

@@ -13,6 +13,8 @@
 // (threadfence + per-tile ticket, no waiting) runs the top-k for that tile.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "moe_internal.h"
 
@@ -206,3 +208,123 @@ cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t*
 }
 
 }  // namespace gb
+
+// ---------------------------------------------------------------------------
+// Routing that allocates nothing (gb_route_noalloc).
+//
+// For callers that cannot call cudaMalloc when they route: a candle custom op
+// whose device buffers must all come from candle's own allocator, or a serving
+// process that has reserved the device's memory up front.  The router kernel
+// above needs scratch beyond its inputs and outputs (the [T, E] logits and one
+// ticket per token tile); here that scratch is a fixed array in this library's
+// device image, so the call allocates nothing.  Every GPU that loads the
+// library holds the array until the process exits.
+// ---------------------------------------------------------------------------
+namespace gb {
+namespace {
+
+constexpr int64_t kNoAllocMaxLogits = 65536;  // T * n_experts
+constexpr int64_t kNoAllocMaxTiles = 4096;    // token tiles (at most T)
+constexpr size_t kNoAllocTicketOffset = (size_t)kNoAllocMaxLogits * sizeof(float);
+constexpr size_t kNoAllocBytes = kNoAllocTicketOffset + (size_t)kNoAllocMaxTiles * sizeof(unsigned);
+constexpr int kNoAllocMaxDevices = 64;
+
+}  // namespace
+}  // namespace gb
+
+// The scratch: logits at offset 0, tickets after them.  In host code this
+// name is only a stand-in for the symbol, never a device address; host code
+// uses the address from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_route_scratch[gb::kNoAllocBytes];
+
+namespace gb {
+namespace {
+
+std::mutex g_route_scratch_mu;
+void* g_route_scratch_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_route_scratch on device `dev` (which must be current),
+// looked up once per device on its first use.
+int route_scratch_address(int dev, void** out) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return set_error(GB_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_route_scratch_mu);
+  if (!g_route_scratch_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_route_scratch);
+    if (e != cudaSuccess || !p)
+      return set_error(GB_ERR_CUDA, "cudaGetSymbolAddress(route scratch) on device %d: %s", dev,
+                       cudaGetErrorString(e));
+    g_route_scratch_addr[dev] = p;
+  }
+  *out = g_route_scratch_addr[dev];
+  return GB_OK;
+}
+
+template <int TT, int EPW>
+cudaError_t launch_noalloc(const float* x, int64_t T, int H, const float* rw, const float* rb,
+                           int E, int K, int kind, const float* sel_bias, float* logits,
+                           unsigned* tickets, int32_t* idx, float* wts, cudaStream_t st) {
+  const int64_t tiles = (T + TT - 1) / TT;
+  cudaError_t err = cudaMemsetAsync(tickets, 0, sizeof(unsigned) * (size_t)tiles, st);
+  if (err != cudaSuccess) return err;
+  dim3 grid((unsigned)tiles, (unsigned)((E + kRouterWarps * EPW - 1) / (kRouterWarps * EPW)));
+  const size_t smem = (size_t)TT * H * sizeof(float);
+  auto kern = router_kernel<TT, EPW>;
+  err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  kern<<<grid, kRouterWarps * 32, smem, st>>>(x, (int)T, H, rw, rb, E, K, kind, sel_bias, logits,
+                                              tickets, idx, wts);
+  return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace gb
+
+extern "C" int gb_route_noalloc(const float* x_dev, const float* router_weight_dev,
+                                const float* router_bias_dev, const float* selection_bias_dev,
+                                int64_t T, int32_t hidden, int32_t n_experts, int32_t top_k,
+                                int32_t router_kind, int32_t* idx_dev, float* w_dev,
+                                void* stream) {
+  using namespace gb;
+  if (T < 0) return set_error(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
+  if (hidden <= 0 || hidden % 32 != 0 || hidden > 8192)
+    return set_error(GB_ERR_INVALID_ARG, "hidden %d must be a positive multiple of 32, <= 8192",
+                     hidden);
+  if (n_experts < 1 || n_experts > 256)
+    return set_error(GB_ERR_INVALID_ARG, "n_experts %d not in 1..256", n_experts);
+  if (top_k < 1 || top_k > 8 || top_k > n_experts)
+    return set_error(GB_ERR_INVALID_ARG, "top_k %d must be in 1..min(8, n_experts)", top_k);
+  if (router_kind != GB_ROUTER_SOFTMAX_TOPK && router_kind != GB_ROUTER_SIGMOID_TOPK)
+    return set_error(GB_ERR_INVALID_ARG, "unknown router_kind %d", router_kind);
+  if (T == 0) return GB_OK;
+  if (!x_dev || !router_weight_dev || !idx_dev || !w_dev)
+    return set_error(GB_ERR_INVALID_ARG, "x, router_weight, idx and w must not be null");
+  if (T * (int64_t)n_experts > kNoAllocMaxLogits || T > kNoAllocMaxTiles)
+    return set_error(GB_ERR_INVALID_ARG,
+                     "T * n_experts = %lld exceeds the fixed routing scratch of %lld logits "
+                     "(and T <= %lld); route in smaller batches",
+                     (long long)(T * (int64_t)n_experts), (long long)kNoAllocMaxLogits,
+                     (long long)kNoAllocMaxTiles);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(GB_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  void* scratch = nullptr;
+  const int rc = route_scratch_address(dev, &scratch);
+  if (rc) return rc;
+  float* logits = static_cast<float*>(scratch);
+  unsigned* tickets = reinterpret_cast<unsigned*>(static_cast<char*>(scratch) + kNoAllocTicketOffset);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T <= 4)
+    e = launch_noalloc<1, 1>(x_dev, T, hidden, router_weight_dev, router_bias_dev, n_experts, top_k,
+                             router_kind, selection_bias_dev, logits, tickets, idx_dev, w_dev, st);
+  else if (T <= 64)
+    e = launch_noalloc<4, 1>(x_dev, T, hidden, router_weight_dev, router_bias_dev, n_experts, top_k,
+                             router_kind, selection_bias_dev, logits, tickets, idx_dev, w_dev, st);
+  else
+    e = launch_noalloc<8, 4>(x_dev, T, hidden, router_weight_dev, router_bias_dev, n_experts, top_k,
+                             router_kind, selection_bias_dev, logits, tickets, idx_dev, w_dev, st);
+  if (e != cudaSuccess)
+    return set_error(GB_ERR_CUDA, "no-alloc router launch: %s", cudaGetErrorString(e));
+  return GB_OK;
+}

@@ -108,6 +108,8 @@ SIGNATURES = {
     "gb_moe_set_profiling": (c_int, [c_void_p, c_int]),
     "gb_moe_stage_times": (c_int, [c_void_p, POINTER(c_float), c_int32, POINTER(c_int32)]),
     "gb_moe_stage_name": (c_char_p, [c_int32]),
+    "gb_route_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
+                                 c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
     "gb_nccl_unique_id": (c_int, [POINTER(c_uint8)]),
     "gb_last_error": (c_char_p, []),
     "gb_abi_version": (c_int, []),
