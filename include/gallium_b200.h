@@ -177,6 +177,18 @@ int gb_moe_dequant_expert(gb_moe* m, int32_t which, int32_t expert, float* out_d
 
 int gb_moe_get_info(const gb_moe* m, gb_moe_info* info);
 
+/* Which kernels run the expert products.  AUTO picks the CUDA-core kernels
+ * (streaming MXFP4 rows, f32 FMA) for decode-sized batches and the tcgen05
+ * tensor-core grouped GEMMs for prefill-sized ones; the other two force one
+ * path (tensor cores need the GPT-OSS activation and H, I multiples of 64).
+ * No counterpart in the reference, which has one CPU path. */
+typedef enum {
+  GB_PATH_AUTO = 0,
+  GB_PATH_CUDA_CORES = 1,
+  GB_PATH_TENSOR_CORES = 2
+} gb_expert_path;
+int gb_moe_set_expert_path(gb_moe* m, int32_t path);
+
 /* Stage timing for profiling (no counterpart in the reference, whose timing
  * is per generated token, crates/gallium-agent/src/llm_candle.rs:302-345).
  * When enabled, each forward records a CUDA event at every stage boundary on

@@ -156,6 +156,14 @@ int alloc_ws(gb::Moe& m, int64_t T) {
       {(void**)&ws.y, sizeof(float) * (size_t)(T * K * H)},
       {(void**)&ws.x_stage, sizeof(float) * (size_t)(T * H)},
       {(void**)&ws.out_stage, sizeof(float) * (size_t)(T * H)},
+      {(void**)&ws.xh, sizeof(__half) * (size_t)(T * K * H)},
+      {(void**)&ws.xl, sizeof(__half) * (size_t)(T * K * H)},
+      {(void**)&ws.xscale, sizeof(float) * (size_t)(T * K)},
+      {(void**)&ws.hh, sizeof(__half) * (size_t)(T * K * I)},
+      {(void**)&ws.hl, sizeof(__half) * (size_t)(T * K * I)},
+      {(void**)&ws.tile_expert, sizeof(int32_t) * (size_t)(T * K / 128 + E + 1)},
+      {(void**)&ws.tile_row0, sizeof(int32_t) * (size_t)(T * K / 128 + E + 1)},
+      {(void**)&ws.tile_rows, sizeof(int32_t) * (size_t)(T * K / 128 + E + 1)},
   };
   size_t total = 0;
   for (auto& p : pieces) total += (size_t)round_up((int64_t)p.bytes, 256);
@@ -180,6 +188,11 @@ int alloc_ws(gb::Moe& m, int64_t T) {
   ws.bytes = total;
   free_ws(m.ws);
   m.ws = ws;
+  if (gb::tc_supported(m)) {
+    e = gb::tc_make_maps(m);
+    if (e != cudaSuccess) return cuda_err(e, "TMA descriptors for the tensor-core path");
+    m.ws.maps_ok = true;
+  }
   return GB_OK;
 }
 
@@ -214,6 +227,8 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.dn_scales);
   cudaFree(m.w.gu_bias);
   cudaFree(m.w.dn_bias);
+  cudaFree(m.w.gu_rowmax);
+  cudaFree(m.w.dn_rowmax);
   free_ws(m.ws);
   m = gb::Moe{};
 }
@@ -355,12 +370,29 @@ int run_route(gb::Moe& m, const float* x, int64_t T, cudaStream_t st) {
   return mark(m, 2, st);
 }
 
+// Batches of at least this many tokens take the tensor-core expert path.
+constexpr int64_t kTensorCoreMinTokens = 64;
+
+bool use_tensor_cores(const gb::Moe& m, int64_t T) {
+  if (!gb::tc_supported(m) || !m.ws.maps_ok) return false;
+  if (m.expert_path == GB_PATH_TENSOR_CORES) return true;
+  if (m.expert_path == GB_PATH_CUDA_CORES) return false;
+  return T >= kTensorCoreMinTokens;
+}
+
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
   int rc = run_route(m, x, T, st);
   if (rc) return rc;
-  GB_CUDA(gb::launch_gate_up(m, x, T, m.ws, st), "gate_up kernel launch");
-  if ((rc = mark(m, 3, st))) return rc;
-  GB_CUDA(gb::launch_down(m, T, m.ws, st), "down kernel launch");
+  if (use_tensor_cores(m, T)) {
+    GB_CUDA(gb::launch_tc_gate_up(m, x, T, m.ws, st), "tensor-core gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(gb::launch_tc_down(m, T, m.ws, st), "tensor-core down launch");
+    m.launches += 2;  // tile table + split/gather
+  } else {
+    GB_CUDA(gb::launch_gate_up(m, x, T, m.ws, st), "gate_up kernel launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(gb::launch_down(m, T, m.ws, st), "down kernel launch");
+  }
   if ((rc = mark(m, 4, st))) return rc;
   GB_CUDA(gb::launch_combine(m, T, m.ws, out, st), "combine kernel launch");
   m.launches += 3;
@@ -424,6 +456,11 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
     return cuda_err(ce, "query SM count");
   }
   rc = upload_weights(m);
+  if (!rc && desc->act_kind == GB_ACT_GPTOSS_CLAMP && desc->hidden % 64 == 0 &&
+      desc->inter % 64 == 0 && desc->hidden <= 3072 && desc->inter <= 3072) {
+    ce = gb::tc_prepare_weights(m);
+    if (ce != cudaSuccess) rc = cuda_err(ce, "row exponents for the tensor-core path");
+  }
   if (!rc) rc = alloc_ws(m, std::max(1, desc->max_tokens));
   if (rc) {
     release_moe(h->m);
@@ -569,6 +606,18 @@ int gb_moe_destroy(gb_moe* h) {
   if (!h) return GB_OK;
   release_moe(h->m);
   delete h;
+  return GB_OK;
+}
+
+int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  if (path != GB_PATH_AUTO && path != GB_PATH_CUDA_CORES && path != GB_PATH_TENSOR_CORES)
+    return set_err(GB_ERR_INVALID_ARG, "unknown expert path %d", path);
+  if (path == GB_PATH_TENSOR_CORES && !(gb::tc_supported(h->m) && h->m.ws.maps_ok))
+    return set_err(GB_ERR_UNSUPPORTED,
+                   "tensor-core expert path needs the GPT-OSS activation and H, I multiples of 64");
+  h->m.expert_path = path;
   return GB_OK;
 }
 

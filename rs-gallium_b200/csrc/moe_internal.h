@@ -1,6 +1,7 @@
 // moe_internal.h -- state of a gb_moe handle and the kernel launchers.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -30,6 +31,10 @@ struct ExpertWeights {
   uint8_t* dn_scales = nullptr;
   float* gu_bias = nullptr;
   float* dn_bias = nullptr;
+  uint8_t* gu_rowmax = nullptr;  // [E_loc][2I] largest E8M0 byte per row (tensor-core path)
+  uint8_t* dn_rowmax = nullptr;  // [E_loc][H]
+  alignas(64) unsigned char map_gu[128] = {};  // CUtensorMap of gu_blocks (TMA)
+  alignas(64) unsigned char map_dn[128] = {};  // CUtensorMap of dn_blocks
   float zero_scale = 0.0f;
   int sp_h = 0, sp_i = 0;  // padded scale row strides
 };
@@ -53,6 +58,20 @@ struct Workspace {
   float* y = nullptr;          // [T*k, H]
   float* x_stage = nullptr;    // [T, H] host-path staging
   float* out_stage = nullptr;  // [T, H]
+  // tensor-core path
+  __half* xh = nullptr;        // [T*k, H] grouped activation rows, f16 hi
+  __half* xl = nullptr;        // [T*k, H] f16 lo
+  float* xscale = nullptr;     // [T*k] exponent s of each row (x = 2^s (hi + lo))
+  __half* hh = nullptr;        // [T*k, I] SwiGLU output, f16 hi
+  __half* hl = nullptr;        // [T*k, I] f16 lo
+  int32_t* tile_expert = nullptr;  // [T*k/128 + E] N-tile table
+  int32_t* tile_row0 = nullptr;
+  int32_t* tile_rows = nullptr;
+  alignas(64) unsigned char map_xh[128] = {};  // CUtensorMap of xh (TMA)
+  alignas(64) unsigned char map_xl[128] = {};
+  alignas(64) unsigned char map_hh[128] = {};
+  alignas(64) unsigned char map_hl[128] = {};
+  bool maps_ok = false;
 };
 
 struct Moe {
@@ -74,6 +93,7 @@ struct Moe {
   bool profiled_once = false;
   cudaEvent_t ev[kStages + 1] = {};
   int64_t launches = 0;
+  int expert_path = 0;  // gb_expert_path
 };
 
 // Records an error message for gb_last_error() and returns `code`.
@@ -87,6 +107,14 @@ cudaError_t launch_permute(const Moe& m, const int32_t* idx, int64_t T, Workspac
 cudaError_t launch_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
                            cudaStream_t st);
 cudaError_t launch_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+// Tensor-core expert path (tc_gemm.cu).
+bool tc_supported(const Moe& m);
+cudaError_t tc_prepare_weights(Moe& m);
+cudaError_t tc_make_maps(Moe& m);
+cudaError_t launch_tc_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+                              cudaStream_t st);
+cudaError_t launch_tc_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, float* out,
                            cudaStream_t st);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,

@@ -34,6 +34,9 @@ GB_ACT_SILU = 1
 GB_FMT_MXFP4_SPLIT = 0
 GB_FMT_MXFP4_GGUF = 1
 GB_FMT_Q4_K = 2
+GB_PATH_AUTO = 0
+GB_PATH_CUDA_CORES = 1
+GB_PATH_TENSOR_CORES = 2
 GB_DTYPE_F32 = 0
 GB_DTYPE_BF16 = 1
 
@@ -105,6 +108,7 @@ SIGNATURES = {
     "gb_moe_dequant_expert": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "gb_moe_get_info": (c_int, [c_void_p, POINTER(MoeInfo)]),
     "gb_moe_destroy": (c_int, [c_void_p]),
+    "gb_moe_set_expert_path": (c_int, [c_void_p, c_int32]),
     "gb_moe_set_profiling": (c_int, [c_void_p, c_int]),
     "gb_moe_stage_times": (c_int, [c_void_p, POINTER(c_float), c_int32, POINTER(c_int32)]),
     "gb_moe_stage_name": (c_char_p, [c_int32]),

@@ -103,6 +103,12 @@ class MoEBlock:
         """Device pointers straight through to gb_moe_forward (no checks)."""
         check(self._lib.gb_moe_forward(self._h, x_ptr, T, out_ptr, stream))
 
+    def set_expert_path(self, path: str) -> None:
+        """'auto', 'cuda_cores' or 'tensor_cores'."""
+        code = {"auto": _lib.GB_PATH_AUTO, "cuda_cores": _lib.GB_PATH_CUDA_CORES,
+                "tensor_cores": _lib.GB_PATH_TENSOR_CORES}[path]
+        check(self._lib.gb_moe_set_expert_path(self._h, code))
+
     def set_profiling(self, enable: bool = True) -> None:
         check(self._lib.gb_moe_set_profiling(self._h, 1 if enable else 0))
 

@@ -252,3 +252,57 @@ def test_full_size_rows_do_not_depend_on_the_batch(moe32, big_run):
     _, xc, out, _ = big_run
     part = moe32.forward(xc[1000:1037]).cpu().numpy()
     assert_parity(part, out[1000:1037], "sub-batch vs full batch")
+
+
+# ---- tensor-core expert path (tcgen05) ---------------------------------------
+
+@pytest.mark.parametrize("T", [1, 8, 64, 300])
+def test_tensor_core_path_matches_oracle(moe32, layer32, T):
+    x = synth.tokens(T, 2880, seed=500 + T)
+    want, _, _ = oracle.OracleMoe(layer32).forward(x)
+    moe32.set_expert_path("tensor_cores")
+    try:
+        got = moe32.forward(_cuda(x)).cpu().numpy()
+    finally:
+        moe32.set_expert_path("auto")
+    assert_parity(got, want, f"tensor cores T={T}")
+
+
+def test_tensor_core_and_cuda_core_paths_agree(moe32):
+    x = _cuda(synth.tokens(200, 2880, seed=42))
+    moe32.set_expert_path("cuda_cores")
+    a = moe32.forward(x).cpu().numpy()
+    moe32.set_expert_path("tensor_cores")
+    b = moe32.forward(x).cpu().numpy()
+    moe32.set_expert_path("auto")
+    assert_parity(b, a, "tensor vs cuda cores")
+
+
+def test_tensor_core_path_skewed_and_gguf(layer32_skew):
+    gg = synth.gptoss_gguf_from_split(layer32_skew)
+    m = GptOssQMoEFFN.load(gg, device=0, max_tokens=256)
+    try:
+        m.set_expert_path("tensor_cores")
+        x = synth.tokens(256, 2880, seed=8)
+        got = m.forward(_cuda(x)).cpu().numpy()
+        want, _, _ = oracle.OracleMoe(layer32_skew, gguf=gg).forward(x)
+        assert_parity(got, want, "tensor cores, skewed, gguf")
+    finally:
+        m.close()
+
+
+def test_tensor_core_path_handles_large_and_tiny_activations(moe32, layer32):
+    # per-row power-of-two scaling keeps f16 hi/lo in range
+    x = synth.tokens(64, 2880, seed=77)
+    x[0] *= 3.0e4
+    x[1] *= 1.0e-5
+    want, _, _ = oracle.OracleMoe(layer32).forward(x)
+    moe32.set_expert_path("tensor_cores")
+    try:
+        got = moe32.forward(_cuda(x)).cpu().numpy()
+    finally:
+        moe32.set_expert_path("auto")
+    assert_parity(got[2:], want[2:], "tensor cores, ordinary rows")
+    for r in (0, 1):
+        err = np.abs(got[r] - want[r])
+        assert err.sum() / np.abs(want[r]).sum() <= MEAN_REL, r
