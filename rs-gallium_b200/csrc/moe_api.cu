@@ -388,6 +388,10 @@ int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t 
     if ((rc = mark(m, 3, st))) return rc;
     GB_CUDA(gb::launch_tc_down(m, T, m.ws, st), "tensor-core down launch");
     m.launches += 2;  // tile table + split/gather
+  } else if (gb::decode_supported(m)) {
+    GB_CUDA(gb::launch_decode_gate_up(m, x, T, m.ws, st), "decode gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(gb::launch_decode_down(m, T, m.ws, st), "decode down launch");
   } else {
     GB_CUDA(gb::launch_gate_up(m, x, T, m.ws, st), "gate_up kernel launch");
     if ((rc = mark(m, 3, st))) return rc;

@@ -107,6 +107,12 @@ cudaError_t launch_permute(const Moe& m, const int32_t* idx, int64_t T, Workspac
 cudaError_t launch_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
                            cudaStream_t st);
 cudaError_t launch_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+// Decode-sized expert GEMV (decode_gemv.cu); needs H, I multiples of 64.
+bool decode_supported(const Moe& m);
+cudaError_t launch_decode_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+                                  cudaStream_t st);
+cudaError_t launch_decode_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+
 // Tensor-core expert path (tc_gemm.cu).
 bool tc_supported(const Moe& m);
 cudaError_t tc_prepare_weights(Moe& m);

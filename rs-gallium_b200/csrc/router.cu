@@ -22,6 +22,7 @@ namespace gb {
 namespace {
 
 constexpr int kRouterWarps = 8;
+constexpr int kPreloadBlocks = 96;  // H <= 3072 for the preloading variant
 
 template <int TT, int EPW>
 __global__ void __launch_bounds__(kRouterWarps * 32)
@@ -56,17 +57,34 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
 #pragma unroll
     for (int q = 0; q < EPW; ++q) wrow[q] = rw + (int64_t)min(e0 + q, E - 1) * H;
     const int nb = H >> 5;
+    if (EPW == 1 && TT <= 4 && nb <= kPreloadBlocks) {
+      // Decode-sized batches: few warps read the router weight, so issue all
+      // of this lane's loads before the FMA chain (one memory round trip).
+      float wv[kPreloadBlocks];
+#pragma unroll
+      for (int j = 0; j < kPreloadBlocks; ++j)
+        if (j < nb) wv[j] = __ldg(wrow[0] + lane + (j << 5));
+#pragma unroll
+      for (int j = 0; j < kPreloadBlocks; ++j) {
+        if (j < nb) {
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            acc[0][t] = __fmaf_rn(xs[t * H + lane + (j << 5)], wv[j], acc[0][t]);
+        }
+      }
+    } else {
 #pragma unroll 6
-    for (int j = 0; j < nb; ++j) {
-      const int kk = lane + (j << 5);
-      float wv[EPW];
+      for (int j = 0; j < nb; ++j) {
+        const int kk = lane + (j << 5);
+        float wv[EPW];
 #pragma unroll
-      for (int q = 0; q < EPW; ++q) wv[q] = __ldg(wrow[q] + kk);
+        for (int q = 0; q < EPW; ++q) wv[q] = __ldg(wrow[q] + kk);
 #pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        const float xv = xs[t * H + kk];
+        for (int t = 0; t < TT; ++t) {
+          const float xv = xs[t * H + kk];
 #pragma unroll
-        for (int q = 0; q < EPW; ++q) acc[q][t] = __fmaf_rn(xv, wv[q], acc[q][t]);
+          for (int q = 0; q < EPW; ++q) acc[q][t] = __fmaf_rn(xv, wv[q], acc[q][t]);
+        }
       }
     }
 #pragma unroll

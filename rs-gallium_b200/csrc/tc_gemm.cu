@@ -34,6 +34,7 @@
 
 #include "common.cuh"
 #include "moe_internal.h"
+#include "ptx.cuh"
 
 namespace gb {
 namespace tc {
@@ -46,7 +47,6 @@ constexpr int RAW_BYTES = BM * 32;  // one stage of MXFP4 weight bytes (two bloc
 constexpr int kScaleRow = 96;       // E8M0 bytes kept per row (K <= 3072)
 constexpr int kThreads = 320;
 constexpr int kTmemCols = 4 * BN;   // two buffers x (hi, lo) accumulators
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait before giving up
 constexpr size_t kSmemBytes =
     (size_t)STAGES * (STAGE_BYTES + RAW_BYTES) + BM * kScaleRow + 1024 + 256;
 
@@ -75,72 +75,6 @@ struct Args {
   int out_stride;            // I or H
   int* err;                  // error flags (bit 1: wait timed out)
 };
-
-// ---- PTX wrappers ----------------------------------------------------------
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)),
-               "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait.  Returns false if the CTA is aborting or the wait ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag,
-                                          int* err) {
-  if (mbar_try_wait(b, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(b, parity)) {
-    if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitNs) {
-      *abort_flag = 1;
-      atomicOr(err, 2);
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
                                             uint64_t* bar) {
