@@ -18,9 +18,10 @@ Arms:
                      on the host cores, one bounded sample per step.
 
 Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): one process
-per GPU, every rank holds all experts and its own batch of --tokens tokens
-(replicas: the path has no exchange step in this build), timing = max over
-ranks, value = all ranks' tokens / that time (weak scaling).
+per GPU, expert parallel: rank r holds experts [r*E/N, (r+1)*E/N) and its own
+batch of --tokens tokens; routed rows go to the owning rank and back by NCCL
+inside the library.  Timing = max over ranks, value = all ranks' tokens / that
+time (weak scaling).
 """
 from __future__ import annotations
 
@@ -307,7 +308,7 @@ def roofline_for(stage_ms, T, n_touched, layer, peaks):
 
 def run_ours(args, world, rank, local):
     import torch
-    from gallium_b200 import OssMoEFFN, synth
+    from gallium_b200 import OssMoEFFN, nccl_unique_id, synth
     from gallium_b200._lib import check, load_library
 
     lib = load_library()
@@ -315,7 +316,13 @@ def run_ours(args, world, rank, local):
     T = args.tokens
     sweep = [int(s) for s in args.sweep.split(",") if s.strip()] if args.sweep else []
     layer = synth.gptoss_layer(n_experts=args.experts, seed=args.seed, skewed=args.skewed)
-    moe = OssMoEFFN.load(layer, device=local, max_tokens=max([T] + sweep))
+    ep = None
+    if world > 1:
+        import torch.distributed as dist
+        obj = [nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ep = (rank, world, obj[0])
+    moe = OssMoEFFN.load(layer, device=local, max_tokens=max([T] + sweep), ep=ep)
     x = synth.tokens(T, H, seed=args.seed + 1000 * rank)
     xd = torch.from_numpy(x).cuda()
     out = torch.empty_like(xd)
@@ -344,6 +351,13 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     counts = moe.route(xd)["counts"].cpu().numpy()
     n_touched = int((counts > 0).sum())
+    if world > 1:
+        # experts this rank's GPU runs: touched by any rank's tokens, among its own
+        import torch.distributed as dist
+        ct = torch.from_numpy(counts.astype(np.int64)).cuda()
+        dist.all_reduce(ct)
+        lo, hi = rank * args.experts // world, (rank + 1) * args.experts // world
+        n_touched = int((ct[lo:hi] > 0).sum())
 
     # ---- timed region: exactly K steps --------------------------------------
     clocks = ClockSampler(gpu_uuid(local))
@@ -384,6 +398,13 @@ def run_ours(args, world, rank, local):
         for _ in range(2):
             fwd_dev(Ts)
         c = moe.route(xd[:Ts])["counts"].cpu().numpy()
+        if world > 1:
+            import torch.distributed as dist
+            ct = torch.from_numpy(c.astype(np.int64)).cuda()
+            dist.all_reduce(ct)
+            lo, hi = rank * args.experts // world, (rank + 1) * args.experts // world
+            c = np.zeros(args.experts, np.int64)
+            c[lo:hi] = ct[lo:hi].cpu().numpy()
         barrier(world)
         ms = allmax(world, timed(args.steps, Ts, fwd_dev)) / args.steps
         st = stage_profile(moe, xd, out, Ts, flush)
@@ -407,7 +428,8 @@ def run_ours(args, world, rank, local):
             "config": {"workload": f"gpt-oss-120b-shaped MoE layer, E={args.experts}, H=I={H}, "
                                    f"top-{TOPK}, MXFP4, T={T} tokens per GPU",
                        "tokens_per_gpu": T, "experts": args.experts, "skewed": args.skewed,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"ep{world} (expert parallel, {args.experts // world} experts "
+                                       f"per GPU, NCCL dispatch/combine)") if world > 1 else "single GPU",
                        "l2": "flushed (256 MiB write) before every timed step",
                        "experts_touched": n_touched},
             "e2e": e2e,

@@ -62,6 +62,7 @@ def lib() -> ctypes.CDLL:
             "or_permute": (c_int, [P, c_int64, c_int64, c_int64, P, P, P, P]),
             "or_moe_forward": (c_int, [POINTER(OrDesc), P, c_int64, P, P, P, c_int]),
             "or_moe_expert_sample": (c_int64, [POINTER(OrDesc), P, P, P, c_int64, P, c_int]),
+            "or_expert_ffn": (c_int, [POINTER(OrDesc), c_int64, P, c_int64, P]),
             "or_act_gptoss": (c_float, [c_float, c_float, c_float]),
             "or_act_silu": (c_float, [c_float, c_float]),
             "or_last_error": (c_char_p, []),
@@ -225,6 +226,12 @@ class OracleMoe:
         _check(lib().or_moe_forward(ctypes.byref(self.desc), _p(x), T, _p(out), _p(idx), _p(w),
                                     n_threads))
         return out, idx, w
+
+    def expert_ffn(self, expert: int, xs: np.ndarray) -> np.ndarray:
+        xs = np.ascontiguousarray(xs, np.float32)
+        ys = np.empty_like(xs)
+        _check(lib().or_expert_ffn(ctypes.byref(self.desc), expert, _p(xs), xs.shape[0], _p(ys)))
+        return ys
 
     def expert_sample(self, x: np.ndarray, experts, ntok, n_threads: int = 0) -> int:
         x = np.ascontiguousarray(x, np.float32)

@@ -531,6 +531,25 @@ done:
   return rc;
 }
 
+int or_expert_ffn(const or_moe_desc* d, int64_t expert, const float* xs, int64_t n, float* ys) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if (expert < 0 || expert >= d->n_experts) return fail(1, "expert %lld out of range", (long long)expert);
+  const int64_t H = d->hidden, I = d->inter;
+  const int64_t cap = (H > I ? H : I);
+  float* rowbuf = (float*)malloc(sizeof(float) * (size_t)(2 * cap));
+  float* hbuf = (float*)malloc(sizeof(float) * (size_t)((n > 0 ? n : 1) * I));
+  if (!rowbuf || !hbuf) {
+    free(rowbuf);
+    free(hbuf);
+    return fail(7, "out of host memory");
+  }
+  if (n > 0) expert_ffn(d, expert, xs, n, ys, hbuf, rowbuf);
+  free(rowbuf);
+  free(hbuf);
+  return 0;
+}
+
 int64_t or_moe_expert_sample(const or_moe_desc* d, const float* x, const int32_t* experts,
                              const int32_t* ntok, int64_t n_items, float* y_scratch,
                              int n_threads) {

@@ -122,6 +122,10 @@ typedef struct {
 int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out,
                    int32_t* idx, float* w, int n_threads);
 
+/* One expert's FFN (the per-expert closure of gpt_oss_q.rs:194-246) on n
+ * rows xs [n, H] -> ys [n, H]. */
+int or_expert_ffn(const or_moe_desc* d, int64_t expert, const float* xs, int64_t n, float* ys);
+
 /* Bounded CPU baseline: run the expert FFN of or_moe_forward for the given
  * (expert, token-count) work list only (routing excluded), returning the
  * number of token-expert rows processed.  Used to time a sample. */

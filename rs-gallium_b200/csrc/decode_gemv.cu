@@ -50,6 +50,7 @@ struct DecArgs {
   int e_begin;
   int act_kind;
   float limit;
+  const int32_t* out_rows;  // DOWN: output row of each position (null: the position)
   float* out;
   int out_stride;
 };
@@ -188,8 +189,9 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
               y0 = __fadd_rn(y0, a.bias[erow + row]);
               y1 = __fadd_rn(y1, a.bias[erow + row + 1]);
             }
-            a.out[pos * a.out_stride + row] = y0;
-            a.out[pos * a.out_stride + row + 1] = y1;
+            const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
+            a.out[orow * a.out_stride + row] = y0;
+            a.out[orow * a.out_stride + row + 1] = y1;
           }
         }
       }
@@ -198,11 +200,10 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
 }
 
 template <int MODE, int TC>
-cudaError_t launch_dec(const Moe& m, const DecArgs& a, int64_t T, cudaStream_t st) {
-  const int n_local = m.e_end - m.e_begin;
-  const int64_t max_active = std::min<int64_t>(n_local, T * m.desc.top_k);
-  if (max_active <= 0) return cudaSuccess;
-  dim3 grid((unsigned)((a.rows + kRowsPerCta - 1) / kRowsPerCta), (unsigned)max_active);
+cudaError_t launch_dec(const Moe& m, const Groups& g, const DecArgs& a, cudaStream_t st) {
+  (void)m;
+  if (g.max_active <= 0) return cudaSuccess;
+  dim3 grid((unsigned)((a.rows + kRowsPerCta - 1) / kRowsPerCta), (unsigned)g.max_active);
   const size_t smem = (size_t)TC * (a.K / 32) * kBlockPitch * sizeof(float);
   auto kern = decode_rows_kernel<MODE, TC>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -211,16 +212,16 @@ cudaError_t launch_dec(const Moe& m, const DecArgs& a, int64_t T, cudaStream_t s
   return cudaGetLastError();
 }
 
-DecArgs base_args(const Moe& m, Workspace& ws) {
+DecArgs base_args(const Moe& m, const Groups& g) {
   const gb_moe_desc& d = m.desc;
   DecArgs a{};
-  a.top_k = d.top_k;
+  a.top_k = g.perm_div;
   a.zero_scale = m.w.zero_scale;
-  a.counts = ws.counts;
-  a.offsets = ws.offsets;
-  a.active = ws.active;
-  a.meta = ws.meta;
-  a.perm = ws.perm;
+  a.counts = g.counts;
+  a.offsets = g.offsets;
+  a.active = g.active;
+  a.meta = g.meta;
+  a.perm = g.perm;
   a.e_begin = m.e_begin;
   a.act_kind = d.act_kind;
   a.limit = d.swiglu_limit;
@@ -235,10 +236,12 @@ bool decode_supported(const Moe& m) {
   return d.hidden % 64 == 0 && d.inter % 64 == 0 && d.hidden <= 3072 && d.inter <= 3072;
 }
 
-cudaError_t launch_decode_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+// Tokens per expert decide the template: one token shares nothing, so the
+// single-token variant keeps its shared-memory footprint minimal.
+cudaError_t launch_decode_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                   cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  DecArgs a = base_args(m, ws);
+  DecArgs a = base_args(m, g);
   a.in = x;
   a.K = d.hidden;
   a.rows = 2 * d.inter;
@@ -246,24 +249,25 @@ cudaError_t launch_decode_gate_up(const Moe& m, const float* x, int64_t T, Works
   a.scales = m.w.gu_scales;
   a.sp = m.w.sp_h;
   a.bias = m.w.gu_bias;
-  a.out = ws.h;
+  a.out = eb.h;
   a.out_stride = d.inter;
-  return T == 1 ? launch_dec<GATE_UP, 1>(m, a, T, st) : launch_dec<GATE_UP, 4>(m, a, T, st);
+  return g.max_per_expert <= 1 ? launch_dec<GATE_UP, 1>(m, g, a, st) : launch_dec<GATE_UP, 4>(m, g, a, st);
 }
 
-cudaError_t launch_decode_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st) {
+cudaError_t launch_decode_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  DecArgs a = base_args(m, ws);
-  a.in = ws.h;
+  DecArgs a = base_args(m, g);
+  a.in = eb.h;
   a.K = d.inter;
   a.rows = d.hidden;
   a.blocks = m.w.dn_blocks;
   a.scales = m.w.dn_scales;
   a.sp = m.w.sp_i;
   a.bias = m.w.dn_bias;
-  a.out = ws.y;
+  a.out_rows = g.out_rows;
+  a.out = eb.y;
   a.out_stride = d.hidden;
-  return T == 1 ? launch_dec<DOWN, 1>(m, a, T, st) : launch_dec<DOWN, 4>(m, a, T, st);
+  return g.max_per_expert <= 1 ? launch_dec<DOWN, 1>(m, g, a, st) : launch_dec<DOWN, 4>(m, g, a, st);
 }
 
 }  // namespace gb

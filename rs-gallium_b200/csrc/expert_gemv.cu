@@ -34,7 +34,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                        const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
                        const int32_t* __restrict__ active, const int32_t* __restrict__ meta,
                        const int32_t* __restrict__ perm, int e_begin, int act_kind, float limit,
-                       float* __restrict__ out, int out_stride) {
+                       const int32_t* __restrict__ out_rows, float* __restrict__ out,
+                       int out_stride) {
   extern __shared__ float xs[];  // [TC][33 * NB], element k at k + k/32
   const int slot = blockIdx.y;
   if (slot >= meta[0]) return;
@@ -143,8 +144,9 @@ __global__ void __launch_bounds__(kWarps * 32)
             y0 = __fadd_rn(y0, bias[(int64_t)le * n_rows_total + row0]);
             if (valid1) y1 = __fadd_rn(y1, bias[(int64_t)le * n_rows_total + row0 + 1]);
           }
-          out[pos * out_stride + row0] = y0;
-          if (valid1) out[pos * out_stride + row0 + 1] = y1;
+          const int64_t orow = out_rows ? out_rows[pos] : pos;
+          out[orow * out_stride + row0] = y0;
+          if (valid1) out[orow * out_stride + row0 + 1] = y1;
         }
       }
     }
@@ -152,17 +154,15 @@ __global__ void __launch_bounds__(kWarps * 32)
 }
 
 template <int MODE, int TC>
-cudaError_t launch_rows(const Moe& m, const float* in, int K_in, int n_rows_total, const uint8_t* blocks,
-                        const uint8_t* scales, int sp, const float* bias, int64_t T, Workspace& ws,
+cudaError_t launch_rows(const Moe& m, const Groups& g, const float* in, int K_in, int n_rows_total,
+                        const uint8_t* blocks, const uint8_t* scales, int sp, const float* bias,
                         float* out, int out_stride, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
   const int NB = K_in / 32;
   const int nbq = (NB + 31) / 32;
-  const int n_local = m.e_end - m.e_begin;
-  const int64_t max_active = std::min<int64_t>(n_local, T * d.top_k);
-  if (max_active <= 0) return cudaSuccess;
+  if (g.max_active <= 0) return cudaSuccess;
   const int pairs = (n_rows_total + 1) / 2;
-  dim3 grid((unsigned)((pairs + kWarps - 1) / kWarps), (unsigned)max_active);
+  dim3 grid((unsigned)((pairs + kWarps - 1) / kWarps), (unsigned)g.max_active);
   const size_t smem = (size_t)TC * 33 * NB * sizeof(float);
   cudaError_t err = cudaSuccess;
 #define GB_LAUNCH_NBQ(Q)                                                                         \
@@ -170,10 +170,10 @@ cudaError_t launch_rows(const Moe& m, const float* in, int K_in, int n_rows_tota
     auto kern = expert_rows_kernel<MODE, TC, Q>;                                                 \
     err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
     if (err != cudaSuccess) return err;                                                          \
-    kern<<<grid, kWarps * 32, smem, st>>>(in, K_in, n_rows_total, d.top_k, blocks, scales, sp,   \
-                                          bias, m.w.zero_scale, ws.counts, ws.offsets, ws.active, \
-                                          ws.meta, ws.perm, m.e_begin, d.act_kind,               \
-                                          d.swiglu_limit, out, out_stride);                      \
+    kern<<<grid, kWarps * 32, smem, st>>>(in, K_in, n_rows_total, g.perm_div, blocks, scales, sp, \
+                                          bias, m.w.zero_scale, g.counts, g.offsets, g.active,   \
+                                          g.meta, g.perm, m.e_begin, d.act_kind, d.swiglu_limit, \
+                                          MODE == DOWN ? g.out_rows : nullptr, out, out_stride); \
   }
   switch (nbq) {
     case 1: GB_LAUNCH_NBQ(1) break;
@@ -267,26 +267,26 @@ __global__ void gguf_to_split_kernel(const uint8_t* __restrict__ raw, int64_t ro
 
 }  // namespace
 
-cudaError_t launch_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+cudaError_t launch_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                            cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  return launch_rows<GATE_UP, 8>(m, x, d.hidden, 2 * d.inter, m.w.gu_blocks, m.w.gu_scales,
-                                 m.w.sp_h, m.w.gu_bias, T, ws, ws.h, d.inter, st);
+  return launch_rows<GATE_UP, 8>(m, g, x, d.hidden, 2 * d.inter, m.w.gu_blocks, m.w.gu_scales,
+                                 m.w.sp_h, m.w.gu_bias, eb.h, d.inter, st);
 }
 
-cudaError_t launch_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st) {
+cudaError_t launch_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  return launch_rows<DOWN, 8>(m, ws.h, d.inter, d.hidden, m.w.dn_blocks, m.w.dn_scales, m.w.sp_i,
-                              m.w.dn_bias, T, ws, ws.y, d.hidden, st);
+  return launch_rows<DOWN, 8>(m, g, eb.h, d.inter, d.hidden, m.w.dn_blocks, m.w.dn_scales,
+                              m.w.sp_i, m.w.dn_bias, eb.y, d.hidden, st);
 }
 
-cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, float* out,
+cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
                            cudaStream_t st) {
   const int H = m.desc.hidden;
   const int threads = 256;
   dim3 grid((unsigned)T, (unsigned)((H / 4 + threads - 1) / threads));
   const int expert_order = m.desc.weight_format != GB_FMT_MXFP4_SPLIT;
-  combine_kernel<<<grid, threads, 0, st>>>(ws.y, ws.inv, ws.wts, ws.idx, H, m.desc.top_k,
+  combine_kernel<<<grid, threads, 0, st>>>(y, ws.inv, ws.wts, ws.idx, H, m.desc.top_k,
                                            expert_order, out);
   return cudaGetLastError();
 }

@@ -8,6 +8,7 @@
 
 #include <algorithm>
 #include <new>
+#include <string>
 #include <vector>
 
 #include "moe_internal.h"
@@ -119,26 +120,55 @@ int validate(const gb_moe_desc* d) {
     if (d->n_experts % d->ep_size != 0)
       return set_err(GB_ERR_INVALID_ARG, "n_experts %d not divisible by ep_size %d", d->n_experts,
                      d->ep_size);
-    return set_err(GB_ERR_UNSUPPORTED, "expert parallelism is not implemented in this build");
+    if (!d->nccl_id) return set_err(GB_ERR_INVALID_ARG, "ep_size > 1 needs nccl_id");
   }
   if (d->max_tokens < 0) return set_err(GB_ERR_INVALID_ARG, "max_tokens %d < 0", d->max_tokens);
   return GB_OK;
 }
 
 void free_ws(gb::Workspace& ws) {
+  gb::free_expert_bufs(ws.eb);
   if (ws.base) cudaFree(ws.base);
   ws = gb::Workspace{};
 }
 
-// Carve the workspace for T tokens out of one allocation (256-byte aligned pieces).
+struct Piece {
+  void** ptr;
+  size_t bytes;
+};
+
+// One allocation carved into 256-byte aligned pieces, zero-filled.
+template <size_t N>
+int carve(Piece (&pieces)[N], void** base_out, size_t* bytes_out, const char* what) {
+  size_t total = 0;
+  for (auto& p : pieces) total += (size_t)round_up((int64_t)p.bytes, 256);
+  void* base = nullptr;
+  cudaError_t e = cudaMalloc(&base, total);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(GB_ERR_NO_MEMORY, "%s: %zu bytes: %s", what, total, cudaGetErrorString(e));
+  }
+  e = cudaMemset(base, 0, total);
+  if (e != cudaSuccess) {
+    cudaFree(base);
+    return cuda_err(e, what);
+  }
+  size_t off = 0;
+  for (auto& p : pieces) {
+    *p.ptr = p.bytes ? static_cast<char*>(base) + off : nullptr;
+    off += (size_t)round_up((int64_t)p.bytes, 256);
+  }
+  *base_out = base;
+  *bytes_out = total;
+  return GB_OK;
+}
+
+// Routing workspace for T local tokens, plus the single-GPU expert buffers.
 int alloc_ws(gb::Moe& m, int64_t T) {
   const gb_moe_desc& d = m.desc;
-  const int64_t E = d.n_experts, K = d.top_k, H = d.hidden, I = d.inter;
+  const int64_t E = d.n_experts, K = d.top_k, H = d.hidden;
   T = std::max<int64_t>(T, 1);
-  struct Piece {
-    void** ptr;
-    size_t bytes;
-  };
+  const bool ep = m.ep_size > 1;
   gb::Workspace ws;
   ws.tokens = T;
   Piece pieces[] = {
@@ -152,47 +182,23 @@ int alloc_ws(gb::Moe& m, int64_t T) {
       {(void**)&ws.meta, sizeof(int32_t) * 4},
       {(void**)&ws.perm, sizeof(int32_t) * (size_t)(T * K)},
       {(void**)&ws.inv, sizeof(int32_t) * (size_t)(T * K)},
-      {(void**)&ws.h, sizeof(float) * (size_t)(T * K * I)},
-      {(void**)&ws.y, sizeof(float) * (size_t)(T * K * H)},
       {(void**)&ws.x_stage, sizeof(float) * (size_t)(T * H)},
       {(void**)&ws.out_stage, sizeof(float) * (size_t)(T * H)},
-      {(void**)&ws.xh, sizeof(__half) * (size_t)(T * K * H)},
-      {(void**)&ws.xl, sizeof(__half) * (size_t)(T * K * H)},
-      {(void**)&ws.xscale, sizeof(float) * (size_t)(T * K)},
-      {(void**)&ws.hh, sizeof(__half) * (size_t)(T * K * I)},
-      {(void**)&ws.hl, sizeof(__half) * (size_t)(T * K * I)},
-      {(void**)&ws.tile_expert, sizeof(int32_t) * (size_t)(T * K / 128 + E + 1)},
-      {(void**)&ws.tile_row0, sizeof(int32_t) * (size_t)(T * K / 128 + E + 1)},
-      {(void**)&ws.tile_rows, sizeof(int32_t) * (size_t)(T * K / 128 + E + 1)},
+      {(void**)&ws.y_back, ep ? sizeof(float) * (size_t)(T * K * H) : 0},
+      {(void**)&ws.send_x, ep ? sizeof(float) * (size_t)(T * K * H) : 0},
   };
-  size_t total = 0;
-  for (auto& p : pieces) total += (size_t)round_up((int64_t)p.bytes, 256);
   void* base = nullptr;
-  cudaError_t e = cudaMalloc(&base, total);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return set_err(GB_ERR_NO_MEMORY, "workspace of %zu bytes for %lld tokens: %s", total,
-                   (long long)T, cudaGetErrorString(e));
-  }
-  e = cudaMemset(base, 0, total);
-  if (e != cudaSuccess) {
-    cudaFree(base);
-    return cuda_err(e, "workspace memset");
-  }
-  size_t off = 0;
-  for (auto& p : pieces) {
-    *p.ptr = static_cast<char*>(base) + off;
-    off += (size_t)round_up((int64_t)p.bytes, 256);
-  }
+  size_t bytes = 0;
+  int rc = carve(pieces, &base, &bytes, "routing workspace");
+  if (rc) return rc;
   ws.base = base;
-  ws.bytes = total;
+  ws.bytes = bytes;
+  if (!ep && (rc = gb::alloc_expert_bufs(m, ws.eb, T * K))) {
+    cudaFree(base);
+    return rc;
+  }
   free_ws(m.ws);
   m.ws = ws;
-  if (gb::tc_supported(m)) {
-    e = gb::tc_make_maps(m);
-    if (e != cudaSuccess) return cuda_err(e, "TMA descriptors for the tensor-core path");
-    m.ws.maps_ok = true;
-  }
   return GB_OK;
 }
 
@@ -230,6 +236,7 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.gu_rowmax);
   cudaFree(m.w.dn_rowmax);
   free_ws(m.ws);
+  gb::ep_destroy(m);
   m = gb::Moe{};
 }
 
@@ -355,10 +362,7 @@ int upload_weights(gb::Moe& m) {
 }
 
 // Stage boundary: record event i when profiling.
-int mark(gb::Moe& m, int i, cudaStream_t st) {
-  if (m.profiling) GB_CUDA(cudaEventRecord(m.ev[i], st), "record stage event");
-  return GB_OK;
-}
+int mark(gb::Moe& m, int i, cudaStream_t st) { return gb::mark_stage(m, i, st); }
 
 int run_route(gb::Moe& m, const float* x, int64_t T, cudaStream_t st) {
   int rc;
@@ -370,40 +374,86 @@ int run_route(gb::Moe& m, const float* x, int64_t T, cudaStream_t st) {
   return mark(m, 2, st);
 }
 
-// Batches of at least this many tokens take the tensor-core expert path.
-constexpr int64_t kTensorCoreMinTokens = 64;
+// Grouped batches of at least this many rows (64 tokens at top-4) take the
+// tensor-core expert path; smaller ones the decode GEMV.
+constexpr int64_t kTensorCoreMinRows = 256;
 
-bool use_tensor_cores(const gb::Moe& m, int64_t T) {
-  if (!gb::tc_supported(m) || !m.ws.maps_ok) return false;
+bool use_tensor_cores(const gb::Moe& m, const gb::ExpertBufs& eb, int64_t rows) {
+  if (!gb::tc_supported(m) || !eb.maps_ok) return false;
   if (m.expert_path == GB_PATH_TENSOR_CORES) return true;
   if (m.expert_path == GB_PATH_CUDA_CORES) return false;
-  return T >= kTensorCoreMinTokens;
+  return rows >= kTensorCoreMinRows;
+}
+
+gb::Groups local_groups(const gb::Moe& m, int64_t T) {
+  gb::Groups g;
+  g.counts = m.ws.counts;
+  g.offsets = m.ws.offsets;
+  g.active = m.ws.active;
+  g.meta = m.ws.meta;
+  g.perm = m.ws.perm;
+  g.perm_div = m.desc.top_k;
+  g.rows = T * m.desc.top_k;
+  g.max_active = (int)std::min<int64_t>(m.e_end - m.e_begin, T * m.desc.top_k);
+  g.max_per_expert = T;
+  g.out_rows = nullptr;
+  return g;
 }
 
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
-  int rc = run_route(m, x, T, st);
-  if (rc) return rc;
-  if (use_tensor_cores(m, T)) {
-    GB_CUDA(gb::launch_tc_gate_up(m, x, T, m.ws, st), "tensor-core gate_up launch");
-    if ((rc = mark(m, 3, st))) return rc;
-    GB_CUDA(gb::launch_tc_down(m, T, m.ws, st), "tensor-core down launch");
-    m.launches += 2;  // tile table + split/gather
-  } else if (gb::decode_supported(m)) {
-    GB_CUDA(gb::launch_decode_gate_up(m, x, T, m.ws, st), "decode gate_up launch");
-    if ((rc = mark(m, 3, st))) return rc;
-    GB_CUDA(gb::launch_decode_down(m, T, m.ws, st), "decode down launch");
+  int rc;
+  if (T > 0) {
+    if ((rc = run_route(m, x, T, st))) return rc;
   } else {
-    GB_CUDA(gb::launch_gate_up(m, x, T, m.ws, st), "gate_up kernel launch");
-    if ((rc = mark(m, 3, st))) return rc;
-    GB_CUDA(gb::launch_down(m, T, m.ws, st), "down kernel launch");
+    GB_CUDA(cudaMemsetAsync(m.ws.counts, 0, sizeof(int32_t) * m.desc.n_experts, st),
+            "clear counts");
   }
+  if (m.ep_size > 1) {
+    if ((rc = gb::ep_forward(m, x, T, out, st))) return rc;
+    if ((rc = mark(m, 5, st))) return rc;
+    m.profiled_once = m.profiling;
+    return GB_OK;
+  }
+  gb::Groups g = local_groups(m, T);
+  if ((rc = gb::run_experts(m, g, x, T, m.ws.eb, st))) return rc;
   if ((rc = mark(m, 4, st))) return rc;
-  GB_CUDA(gb::launch_combine(m, T, m.ws, out, st), "combine kernel launch");
-  m.launches += 3;
+  GB_CUDA(gb::launch_combine(m, T, m.ws, m.ws.eb.y, out, st), "combine kernel launch");
+  m.launches += 1;
   if ((rc = mark(m, 5, st))) return rc;
   m.profiled_once = m.profiling;
   return GB_OK;
 }
+
+}  // namespace
+
+namespace gb {
+
+int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& eb,
+                cudaStream_t st) {
+  int rc;
+  (void)T;
+  if (use_tensor_cores(m, eb, g.rows)) {
+    GB_CUDA(launch_tc_gate_up(m, g, x, eb, st), "tensor-core gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(launch_tc_down(m, g, eb, st), "tensor-core down launch");
+    m.launches += 4;  // tile table, split/gather, two GEMMs
+  } else if (decode_supported(m)) {
+    GB_CUDA(launch_decode_gate_up(m, g, x, eb, st), "decode gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(launch_decode_down(m, g, eb, st), "decode down launch");
+    m.launches += 2;
+  } else {
+    GB_CUDA(launch_gate_up(m, g, x, eb, st), "gate_up kernel launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(launch_down(m, g, eb, st), "down kernel launch");
+    m.launches += 2;
+  }
+  return GB_OK;
+}
+
+}  // namespace gb
+
+namespace {
 
 int check_handle(gb_moe* h) {
   if (!h) return set_err(GB_ERR_INVALID_ARG, "handle is null");
@@ -420,6 +470,54 @@ int set_error(int code, const char* fmt, ...) {
   va_end(ap);
   return code;
 }
+}  // namespace gb
+
+namespace gb {
+
+int mark_stage(Moe& m, int i, cudaStream_t st) {
+  if (m.profiling) GB_CUDA(cudaEventRecord(m.ev[i], st), "record stage event");
+  return GB_OK;
+}
+
+void free_expert_bufs(ExpertBufs& eb) {
+  if (eb.base) cudaFree(eb.base);
+  eb = ExpertBufs{};
+}
+
+int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
+  const gb_moe_desc& d = m.desc;
+  const int64_t E = d.n_experts, H = d.hidden, I = d.inter;
+  rows = std::max<int64_t>(rows, 1);
+  const bool tc = tc_supported(m);
+  ExpertBufs nb;
+  nb.rows_cap = rows;
+  Piece pieces[] = {
+      {(void**)&nb.h, sizeof(float) * (size_t)(rows * I)},
+      {(void**)&nb.y, sizeof(float) * (size_t)(rows * H)},
+      {(void**)&nb.xh, tc ? sizeof(__half) * (size_t)(rows * H) : 0},
+      {(void**)&nb.xl, tc ? sizeof(__half) * (size_t)(rows * H) : 0},
+      {(void**)&nb.xscale, tc ? sizeof(float) * (size_t)rows : 0},
+      {(void**)&nb.hh, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
+      {(void**)&nb.hl, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
+      {(void**)&nb.tile_expert, sizeof(int32_t) * (size_t)(rows / 128 + E + 1)},
+      {(void**)&nb.tile_row0, sizeof(int32_t) * (size_t)(rows / 128 + E + 1)},
+      {(void**)&nb.tile_rows, sizeof(int32_t) * (size_t)(rows / 128 + E + 1)},
+  };
+  int rc = carve(pieces, &nb.base, &nb.bytes, "expert buffers");
+  if (rc) return rc;
+  if (tc) {
+    cudaError_t e = tc_make_maps(m, nb);
+    if (e != cudaSuccess) {
+      cudaFree(nb.base);
+      return cuda_err(e, "TMA descriptors for the tensor-core path");
+    }
+    nb.maps_ok = true;
+  }
+  free_expert_bufs(eb);
+  eb = nb;
+  return GB_OK;
+}
+
 }  // namespace gb
 
 struct gb_moe {
@@ -459,7 +557,8 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
     delete h;
     return cuda_err(ce, "query SM count");
   }
-  rc = upload_weights(m);
+  if (m.ep_size > 1) rc = gb::ep_init(m, desc->nccl_id);
+  if (!rc) rc = upload_weights(m);
   if (!rc && desc->act_kind == GB_ACT_GPTOSS_CLAMP && desc->hidden % 64 == 0 &&
       desc->inter % 64 == 0 && desc->hidden <= 3072 && desc->inter <= 3072) {
     ce = gb::tc_prepare_weights(m);
@@ -467,8 +566,10 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
   }
   if (!rc) rc = alloc_ws(m, std::max(1, desc->max_tokens));
   if (rc) {
+    const std::string msg = g_err;  // release must not overwrite the cause
     release_moe(h->m);
     delete h;
+    snprintf(g_err, sizeof g_err, "%s", msg.c_str());
     return rc;
   }
   *out = h;
@@ -479,8 +580,9 @@ int gb_moe_forward(gb_moe* h, const float* x_dev, int64_t T, float* out_dev, voi
   int rc = check_handle(h);
   if (rc) return rc;
   if (T < 0) return set_err(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
-  if (T == 0) return GB_OK;
-  if (!x_dev || !out_dev) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
+  // With expert parallelism every rank joins the exchanges, even with no tokens.
+  if (T == 0 && h->m.ep_size == 1) return GB_OK;
+  if (T > 0 && (!x_dev || !out_dev)) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
   if (T > (int64_t)1 << 24) return set_err(GB_ERR_UNSUPPORTED, "T = %lld too large", (long long)T);
   gb::Moe& m = h->m;
   DeviceScope ds(m.device);
@@ -494,17 +596,19 @@ int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_ho
   int rc = check_handle(h);
   if (rc) return rc;
   if (T < 0) return set_err(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
-  if (T == 0) return GB_OK;
-  if (!x_host || !out_host) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
+  if (T == 0 && h->m.ep_size == 1) return GB_OK;
+  if (T > 0 && (!x_host || !out_host)) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
   gb::Moe& m = h->m;
   DeviceScope ds(m.device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = ensure_ws(m, T, st))) return rc;
   const size_t bytes = sizeof(float) * (size_t)(T * m.desc.hidden);
-  GB_CUDA(cudaMemcpyAsync(m.ws.x_stage, x_host, bytes, cudaMemcpyHostToDevice, st), "copy x in");
+  if (bytes)
+    GB_CUDA(cudaMemcpyAsync(m.ws.x_stage, x_host, bytes, cudaMemcpyHostToDevice, st), "copy x in");
   if ((rc = run_forward(m, m.ws.x_stage, T, m.ws.out_stage, st))) return rc;
-  GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
-          "copy out");
+  if (bytes)
+    GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
+            "copy out");
   GB_CUDA(cudaStreamSynchronize(st), "synchronise forward");
   return GB_OK;
 }
@@ -618,7 +722,7 @@ int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
   if (rc) return rc;
   if (path != GB_PATH_AUTO && path != GB_PATH_CUDA_CORES && path != GB_PATH_TENSOR_CORES)
     return set_err(GB_ERR_INVALID_ARG, "unknown expert path %d", path);
-  if (path == GB_PATH_TENSOR_CORES && !(gb::tc_supported(h->m) && h->m.ws.maps_ok))
+  if (path == GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m))
     return set_err(GB_ERR_UNSUPPORTED,
                    "tensor-core expert path needs the GPT-OSS activation and H, I multiples of 64");
   h->m.expert_path = path;
@@ -626,8 +730,8 @@ int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
 }
 
 int gb_nccl_unique_id(uint8_t out[128]) {
-  (void)out;
-  return set_err(GB_ERR_UNSUPPORTED, "expert parallelism is not implemented in this build");
+  if (!out) return set_err(GB_ERR_INVALID_ARG, "out is null");
+  return gb::nccl_unique_id(out);
 }
 
 }  // extern "C"

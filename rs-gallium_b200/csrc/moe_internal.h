@@ -39,7 +39,44 @@ struct ExpertWeights {
   int sp_h = 0, sp_i = 0;  // padded scale row strides
 };
 
-// Per-forward scratch, sized for `tokens` tokens.
+// The grouped view the expert kernels work on: rows grouped by expert
+// (expert ascending), each group a contiguous range of positions.
+struct Groups {
+  const int32_t* counts = nullptr;    // [E] rows per (global) expert id
+  const int32_t* offsets = nullptr;   // [E+1] first position of each expert
+  const int32_t* active = nullptr;    // local experts with rows (global ids), ascending
+  int32_t* meta = nullptr;            // [0] active count, [1] error bits, [2] N tiles
+  const int32_t* perm = nullptr;      // position -> input row * perm_div (+ slot)
+  int perm_div = 1;
+  int64_t rows = 0;                   // positions in use this forward (upper bound)
+  int max_active = 0;                 // bound on the active count (grid size)
+  int64_t max_per_expert = 0;         // bound on the rows of one expert
+  const int32_t* out_rows = nullptr;  // output row of position p for DOWN (null: p)
+};
+
+// Buffers indexed by grouped position, sized for rows_cap positions.
+struct ExpertBufs {
+  int64_t rows_cap = 0;
+  size_t bytes = 0;
+  void* base = nullptr;
+  float* h = nullptr;          // [rows, I] SwiGLU output (CUDA-core paths)
+  float* y = nullptr;          // [rows, H] expert outputs (row = out_rows[p] or p)
+  __half* xh = nullptr;        // [rows, H] grouped activation rows, f16 hi (tensor cores)
+  __half* xl = nullptr;        // [rows, H] f16 lo
+  float* xscale = nullptr;     // [rows] exponent s of each row (x = 2^s (hi + lo))
+  __half* hh = nullptr;        // [rows, I] SwiGLU output, f16 hi
+  __half* hl = nullptr;        // [rows, I] f16 lo
+  int32_t* tile_expert = nullptr;  // [rows/128 + E] N-tile table
+  int32_t* tile_row0 = nullptr;
+  int32_t* tile_rows = nullptr;
+  alignas(64) unsigned char map_xh[128] = {};  // CUtensorMap of xh (TMA)
+  alignas(64) unsigned char map_xl[128] = {};
+  alignas(64) unsigned char map_hh[128] = {};
+  alignas(64) unsigned char map_hl[128] = {};
+  bool maps_ok = false;
+};
+
+// Per-forward routing scratch, sized for `tokens` local tokens.
 struct Workspace {
   int64_t tokens = 0;
   size_t bytes = 0;
@@ -50,28 +87,15 @@ struct Workspace {
   float* wts = nullptr;        // [T*k]
   int32_t* counts = nullptr;   // [E]
   int32_t* offsets = nullptr;  // [E+1]
-  int32_t* active = nullptr;   // [E] active expert ids, ascending
-  int32_t* meta = nullptr;     // [0] = number of active experts, [1] = error flags
+  int32_t* active = nullptr;   // [E] active local expert ids, ascending
+  int32_t* meta = nullptr;     // [0] active count, [1] error flags, [2] N tiles
   int32_t* perm = nullptr;     // [T*k]
   int32_t* inv = nullptr;      // [T*k]
-  float* h = nullptr;          // [T*k, I]
-  float* y = nullptr;          // [T*k, H]
   float* x_stage = nullptr;    // [T, H] host-path staging
   float* out_stage = nullptr;  // [T, H]
-  // tensor-core path
-  __half* xh = nullptr;        // [T*k, H] grouped activation rows, f16 hi
-  __half* xl = nullptr;        // [T*k, H] f16 lo
-  float* xscale = nullptr;     // [T*k] exponent s of each row (x = 2^s (hi + lo))
-  __half* hh = nullptr;        // [T*k, I] SwiGLU output, f16 hi
-  __half* hl = nullptr;        // [T*k, I] f16 lo
-  int32_t* tile_expert = nullptr;  // [T*k/128 + E] N-tile table
-  int32_t* tile_row0 = nullptr;
-  int32_t* tile_rows = nullptr;
-  alignas(64) unsigned char map_xh[128] = {};  // CUtensorMap of xh (TMA)
-  alignas(64) unsigned char map_xl[128] = {};
-  alignas(64) unsigned char map_hh[128] = {};
-  alignas(64) unsigned char map_hl[128] = {};
-  bool maps_ok = false;
+  float* y_back = nullptr;     // [T*k, H] expert outputs returned to this rank (expert parallel)
+  float* send_x = nullptr;     // [T*k, H] activation rows in grouped order (expert parallel)
+  ExpertBufs eb;               // single GPU: T*k positions
 };
 
 struct Moe {
@@ -87,6 +111,7 @@ struct Moe {
   ExpertWeights w;
   int64_t weight_bytes = 0;
   Workspace ws;
+  struct Ep* ep = nullptr;  // expert-parallel state (ep_size > 1), ep.cu
   // profiling: events at the stage boundaries of the last forward
   static constexpr int kStages = 5;  // router, permute, gate_up, down, combine
   bool profiling = false;
@@ -99,34 +124,57 @@ struct Moe {
 // Records an error message for gb_last_error() and returns `code`.
 int set_error(int code, const char* fmt, ...);
 
-// Launchers (router.cu, permute.cu, expert_gemv.cu).  All asynchronous.
+// Records stage boundary event i on `st` when profiling is on.
+int mark_stage(Moe& m, int i, cudaStream_t st);
+
+// Launchers.  All asynchronous on `st`.
 cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
                                cudaStream_t st);
 cudaError_t launch_permute(const Moe& m, const int32_t* idx, int64_t T, Workspace& ws,
                            cudaStream_t st);
-cudaError_t launch_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+
+// CUDA-core expert kernels, any shape (expert_gemv.cu).
+cudaError_t launch_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                            cudaStream_t st);
-cudaError_t launch_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+cudaError_t launch_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
 // Decode-sized expert GEMV (decode_gemv.cu); needs H, I multiples of 64.
 bool decode_supported(const Moe& m);
-cudaError_t launch_decode_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+cudaError_t launch_decode_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                   cudaStream_t st);
-cudaError_t launch_decode_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+cudaError_t launch_decode_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
 
 // Tensor-core expert path (tc_gemm.cu).
 bool tc_supported(const Moe& m);
 cudaError_t tc_prepare_weights(Moe& m);
-cudaError_t tc_make_maps(Moe& m);
-cudaError_t launch_tc_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+cudaError_t tc_make_maps(const Moe& m, ExpertBufs& eb);
+cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               cudaStream_t st);
-cudaError_t launch_tc_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st);
+cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
 
-cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, float* out,
+// out[t] = sum_r w[t, r] * y[inv[t*k + r]] in the fixed order (expert_gemv.cu).
+cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
                            cudaStream_t st);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
                                   cudaStream_t st);
 cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,
                                  int64_t row_stride_blocks, uint8_t* scales_dev,
                                  int64_t row_stride_scales, cudaStream_t st);
+
+// Expert parallelism (ep.cu).
+struct Ep;
+int nccl_unique_id(uint8_t out[128]);
+int ep_init(Moe& m, const uint8_t* nccl_id);
+void ep_destroy(Moe& m);
+int ep_forward(Moe& m, const float* x, int64_t T, float* out, cudaStream_t st);
+
+// Allocates the grouped-position buffers for `rows` positions (and their TMA
+// descriptors when the tensor-core path applies); frees the previous ones.
+int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows);
+void free_expert_bufs(ExpertBufs& eb);
+
+// Runs the expert products for a grouped view, choosing the kernels for T
+// (local tokens) and the handle's expert path.  Returns a gb_status.
+int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& eb,
+                cudaStream_t st);
 
 }  // namespace gb

@@ -71,7 +71,8 @@ struct Args {
   float limit;               // SwiGLU clamp
   __half* out_hi;            // GATE_UP: h hi [positions][I]
   __half* out_lo;            // GATE_UP: h lo
-  float* out_y;              // DOWN: y [positions][H]
+  float* out_y;              // DOWN: y [rows][H], row = out_rows[position] (or position)
+  const int32_t* out_rows;
   int out_stride;            // I or H
   int* err;                  // error flags (bit 1: wait timed out)
 };
@@ -396,7 +397,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               a.out_lo[o] = lo;
             }
           } else {
-            if (valid && n < it.nrows) a.out_y[pos * a.out_stride + row] = val;
+            if (valid && n < it.nrows) {
+              const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
+              a.out_y[orow * a.out_stride + row] = val;
+            }
           }
         }
       }
@@ -557,44 +561,42 @@ cudaError_t tc_prepare_weights(Moe& m) {
   return cudaDeviceSynchronize();
 }
 
-cudaError_t tc_make_maps(Moe& m) {
+cudaError_t tc_make_maps(const Moe& m, ExpertBufs& eb) {
   auto encode = tc::get_encode();
   if (!encode) return cudaErrorNotSupported;
   const gb_moe_desc& d = m.desc;
-  const uint64_t rows = (uint64_t)m.ws.tokens * d.top_k;
-  auto make = [&](CUtensorMap* map, void* base, uint64_t K) -> cudaError_t {
+  const uint64_t rows = (uint64_t)eb.rows_cap;
+  auto make = [&](void* map, void* base, uint64_t K) -> cudaError_t {
     cuuint64_t dims[2] = {K, rows};
     cuuint64_t strides[1] = {K * 2};
     cuuint32_t box[2] = {tc::BK, tc::BN};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode(reinterpret_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
   };
   cudaError_t e;
-  if ((e = make(reinterpret_cast<CUtensorMap*>(m.ws.map_xh), m.ws.xh, d.hidden)) != cudaSuccess)
-    return e;
-  if ((e = make(reinterpret_cast<CUtensorMap*>(m.ws.map_xl), m.ws.xl, d.hidden)) != cudaSuccess)
-    return e;
-  if ((e = make(reinterpret_cast<CUtensorMap*>(m.ws.map_hh), m.ws.hh, d.inter)) != cudaSuccess)
-    return e;
-  return make(reinterpret_cast<CUtensorMap*>(m.ws.map_hl), m.ws.hl, d.inter);
+  if ((e = make(eb.map_xh, eb.xh, d.hidden)) != cudaSuccess) return e;
+  if ((e = make(eb.map_xl, eb.xl, d.hidden)) != cudaSuccess) return e;
+  if ((e = make(eb.map_hh, eb.hh, d.inter)) != cudaSuccess) return e;
+  return make(eb.map_hl, eb.hl, d.inter);
 }
 
 namespace {
 
-tc::Args common_args(const Moe& m, Workspace& ws) {
+tc::Args common_args(const Moe& m, const Groups& g, ExpertBufs& eb) {
   const gb_moe_desc& d = m.desc;
   tc::Args a{};
   a.split_zero = d.weight_format == GB_FMT_MXFP4_SPLIT ? 1 : 0;
   a.e_begin = m.e_begin;
-  a.meta = ws.meta;
-  a.tile_expert = ws.tile_expert;
-  a.tile_row0 = ws.tile_row0;
-  a.tile_rows = ws.tile_rows;
+  a.meta = g.meta;
+  a.tile_expert = eb.tile_expert;
+  a.tile_row0 = eb.tile_row0;
+  a.tile_rows = eb.tile_rows;
   a.limit = d.swiglu_limit;
-  a.err = ws.meta + 1;
+  a.err = g.meta + 1;
   return a;
 }
 
@@ -614,18 +616,20 @@ cudaError_t launch_gemm(const Moe& m, const tc::Args& a, const void* map_w, cons
 
 }  // namespace
 
-cudaError_t launch_tc_gate_up(const Moe& m, const float* x, int64_t T, Workspace& ws,
+cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  const int positions = (int)(T * d.top_k);
+  const int positions = (int)g.rows;
   cudaError_t e;
-  tc::tile_table_kernel<<<1, 32, 0, st>>>(ws.counts, ws.offsets, m.e_begin, m.e_end, ws.meta,
-                                          ws.tile_expert, ws.tile_row0, ws.tile_rows);
+  tc::tile_table_kernel<<<1, 32, 0, st>>>(g.counts, g.offsets, m.e_begin, m.e_end, g.meta,
+                                          eb.tile_expert, eb.tile_row0, eb.tile_rows);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  tc::split_gather_kernel<<<positions, 256, 0, st>>>(x, ws.perm, d.top_k, d.hidden, positions,
-                                                     ws.xh, ws.xl, ws.xscale);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  tc::Args a = common_args(m, ws);
+  if (positions > 0) {
+    tc::split_gather_kernel<<<positions, 256, 0, st>>>(x, g.perm, g.perm_div, d.hidden, positions,
+                                                       eb.xh, eb.xl, eb.xscale);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  }
+  tc::Args a = common_args(m, g, eb);
   a.blocks = m.w.gu_blocks;
   a.scales = m.w.gu_scales;
   a.rowmax = m.w.gu_rowmax;
@@ -634,17 +638,16 @@ cudaError_t launch_tc_gate_up(const Moe& m, const float* x, int64_t T, Workspace
   a.K = d.hidden;
   a.rows = 2 * d.inter;
   a.m_tiles = (a.rows + tc::BM - 1) / tc::BM;
-  a.xscale = ws.xscale;
-  a.out_hi = ws.hh;
-  a.out_lo = ws.hl;
+  a.xscale = eb.xscale;
+  a.out_hi = eb.hh;
+  a.out_lo = eb.hl;
   a.out_stride = d.inter;
-  return launch_gemm<tc::GATE_UP>(m, a, m.w.map_gu, ws.map_xh, ws.map_xl, st);
+  return launch_gemm<tc::GATE_UP>(m, a, m.w.map_gu, eb.map_xh, eb.map_xl, st);
 }
 
-cudaError_t launch_tc_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t st) {
-  (void)T;
+cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  tc::Args a = common_args(m, ws);
+  tc::Args a = common_args(m, g, eb);
   a.blocks = m.w.dn_blocks;
   a.scales = m.w.dn_scales;
   a.rowmax = m.w.dn_rowmax;
@@ -653,9 +656,10 @@ cudaError_t launch_tc_down(const Moe& m, int64_t T, Workspace& ws, cudaStream_t 
   a.K = d.inter;
   a.rows = d.hidden;
   a.m_tiles = (a.rows + tc::BM - 1) / tc::BM;
-  a.out_y = ws.y;
+  a.out_y = eb.y;
+  a.out_rows = g.out_rows;
   a.out_stride = d.hidden;
-  return launch_gemm<tc::DOWN>(m, a, m.w.map_dn, ws.map_hh, ws.map_hl, st);
+  return launch_gemm<tc::DOWN>(m, a, m.w.map_dn, eb.map_hh, eb.map_hl, st);
 }
 
 }  // namespace gb

@@ -6,5 +6,5 @@ Public surface:
   GalliumError              -- raised for any non-OK gb_status
 """
 from ._lib import GalliumError, load_library  # noqa: F401
-from .moe import GptOssQMoEFFN, MoEBlock, OssMoEFFN  # noqa: F401
+from .moe import GptOssQMoEFFN, MoEBlock, OssMoEFFN, nccl_unique_id  # noqa: F401
 from . import synth  # noqa: F401

@@ -150,13 +150,27 @@ class MoEBlock:
         return out
 
 
-def _base_desc(hidden, inter, n_experts, top_k, device, max_tokens) -> MoeDesc:
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id (rank 0 creates it and shares it)."""
+    lib = load_library()
+    buf = (ctypes.c_uint8 * 128)()
+    check(lib.gb_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+def _base_desc(hidden, inter, n_experts, top_k, device, max_tokens, ep=None) -> MoeDesc:
+    """ep: None (one GPU) or (rank, size, nccl_id bytes) for expert parallelism."""
     d = MoeDesc()
     d.struct_size = ctypes.sizeof(MoeDesc)
     d.hidden, d.inter, d.n_experts, d.top_k = hidden, inter, n_experts, top_k
     d.device = device
     d.max_tokens = max_tokens
     d.ep_size = 1
+    if ep is not None:
+        rank, size, nid = ep
+        d.ep_rank, d.ep_size = rank, size
+        d._nccl_id_buf = (ctypes.c_uint8 * 128).from_buffer_copy(nid)
+        d.nccl_id = ctypes.addressof(d._nccl_id_buf)
     return d
 
 
@@ -164,8 +178,11 @@ class OssMoEFFN(MoEBlock):
     """Safetensors GPT-OSS MoE block (gpt_oss.rs:97-231)."""
 
     @classmethod
-    def load(cls, layer: GptOssLayer, device: int = 0, max_tokens: int = 64) -> "OssMoEFFN":
-        d = _base_desc(layer.hidden, layer.inter, layer.n_experts, layer.top_k, device, max_tokens)
+    def load(cls, layer: GptOssLayer, device: int = 0, max_tokens: int = 64,
+             ep=None) -> "OssMoEFFN":
+        """ep = (rank, size, nccl_id) shards the experts over `size` GPUs."""
+        d = _base_desc(layer.hidden, layer.inter, layer.n_experts, layer.top_k, device, max_tokens,
+                       ep)
         d.router_kind = _lib.GB_ROUTER_SOFTMAX_TOPK
         d.act_kind = _lib.GB_ACT_GPTOSS_CLAMP
         d.weight_format = _lib.GB_FMT_MXFP4_SPLIT
@@ -177,17 +194,17 @@ class OssMoEFFN(MoEBlock):
          d.down_scales, d.gate_up_bias, d.down_bias) = [_ptr(a) for a in arrs]
         d.router_dtype = _lib.GB_DTYPE_BF16
         d.bias_dtype = _lib.GB_DTYPE_BF16
-        return cls(d, arrs)
+        return cls(d, arrs + [getattr(d, "_nccl_id_buf", None)])
 
 
 class GptOssQMoEFFN(MoEBlock):
     """GGUF GPT-OSS MoE block (QMoEFFN, gpt_oss_q.rs:119-269)."""
 
     @classmethod
-    def load(cls, layer: GptOssGgufLayer, device: int = 0,
-             max_tokens: int = 64) -> "GptOssQMoEFFN":
+    def load(cls, layer: GptOssGgufLayer, device: int = 0, max_tokens: int = 64,
+             ep=None) -> "GptOssQMoEFFN":
         b = layer.base
-        d = _base_desc(b.hidden, b.inter, b.n_experts, b.top_k, device, max_tokens)
+        d = _base_desc(b.hidden, b.inter, b.n_experts, b.top_k, device, max_tokens, ep)
         d.router_kind = _lib.GB_ROUTER_SOFTMAX_TOPK
         d.act_kind = _lib.GB_ACT_GPTOSS_CLAMP
         d.weight_format = _lib.GB_FMT_MXFP4_GGUF
