@@ -66,8 +66,8 @@ typedef enum {
    * j -> element j, high nibble -> j+16. */
   GB_FMT_MXFP4_GGUF = 1,
   /* GGML Q4_K (144-byte, 256-element super-blocks), separate gate/up/down
-   * like GGUF (quantized.rs:139-178).  Not implemented yet: create returns
-   * GB_ERR_UNSUPPORTED. */
+   * like GGUF (quantized.rs:139-178, the LFM2.5 experts of
+   * lfm2moe_q.rs:203-232).  H and I multiples of 256. */
   GB_FMT_Q4_K = 2
 } gb_weight_format;
 

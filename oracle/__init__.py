@@ -240,3 +240,26 @@ class OracleMoe:
         assert x.shape[0] >= int(nt.max())
         return lib().or_moe_expert_sample(ctypes.byref(self.desc), _p(x), _p(ex), _p(nt),
                                           len(ex), None, n_threads)
+
+
+class OracleLfm2:
+    """The oracle for one LFM2.5 layer (Q4_K experts, sigmoid router, SiLU)."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        d = OrDesc()
+        d.hidden, d.inter, d.n_experts, d.top_k = (layer.hidden, layer.inter, layer.n_experts,
+                                                   layer.top_k)
+        d.router_kind = OR_ROUTER_SIGMOID_TOPK
+        d.act_kind = OR_ACT_SILU
+        d.weight_format = OR_FMT_Q4_K
+        keep = {k: np.ascontiguousarray(getattr(layer, k))
+                for k in ("router_w", "sel_bias", "gate_raw", "up_raw", "down_raw")}
+        d.router_w, d.sel_bias = _p(keep["router_w"]), _p(keep["sel_bias"])
+        d.gate_raw, d.up_raw, d.down_raw = _p(keep["gate_raw"]), _p(keep["up_raw"]), _p(keep["down_raw"])
+        self.desc = d
+        self._keep = keep
+
+    forward = OracleMoe.forward
+    expert_ffn = OracleMoe.expert_ffn
+    expert_sample = OracleMoe.expert_sample

@@ -8,9 +8,11 @@
 // flight while keeping the per-element instruction count low.
 //
 //  * One CTA = 4 warps = 64 weight rows of one active expert; a warp walks 8
-//    row pairs (gate/up pairs for gate_up).  Lane l loads block l, l+32, l+64
-//    of a row, so each 128-bit load instruction reads 512 contiguous bytes
-//    (fully used sectors); the next two row pairs are always in flight.
+//    row pairs (gate/up pairs for gate_up).  Each warp stages its next three
+//    row pairs (MXFP4 blocks and E8M0 bytes, ~9 KB) in its own shared-memory
+//    ring with 16-byte cp.async copies, lane l taking blocks l, l+32, l+64 of
+//    a row, so every copy instruction moves 512 contiguous bytes and nothing
+//    in flight occupies registers.
 //  * Each block is decoded in registers (hardware E2M1 -> f16x2, then f32) and
 //    dotted with up to TC tokens' activations, staged once per CTA in shared
 //    memory with a 36-float pitch per 32-element block (conflict-free 128-bit
@@ -29,6 +31,7 @@ constexpr int kPairs = 8;                        // row pairs per warp
 constexpr int kRowsPerCta = kDecWarps * 2 * kPairs;
 constexpr int kLoadsPerRow = 3;                  // 16-byte loads per lane per row (K <= 3072)
 constexpr int kBlockPitch = 36;                  // floats per staged 32-element block (+4 pad)
+constexpr int kRing = 4;                         // row-pair slots per warp (3 in flight)
 
 enum Mode { GATE_UP = 0, DOWN = 1 };
 
@@ -55,13 +58,32 @@ struct DecArgs {
   int out_stride;
 };
 
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(gmem_src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <int MODE, int TC>
 __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecArgs a) {
-  extern __shared__ float smem_f[];
+  extern __shared__ __align__(16) uint8_t smem_b[];
   const int K = a.K;
   const int NB = K >> 5;
-  const int xstride = NB * kBlockPitch;  // floats per staged token row
-  float* xs = smem_f;                     // [TC][NB][kBlockPitch]
+  const int row_bytes = NB * 16;
+  const int slot_bytes = 2 * (row_bytes + a.sp);  // a row pair: blocks then scales
+  const int xstride = NB * kBlockPitch;           // floats per staged token row
+  float* xs = reinterpret_cast<float*>(smem_b);   // [TC][NB][kBlockPitch]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint8_t* ring = smem_b + (size_t)TC * xstride * sizeof(float) +
+                  (size_t)warp * kRing * slot_bytes;  // this warp's [kRing] pair slots
 
   const int slot = blockIdx.y;
   if (slot >= a.meta[0]) return;
@@ -69,45 +91,33 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
   const int le = e - a.e_begin;
   const int n = a.counts[e];
   const int p0 = a.offsets[e];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // this warp's rows: kPairs pairs (2p, 2p+1) starting at row0
   const int row0 = blockIdx.x * kRowsPerCta + warp * 2 * kPairs;
   const int npairs = max(0, min(kPairs, (a.rows - row0) >> 1));
   const int64_t erow = (int64_t)le * a.rows;
 
-  // weights of pair p: two rows x kLoadsPerRow 16-byte loads per lane (lane = block)
-  auto load_pair = [&](int p, uint4 (&q)[2][kLoadsPerRow], uint32_t (&sc)[2][kLoadsPerRow]) {
+  // Copy row pair p into ring slot (p % kRing); always commits a group so the
+  // wait counts stay aligned (an out-of-range pair commits an empty group).
+  auto fetch_pair = [&](int p) {
+    if (p < npairs) {
+      uint8_t* dst = ring + (p % kRing) * slot_bytes;
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int64_t row = erow + row0 + 2 * p + r;
-      const uint8_t* rb = a.blocks + row * NB * 16;
-      const uint8_t* rs = a.scales + row * a.sp;
-#pragma unroll
-      for (int i = 0; i < kLoadsPerRow; ++i) {
-        const int b = lane + 32 * i;
-        if (p < npairs && b < NB) {
-          q[r][i] = ld_stream_u4(rb + b * 16);
-          sc[r][i] = rs[b];
-        } else {
-          q[r][i] = make_uint4(0, 0, 0, 0);
-          sc[r][i] = 0;
-        }
+      for (int r = 0; r < 2; ++r) {
+        const int64_t row = erow + row0 + 2 * p + r;
+        const uint8_t* rb = a.blocks + row * row_bytes;
+        for (int c = lane; c < NB; c += 32) cp_async16(dst + r * row_bytes + c * 16, rb + c * 16);
+        const uint8_t* rs = a.scales + row * a.sp;
+        for (int c = lane; c < (a.sp >> 4); c += 32)
+          cp_async16(dst + 2 * row_bytes + r * a.sp + c * 16, rs + c * 16);
       }
     }
+    cp_async_commit();
   };
-
-  uint4 qa[2][kLoadsPerRow], qb[2][kLoadsPerRow];
-  uint32_t sa[2][kLoadsPerRow], sb[2][kLoadsPerRow];
-  load_pair(0, qa, sa);
-  load_pair(1, qb, sb);
 
   for (int c0 = 0; c0 < n; c0 += TC) {
     const int nc = min(TC, n - c0);
-    if (c0 > 0) {
-      __syncthreads();
-      load_pair(0, qa, sa);
-      load_pair(1, qb, sb);
-    }
+    if (c0 > 0) __syncthreads();
+#pragma unroll
+    for (int p = 0; p < kRing - 1; ++p) fetch_pair(p);
     for (int j = 0; j < nc; ++j) {
       const float* src = MODE == GATE_UP
                              ? a.in + (int64_t)(a.perm[p0 + c0 + j] / a.top_k) * K
@@ -121,18 +131,10 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
     __syncthreads();
 
     for (int p = 0; p < npairs; ++p) {
-      uint4 q[2][kLoadsPerRow];
-      uint32_t scb[2][kLoadsPerRow];
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int i = 0; i < kLoadsPerRow; ++i) {
-          q[r][i] = qa[r][i];
-          scb[r][i] = sa[r][i];
-          qa[r][i] = qb[r][i];
-          sa[r][i] = sb[r][i];
-        }
-      load_pair(p + 2, qb, sb);  // two pairs ahead
+      fetch_pair(p + kRing - 1);
+      cp_async_wait<kRing - 1>();  // pair p has landed (this lane's copies)
+      __syncwarp();                // ... and every lane's
+      const uint8_t* sl = ring + (p % kRing) * slot_bytes;
 
       float acc[2][TC];
 #pragma unroll
@@ -145,9 +147,10 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
         for (int i = 0; i < kLoadsPerRow; ++i) {
           const int b = lane + 32 * i;
           if (b >= NB) continue;
+          const uint4 q = *reinterpret_cast<const uint4*>(sl + r * row_bytes + b * 16);
+          const float sc = e8m0_scale(sl[2 * row_bytes + r * a.sp + b], a.zero_scale);
           float v[32];
-          decode_block_f32(q[r][i], v);
-          const float sc = e8m0_scale(scb[r][i], a.zero_scale);
+          decode_block_f32(q, v);
 #pragma unroll
           for (int t = 0; t < TC; ++t) {
             if (t < nc) {
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
           }
         }
       }
+      __syncwarp();  // slot p % kRing is refilled by a later fetch
       const int row = row0 + 2 * p;  // gate (GATE_UP) / first output row (DOWN)
 #pragma unroll
       for (int t = 0; t < TC; ++t) {
@@ -196,6 +200,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
         }
       }
     }
+    cp_async_wait<0>();
   }
 }
 
@@ -204,7 +209,8 @@ cudaError_t launch_dec(const Moe& m, const Groups& g, const DecArgs& a, cudaStre
   (void)m;
   if (g.max_active <= 0) return cudaSuccess;
   dim3 grid((unsigned)((a.rows + kRowsPerCta - 1) / kRowsPerCta), (unsigned)g.max_active);
-  const size_t smem = (size_t)TC * (a.K / 32) * kBlockPitch * sizeof(float);
+  const size_t smem = (size_t)TC * (a.K / 32) * kBlockPitch * sizeof(float) +
+                      (size_t)kDecWarps * kRing * 2 * ((a.K / 32) * 16 + a.sp);
   auto kern = decode_rows_kernel<MODE, TC>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
@@ -233,7 +239,8 @@ DecArgs base_args(const Moe& m, const Groups& g) {
 bool decode_supported(const Moe& m) {
   const gb_moe_desc& d = m.desc;
   // whole row pairs; a row is at most 3 x 32 blocks (K <= 3072)
-  return d.hidden % 64 == 0 && d.inter % 64 == 0 && d.hidden <= 3072 && d.inter <= 3072;
+  return d.weight_format != GB_FMT_Q4_K && d.hidden % 64 == 0 && d.inter % 64 == 0 &&
+         d.hidden <= 3072 && d.inter <= 3072;
 }
 
 // Tokens per expert decide the template: one token shares nothing, so the

@@ -101,7 +101,15 @@ int validate(const gb_moe_desc* d) {
         return set_err(GB_ERR_INVALID_ARG, "MXFP4_GGUF needs gate_raw, up_raw and down_raw");
       break;
     case GB_FMT_Q4_K:
-      return set_err(GB_ERR_UNSUPPORTED, "Q4_K experts are not implemented in this build");
+      if (!d->gate_raw || !d->up_raw || !d->down_raw)
+        return set_err(GB_ERR_INVALID_ARG, "Q4_K needs gate_raw, up_raw and down_raw");
+      // QExperts::dequantize_expert (quantized.rs:162-177) refuses a ragged expert
+      if (d->hidden % 256 != 0 || d->inter % 256 != 0)
+        return set_err(GB_ERR_SHAPE,
+                       "Q4_K expert rows of %d (hidden) / %d (inter) elements are not a whole "
+                       "number of 256-element super-blocks",
+                       d->hidden, d->inter);
+      break;
     default:
       return set_err(GB_ERR_INVALID_ARG, "unknown weight_format %d", d->weight_format);
   }
@@ -235,14 +243,46 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.dn_bias);
   cudaFree(m.w.gu_rowmax);
   cudaFree(m.w.dn_rowmax);
+  cudaFree(m.w.q4_gu);
+  cudaFree(m.w.q4_dn);
   free_ws(m.ws);
   gb::ep_destroy(m);
   m = gb::Moe{};
 }
 
+int upload_router(gb::Moe& m);
+
+// Q4_K: the caller's blocks as they are, gate and up rows interleaved.
+int upload_q4k(gb::Moe& m) {
+  const gb_moe_desc& d = m.desc;
+  const int64_t H = d.hidden, I = d.inter;
+  const int64_t nloc = m.e_end - m.e_begin;
+  const size_t rb_h = (size_t)(H / 256) * 144, rb_i = (size_t)(I / 256) * 144;
+  const size_t gu_bytes = (size_t)(nloc * 2 * I) * rb_h, dn_bytes = (size_t)(nloc * H) * rb_i;
+  int rc;
+  if ((rc = dev_alloc(&m.w.q4_gu, gu_bytes, "Q4_K gate_up"))) return rc;
+  if ((rc = dev_alloc(&m.w.q4_dn, dn_bytes, "Q4_K down"))) return rc;
+  m.weight_bytes = (int64_t)(gu_bytes + dn_bytes);
+  for (int64_t le = 0; le < nloc; ++le) {
+    const int64_t e = m.e_begin + le;
+    uint8_t* dst = m.w.q4_gu + (size_t)(le * 2 * I) * rb_h;
+    GB_CUDA(cudaMemcpy2D(dst, 2 * rb_h, d.gate_raw + (size_t)(e * I) * rb_h, rb_h, rb_h, (size_t)I,
+                         cudaMemcpyHostToDevice),
+            "upload Q4_K gate");
+    GB_CUDA(cudaMemcpy2D(dst + rb_h, 2 * rb_h, d.up_raw + (size_t)(e * I) * rb_h, rb_h, rb_h,
+                         (size_t)I, cudaMemcpyHostToDevice),
+            "upload Q4_K up");
+  }
+  GB_CUDA(cudaMemcpy(m.w.q4_dn, d.down_raw + (size_t)(m.e_begin * H) * rb_i, dn_bytes,
+                     cudaMemcpyHostToDevice),
+          "upload Q4_K down");
+  return upload_router(m);
+}
+
 int upload_weights(gb::Moe& m) {
   const gb_moe_desc& d = m.desc;
-  const int64_t H = d.hidden, I = d.inter, E = d.n_experts;
+  if (d.weight_format == GB_FMT_Q4_K) return upload_q4k(m);
+  const int64_t H = d.hidden, I = d.inter;
   const int64_t nloc = m.e_end - m.e_begin;
   const int64_t nbh = H / 32, nbi = I / 32;
   m.w.sp_h = (int)round_up(nbh, 16);
@@ -342,6 +382,13 @@ int upload_weights(gb::Moe& m) {
             "upload down bias");
   }
 
+  return upload_router(m);
+}
+
+int upload_router(gb::Moe& m) {
+  const gb_moe_desc& d = m.desc;
+  const int64_t H = d.hidden, E = d.n_experts;
+  int rc;
   // Router (replicated).
   std::vector<float> rw = widen(d.router_weight, E * H, d.router_dtype);
   if ((rc = dev_alloc(&m.router_w, rw.size() * 4, "router weight"))) return rc;
@@ -432,7 +479,12 @@ int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& 
                 cudaStream_t st) {
   int rc;
   (void)T;
-  if (use_tensor_cores(m, eb, g.rows)) {
+  if (m.desc.weight_format == GB_FMT_Q4_K) {
+    GB_CUDA(launch_q4k_gate_up(m, g, x, eb, st), "Q4_K gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(launch_q4k_down(m, g, eb, st), "Q4_K down launch");
+    m.launches += 2;
+  } else if (use_tensor_cores(m, eb, g.rows)) {
     GB_CUDA(launch_tc_gate_up(m, g, x, eb, st), "tensor-core gate_up launch");
     if ((rc = mark(m, 3, st))) return rc;
     GB_CUDA(launch_tc_down(m, g, eb, st), "tensor-core down launch");
@@ -655,7 +707,10 @@ int gb_moe_dequant_expert(gb_moe* h, int32_t which, int32_t expert, float* out_d
   if (!out_dev) return set_err(GB_ERR_INVALID_ARG, "out is null");
   DeviceScope ds(m.device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  GB_CUDA(gb::launch_dequant_expert(m, which, expert - m.e_begin, out_dev, st), "dequant launch");
+  if (m.desc.weight_format == GB_FMT_Q4_K)
+    GB_CUDA(gb::launch_q4k_dequant(m, which, expert - m.e_begin, out_dev, st), "dequant launch");
+  else
+    GB_CUDA(gb::launch_dequant_expert(m, which, expert - m.e_begin, out_dev, st), "dequant launch");
   GB_CUDA(cudaStreamSynchronize(st), "synchronise dequant");
   return GB_OK;
 }

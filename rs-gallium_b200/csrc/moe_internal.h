@@ -37,6 +37,10 @@ struct ExpertWeights {
   alignas(64) unsigned char map_dn[128] = {};  // CUtensorMap of dn_blocks
   float zero_scale = 0.0f;
   int sp_h = 0, sp_i = 0;  // padded scale row strides
+  // GGML Q4_K experts (144-byte super-blocks), gate/up rows interleaved:
+  // q4_gu [E_loc][2I][H/256][144], q4_dn [E_loc][H][I/256][144]
+  uint8_t* q4_gu = nullptr;
+  uint8_t* q4_dn = nullptr;
 };
 
 // The grouped view the expert kernels work on: rows grouped by expert
@@ -142,6 +146,13 @@ bool decode_supported(const Moe& m);
 cudaError_t launch_decode_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                   cudaStream_t st);
 cudaError_t launch_decode_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+
+// Q4_K expert kernels (q4k_gemv.cu).
+cudaError_t launch_q4k_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                               cudaStream_t st);
+cudaError_t launch_q4k_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float* out,
+                               cudaStream_t st);
 
 // Tensor-core expert path (tc_gemm.cu).
 bool tc_supported(const Moe& m);

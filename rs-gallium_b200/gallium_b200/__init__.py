@@ -1,10 +1,10 @@
 """gallium_b200: the rs-gallium MoE FFN block on B200 (sm_100a), behind a C ABI.
 
 Public surface:
-  OssMoEFFN, GptOssQMoEFFN  -- the reference's MoE blocks (load / forward)
+  OssMoEFFN, GptOssQMoEFFN, Lfm2QMoEFFN -- the reference's MoE blocks (load / forward)
   synth                     -- seeded synthetic layers and inputs
   GalliumError              -- raised for any non-OK gb_status
 """
 from ._lib import GalliumError, load_library  # noqa: F401
-from .moe import GptOssQMoEFFN, MoEBlock, OssMoEFFN, nccl_unique_id  # noqa: F401
+from .moe import GptOssQMoEFFN, Lfm2QMoEFFN, MoEBlock, OssMoEFFN, nccl_unique_id  # noqa: F401
 from . import synth  # noqa: F401

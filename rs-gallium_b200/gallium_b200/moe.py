@@ -23,7 +23,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import MoeDesc, MoeInfo, check, load_library
-from .synth import GptOssGgufLayer, GptOssLayer, bf16_bits_to_f32
+from .synth import GptOssGgufLayer, GptOssLayer, Lfm2Layer, bf16_bits_to_f32
 
 
 def _ptr(a: Optional[np.ndarray]) -> Optional[int]:
@@ -221,3 +221,23 @@ class GptOssQMoEFFN(MoEBlock):
         d.router_dtype = _lib.GB_DTYPE_F32
         d.bias_dtype = _lib.GB_DTYPE_F32
         return cls(d, arrs)
+
+
+class Lfm2QMoEFFN(MoEBlock):
+    """LFM2.5 MoE block with Q4_K experts (QMoEFFN, lfm2moe_q.rs:203-313)."""
+
+    @classmethod
+    def load(cls, layer: Lfm2Layer, device: int = 0, max_tokens: int = 64,
+             ep=None) -> "Lfm2QMoEFFN":
+        d = _base_desc(layer.hidden, layer.inter, layer.n_experts, layer.top_k, device,
+                       max_tokens, ep)
+        d.router_kind = _lib.GB_ROUTER_SIGMOID_TOPK
+        d.act_kind = _lib.GB_ACT_SILU
+        d.weight_format = _lib.GB_FMT_Q4_K
+        arrs = [np.ascontiguousarray(a) for a in (
+            layer.router_w, layer.sel_bias, layer.gate_raw, layer.up_raw, layer.down_raw)]
+        (d.router_weight, d.selection_bias, d.gate_raw, d.up_raw, d.down_raw) = [
+            _ptr(a) for a in arrs]
+        d.router_dtype = _lib.GB_DTYPE_F32
+        d.bias_dtype = _lib.GB_DTYPE_F32
+        return cls(d, arrs + [getattr(d, "_nccl_id_buf", None)])

@@ -148,3 +148,55 @@ def algorithmic_flops(layer: GptOssLayer, T: int) -> int:
     """Expert GEMM FLOPs (2 * (2I*H + H*I) per token-expert) plus the router."""
     H, I, E, k = layer.hidden, layer.inter, layer.n_experts, layer.top_k
     return T * k * 6 * H * I + 2 * T * H * E
+
+
+# ---- LFM2.5 MoE block with GGML Q4_K experts ---------------------------------
+
+@dataclass
+class Lfm2Layer:
+    """LFM2.5-shaped MoE block (lfm2moe_q.rs:203-313): sigmoid router with a
+    selection-only bias, SiLU-gated experts without biases, Q4_K weights as
+    GGUF tensors gate/up [E, I, H] and down [E, H, I] (144-byte super-blocks)."""
+    hidden: int
+    inter: int
+    n_experts: int
+    top_k: int
+    router_w: np.ndarray   # [E, H] f32
+    sel_bias: np.ndarray   # [E] f32 (exp_probs_b)
+    gate_raw: np.ndarray   # [E, I, H/256 * 144] uint8
+    up_raw: np.ndarray
+    down_raw: np.ndarray   # [E, H, I/256 * 144] uint8
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def expert_bytes(self) -> int:
+        """Q4_K bytes of one expert: 0.5625 bytes per element, 6,193,152 at 2048/1792."""
+        return (2 * self.inter * self.hidden + self.hidden * self.inter) // 256 * 144
+
+
+def q4k_blocks(rng, rows: int, k: int, d: float, dmin: float) -> np.ndarray:
+    """rows x (k/256) Q4_K super-blocks: the given f16 d and dmin, uniform 6-bit
+    scales and mins (every bit of the 12 packed bytes is used once, so uniform
+    bytes give uniform 6-bit values) and uniform 4-bit codes."""
+    nb = k // 256
+    blk = rng.integers(0, 256, (rows, nb, 144), dtype=np.uint8)
+    blk[..., 0:2] = np.frombuffer(np.float16(d).tobytes(), np.uint8)
+    blk[..., 2:4] = np.frombuffer(np.float16(dmin).tobytes(), np.uint8)
+    return np.ascontiguousarray(blk.reshape(rows, nb * 144))
+
+
+def lfm2_layer(n_experts: int = 32, hidden: int = 2048, inter: int = 1792, top_k: int = 4,
+               seed: int = 0, d: float = 2.0 ** -11, dmin: float = 15 * 2.0 ** -12) -> Lfm2Layer:
+    """Default d = 2^-11 and dmin = 7.5 d.  With scales, mins and codes uniform,
+    E[d*sc*q - dmin*m] = 31.5 (7.5 d - dmin) = 0, so the weights are centred
+    like a trained Q4_K tensor, with a standard deviation near 0.13 (the
+    GPT-OSS blocks' is 0.32).  d = dmin would give every weight a positive
+    mean and outputs near 1e5, where no two f32 evaluations agree to 2e-2."""
+    rng = np.random.default_rng(seed)
+    E, H, I = n_experts, hidden, inter
+    router_w = rng.normal(0.0, 0.02, (E, H)).astype(np.float32)
+    gate = np.stack([q4k_blocks(rng, I, H, d, dmin) for _ in range(E)])
+    up = np.stack([q4k_blocks(rng, I, H, d, dmin) for _ in range(E)])
+    down = np.stack([q4k_blocks(rng, H, I, d, dmin) for _ in range(E)])
+    return Lfm2Layer(H, I, E, top_k, router_w, np.zeros(E, np.float32), gate, up, down,
+                     meta={"seed": seed, "d": d, "dmin": dmin})

@@ -98,7 +98,9 @@ def _full(**kw):
     (dict(hidden=100), _lib.GB_ERR_SHAPE, "100"),
     (dict(inter=48), _lib.GB_ERR_SHAPE, "32-element"),
     (dict(n_experts=300, top_k=2), _lib.GB_ERR_UNSUPPORTED, "256"),
-    (dict(weight_format=_lib.GB_FMT_Q4_K), _lib.GB_ERR_UNSUPPORTED, "Q4_K"),
+    (dict(weight_format=_lib.GB_FMT_Q4_K, gate_raw=P, up_raw=P, down_raw=P), _lib.GB_ERR_SHAPE,
+     "256-element"),
+    (dict(weight_format=_lib.GB_FMT_Q4_K), _lib.GB_ERR_INVALID_ARG, "Q4_K needs"),
     (dict(ep_size=2, ep_rank=3), _lib.GB_ERR_INVALID_ARG, "ep_rank"),
     (dict(max_tokens=-1), _lib.GB_ERR_INVALID_ARG, "max_tokens"),
 ])

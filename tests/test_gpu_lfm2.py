@@ -1,0 +1,88 @@
+"""LFM2.5-shaped MoE block with GGML Q4_K experts on the GPU vs the oracle:
+hidden 2048, 32 experts, top-4, intermediate 1792, sigmoid router whose
+selection bias only steers selection (lfm2moe_q.rs:241-258), SiLU-gated
+experts without biases, combine in ascending expert order."""
+import numpy as np
+import pytest
+
+import oracle
+from gallium_b200 import GalliumError, Lfm2QMoEFFN, synth
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_REL = 2e-2, 1e-3
+
+
+def _cuda(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _parity(got, want, what):
+    err = np.abs(np.asarray(got, np.float64) - want)
+    max_abs, mean_rel = float(err.max()), float(err.sum() / np.abs(want).sum())
+    assert max_abs <= MAX_ABS and mean_rel <= MEAN_REL, (what, max_abs, mean_rel)
+
+
+@pytest.fixture(scope="module")
+def layer():
+    lay = synth.lfm2_layer(n_experts=32, seed=0)
+    lay.sel_bias[:] = np.random.default_rng(1).normal(0, 0.05, 32).astype(np.float32)
+    return lay
+
+
+@pytest.fixture(scope="module")
+def moe(layer):
+    m = Lfm2QMoEFFN.load(layer, device=0, max_tokens=64)
+    yield m
+    m.close()
+
+
+@pytest.mark.parametrize("expert", [0, 31])
+def test_q4k_device_dequant_is_bit_exact(moe, layer, expert):
+    H, I = layer.hidden, layer.inter
+    g = oracle.q4k_dequant(layer.gate_raw[expert].ravel(), I * H).reshape(I, H)
+    u = oracle.q4k_dequant(layer.up_raw[expert].ravel(), I * H).reshape(I, H)
+    d = oracle.q4k_dequant(layer.down_raw[expert].ravel(), H * I).reshape(H, I)
+    for which, want in ((0, g), (1, u), (2, d)):
+        got = moe.dequant_expert(which, expert).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), which
+
+
+@pytest.mark.parametrize("T", [1, 5, 64])
+def test_sigmoid_routing_is_bit_exact(moe, layer, T):
+    x = synth.tokens(T, 2048, seed=T)
+    r = moe.route(_cuda(x))
+    idx, w = oracle.route_sigmoid_topk(oracle.router_logits(x, layer.router_w), layer.sel_bias, 4)
+    counts, offsets, perm, _ = oracle.permute(idx, 32)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx)
+    assert np.array_equal(r["perm"].cpu().numpy(), perm)
+    np.testing.assert_allclose(r["w"].cpu().numpy(), w, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64])
+def test_lfm2_forward_matches_oracle(moe, layer, T):
+    x = synth.tokens(T, 2048, seed=900 + T)
+    got = moe.forward(_cuda(x)).cpu().numpy()
+    want, _, _ = oracle.OracleLfm2(layer).forward(x)
+    _parity(got, want, f"T={T}")
+
+
+def test_lfm2_full_size_sampled_rows_and_determinism(moe, layer):
+    T = 2048
+    x = synth.tokens(T, 2048, seed=2048)
+    xc = _cuda(x)
+    a = moe.forward(xc).cpu().numpy()
+    b = moe.forward(xc).cpu().numpy()
+    assert np.array_equal(a, b)
+    rows = np.random.default_rng(3).choice(T, 16, replace=False)
+    want, _, _ = oracle.OracleLfm2(layer).forward(x[rows])
+    _parity(a[rows], want, "T=2048 sampled rows")
+
+
+def test_q4k_ragged_rows_are_refused():
+    lay = synth.lfm2_layer(n_experts=4, hidden=256, inter=256, top_k=2, seed=1)
+    lay.hidden = 200
+    with pytest.raises(GalliumError) as ei:
+        Lfm2QMoEFFN.load(lay, device=0)
+    assert "256-element" in str(ei.value)

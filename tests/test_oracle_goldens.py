@@ -290,3 +290,36 @@ def test_oracle_gguf_view_matches_split():
     assert np.array_equal(ia, ib)
     # same values; the GGUF path only changes the combine order (expert ascending)
     assert np.allclose(a, b, rtol=1e-5, atol=1e-4)
+
+
+# ---- LFM2.5 (Q4_K, sigmoid router, SiLU) vs a float64 restatement ----------
+
+def _numpy_lfm2(layer, x):
+    """lfm2moe_q.rs:234-313 in float64 numpy, Q4_K decoded by _q4k_numpy."""
+    H, I, E, k = layer.hidden, layer.inter, layer.n_experts, layer.top_k
+    logits = x.astype(np.float64) @ layer.router_w.astype(np.float64).T
+    p = 1 / (1 + np.exp(-logits))
+    out = np.zeros((x.shape[0], H))
+    for t in range(x.shape[0]):
+        order = sorted(range(E), key=lambda e: (-(p[t, e] + layer.sel_bias[e]), e))[:k]
+        wts = p[t, order] / p[t, order].sum()
+        # combine in ascending expert order (lfm2moe_q.rs:303-311)
+        for e, wv in sorted(zip(order, wts)):
+            g = _q4k_numpy(layer.gate_raw[e].ravel(), I * H).reshape(I, H) @ x[t]
+            u = _q4k_numpy(layer.up_raw[e].ravel(), I * H).reshape(I, H) @ x[t]
+            h = g / (1 + np.exp(-g)) * u
+            y = _q4k_numpy(layer.down_raw[e].ravel(), H * I).reshape(H, I) @ h
+            out[t] += wv * y
+    return out
+
+
+def test_oracle_lfm2_block_matches_float64_restatement():
+    layer = synth.lfm2_layer(n_experts=6, hidden=256, inter=256, top_k=3, seed=5)
+    layer.sel_bias[:] = np.array([0, 0.3, 0, 0, -0.2, 0], np.float32)
+    x = synth.tokens(4, 256, seed=6)
+    got, idx, w = oracle.OracleLfm2(layer).forward(x)
+    want = _numpy_lfm2(layer, x)
+    err = np.abs(got - want)
+    assert err.max() <= 1e-3 * max(1.0, np.abs(want).max())
+    assert err.sum() / np.abs(want).sum() < 1e-5
+    assert np.allclose(w.sum(axis=1), 1.0, atol=1e-6)
