@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--sweep", default="1,32,1024",
                     help="extra per-GPU batch sizes to measure ('' = none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--expert-path", default="auto",
+                    choices=["auto", "cuda_cores", "tensor_cores", "tensor_cores_small_tiles",
+                             "tensor_cores_f16"],
+                    help="force one expert kernel (gb_moe_set_expert_path)")
     ap.add_argument("--cpu-threads", type=int, default=0)
     return ap.parse_args()
 
@@ -323,9 +327,12 @@ def run_ours(args, world, rank, local):
         dist.broadcast_object_list(obj, src=0)
         ep = (rank, world, obj[0])
     moe = OssMoEFFN.load(layer, device=local, max_tokens=max([T] + sweep), ep=ep)
-    x = synth.tokens(T, H, seed=args.seed + 1000 * rank)
+    moe.set_expert_path(args.expert_path)
+    # buffers hold the largest batch of the run (T and every sweep size)
+    x = synth.tokens(max([T] + sweep), H, seed=args.seed + 1000 * rank)
     xd = torch.from_numpy(x).cuda()
     out = torch.empty_like(xd)
+    x = x[:T]
     flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
 
     def flush():
@@ -349,7 +356,7 @@ def run_ours(args, world, rank, local):
     for _ in range(args.warmup):
         fwd_dev(T)
     torch.cuda.synchronize()
-    counts = moe.route(xd)["counts"].cpu().numpy()
+    counts = moe.route(xd[:T])["counts"].cpu().numpy()
     n_touched = int((counts > 0).sum())
     if world > 1:
         # experts this rank's GPU runs: touched by any rank's tokens, among its own

@@ -177,15 +177,34 @@ int gb_moe_dequant_expert(gb_moe* m, int32_t which, int32_t expert, float* out_d
 
 int gb_moe_get_info(const gb_moe* m, gb_moe_info* info);
 
-/* Which kernels run the expert products.  AUTO picks the CUDA-core kernels
- * (streaming MXFP4 rows, f32 FMA) for decode-sized batches and the tcgen05
- * tensor-core grouped GEMMs for prefill-sized ones; the other two force one
- * path (tensor cores need the GPT-OSS activation and H, I multiples of 64).
- * No counterpart in the reference, which has one CPU path. */
+/* Error bits the forward kernels recorded on the device since the last call:
+ * synchronises `stream`, reads and clears them.  Returns GB_OK, or
+ * GB_ERR_TIMEOUT when a tensor-core pipeline wait ran out (that forward's
+ * output is invalid), or GB_ERR_INVALID_ARG when routing produced an expert
+ * index out of range.  gb_moe_forward_host checks them itself; callers of
+ * the asynchronous gb_moe_forward call this when they consume the output.
+ * No counterpart in the reference, whose CPU path has no asynchronous
+ * failure. */
+int gb_moe_device_status(gb_moe* m, void* stream);
+
+/* Which kernels run the expert products.  AUTO picks, for batches averaging
+ * at most 32 rows per local expert, the block-scaled tcgen05 GEMM with
+ * decode tiles (MXFP4 weights as stored, 256 weight rows x 1-16 positions,
+ * activations as E4M3 pieces), and for larger ones the kind::f16 GEMM with
+ * 128-position tiles that decodes the weights to f16 in shared memory
+ * (activations as f16 hi + lo).  The others force one kernel: CUDA_CORES the
+ * streaming MXFP4 rows with f32 FMA; TENSOR_CORES the block-scaled GEMM with
+ * 128-position tiles; TENSOR_CORES_SMALL_TILES the block-scaled decode
+ * tiles; TENSOR_CORES_F16 the kind::f16 GEMM.  The tensor-core kernels need
+ * the GPT-OSS activation and H, I multiples of 64; without them AUTO uses
+ * the CUDA cores.  Q4_K experts always run on the CUDA cores.  No
+ * counterpart in the reference, which has one CPU path. */
 typedef enum {
   GB_PATH_AUTO = 0,
   GB_PATH_CUDA_CORES = 1,
-  GB_PATH_TENSOR_CORES = 2
+  GB_PATH_TENSOR_CORES = 2,
+  GB_PATH_TENSOR_CORES_SMALL_TILES = 3,
+  GB_PATH_TENSOR_CORES_F16 = 4
 } gb_expert_path;
 int gb_moe_set_expert_path(gb_moe* m, int32_t path);
 

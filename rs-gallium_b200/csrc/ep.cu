@@ -200,6 +200,8 @@ int ep_init(Moe& m, const uint8_t* id_bytes) {
   return GB_OK;
 }
 
+int32_t* ep_meta(Moe& m) { return m.ep ? m.ep->meta2 : nullptr; }
+
 void ep_destroy(Moe& m) {
   Ep* ep = m.ep;
   if (!ep) return;

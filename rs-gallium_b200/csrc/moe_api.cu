@@ -245,6 +245,7 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.dn_rowmax);
   cudaFree(m.w.q4_gu);
   cudaFree(m.w.q4_dn);
+  gb::mx_release(m.mx);
   free_ws(m.ws);
   gb::ep_destroy(m);
   m = gb::Moe{};
@@ -421,15 +422,32 @@ int run_route(gb::Moe& m, const float* x, int64_t T, cudaStream_t st) {
   return mark(m, 2, st);
 }
 
-// Grouped batches of at least this many rows (64 tokens at top-4) take the
-// tensor-core expert path; smaller ones the decode GEMV.
-constexpr int64_t kTensorCoreMinRows = 256;
+// Batches averaging more than this many rows per local expert take the
+// 128-position prefill tiles; smaller ones the decode tiles, which read each
+// weight tile once per 1-16 positions.
+constexpr int64_t kDecodeMaxRowsPerExpert = 32;
 
-bool use_tensor_cores(const gb::Moe& m, const gb::ExpertBufs& eb, int64_t rows) {
-  if (!gb::tc_supported(m) || !eb.maps_ok) return false;
-  if (m.expert_path == GB_PATH_TENSOR_CORES) return true;
-  if (m.expert_path == GB_PATH_CUDA_CORES) return false;
-  return rows >= kTensorCoreMinRows;
+enum class ExpertKernel { kCudaCores, kF16Large, kF16Small, kMxLarge, kMxSmall };
+
+ExpertKernel pick_expert_kernel(const gb::Moe& m, const gb::ExpertBufs& eb, int64_t rows) {
+  const bool mx = m.mx.ok && eb.mx_maps_ok;
+  const bool f16 = gb::tc_supported(m) && eb.maps_ok;
+  const bool large = rows > kDecodeMaxRowsPerExpert * std::max<int64_t>(1, m.e_end - m.e_begin);
+  switch (m.expert_path) {
+    case GB_PATH_CUDA_CORES:
+      return ExpertKernel::kCudaCores;
+    case GB_PATH_TENSOR_CORES_F16:
+      return f16 ? ExpertKernel::kF16Large : ExpertKernel::kCudaCores;
+    case GB_PATH_TENSOR_CORES:
+      return mx ? ExpertKernel::kMxLarge : f16 ? ExpertKernel::kF16Large : ExpertKernel::kCudaCores;
+    case GB_PATH_TENSOR_CORES_SMALL_TILES:
+      return mx ? ExpertKernel::kMxSmall : f16 ? ExpertKernel::kF16Small : ExpertKernel::kCudaCores;
+    default:
+      // prefill: the f16 tiles are faster than the block-scaled ones so far
+      if (large) return f16 ? ExpertKernel::kF16Large : mx ? ExpertKernel::kMxLarge
+                                                         : ExpertKernel::kCudaCores;
+      return mx ? ExpertKernel::kMxSmall : f16 ? ExpertKernel::kF16Small : ExpertKernel::kCudaCores;
+  }
 }
 
 gb::Groups local_groups(const gb::Moe& m, int64_t T) {
@@ -445,6 +463,28 @@ gb::Groups local_groups(const gb::Moe& m, int64_t T) {
   g.max_per_expert = T;
   g.out_rows = nullptr;
   return g;
+}
+
+// Reads and clears the error bits the kernels OR into meta[1] (bit 0: an
+// expert index out of range in routing; bit 1: a pipeline wait timed out).
+int read_device_status(gb::Moe& m, cudaStream_t st) {
+  int32_t bits = 0, b2 = 0;
+  const int32_t zero = 0;
+  GB_CUDA(cudaMemcpyAsync(&bits, m.ws.meta + 1, sizeof bits, cudaMemcpyDeviceToHost, st),
+          "read device status");
+  GB_CUDA(cudaMemcpyAsync(m.ws.meta + 1, &zero, sizeof zero, cudaMemcpyHostToDevice, st),
+          "clear device status");
+  if (int32_t* em = gb::ep_meta(m)) {
+    GB_CUDA(cudaMemcpyAsync(&b2, em + 1, sizeof b2, cudaMemcpyDeviceToHost, st),
+            "read device status");
+    GB_CUDA(cudaMemcpyAsync(em + 1, &zero, sizeof zero, cudaMemcpyHostToDevice, st),
+            "clear device status");
+  }
+  GB_CUDA(cudaStreamSynchronize(st), "synchronise device status");
+  bits |= b2;
+  if (bits & 2) return set_err(GB_ERR_TIMEOUT, "a tensor-core pipeline wait timed out on the device");
+  if (bits & 1) return set_err(GB_ERR_INVALID_ARG, "routing produced an expert index out of range");
+  return GB_OK;
 }
 
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
@@ -484,11 +524,20 @@ int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& 
     if ((rc = mark(m, 3, st))) return rc;
     GB_CUDA(launch_q4k_down(m, g, eb, st), "Q4_K down launch");
     m.launches += 2;
-  } else if (use_tensor_cores(m, eb, g.rows)) {
-    GB_CUDA(launch_tc_gate_up(m, g, x, eb, st), "tensor-core gate_up launch");
-    if ((rc = mark(m, 3, st))) return rc;
-    GB_CUDA(launch_tc_down(m, g, eb, st), "tensor-core down launch");
-    m.launches += 4;  // tile table, split/gather, two GEMMs
+  } else if (const ExpertKernel k = pick_expert_kernel(m, eb, g.rows);
+             k != ExpertKernel::kCudaCores) {
+    if (k == ExpertKernel::kMxLarge || k == ExpertKernel::kMxSmall) {
+      const bool small = k == ExpertKernel::kMxSmall;
+      GB_CUDA(launch_mx_gate_up(m, g, x, eb, small, st), "block-scaled gate_up launch");
+      if ((rc = mark(m, 3, st))) return rc;
+      GB_CUDA(launch_mx_down(m, g, eb, small, st), "block-scaled down launch");
+    } else {
+      const bool small = k == ExpertKernel::kF16Small;
+      GB_CUDA(launch_tc_gate_up(m, g, x, eb, small, st), "tensor-core gate_up launch");
+      if ((rc = mark(m, 3, st))) return rc;
+      GB_CUDA(launch_tc_down(m, g, eb, small, st), "tensor-core down launch");
+    }
+    m.launches += 4;  // tile table, split, two GEMMs
   } else if (decode_supported(m)) {
     GB_CUDA(launch_decode_gate_up(m, g, x, eb, st), "decode gate_up launch");
     if ((rc = mark(m, 3, st))) return rc;
@@ -548,12 +597,14 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
       {(void**)&nb.y, sizeof(float) * (size_t)(rows * H)},
       {(void**)&nb.xh, tc ? sizeof(__half) * (size_t)(rows * H) : 0},
       {(void**)&nb.xl, tc ? sizeof(__half) * (size_t)(rows * H) : 0},
-      {(void**)&nb.xscale, tc ? sizeof(float) * (size_t)rows : 0},
+      {(void**)&nb.xscale, (tc || m.mx.ok) ? sizeof(float) * (size_t)rows : 0},
       {(void**)&nb.hh, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
       {(void**)&nb.hl, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
-      {(void**)&nb.tile_expert, sizeof(int32_t) * (size_t)(rows / 128 + E + 1)},
-      {(void**)&nb.tile_row0, sizeof(int32_t) * (size_t)(rows / 128 + E + 1)},
-      {(void**)&nb.tile_rows, sizeof(int32_t) * (size_t)(rows / 128 + E + 1)},
+      {(void**)&nb.xq, m.mx.ok ? mx_piece_bytes(rows, (int)H) : 0},
+      {(void**)&nb.hq, m.mx.ok ? mx_piece_bytes(rows, (int)I) : 0},
+      {(void**)&nb.tile_expert, sizeof(int32_t) * (size_t)(rows + E + 1)},
+      {(void**)&nb.tile_row0, sizeof(int32_t) * (size_t)(rows + E + 1)},
+      {(void**)&nb.tile_rows, sizeof(int32_t) * (size_t)(rows + E + 1)},
   };
   int rc = carve(pieces, &nb.base, &nb.bytes, "expert buffers");
   if (rc) return rc;
@@ -564,6 +615,14 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
       return cuda_err(e, "TMA descriptors for the tensor-core path");
     }
     nb.maps_ok = true;
+  }
+  if (m.mx.ok) {
+    cudaError_t e = mx_make_maps(m, nb);
+    if (e != cudaSuccess) {
+      cudaFree(nb.base);
+      return cuda_err(e, "TMA descriptors for the block-scaled path");
+    }
+    nb.mx_maps_ok = true;
   }
   free_expert_bufs(eb);
   eb = nb;
@@ -616,6 +675,10 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
     ce = gb::tc_prepare_weights(m);
     if (ce != cudaSuccess) rc = cuda_err(ce, "row exponents for the tensor-core path");
   }
+  if (!rc && gb::mx_supported(m)) {
+    ce = gb::mx_prepare_weights(m);
+    if (ce != cudaSuccess) rc = cuda_err(ce, "block-scaled weight layout");
+  }
   if (!rc) rc = alloc_ws(m, std::max(1, desc->max_tokens));
   if (rc) {
     const std::string msg = g_err;  // release must not overwrite the cause
@@ -662,7 +725,7 @@ int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_ho
     GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
             "copy out");
   GB_CUDA(cudaStreamSynchronize(st), "synchronise forward");
-  return GB_OK;
+  return read_device_status(m, st);
 }
 
 int gb_moe_route(gb_moe* h, const float* x_dev, int64_t T, int32_t* idx_dev, float* w_dev,
@@ -713,6 +776,13 @@ int gb_moe_dequant_expert(gb_moe* h, int32_t which, int32_t expert, float* out_d
     GB_CUDA(gb::launch_dequant_expert(m, which, expert - m.e_begin, out_dev, st), "dequant launch");
   GB_CUDA(cudaStreamSynchronize(st), "synchronise dequant");
   return GB_OK;
+}
+
+int gb_moe_device_status(gb_moe* h, void* stream) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  DeviceScope ds(h->m.device);
+  return read_device_status(h->m, static_cast<cudaStream_t>(stream));
 }
 
 int gb_moe_get_info(const gb_moe* h, gb_moe_info* info) {
@@ -775,9 +845,9 @@ int gb_moe_destroy(gb_moe* h) {
 int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
   int rc = check_handle(h);
   if (rc) return rc;
-  if (path != GB_PATH_AUTO && path != GB_PATH_CUDA_CORES && path != GB_PATH_TENSOR_CORES)
+  if (path < GB_PATH_AUTO || path > GB_PATH_TENSOR_CORES_F16)
     return set_err(GB_ERR_INVALID_ARG, "unknown expert path %d", path);
-  if (path == GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m))
+  if (path >= GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m) && !h->m.mx.ok)
     return set_err(GB_ERR_UNSUPPORTED,
                    "tensor-core expert path needs the GPT-OSS activation and H, I multiples of 64");
   h->m.expert_path = path;

@@ -43,6 +43,28 @@ struct ExpertWeights {
   uint8_t* q4_dn = nullptr;
 };
 
+// Weights in the block-scaled tensor-core layout (mx_gemm.cu), built from
+// ExpertWeights at load time (KC = roundup(K, 128) / 128):
+//   gu_nib [E_loc][KC_H][2I][64 B], dn_nib [E_loc][KC_I][H][64 B]  nibbles,
+//     K-chunk major, codes past K zero
+//   gu_sfa [E_loc][KC_H][MT2_GU][512], dn_sfa likewise: E8M0 bytes of each
+//     128-row x 4-block tile in the MMA's scale-factor order
+struct MxWeights {
+  bool ok = false;
+  uint8_t* gu_nib = nullptr;
+  uint8_t* dn_nib = nullptr;
+  uint8_t* gu_sfa = nullptr;
+  uint8_t* dn_sfa = nullptr;
+  int kc_h = 0, kc_i = 0;      // 128-code chunks of gate_up (H) and down (I)
+  int mt2_gu = 0, mt2_dn = 0;  // scale atoms per chunk (128-row tiles, even)
+  int h_exp = 0;               // h enters down as pieces of h * 2^-h_exp
+  int64_t weight_bytes = 0;
+  alignas(64) unsigned char map_gu128[128] = {};  // CUtensorMaps, 128- and 256-row boxes
+  alignas(64) unsigned char map_dn128[128] = {};
+  alignas(64) unsigned char map_gu256[128] = {};
+  alignas(64) unsigned char map_dn256[128] = {};
+};
+
 // The grouped view the expert kernels work on: rows grouped by expert
 // (expert ascending), each group a contiguous range of positions.
 struct Groups {
@@ -70,14 +92,26 @@ struct ExpertBufs {
   float* xscale = nullptr;     // [rows] exponent s of each row (x = 2^s (hi + lo))
   __half* hh = nullptr;        // [rows, I] SwiGLU output, f16 hi
   __half* hl = nullptr;        // [rows, I] f16 lo
-  int32_t* tile_expert = nullptr;  // [rows/128 + E] N-tile table
+  int32_t* tile_expert = nullptr;  // [rows + E + 1] N-tile table (tiles of >= 1 row)
   int32_t* tile_row0 = nullptr;
   int32_t* tile_rows = nullptr;
   alignas(64) unsigned char map_xh[128] = {};  // CUtensorMap of xh (TMA)
   alignas(64) unsigned char map_xl[128] = {};
   alignas(64) unsigned char map_hh[128] = {};
   alignas(64) unsigned char map_hl[128] = {};
+  alignas(64) unsigned char map_xh16[128] = {};  // the same tensors, 16-row boxes
+  alignas(64) unsigned char map_xl16[128] = {};
+  alignas(64) unsigned char map_hh16[128] = {};
+  alignas(64) unsigned char map_hl16[128] = {};
+  uint8_t* xq = nullptr;       // E4M3 pieces of the grouped activations, 5 per element:
+  uint8_t* hq = nullptr;       //   [5][rows][H] (prefill tiles) or [rows][5][H] (decode
+                               //   tiles); hq likewise for the SwiGLU output (I)
+  alignas(64) unsigned char map_xq_p[128] = {};  // CUtensorMaps, prefill layout
+  alignas(64) unsigned char map_hq_p[128] = {};
+  alignas(64) unsigned char map_xq_d[5][128] = {};  // decode layout, tiles of 1..16
+  alignas(64) unsigned char map_hq_d[5][128] = {};  // positions (index log2)
   bool maps_ok = false;
+  bool mx_maps_ok = false;
 };
 
 // Per-forward routing scratch, sized for `tokens` local tokens.
@@ -113,6 +147,7 @@ struct Moe {
   float* router_b = nullptr;  // [E] or null
   float* sel_bias = nullptr;  // [E] or null
   ExpertWeights w;
+  MxWeights mx;
   int64_t weight_bytes = 0;
   Workspace ws;
   struct Ep* ep = nullptr;  // expert-parallel state (ep_size > 1), ep.cu
@@ -154,13 +189,34 @@ cudaError_t launch_q4k_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaS
 cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float* out,
                                cudaStream_t st);
 
+// Block-scaled tensor-core expert path (mx_gemm.cu).
+constexpr int kDecodeTileKinds = 5;  // decode tiles of 1, 2, 4, 8, 16 positions
+bool mx_supported(const Moe& m);
+cudaError_t mx_prepare_weights(Moe& m);
+void mx_release(MxWeights& x);
+cudaError_t mx_make_maps(const Moe& m, ExpertBufs& eb);
+size_t mx_piece_bytes(int64_t rows, int k);
+// decode_tiles: operands swapped, 16 positions x 8 piece slots per tile
+// (decode-sized batches); otherwise 128 weight rows x 128 positions.
+cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                              bool decode_tiles, cudaStream_t st);
+cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, bool decode_tiles,
+                           cudaStream_t st);
+
+// N-tile table of the local experts' grouped rows, tiles of bn rows (tc_gemm.cu).
+cudaError_t launch_tile_table(const Moe& m, const Groups& g, int bn, ExpertBufs& eb,
+                              cudaStream_t st);
+
 // Tensor-core expert path (tc_gemm.cu).
 bool tc_supported(const Moe& m);
 cudaError_t tc_prepare_weights(Moe& m);
 cudaError_t tc_make_maps(const Moe& m, ExpertBufs& eb);
+// small_tiles: 16-token tiles with the weights decoded into tensor memory
+// (decode-sized batches); otherwise 128-token tiles.
 cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
-                              cudaStream_t st);
-cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+                              bool small_tiles, cudaStream_t st);
+cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, bool small_tiles,
+                           cudaStream_t st);
 
 // out[t] = sum_r w[t, r] * y[inv[t*k + r]] in the fixed order (expert_gemv.cu).
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
@@ -174,6 +230,8 @@ cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, ui
 // Expert parallelism (ep.cu).
 struct Ep;
 int nccl_unique_id(uint8_t out[128]);
+// The EP grouping's meta array ([1] holds error bits), or null without EP.
+int32_t* ep_meta(Moe& m);
 int ep_init(Moe& m, const uint8_t* nccl_id);
 void ep_destroy(Moe& m);
 int ep_forward(Moe& m, const float* x, int64_t T, float* out, cudaStream_t st);

@@ -37,6 +37,8 @@ GB_FMT_Q4_K = 2
 GB_PATH_AUTO = 0
 GB_PATH_CUDA_CORES = 1
 GB_PATH_TENSOR_CORES = 2
+GB_PATH_TENSOR_CORES_SMALL_TILES = 3
+GB_PATH_TENSOR_CORES_F16 = 4
 GB_DTYPE_F32 = 0
 GB_DTYPE_BF16 = 1
 
@@ -107,6 +109,7 @@ SIGNATURES = {
                              c_void_p, c_void_p, c_void_p]),
     "gb_moe_dequant_expert": (c_int, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "gb_moe_get_info": (c_int, [c_void_p, POINTER(MoeInfo)]),
+    "gb_moe_device_status": (c_int, [c_void_p, c_void_p]),
     "gb_moe_destroy": (c_int, [c_void_p]),
     "gb_moe_set_expert_path": (c_int, [c_void_p, c_int32]),
     "gb_moe_set_profiling": (c_int, [c_void_p, c_int]),

@@ -78,8 +78,12 @@ class MoEBlock:
         return {f: getattr(inf, f) for f, _ in MoeInfo._fields_ if f != "struct_size"}
 
     # -- forward -------------------------------------------------------------
-    def forward(self, x):
-        """x: torch.Tensor (batch, seq, hidden) or (tokens, hidden)."""
+    def forward(self, x, check_status: bool = True):
+        """x: torch.Tensor (batch, seq, hidden) or (tokens, hidden).
+
+        With check_status (the default) a device input waits for the forward
+        and raises if a kernel recorded an error; pass False to keep the call
+        asynchronous and call device_status() when the output is consumed."""
         import torch
 
         shape = x.shape
@@ -92,6 +96,8 @@ class MoEBlock:
             out = torch.empty_like(xf)
             stream = torch.cuda.current_stream(xf.device).cuda_stream
             check(self._lib.gb_moe_forward(self._h, xf.data_ptr(), T, out.data_ptr(), stream))
+            if check_status:
+                check(self._lib.gb_moe_device_status(self._h, stream))
         else:
             out = torch.empty_like(xf)
             check(self._lib.gb_moe_forward_host(self._h, xf.data_ptr(), T, out.data_ptr(), None))
@@ -99,14 +105,21 @@ class MoEBlock:
 
     __call__ = forward
 
+    def device_status(self, stream: int = 0) -> None:
+        """Waits for `stream` and raises if a forward kernel recorded an error."""
+        check(self._lib.gb_moe_device_status(self._h, stream))
+
     def forward_raw(self, x_ptr: int, T: int, out_ptr: int, stream: int = 0) -> None:
         """Device pointers straight through to gb_moe_forward (no checks)."""
         check(self._lib.gb_moe_forward(self._h, x_ptr, T, out_ptr, stream))
 
     def set_expert_path(self, path: str) -> None:
-        """'auto', 'cuda_cores' or 'tensor_cores'."""
+        """'auto', 'cuda_cores', 'tensor_cores', 'tensor_cores_small_tiles' or
+        'tensor_cores_f16' (gb_moe_set_expert_path)."""
         code = {"auto": _lib.GB_PATH_AUTO, "cuda_cores": _lib.GB_PATH_CUDA_CORES,
-                "tensor_cores": _lib.GB_PATH_TENSOR_CORES}[path]
+                "tensor_cores": _lib.GB_PATH_TENSOR_CORES,
+                "tensor_cores_small_tiles": _lib.GB_PATH_TENSOR_CORES_SMALL_TILES,
+                "tensor_cores_f16": _lib.GB_PATH_TENSOR_CORES_F16}[path]
         check(self._lib.gb_moe_set_expert_path(self._h, code))
 
     def set_profiling(self, enable: bool = True) -> None:

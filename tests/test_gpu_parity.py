@@ -256,53 +256,92 @@ def test_full_size_rows_do_not_depend_on_the_batch(moe32, big_run):
 
 # ---- tensor-core expert path (tcgen05) ---------------------------------------
 
+# "tensor_cores": block-scaled MMA, 128 weight rows x 128 positions;
+# "tensor_cores_small_tiles": block-scaled MMA, operands swapped, 16 positions;
+# "tensor_cores_f16": weights decoded to f16 in shared memory, kind::f16.
+TC_PATHS = ["tensor_cores", "tensor_cores_small_tiles", "tensor_cores_f16"]
+
+
+@pytest.mark.parametrize("path", TC_PATHS)
 @pytest.mark.parametrize("T", [1, 8, 64, 300])
-def test_tensor_core_path_matches_oracle(moe32, layer32, T):
+def test_tensor_core_path_matches_oracle(moe32, layer32, T, path):
     x = synth.tokens(T, 2880, seed=500 + T)
     want, _, _ = oracle.OracleMoe(layer32).forward(x)
-    moe32.set_expert_path("tensor_cores")
+    moe32.set_expert_path(path)
     try:
         got = moe32.forward(_cuda(x)).cpu().numpy()
     finally:
         moe32.set_expert_path("auto")
-    assert_parity(got, want, f"tensor cores T={T}")
+    assert_parity(got, want, f"{path} T={T}")
 
 
-def test_tensor_core_and_cuda_core_paths_agree(moe32):
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_tensor_core_and_cuda_core_paths_agree(moe32, path):
     x = _cuda(synth.tokens(200, 2880, seed=42))
     moe32.set_expert_path("cuda_cores")
     a = moe32.forward(x).cpu().numpy()
-    moe32.set_expert_path("tensor_cores")
+    moe32.set_expert_path(path)
     b = moe32.forward(x).cpu().numpy()
     moe32.set_expert_path("auto")
-    assert_parity(b, a, "tensor vs cuda cores")
+    assert_parity(b, a, f"{path} vs cuda cores")
 
 
-def test_tensor_core_path_skewed_and_gguf(layer32_skew):
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_tensor_core_path_skewed_and_gguf(layer32_skew, path):
     gg = synth.gptoss_gguf_from_split(layer32_skew)
     m = GptOssQMoEFFN.load(gg, device=0, max_tokens=256)
     try:
-        m.set_expert_path("tensor_cores")
+        m.set_expert_path(path)
         x = synth.tokens(256, 2880, seed=8)
         got = m.forward(_cuda(x)).cpu().numpy()
         want, _, _ = oracle.OracleMoe(layer32_skew, gguf=gg).forward(x)
-        assert_parity(got, want, "tensor cores, skewed, gguf")
+        assert_parity(got, want, f"{path}, skewed, gguf")
     finally:
         m.close()
 
 
-def test_tensor_core_path_handles_large_and_tiny_activations(moe32, layer32):
+@pytest.mark.parametrize("path", TC_PATHS)
+def test_tensor_core_path_handles_large_and_tiny_activations(moe32, layer32, path):
     # per-row power-of-two scaling keeps f16 hi/lo in range
     x = synth.tokens(64, 2880, seed=77)
     x[0] *= 3.0e4
     x[1] *= 1.0e-5
     want, _, _ = oracle.OracleMoe(layer32).forward(x)
-    moe32.set_expert_path("tensor_cores")
+    moe32.set_expert_path(path)
     try:
         got = moe32.forward(_cuda(x)).cpu().numpy()
     finally:
         moe32.set_expert_path("auto")
-    assert_parity(got[2:], want[2:], "tensor cores, ordinary rows")
+    assert_parity(got[2:], want[2:], f"{path}, ordinary rows")
     for r in (0, 1):
         err = np.abs(got[r] - want[r])
         assert err.sum() / np.abs(want[r]).sum() <= MEAN_REL, r
+
+
+@pytest.mark.parametrize("T", [2, 16, 32, 100])
+def test_small_tiles_every_tile_width(moe32, layer32, T):
+    # 32 experts, top-4: the decode tile holds 1, 2, 4, 8 or 16 positions,
+    # chosen from the mean rows per expert (T = 2, 8, 16, 32, >= 64)
+    x = synth.tokens(T, 2880, seed=900 + T)
+    want, _, _ = oracle.OracleMoe(layer32).forward(x)
+    moe32.set_expert_path("tensor_cores_small_tiles")
+    try:
+        got = moe32.forward(_cuda(x)).cpu().numpy()
+    finally:
+        moe32.set_expert_path("auto")
+    assert_parity(got, want, f"small tiles T={T}")
+
+
+def test_small_tiles_on_odd_shapes():
+    # H, I multiples of 64 but not of 128: partial M tiles on both GEMMs
+    layer = synth.gptoss_layer(n_experts=8, hidden=320, inter=192, seed=12)
+    m = OssMoEFFN.load(layer, device=0, max_tokens=40)
+    try:
+        for path in TC_PATHS:
+            m.set_expert_path(path)
+            x = synth.tokens(37, 320, seed=13)
+            got = m.forward(_cuda(x)).cpu().numpy()
+            want, _, _ = oracle.OracleMoe(layer).forward(x)
+            assert_parity(got, want, f"{path}, H=320 I=192")
+    finally:
+        m.close()
