@@ -41,9 +41,9 @@
 //   mx_expert_gemm  many positions per expert.  A = 128 weight rows, B = 128
 //     positions, one MMA per piece (piece 0 into one accumulator, pieces 1-4
 //     into another, so small terms are not added into the large sum).
-// Both run a persistent grid (one CTA per SM) over work items (N tile,
-// M tile), M fastest, with warp roles: 0-3 epilogue (TMEM lanes 0-127), TMA
-// producer(s), MMA issuer.  Every mbarrier wait is bounded: on timeout the CTA
+// Both run a persistent grid (one or two CTAs per SM) over work items
+// (N tile, M tile), M fastest, with warp roles: 0-3 epilogue (TMEM lanes
+// 0-127), TMA producer(s), MMA issuer.  Every mbarrier wait is bounded: on timeout the CTA
 // raises an abort flag, records error bit 2, lets in-flight copies land,
 // frees its TMEM and returns.
 #include <cuda.h>
@@ -207,24 +207,28 @@ __device__ __forceinline__ void linger_2ms() {
 constexpr int kDecThreads = 224;  // warps 0-3 epilogue, 4 and 6 TMA, 5 MMA
 constexpr int DM = 256;           // weight rows per tile
 
+// CPS CTAs share an SM (2 for NT <= 8: each issues its own copies, which
+// raises the SM's copy rate; TMEM <= 256 columns and half the shared memory
+// each).
 template <int NT>
 struct Dec {
+  static constexpr int CPS = NT <= 8 ? 2 : 1;
   static constexpr int N = 8 * NT;
   static constexpr int W_BYTES = DM * BK;            // 32 KB in shared memory, 16 KB packed
   static constexpr int X_BYTES = N * BK;             // NT positions x 8 slots x 128 bytes
   static constexpr int SFW = 2 * SF_BYTES;           // scale atoms of the two halves
   static constexpr int STAGE = (W_BYTES + X_BYTES + SFW + 1023) / 1024 * 1024;
-  static constexpr int STAGES = std::min(6, (kSmemLimit - 1024 - SF_BYTES - 256) / STAGE);
-  static constexpr int ACCS = N <= 32 ? 2 : 1;       // accumulators per half and tile
-  static constexpr int NACC = NT <= 8 ? 2 : 1;       // tile buffers
+  static constexpr int STAGES = std::min(6, (kSmemLimit / CPS - 1024 - SF_BYTES - 256) / STAGE);
+  static constexpr int ACCS = N <= 16 ? 2 : 1;       // accumulators per half and tile
+  static constexpr int NACC = NT <= 4 ? 2 : 1;       // tile buffers
   static constexpr int BUF = 2 * ACCS * N;
   static constexpr int SFB_COL = NACC * BUF;         // constant slot scales, 4 columns
   static constexpr int SFA_COL = SFB_COL + 4;        // 8 columns per stage
   static constexpr int USED = SFA_COL + 8 * STAGES;
   static constexpr int TMEM_COLS = USED <= 128 ? 128 : USED <= 256 ? 256 : 512;
   static constexpr size_t SMEM = (size_t)STAGES * STAGE + SF_BYTES + 1024 + 256;
-  static_assert(USED <= 512, "tensor memory");
-  static_assert(SMEM <= (size_t)kSmemLimit, "shared memory");
+  static_assert(TMEM_COLS * CPS <= 512, "tensor memory");
+  static_assert(SMEM * CPS <= (size_t)kSmemLimit, "shared memory");
   // A = E2M1 (5), B = E4M3 (0), N, M = 128, E8M0 scales; bits 29-30 select
   // the A scale block (the weights' scale byte of the K = 32 step).
   static constexpr uint32_t IDESC = (5u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) |
@@ -232,7 +236,7 @@ struct Dec {
 };
 
 template <int MODE, int NT>
-__global__ void __launch_bounds__(kDecThreads, 1)
+__global__ void __launch_bounds__(kDecThreads, Dec<NT>::CPS)
     mx_decode_gemm(const __grid_constant__ CUtensorMap tmap_w,
                    const __grid_constant__ CUtensorMap tmap_x, const Args a) {
   using D = Dec<NT>;
@@ -785,7 +789,8 @@ cudaError_t launch_decode(const Moe& m, const mx::Args& a, const void* map_w, co
   const size_t smem = mx::Dec<NT>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k<<<m.sm_count, mx::kDecThreads, smem, st>>>(*reinterpret_cast<const CUtensorMap*>(map_w),
+  k<<<m.sm_count * mx::Dec<NT>::CPS, mx::kDecThreads, smem, st>>>(
+      *reinterpret_cast<const CUtensorMap*>(map_w),
                                                *reinterpret_cast<const CUtensorMap*>(map_x), a);
   return cudaGetLastError();
 }
@@ -816,13 +821,15 @@ cudaError_t launch_mx(const Moe& m, const mx::Args& a, const ExpertBufs& eb, int
   return cudaGetLastError();
 }
 
-// Positions per decode tile: the power of two (1..16) at or above twice the
-// mean rows per local expert.
+// Positions per decode tile: the power of two at or above twice the mean
+// rows per local expert, at most 8 (two CTAs per SM) while the mean is at
+// most 8, else 16.
 int decode_nt_log2(const Moe& m, const Groups& g) {
   const int64_t nloc = std::max<int64_t>(1, m.e_end - m.e_begin);
+  if (g.rows > 8 * nloc) return kDecodeTileKinds - 1;
   const int64_t target = (2 * g.rows + nloc - 1) / nloc;
   int l = 0;
-  while (l < kDecodeTileKinds - 1 && (int64_t(1) << l) < target) ++l;
+  while (l < kDecodeTileKinds - 2 && (int64_t(1) << l) < target) ++l;
   return l;
 }
 

@@ -691,24 +691,36 @@ __global__ void split_gather_kernel(const float* __restrict__ x, const int32_t* 
 }
 
 // N-tile table over the local experts: tile j covers grouped positions
-// [row0, row0 + rows) of expert tile_expert[j].  meta[2] = number of tiles.
+// [row0, row0 + rows) of expert tile_expert[j], experts ascending.
+// meta[2] = number of tiles.  One warp: lane l takes expert base + l, an
+// exclusive warp scan of the tile counts places its tiles.
 __global__ void tile_table_kernel(const int32_t* __restrict__ counts,
                                   const int32_t* __restrict__ offsets, int e_begin, int e_end,
                                   int bn, int32_t* __restrict__ meta,
                                   int32_t* __restrict__ tile_expert,
                                   int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows) {
-  if (threadIdx.x != 0) return;
-  int j = 0;
-  for (int e = e_begin; e < e_end; ++e) {
-    const int c = counts[e];
-    for (int i = 0; i < c; i += bn) {
-      tile_expert[j] = e;
-      tile_row0[j] = offsets[e] + i;
-      tile_rows[j] = min(bn, c - i);
-      ++j;
+  const int lane = threadIdx.x;
+  int base_j = 0;
+  for (int e0 = e_begin; e0 < e_end; e0 += 32) {
+    const int e = e0 + lane;
+    const int c = e < e_end ? counts[e] : 0;
+    const int off = e < e_end ? offsets[e] : 0;
+    const int nt = (c + bn - 1) / bn;
+    int incl = nt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int v = __shfl_up_sync(kFullMask, incl, d);
+      if (lane >= d) incl += v;
     }
+    int j = base_j + incl - nt;
+    for (int i = 0; i < c; i += bn, ++j) {
+      tile_expert[j] = e;
+      tile_row0[j] = off + i;
+      tile_rows[j] = min(bn, c - i);
+    }
+    base_j += __shfl_sync(kFullMask, incl, 31);
   }
-  meta[2] = j;
+  if (lane == 0) meta[2] = base_j;
 }
 
 // Largest E8M0 byte of each weight row.

@@ -318,10 +318,11 @@ def test_tensor_core_path_handles_large_and_tiny_activations(moe32, layer32, pat
         assert err.sum() / np.abs(want[r]).sum() <= MEAN_REL, r
 
 
-@pytest.mark.parametrize("T", [2, 16, 32, 100])
+@pytest.mark.parametrize("T", [2, 8, 16, 32, 100])
 def test_small_tiles_every_tile_width(moe32, layer32, T):
-    # 32 experts, top-4: the decode tile holds 1, 2, 4, 8 or 16 positions,
-    # chosen from the mean rows per expert (T = 2, 8, 16, 32, >= 64)
+    # 32 experts, top-4, mean T / 8 rows per expert: the decode tile holds
+    # 1, 2, 4, 8 or 16 positions (twice the mean, rounded up to a power of
+    # two, at most 8 while the mean is at most 8)
     x = synth.tokens(T, 2880, seed=900 + T)
     want, _, _ = oracle.OracleMoe(layer32).forward(x)
     moe32.set_expert_path("tensor_cores_small_tiles")
