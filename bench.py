@@ -62,8 +62,7 @@ def parse_args():
                     help="extra per-GPU batch sizes to measure ('' = none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--expert-path", default="auto",
-                    choices=["auto", "cuda_cores", "tensor_cores", "tensor_cores_small_tiles",
-                             "tensor_cores_f16"],
+                    choices=["auto", "cuda_cores", "tensor_cores", "tensor_cores_f16"],
                     help="force one expert kernel (gb_moe_set_expert_path)")
     ap.add_argument("--cpu-threads", type=int, default=0)
     return ap.parse_args()

@@ -187,24 +187,20 @@ int gb_moe_get_info(const gb_moe* m, gb_moe_info* info);
  * failure. */
 int gb_moe_device_status(gb_moe* m, void* stream);
 
-/* Which kernels run the expert products.  AUTO picks, for batches averaging
- * at most 32 rows per local expert, the block-scaled tcgen05 GEMM with
- * decode tiles (MXFP4 weights as stored, 256 weight rows x 1-16 positions,
- * activations as E4M3 pieces), and for larger ones the kind::f16 GEMM with
- * 128-position tiles that decodes the weights to f16 in shared memory
- * (activations as f16 hi + lo).  The others force one kernel: CUDA_CORES the
- * streaming MXFP4 rows with f32 FMA; TENSOR_CORES the block-scaled GEMM with
- * 128-position tiles; TENSOR_CORES_SMALL_TILES the block-scaled decode
- * tiles; TENSOR_CORES_F16 the kind::f16 GEMM.  The tensor-core kernels need
- * the GPT-OSS activation and H, I multiples of 64; without them AUTO uses
- * the CUDA cores.  Q4_K experts always run on the CUDA cores.  No
- * counterpart in the reference, which has one CPU path. */
+/* Which kernels run the expert products.  AUTO and TENSOR_CORES pick the
+ * block-scaled tcgen05 GEMM (MXFP4 weights as stored, activations as four
+ * E4M3 pieces, tiles of 256 weight rows x 2-32 positions chosen from the
+ * batch); CUDA_CORES forces the streaming MXFP4 rows with f32 FMA;
+ * TENSOR_CORES_F16 the kind::f16 GEMM that decodes the weights to f16 in
+ * shared memory (activations as f16 hi + lo, 128-position tiles).  The
+ * tensor-core kernels need the GPT-OSS activation and H, I multiples of 64;
+ * without them every path uses the CUDA cores.  Q4_K experts always run on
+ * the CUDA cores.  No counterpart in the reference, which has one CPU path. */
 typedef enum {
   GB_PATH_AUTO = 0,
   GB_PATH_CUDA_CORES = 1,
   GB_PATH_TENSOR_CORES = 2,
-  GB_PATH_TENSOR_CORES_SMALL_TILES = 3,
-  GB_PATH_TENSOR_CORES_F16 = 4
+  GB_PATH_TENSOR_CORES_F16 = 3
 } gb_expert_path;
 int gb_moe_set_expert_path(gb_moe* m, int32_t path);
 

@@ -422,31 +422,18 @@ int run_route(gb::Moe& m, const float* x, int64_t T, cudaStream_t st) {
   return mark(m, 2, st);
 }
 
-// Batches averaging more than this many rows per local expert take the
-// 128-position prefill tiles; smaller ones the decode tiles, which read each
-// weight tile once per 1-16 positions.
-constexpr int64_t kDecodeMaxRowsPerExpert = 32;
+enum class ExpertKernel { kCudaCores, kF16, kMx };
 
-enum class ExpertKernel { kCudaCores, kF16Large, kF16Small, kMxLarge, kMxSmall };
-
-ExpertKernel pick_expert_kernel(const gb::Moe& m, const gb::ExpertBufs& eb, int64_t rows) {
+ExpertKernel pick_expert_kernel(const gb::Moe& m, const gb::ExpertBufs& eb) {
   const bool mx = m.mx.ok && eb.mx_maps_ok;
   const bool f16 = gb::tc_supported(m) && eb.maps_ok;
-  const bool large = rows > kDecodeMaxRowsPerExpert * std::max<int64_t>(1, m.e_end - m.e_begin);
   switch (m.expert_path) {
     case GB_PATH_CUDA_CORES:
       return ExpertKernel::kCudaCores;
     case GB_PATH_TENSOR_CORES_F16:
-      return f16 ? ExpertKernel::kF16Large : ExpertKernel::kCudaCores;
-    case GB_PATH_TENSOR_CORES:
-      return mx ? ExpertKernel::kMxLarge : f16 ? ExpertKernel::kF16Large : ExpertKernel::kCudaCores;
-    case GB_PATH_TENSOR_CORES_SMALL_TILES:
-      return mx ? ExpertKernel::kMxSmall : f16 ? ExpertKernel::kF16Small : ExpertKernel::kCudaCores;
-    default:
-      // prefill: the f16 tiles are faster than the block-scaled ones so far
-      if (large) return f16 ? ExpertKernel::kF16Large : mx ? ExpertKernel::kMxLarge
-                                                         : ExpertKernel::kCudaCores;
-      return mx ? ExpertKernel::kMxSmall : f16 ? ExpertKernel::kF16Small : ExpertKernel::kCudaCores;
+      return f16 ? ExpertKernel::kF16 : ExpertKernel::kCudaCores;
+    default:  // AUTO, TENSOR_CORES
+      return mx ? ExpertKernel::kMx : f16 ? ExpertKernel::kF16 : ExpertKernel::kCudaCores;
   }
 }
 
@@ -524,18 +511,16 @@ int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& 
     if ((rc = mark(m, 3, st))) return rc;
     GB_CUDA(launch_q4k_down(m, g, eb, st), "Q4_K down launch");
     m.launches += 2;
-  } else if (const ExpertKernel k = pick_expert_kernel(m, eb, g.rows);
-             k != ExpertKernel::kCudaCores) {
-    if (k == ExpertKernel::kMxLarge || k == ExpertKernel::kMxSmall) {
-      const bool small = k == ExpertKernel::kMxSmall;
-      GB_CUDA(launch_mx_gate_up(m, g, x, eb, small, st), "block-scaled gate_up launch");
+  } else if (const ExpertKernel k = pick_expert_kernel(m, eb); k != ExpertKernel::kCudaCores) {
+    if (k == ExpertKernel::kMx) {
+      const int kind = gb::mx_tile_kind(m, g);
+      GB_CUDA(launch_mx_gate_up(m, g, x, eb, kind, st), "block-scaled gate_up launch");
       if ((rc = mark(m, 3, st))) return rc;
-      GB_CUDA(launch_mx_down(m, g, eb, small, st), "block-scaled down launch");
+      GB_CUDA(launch_mx_down(m, g, eb, kind, st), "block-scaled down launch");
     } else {
-      const bool small = k == ExpertKernel::kF16Small;
-      GB_CUDA(launch_tc_gate_up(m, g, x, eb, small, st), "tensor-core gate_up launch");
+      GB_CUDA(launch_tc_gate_up(m, g, x, eb, st), "tensor-core gate_up launch");
       if ((rc = mark(m, 3, st))) return rc;
-      GB_CUDA(launch_tc_down(m, g, eb, small, st), "tensor-core down launch");
+      GB_CUDA(launch_tc_down(m, g, eb, st), "tensor-core down launch");
     }
     m.launches += 4;  // tile table, split, two GEMMs
   } else if (decode_supported(m)) {

@@ -59,10 +59,8 @@ struct MxWeights {
   int mt2_gu = 0, mt2_dn = 0;  // scale atoms per chunk (128-row tiles, even)
   int h_exp = 0;               // h enters down as pieces of h * 2^-h_exp
   int64_t weight_bytes = 0;
-  alignas(64) unsigned char map_gu128[128] = {};  // CUtensorMaps, 128- and 256-row boxes
-  alignas(64) unsigned char map_dn128[128] = {};
-  alignas(64) unsigned char map_gu256[128] = {};
-  alignas(64) unsigned char map_dn256[128] = {};
+  alignas(64) unsigned char map_gu[128] = {};  // CUtensorMaps, 256-row boxes of one chunk
+  alignas(64) unsigned char map_dn[128] = {};
 };
 
 // The grouped view the expert kernels work on: rows grouped by expert
@@ -99,17 +97,10 @@ struct ExpertBufs {
   alignas(64) unsigned char map_xl[128] = {};
   alignas(64) unsigned char map_hh[128] = {};
   alignas(64) unsigned char map_hl[128] = {};
-  alignas(64) unsigned char map_xh16[128] = {};  // the same tensors, 16-row boxes
-  alignas(64) unsigned char map_xl16[128] = {};
-  alignas(64) unsigned char map_hh16[128] = {};
-  alignas(64) unsigned char map_hl16[128] = {};
-  uint8_t* xq = nullptr;       // E4M3 pieces of the grouped activations, 5 per element:
-  uint8_t* hq = nullptr;       //   [5][rows][H] (prefill tiles) or [rows][5][H] (decode
-                               //   tiles); hq likewise for the SwiGLU output (I)
-  alignas(64) unsigned char map_xq_p[128] = {};  // CUtensorMaps, prefill layout
-  alignas(64) unsigned char map_hq_p[128] = {};
-  alignas(64) unsigned char map_xq_d[5][128] = {};  // decode layout, tiles of 1..16
-  alignas(64) unsigned char map_hq_d[5][128] = {};  // positions (index log2)
+  uint8_t* xq = nullptr;       // [rows][4][H] E4M3 pieces of the grouped activations
+  uint8_t* hq = nullptr;       // [rows][4][I] E4M3 pieces of the SwiGLU output
+  alignas(64) unsigned char map_xq[5][128] = {};  // CUtensorMaps, tiles of 2, 4, 8, 16, 30
+  alignas(64) unsigned char map_hq[5][128] = {};  // positions (index: kind)
   bool maps_ok = false;
   bool mx_maps_ok = false;
 };
@@ -190,17 +181,18 @@ cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float*
                                cudaStream_t st);
 
 // Block-scaled tensor-core expert path (mx_gemm.cu).
-constexpr int kDecodeTileKinds = 5;  // decode tiles of 1, 2, 4, 8, 16 positions
+constexpr int kMxTileKinds = 5;  // tiles of 2, 4, 8, 16, 30 positions
 bool mx_supported(const Moe& m);
 cudaError_t mx_prepare_weights(Moe& m);
 void mx_release(MxWeights& x);
 cudaError_t mx_make_maps(const Moe& m, ExpertBufs& eb);
 size_t mx_piece_bytes(int64_t rows, int k);
-// decode_tiles: operands swapped, 16 positions x 8 piece slots per tile
-// (decode-sized batches); otherwise 128 weight rows x 128 positions.
+// Tile kind for a grouping of this size, and the positions per tile of a kind.
+int mx_tile_kind(const Moe& m, const Groups& g);
+int mx_tile_positions(int kind);
 cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
-                              bool decode_tiles, cudaStream_t st);
-cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, bool decode_tiles,
+                              int kind, cudaStream_t st);
+cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, int kind,
                            cudaStream_t st);
 
 // N-tile table of the local experts' grouped rows, tiles of bn rows (tc_gemm.cu).
@@ -211,12 +203,9 @@ cudaError_t launch_tile_table(const Moe& m, const Groups& g, int bn, ExpertBufs&
 bool tc_supported(const Moe& m);
 cudaError_t tc_prepare_weights(Moe& m);
 cudaError_t tc_make_maps(const Moe& m, ExpertBufs& eb);
-// small_tiles: 16-token tiles with the weights decoded into tensor memory
-// (decode-sized batches); otherwise 128-token tiles.
 cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
-                              bool small_tiles, cudaStream_t st);
-cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, bool small_tiles,
-                           cudaStream_t st);
+                              cudaStream_t st);
+cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
 
 // out[t] = sum_r w[t, r] * y[inv[t*k + r]] in the fixed order (expert_gemv.cu).
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,

@@ -385,259 +385,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
-// ---------------------------------------------------------------------------
-// Decode-sized batches: the same math with the A operand in TMEM.
-//
-// Tokens per expert are few, so the tile is M = 128 weight rows x N = 16
-// tokens and the weight stream dominates.  The decode warps write each
-// 64-element K chunk of their row straight into TMEM (tcgen05.st; lane = row,
-// two f16 per 32-bit column), and the MMA reads A from there (kind::f16 with
-// A in tensor memory), so shared memory holds only the TMA ring: 24 stages of
-// {activation hi 2 KB, lo 2 KB, raw MXFP4 4 KB}, about 96 KB of weight bytes
-// in flight per SM.  TMEM: four A stages (4 x 32 columns) and two hi/lo
-// accumulator pairs (2 x 32 columns).
-// ---------------------------------------------------------------------------
-constexpr int DBN = 16;
-constexpr int DRS = 24;
-constexpr int DAS = 4;
-constexpr int D_B_BYTES = DBN * BK * 2;                  // 2 KB
-constexpr int D_STAGE = 2 * D_B_BYTES + RAW_BYTES;        // 8 KB
-constexpr int D_TMEM_COLS = 256;
-constexpr int D_ACC_COL = DAS * 32;                       // first accumulator column
-constexpr size_t kDecSmemBytes = (size_t)DRS * D_STAGE + BM * kScaleRow + 1024 + 512;
-constexpr uint32_t kIdescDec =
-    (1u << 4) | ((uint32_t)(DBN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
-
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                           uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(kIdescDec), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
-      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
-      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
-      "r"(v[29]), "r"(v[30]), "r"(v[31])
-      : "memory");
-}
-
-__device__ __forceinline__ void tmem_wait_st() {
-  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
-template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
-    tc_decode_gemm(const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_hi,
-                   const __grid_constant__ CUtensorMap tmap_lo, const Args a) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  // ring stage s: [hi tile 2 KB][lo tile 2 KB][raw weights 4 KB]
-  uint8_t* scale_s = smem + DRS * D_STAGE;  // [128 rows][kScaleRow]
-  uint64_t* ring_full = reinterpret_cast<uint64_t*>(scale_s + BM * kScaleRow);
-  uint64_t* ring_empty = ring_full + DRS;
-  uint64_t* a_full = ring_empty + DRS;
-  uint64_t* a_empty = a_full + DAS;
-  uint64_t* acc_full = a_empty + DAS;
-  uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_items = a.meta[2] * a.m_tiles;
-  const int nk = a.K / BK;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < DRS; ++s) {
-      mbar_init(&ring_full[s], 1);     // producer's expect_tx arrival + bytes
-      mbar_init(&ring_empty[s], 129);  // 128 decode threads (raw read) + MMA commit (B read)
-    }
-    for (int s = 0; s < DAS; ++s) {
-      mbar_init(&a_full[s], 128);  // decode threads' TMEM stores
-      mbar_init(&a_empty[s], 1);   // MMA commit
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
-    }
-    *abort_flag = 0;
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(tmem_slot)),
-                 "r"(D_TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-
-  if (warp == 8) {
-    // ---------------- TMA producer ------------------------------------------
-    if (lane == 0) {
-      uint32_t g = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const Item it = decode_item(a, item);
-        const int wrow = it.le * a.rows + it.m_tile * BM;
-        for (int kc = 0; kc < nk; ++kc, ++g) {
-          const uint32_t rs = g % DRS, rph = (g / DRS) & 1u;
-          if (!mbar_wait(&ring_empty[rs], rph ^ 1u, abort_flag, a.err)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + rs * D_STAGE;
-          mbar_arrive_expect_tx(&ring_full[rs], RAW_BYTES + 2 * D_B_BYTES);
-          tma_load_2d(st + 2 * D_B_BYTES, &tmap_w, kc * 32, wrow, &ring_full[rs]);
-          tma_load_2d(st, &tmap_hi, kc * BK, it.row0, &ring_full[rs]);
-          tma_load_2d(st + D_B_BYTES, &tmap_lo, kc * BK, it.row0, &ring_full[rs]);
-        }
-      }
-      if (!ok) {
-        const uint64_t t0 = globaltimer();
-        while (globaltimer() - t0 < 2000000ull) {
-        }
-      }
-    }
-  } else if (warp == 9) {
-    // ---------------- MMA issuer ---------------------------------------------
-    if (lane == 0) {
-      uint32_t g = 0;
-      int acc_iter = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x, ++acc_iter) {
-        const int b = acc_iter & 1;
-        const uint32_t acc_phase = (acc_iter >> 1) & 1;
-        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1, abort_flag, a.err)) break;
-        tc_fence_after();
-        const uint32_t d_hi = tmem_base + (uint32_t)(D_ACC_COL + b * 2 * DBN);
-        const uint32_t d_lo = d_hi + (uint32_t)DBN;
-        for (int kc = 0; kc < nk; ++kc, ++g) {
-          const uint32_t rs = g % DRS, rph = (g / DRS) & 1u;
-          const uint32_t as = g % DAS, aph = (g / DAS) & 1u;
-          if (!mbar_wait(&a_full[as], aph, abort_flag, a.err) ||
-              !mbar_wait(&ring_full[rs], rph, abort_flag, a.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t sh = smem_u32(smem + rs * D_STAGE);
-          const uint32_t sl = sh + D_B_BYTES;
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint32_t at = tmem_base + as * 32 + kk * 8;
-            const uint32_t acc = (kc | kk) != 0;
-            mma_f16_ts(d_hi, at, sw128_desc(sh + kk * 32), acc);
-            mma_f16_ts(d_lo, at, sw128_desc(sl + kk * 32), acc);
-          }
-          mma_commit(&a_empty[as]);
-          mma_commit(&ring_empty[rs]);
-        }
-        if (ok) mma_commit(&acc_full[b]);
-      }
-      if (!ok || *abort_flag) {
-        const uint64_t t0 = globaltimer();
-        while (globaltimer() - t0 < 2000000ull) {
-        }
-      }
-    }
-  } else if (warp >= 4) {
-    // ---------------- weight decode into TMEM: thread r owns row r -----------
-    const int r = threadIdx.x - 128;
-    uint8_t* my_scales = scale_s + r * kScaleRow;
-    const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
-    uint32_t g = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-      const Item it = decode_item(a, item);
-      const int row = it.m_tile * BM + r;
-      const bool valid = row < a.rows;
-      const int64_t grow = (int64_t)it.le * a.rows + (valid ? row : 0);
-      const int rmax = valid ? (int)a.rowmax[grow] : 0;
-      {
-        const uint4* src = reinterpret_cast<const uint4*>(a.scales + grow * a.sp);
-        uint4* dst = reinterpret_cast<uint4*>(my_scales);
-        for (int i = 0; i < a.sp / 16; ++i) dst[i] = valid ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
-      }
-      for (int kc = 0; kc < nk; ++kc, ++g) {
-        const uint32_t rs = g % DRS, rph = (g / DRS) & 1u;
-        const uint32_t as = g % DAS, aph = (g / DAS) & 1u;
-        if (!mbar_wait(&ring_full[rs], rph, abort_flag, a.err)) {
-          ok = false;
-          break;
-        }
-        const uint4* rw =
-            reinterpret_cast<const uint4*>(smem + rs * D_STAGE + 2 * D_B_BYTES + r * 32);
-        const uint4 q0 = rw[0], q1 = rw[1];
-        mbar_arrive(&ring_empty[rs]);  // this thread is done with the raw bytes
-        const uint32_t s01 = *reinterpret_cast<const uint16_t*>(my_scales + 2 * kc);
-        uint32_t w[32];
-        {
-          uint32_t w0[16], w1[16];
-          const int s0 = (int)(s01 & 0xffu), s1 = (int)(s01 >> 8);
-          const uint32_t m0 =
-              (!valid || (a.split_zero && s0 == 0)) ? 0u : f16_pow2_bits(s0 - rmax + 13);
-          const uint32_t m1 =
-              (!valid || (a.split_zero && s1 == 0)) ? 0u : f16_pow2_bits(s1 - rmax + 13);
-          decode_block_f16(q0, m0, w0);
-          decode_block_f16(q1, m1, w1);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            w[i] = w0[i];
-            w[16 + i] = w1[i];
-          }
-        }
-        if (!mbar_wait(&a_empty[as], aph ^ 1u, abort_flag, a.err)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        tmem_st32(tmem_base + lane_off + as * 32, w);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&a_full[as]);
-      }
-    }
-  } else {
-    // ---------------- epilogue ------------------------------------------------
-    const int m = threadIdx.x;
-    int acc_iter = 0;
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++acc_iter) {
-      const int b = acc_iter & 1;
-      const uint32_t acc_phase = (acc_iter >> 1) & 1;
-      if (!mbar_wait(&acc_full[b], acc_phase, abort_flag, a.err)) break;
-      tc_fence_after();
-      const Item it = decode_item(a, item);
-      const uint32_t hi_addr = tmem_base + ((uint32_t)(warp * 32) << 16) +
-                               (uint32_t)(D_ACC_COL + b * 2 * DBN);
-      epilogue_tile<MODE, DBN>(a, it, hi_addr, hi_addr + (uint32_t)DBN, m);
-      tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 0) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(D_TMEM_COLS));
-  }
-}
-
 // x rows (gathered through perm) -> f16 hi / lo with a per-row power of two.
 // xscale stores the exponent s as a float: x = 2^s * (hi + lo).
 __global__ void split_gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm,
@@ -816,11 +563,7 @@ cudaError_t tc_make_maps(const Moe& m, ExpertBufs& eb) {
   if ((e = make(eb.map_xh, eb.xh, d.hidden, tc::BN)) != cudaSuccess) return e;
   if ((e = make(eb.map_xl, eb.xl, d.hidden, tc::BN)) != cudaSuccess) return e;
   if ((e = make(eb.map_hh, eb.hh, d.inter, tc::BN)) != cudaSuccess) return e;
-  if ((e = make(eb.map_hl, eb.hl, d.inter, tc::BN)) != cudaSuccess) return e;
-  if ((e = make(eb.map_xh16, eb.xh, d.hidden, tc::DBN)) != cudaSuccess) return e;
-  if ((e = make(eb.map_xl16, eb.xl, d.hidden, tc::DBN)) != cudaSuccess) return e;
-  if ((e = make(eb.map_hh16, eb.hh, d.inter, tc::DBN)) != cudaSuccess) return e;
-  return make(eb.map_hl16, eb.hl, d.inter, tc::DBN);
+  return make(eb.map_hl, eb.hl, d.inter, tc::BN);
 }
 
 namespace {
@@ -839,16 +582,17 @@ tc::Args common_args(const Moe& m, const Groups& g, ExpertBufs& eb) {
   return a;
 }
 
-template <int MODE, bool SMALL>
+template <int MODE>
 cudaError_t launch_gemm(const Moe& m, const tc::Args& a, const void* map_w, const void* map_hi,
                         const void* map_lo, cudaStream_t st) {
-  auto k = SMALL ? tc::tc_decode_gemm<MODE> : tc::tc_expert_gemm<MODE>;
-  const size_t smem = SMALL ? tc::kDecSmemBytes : tc::kSmemBytes;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto k = tc::tc_expert_gemm<MODE>;
+  cudaError_t e =
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
   if (e != cudaSuccess) return e;
-  k<<<m.sm_count, tc::kThreads, smem, st>>>(*reinterpret_cast<const CUtensorMap*>(map_w),
-                                            *reinterpret_cast<const CUtensorMap*>(map_hi),
-                                            *reinterpret_cast<const CUtensorMap*>(map_lo), a);
+  k<<<m.sm_count, tc::kThreads, tc::kSmemBytes, st>>>(*reinterpret_cast<const CUtensorMap*>(map_w),
+                                                      *reinterpret_cast<const CUtensorMap*>(map_hi),
+                                                      *reinterpret_cast<const CUtensorMap*>(map_lo),
+                                                      a);
   return cudaGetLastError();
 }
 
@@ -863,16 +607,14 @@ cudaError_t launch_tile_table(const Moe& m, const Groups& g, int bn, ExpertBufs&
 
 namespace {
 
-template <bool SMALL>
-cudaError_t gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
-                    cudaStream_t st) {
+}  // namespace
+
+cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                              cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
   const int positions = (int)g.rows;
   cudaError_t e;
-  tc::tile_table_kernel<<<1, 32, 0, st>>>(g.counts, g.offsets, m.e_begin, m.e_end,
-                                          SMALL ? tc::DBN : tc::BN, g.meta, eb.tile_expert,
-                                          eb.tile_row0, eb.tile_rows);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if ((e = launch_tile_table(m, g, tc::BN, eb, st)) != cudaSuccess) return e;
   if (positions > 0) {
     tc::split_gather_kernel<<<positions, 256, 0, st>>>(x, g.perm, g.perm_div, d.hidden, positions,
                                                        eb.xh, eb.xl, eb.xscale);
@@ -891,12 +633,10 @@ cudaError_t gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& e
   a.out_hi = eb.hh;
   a.out_lo = eb.hl;
   a.out_stride = d.inter;
-  return launch_gemm<tc::GATE_UP, SMALL>(m, a, m.w.map_gu, SMALL ? eb.map_xh16 : eb.map_xh,
-                                         SMALL ? eb.map_xl16 : eb.map_xl, st);
+  return launch_gemm<tc::GATE_UP>(m, a, m.w.map_gu, eb.map_xh, eb.map_xl, st);
 }
 
-template <bool SMALL>
-cudaError_t down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
+cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
   tc::Args a = common_args(m, g, eb);
   a.blocks = m.w.dn_blocks;
@@ -910,20 +650,7 @@ cudaError_t down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st)
   a.out_y = eb.y;
   a.out_rows = g.out_rows;
   a.out_stride = d.hidden;
-  return launch_gemm<tc::DOWN, SMALL>(m, a, m.w.map_dn, SMALL ? eb.map_hh16 : eb.map_hh,
-                                      SMALL ? eb.map_hl16 : eb.map_hl, st);
-}
-
-}  // namespace
-
-cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
-                              bool small_tiles, cudaStream_t st) {
-  return small_tiles ? gate_up<true>(m, g, x, eb, st) : gate_up<false>(m, g, x, eb, st);
-}
-
-cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, bool small_tiles,
-                           cudaStream_t st) {
-  return small_tiles ? down<true>(m, g, eb, st) : down<false>(m, g, eb, st);
+  return launch_gemm<tc::DOWN>(m, a, m.w.map_dn, eb.map_hh, eb.map_hl, st);
 }
 
 }  // namespace gb

@@ -114,11 +114,10 @@ class MoEBlock:
         check(self._lib.gb_moe_forward(self._h, x_ptr, T, out_ptr, stream))
 
     def set_expert_path(self, path: str) -> None:
-        """'auto', 'cuda_cores', 'tensor_cores', 'tensor_cores_small_tiles' or
-        'tensor_cores_f16' (gb_moe_set_expert_path)."""
+        """'auto', 'cuda_cores', 'tensor_cores' or 'tensor_cores_f16'
+        (gb_moe_set_expert_path)."""
         code = {"auto": _lib.GB_PATH_AUTO, "cuda_cores": _lib.GB_PATH_CUDA_CORES,
                 "tensor_cores": _lib.GB_PATH_TENSOR_CORES,
-                "tensor_cores_small_tiles": _lib.GB_PATH_TENSOR_CORES_SMALL_TILES,
                 "tensor_cores_f16": _lib.GB_PATH_TENSOR_CORES_F16}[path]
         check(self._lib.gb_moe_set_expert_path(self._h, code))
 

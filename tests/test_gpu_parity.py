@@ -256,10 +256,9 @@ def test_full_size_rows_do_not_depend_on_the_batch(moe32, big_run):
 
 # ---- tensor-core expert path (tcgen05) ---------------------------------------
 
-# "tensor_cores": block-scaled MMA, 128 weight rows x 128 positions;
-# "tensor_cores_small_tiles": block-scaled MMA, operands swapped, 16 positions;
+# "tensor_cores": block-scaled MMA, MXFP4 weights as stored, E4M3 pieces;
 # "tensor_cores_f16": weights decoded to f16 in shared memory, kind::f16.
-TC_PATHS = ["tensor_cores", "tensor_cores_small_tiles", "tensor_cores_f16"]
+TC_PATHS = ["tensor_cores", "tensor_cores_f16"]
 
 
 @pytest.mark.parametrize("path", TC_PATHS)
@@ -318,22 +317,22 @@ def test_tensor_core_path_handles_large_and_tiny_activations(moe32, layer32, pat
         assert err.sum() / np.abs(want[r]).sum() <= MEAN_REL, r
 
 
-@pytest.mark.parametrize("T", [2, 8, 16, 32, 100])
-def test_small_tiles_every_tile_width(moe32, layer32, T):
-    # 32 experts, top-4, mean T / 8 rows per expert: the decode tile holds
-    # 1, 2, 4, 8 or 16 positions (twice the mean, rounded up to a power of
-    # two, at most 8 while the mean is at most 8)
+@pytest.mark.parametrize("T", [2, 16, 32, 64, 100])
+def test_block_scaled_every_tile_width(moe32, layer32, T):
+    # 32 experts, top-4, mean T / 8 rows per expert: the tile holds 2, 4, 8,
+    # 16 or 32 positions (twice the mean, rounded up to a power of two, at
+    # most 16 while the mean is at most 8)
     x = synth.tokens(T, 2880, seed=900 + T)
     want, _, _ = oracle.OracleMoe(layer32).forward(x)
-    moe32.set_expert_path("tensor_cores_small_tiles")
+    moe32.set_expert_path("tensor_cores")
     try:
         got = moe32.forward(_cuda(x)).cpu().numpy()
     finally:
         moe32.set_expert_path("auto")
-    assert_parity(got, want, f"small tiles T={T}")
+    assert_parity(got, want, f"block-scaled T={T}")
 
 
-def test_small_tiles_on_odd_shapes():
+def test_tensor_cores_on_odd_shapes():
     # H, I multiples of 64 but not of 128: partial M tiles on both GEMMs
     layer = synth.gptoss_layer(n_experts=8, hidden=320, inter=192, seed=12)
     m = OssMoEFFN.load(layer, device=0, max_tokens=40)
