@@ -180,17 +180,19 @@ __device__ __forceinline__ void linger_2ms() {
   }
 }
 
-// Tile of 256 weight rows x NT positions (N = 4 NT piece rows).  CPS CTAs
-// share an SM (2 for N <= 64: each issues its own copies, which raises the
-// SM's copy rate; TMEM <= 256 columns and half the shared memory each).
+// Tile of 256 weight rows x NT positions (N = 4 NT piece rows).  Two CTAs
+// share an SM: each issues its own copies (one CTA's copies stall near
+// 40 GB/s), and one CTA's epilogue overlaps the other's MMAs; each has at most
+// 256 TMEM columns and half the shared memory.
 // TMEM: NACC tile buffers of (2 halves x ACCS accumulators x N columns), then
-// the constant piece scales (4 columns) and one slot of weight scales (8
-// columns, rewritten by tcgen05.cp before each stage's MMAs; the tcgen05
-// pipeline runs a thread's copies and MMAs in issue order).
+// the constant piece scales (4 columns) and one 8-column slot of weight
+// scales, rewritten by tcgen05.cp before each stage's MMAs (the tcgen05
+// pipeline runs a thread's copies and MMAs in issue order; a ring of slots
+// measured no faster and costs the widest tile 2 positions).
 template <int NT>
 struct Tile {
   static constexpr int N = kPieces * NT;
-  static constexpr int CPS = N <= 64 ? 2 : 1;
+  static constexpr int CPS = 2;
   static constexpr int W_BYTES = DM * BK;            // 32 KB in shared memory, 16 KB packed
   static constexpr int X_BYTES = N * BK;             // NT positions x 4 pieces x 128 bytes
   static constexpr int SFW = 2 * SF_BYTES;           // scale atoms of the two halves
@@ -620,7 +622,7 @@ int mx_tile_kind(const Moe& m, const Groups& g) {
   const int64_t nloc = std::max<int64_t>(1, m.e_end - m.e_begin);
   // positions per tile: the power of two at or above twice the mean rows per
   // local expert, at least 2; at most 16 (two CTAs per SM) while the mean is
-  // at most 8, else 30 (the widest tile whose accumulators fit TMEM twice)
+  // at most 8, else 30 (the widest tile whose accumulators fit half the TMEM)
   if (g.rows > 8 * nloc) return kMxTileKinds - 1;
   const int64_t target = (2 * g.rows + nloc - 1) / nloc;
   int i = 0;

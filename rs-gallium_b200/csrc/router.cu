@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "moe_internal.h"
+#include "ptx.cuh"
 
 namespace gb {
 namespace {
@@ -24,82 +25,17 @@ namespace {
 constexpr int kRouterWarps = 8;
 constexpr int kPreloadBlocks = 96;  // H <= 3072 for the preloading variant
 
-template <int TT, int EPW>
-__global__ void __launch_bounds__(kRouterWarps * 32)
-    router_kernel(const float* __restrict__ x, int T, int H, const float* __restrict__ rw,
-                  const float* __restrict__ rb, int E, int K, int kind,
-                  const float* __restrict__ sel_bias, float* __restrict__ logits,
-                  unsigned* __restrict__ tickets, int32_t* __restrict__ idx_out,
-                  float* __restrict__ w_out) {
-  extern __shared__ float xs[];  // [TT][H]
+// After this CTA stored its logits of token tile blockIdx.x: the last CTA of
+// the tile to finish (threadfence + per-tile ticket, no waiting) runs the
+// top-k and combine weights of the tile's nt tokens, one warp per token.
+__device__ __forceinline__ void route_tail(int t0, int nt, const float* __restrict__ logits,
+                                           unsigned* __restrict__ tickets, int E, int K,
+                                           int kind, const float* __restrict__ sel_bias,
+                                           int32_t* __restrict__ idx_out,
+                                           float* __restrict__ w_out) {
   __shared__ unsigned s_ticket;
-  const int t0 = blockIdx.x * TT;
-  const int nt = min(TT, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  {
-    const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t0 * H);
-    float4* dst = reinterpret_cast<float4*>(xs);
-    const int n4 = nt * H / 4;
-    for (int i = threadIdx.x; i < TT * H / 4; i += blockDim.x)
-      dst[i] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  __syncthreads();
-
-  const int e0 = (blockIdx.y * kRouterWarps + warp) * EPW;
-  if (e0 < E) {
-    float acc[EPW][TT];
-#pragma unroll
-    for (int q = 0; q < EPW; ++q)
-#pragma unroll
-      for (int t = 0; t < TT; ++t) acc[q][t] = 0.0f;
-    const float* wrow[EPW];
-#pragma unroll
-    for (int q = 0; q < EPW; ++q) wrow[q] = rw + (int64_t)min(e0 + q, E - 1) * H;
-    const int nb = H >> 5;
-    if (EPW == 1 && TT <= 4 && nb <= kPreloadBlocks) {
-      // Decode-sized batches: few warps read the router weight, so issue all
-      // of this lane's loads before the FMA chain (one memory round trip).
-      float wv[kPreloadBlocks];
-#pragma unroll
-      for (int j = 0; j < kPreloadBlocks; ++j)
-        if (j < nb) wv[j] = __ldg(wrow[0] + lane + (j << 5));
-#pragma unroll
-      for (int j = 0; j < kPreloadBlocks; ++j) {
-        if (j < nb) {
-#pragma unroll
-          for (int t = 0; t < TT; ++t)
-            acc[0][t] = __fmaf_rn(xs[t * H + lane + (j << 5)], wv[j], acc[0][t]);
-        }
-      }
-    } else {
-#pragma unroll 6
-      for (int j = 0; j < nb; ++j) {
-        const int kk = lane + (j << 5);
-        float wv[EPW];
-#pragma unroll
-        for (int q = 0; q < EPW; ++q) wv[q] = __ldg(wrow[q] + kk);
-#pragma unroll
-        for (int t = 0; t < TT; ++t) {
-          const float xv = xs[t * H + kk];
-#pragma unroll
-          for (int q = 0; q < EPW; ++q) acc[q][t] = __fmaf_rn(xv, wv[q], acc[q][t]);
-        }
-      }
-    }
-#pragma unroll
-    for (int q = 0; q < EPW; ++q) {
-#pragma unroll
-      for (int t = 0; t < TT; ++t) {
-        const float v = warp_sum_butterfly(acc[q][t]);
-        const int e = e0 + q;
-        if (lane == 0 && e < E && t < nt)
-          logits[(int64_t)(t0 + t) * E + e] = rb ? __fadd_rn(v, rb[e]) : v;
-      }
-    }
-  }
-
-  // Last CTA of this token tile runs the top-k.
+  const int nwarps = blockDim.x >> 5;
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_ticket = atomicAdd(&tickets[blockIdx.x], 1u);
@@ -108,7 +44,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
   __threadfence();
   if (threadIdx.x == 0) tickets[blockIdx.x] = 0;  // ready for the next forward
 
-  for (int t = warp; t < nt; t += kRouterWarps) {
+  for (int t = warp; t < nt; t += nwarps) {
     const float* lg = logits + (int64_t)(t0 + t) * E;
     constexpr int kMaxPerLane = 8;  // E <= 256
     float key[kMaxPerLane];
@@ -200,6 +136,208 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
 }
 
 template <int TT, int EPW>
+__global__ void __launch_bounds__(kRouterWarps * 32)
+    router_kernel(const float* __restrict__ x, int T, int H, const float* __restrict__ rw,
+                  const float* __restrict__ rb, int E, int K, int kind,
+                  const float* __restrict__ sel_bias, float* __restrict__ logits,
+                  unsigned* __restrict__ tickets, int32_t* __restrict__ idx_out,
+                  float* __restrict__ w_out) {
+  extern __shared__ float xs[];  // [TT][H]
+  const int t0 = blockIdx.x * TT;
+  const int nt = min(TT, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  {
+    const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t0 * H);
+    float4* dst = reinterpret_cast<float4*>(xs);
+    const int n4 = nt * H / 4;
+    for (int i = threadIdx.x; i < TT * H / 4; i += blockDim.x)
+      dst[i] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+
+  const int e0 = (blockIdx.y * kRouterWarps + warp) * EPW;
+  if (e0 < E) {
+    float acc[EPW][TT];
+#pragma unroll
+    for (int q = 0; q < EPW; ++q)
+#pragma unroll
+      for (int t = 0; t < TT; ++t) acc[q][t] = 0.0f;
+    const float* wrow[EPW];
+#pragma unroll
+    for (int q = 0; q < EPW; ++q) wrow[q] = rw + (int64_t)min(e0 + q, E - 1) * H;
+    const int nb = H >> 5;
+    if (EPW == 1 && TT <= 4 && nb <= kPreloadBlocks) {
+      // Decode-sized batches: few warps read the router weight, so issue all
+      // of this lane's loads before the FMA chain (one memory round trip).
+      float wv[kPreloadBlocks];
+#pragma unroll
+      for (int j = 0; j < kPreloadBlocks; ++j)
+        if (j < nb) wv[j] = __ldg(wrow[0] + lane + (j << 5));
+#pragma unroll
+      for (int j = 0; j < kPreloadBlocks; ++j) {
+        if (j < nb) {
+#pragma unroll
+          for (int t = 0; t < TT; ++t)
+            acc[0][t] = __fmaf_rn(xs[t * H + lane + (j << 5)], wv[j], acc[0][t]);
+        }
+      }
+    } else {
+#pragma unroll 6
+      for (int j = 0; j < nb; ++j) {
+        const int kk = lane + (j << 5);
+        float wv[EPW];
+#pragma unroll
+        for (int q = 0; q < EPW; ++q) wv[q] = __ldg(wrow[q] + kk);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const float xv = xs[t * H + kk];
+#pragma unroll
+          for (int q = 0; q < EPW; ++q) acc[q][t] = __fmaf_rn(xv, wv[q], acc[q][t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < EPW; ++q) {
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        const float v = warp_sum_butterfly(acc[q][t]);
+        const int e = e0 + q;
+        if (lane == 0 && e < E && t < nt)
+          logits[(int64_t)(t0 + t) * E + e] = rb ? __fadd_rn(v, rb[e]) : v;
+      }
+    }
+  }
+
+  route_tail(t0, nt, logits, tickets, E, K, kind, sel_bias, idx_out, w_out);
+}
+
+// Prefill-sized batches: a CTA computes the logits of 32 tokens x 16 experts,
+// each warp 8 tokens x 8 experts (64 partial sums per lane), with x and W
+// staged through shared memory 256 k at a time (cp.async, two buffers).  Lane l still accumulates
+// k = l, l + 32, ... in increasing k with FMAs, and the 64 sums are reduced
+// over the lanes in the butterfly's pairing (xor 16, 8, 4, 2, 1; IEEE
+// addition commutes, so every lane of the butterfly holds the same value),
+// as a reduce-scatter that leaves lane l the sums of (token l / 4, experts
+// 2 (l % 4) and 2 (l % 4) + 1).  Logits are bit-identical to router_kernel.
+constexpr int kTileTokens = 32, kTileExperts = 16, kTileK = 256;
+
+__global__ void __launch_bounds__(256, 2)
+    router_tiled_kernel(const float* __restrict__ x, int T, int H, const float* __restrict__ rw,
+                        const float* __restrict__ rb, int E, int K, int kind,
+                        const float* __restrict__ sel_bias, float* __restrict__ logits,
+                        unsigned* __restrict__ tickets, int32_t* __restrict__ idx_out,
+                        float* __restrict__ w_out) {
+  extern __shared__ __align__(16) float sm[];  // two buffers of [32 tokens + 16 experts][256]
+  constexpr int kBuf = (kTileTokens + kTileExperts) * kTileK;
+  const int t0 = blockIdx.x * kTileTokens, e0 = blockIdx.y * kTileExperts;
+  const int nt = min(kTileTokens, T - t0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tw = (warp & 3) * 8, ew = (warp >> 2) * 8;
+  const int nchunks = (H + kTileK - 1) / kTileK;
+  float acc[8][8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[t][e] = 0.0f;
+
+  // chunk c of x (rows past T zero-filled) and W into buffer c % 2
+  auto stage = [&](int c) {
+    float* xs = sm + (c & 1) * kBuf;
+    float* ws = xs + kTileTokens * kTileK;
+    const int k0 = c * kTileK, q4 = min(kTileK, H - k0) / 4;
+    for (int i = threadIdx.x; i < (kTileTokens + kTileExperts) * q4; i += blockDim.x) {
+      const int r = i / q4, col = 4 * (i - r * q4);
+      const float* src;
+      float* dst;
+      int bytes = 16;
+      if (r < kTileTokens) {
+        const int tr = r < nt ? r : 0;
+        src = x + (int64_t)(t0 + tr) * H + k0 + col;
+        dst = xs + r * kTileK + col;
+        if (r >= nt) bytes = 0;
+      } else {
+        src = rw + (int64_t)min(e0 + r - kTileTokens, E - 1) * H + k0 + col;
+        dst = ws + (r - kTileTokens) * kTileK + col;
+      }
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+                   "r"(bytes)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  stage(0);
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) {
+      stage(c + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // chunk c has landed for every thread
+    const float* xs = sm + (c & 1) * kBuf;
+    const float* ws = xs + kTileTokens * kTileK;
+    const int kl = min(kTileK, H - c * kTileK);  // a multiple of 32
+#pragma unroll 2
+    for (int jj = 0; jj < kl / 32; ++jj) {
+      const int kk = jj * 32 + lane;
+      float xv[8], wv[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) xv[t] = xs[(tw + t) * kTileK + kk];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) wv[e] = ws[(ew + e) * kTileK + kk];
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[t][e] = __fmaf_rn(xv[t], wv[e], acc[t][e]);
+    }
+    __syncthreads();  // buffer c % 2 may be refilled by the next iteration
+  }
+
+  // reduce-scatter of the 64 sums (index 8 t + e) over the 32 lanes
+  float r32[32], r16[16], r8[8], r4[4];
+#pragma unroll
+  for (int q = 0; q < 32; ++q) {
+    const bool up = lane & 16;
+    const float lo = acc[q >> 3][q & 7], hi = acc[(q + 32) >> 3][(q + 32) & 7];
+    r32[q] = __fadd_rn(up ? hi : lo, __shfl_xor_sync(kFullMask, up ? lo : hi, 16));
+  }
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const bool up = lane & 8;
+    r16[q] = __fadd_rn(up ? r32[q + 16] : r32[q],
+                       __shfl_xor_sync(kFullMask, up ? r32[q] : r32[q + 16], 8));
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const bool up = lane & 4;
+    r8[q] = __fadd_rn(up ? r16[q + 8] : r16[q],
+                      __shfl_xor_sync(kFullMask, up ? r16[q] : r16[q + 8], 4));
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const bool up = lane & 2;
+    r4[q] = __fadd_rn(up ? r8[q + 4] : r8[q], __shfl_xor_sync(kFullMask, up ? r8[q] : r8[q + 4], 2));
+  }
+  float res[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const bool up = lane & 1;
+    res[q] = __fadd_rn(up ? r4[q + 2] : r4[q], __shfl_xor_sync(kFullMask, up ? r4[q] : r4[q + 2], 1));
+  }
+  const int t = tw + (lane >> 2);
+  if (t < nt) {
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const int e = e0 + ew + 2 * (lane & 3) + q;
+      if (e < E) logits[(int64_t)(t0 + t) * E + e] = rb ? __fadd_rn(res[q], rb[e]) : res[q];
+    }
+  }
+  route_tail(t0, nt, logits, tickets, E, K, kind, sel_bias, idx_out, w_out);
+}
+
+template <int TT, int EPW>
 cudaError_t launch(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
                    cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
@@ -222,7 +360,17 @@ cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t*
   if (T <= 0) return cudaSuccess;
   if (T <= 4) return launch<1, 1>(m, x, T, idx, wts, st);
   if (T <= 64) return launch<4, 1>(m, x, T, idx, wts, st);
-  return launch<8, 4>(m, x, T, idx, wts, st);
+  const gb_moe_desc& d = m.desc;
+  dim3 grid((unsigned)((T + kTileTokens - 1) / kTileTokens),
+            (unsigned)((d.n_experts + kTileExperts - 1) / kTileExperts));
+  const size_t smem = 2 * (size_t)(kTileTokens + kTileExperts) * kTileK * sizeof(float);
+  cudaError_t err = cudaFuncSetAttribute(router_tiled_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return err;
+  router_tiled_kernel<<<grid, 256, smem, st>>>(x, (int)T, d.hidden, m.router_w, m.router_b,
+                                               d.n_experts, d.top_k, d.router_kind, m.sel_bias,
+                                               m.ws.logits, m.ws.tickets, idx, wts);
+  return cudaGetLastError();
 }
 
 }  // namespace gb
