@@ -232,6 +232,10 @@ void release_moe(gb::Moe& m) {
   DeviceScope ds(m.device);
   for (auto& e : m.ev)
     if (e) cudaEventDestroy(e);
+  for (auto& e : m.host_ev)
+    if (e) cudaEventDestroy(e);
+  if (m.h2d) cudaStreamDestroy(m.h2d);
+  if (m.d2h) cudaStreamDestroy(m.d2h);
   cudaFree(m.router_w);
   cudaFree(m.router_b);
   cudaFree(m.sel_bias);
@@ -691,6 +695,62 @@ int gb_moe_forward(gb_moe* h, const float* x_dev, int64_t T, float* out_dev, voi
   return run_forward(m, x_dev, T, out_dev, st);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Host buffers of at least 2 kHostChunkMin tokens go through in up to four
+// chunks: chunk i's copy in (h2d stream) overlaps the forward of chunk i - 1
+// and its copy out (d2h stream) the forward of chunk i + 1.  The forward of a
+// chunk is the forward of those tokens (routing and experts are per token),
+// so the result equals the one-chunk forward.  Expert-parallel forwards stay
+// one chunk: every rank must make the same collective calls.
+constexpr int64_t kHostChunkMin = 1024;
+constexpr int kHostChunks = 4;
+
+int forward_host_pipelined(gb::Moe& m, const float* x_host, int64_t T, float* out_host,
+                           cudaStream_t st) {
+  const int64_t H = m.desc.hidden;
+  const int64_t chunk = std::max<int64_t>(kHostChunkMin, (T + kHostChunks - 1) / kHostChunks);
+  const int n = (int)((T + chunk - 1) / chunk);
+  if (!m.h2d) GB_CUDA(cudaStreamCreateWithFlags(&m.h2d, cudaStreamNonBlocking), "copy stream");
+  if (!m.d2h) GB_CUDA(cudaStreamCreateWithFlags(&m.d2h, cudaStreamNonBlocking), "copy stream");
+  for (auto& e : m.host_ev)
+    if (!e) GB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
+  cudaEvent_t start = m.host_ev[0], done = m.host_ev[1];
+  cudaEvent_t* in = m.host_ev + 2;   // [kHostChunks]
+  cudaEvent_t* fwd = m.host_ev + 6;  // [kHostChunks]
+  // the staging buffers may still be in use by work queued earlier on st
+  GB_CUDA(cudaEventRecord(start, st), "record chunk event");
+  GB_CUDA(cudaStreamWaitEvent(m.h2d, start, 0), "order copy stream");
+  GB_CUDA(cudaStreamWaitEvent(m.d2h, start, 0), "order copy stream");
+  for (int i = 0; i < n; ++i) {
+    const int64_t t0 = i * chunk, tn = std::min(chunk, T - t0);
+    GB_CUDA(cudaMemcpyAsync(m.ws.x_stage + t0 * H, x_host + t0 * H, sizeof(float) * tn * H,
+                            cudaMemcpyHostToDevice, m.h2d),
+            "copy x in");
+    GB_CUDA(cudaEventRecord(in[i], m.h2d), "record chunk event");
+  }
+  int rc;
+  for (int i = 0; i < n; ++i) {
+    const int64_t t0 = i * chunk, tn = std::min(chunk, T - t0);
+    GB_CUDA(cudaStreamWaitEvent(st, in[i], 0), "wait for chunk in");
+    if ((rc = run_forward(m, m.ws.x_stage + t0 * H, tn, m.ws.out_stage + t0 * H, st))) return rc;
+    GB_CUDA(cudaEventRecord(fwd[i], st), "record chunk event");
+    GB_CUDA(cudaStreamWaitEvent(m.d2h, fwd[i], 0), "wait for chunk forward");
+    GB_CUDA(cudaMemcpyAsync(out_host + t0 * H, m.ws.out_stage + t0 * H, sizeof(float) * tn * H,
+                            cudaMemcpyDeviceToHost, m.d2h),
+            "copy out");
+  }
+  GB_CUDA(cudaEventRecord(done, m.d2h), "record chunk event");
+  GB_CUDA(cudaStreamWaitEvent(st, done, 0), "wait for copies out");
+  return GB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_host,
                         void* stream) {
   int rc = check_handle(h);
@@ -702,13 +762,18 @@ int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_ho
   DeviceScope ds(m.device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = ensure_ws(m, T, st))) return rc;
-  const size_t bytes = sizeof(float) * (size_t)(T * m.desc.hidden);
-  if (bytes)
-    GB_CUDA(cudaMemcpyAsync(m.ws.x_stage, x_host, bytes, cudaMemcpyHostToDevice, st), "copy x in");
-  if ((rc = run_forward(m, m.ws.x_stage, T, m.ws.out_stage, st))) return rc;
-  if (bytes)
-    GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
-            "copy out");
+  if (m.ep_size == 1 && T >= 2 * kHostChunkMin) {
+    if ((rc = forward_host_pipelined(m, x_host, T, out_host, st))) return rc;
+  } else {
+    const size_t bytes = sizeof(float) * (size_t)(T * m.desc.hidden);
+    if (bytes)
+      GB_CUDA(cudaMemcpyAsync(m.ws.x_stage, x_host, bytes, cudaMemcpyHostToDevice, st),
+              "copy x in");
+    if ((rc = run_forward(m, m.ws.x_stage, T, m.ws.out_stage, st))) return rc;
+    if (bytes)
+      GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
+              "copy out");
+  }
   GB_CUDA(cudaStreamSynchronize(st), "synchronise forward");
   return read_device_status(m, st);
 }

@@ -149,6 +149,9 @@ struct Moe {
   cudaEvent_t ev[kStages + 1] = {};
   int64_t launches = 0;
   int expert_path = 0;  // gb_expert_path
+  // gb_moe_forward_host pipelining: copy streams and chunk events (lazily made)
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t host_ev[10] = {};
 };
 
 // Records an error message for gb_last_error() and returns `code`.
