@@ -282,6 +282,21 @@ def stage_profile(moe, xd, out, T, flush, reps=3):
     return {k: statistics.median(v) for k, v in acc.items()}
 
 
+def measured_traffic(T, E, stage):
+    """DRAM bytes per launch of `stage`'s GEMM from the committed ncu capture
+    (profiles/roofline_traffic.json), or None when none matches."""
+    path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    try:
+        with open(path) as f:
+            entries = json.load(f)["entries"]
+    except (OSError, ValueError, KeyError):
+        return None
+    for e in entries:
+        if e["tokens"] == T and e["experts"] == E and e["stage"] == stage:
+            return e["dram_read_bytes"] + e["dram_write_bytes"]
+    return None
+
+
 def roofline_for(stage_ms, T, n_touched, layer, peaks):
     """Roofline of the dominant expert kernel (gate_up or down)."""
     E = layer.n_experts
@@ -301,12 +316,12 @@ def roofline_for(stage_ms, T, n_touched, layer, peaks):
         return {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
                 "peak_source": peaks["source"], "algorithmic_bytes": stage_bytes[dom],
-                "launch_ms": stage_ms[dom], "traffic": None}
+                "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom)}
     ach = stage_flops[dom] / t / 1e12
     return {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"],
             "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"],
             "peak_source": peaks["source"], "algorithmic_flops": stage_flops[dom],
-            "launch_ms": stage_ms[dom], "traffic": None}
+            "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom)}
 
 
 def run_ours(args, world, rank, local):
