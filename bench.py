@@ -97,7 +97,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", self.gpu_id, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -108,6 +108,13 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def wait_first(self, timeout_s: float = 5.0):
+        """Blocks until nvidia-smi printed its first sample (it takes a while
+        to start, longer with one sampler per rank), at most timeout_s."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout_s:
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -282,7 +289,7 @@ def stage_profile(moe, xd, out, T, flush, reps=3):
     return {k: statistics.median(v) for k, v in acc.items()}
 
 
-def measured_traffic(T, E, stage):
+def measured_traffic(T, E, stage, n_gpus):
     """DRAM bytes per launch of `stage`'s GEMM from the committed ncu capture
     (profiles/roofline_traffic.json), or None when none matches."""
     path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
@@ -292,12 +299,13 @@ def measured_traffic(T, E, stage):
     except (OSError, ValueError, KeyError):
         return None
     for e in entries:
-        if e["tokens"] == T and e["experts"] == E and e["stage"] == stage:
+        if (e["tokens"] == T and e["experts"] == E and e["stage"] == stage
+                and e.get("n_gpus", 1) == n_gpus):
             return e["dram_read_bytes"] + e["dram_write_bytes"]
     return None
 
 
-def roofline_for(stage_ms, T, n_touched, layer, peaks):
+def roofline_for(stage_ms, T, n_touched, layer, peaks, n_gpus=1):
     """Roofline of the dominant expert kernel (gate_up or down)."""
     E = layer.n_experts
     k = layer.top_k
@@ -316,12 +324,12 @@ def roofline_for(stage_ms, T, n_touched, layer, peaks):
         return {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
                 "peak_source": peaks["source"], "algorithmic_bytes": stage_bytes[dom],
-                "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom)}
+                "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom, n_gpus)}
     ach = stage_flops[dom] / t / 1e12
     return {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"],
             "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"],
             "peak_source": peaks["source"], "algorithmic_flops": stage_flops[dom],
-            "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom)}
+            "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom, n_gpus)}
 
 
 def run_ours(args, world, rank, local):
@@ -382,10 +390,11 @@ def run_ours(args, world, rank, local):
 
     # ---- timed region: exactly K steps --------------------------------------
     clocks = ClockSampler(gpu_uuid(local))
+    clocks.start()
+    clocks.wait_first()
     launches0 = moe.info()["kernel_launches"]
     barrier(world)
     torch.cuda.synchronize()
-    clocks.start()
     total_ms = timed(args.steps, T, fwd_dev)
     torch.cuda.synchronize()
     barrier(world)
@@ -411,7 +420,7 @@ def run_ours(args, world, rank, local):
 
     # ---- roofline of the dominant kernel ------------------------------------
     stages = stage_profile(moe, xd, out, T, flush)
-    roof = roofline_for(stages, T, n_touched, layer, peaks)
+    roof = roofline_for(stages, T, n_touched, layer, peaks, world)
 
     # ---- other batch sizes of the workload -----------------------------------
     sweep_out = []
@@ -431,7 +440,8 @@ def run_ours(args, world, rank, local):
         st = stage_profile(moe, xd, out, Ts, flush)
         sweep_out.append({"tokens": Ts, "value": world * Ts / (ms / 1e3), "ms_per_step": ms,
                           "stages_ms": st,
-                          "roofline": roofline_for(st, Ts, int((c > 0).sum()), layer, peaks)})
+                          "roofline": roofline_for(st, Ts, int((c > 0).sum()), layer, peaks,
+                                                   world)})
 
     # ---- CPU baseline (rank 0, one GPU only) ---------------------------------
     cpu = None
