@@ -591,6 +591,8 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
       {(void**)&nb.hl, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
       {(void**)&nb.xq, m.mx.ok ? mx_piece_bytes(rows, (int)H) : 0},
       {(void**)&nb.hq, m.mx.ok ? mx_piece_bytes(rows, (int)I) : 0},
+      {(void**)&nb.mx_partial, m.mx.ok ? kMxPartialBytes : 0},
+      {(void**)&nb.mx_arrivals, m.mx.ok ? sizeof(int) * (size_t)kMxSplitSlots : 0},
       {(void**)&nb.tile_expert, sizeof(int32_t) * (size_t)(rows + E + 1)},
       {(void**)&nb.tile_row0, sizeof(int32_t) * (size_t)(rows + E + 1)},
       {(void**)&nb.tile_rows, sizeof(int32_t) * (size_t)(rows + E + 1)},
@@ -606,7 +608,8 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
     nb.maps_ok = true;
   }
   if (m.mx.ok) {
-    cudaError_t e = mx_make_maps(m, nb);
+    cudaError_t e = cudaMemset(nb.mx_arrivals, 0, sizeof(int) * (size_t)kMxSplitSlots);
+    if (e == cudaSuccess) e = mx_make_maps(m, nb);
     if (e != cudaSuccess) {
       cudaFree(nb.base);
       return cuda_err(e, "TMA descriptors for the block-scaled path");

@@ -101,6 +101,8 @@ struct ExpertBufs {
   uint8_t* hq = nullptr;       // [rows][4][I] E4M3 pieces of the SwiGLU output
   alignas(64) unsigned char map_xq[5][128] = {};  // CUtensorMaps, tiles of 2, 4, 8, 16, 30
   alignas(64) unsigned char map_hq[5][128] = {};  // positions (index: kind)
+  float* mx_partial = nullptr;  // split-K partial sums (kMxPartialBytes)
+  int* mx_arrivals = nullptr;   // split-K tickets [kMxSplitSlots], zero between forwards
   bool maps_ok = false;
   bool mx_maps_ok = false;
 };
@@ -185,6 +187,8 @@ cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float*
 
 // Block-scaled tensor-core expert path (mx_gemm.cu).
 constexpr int kMxTileKinds = 5;  // tiles of 2, 4, 8, 16, 30 positions
+constexpr size_t kMxPartialBytes = size_t(8) << 20;  // split-K partial sums
+constexpr int kMxSplitSlots = 4096;                  // split-K tiles x splits
 bool mx_supported(const Moe& m);
 cudaError_t mx_prepare_weights(Moe& m);
 void mx_release(MxWeights& x);

@@ -158,20 +158,66 @@ struct Args {
   float* out_y;               // DOWN: y [rows][H], row = out_rows[position] (or position)
   const int32_t* out_rows;
   int* err;                   // error bits (2: a wait timed out)
+  // split K: each (N tile, M tile) runs as ksplit items over consecutive
+  // ranges of K chunks; partial sums meet in `partial`, the last to arrive
+  // (ticket in `arrivals`, reset by it) adds them in split order
+  int ksplit;
+  float* partial;             // [tile * m_tiles + m_tile][ksplit][256 rows][NT]
+  int* arrivals;              // [tile * m_tiles + m_tile]
 };
 
 struct Item {
   int le, m_tile, row0, nrows;
+  int slot;         // tile * m_tiles + m_tile
+  int split;        // which K range
+  int kc0, kc1;     // K chunks [kc0, kc1)
 };
 
 __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   Item it;
-  const int j = item / a.m_tiles;
-  it.m_tile = item - j * a.m_tiles;
+  it.split = item % a.ksplit;
+  it.slot = item / a.ksplit;
+  const int j = it.slot / a.m_tiles;
+  it.m_tile = it.slot - j * a.m_tiles;
   it.le = a.tile_expert[j] - a.e_begin;
   it.row0 = a.tile_row0[j];
   it.nrows = a.tile_rows[j];
+  it.kc0 = it.split * a.kchunks / a.ksplit;
+  it.kc1 = (it.split + 1) * a.kchunks / a.ksplit;
   return it;
+}
+
+// Bias + clamped SwiGLU + pieces of h (GATE_UP) or bias + y (DOWN) for
+// positions n and n + 1 of the tile, val[u] being the sum of weight row
+// `row` for position n + u.  Every lane of the warp calls it (the gate/up
+// pair of rows 2i, 2i+1 is exchanged between neighbouring lanes: the even
+// lane finishes position n, the odd lane position n + 1).
+template <int MODE>
+__device__ __forceinline__ void finish_pair(const Args& a, const Item& it, int row, bool valid,
+                                            float bias, int n, float (&val)[2],
+                                            float lane_scale, int64_t lane_orow, int m) {
+  if (MODE == 0) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u)
+      val[u] = __fadd_rn(__fmul_rn(val[u], __shfl_sync(kFullMask, lane_scale, n + u)), bias);
+    const bool odd = m & 1;
+    const float other = __shfl_xor_sync(kFullMask, odd ? val[0] : val[1], 1);
+    const float gate = odd ? other : val[0];
+    const float up = odd ? val[1] : other;
+    const int np = n + (odd ? 1 : 0);
+    if (valid && np < it.nrows)
+      store_pieces(__fmul_rn(act_gptoss(gate, up, a.limit), pow2f(-a.h_exp)),
+                   a.out_q + ((int64_t)it.row0 + np) * (kPieces * a.out_stride) + (row >> 1),
+                   a.out_stride);
+  } else {
+    const float f = pow2f(a.in_exp);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int64_t orow = __shfl_sync(kFullMask, lane_orow, n + u);
+      if (valid && n + u < it.nrows)
+        a.out_y[orow * a.out_stride + row] = __fadd_rn(__fmul_rn(val[u], f), bias);
+    }
+  }
 }
 
 __device__ __forceinline__ void linger_2ms() {
@@ -236,8 +282,9 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_items = a.meta[2] * a.m_tiles;
+  const int total_items = a.meta[2] * a.m_tiles * a.ksplit;
   const int nk = a.kchunks;
+  __shared__ int s_last;
 
   for (int i = threadIdx.x; i < SF_BYTES / 4; i += kThreads)
     reinterpret_cast<uint32_t*>(sfb_const)[i] = piece_scale_word(i);
@@ -268,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       bool ok = true;
       for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
         const Item it = decode_item(a, item);
-        for (int kc = 0; kc < nk; ++kc, ++g) {
+        for (int kc = it.kc0; kc < it.kc1; ++kc, ++g) {
           if ((g & 1u) != mine) continue;
           const uint32_t s = g % D::STAGES, ph = (g / D::STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) {
@@ -301,7 +348,8 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
         if (!mbar_wait(&acc_empty[b], acc_phase ^ 1u, abort_flag, a.err)) break;
         tc_fence_after();
         const uint32_t dbase = tmem_base + (uint32_t)(b * D::BUF);
-        for (int kc = 0; kc < nk; ++kc, ++g) {
+        const Item it = decode_item(a, item);
+        for (int kc = it.kc0; kc < it.kc1; ++kc, ++g) {
           const uint32_t s = g % D::STAGES, ph = (g / D::STAGES) & 1u;
           if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
             ok = false;
@@ -318,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
           for (int j = 0; j < BK / 32; ++j) {
             const uint64_t bdesc = sw128_desc(sx + 32 * j);
             const uint32_t acc = (uint32_t)(j % D::ACCS);
-            const uint32_t on = (kc != 0 || j >= D::ACCS) ? 1u : 0u;
+            const uint32_t on = (kc != it.kc0 || j >= D::ACCS) ? 1u : 0u;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               mma_mx(dbase + (uint32_t)((h * D::ACCS + acc) * D::N),
@@ -341,6 +389,8 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       if (!mbar_wait(&acc_full[b], acc_phase, abort_flag, a.err)) break;
       tc_fence_after();
       const Item it = decode_item(a, item);
+      const bool split = a.ksplit > 1;
+      float* part = a.partial + ((int64_t)it.slot * a.ksplit + it.split) * (DM * NT);
       // lane n holds position n's activation scale (GATE_UP) or output row (DOWN)
       float lane_scale = 0.0f;
       int64_t lane_orow = 0;
@@ -387,37 +437,47 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
               }
               val[u] = sum;
             }
-            if (MODE == 0) {
-              // rows 2i (gate, even lane) and 2i+1 (up, odd lane): the even lane
-              // finishes position n, the odd lane position n + 1
-#pragma unroll
-              for (int u = 0; u < 2; ++u)
-                val[u] = __fadd_rn(__fmul_rn(val[u], __shfl_sync(kFullMask, lane_scale, n + u)),
-                                   bias);
-              const bool odd = m & 1;
-              const float other = __shfl_xor_sync(kFullMask, odd ? val[0] : val[1], 1);
-              const float gate = odd ? other : val[0];
-              const float up = odd ? val[1] : other;
-              const int np = n + (odd ? 1 : 0);
-              if (valid && np < it.nrows)
-                store_pieces(__fmul_rn(act_gptoss(gate, up, a.limit), pow2f(-a.h_exp)),
-                             a.out_q + ((int64_t)it.row0 + np) * (kPieces * a.out_stride) +
-                                 (row >> 1),
-                             a.out_stride);
+            if (split) {
+              *reinterpret_cast<float2*>(part + (h * BM + m) * NT + n) = make_float2(val[0], val[1]);
             } else {
-              const float f = pow2f(a.in_exp);
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int64_t orow = __shfl_sync(kFullMask, lane_orow, n + u);
-                if (valid && n + u < it.nrows)
-                  a.out_y[orow * a.out_stride + row] = __fadd_rn(__fmul_rn(val[u], f), bias);
-              }
+              finish_pair<MODE>(a, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
             }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
+      if (split) {
+        // the last of the tile's ksplit items adds the partial sums in split
+        // order and finishes the tile (no waiting: a ticket per tile)
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (m == 0) s_last = atomicAdd(&a.arrivals[it.slot], 1) == a.ksplit - 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (s_last) {
+          __threadfence();
+          if (m == 0) a.arrivals[it.slot] = 0;  // ready for the next forward
+          const float* p0 = a.partial + (int64_t)it.slot * a.ksplit * (DM * NT);
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int row = it.m_tile * DM + h * BM + m;
+            const bool valid = row < a.rows;
+            const int64_t grow = (int64_t)it.le * a.rows + (valid ? row : 0);
+            const float bias = (valid && a.bias) ? a.bias[grow] : 0.0f;
+#pragma unroll 1
+            for (int n = 0; n < NT; n += 2) {
+              float val[2] = {0.0f, 0.0f};
+              for (int sp = 0; sp < a.ksplit; ++sp) {
+                const float2 pv = __ldcg(reinterpret_cast<const float2*>(
+                    p0 + (int64_t)sp * (DM * NT) + (h * BM + m) * NT + n));
+                val[0] = sp == 0 ? pv.x : __fadd_rn(val[0], pv.x);
+                val[1] = sp == 0 ? pv.y : __fadd_rn(val[1], pv.y);
+              }
+              finish_pair<MODE>(a, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+            }
+          }
+        }
+      }
     }
   }
 
@@ -659,6 +719,27 @@ cudaError_t launch_mx(const Moe& m, const mx::Args& a, const ExpertBufs& eb, int
   }
 }
 
+// K splits for a launch of at most `items` work items on `slots` CTAs: the
+// fewest (1..8, at most the K chunks) that fill at least 80 % of the waves,
+// within the partial-sum buffer.
+int choose_ksplit(int64_t items, int slots, int kchunks, int nt) {
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= std::min(8, kchunks); ++s) {
+    if (s > 1 && (items * s > kMxSplitSlots ||
+                  items * s * mx::DM * nt * (int64_t)sizeof(float) > (int64_t)kMxPartialBytes))
+      break;
+    const int64_t n = items * s;
+    const double eff = (double)n / ((double)((n + slots - 1) / slots) * slots);
+    if (eff >= 0.8) return s;
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
 mx::Args mx_common(const Moe& m, const Groups& g, const ExpertBufs& eb, int rows) {
   mx::Args a{};
   a.e_begin = m.e_begin;
@@ -670,7 +751,19 @@ mx::Args mx_common(const Moe& m, const Groups& g, const ExpertBufs& eb, int rows
   a.err = g.meta + 1;
   a.rows = rows;
   a.m_tiles = (rows + mx::DM - 1) / mx::DM;
+  a.ksplit = 1;
+  a.partial = eb.mx_partial;
+  a.arrivals = eb.mx_arrivals;
   return a;
+}
+
+// Split K when the tiles cannot fill the CTAs: bounded by the most N tiles a
+// grouping of g.rows rows can make.
+void set_ksplit(const Moe& m, const Groups& g, int kind, mx::Args& a) {
+  const int nt = mx_tile_positions(kind);
+  const int64_t nloc = std::max<int64_t>(1, m.e_end - m.e_begin);
+  const int64_t tiles = std::min<int64_t>(g.rows, nloc + g.rows / nt);
+  a.ksplit = choose_ksplit(tiles * a.m_tiles, m.sm_count * 2, a.kchunks, nt);
 }
 
 }  // namespace
@@ -695,6 +788,7 @@ cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, Exp
   a.h_exp = m.mx.h_exp;
   a.out_q = eb.hq;
   a.out_stride = d.inter;
+  set_ksplit(m, g, kind, a);
   return launch_mx<0>(m, a, eb, kind, st);
 }
 
@@ -710,6 +804,7 @@ cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, int ki
   a.out_y = eb.y;
   a.out_rows = g.out_rows;
   a.out_stride = d.hidden;
+  set_ksplit(m, g, kind, a);
   return launch_mx<1>(m, a, eb, kind, st);
 }
 
