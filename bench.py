@@ -17,6 +17,10 @@ Arms:
                      oracle/, built from the reference's Rust sources' logic)
                      on the host cores, one bounded sample per step.
 
+--model lfm2 measures the LFM2.5-shaped layer instead (hidden 2048,
+intermediate 1792, 32 experts, top-4, Q4_K experts, sigmoid router with a
+selection bias, SiLU; d = 2^-11, dmin = 7.5 d).  The default is GPT-OSS.
+
 Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): one process
 per GPU, expert parallel: rank r holds experts [r*E/N, (r+1)*E/N) and its own
 batch of --tokens tokens; routed rows go to the owning rank and back by NCCL
@@ -41,11 +45,54 @@ for _p in (ROOT, os.path.join(ROOT, "rs-gallium_b200")):
 
 import numpy as np  # noqa: E402
 
-H = 2880
-I = 2880
 TOPK = 4
-METRIC = "MoE-layer tokens/s (GPT-OSS-120B shape, MXFP4)"
 L2_BYTES = 126 * 1024 * 1024
+
+
+class Model:
+    """Shapes, loader and byte counts of one measured MoE layer."""
+
+    def __init__(self, name, experts):
+        self.name = name
+        if name == "gptoss":
+            self.H, self.I, self.E = 2880, 2880, experts or 128
+            self.metric = "MoE-layer tokens/s (GPT-OSS-120B shape, MXFP4)"
+            self.shape = f"gpt-oss-120b-shaped MoE layer, E={self.E}, H=I=2880, top-{TOPK}, MXFP4"
+        else:
+            self.H, self.I, self.E = 2048, 1792, experts or 32
+            self.metric = "MoE-layer tokens/s (LFM2.5 shape, Q4_K)"
+            self.shape = (f"lfm2.5-shaped MoE layer, E={self.E}, H=2048, I=1792, top-{TOPK}, "
+                          f"Q4_K, sigmoid router")
+
+    def layer(self, args):
+        from gallium_b200 import synth
+        if self.name == "gptoss":
+            return synth.gptoss_layer(n_experts=self.E, seed=args.seed, skewed=args.skewed)
+        return synth.lfm2_layer(n_experts=self.E, seed=args.seed)
+
+    def load(self, layer, device, max_tokens, ep):
+        from gallium_b200 import Lfm2QMoEFFN, OssMoEFFN
+        cls = OssMoEFFN if self.name == "gptoss" else Lfm2QMoEFFN
+        return cls.load(layer, device=device, max_tokens=max_tokens, ep=ep)
+
+    def stage_weight_bytes(self):
+        """(gate_up, down) bytes of one expert: codes + scales (+ bf16 biases)."""
+        H, I = self.H, self.I
+        if self.name == "gptoss":
+            return (2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 2, H * I // 2 + H * I // 32 + H * 2)
+        return (2 * I * H // 256 * 144, H * I // 256 * 144)
+
+    def route(self, layer, x):
+        """Oracle routing of x: (idx [T, k], oracle object for the experts)."""
+        import oracle
+        if self.name == "gptoss":
+            rw = (layer.router_w.astype(np.uint32) << 16).view(np.float32)
+            rb = (layer.router_b.astype(np.uint32) << 16).view(np.float32)
+            idx, _ = oracle.route_softmax_topk(oracle.router_logits(x, rw, rb), TOPK)
+            return idx, oracle.OracleMoe(layer)
+        lg = oracle.router_logits(x, layer.router_w, None)
+        idx, _ = oracle.route_sigmoid_topk(lg, layer.sel_bias, TOPK)
+        return idx, oracle.OracleLfm2(layer)
 
 
 def parse_args():
@@ -55,7 +102,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=8192)
-    ap.add_argument("--experts", type=int, default=128)
+    ap.add_argument("--model", choices=["gptoss", "lfm2"], default="gptoss")
+    ap.add_argument("--experts", type=int, default=0, help="default 128 (gptoss) / 32 (lfm2)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--skewed", action="store_true", help="Zipf(1.2) router bias")
     ap.add_argument("--sweep", default="1,32,1024",
@@ -206,14 +254,17 @@ def cpu_cores(requested: int) -> int:
         return os.cpu_count() or 1
 
 
-def cpu_sample(layer, x, counts, cores):
-    """Time the reference's per-expert work (dequantise once, f32 GEMMs, clamped
-    SwiGLU; gpt_oss_q.rs:194-246) for a bounded set of experts with their real
-    token counts, plus the routing of a bounded token sample, and scale both to
-    the whole batch.  Returns (tokens/s, description)."""
-    import oracle
-    om = oracle.OracleMoe(layer)
+def cpu_sample(model, layer, x, counts, cores):
+    """Time the reference's per-expert work (dequantise once, f32 GEMMs, the
+    activation; gpt_oss_q.rs:194-246, lfm2moe_q.rs:279-296) for a bounded set
+    of experts with their real token counts, plus the routing of a bounded
+    token sample, and scale both to the whole batch.  Returns (tokens/s,
+    description)."""
     T = x.shape[0]
+    tr = min(T, 256)
+    t0 = time.perf_counter()
+    _, om = model.route(layer, x[:tr])
+    t_route = time.perf_counter() - t0
     active = [e for e in range(len(counts)) if counts[e] > 0]
     m = min(len(active), max(1, cores))
     sample = np.array(active[:m], np.int32)
@@ -221,13 +272,6 @@ def cpu_sample(layer, x, counts, cores):
     t0 = time.perf_counter()
     om.expert_sample(x[: int(ntok.max())], sample, ntok, n_threads=cores)
     t_exp = time.perf_counter() - t0
-    tr = min(T, 256)
-    rw = (layer.router_w.astype(np.uint32) << 16).view(np.float32)
-    rb = (layer.router_b.astype(np.uint32) << 16).view(np.float32)
-    t0 = time.perf_counter()
-    lg = oracle.router_logits(x[:tr], rw, rb)
-    oracle.route_softmax_topk(lg, layer.top_k)
-    t_route = time.perf_counter() - t0
     est = t_exp * len(active) / m + t_route * T / tr
     desc = (f"{m} of {len(active)} active experts with their routed token counts "
             f"({int(ntok.sum())} token-expert rows) + routing of {tr} of {T} tokens, "
@@ -243,29 +287,26 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     from gallium_b200 import synth
-    import oracle
-    layer = synth.gptoss_layer(n_experts=args.experts, seed=args.seed, skewed=args.skewed)
+    model = Model(args.model, args.experts)
+    layer = model.layer(args)
     T = args.tokens
-    x = synth.tokens(T, H, seed=args.seed)
+    x = synth.tokens(T, model.H, seed=args.seed)
     cores = cpu_cores(args.cpu_threads)
-    rw = (layer.router_w.astype(np.uint32) << 16).view(np.float32)
-    rb = (layer.router_b.astype(np.uint32) << 16).view(np.float32)
-    idx, _ = oracle.route_softmax_topk(oracle.router_logits(x, rw, rb), TOPK)
-    counts = np.bincount(idx.ravel(), minlength=args.experts)
+    idx, _ = model.route(layer, x)
+    counts = np.bincount(idx.ravel(), minlength=model.E)
     vals, desc = [], ""
     for i in range(args.warmup + args.steps):
-        v, desc = cpu_sample(layer, x, counts, cores)
+        v, desc = cpu_sample(model, layer, x, counts, cores)
         if i >= args.warmup:
             vals.append(v)
     value = statistics.mean(vals)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "impl": "reference", "metric": model.metric, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * T / value, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"gpt-oss-120b-shaped MoE layer, E={args.experts}, H=I={H}, "
-                               f"top-{TOPK}, MXFP4, T={T} tokens",
-                   "tokens": T, "experts": args.experts, "skewed": args.skewed},
+        "config": {"workload": f"{model.shape}, T={T} tokens",
+                   "tokens": T, "experts": model.E, "skewed": args.skewed},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": desc},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -305,13 +346,11 @@ def measured_traffic(T, E, stage, n_gpus):
     return None
 
 
-def roofline_for(stage_ms, T, n_touched, layer, peaks, n_gpus=1):
+def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
     """Roofline of the dominant expert kernel (gate_up or down)."""
-    E = layer.n_experts
-    k = layer.top_k
+    H, I, E, k = model.H, model.I, model.E, TOPK
     rows = T * k
-    gu_w = 2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 2   # nibbles + scales + bf16 bias per expert
-    dn_w = H * I // 2 + H * I // 32 + H * 2
+    gu_w, dn_w = model.stage_weight_bytes()
     stage_bytes = {
         "gate_up": n_touched * gu_w + rows * H * 4 + rows * I * 4,  # weights + gathered x + h
         "down": n_touched * dn_w + rows * I * 4 + rows * H * 4,
@@ -319,36 +358,39 @@ def roofline_for(stage_ms, T, n_touched, layer, peaks, n_gpus=1):
     stage_flops = {"gate_up": 2 * rows * 2 * I * H, "down": 2 * rows * H * I}
     dom = max(("gate_up", "down"), key=lambda s: stage_ms.get(s, 0.0))
     t = stage_ms[dom] / 1e3
+    traffic = measured_traffic(T, E, dom, n_gpus) if model.name == "gptoss" else None
     if T <= 64:
         ach = stage_bytes[dom] / t / 1e9
         return {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
                 "peak_source": peaks["source"], "algorithmic_bytes": stage_bytes[dom],
-                "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom, n_gpus)}
+                "launch_ms": stage_ms[dom], "traffic": traffic}
     ach = stage_flops[dom] / t / 1e12
     return {"kernel": dom, "bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"],
             "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"],
             "peak_source": peaks["source"], "algorithmic_flops": stage_flops[dom],
-            "launch_ms": stage_ms[dom], "traffic": measured_traffic(T, E, dom, n_gpus)}
+            "launch_ms": stage_ms[dom], "traffic": traffic}
 
 
 def run_ours(args, world, rank, local):
     import torch
-    from gallium_b200 import OssMoEFFN, nccl_unique_id, synth
+    from gallium_b200 import nccl_unique_id, synth
     from gallium_b200._lib import check, load_library
 
     lib = load_library()
     peaks = load_peaks()
+    model = Model(args.model, args.experts)
+    H = model.H
     T = args.tokens
     sweep = [int(s) for s in args.sweep.split(",") if s.strip()] if args.sweep else []
-    layer = synth.gptoss_layer(n_experts=args.experts, seed=args.seed, skewed=args.skewed)
+    layer = model.layer(args)
     ep = None
     if world > 1:
         import torch.distributed as dist
         obj = [nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
         ep = (rank, world, obj[0])
-    moe = OssMoEFFN.load(layer, device=local, max_tokens=max([T] + sweep), ep=ep)
+    moe = model.load(layer, local, max([T] + sweep), ep)
     moe.set_expert_path(args.expert_path)
     # buffers hold the largest batch of the run (T and every sweep size)
     x = synth.tokens(max([T] + sweep), H, seed=args.seed + 1000 * rank)
@@ -385,7 +427,7 @@ def run_ours(args, world, rank, local):
         import torch.distributed as dist
         ct = torch.from_numpy(counts.astype(np.int64)).cuda()
         dist.all_reduce(ct)
-        lo, hi = rank * args.experts // world, (rank + 1) * args.experts // world
+        lo, hi = rank * model.E // world, (rank + 1) * model.E // world
         n_touched = int((ct[lo:hi] > 0).sum())
 
     # ---- timed region: exactly K steps --------------------------------------
@@ -420,7 +462,7 @@ def run_ours(args, world, rank, local):
 
     # ---- roofline of the dominant kernel ------------------------------------
     stages = stage_profile(moe, xd, out, T, flush)
-    roof = roofline_for(stages, T, n_touched, layer, peaks, world)
+    roof = roofline_for(model, stages, T, n_touched, peaks, world)
 
     # ---- other batch sizes of the workload -----------------------------------
     sweep_out = []
@@ -432,34 +474,33 @@ def run_ours(args, world, rank, local):
             import torch.distributed as dist
             ct = torch.from_numpy(c.astype(np.int64)).cuda()
             dist.all_reduce(ct)
-            lo, hi = rank * args.experts // world, (rank + 1) * args.experts // world
-            c = np.zeros(args.experts, np.int64)
+            lo, hi = rank * model.E // world, (rank + 1) * model.E // world
+            c = np.zeros(model.E, np.int64)
             c[lo:hi] = ct[lo:hi].cpu().numpy()
         barrier(world)
         ms = allmax(world, timed(args.steps, Ts, fwd_dev)) / args.steps
         st = stage_profile(moe, xd, out, Ts, flush)
         sweep_out.append({"tokens": Ts, "value": world * Ts / (ms / 1e3), "ms_per_step": ms,
                           "stages_ms": st,
-                          "roofline": roofline_for(st, Ts, int((c > 0).sum()), layer, peaks,
+                          "roofline": roofline_for(model, st, Ts, int((c > 0).sum()), peaks,
                                                    world)})
 
     # ---- CPU baseline (rank 0, one GPU only) ---------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = cpu_cores(args.cpu_threads)
-        v, desc = cpu_sample(layer, x, counts, cores)
+        v, desc = cpu_sample(model, layer, x, counts, cores)
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "metric": model.metric, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded weights and inputs of the workload's shapes)",
-            "config": {"workload": f"gpt-oss-120b-shaped MoE layer, E={args.experts}, H=I={H}, "
-                                   f"top-{TOPK}, MXFP4, T={T} tokens per GPU",
-                       "tokens_per_gpu": T, "experts": args.experts, "skewed": args.skewed,
-                       "parallelism": (f"ep{world} (expert parallel, {args.experts // world} experts "
+            "config": {"workload": f"{model.shape}, T={T} tokens per GPU",
+                       "tokens_per_gpu": T, "experts": model.E, "skewed": args.skewed,
+                       "parallelism": (f"ep{world} (expert parallel, {model.E // world} experts "
                                        f"per GPU, NCCL dispatch/combine)") if world > 1 else "single GPU",
                        "l2": "flushed (256 MiB write) before every timed step",
                        "experts_touched": n_touched},
