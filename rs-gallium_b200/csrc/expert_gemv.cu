@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "moe_internal.h"
+#include "ptx.cuh"
 
 namespace gb {
 namespace {
@@ -192,6 +193,8 @@ cudaError_t launch_rows(const Moe& m, const Groups& g, const float* in, int K_in
 __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv,
                                const float* __restrict__ wts, const int32_t* __restrict__ idx,
                                int H, int K, int expert_order, float* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const int o4 = blockIdx.y * blockDim.x + threadIdx.x;
   if (o4 * 4 >= H) return;
@@ -286,9 +289,8 @@ cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const f
   const int threads = 256;
   dim3 grid((unsigned)T, (unsigned)((H / 4 + threads - 1) / threads));
   const int expert_order = m.desc.weight_format != GB_FMT_MXFP4_SPLIT;
-  combine_kernel<<<grid, threads, 0, st>>>(y, ws.inv, ws.wts, ws.idx, H, m.desc.top_k,
-                                           expert_order, out);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, y, ws.inv, ws.wts, ws.idx, H,
+                    m.desc.top_k, expert_order, out);
 }
 
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,

@@ -11,6 +11,25 @@
 
 namespace gb {
 
+// Launches `kern` with programmatic stream serialization: its blocks may be
+// scheduled while the previous kernel on the stream finishes (its own
+// pdl_wait() orders its memory accesses after that kernel).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Repacked expert weights of the local experts (device memory).
 //
 // Layout (MXFP4, one layout for both caller formats):

@@ -282,9 +282,9 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_items = a.meta[2] * a.m_tiles * a.ksplit;
   const int nk = a.kchunks;
   __shared__ int s_last;
+  pdl_trigger();
 
   for (int i = threadIdx.x; i < SF_BYTES / 4; i += kThreads)
     reinterpret_cast<uint32_t*>(sfb_const)[i] = piece_scale_word(i);
@@ -306,6 +306,10 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touches only this CTA's shared memory and TMEM, so it
+  // overlaps the tail of the grid before; global memory is read after the wait.
+  pdl_wait();
+  const int total_items = a.meta[2] * a.m_tiles * a.ksplit;
 
   if (warp == 4 || warp == 6) {
     // ---------------- TMA producers: warp 4 even steps, warp 6 odd ----------
@@ -494,6 +498,8 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
 __global__ void __launch_bounds__(128) split_pieces_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ perm, int perm_div, int K,
     int positions, uint8_t* __restrict__ q, float* __restrict__ xscale) {
+  pdl_trigger();
+  pdl_wait();
   const int pos = blockIdx.x;
   if (pos >= positions) return;
   const float4* src = reinterpret_cast<const float4*>(x + (int64_t)(perm[pos] / perm_div) * K);
@@ -699,10 +705,9 @@ cudaError_t launch_tiles(const Moe& m, const mx::Args& a, const void* map_w, con
   const size_t smem = mx::Tile<NT>::SMEM;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  k<<<m.sm_count * mx::Tile<NT>::CPS, mx::kThreads, smem, st>>>(
-      *reinterpret_cast<const CUtensorMap*>(map_w), *reinterpret_cast<const CUtensorMap*>(map_x),
-      a);
-  return cudaGetLastError();
+  return launch_pdl(k, dim3(m.sm_count * mx::Tile<NT>::CPS), dim3(mx::kThreads), smem, st,
+                    *reinterpret_cast<const CUtensorMap*>(map_w),
+                    *reinterpret_cast<const CUtensorMap*>(map_x), a);
 }
 
 template <int MODE>
@@ -775,9 +780,9 @@ cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, Exp
   cudaError_t e;
   if ((e = launch_tile_table(m, g, mx_tile_positions(kind), eb, st)) != cudaSuccess) return e;
   if (positions > 0) {
-    mx::split_pieces_kernel<<<positions, 128, 0, st>>>(x, g.perm, g.perm_div, d.hidden, positions,
-                                                      eb.xq, eb.xscale);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    if ((e = launch_pdl(mx::split_pieces_kernel, dim3(positions), dim3(128), 0, st, x, g.perm,
+                        g.perm_div, d.hidden, positions, eb.xq, eb.xscale)) != cudaSuccess)
+      return e;
   }
   mx::Args a = mx_common(m, g, eb, 2 * d.inter);
   a.sfa = m.mx.gu_sfa;

@@ -12,6 +12,7 @@
 // of the lower lanes' bits gives the token's place inside its word.
 #include "common.cuh"
 #include "moe_internal.h"
+#include "ptx.cuh"
 
 namespace gb {
 namespace {
@@ -31,6 +32,8 @@ __global__ void __launch_bounds__(kPermThreads)
   unsigned* wpre = bits + E * kWords;  // [E][kWords]
   unsigned* chunk = wpre + E * kWords; // [E]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_trigger();
+  pdl_wait();
 
   for (int e = tid; e < E; e += kPermThreads) cnt[e] = 0;
   __syncthreads();
@@ -136,10 +139,9 @@ cudaError_t launch_permute(const Moe& m, const int32_t* idx, int64_t T, Workspac
   cudaError_t err =
       cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  permute_kernel<<<1, kPermThreads, smem, st>>>(idx, (int)T, E, m.desc.top_k, m.e_begin, m.e_end,
-                                                ws.counts, ws.offsets, ws.active, ws.meta,
-                                                ws.perm, ws.inv);
-  return cudaGetLastError();
+  return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), smem, st, idx, (int)T, E,
+                    m.desc.top_k, m.e_begin, m.e_end, ws.counts, ws.offsets, ws.active, ws.meta,
+                    ws.perm, ws.inv);
 }
 
 }  // namespace gb

@@ -63,6 +63,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
   return true;
 }
 
+// Programmatic dependent launch.  pdl_wait: wait until the grids this one
+// depends on have completed and their writes are visible (returns at once for
+// an ordinary launch); every kernel launched with launch_pdl calls it before
+// its first global-memory access.  pdl_trigger: let the next grid on the
+// stream begin launching (it still waits in its own pdl_wait).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -143,6 +143,8 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
                   unsigned* __restrict__ tickets, int32_t* __restrict__ idx_out,
                   float* __restrict__ w_out) {
   extern __shared__ float xs[];  // [TT][H]
+  pdl_trigger();
+  pdl_wait();
   const int t0 = blockIdx.x * TT;
   const int nt = min(TT, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -229,6 +231,8 @@ __global__ void __launch_bounds__(256, 2)
                         unsigned* __restrict__ tickets, int32_t* __restrict__ idx_out,
                         float* __restrict__ w_out) {
   extern __shared__ __align__(16) float sm[];  // two buffers of [32 tokens + 16 experts][256]
+  pdl_trigger();
+  pdl_wait();
   constexpr int kBuf = (kTileTokens + kTileExperts) * kTileK;
   const int t0 = blockIdx.x * kTileTokens, e0 = blockIdx.y * kTileExperts;
   const int nt = min(kTileTokens, T - t0);
@@ -347,10 +351,9 @@ cudaError_t launch(const Moe& m, const float* x, int64_t T, int32_t* idx, float*
   auto kern = router_kernel<TT, EPW>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  kern<<<grid, kRouterWarps * 32, smem, st>>>(x, (int)T, H, m.router_w, m.router_b, E, d.top_k,
-                                              d.router_kind, m.sel_bias, m.ws.logits,
-                                              m.ws.tickets, idx, wts);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, dim3(kRouterWarps * 32), smem, st, x, (int)T, H, m.router_w,
+                    m.router_b, E, d.top_k, d.router_kind, m.sel_bias, m.ws.logits, m.ws.tickets,
+                    idx, wts);
 }
 
 }  // namespace
@@ -367,10 +370,9 @@ cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t*
   cudaError_t err = cudaFuncSetAttribute(router_tiled_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;
-  router_tiled_kernel<<<grid, 256, smem, st>>>(x, (int)T, d.hidden, m.router_w, m.router_b,
-                                               d.n_experts, d.top_k, d.router_kind, m.sel_bias,
-                                               m.ws.logits, m.ws.tickets, idx, wts);
-  return cudaGetLastError();
+  return launch_pdl(router_tiled_kernel, grid, dim3(256), smem, st, x, (int)T, d.hidden,
+                    m.router_w, m.router_b, d.n_experts, d.top_k, d.router_kind, m.sel_bias,
+                    m.ws.logits, m.ws.tickets, idx, wts);
 }
 
 }  // namespace gb

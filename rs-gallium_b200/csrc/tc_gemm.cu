@@ -446,6 +446,8 @@ __global__ void tile_table_kernel(const int32_t* __restrict__ counts,
                                   int bn, int32_t* __restrict__ meta,
                                   int32_t* __restrict__ tile_expert,
                                   int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows) {
+  pdl_trigger();
+  pdl_wait();
   const int lane = threadIdx.x;
   int base_j = 0;
   for (int e0 = e_begin; e0 < e_end; e0 += 32) {
@@ -600,14 +602,9 @@ cudaError_t launch_gemm(const Moe& m, const tc::Args& a, const void* map_w, cons
 
 cudaError_t launch_tile_table(const Moe& m, const Groups& g, int bn, ExpertBufs& eb,
                               cudaStream_t st) {
-  tc::tile_table_kernel<<<1, 32, 0, st>>>(g.counts, g.offsets, m.e_begin, m.e_end, bn, g.meta,
-                                          eb.tile_expert, eb.tile_row0, eb.tile_rows);
-  return cudaGetLastError();
+  return launch_pdl(tc::tile_table_kernel, dim3(1), dim3(32), 0, st, g.counts, g.offsets,
+                    m.e_begin, m.e_end, bn, g.meta, eb.tile_expert, eb.tile_row0, eb.tile_rows);
 }
-
-namespace {
-
-}  // namespace
 
 cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               cudaStream_t st) {
