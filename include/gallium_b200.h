@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define GB_ABI_VERSION 1
+#define GB_ABI_VERSION 2
 
 typedef enum gb_status {
   GB_OK = 0,
@@ -139,6 +139,7 @@ typedef struct gb_moe_info {
   int32_t workspace_tokens;
   int32_t sm_count;
   int64_t kernel_launches;  /* kernels this handle has launched so far */
+  int64_t graph_captures;   /* forward graphs captured so far (gb_moe_set_graphs) */
 } gb_moe_info;
 
 /* Create: validates the descriptor, uploads and repacks the weights.
@@ -203,6 +204,17 @@ typedef enum {
   GB_PATH_TENSOR_CORES_F16 = 3
 } gb_expert_path;
 int gb_moe_set_expert_path(gb_moe* m, int32_t path);
+
+/* Forward graphs.  A single-GPU gb_moe_forward (and gb_moe_forward_host) of
+ * at most 512 tokens is captured once per (x, out, T) into a CUDA graph and
+ * replayed on later calls with the same triple, which removes the host launch
+ * cost of its kernels; the graph reads x and writes out at replay time, so
+ * new contents of the same buffers are used.  Up to `max_graphs` (0..16,
+ * default 16) graphs are kept, least recently used replaced; 0 launches
+ * every kernel directly.  Changing the expert path, growing the workspace
+ * or calling this clears the cache.  No counterpart in the reference, which
+ * has one CPU path. */
+int gb_moe_set_graphs(gb_moe* m, int32_t max_graphs);
 
 /* Stage timing for profiling (no counterpart in the reference, whose timing
  * is per generated token, crates/gallium-agent/src/llm_candle.rs:302-345).

@@ -212,7 +212,7 @@ cudaError_t launch_dec(const Moe& m, const Groups& g, const DecArgs& a, cudaStre
   const size_t smem = (size_t)TC * (a.K / 32) * kBlockPitch * sizeof(float) +
                       (size_t)kDecWarps * kRing * 2 * ((a.K / 32) * 16 + a.sp);
   auto kern = decode_rows_kernel<MODE, TC>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = set_smem_limit(kern, smem);
   if (err != cudaSuccess) return err;
   kern<<<grid, kDecWarps * 32, smem, st>>>(a);
   return cudaGetLastError();

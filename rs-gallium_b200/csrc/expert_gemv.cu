@@ -169,7 +169,7 @@ cudaError_t launch_rows(const Moe& m, const Groups& g, const float* in, int K_in
 #define GB_LAUNCH_NBQ(Q)                                                                         \
   {                                                                                              \
     auto kern = expert_rows_kernel<MODE, TC, Q>;                                                 \
-    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
+    err = set_smem_limit(kern, smem);                                                            \
     if (err != cudaSuccess) return err;                                                          \
     kern<<<grid, kWarps * 32, smem, st>>>(in, K_in, n_rows_total, g.perm_div, blocks, scales, sp, \
                                           bias, m.w.zero_scale, g.counts, g.offsets, g.active,   \

@@ -7,8 +7,10 @@
 #include <string.h>
 
 #include <algorithm>
+#include <mutex>
 #include <new>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "moe_internal.h"
@@ -140,6 +142,20 @@ void free_ws(gb::Workspace& ws) {
   ws = gb::Workspace{};
 }
 
+// Destroys the cached forward graphs once the device has finished them.
+// The handle's device is current.
+void clear_graphs(gb::Moe& m) {
+  bool any = false;
+  for (const auto& g : m.graphs) any |= g.exec != nullptr;
+  if (!any) return;
+  cudaDeviceSynchronize();
+  for (auto& g : m.graphs) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    g = gb::Moe::Graph{};
+  }
+  for (auto& g : m.seen) g = gb::Moe::Graph{};
+}
+
 struct Piece {
   void** ptr;
   size_t bytes;
@@ -205,6 +221,7 @@ int alloc_ws(gb::Moe& m, int64_t T) {
     cudaFree(base);
     return rc;
   }
+  clear_graphs(m);
   free_ws(m.ws);
   m.ws = ws;
   return GB_OK;
@@ -234,6 +251,8 @@ void release_moe(gb::Moe& m) {
     if (e) cudaEventDestroy(e);
   for (auto& e : m.host_ev)
     if (e) cudaEventDestroy(e);
+  clear_graphs(m);
+  if (m.cap) cudaStreamDestroy(m.cap);
   if (m.h2d) cudaStreamDestroy(m.h2d);
   if (m.d2h) cudaStreamDestroy(m.d2h);
   cudaFree(m.router_w);
@@ -478,8 +497,38 @@ int read_device_status(gb::Moe& m, cudaStream_t st) {
   return GB_OK;
 }
 
+// Router, then grouping, tile table and pieces in one launch (small
+// single-GPU batches on the block-scaled path); g.grouped set.
+int run_route_grouped(gb::Moe& m, const float* x, int64_t T, gb::Groups& g, int kind,
+                      cudaStream_t st) {
+  int rc;
+  if ((rc = mark(m, 0, st))) return rc;
+  GB_CUDA(gb::launch_router_topk(m, x, T, m.ws.idx, m.ws.wts, st), "router kernel launch");
+  if ((rc = mark(m, 1, st))) return rc;
+  GB_CUDA(gb::launch_mx_group(m, x, T, m.ws, kind, st), "grouping kernel launch");
+  m.launches += 2;
+  g.grouped = true;
+  return mark(m, 2, st);
+}
+
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
   int rc;
+  if (m.ep_size == 1 && m.desc.weight_format != GB_FMT_Q4_K && gb::mx_group_fits(m, T) &&
+      pick_expert_kernel(m, m.ws.eb) == ExpertKernel::kMx) {
+    gb::Groups g = local_groups(m, T);
+    const int kind = gb::mx_tile_kind(m, g);
+    if ((rc = run_route_grouped(m, x, T, g, kind, st))) return rc;
+    GB_CUDA(gb::launch_mx_gate_up(m, g, x, m.ws.eb, kind, st), "block-scaled gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(gb::launch_mx_down(m, g, m.ws.eb, kind, st), "block-scaled down launch");
+    m.launches += 2;
+    if ((rc = mark(m, 4, st))) return rc;
+    GB_CUDA(gb::launch_combine(m, T, m.ws, m.ws.eb.y, out, st), "combine kernel launch");
+    m.launches += 1;
+    if ((rc = mark(m, 5, st))) return rc;
+    m.profiled_once = m.profiling;
+    return GB_OK;
+  }
   if (T > 0) {
     if ((rc = run_route(m, x, T, st))) return rc;
   } else {
@@ -502,9 +551,99 @@ int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t 
   return GB_OK;
 }
 
+// Captures the forward of (x, T, out) into `slot` (replacing what it held).
+int capture_forward(gb::Moe& m, const float* x, int64_t T, float* out, gb::Moe::Graph* slot) {
+  if (!m.cap) GB_CUDA(cudaStreamCreateWithFlags(&m.cap, cudaStreamNonBlocking), "capture stream");
+  if (slot->exec) {
+    // the replaced graph may still be running on any stream
+    GB_CUDA(cudaDeviceSynchronize(), "synchronise before replacing a forward graph");
+    cudaGraphExecDestroy(slot->exec);
+    *slot = gb::Moe::Graph{};
+  }
+  const int64_t before = m.launches;
+  GB_CUDA(cudaStreamBeginCapture(m.cap, cudaStreamCaptureModeThreadLocal), "begin forward capture");
+  const int rc = run_forward(m, x, T, out, m.cap);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(m.cap, &graph);
+  const int64_t n = m.launches - before;
+  m.launches = before;
+  if (rc || ce != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc ? rc : cuda_err(ce, "capture forward");
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) return cuda_err(ie, "instantiate forward graph");
+  slot->x = x;
+  slot->out = out;
+  slot->T = T;
+  slot->exec = exec;
+  slot->launches = n;
+  ++m.graph_captures;
+  return GB_OK;
+}
+
+// Slot of `slots[0..n)` holding (x, out, T), or null; `victim` gets the
+// empty or least recently used slot.
+gb::Moe::Graph* find_slot(gb::Moe::Graph* slots, int n, const float* x, int64_t T,
+                          const float* out, gb::Moe::Graph** victim) {
+  *victim = &slots[0];
+  for (int i = 0; i < n; ++i) {
+    gb::Moe::Graph& g = slots[i];
+    if (g.used && g.x == x && g.out == out && g.T == T) return &g;
+    if ((*victim)->used && (!g.used || g.used < (*victim)->used)) *victim = &g;
+  }
+  return nullptr;
+}
+
+// The forward as gb_moe_forward runs it.  A single-GPU batch of at most
+// kGraphMaxTokens tokens whose (x, out, T) came before replays a cached CUDA
+// graph (its kernels last a few microseconds each, so launching them one by
+// one from the host would dominate); other forwards launch their kernels
+// directly.
+int forward_dispatch(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
+  if (m.ep_size > 1 || m.profiling || m.graph_slots <= 0 || T <= 0 ||
+      T > gb::Moe::kGraphMaxTokens)
+    return run_forward(m, x, T, out, st);
+  gb::Moe::Graph* victim = nullptr;
+  gb::Moe::Graph* hit = find_slot(m.graphs, m.graph_slots, x, T, out, &victim);
+  if (!hit) {
+    gb::Moe::Graph* seen_victim = nullptr;
+    gb::Moe::Graph* seen = find_slot(m.seen, m.graph_slots, x, T, out, &seen_victim);
+    if (!seen) {
+      // first sighting: remember it and launch directly
+      *seen_victim = gb::Moe::Graph{x, out, T, nullptr, 0, ++m.graph_clock};
+      return run_forward(m, x, T, out, st);
+    }
+    *seen = gb::Moe::Graph{};
+    int rc = capture_forward(m, x, T, out, victim);
+    if (rc) return rc;
+    hit = victim;
+  }
+  hit->used = ++m.graph_clock;
+  GB_CUDA(cudaGraphLaunch(hit->exec, st), "forward graph launch");
+  m.launches += hit->launches;
+  return GB_OK;
+}
+
 }  // namespace
 
 namespace gb {
+
+cudaError_t set_smem_limit_fn(const void* kern, size_t bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::vector<std::tuple<const void*, int, size_t>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& [k, d, b] : done)
+    if (k == kern && d == dev && b >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess) done.emplace_back(kern, dev, bytes);
+  return e;
+}
 
 int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& eb,
                 cudaStream_t st) {
@@ -695,7 +834,7 @@ int gb_moe_forward(gb_moe* h, const float* x_dev, int64_t T, float* out_dev, voi
   DeviceScope ds(m.device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = ensure_ws(m, T, st))) return rc;
-  return run_forward(m, x_dev, T, out_dev, st);
+  return forward_dispatch(m, x_dev, T, out_dev, st);
 }
 
 }  // extern "C"
@@ -772,7 +911,7 @@ int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_ho
     if (bytes)
       GB_CUDA(cudaMemcpyAsync(m.ws.x_stage, x_host, bytes, cudaMemcpyHostToDevice, st),
               "copy x in");
-    if ((rc = run_forward(m, m.ws.x_stage, T, m.ws.out_stage, st))) return rc;
+    if ((rc = forward_dispatch(m, m.ws.x_stage, T, m.ws.out_stage, st))) return rc;
     if (bytes)
       GB_CUDA(cudaMemcpyAsync(out_host, m.ws.out_stage, bytes, cudaMemcpyDeviceToHost, st),
               "copy out");
@@ -851,6 +990,7 @@ int gb_moe_get_info(const gb_moe* h, gb_moe_info* info) {
   info->workspace_tokens = (int32_t)m.ws.tokens;
   info->sm_count = m.sm_count;
   info->kernel_launches = m.launches;
+  info->graph_captures = m.graph_captures;
   return GB_OK;
 }
 
@@ -903,7 +1043,21 @@ int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
   if (path >= GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m) && !h->m.mx.ok)
     return set_err(GB_ERR_UNSUPPORTED,
                    "tensor-core expert path needs the GPT-OSS activation and H, I multiples of 64");
+  DeviceScope ds(h->m.device);
+  clear_graphs(h->m);
   h->m.expert_path = path;
+  return GB_OK;
+}
+
+int gb_moe_set_graphs(gb_moe* h, int32_t max_graphs) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  if (max_graphs < 0 || max_graphs > gb::Moe::kGraphSlots)
+    return set_err(GB_ERR_INVALID_ARG, "max_graphs %d outside [0, %d]", max_graphs,
+                   gb::Moe::kGraphSlots);
+  DeviceScope ds(h->m.device);
+  clear_graphs(h->m);
+  h->m.graph_slots = max_graphs;
   return GB_OK;
 }
 

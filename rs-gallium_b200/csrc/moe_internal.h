@@ -14,6 +14,14 @@ namespace gb {
 // Launches `kern` with programmatic stream serialization: its blocks may be
 // scheduled while the previous kernel on the stream finishes (its own
 // pdl_wait() orders its memory accesses after that kernel).
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the current
+// device; the attribute is set once per kernel and device (moe_api.cu).
+cudaError_t set_smem_limit_fn(const void* kern, size_t bytes);
+template <typename... KArgs>
+cudaError_t set_smem_limit(void (*kern)(KArgs...), size_t bytes) {
+  return set_smem_limit_fn(reinterpret_cast<const void*>(kern), bytes);
+}
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
                        cudaStream_t st, Args... args) {
@@ -95,6 +103,7 @@ struct Groups {
   int max_active = 0;                 // bound on the active count (grid size)
   int64_t max_per_expert = 0;         // bound on the rows of one expert
   const int32_t* out_rows = nullptr;  // output row of position p for DOWN (null: p)
+  bool grouped = false;  // tile table and activation pieces already written (mx_group)
 };
 
 // Buffers indexed by grouped position, sized for rows_cap positions.
@@ -173,6 +182,27 @@ struct Moe {
   // gb_moe_forward_host pipelining: copy streams and chunk events (lazily made)
   cudaStream_t h2d = nullptr, d2h = nullptr;
   cudaEvent_t host_ev[10] = {};
+  // Replayed forwards: one CUDA graph per (x, out, T), captured on `cap` the
+  // second time a single-GPU forward of at most kGraphMaxTokens tokens meets
+  // that triple (a triple seen once sits in `seen`); least recently used
+  // replaced.  Cleared whenever the workspace, the expert path or the graph
+  // count changes.
+  struct Graph {
+    const float* x = nullptr;
+    float* out = nullptr;
+    int64_t T = 0;
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;  // kernels in the graph
+    uint64_t used = 0;
+  };
+  static constexpr int kGraphSlots = 16;
+  static constexpr int64_t kGraphMaxTokens = 512;
+  Graph graphs[kGraphSlots];
+  Graph seen[kGraphSlots];  // exec unused
+  int graph_slots = kGraphSlots;  // gb_moe_set_graphs; 0 = launch kernels directly
+  uint64_t graph_clock = 0;
+  int64_t graph_captures = 0;
+  cudaStream_t cap = nullptr;
 };
 
 // Records an error message for gb_last_error() and returns `code`.
@@ -216,6 +246,11 @@ size_t mx_piece_bytes(int64_t rows, int k);
 // Tile kind for a grouping of this size, and the positions per tile of a kind.
 int mx_tile_kind(const Moe& m, const Groups& g);
 int mx_tile_positions(int kind);
+// Small single-GPU batches: grouping, tile table and pieces in one launch
+// (replaces launch_permute, the tile table and the pieces of launch_mx_gate_up).
+bool mx_group_fits(const Moe& m, int64_t T);
+cudaError_t launch_mx_group(const Moe& m, const float* x, int64_t T, Workspace& ws, int kind,
+                            cudaStream_t st);
 cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               int kind, cudaStream_t st);
 cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, int kind,

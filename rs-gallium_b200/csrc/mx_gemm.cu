@@ -493,16 +493,14 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   }
 }
 
-// Activation rows (gathered through perm) -> exponent s and four E4M3 pieces
-// of x * 2^-s, written [position][4][K].  One CTA per position.
-__global__ void __launch_bounds__(128) split_pieces_kernel(
-    const float* __restrict__ x, const int32_t* __restrict__ perm, int perm_div, int K,
-    int positions, uint8_t* __restrict__ q, float* __restrict__ xscale) {
-  pdl_trigger();
-  pdl_wait();
-  const int pos = blockIdx.x;
-  if (pos >= positions) return;
-  const float4* src = reinterpret_cast<const float4*>(x + (int64_t)(perm[pos] / perm_div) * K);
+// One activation row -> exponent s and four E4M3 pieces of x * 2^-s, written
+// [4][K] at each of the `ndst` destinations (a token routed to several
+// experts has one grouped position per expert).  128 threads.
+__device__ __forceinline__ void row_pieces(const float* __restrict__ xrow, int K,
+                                           uint8_t* __restrict__ q,
+                                           float* __restrict__ xscale, const int* dst_pos,
+                                           int ndst) {
+  const float4* src = reinterpret_cast<const float4*>(xrow);
   const int n4 = K / 4;
   __shared__ float red[4];
   float mx = 0.0f;
@@ -519,23 +517,167 @@ __global__ void __launch_bounds__(128) split_pieces_kernel(
   int s = mx > 0.0f ? ilogbf(mx) - 7 : 0;
   s = max(-120, min(120, s));
   const float inv = pow2f(-s);
-  if (threadIdx.x == 0) xscale[pos] = (float)s;
-  uint32_t* dst = reinterpret_cast<uint32_t*>(q + (int64_t)pos * kPieces * K);
+  if (threadIdx.x < ndst) xscale[dst_pos[threadIdx.x]] = (float)s;
   for (int i = threadIdx.x; i < n4; i += blockDim.x) {
     const float4 v = src[i];
     float r[4] = {__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
                   __fmul_rn(v.w, inv)};
+    uint32_t w[kPieces];
 #pragma unroll
     for (int p = 0; p < kPieces; ++p) {
       const uint32_t lo = e4m3x2_of(r[1], r[0]), hi = e4m3x2_of(r[3], r[2]);
-      dst[p * n4 + i] = lo | (hi << 16);
+      w[p] = lo | (hi << 16);
       const float2 a = e4m3x2_value(lo), b = e4m3x2_value(hi);
       r[0] = __fmul_rn(__fsub_rn(r[0], a.x), 16.0f);
       r[1] = __fmul_rn(__fsub_rn(r[1], a.y), 16.0f);
       r[2] = __fmul_rn(__fsub_rn(r[2], b.x), 16.0f);
       r[3] = __fmul_rn(__fsub_rn(r[3], b.y), 16.0f);
     }
+    for (int d = 0; d < ndst; ++d) {
+      uint32_t* dst = reinterpret_cast<uint32_t*>(q + (int64_t)dst_pos[d] * kPieces * K);
+#pragma unroll
+      for (int p = 0; p < kPieces; ++p) dst[p * n4 + i] = w[p];
+    }
   }
+}
+
+// Activation rows (gathered through perm) -> pieces, [position][4][K].  One
+// CTA per position.
+__global__ void __launch_bounds__(128) split_pieces_kernel(
+    const float* __restrict__ x, const int32_t* __restrict__ perm, int perm_div, int K,
+    int positions, uint8_t* __restrict__ q, float* __restrict__ xscale) {
+  pdl_trigger();
+  pdl_wait();
+  const int pos = blockIdx.x;
+  if (pos >= positions) return;
+  row_pieces(x + (int64_t)(perm[pos] / perm_div) * K, K, q, xscale, &pos, 1);
+}
+
+// Small batches (T * top_k <= kGroupEntries): grouping, N-tile table and
+// pieces in one launch, one CTA per token.  Every CTA counts all T * top_k
+// routing entries in shared memory and scans them to the expert offsets
+// (a few hundred entries); the entry of token t, rank r goes to position
+// offsets[e] + (entries before it with the same expert), the stable
+// (expert, token) order of permute_kernel, so perm, inv, counts, offsets,
+// active and meta[0] are the same as there.  CTA 0 writes the per-expert
+// arrays and the tile table of tile_table_kernel; CTA t writes perm and inv
+// of its entries and the pieces of x[t] at each of its positions.
+constexpr int kGroupEntries = 512;
+constexpr int kGroupExperts = 256;
+
+__global__ void __launch_bounds__(128) group_pieces_kernel(
+    const float* __restrict__ x, const int32_t* __restrict__ idx, int T, int E, int topk,
+    int H, int e_begin, int e_end, int bn, int32_t* __restrict__ counts,
+    int32_t* __restrict__ offsets, int32_t* __restrict__ active, int32_t* __restrict__ meta,
+    int32_t* __restrict__ perm, int32_t* __restrict__ inv, int32_t* __restrict__ tile_expert,
+    int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows, uint8_t* __restrict__ q,
+    float* __restrict__ xscale) {
+  __shared__ int s_idx[kGroupEntries];
+  __shared__ int s_cnt[kGroupExperts], s_off[kGroupExperts];
+  __shared__ int s_pos[8];
+  pdl_trigger();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n = T * topk, t = blockIdx.x;
+  for (int e = tid; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  unsigned bad = 0;
+  for (int i = tid; i < n; i += blockDim.x) {
+    int e = __ldg(idx + i);
+    if (e < 0 || e >= E) {
+      bad = 1;
+      e = -1;
+    } else {
+      atomicAdd(&s_cnt[e], 1);
+    }
+    s_idx[i] = e;
+  }
+  if (bad && t == 0) atomicOr(reinterpret_cast<unsigned*>(meta + 1), 1u);
+  __syncthreads();
+  if (warp == 0) {
+    // exclusive scan of the counts, 8 experts per lane
+    const int per = (E + 31) / 32;
+    int local = 0;
+    for (int q2 = 0; q2 < per; ++q2) {
+      const int e = lane * per + q2;
+      if (e < E) local += s_cnt[e];
+    }
+    int incl = local;
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+      const int o = __shfl_up_sync(kFullMask, incl, s);
+      if (lane >= s) incl += o;
+    }
+    const int total = __shfl_sync(kFullMask, incl, 31);
+    int run = incl - local;
+    for (int q2 = 0; q2 < per; ++q2) {
+      const int e = lane * per + q2;
+      if (e < E) {
+        s_off[e] = run;
+        run += s_cnt[e];
+      }
+    }
+    if (t == 0) {
+      __syncwarp();
+      int arun = 0, tiles = 0;
+      for (int e0 = 0; e0 < E; e0 += 32) {
+        const int e = e0 + lane;
+        const bool local_e = e < E && e >= e_begin && e < e_end;
+        const int c = e < E ? s_cnt[e] : 0;
+        const int off = e < E ? s_off[e] : 0;
+        if (e < E) {
+          counts[e] = c;
+          offsets[e] = off;
+        }
+        const int act = local_e && c > 0;
+        const unsigned am = __ballot_sync(kFullMask, act);
+        if (act) active[arun + __popc(am & ((1u << lane) - 1u))] = e;
+        arun += __popc(am);
+        const int nt = local_e ? (c + bn - 1) / bn : 0;
+        int tin = nt;
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {
+          const int o = __shfl_up_sync(kFullMask, tin, s);
+          if (lane >= s) tin += o;
+        }
+        int j = tiles + tin - nt;
+        for (int i = 0; i < c && local_e; i += bn, ++j) {
+          tile_expert[j] = e;
+          tile_row0[j] = off + i;
+          tile_rows[j] = min(bn, c - i);
+        }
+        tiles += __shfl_sync(kFullMask, tin, 31);
+      }
+      if (lane == 0) {
+        offsets[E] = total;
+        meta[0] = arun;
+        meta[2] = tiles;
+      }
+    }
+  }
+  __syncthreads();
+  // positions of this token's entries: warp w takes rank w, w + 4, ...
+  for (int r = warp; r < topk; r += 4) {
+    const int i = t * topk + r;
+    const int e = s_idx[i];
+    int before = 0;
+    for (int j0 = 0; j0 < i; j0 += 32) {
+      const int j = j0 + lane;
+      before += __popc(__ballot_sync(kFullMask, j < i && s_idx[j] == e));
+    }
+    const int pos = e >= 0 ? s_off[e] + before : -1;
+    if (lane == 0) {
+      s_pos[r] = pos;
+      if (pos >= 0) perm[pos] = i;
+      inv[i] = max(pos, 0);  // an invalid entry is flagged in meta[1]; keep inv in range
+    }
+  }
+  __syncthreads();
+  int nd = 0;
+  int dpos[8];
+  for (int r = 0; r < topk; ++r)
+    if (s_pos[r] >= 0) dpos[nd++] = s_pos[r];
+  row_pieces(x + (int64_t)t * H, H, q, xscale, dpos, nd);
 }
 
 // Caller nibbles [E_loc][rows][nb][16] -> [E_loc][KC][rows][4 blocks][16],
@@ -703,7 +845,7 @@ cudaError_t launch_tiles(const Moe& m, const mx::Args& a, const void* map_w, con
                          cudaStream_t st) {
   auto k = mx::mx_expert_gemm<MODE, NT>;
   const size_t smem = mx::Tile<NT>::SMEM;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = set_smem_limit(k, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(k, dim3(m.sm_count * mx::Tile<NT>::CPS), dim3(mx::kThreads), smem, st,
                     *reinterpret_cast<const CUtensorMap*>(map_w),
@@ -773,13 +915,31 @@ void set_ksplit(const Moe& m, const Groups& g, int kind, mx::Args& a) {
 
 }  // namespace
 
+bool mx_group_fits(const Moe& m, int64_t T) {
+  const gb_moe_desc& d = m.desc;
+  return T > 0 && T * d.top_k <= mx::kGroupEntries && d.n_experts <= mx::kGroupExperts &&
+         d.top_k <= 8 && d.hidden % 4 == 0;
+}
+
+cudaError_t launch_mx_group(const Moe& m, const float* x, int64_t T, Workspace& ws, int kind,
+                            cudaStream_t st) {
+  const gb_moe_desc& d = m.desc;
+  return launch_pdl(mx::group_pieces_kernel, dim3((unsigned)T), dim3(128), 0, st, x,
+                    (const int32_t*)ws.idx, (int)T, d.n_experts, d.top_k, d.hidden, m.e_begin,
+                    m.e_end, mx_tile_positions(kind), ws.counts, ws.offsets, ws.active, ws.meta,
+                    ws.perm, ws.inv, ws.eb.tile_expert, ws.eb.tile_row0, ws.eb.tile_rows,
+                    ws.eb.xq, ws.eb.xscale);
+}
+
 cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               int kind, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
   const int positions = (int)g.rows;
   cudaError_t e;
-  if ((e = launch_tile_table(m, g, mx_tile_positions(kind), eb, st)) != cudaSuccess) return e;
-  if (positions > 0) {
+  if (!g.grouped &&
+      (e = launch_tile_table(m, g, mx_tile_positions(kind), eb, st)) != cudaSuccess)
+    return e;
+  if (!g.grouped && positions > 0) {
     if ((e = launch_pdl(mx::split_pieces_kernel, dim3(positions), dim3(128), 0, st, x, g.perm,
                         g.perm_div, d.hidden, positions, eb.xq, eb.xscale)) != cudaSuccess)
       return e;

@@ -136,8 +136,7 @@ cudaError_t launch_permute(const Moe& m, const int32_t* idx, int64_t T, Workspac
                            cudaStream_t st) {
   const int E = m.desc.n_experts;
   const size_t smem = sizeof(unsigned) * ((size_t)3 * E + (size_t)2 * E * kWords);
-  cudaError_t err =
-      cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = set_smem_limit(permute_kernel, smem);
   if (err != cudaSuccess) return err;
   return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), smem, st, idx, (int)T, E,
                     m.desc.top_k, m.e_begin, m.e_end, ws.counts, ws.offsets, ws.active, ws.meta,

@@ -187,7 +187,7 @@ cudaError_t launch_q(const Groups& g, const QArgs& a, cudaStream_t st) {
   const int NB = a.K / 32;
   const size_t smem = (size_t)kQTok * NB * kQPitch * sizeof(float) + (size_t)kQTok * NB * sizeof(float);
   auto kern = q4k_rows_kernel<MODE>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = set_smem_limit(kern, smem);
   if (err != cudaSuccess) return err;
   kern<<<grid, kQWarps * 32, smem, st>>>(a);
   return cudaGetLastError();

@@ -148,17 +148,33 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
   const int t0 = blockIdx.x * TT;
   const int nt = min(TT, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e0 = (blockIdx.y * kRouterWarps + warp) * EPW;
+  const int nb = H >> 5;
+  // Decode-sized batches: few warps read the router weight, so each lane
+  // issues all of its weight loads first, then the x loads, and only then
+  // waits (one memory round trip for the CTA).
+  constexpr bool kPreload = EPW == 1 && TT <= 4;
+  const bool preload = kPreload && nb <= kPreloadBlocks && e0 < E;
+  float wv[kPreload ? kPreloadBlocks : 1];
+  if constexpr (kPreload) {
+    if (preload) {
+      const float* wr = rw + (int64_t)e0 * H;
+#pragma unroll
+      for (int j = 0; j < kPreloadBlocks; ++j)
+        if (j < nb) wv[j] = __ldg(wr + lane + (j << 5));
+    }
+  }
 
   {
     const float4* src = reinterpret_cast<const float4*>(x + (int64_t)t0 * H);
     float4* dst = reinterpret_cast<float4*>(xs);
     const int n4 = nt * H / 4;
+#pragma unroll 4
     for (int i = threadIdx.x; i < TT * H / 4; i += blockDim.x)
       dst[i] = i < n4 ? src[i] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncthreads();
 
-  const int e0 = (blockIdx.y * kRouterWarps + warp) * EPW;
   if (e0 < E) {
     float acc[EPW][TT];
 #pragma unroll
@@ -168,14 +184,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
     const float* wrow[EPW];
 #pragma unroll
     for (int q = 0; q < EPW; ++q) wrow[q] = rw + (int64_t)min(e0 + q, E - 1) * H;
-    const int nb = H >> 5;
-    if (EPW == 1 && TT <= 4 && nb <= kPreloadBlocks) {
-      // Decode-sized batches: few warps read the router weight, so issue all
-      // of this lane's loads before the FMA chain (one memory round trip).
-      float wv[kPreloadBlocks];
-#pragma unroll
-      for (int j = 0; j < kPreloadBlocks; ++j)
-        if (j < nb) wv[j] = __ldg(wrow[0] + lane + (j << 5));
+    if (preload) {
 #pragma unroll
       for (int j = 0; j < kPreloadBlocks; ++j) {
         if (j < nb) {
@@ -349,7 +358,7 @@ cudaError_t launch(const Moe& m, const float* x, int64_t T, int32_t* idx, float*
   dim3 grid((unsigned)((T + TT - 1) / TT), (unsigned)((E + kRouterWarps * EPW - 1) / (kRouterWarps * EPW)));
   const size_t smem = (size_t)TT * H * sizeof(float);
   auto kern = router_kernel<TT, EPW>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = set_smem_limit(kern, smem);
   if (err != cudaSuccess) return err;
   return launch_pdl(kern, grid, dim3(kRouterWarps * 32), smem, st, x, (int)T, H, m.router_w,
                     m.router_b, E, d.top_k, d.router_kind, m.sel_bias, m.ws.logits, m.ws.tickets,
@@ -367,8 +376,7 @@ cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t*
   dim3 grid((unsigned)((T + kTileTokens - 1) / kTileTokens),
             (unsigned)((d.n_experts + kTileExperts - 1) / kTileExperts));
   const size_t smem = 2 * (size_t)(kTileTokens + kTileExperts) * kTileK * sizeof(float);
-  cudaError_t err = cudaFuncSetAttribute(router_tiled_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t err = set_smem_limit(router_tiled_kernel, smem);
   if (err != cudaSuccess) return err;
   return launch_pdl(router_tiled_kernel, grid, dim3(256), smem, st, x, (int)T, d.hidden,
                     m.router_w, m.router_b, d.n_experts, d.top_k, d.router_kind, m.sel_bias,

@@ -588,8 +588,7 @@ template <int MODE>
 cudaError_t launch_gemm(const Moe& m, const tc::Args& a, const void* map_w, const void* map_hi,
                         const void* map_lo, cudaStream_t st) {
   auto k = tc::tc_expert_gemm<MODE>;
-  cudaError_t e =
-      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc::kSmemBytes);
+  cudaError_t e = set_smem_limit(k, tc::kSmemBytes);
   if (e != cudaSuccess) return e;
   k<<<m.sm_count, tc::kThreads, tc::kSmemBytes, st>>>(*reinterpret_cast<const CUtensorMap*>(map_w),
                                                       *reinterpret_cast<const CUtensorMap*>(map_hi),

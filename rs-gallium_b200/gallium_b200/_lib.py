@@ -96,6 +96,7 @@ class MoeInfo(ctypes.Structure):
         ("workspace_tokens", c_int32),
         ("sm_count", c_int32),
         ("kernel_launches", c_int64),
+        ("graph_captures", c_int64),
     ]
 
 
@@ -111,6 +112,7 @@ SIGNATURES = {
     "gb_moe_device_status": (c_int, [c_void_p, c_void_p]),
     "gb_moe_destroy": (c_int, [c_void_p]),
     "gb_moe_set_expert_path": (c_int, [c_void_p, c_int32]),
+    "gb_moe_set_graphs": (c_int, [c_void_p, c_int32]),
     "gb_moe_set_profiling": (c_int, [c_void_p, c_int]),
     "gb_moe_stage_times": (c_int, [c_void_p, POINTER(c_float), c_int32, POINTER(c_int32)]),
     "gb_moe_stage_name": (c_char_p, [c_int32]),

@@ -121,6 +121,11 @@ class MoEBlock:
                 "tensor_cores_f16": _lib.GB_PATH_TENSOR_CORES_F16}[path]
         check(self._lib.gb_moe_set_expert_path(self._h, code))
 
+    def set_graphs(self, max_graphs: int) -> None:
+        """Forward graphs kept for replay, 0..16; 0 launches every kernel
+        directly (gb_moe_set_graphs)."""
+        check(self._lib.gb_moe_set_graphs(self._h, int(max_graphs)))
+
     def set_profiling(self, enable: bool = True) -> None:
         check(self._lib.gb_moe_set_profiling(self._h, 1 if enable else 0))
 

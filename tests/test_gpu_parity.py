@@ -356,3 +356,76 @@ def test_tensor_cores_on_odd_shapes():
             assert_parity(got, want, f"{path}, H=320 I=192")
     finally:
         m.close()
+
+
+# ---- forward graphs ---------------------------------------------------------
+
+def test_graph_replay_equals_direct_launches(moe32, layer32):
+    # the same buffers three times: launched directly, captured, replayed; new
+    # contents of x between calls are read by the replay
+    torch = _torch()
+    for T in (1, 7, 64):
+        xs = [synth.tokens(T, 2880, seed=400 + 10 * T + i) for i in range(3)]
+        xd = torch.empty((T, 2880), device="cuda")
+        out = torch.empty_like(xd)
+        moe32.set_graphs(0)
+        direct = []
+        for x in xs:
+            xd.copy_(torch.from_numpy(x))
+            moe32.forward_raw(xd.data_ptr(), T, out.data_ptr())
+            torch.cuda.synchronize()
+            direct.append(out.cpu().numpy())
+        moe32.set_graphs(16)
+        c0 = moe32.info()["graph_captures"]
+        for i, x in enumerate(xs * 2):
+            xd.copy_(torch.from_numpy(x))
+            moe32.forward_raw(xd.data_ptr(), T, out.data_ptr())
+            moe32.device_status()
+            assert np.array_equal(out.cpu().numpy(), direct[i % 3]), f"T={T} call {i}"
+        assert moe32.info()["graph_captures"] - c0 == 1
+        want, _, _ = oracle.OracleMoe(layer32).forward(xs[2])
+        assert_parity(direct[2], want, f"graph T={T}")
+
+
+def test_graph_cache_replaces_the_least_recently_used(moe32):
+    torch = _torch()
+    moe32.set_graphs(2)
+    try:
+        xd = _cuda(synth.tokens(8, 2880, seed=77))
+        out = torch.empty_like(xd)
+        ref = {}
+        moe32.set_graphs(0)
+        for T in (2, 4, 8):
+            moe32.forward_raw(xd.data_ptr(), T, out.data_ptr())
+            torch.cuda.synchronize()
+            ref[T] = out[:T].cpu().numpy()
+        moe32.set_graphs(2)
+        c0 = moe32.info()["graph_captures"]
+        for T in (2, 2, 4, 4, 8, 8, 2, 2):
+            out.zero_()
+            moe32.forward_raw(xd.data_ptr(), T, out.data_ptr())
+            torch.cuda.synchronize()
+            assert np.array_equal(out[:T].cpu().numpy(), ref[T]), f"T={T}"
+        # 2, 4, 8 captured; 8 replaced 2, so 2 was seen again and captured again
+        assert moe32.info()["graph_captures"] - c0 == 4
+    finally:
+        moe32.set_graphs(16)
+
+
+@pytest.mark.parametrize("T", [1, 5, 127, 128, 129])
+def test_one_launch_grouping_matches_oracle(layer32_skew, T):
+    # up to 512 routing entries the grouping, tile table and activation pieces
+    # come from one launch; 129 tokens x top-4 take the separate kernels
+    m = OssMoEFFN.load(layer32_skew, device=0, max_tokens=T)
+    try:
+        x = synth.tokens(T, 2880, seed=500 + T)
+        got = m.forward(_cuda(x)).cpu().numpy()
+        want, _, _ = oracle.OracleMoe(layer32_skew).forward(x)
+        assert_parity(got, want, f"T={T}")
+        # a second forward of other tokens in the same buffers
+        x2 = synth.tokens(T, 2880, seed=600 + T)
+        got2 = m.forward(_cuda(x2)).cpu().numpy()
+        want2, _, _ = oracle.OracleMoe(layer32_skew).forward(x2)
+        assert_parity(got2, want2, f"T={T} second")
+    finally:
+        m.close()
