@@ -347,7 +347,8 @@ def measured_traffic(T, E, stage, n_gpus):
 
 
 def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
-    """Roofline of the dominant expert kernel (gate_up or down)."""
+    """Roofline of the dominant expert kernel (gate_up or down, or both when
+    one launch runs them: the library then records an empty down stage)."""
     H, I, E, k = model.H, model.I, model.E, TOPK
     rows = T * k
     gu_w, dn_w = model.stage_weight_bytes()
@@ -356,7 +357,13 @@ def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
         "down": n_touched * dn_w + rows * I * 4 + rows * H * 4,
     }
     stage_flops = {"gate_up": 2 * rows * 2 * I * H, "down": 2 * rows * H * I}
-    dom = max(("gate_up", "down"), key=lambda s: stage_ms.get(s, 0.0))
+    stage_ms = dict(stage_ms)
+    if stage_ms.get("down", 0.0) < 0.005:  # two adjacent events: no kernel between them
+        stage_ms["gate_up+down"] = stage_ms["gate_up"]
+        stage_bytes["gate_up+down"] = stage_bytes["gate_up"] + stage_bytes["down"]
+        stage_flops["gate_up+down"] = stage_flops["gate_up"] + stage_flops["down"]
+        stage_ms["gate_up"] = stage_ms["down"] = 0.0
+    dom = max(stage_ms.keys() & stage_bytes.keys(), key=lambda s: stage_ms[s])
     t = stage_ms[dom] / 1e3
     traffic = measured_traffic(T, E, dom, n_gpus) if model.name == "gptoss" else None
     if T <= 64:

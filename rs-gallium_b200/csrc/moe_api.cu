@@ -518,10 +518,17 @@ int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t 
     gb::Groups g = local_groups(m, T);
     const int kind = gb::mx_tile_kind(m, g);
     if ((rc = run_route_grouped(m, x, T, g, kind, st))) return rc;
-    GB_CUDA(gb::launch_mx_gate_up(m, g, x, m.ws.eb, kind, st), "block-scaled gate_up launch");
-    if ((rc = mark(m, 3, st))) return rc;
-    GB_CUDA(gb::launch_mx_down(m, g, m.ws.eb, kind, st), "block-scaled down launch");
-    m.launches += 2;
+    if (g.rows >= gb::kMxOneLaunchRows) {
+      // gate_up and down in one launch: the "down" stage is empty
+      GB_CUDA(gb::launch_mx_ffn(m, g, m.ws.eb, kind, st), "block-scaled expert launch");
+      m.launches += 1;
+      if ((rc = mark(m, 3, st))) return rc;
+    } else {
+      GB_CUDA(gb::launch_mx_gate_up(m, g, x, m.ws.eb, kind, st), "block-scaled gate_up launch");
+      if ((rc = mark(m, 3, st))) return rc;
+      GB_CUDA(gb::launch_mx_down(m, g, m.ws.eb, kind, st), "block-scaled down launch");
+      m.launches += 2;
+    }
     if ((rc = mark(m, 4, st))) return rc;
     GB_CUDA(gb::launch_combine(m, T, m.ws, m.ws.eb.y, out, st), "combine kernel launch");
     m.launches += 1;
@@ -730,8 +737,12 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
       {(void**)&nb.hl, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
       {(void**)&nb.xq, m.mx.ok ? mx_piece_bytes(rows, (int)H) : 0},
       {(void**)&nb.hq, m.mx.ok ? mx_piece_bytes(rows, (int)I) : 0},
-      {(void**)&nb.mx_partial, m.mx.ok ? kMxPartialBytes : 0},
-      {(void**)&nb.mx_arrivals, m.mx.ok ? sizeof(int) * (size_t)kMxSplitSlots : 0},
+      {(void**)&nb.mx_partial, m.mx.ok ? 2 * kMxPartialBytes : 0},
+      {(void**)&nb.mx_arrivals, m.mx.ok ? 2 * sizeof(int) * (size_t)kMxSplitSlots : 0},
+      {(void**)&nb.mx_ready,
+       m.mx.ok ? sizeof(int) * (size_t)(1 + std::min<int64_t>(rows, kMxGroupEntries) *
+                                               mx_ready_per_tile(m))
+               : 0},
       {(void**)&nb.tile_expert, sizeof(int32_t) * (size_t)(rows + E + 1)},
       {(void**)&nb.tile_row0, sizeof(int32_t) * (size_t)(rows + E + 1)},
       {(void**)&nb.tile_rows, sizeof(int32_t) * (size_t)(rows + E + 1)},
@@ -747,7 +758,7 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
     nb.maps_ok = true;
   }
   if (m.mx.ok) {
-    cudaError_t e = cudaMemset(nb.mx_arrivals, 0, sizeof(int) * (size_t)kMxSplitSlots);
+    cudaError_t e = cudaMemset(nb.mx_arrivals, 0, 2 * sizeof(int) * (size_t)kMxSplitSlots);
     if (e == cudaSuccess) e = mx_make_maps(m, nb);
     if (e != cudaSuccess) {
       cudaFree(nb.base);

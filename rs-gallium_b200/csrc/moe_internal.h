@@ -129,8 +129,10 @@ struct ExpertBufs {
   uint8_t* hq = nullptr;       // [rows][4][I] E4M3 pieces of the SwiGLU output
   alignas(64) unsigned char map_xq[5][128] = {};  // CUtensorMaps, tiles of 2, 4, 8, 16, 30
   alignas(64) unsigned char map_hq[5][128] = {};  // positions (index: kind)
-  float* mx_partial = nullptr;  // split-K partial sums (kMxPartialBytes)
-  int* mx_arrivals = nullptr;   // split-K tickets [kMxSplitSlots], zero between forwards
+  float* mx_partial = nullptr;  // split-K partial sums (2 x kMxPartialBytes: gate_up, down)
+  int* mx_arrivals = nullptr;   // split-K tickets [2 x kMxSplitSlots], zero between forwards
+  int* mx_ready = nullptr;      // one-launch expert kernel: [0] item counter, then
+                                //   [tile][gate_up M tile] ready flags
   bool maps_ok = false;
   bool mx_maps_ok = false;
 };
@@ -238,6 +240,11 @@ cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float*
 constexpr int kMxTileKinds = 5;  // tiles of 2, 4, 8, 16, 30 positions
 constexpr size_t kMxPartialBytes = size_t(8) << 20;  // split-K partial sums
 constexpr int kMxSplitSlots = 4096;                  // split-K tiles x splits
+constexpr int kMxGroupEntries = 512;  // routing entries of the one-launch grouping
+// Grouped forwards of at least this many positions run gate_up and down as
+// one launch; below it the two launches measured faster (the wait for h
+// chunks costs more than the second launch when each CTA has one item).
+constexpr int64_t kMxOneLaunchRows = 16;
 bool mx_supported(const Moe& m);
 cudaError_t mx_prepare_weights(Moe& m);
 void mx_release(MxWeights& x);
@@ -251,6 +258,11 @@ int mx_tile_positions(int kind);
 bool mx_group_fits(const Moe& m, int64_t T);
 cudaError_t launch_mx_group(const Moe& m, const float* x, int64_t T, Workspace& ws, int kind,
                             cudaStream_t st);
+// gate_up and down in one launch (needs g.grouped): the down copies of h wait
+// per K chunk for the gate_up tile that writes it.
+cudaError_t launch_mx_ffn(const Moe& m, const Groups& g, ExpertBufs& eb, int kind,
+                          cudaStream_t st);
+int mx_ready_per_tile(const Moe& m);  // gate_up M tiles = down K chunks
 cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               int kind, cudaStream_t st);
 cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, int kind,

@@ -69,6 +69,8 @@ constexpr int DM = 256;  // weight rows per tile
 constexpr int SF_BYTES = 512;
 constexpr int kSmemLimit = 232448;
 constexpr int kThreads = 224;  // warps 0-3 epilogue, 4 and 6 TMA, 5 MMA
+constexpr int kMaxSplit = 8;   // K splits of one tile (choose_ksplit)
+constexpr int kSchedRing = 8;  // items handed out ahead (one-launch mode)
 
 // ---- device helpers ----------------------------------------------------------
 
@@ -164,9 +166,15 @@ struct Args {
   int ksplit;
   float* partial;             // [tile * m_tiles + m_tile][ksplit][256 rows][NT]
   int* arrivals;              // [tile * m_tiles + m_tile]
+  // one-launch gate_up + down: gate_up tile (j, m) sets ready[j * ready_stride
+  // + m] once its h pieces are stored (the 128 h columns of down K chunk m)
+  int* ready;
+  int ready_stride;
+  int* next_item;             // one-launch mode: items handed out so far beyond the grid
 };
 
 struct Item {
+  int tile;         // N tile
   int le, m_tile, row0, nrows;
   int slot;         // tile * m_tiles + m_tile
   int split;        // which K range
@@ -178,6 +186,7 @@ __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   it.split = item % a.ksplit;
   it.slot = item / a.ksplit;
   const int j = it.slot / a.m_tiles;
+  it.tile = j;
   it.m_tile = it.slot - j * a.m_tiles;
   it.le = a.tile_expert[j] - a.e_begin;
   it.row0 = a.tile_row0[j];
@@ -264,10 +273,60 @@ struct Tile {
                                     (1u << 23) | ((uint32_t)(BM >> 4) << 24);
 };
 
+// Acquire load of a flag another CTA releases.
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait for a ready flag; false if the CTA is aborting or it ran out.
+__device__ __forceinline__ bool wait_ready(const int* p, volatile int* abort_flag, int* err) {
+  if (ld_acquire(p)) return true;
+  const uint64_t t0 = globaltimer();
+  while (!ld_acquire(p)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kMbarWaitNs) {
+      *abort_flag = 1;
+      atomicOr(err, 2);
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+// Orders this thread's generic-proxy view of global memory (a flag just
+// acquired, or h just stored) with its later async-proxy (TMA) copies.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// After the 128 epilogue threads stored a gate_up tile's h pieces: publish
+// ready[tile * ready_stride + m_tile] for the down copies of that K chunk.
+__device__ __forceinline__ void publish_ready(const Args& a, const Item& it, int m) {
+  __threadfence();
+  fence_proxy_async_global();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (m == 0) {
+    int* f = a.ready + (int64_t)it.tile * a.ready_stride + it.m_tile;
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
+  }
+}
+
+// MODE 0: gate_up (a0, maps w0/x0).  MODE 1: down (a1, maps w1/x1).
+// MODE 2: both in one launch: the gate_up items come first in every CTA's
+// list, then the down items.  A down stage copies its weights and scales at
+// once; its h chunk kc waits for ready[tile][kc] (the gate_up tile that
+// writes those 128 h columns), the copy parked in a small queue meanwhile so
+// that the producer keeps streaming weights.  Gate_up items wait on nothing,
+// so with every CTA resident (one grid of 2 CTAs per SM) the waits end.
 template <int MODE, int NT>
 __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
-    mx_expert_gemm(const __grid_constant__ CUtensorMap tmap_w,
-                   const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+    mx_expert_gemm(const __grid_constant__ CUtensorMap tmap_w0,
+                   const __grid_constant__ CUtensorMap tmap_x0,
+                   const __grid_constant__ CUtensorMap tmap_w1,
+                   const __grid_constant__ CUtensorMap tmap_x1, const Args a0, const Args a1) {
   using D = Tile<NT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -282,8 +341,12 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nk = a.kchunks;
   __shared__ int s_last;
+  // MODE 2 schedule: producer warp 4 takes items from a0.next_item (the
+  // first is blockIdx.x) and hands each to warp 6, the MMA warp and the
+  // epilogue through this ring; -1 ends the list
+  __shared__ int s_sched[kSchedRing];
+  __shared__ __align__(8) uint64_t s_sched_full[kSchedRing], s_sched_empty[kSchedRing];
   pdl_trigger();
 
   for (int i = threadIdx.x; i < SF_BYTES / 4; i += kThreads)
@@ -298,8 +361,20 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 128);
     }
+    for (int r = 0; r < kSchedRing; ++r) {
+      mbar_init(&s_sched_full[r], 1);
+      mbar_init(&s_sched_empty[r], 3);  // warp 6, the MMA warp, the epilogue
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 4 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w0) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x0) : "memory");
+    if (MODE != 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_w1) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tmap_x1) : "memory");
+    }
   }
   if (warp == 0) tmem_alloc(tmem_slot, D::TMEM_COLS);
   tc_fence_before();
@@ -309,7 +384,31 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   // Everything above touches only this CTA's shared memory and TMEM, so it
   // overlaps the tail of the grid before; global memory is read after the wait.
   pdl_wait();
-  const int total_items = a.meta[2] * a.m_tiles * a.ksplit;
+  const int n0 = MODE == 1 ? 0 : a0.meta[2] * a0.m_tiles * a0.ksplit;
+  const int total_items = n0 + (MODE == 0 ? 0 : a1.meta[2] * a1.m_tiles * a1.ksplit);
+  // item -> phase (0 gate_up, 1 down) and index within the phase
+  auto phase_of = [&](int item) -> int { return MODE == 2 ? (item >= n0 ? 1 : 0) : MODE; };
+  auto local_of = [&](int item) -> int { return MODE == 2 && item >= n0 ? item - n0 : item; };
+  // i-th item of this CTA, or -1.  MODE 0 / 1: items blockIdx.x + i gridDim.x.
+  // MODE 2: `publish` (warp 4) fetches and hands it out, the others read it.
+  auto static_item = [&](int i) -> int {
+    const int item = blockIdx.x + i * gridDim.x;
+    return item < total_items ? item : -1;
+  };
+  auto publish_item = [&](int i) -> int {
+    const int r = i % kSchedRing;
+    if (!mbar_wait(&s_sched_empty[r], ((i / kSchedRing) & 1) ^ 1, abort_flag, a0.err)) return -1;
+    int item = i == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(a0.next_item, 1);
+    if (item >= total_items) item = -1;
+    s_sched[r] = item;
+    mbar_arrive(&s_sched_full[r]);
+    return item;
+  };
+  auto read_item = [&](int i) -> int {
+    const int r = i % kSchedRing;
+    if (!mbar_wait(&s_sched_full[r], (i / kSchedRing) & 1, abort_flag, a0.err)) return -1;
+    return *reinterpret_cast<volatile int*>(&s_sched[r]);
+  };
 
   if (warp == 4 || warp == 6) {
     // ---------------- TMA producers: warp 4 even steps, warp 6 odd ----------
@@ -317,25 +416,90 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       const uint32_t mine = warp == 4 ? 0u : 1u;
       uint32_t g = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const Item it = decode_item(a, item);
+      // MODE 2: down stages whose h copy waits for its gate_up tile, oldest first
+      constexpr int QCAP = 8;
+      uint32_t q_g[QCAP] = {};
+      int q_kc[QCAP] = {}, q_row0[QCAP] = {}, q_flag[QCAP] = {};
+      int qh = 0, qn = 0;
+      auto issue_front = [&]() {
+        const uint32_t s = q_g[qh] % D::STAGES;
+        fence_proxy_async_global();
+        tma_load_3d(smem + s * D::STAGE + D::W_BYTES, &tmap_x1, q_kc[qh] * BK, 0, q_row0[qh],
+                    &full[s]);
+        qh = (qh + 1) % QCAP;
+        --qn;
+      };
+      // Parked h copies are issued before any wait on the schedule ring: the
+      // other producer may be waiting (through the MMA's in-order stages) for
+      // one of them, and the ring may be waiting for that producer.  Flags
+      // depend on gate_up items only, which wait on nothing.
+      auto drain = [&]() {
+        while (ok && qn > 0) {
+          if (!wait_ready(a1.ready + q_flag[qh], abort_flag, a1.err)) ok = false;
+          else issue_front();
+        }
+      };
+      for (int i = 0; ok; ++i) {
+        int item;
+        if (MODE != 2) {
+          item = static_item(i);
+        } else {
+          const int r = i % kSchedRing;
+          const uint32_t rph = (uint32_t)(i / kSchedRing) & 1u;
+          if (qn > 0 && !mbar_try_wait(warp == 4 ? &s_sched_empty[r] : &s_sched_full[r],
+                                       warp == 4 ? rph ^ 1u : rph))
+            drain();
+          if (!ok) break;
+          if (warp == 4) {
+            item = publish_item(i);
+          } else {
+            item = read_item(i);
+            mbar_arrive(&s_sched_empty[r]);
+          }
+        }
+        if (item < 0) break;
+        const int ph = phase_of(item);
+        const Args& A = ph ? a1 : a0;
+        const CUtensorMap* tw = ph ? &tmap_w1 : &tmap_w0;
+        const CUtensorMap* tx = ph ? &tmap_x1 : &tmap_x0;
+        const Item it = decode_item(A, local_of(item));
         for (int kc = it.kc0; kc < it.kc1; ++kc, ++g) {
           if ((g & 1u) != mine) continue;
-          const uint32_t s = g % D::STAGES, ph = (g / D::STAGES) & 1u;
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, a.err)) {
+          const uint32_t s = g % D::STAGES, sph = (g / D::STAGES) & 1u;
+          if (MODE == 2) {
+            // the stage that last used slot s needs its h copy before slot s frees
+            while (ok && qn > 0 && (q_g[qh] + D::STAGES <= g || qn == QCAP)) {
+              if (!wait_ready(a1.ready + q_flag[qh], abort_flag, A.err)) ok = false;
+              else issue_front();
+            }
+            if (!ok) break;
+          }
+          if (!mbar_wait(&empty[s], sph ^ 1u, abort_flag, A.err)) {
             ok = false;
             break;
           }
           uint8_t* st = smem + s * D::STAGE;
           // the weight box counts its packed bytes
           mbar_arrive_expect_tx(&full[s], D::W_BYTES / 2 + D::X_BYTES + D::SFW);
-          tma_load_3d(st, &tmap_w, 0, it.m_tile * DM, it.le * nk + kc, &full[s]);
-          tma_load_3d(st + D::W_BYTES, &tmap_x, kc * BK, 0, it.row0, &full[s]);
+          tma_load_3d(st, tw, 0, it.m_tile * DM, it.le * A.kchunks + kc, &full[s]);
           bulk_load(st + D::W_BYTES + D::X_BYTES,
-                    a.sfa + (((int64_t)it.le * nk + kc) * a.mt2 + 2 * it.m_tile) * SF_BYTES,
+                    A.sfa + (((int64_t)it.le * A.kchunks + kc) * A.mt2 + 2 * it.m_tile) * SF_BYTES,
                     D::SFW, &full[s]);
+          if (MODE == 2 && ph == 1) {
+            const int flag = it.tile * a1.ready_stride + kc;
+            const int t = (qh + qn) % QCAP;
+            q_g[t] = g;
+            q_kc[t] = kc;
+            q_row0[t] = it.row0;
+            q_flag[t] = flag;
+            ++qn;
+            while (qn > 0 && ld_acquire(a1.ready + q_flag[qh])) issue_front();
+          } else {
+            tma_load_3d(st + D::W_BYTES, tx, kc * BK, 0, it.row0, &full[s]);
+          }
         }
       }
+      if (MODE == 2) drain();
       if (!ok) linger_2ms();
     }
   } else if (warp == 5) {
@@ -346,16 +510,26 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       uint32_t g = 0;
       int acc_iter = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x, ++acc_iter) {
+      for (int i = 0; ok; ++i, ++acc_iter) {
+        int item;
+        if (MODE != 2) {
+          item = static_item(i);
+        } else {
+          item = read_item(i);
+          mbar_arrive(&s_sched_empty[i % kSchedRing]);
+        }
+        if (item < 0) break;
+        const int ph = phase_of(item);
+        const Args& A = ph ? a1 : a0;
         const int b = acc_iter % D::NACC;
         const uint32_t acc_phase = (uint32_t)(acc_iter / D::NACC) & 1u;
-        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1u, abort_flag, a.err)) break;
+        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1u, abort_flag, A.err)) break;
         tc_fence_after();
         const uint32_t dbase = tmem_base + (uint32_t)(b * D::BUF);
-        const Item it = decode_item(a, item);
+        const Item it = decode_item(A, local_of(item));
         for (int kc = it.kc0; kc < it.kc1; ++kc, ++g) {
-          const uint32_t s = g % D::STAGES, ph = (g / D::STAGES) & 1u;
-          if (!mbar_wait(&full[s], ph, abort_flag, a.err)) {
+          const uint32_t s = g % D::STAGES, sph = (g / D::STAGES) & 1u;
+          if (!mbar_wait(&full[s], sph, abort_flag, A.err)) {
             ok = false;
             break;
           }
@@ -385,47 +559,67 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
     }
   } else if (warp < 4) {
     // ---------------- epilogue: thread m owns TMEM lane m -------------------
+    // Thread 0 takes the item and waits for its accumulator, then the 128
+    // threads agree on it at a named barrier (so that a wait that gave up
+    // ends every thread's loop at the same item).
     const int m = threadIdx.x;
+    __shared__ int s_epi_item[2];
     int acc_iter = 0;
-    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++acc_iter) {
+    for (int i = 0;; ++i, ++acc_iter) {
       const int b = acc_iter % D::NACC;
       const uint32_t acc_phase = (uint32_t)(acc_iter / D::NACC) & 1u;
-      if (!mbar_wait(&acc_full[b], acc_phase, abort_flag, a.err)) break;
+      if (m == 0) {
+        int item = MODE != 2 ? static_item(i) : read_item(i);
+        if (MODE == 2 && item >= 0) mbar_arrive(&s_sched_empty[i % kSchedRing]);
+        if (item >= 0 && !mbar_wait(&acc_full[b], acc_phase, abort_flag, a0.err)) item = -1;
+        s_epi_item[i & 1] = item;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int item = *reinterpret_cast<volatile int*>(&s_epi_item[i & 1]);
+      if (item < 0) break;
+      const int ph = phase_of(item);
+      const Args& A = ph ? a1 : a0;
       tc_fence_after();
-      const Item it = decode_item(a, item);
-      const bool split = a.ksplit > 1;
-      float* part = a.partial + ((int64_t)it.slot * a.ksplit + it.split) * (DM * NT);
-      // lane n holds position n's activation scale (GATE_UP) or output row (DOWN)
+      const Item it = decode_item(A, local_of(item));
+      const bool split = A.ksplit > 1;
+      float* part = A.partial + ((int64_t)it.slot * A.ksplit + it.split) * (DM * NT);
+      // lane n holds position n's activation scale (gate_up) or output row (down)
       float lane_scale = 0.0f;
       int64_t lane_orow = 0;
       if (lane < it.nrows) {
         const int64_t pos = (int64_t)it.row0 + lane;
-        if (MODE == 0) lane_scale = pow2f((int)a.xscale[pos]);
-        else lane_orow = a.out_rows ? a.out_rows[pos] : pos;
+        if (ph == 0) lane_scale = pow2f((int)A.xscale[pos]);
+        else lane_orow = A.out_rows ? A.out_rows[pos] : pos;
       }
+      auto finish = [&](int row, bool valid, float bias, int n, float (&val)[2]) {
+        if (MODE != 1 && ph == 0)
+          finish_pair<0>(a0, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+        else if (MODE != 0)
+          finish_pair<1>(a1, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+      };
       const uint32_t base =
           tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * D::BUF);
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         const int row = it.m_tile * DM + h * BM + m;
-        const bool valid = row < a.rows;
-        const int64_t grow = (int64_t)it.le * a.rows + (valid ? row : 0);
-        const float bias = (valid && a.bias) ? a.bias[grow] : 0.0f;
+        const bool valid = row < A.rows;
+        const int64_t grow = (int64_t)it.le * A.rows + (valid ? row : 0);
+        const float bias = (valid && A.bias) ? A.bias[grow] : 0.0f;
 #pragma unroll 1
-        for (int n0 = 0; n0 < NT; n0 += 2 * D::PAIRS) {
+        for (int n0p = 0; n0p < NT; n0p += 2 * D::PAIRS) {
           // columns 4n .. 4n + 7 hold the pieces of positions n and n + 1
           uint32_t v[D::PAIRS][D::ACCS][8];
 #pragma unroll
           for (int pp = 0; pp < D::PAIRS; ++pp)
 #pragma unroll
             for (int q = 0; q < D::ACCS; ++q)
-              if (n0 + 2 * pp < NT)
-                tmem_ld8(base + (uint32_t)((h * D::ACCS + q) * D::N + kPieces * (n0 + 2 * pp)),
+              if (n0p + 2 * pp < NT)
+                tmem_ld8(base + (uint32_t)((h * D::ACCS + q) * D::N + kPieces * (n0p + 2 * pp)),
                          v[pp][q]);
           tmem_wait_ld();
 #pragma unroll
           for (int pp = 0; pp < D::PAIRS; ++pp) {
-            const int n = n0 + 2 * pp;
+            const int n = n0p + 2 * pp;
             if (n >= NT) break;
             float val[2];
 #pragma unroll
@@ -444,42 +638,58 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
             if (split) {
               *reinterpret_cast<float2*>(part + (h * BM + m) * NT + n) = make_float2(val[0], val[1]);
             } else {
-              finish_pair<MODE>(a, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+              finish(row, valid, bias, n, val);
             }
           }
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
-      if (split) {
+      if (!split) {
+        if (MODE == 2 && ph == 0) publish_ready(a0, it, m);
+      } else {
         // the last of the tile's ksplit items adds the partial sums in split
         // order and finishes the tile (no waiting: a ticket per tile)
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (m == 0) s_last = atomicAdd(&a.arrivals[it.slot], 1) == a.ksplit - 1;
+        if (m == 0) s_last = atomicAdd(&A.arrivals[it.slot], 1) == A.ksplit - 1;
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (s_last) {
           __threadfence();
-          if (m == 0) a.arrivals[it.slot] = 0;  // ready for the next forward
-          const float* p0 = a.partial + (int64_t)it.slot * a.ksplit * (DM * NT);
-#pragma unroll 1
+          if (m == 0) A.arrivals[it.slot] = 0;  // ready for the next forward
+          const float* p0 = A.partial + (int64_t)it.slot * A.ksplit * (DM * NT);
+          float bias[2];
+#pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int row = it.m_tile * DM + h * BM + m;
-            const bool valid = row < a.rows;
-            const int64_t grow = (int64_t)it.le * a.rows + (valid ? row : 0);
-            const float bias = (valid && a.bias) ? a.bias[grow] : 0.0f;
+            const int64_t grow = (int64_t)it.le * A.rows + (row < A.rows ? row : 0);
+            bias[h] = (row < A.rows && A.bias) ? A.bias[grow] : 0.0f;
+          }
 #pragma unroll 1
-            for (int n = 0; n < NT; n += 2) {
-              float val[2] = {0.0f, 0.0f};
-              for (int sp = 0; sp < a.ksplit; ++sp) {
-                const float2 pv = __ldcg(reinterpret_cast<const float2*>(
-                    p0 + (int64_t)sp * (DM * NT) + (h * BM + m) * NT + n));
-                val[0] = sp == 0 ? pv.x : __fadd_rn(val[0], pv.x);
-                val[1] = sp == 0 ? pv.y : __fadd_rn(val[1], pv.y);
-              }
-              finish_pair<MODE>(a, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+          for (int n = 0; n < NT; n += 2) {
+            // every split's partial sums of both halves in flight at once
+            float2 pv[2][kMaxSplit];
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int sp = 0; sp < kMaxSplit; ++sp)
+                if (sp < A.ksplit)
+                  pv[h][sp] = __ldcg(reinterpret_cast<const float2*>(
+                      p0 + (int64_t)sp * (DM * NT) + (h * BM + m) * NT + n));
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float val[2] = {pv[h][0].x, pv[h][0].y};
+#pragma unroll
+              for (int sp = 1; sp < kMaxSplit; ++sp)
+                if (sp < A.ksplit) {
+                  val[0] = __fadd_rn(val[0], pv[h][sp].x);
+                  val[1] = __fadd_rn(val[1], pv[h][sp].y);
+                }
+              const int row = it.m_tile * DM + h * BM + m;
+              finish(row, row < A.rows, bias[h], n, val);
             }
           }
+          if (MODE == 2 && ph == 0) publish_ready(a0, it, m);
         }
       }
     }
@@ -560,9 +770,10 @@ __global__ void __launch_bounds__(128) split_pieces_kernel(
 // offsets[e] + (entries before it with the same expert), the stable
 // (expert, token) order of permute_kernel, so perm, inv, counts, offsets,
 // active and meta[0] are the same as there.  CTA 0 writes the per-expert
-// arrays and the tile table of tile_table_kernel; CTA t writes perm and inv
-// of its entries and the pieces of x[t] at each of its positions.
-constexpr int kGroupEntries = 512;
+// arrays and the tile table of tile_table_kernel and clears the one-launch
+// expert kernel's ready flags of those tiles; CTA t writes perm and inv of
+// its entries and the pieces of x[t] at each of its positions.
+constexpr int kGroupEntries = kMxGroupEntries;
 constexpr int kGroupExperts = 256;
 
 __global__ void __launch_bounds__(128) group_pieces_kernel(
@@ -571,8 +782,10 @@ __global__ void __launch_bounds__(128) group_pieces_kernel(
     int32_t* __restrict__ offsets, int32_t* __restrict__ active, int32_t* __restrict__ meta,
     int32_t* __restrict__ perm, int32_t* __restrict__ inv, int32_t* __restrict__ tile_expert,
     int32_t* __restrict__ tile_row0, int32_t* __restrict__ tile_rows, uint8_t* __restrict__ q,
-    float* __restrict__ xscale) {
+    float* __restrict__ xscale, int* __restrict__ ready, int ready_per_tile,
+    int* __restrict__ next_item) {
   __shared__ int s_idx[kGroupEntries];
+  __shared__ int s_tiles;
   __shared__ int s_cnt[kGroupExperts], s_off[kGroupExperts];
   __shared__ int s_pos[8];
   pdl_trigger();
@@ -652,10 +865,16 @@ __global__ void __launch_bounds__(128) group_pieces_kernel(
         offsets[E] = total;
         meta[0] = arun;
         meta[2] = tiles;
+        s_tiles = tiles;
       }
     }
   }
   __syncthreads();
+  // the one-launch expert kernel's ready flags of this forward's tiles
+  if (t == 0 && ready) {
+    for (int i = tid; i < s_tiles * ready_per_tile; i += blockDim.x) ready[i] = 0;
+    if (tid == 0) *next_item = 0;
+  }
   // positions of this token's entries: warp w takes rank w, w + 4, ...
   for (int r = warp; r < topk; r += 4) {
     const int i = t * topk + r;
@@ -840,29 +1059,31 @@ int mx_tile_kind(const Moe& m, const Groups& g) {
 
 namespace {
 
+// One launch of 2 CTAs per SM (every CTA resident: the one-launch mode's
+// waits rely on it).  a0 / maps 0 are gate_up's, a1 / maps 1 down's.
 template <int MODE, int NT>
-cudaError_t launch_tiles(const Moe& m, const mx::Args& a, const void* map_w, const void* map_x,
-                         cudaStream_t st) {
+cudaError_t launch_tiles(const Moe& m, const mx::Args& a0, const mx::Args& a1,
+                         const ExpertBufs& eb, int kind, cudaStream_t st) {
   auto k = mx::mx_expert_gemm<MODE, NT>;
   const size_t smem = mx::Tile<NT>::SMEM;
   cudaError_t e = set_smem_limit(k, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(k, dim3(m.sm_count * mx::Tile<NT>::CPS), dim3(mx::kThreads), smem, st,
-                    *reinterpret_cast<const CUtensorMap*>(map_w),
-                    *reinterpret_cast<const CUtensorMap*>(map_x), a);
+                    *reinterpret_cast<const CUtensorMap*>(m.mx.map_gu),
+                    *reinterpret_cast<const CUtensorMap*>(eb.map_xq[kind]),
+                    *reinterpret_cast<const CUtensorMap*>(m.mx.map_dn),
+                    *reinterpret_cast<const CUtensorMap*>(eb.map_hq[kind]), a0, a1);
 }
 
 template <int MODE>
-cudaError_t launch_mx(const Moe& m, const mx::Args& a, const ExpertBufs& eb, int kind,
-                      cudaStream_t st) {
-  const void* w = MODE == 0 ? m.mx.map_gu : m.mx.map_dn;
-  const unsigned char(*maps)[128] = MODE == 0 ? eb.map_xq : eb.map_hq;
+cudaError_t launch_mx(const Moe& m, const mx::Args& a0, const mx::Args& a1,
+                      const ExpertBufs& eb, int kind, cudaStream_t st) {
   switch (kind) {
-    case 0: return launch_tiles<MODE, 2>(m, a, w, maps[0], st);
-    case 1: return launch_tiles<MODE, 4>(m, a, w, maps[1], st);
-    case 2: return launch_tiles<MODE, 8>(m, a, w, maps[2], st);
-    case 3: return launch_tiles<MODE, 16>(m, a, w, maps[3], st);
-    default: return launch_tiles<MODE, 30>(m, a, w, maps[4], st);
+    case 0: return launch_tiles<MODE, 2>(m, a0, a1, eb, kind, st);
+    case 1: return launch_tiles<MODE, 4>(m, a0, a1, eb, kind, st);
+    case 2: return launch_tiles<MODE, 8>(m, a0, a1, eb, kind, st);
+    case 3: return launch_tiles<MODE, 16>(m, a0, a1, eb, kind, st);
+    default: return launch_tiles<MODE, 30>(m, a0, a1, eb, kind, st);
   }
 }
 
@@ -872,7 +1093,7 @@ cudaError_t launch_mx(const Moe& m, const mx::Args& a, const ExpertBufs& eb, int
 int choose_ksplit(int64_t items, int slots, int kchunks, int nt) {
   int best = 1;
   double best_eff = 0.0;
-  for (int s = 1; s <= std::min(8, kchunks); ++s) {
+  for (int s = 1; s <= std::min(mx::kMaxSplit, kchunks); ++s) {
     if (s > 1 && (items * s > kMxSplitSlots ||
                   items * s * mx::DM * nt * (int64_t)sizeof(float) > (int64_t)kMxPartialBytes))
       break;
@@ -913,7 +1134,39 @@ void set_ksplit(const Moe& m, const Groups& g, int kind, mx::Args& a) {
   a.ksplit = choose_ksplit(tiles * a.m_tiles, m.sm_count * 2, a.kchunks, nt);
 }
 
+mx::Args gate_up_args(const Moe& m, const Groups& g, ExpertBufs& eb, int kind) {
+  const gb_moe_desc& d = m.desc;
+  mx::Args a = mx_common(m, g, eb, 2 * d.inter);
+  a.sfa = m.mx.gu_sfa;
+  a.kchunks = m.mx.kc_h;
+  a.mt2 = m.mx.mt2_gu;
+  a.bias = m.w.gu_bias;
+  a.xscale = eb.xscale;
+  a.h_exp = m.mx.h_exp;
+  a.out_q = eb.hq;
+  a.out_stride = d.inter;
+  set_ksplit(m, g, kind, a);
+  return a;
+}
+
+mx::Args down_args(const Moe& m, const Groups& g, ExpertBufs& eb, int kind) {
+  const gb_moe_desc& d = m.desc;
+  mx::Args a = mx_common(m, g, eb, d.hidden);
+  a.sfa = m.mx.dn_sfa;
+  a.kchunks = m.mx.kc_i;
+  a.mt2 = m.mx.mt2_dn;
+  a.bias = m.w.dn_bias;
+  a.in_exp = m.mx.h_exp;
+  a.out_y = eb.y;
+  a.out_rows = g.out_rows;
+  a.out_stride = d.hidden;
+  set_ksplit(m, g, kind, a);
+  return a;
+}
+
 }  // namespace
+
+int mx_ready_per_tile(const Moe& m) { return (2 * m.desc.inter + mx::DM - 1) / mx::DM; }
 
 bool mx_group_fits(const Moe& m, int64_t T) {
   const gb_moe_desc& d = m.desc;
@@ -928,7 +1181,8 @@ cudaError_t launch_mx_group(const Moe& m, const float* x, int64_t T, Workspace& 
                     (const int32_t*)ws.idx, (int)T, d.n_experts, d.top_k, d.hidden, m.e_begin,
                     m.e_end, mx_tile_positions(kind), ws.counts, ws.offsets, ws.active, ws.meta,
                     ws.perm, ws.inv, ws.eb.tile_expert, ws.eb.tile_row0, ws.eb.tile_rows,
-                    ws.eb.xq, ws.eb.xscale);
+                    ws.eb.xq, ws.eb.xscale, ws.eb.mx_ready + 1, mx_ready_per_tile(m),
+                    ws.eb.mx_ready);
 }
 
 cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
@@ -944,33 +1198,29 @@ cudaError_t launch_mx_gate_up(const Moe& m, const Groups& g, const float* x, Exp
                         g.perm_div, d.hidden, positions, eb.xq, eb.xscale)) != cudaSuccess)
       return e;
   }
-  mx::Args a = mx_common(m, g, eb, 2 * d.inter);
-  a.sfa = m.mx.gu_sfa;
-  a.kchunks = m.mx.kc_h;
-  a.mt2 = m.mx.mt2_gu;
-  a.bias = m.w.gu_bias;
-  a.xscale = eb.xscale;
-  a.h_exp = m.mx.h_exp;
-  a.out_q = eb.hq;
-  a.out_stride = d.inter;
-  set_ksplit(m, g, kind, a);
-  return launch_mx<0>(m, a, eb, kind, st);
+  const mx::Args a = gate_up_args(m, g, eb, kind);
+  return launch_mx<0>(m, a, a, eb, kind, st);
 }
 
 cudaError_t launch_mx_down(const Moe& m, const Groups& g, ExpertBufs& eb, int kind,
                            cudaStream_t st) {
-  const gb_moe_desc& d = m.desc;
-  mx::Args a = mx_common(m, g, eb, d.hidden);
-  a.sfa = m.mx.dn_sfa;
-  a.kchunks = m.mx.kc_i;
-  a.mt2 = m.mx.mt2_dn;
-  a.bias = m.w.dn_bias;
-  a.in_exp = m.mx.h_exp;
-  a.out_y = eb.y;
-  a.out_rows = g.out_rows;
-  a.out_stride = d.hidden;
-  set_ksplit(m, g, kind, a);
-  return launch_mx<1>(m, a, eb, kind, st);
+  const mx::Args a = down_args(m, g, eb, kind);
+  return launch_mx<1>(m, a, a, eb, kind, st);
+}
+
+cudaError_t launch_mx_ffn(const Moe& m, const Groups& g, ExpertBufs& eb, int kind,
+                          cudaStream_t st) {
+  if (!g.grouped || !eb.mx_ready) return cudaErrorInvalidValue;
+  mx::Args a0 = gate_up_args(m, g, eb, kind);
+  mx::Args a1 = down_args(m, g, eb, kind);
+  // down's split-K sums and tickets live in the second half of each buffer
+  a1.partial = eb.mx_partial + kMxPartialBytes / sizeof(float);
+  a1.arrivals = eb.mx_arrivals + kMxSplitSlots;
+  // mx_ready[0] counts the items handed out, the flags follow
+  a0.next_item = a1.next_item = eb.mx_ready;
+  a0.ready = a1.ready = eb.mx_ready + 1;
+  a0.ready_stride = a1.ready_stride = mx_ready_per_tile(m);
+  return launch_mx<2>(m, a0, a1, eb, kind, st);
 }
 
 }  // namespace gb
