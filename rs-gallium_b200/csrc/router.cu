@@ -370,8 +370,10 @@ cudaError_t launch(const Moe& m, const float* x, int64_t T, int32_t* idx, float*
 cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
                                cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
-  if (T <= 4) return launch<1, 1>(m, x, T, idx, wts, st);
-  if (T <= 64) return launch<4, 1>(m, x, T, idx, wts, st);
+  // measured on 128 experts x 2880: one token per CTA is fastest to 16
+  // tokens, two to 64 (more tokens per warp lengthen its dependent chains)
+  if (T <= 16) return launch<1, 1>(m, x, T, idx, wts, st);
+  if (T <= 64) return launch<2, 1>(m, x, T, idx, wts, st);
   const gb_moe_desc& d = m.desc;
   dim3 grid((unsigned)((T + kTileTokens - 1) / kTileTokens),
             (unsigned)((d.n_experts + kTileExperts - 1) / kTileExperts));
