@@ -11,11 +11,7 @@
 // interleaved into one fused matrix (row 2i = gate_i, 2i+1 = up_i) like the
 // MXFP4 path: q4_gu [E_loc][2I][H/256][144], q4_dn [E_loc][H][I/256][144].
 //
-// Kernel: one CTA per (active expert, 16 row pairs); a warp owns row pairs,
-// lane l takes sub-blocks l, l+32, ... of a row.  For each sub-block the lane
-// loads the super-block header (16 bytes) and its 32 quant bytes, and adds
-// d1 * sum(x q) - m1 * sum(x) to the row sum (sum(x) per 32-element block is
-// computed once per staged token); a butterfly folds the lanes.
+// Kernel: q4k_rows_kernel below.
 #include <algorithm>
 
 #include "common.cuh"
@@ -24,11 +20,8 @@
 namespace gb {
 namespace {
 
-constexpr int kQWarps = 4;
-constexpr int kQPairs = 4;
-constexpr int kQRowsPerCta = kQWarps * 2 * kQPairs;
-constexpr int kQPitch = 36;  // floats per staged 32-element block (+4 pad)
-constexpr int kQTok = 4;
+constexpr int kQWarps = 8;
+constexpr int kQPitch = 68;  // floats per staged 64-element task (+4: lanes 0-7 on distinct banks)
 
 enum Mode { GATE_UP = 0, DOWN = 1 };
 
@@ -66,15 +59,28 @@ __device__ __forceinline__ float half_bits_to_f32(uint16_t h) {
   return __half2float(*reinterpret_cast<const __half*>(&h));
 }
 
-template <int MODE>
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
+  return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// One CTA per (active expert, 16 PAIRS rows); warp w owns PAIRS row pairs.
+// Lane c takes the 64-element tasks c, c + 32, ... of a row: the sub-block
+// pair (2j, 2j+1) of a super-block, whose 32 quant bytes hold sub-block 2j
+// in the low nibbles and 2j+1 in the high ones, so each quant byte is loaded
+// once.  TT tokens are staged in shared memory with their 32-element sums;
+// a task adds d1 * sum(x q) - m1 * sum(x) per sub-block for the two rows of
+// a pair and every staged token, each nibble converted once for all tokens;
+// a butterfly folds the lanes.
+template <int MODE, int TT, int PAIRS>
 __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
   extern __shared__ float qsm[];
   const int K = a.K;
-  const int NB = K >> 5;        // 32-element sub-blocks per row
-  const int nsb = K >> 8;       // super-blocks per row
-  const int xstride = NB * kQPitch;
-  float* xs = qsm;                      // [kQTok][NB][kQPitch]
-  float* xsum = xs + kQTok * xstride;   // [kQTok][NB]
+  const int NP = K >> 6;  // 64-element tasks per row
+  const int NB = K >> 5;  // 32-element sub-blocks per row
+  const int nsb = K >> 8;
+  const int xstride = NP * kQPitch;
+  float* xs = qsm;                   // [TT][NP][kQPitch]
+  float* xsum = xs + TT * xstride;   // [TT][NB]
 
   const int slot = blockIdx.y;
   if (slot >= a.meta[0]) return;
@@ -83,84 +89,120 @@ __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
   const int n = a.counts[e];
   const int p0 = a.offsets[e];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row0 = blockIdx.x * kQRowsPerCta + warp * 2 * kQPairs;
-  const int npairs = max(0, min(kQPairs, (a.rows - row0) >> 1));
-  const int64_t erow = (int64_t)le * a.rows;
+  const int wrow0 = blockIdx.x * (kQWarps * 2 * PAIRS) + warp * 2 * PAIRS;
   const int64_t row_bytes = (int64_t)nsb * 144;
+  const uint8_t* ebase = a.q + (int64_t)le * a.rows * row_bytes;
 
-  for (int c0 = 0; c0 < n; c0 += kQTok) {
-    const int nc = min(kQTok, n - c0);
+  for (int c0 = 0; c0 < n; c0 += TT) {
+    const int nc = min(TT, n - c0);
     __syncthreads();
-    for (int j = 0; j < nc; ++j) {
-      const float* src = MODE == GATE_UP
-                             ? a.in + (int64_t)(a.perm[p0 + c0 + j] / a.top_k) * K
-                             : a.in + (int64_t)(p0 + c0 + j) * K;
-      for (int k4 = threadIdx.x; k4 < (K >> 2); k4 += blockDim.x) {
-        const int k = k4 << 2;
-        *reinterpret_cast<float4*>(xs + j * xstride + (k >> 5) * kQPitch + (k & 31)) =
-            reinterpret_cast<const float4*>(src)[k4];
+    // Every (token, float4) is independent, so all the row loads are in
+    // flight; eight consecutive threads hold one 32-element sub-block and
+    // fold its sum with three shuffles (the trip count is a multiple of the
+    // block so that whole warps shuffle).
+    const int per = K >> 2;
+    const int span = (TT * per + blockDim.x - 1) / blockDim.x * blockDim.x;
+#pragma unroll 2
+    for (int i = threadIdx.x; i < span; i += blockDim.x) {
+      const int j = i / per, k4 = i - j * per, k = k4 << 2;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < nc) {
+        const int64_t src = MODE == GATE_UP ? a.perm[p0 + c0 + j] / a.top_k : p0 + c0 + j;
+        v = reinterpret_cast<const float4*>(a.in + src * K)[k4];
+      }
+      float sum = __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w));
+#pragma unroll
+      for (int o = 4; o >= 1; o >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(kFullMask, sum, o));
+      if (j < TT) {
+        *reinterpret_cast<float4*>(xs + j * xstride + (k >> 6) * kQPitch + (k & 63)) = v;
+        if ((k4 & 7) == 0) xsum[j * NB + (k >> 5)] = sum;
       }
     }
     __syncthreads();
-    for (int jb = warp; jb < nc * NB; jb += kQWarps) {
-      const int j = jb / NB, b = jb - j * NB;
-      float v = xs[j * xstride + b * kQPitch + lane];
-      v = warp_sum_butterfly(v);
-      if (lane == 0) xsum[j * NB + b] = v;
-    }
-    __syncthreads();
 
-    for (int p = 0; p < npairs; ++p) {
-      float acc[2][kQTok];
+    for (int p = 0; p < PAIRS; ++p) {
+      const int row = wrow0 + 2 * p;
+      if (row >= a.rows) break;
+      float acc[2][TT];
 #pragma unroll
       for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int t = 0; t < kQTok; ++t) acc[r][t] = 0.0f;
+        for (int t = 0; t < TT; ++t) acc[r][t] = 0.0f;
+      for (int c = lane; c < NP; c += 32) {
+        const int sb = c >> 2, jj = 2 * (c & 3);
+        uint4 hdr[2], qa[2], qb[2];
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const uint8_t* rowp = a.q + (erow + row0 + 2 * p + r) * row_bytes;
-        for (int sbk = lane; sbk < NB; sbk += 32) {
-          const int sb = sbk >> 3, jj = sbk & 7;
-          const uint8_t* blk = rowp + sb * 144;
-          const uint4 hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-          const uint4 qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (jj >> 1)));
-          const uint4 qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (jj >> 1)));
-          const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
+        for (int r = 0; r < 2; ++r) {
+          const uint8_t* blk = ebase + (int64_t)(row + r) * row_bytes + sb * 144;
+          hdr[r] = __ldg(reinterpret_cast<const uint4*>(blk));
+          qa[r] = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * jj));
+          qb[r] = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 16 * jj));
+        }
+        float d1[2][2], m1[2][2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr[r]);
           const float d = half_bits_to_f32((uint16_t)(hb[0] | (hb[1] << 8)));
           const float dmin = half_bits_to_f32((uint16_t)(hb[2] | (hb[3] << 8)));
-          int sc, mn;
-          q4k_scale_min(jj, hb + 4, sc, mn);
-          const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
-          const int shift = (jj & 1) ? 4 : 0;
-          const uint32_t w[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-          float qv[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
+          for (int h = 0; h < 2; ++h) {
+            int sc, mn;
+            q4k_scale_min(jj + h, hb + 4, sc, mn);
+            d1[r][h] = __fmul_rn(d, (float)sc);
+            m1[r][h] = __fmul_rn(dmin, (float)mn);
+          }
+        }
+        // s[r][h][t]: sum over the sub-block (h = 0 low nibbles, 1 high) of x q
+        float s[2][2][TT];
 #pragma unroll
-            for (int bb = 0; bb < 4; ++bb) qv[i * 4 + bb] = (float)((w[i] >> (8 * bb + shift)) & 0xF);
+        for (int r = 0; r < 2; ++r)
 #pragma unroll
-          for (int t = 0; t < kQTok; ++t) {
-            if (t < nc) {
-              const float4* x4 = reinterpret_cast<const float4*>(xs + t * xstride + sbk * kQPitch);
-              float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f, f3 = 0.0f;
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int q4 = 0; q4 < 8; ++q4) {
-                const float4 xv = x4[q4];
-                f0 = __fmaf_rn(xv.x, qv[4 * q4], f0);
-                f1 = __fmaf_rn(xv.y, qv[4 * q4 + 1], f1);
-                f2 = __fmaf_rn(xv.z, qv[4 * q4 + 2], f2);
-                f3 = __fmaf_rn(xv.w, qv[4 * q4 + 3], f3);
-              }
-              const float sxq = __fadd_rn(__fadd_rn(f0, f1), __fadd_rn(f2, f3));
-              const float part = __fsub_rn(__fmul_rn(d1, sxq), __fmul_rn(m1, xsum[t * NB + sbk]));
-              acc[r][t] = __fadd_rn(acc[r][t], part);
+            for (int t = 0; t < TT; ++t) s[r][h][t] = 0.0f;
+        const float* xp = xs + c * kQPitch;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          float qv[2][2][4];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t word = w < 4 ? word_of(qa[r], w) : word_of(qb[r], w - 4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              qv[r][0][i] = (float)((word >> (8 * i)) & 0xF);
+              qv[r][1][i] = (float)((word >> (8 * i + 4)) & 0xF);
+            }
+          }
+#pragma unroll
+          for (int t = 0; t < TT; ++t) {
+            const float4 xl = *reinterpret_cast<const float4*>(xp + t * xstride + 4 * w);
+            const float4 xh = *reinterpret_cast<const float4*>(xp + t * xstride + 32 + 4 * w);
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              s[r][0][t] = __fmaf_rn(xl.x, qv[r][0][0], s[r][0][t]);
+              s[r][0][t] = __fmaf_rn(xl.y, qv[r][0][1], s[r][0][t]);
+              s[r][0][t] = __fmaf_rn(xl.z, qv[r][0][2], s[r][0][t]);
+              s[r][0][t] = __fmaf_rn(xl.w, qv[r][0][3], s[r][0][t]);
+              s[r][1][t] = __fmaf_rn(xh.x, qv[r][1][0], s[r][1][t]);
+              s[r][1][t] = __fmaf_rn(xh.y, qv[r][1][1], s[r][1][t]);
+              s[r][1][t] = __fmaf_rn(xh.z, qv[r][1][2], s[r][1][t]);
+              s[r][1][t] = __fmaf_rn(xh.w, qv[r][1][3], s[r][1][t]);
             }
           }
         }
-      }
-      const int row = row0 + 2 * p;
 #pragma unroll
-      for (int t = 0; t < kQTok; ++t) {
+        for (int t = 0; t < TT; ++t) {
+          const float xa = xsum[t * NB + 2 * c], xb = xsum[t * NB + 2 * c + 1];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const float pa = __fsub_rn(__fmul_rn(d1[r][0], s[r][0][t]), __fmul_rn(m1[r][0], xa));
+            const float pb = __fsub_rn(__fmul_rn(d1[r][1], s[r][1][t]), __fmul_rn(m1[r][1], xb));
+            acc[r][t] = __fadd_rn(acc[r][t], __fadd_rn(pa, pb));
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
         if (t >= nc) break;
         const float s0 = warp_sum_butterfly(acc[0][t]);
         const float s1 = warp_sum_butterfly(acc[1][t]);
@@ -180,17 +222,31 @@ __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
   }
 }
 
-template <int MODE>
-cudaError_t launch_q(const Groups& g, const QArgs& a, cudaStream_t st) {
-  if (g.max_active <= 0) return cudaSuccess;
-  dim3 grid((unsigned)((a.rows + kQRowsPerCta - 1) / kQRowsPerCta), (unsigned)g.max_active);
-  const int NB = a.K / 32;
-  const size_t smem = (size_t)kQTok * NB * kQPitch * sizeof(float) + (size_t)kQTok * NB * sizeof(float);
-  auto kern = q4k_rows_kernel<MODE>;
+template <int MODE, int TT, int PAIRS>
+cudaError_t launch_q_shape(const Groups& g, const QArgs& a, cudaStream_t st) {
+  constexpr int rows_cta = kQWarps * 2 * PAIRS;
+  dim3 grid((unsigned)((a.rows + rows_cta - 1) / rows_cta), (unsigned)g.max_active);
+  const size_t smem = (size_t)TT * (a.K / 64) * kQPitch * sizeof(float) +
+                      (size_t)TT * (a.K / 32) * sizeof(float);
+  auto kern = q4k_rows_kernel<MODE, TT, PAIRS>;
   cudaError_t err = set_smem_limit(kern, smem);
   if (err != cudaSuccess) return err;
   kern<<<grid, kQWarps * 32, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+// Tokens staged per pass from the mean rows per local expert (an expert with
+// more rows takes several passes over its weights, from L2); each warp owns
+// four row pairs, so that a staged token serves 64 rows.
+template <int MODE>
+cudaError_t launch_q(const Moe& m, const Groups& g, const QArgs& a, cudaStream_t st) {
+  if (g.max_active <= 0) return cudaSuccess;
+  const int64_t nloc = std::max(1, m.e_end - m.e_begin);
+  const int64_t mean = (g.rows + nloc - 1) / nloc;
+  if (mean <= 1) return launch_q_shape<MODE, 1, 4>(g, a, st);
+  if (mean <= 2) return launch_q_shape<MODE, 2, 4>(g, a, st);
+  if (mean <= 4) return launch_q_shape<MODE, 4, 4>(g, a, st);
+  return launch_q_shape<MODE, 8, 4>(g, a, st);
 }
 
 QArgs q_args(const Moe& m, const Groups& g) {
@@ -241,7 +297,7 @@ cudaError_t launch_q4k_gate_up(const Moe& m, const Groups& g, const float* x, Ex
   a.q = m.w.q4_gu;
   a.out = eb.h;
   a.out_stride = m.desc.inter;
-  return launch_q<GATE_UP>(g, a, st);
+  return launch_q<GATE_UP>(m, g, a, st);
 }
 
 cudaError_t launch_q4k_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
@@ -253,7 +309,7 @@ cudaError_t launch_q4k_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaS
   a.out_rows = g.out_rows;
   a.out = eb.y;
   a.out_stride = m.desc.hidden;
-  return launch_q<DOWN>(g, a, st);
+  return launch_q<DOWN>(m, g, a, st);
 }
 
 cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float* out,
