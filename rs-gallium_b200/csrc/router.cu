@@ -371,9 +371,10 @@ cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t*
                                cudaStream_t st) {
   if (T <= 0) return cudaSuccess;
   // measured on 128 experts x 2880: one token per CTA is fastest to 16
-  // tokens, two to 64 (more tokens per warp lengthen its dependent chains)
+  // tokens, two to 64 (more tokens per warp lengthen its dependent chains);
+  // the tiled kernel needs more than a few hundred tokens to fill the GPU
   if (T <= 16) return launch<1, 1>(m, x, T, idx, wts, st);
-  if (T <= 64) return launch<2, 1>(m, x, T, idx, wts, st);
+  if (T <= 256) return launch<2, 1>(m, x, T, idx, wts, st);
   const gb_moe_desc& d = m.desc;
   dim3 grid((unsigned)((T + kTileTokens - 1) / kTileTokens),
             (unsigned)((d.n_experts + kTileExperts - 1) / kTileExperts));
