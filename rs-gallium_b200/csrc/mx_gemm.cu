@@ -505,9 +505,15 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   } else if (warp == 5) {
     // ---------------- MMA issuer ---------------------------------------------
     if (lane == 0) {
+      // The issue loop is kept short (one thread issues for the whole tile):
+      // stage index and phase advance incrementally, shared-memory
+      // descriptors are a constant OR the address (+2 per 32 K bytes).
       const uint32_t sfb = tmem_base + (uint32_t)D::SFB_COL;
+      const uint32_t sfa = tmem_base + (uint32_t)D::SFA_COL;
       tmem_cp_sf(sfb, rows16_desc(smem_u32(sfb_const)));
-      uint32_t g = 0;
+      const uint64_t dconst = sw128_desc(0), rconst = rows16_desc(0);
+      const uint32_t smem0 = smem_u32(smem);
+      uint32_t s = 0, sph = 0, sw = smem0;
       int acc_iter = 0;
       bool ok = true;
       for (int i = 0; ok; ++i, ++acc_iter) {
@@ -527,31 +533,36 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
         tc_fence_after();
         const uint32_t dbase = tmem_base + (uint32_t)(b * D::BUF);
         const Item it = decode_item(A, local_of(item));
-        for (int kc = it.kc0; kc < it.kc1; ++kc, ++g) {
-          const uint32_t s = g % D::STAGES, sph = (g / D::STAGES) & 1u;
+        for (int kc = it.kc0; kc < it.kc1; ++kc) {
           if (!mbar_wait(&full[s], sph, abort_flag, A.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sw = smem_u32(smem + s * D::STAGE);
-          const uint32_t sx = sw + D::W_BYTES;
-          const uint32_t sf = sx + D::X_BYTES;
-          const uint32_t sfa = tmem_base + (uint32_t)D::SFA_COL;
-          tmem_cp_sf(sfa, rows16_desc(sf));
-          tmem_cp_sf(sfa + 4, rows16_desc(sf + SF_BYTES));
+          const uint64_t da = dconst | (sw >> 4);                           // weights
+          const uint64_t db = dconst | ((sw + D::W_BYTES) >> 4);            // pieces
+          const uint64_t dsf = rconst | ((sw + D::W_BYTES + D::X_BYTES) >> 4);
+          tmem_cp_sf(sfa, dsf);
+          tmem_cp_sf(sfa + 4, dsf + (SF_BYTES >> 4));
+          const bool first = kc == it.kc0;
 #pragma unroll
           for (int j = 0; j < BK / 32; ++j) {
-            const uint64_t bdesc = sw128_desc(sx + 32 * j);
             const uint32_t acc = (uint32_t)(j % D::ACCS);
-            const uint32_t on = (kc != it.kc0 || j >= D::ACCS) ? 1u : 0u;
+            const uint32_t on = (!first || j >= D::ACCS) ? 1u : 0u;
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               mma_mx(dbase + (uint32_t)((h * D::ACCS + acc) * D::N),
-                     sw128_desc(sw + h * (BM * BK) + 32 * j), bdesc,
+                     da + (uint64_t)((h * BM * BK) >> 4) + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
                      D::IDESC | ((uint32_t)j << 29), (sfa + 4 * h) | ((uint32_t)j << 30), sfb, on);
           }
           mma_commit(&empty[s]);
+          if (++s == (uint32_t)D::STAGES) {
+            s = 0;
+            sph ^= 1u;
+            sw = smem0;
+          } else {
+            sw += (uint32_t)D::STAGE;
+          }
         }
         if (ok) mma_commit(&acc_full[b]);
       }
