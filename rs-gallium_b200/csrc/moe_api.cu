@@ -268,6 +268,7 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.dn_rowmax);
   cudaFree(m.w.q4_gu);
   cudaFree(m.w.q4_dn);
+  cudaFree(m.w.q4_gu_exp);
   gb::mx_release(m.mx);
   free_ws(m.ws);
   gb::ep_destroy(m);
@@ -638,6 +639,17 @@ int forward_dispatch(gb::Moe& m, const float* x, int64_t T, float* out, cudaStre
 
 namespace gb {
 
+// Q4_K experts: the tensor-core kernel for groups averaging more than 32 rows
+// per local expert (or when the tensor cores are forced); the CUDA-core
+// kernel streams decode-sized groups faster.
+bool use_q4k_tc(const Moe& m, const Groups& g, const ExpertBufs& eb) {
+  if (!q4k_tc_supported(m) || !eb.maps_ok || m.expert_path == GB_PATH_CUDA_CORES) return false;
+  if (m.expert_path == GB_PATH_TENSOR_CORES || m.expert_path == GB_PATH_TENSOR_CORES_F16)
+    return true;
+  const int64_t nloc = std::max(1, m.e_end - m.e_begin);
+  return g.rows > 32 * nloc;
+}
+
 cudaError_t set_smem_limit_fn(const void* kern, size_t bytes) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -656,7 +668,12 @@ int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& 
                 cudaStream_t st) {
   int rc;
   (void)T;
-  if (m.desc.weight_format == GB_FMT_Q4_K) {
+  if (m.desc.weight_format == GB_FMT_Q4_K && use_q4k_tc(m, g, eb)) {
+    GB_CUDA(launch_q4k_tc_gate_up(m, g, x, eb, st), "Q4_K tensor-core gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(launch_q4k_tc_down(m, g, eb, st), "Q4_K tensor-core down launch");
+    m.launches += 4;  // tile table, split, two GEMMs
+  } else if (m.desc.weight_format == GB_FMT_Q4_K) {
     GB_CUDA(launch_q4k_gate_up(m, g, x, eb, st), "Q4_K gate_up launch");
     if ((rc = mark(m, 3, st))) return rc;
     GB_CUDA(launch_q4k_down(m, g, eb, st), "Q4_K down launch");
@@ -724,7 +741,7 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
   const gb_moe_desc& d = m.desc;
   const int64_t E = d.n_experts, H = d.hidden, I = d.inter;
   rows = std::max<int64_t>(rows, 1);
-  const bool tc = tc_supported(m);
+  const bool tc = tc_supported(m) || q4k_tc_supported(m);
   ExpertBufs nb;
   nb.rows_cap = rows;
   Piece pieces[] = {
@@ -816,6 +833,10 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
       desc->inter % 64 == 0 && desc->hidden <= 3072 && desc->inter <= 3072) {
     ce = gb::tc_prepare_weights(m);
     if (ce != cudaSuccess) rc = cuda_err(ce, "row exponents for the tensor-core path");
+  }
+  if (!rc && desc->weight_format == GB_FMT_Q4_K) {
+    ce = gb::q4k_tc_prepare(m);
+    if (ce != cudaSuccess) rc = cuda_err(ce, "decode exponents for the tensor-core Q4_K path");
   }
   if (!rc && gb::mx_supported(m)) {
     ce = gb::mx_prepare_weights(m);
@@ -1051,7 +1072,8 @@ int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
   if (rc) return rc;
   if (path < GB_PATH_AUTO || path > GB_PATH_TENSOR_CORES_F16)
     return set_err(GB_ERR_INVALID_ARG, "unknown expert path %d", path);
-  if (path >= GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m) && !h->m.mx.ok)
+  if (path >= GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m) && !h->m.mx.ok &&
+      !gb::q4k_tc_supported(h->m))
     return set_err(GB_ERR_UNSUPPORTED,
                    "tensor-core expert path needs the GPT-OSS activation and H, I multiples of 64");
   DeviceScope ds(h->m.device);

@@ -68,6 +68,9 @@ struct ExpertWeights {
   // q4_gu [E_loc][2I][H/256][144], q4_dn [E_loc][H][I/256][144]
   uint8_t* q4_gu = nullptr;
   uint8_t* q4_dn = nullptr;
+  // tensor-core Q4_K path: per local expert, weights decode as w * 2^exp
+  int32_t* q4_gu_exp = nullptr;  // [E_loc] (one allocation with q4_dn_exp)
+  int32_t* q4_dn_exp = nullptr;  // [E_loc]
 };
 
 // Weights in the block-scaled tensor-core layout (mx_gemm.cu), built from
@@ -228,6 +231,18 @@ bool decode_supported(const Moe& m);
 cudaError_t launch_decode_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                   cudaStream_t st);
 cudaError_t launch_decode_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+
+// Q4_K expert kernels on the tensor cores (q4k_tc.cu): kind::f16 with the
+// weights split into f16 hi + lo while they are decoded.
+bool q4k_tc_supported(const Moe& m);
+cudaError_t q4k_tc_prepare(Moe& m);
+cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                                  cudaStream_t st);
+cudaError_t launch_q4k_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+// Activation rows (through perm) -> f16 hi / lo with a per-row power of two
+// (tc_gemm.cu), the B operand of the kind::f16 kernels.
+cudaError_t launch_split_gather(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                                cudaStream_t st);
 
 // Q4_K expert kernels (q4k_gemv.cu).
 cudaError_t launch_q4k_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,

@@ -1,0 +1,499 @@
+// q4k_tc.cu -- grouped Q4_K expert GEMMs on the tensor cores (LFM2.5 batches
+// of more than 32 rows per expert).
+//
+// Reference math: lfm2moe_q.rs:279-296 (h = silu(x Wg^T) * (x Wu^T), y =
+// h Wd^T, no biases) over candle's Q4_K dequantiser (quantized.rs:162-177):
+// element j of sub-block s of a 144-byte super-block is w = d1 * q - m1 with
+// d1 = d * sc_s and m1 = dmin * m_s, each product rounded to f32.
+//
+// Precision.  w carries up to 21 significant bits, so it goes onto the tensor
+// cores as two f16 values: w' = w * 2^e (e per expert, so that |w'| <= 2^14),
+// hi = f16(w'), lo = f16(w' - hi).  Activations are split the same way as on
+// the MXFP4 kind::f16 path (x' = x * 2^-s, hi + lo).  Three kind::f16 MMAs per
+// K step: A_hi * B_hi into one TMEM accumulator, A_hi * B_lo and A_lo * B_hi
+// into a second (the small terms keep their own rounding); the epilogue adds
+// them and applies 2^-e and 2^s.
+//
+// Tiles and roles follow tc_gemm.cu: D[m, n] = sum_k W[m, k] X[n, k] with
+// M = 128 weight rows, N = 128 grouped positions of one expert, K stepped by
+// 64 (one Q4_K sub-block pair).  Warps 4-7 decode: thread r loads row r's
+// super-block header and 32 quant bytes straight from HBM (the next stage's
+// bytes are in flight while it decodes) and writes A hi / lo into shared
+// memory in the K-major 128-byte-swizzled layout; warp 8 copies B hi / lo by
+// TMA; warp 9 issues the MMAs; warps 0-3 run the epilogue (bias-free SiLU or
+// clamped SwiGLU into h hi / lo, or y).  Three 64 KB stages; two TMEM
+// accumulator pairs so the epilogue of one tile overlaps the next tile's MMAs.
+// Every mbarrier wait is bounded (timeout -> abort flag, error bit 2, TMEM
+// freed, return).
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+#include "moe_internal.h"
+#include "ptx.cuh"
+#include "umma.cuh"
+
+namespace gb {
+namespace q4tc {
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // A hi, A lo, B hi, B lo
+constexpr int kThreads = 320;
+constexpr int kTmemCols = 4 * BN;  // two buffers x (hi, lo) accumulators
+constexpr size_t kSmemBytes = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
+
+enum Mode { GATE_UP = 0, DOWN = 1 };
+
+struct Args {
+  const uint8_t* q;       // [E_loc][rows][K/256][144]
+  const int32_t* wexp;    // [E_loc] decode scale exponent e
+  int K;
+  int rows;               // 2I (gate/up interleaved) or H
+  int m_tiles;
+  int e_begin;
+  const int32_t* meta;    // [2] = number of N tiles
+  const int32_t* tile_expert;
+  const int32_t* tile_row0;
+  const int32_t* tile_rows;
+  const float* xscale;    // GATE_UP: exponent s of each position's row
+  int act_kind;
+  float limit;
+  __half* out_hi;         // GATE_UP: h hi [positions][I]
+  __half* out_lo;
+  float* out_y;           // DOWN: y [rows][H], row = out_rows[position] (or position)
+  const int32_t* out_rows;
+  int out_stride;
+  int* err;
+};
+
+// kind::f16, A = B = f16, D = f32, K-major, N = BN, M = BM.
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* s, int& sc, int& m) {
+  if (j < 4) {
+    sc = s[j] & 63;
+    m = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+    m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
+  const uint16_t b = (uint16_t)h;
+  return __half2float(*reinterpret_cast<const __half*>(&b));
+}
+
+struct Item {
+  int le, m_tile, row0, nrows;
+};
+
+__device__ __forceinline__ Item decode_item(const Args& a, int item) {
+  Item it;
+  const int j = item / a.m_tiles;
+  it.m_tile = item - j * a.m_tiles;
+  it.le = a.tile_expert[j] - a.e_begin;
+  it.row0 = a.tile_row0[j];
+  it.nrows = a.tile_rows[j];
+  return it;
+}
+
+// The 64 values of one sub-block pair (low nibbles: sub-block 2c, high: 2c+1)
+// times 2^e, as f16 hi / lo pairs packed two per word in element order.
+__device__ __forceinline__ void decode_pair(const uint4& hdr, const uint4& qa, const uint4& qb,
+                                            int c, float scale, uint32_t (&hi)[32],
+                                            uint32_t (&lo)[32]) {
+  const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
+  const float d = f16_bits_to_f32((uint32_t)hb[0] | ((uint32_t)hb[1] << 8));
+  const float dmin = f16_bits_to_f32((uint32_t)hb[2] | ((uint32_t)hb[3] << 8));
+  float d1[2], m1[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    int sc, mn;
+    q4k_scale_min(2 * c + h, hb + 4, sc, mn);
+    d1[h] = __fmul_rn(d, (float)sc);
+    m1[h] = __fmul_rn(dmin, (float)mn);
+  }
+  const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {  // elements 32h + 2i, 32h + 2i + 1
+      float v[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int byte = 2 * i + u;
+        const uint32_t qv = (words[byte >> 2] >> (8 * (byte & 3) + 4 * h)) & 0xFu;
+        v[u] = __fmul_rn(__fsub_rn(__fmul_rn(d1[h], (float)qv), m1[h]), scale);
+      }
+      const __half2 vh = __floats2half2_rn(v[0], v[1]);
+      const float2 back = __half22float2(vh);
+      const __half2 vl = __floats2half2_rn(__fsub_rn(v[0], back.x), __fsub_rn(v[1], back.y));
+      hi[16 * h + i] = *reinterpret_cast<const uint32_t*>(&vh);
+      lo[16 * h + i] = *reinterpret_cast<const uint32_t*>(&vl);
+    }
+  }
+}
+
+template <int MODE>
+__device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uint32_t hi_addr,
+                                              uint32_t lo_addr, int m) {
+  const int row = it.m_tile * BM + m;
+  const bool valid = row < a.rows;
+  const float row_f = pow2f(-a.wexp[it.le]);
+#pragma unroll 1
+  for (int c0 = 0; c0 < BN; c0 += 16) {
+    uint32_t vh[16], vl[16];
+    tmem_ld16(hi_addr + (uint32_t)c0, vh);
+    tmem_ld16(lo_addr + (uint32_t)c0, vl);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int n = c0 + j;
+      const int64_t pos = (int64_t)it.row0 + n;
+      float val = __fmul_rn(__fadd_rn(__uint_as_float(vh[j]), __uint_as_float(vl[j])), row_f);
+      if (MODE == GATE_UP) {
+        if (n < it.nrows) val = __fmul_rn(val, pow2f((int)a.xscale[pos]));
+        // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
+        const float up = __shfl_down_sync(kFullMask, val, 1);
+        if ((m & 1) == 0 && valid && n < it.nrows) {
+          const float h = a.act_kind == GB_ACT_GPTOSS_CLAMP ? act_gptoss(val, up, a.limit)
+                                                            : act_silu(val, up);
+          const __half hi = __float2half_rn(h);
+          const __half lo = __float2half_rn(__fsub_rn(h, __half2float(hi)));
+          const int64_t o = pos * a.out_stride + (row >> 1);
+          a.out_hi[o] = hi;
+          a.out_lo[o] = lo;
+        }
+      } else if (valid && n < it.nrows) {
+        const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
+        a.out_y[orow * a.out_stride + row] = val;
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    q4k_tc_gemm(const __grid_constant__ CUtensorMap tmap_hi,
+                const __grid_constant__ CUtensorMap tmap_lo, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* tma_full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* a_full = tma_full + STAGES;
+  uint64_t* empty = a_full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_items = a.meta[2] * a.m_tiles;
+  const int nk = a.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&tma_full[s], 1);
+      mbar_init(&a_full[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 8) {
+    // ---------------- TMA producer: activation hi / lo -----------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+        const Item it = decode_item(a, item);
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + stage * STAGE_BYTES + 2 * A_BYTES;
+          mbar_arrive_expect_tx(&tma_full[stage], 2 * B_BYTES);
+          tma_load_2d(sb, &tmap_hi, kc * BK, it.row0, &tma_full[stage]);
+          tma_load_2d(sb + B_BYTES, &tmap_lo, kc * BK, it.row0, &tma_full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer ---------------------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc_iter = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x, ++acc_iter) {
+        const int b = acc_iter & 1;
+        const uint32_t acc_phase = (acc_iter >> 1) & 1;
+        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1, abort_flag, a.err)) break;
+        tc_fence_after();
+        const uint32_t d_hi = tmem_base + (uint32_t)(b * 2 * BN);
+        const uint32_t d_lo = d_hi + (uint32_t)BN;
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&a_full[stage], phase, abort_flag, a.err) ||
+              !mbar_wait(&tma_full[stage], phase, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sah = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sal = sah + A_BYTES;
+          const uint32_t sbh = sal + A_BYTES;
+          const uint32_t sbl = sbh + B_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t dah = sw128_desc(sah + kk * 32), dal = sw128_desc(sal + kk * 32);
+            const uint64_t dbh = sw128_desc(sbh + kk * 32), dbl = sw128_desc(sbl + kk * 32);
+            const uint32_t acc = (kc | kk) != 0;
+            mma_f16(d_hi, dah, dbh, acc);
+            mma_f16(d_lo, dah, dbl, acc);
+            mma_f16(d_lo, dal, dbh, 1u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) mma_commit(&acc_full[b]);
+      }
+      if (!ok || *abort_flag) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- weight decode: thread r owns row r of the M tile -------
+    const int r = threadIdx.x - 128;
+    const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      const Item it = decode_item(a, item);
+      const int row = it.m_tile * BM + r;
+      const bool valid = row < a.rows;
+      const uint8_t* rowp = a.q + ((int64_t)it.le * a.rows + (valid ? row : 0)) * row_bytes;
+      const float scale = valid ? pow2f(a.wexp[it.le]) : 0.0f;
+      // bytes of K step kc: header of super-block kc / 4, quants of pair kc % 4
+      auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) {
+        const uint8_t* blk = rowp + (kc >> 2) * 144;
+        hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+        qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
+        qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
+      };
+      uint4 hdr, qa, qb;
+      load(0, hdr, qa, qb);
+      for (int kc = 0; kc < nk; ++kc) {
+        uint4 nh = hdr, na = qa, nb = qb;
+        if (kc + 1 < nk) load(kc + 1, nh, na, nb);
+        uint32_t hi[32], lo[32];
+        decode_pair(hdr, qa, qb, kc & 3, scale, hi, lo);
+        if (!mbar_wait(&tma_full[stage], phase, abort_flag, a.err)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sah = smem + stage * STAGE_BYTES;
+        const int rb = (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int off = rb + ((c ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(sah + off) =
+              make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+          *reinterpret_cast<uint4*>(sah + A_BYTES + off) =
+              make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&a_full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+        hdr = nh;
+        qa = na;
+        qb = nb;
+      }
+    }
+  } else {
+    // ---------------- epilogue: thread = TMEM lane = weight row ---------------
+    const int m = threadIdx.x;
+    int acc_iter = 0;
+    for (int item = blockIdx.x; item < total_items; item += gridDim.x, ++acc_iter) {
+      const int b = acc_iter & 1;
+      const uint32_t acc_phase = (acc_iter >> 1) & 1;
+      if (!mbar_wait(&acc_full[b], acc_phase, abort_flag, a.err)) break;
+      tc_fence_after();
+      const Item it = decode_item(a, item);
+      const uint32_t hi_addr =
+          tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 2 * BN);
+      epilogue_tile<MODE>(a, it, hi_addr, hi_addr + (uint32_t)BN, m);
+      tc_fence_before();
+      mbar_arrive(&acc_empty[b]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Decode exponent e of one local expert's matrix: the largest |d| * 63 * 15 +
+// |dmin| * 63 over its super-blocks bounds |w|; e puts that bound at or below
+// 2^14.  One CTA per local expert.
+__global__ void wexp_kernel(const uint8_t* __restrict__ q, int64_t blocks_per_expert,
+                            int32_t* __restrict__ wexp) {
+  __shared__ float red[32];
+  const int le = blockIdx.x;
+  const uint8_t* base = q + (int64_t)le * blocks_per_expert * 144;
+  float mx = 0.0f;
+  for (int64_t b = threadIdx.x; b < blocks_per_expert; b += blockDim.x) {
+    const uint8_t* blk = base + b * 144;
+    const float d = fabsf(f16_bits_to_f32((uint32_t)blk[0] | ((uint32_t)blk[1] << 8)));
+    const float dmin = fabsf(f16_bits_to_f32((uint32_t)blk[2] | ((uint32_t)blk[3] << 8)));
+    const float bound = d * 945.0f + dmin * 63.0f;
+    if (isfinite(bound)) mx = fmaxf(mx, bound);
+  }
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, s));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
+    mx = fmaxf(mx, red[0]);
+    int e = 0;
+    if (mx > 0.0f) {
+      int ex;
+      frexpf(mx, &ex);  // mx < 2^ex
+      e = 14 - ex;
+    }
+    wexp[le] = max(-60, min(60, e));
+  }
+}
+
+}  // namespace q4tc
+
+bool q4k_tc_supported(const Moe& m) {
+  const gb_moe_desc& d = m.desc;
+  return d.weight_format == GB_FMT_Q4_K && d.hidden % 256 == 0 && d.inter % 256 == 0 &&
+         m.w.q4_gu_exp != nullptr;
+}
+
+cudaError_t q4k_tc_prepare(Moe& m) {
+  const gb_moe_desc& d = m.desc;
+  const int nloc = m.e_end - m.e_begin;
+  if (d.weight_format != GB_FMT_Q4_K || nloc <= 0) return cudaSuccess;
+  cudaError_t e = cudaMalloc(&m.w.q4_gu_exp, sizeof(int32_t) * 2 * (size_t)nloc);
+  if (e != cudaSuccess) return e;
+  m.w.q4_dn_exp = m.w.q4_gu_exp + nloc;
+  q4tc::wexp_kernel<<<nloc, 256>>>(m.w.q4_gu, (int64_t)2 * d.inter * (d.hidden / 256),
+                                   m.w.q4_gu_exp);
+  q4tc::wexp_kernel<<<nloc, 256>>>(m.w.q4_dn, (int64_t)d.hidden * (d.inter / 256),
+                                   m.w.q4_dn_exp);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  return cudaDeviceSynchronize();
+}
+
+namespace {
+
+q4tc::Args q4tc_args(const Moe& m, const Groups& g, ExpertBufs& eb) {
+  q4tc::Args a{};
+  a.e_begin = m.e_begin;
+  a.meta = g.meta;
+  a.tile_expert = eb.tile_expert;
+  a.tile_row0 = eb.tile_row0;
+  a.tile_rows = eb.tile_rows;
+  a.act_kind = m.desc.act_kind;
+  a.limit = m.desc.swiglu_limit;
+  a.err = g.meta + 1;
+  return a;
+}
+
+template <int MODE>
+cudaError_t launch_q4tc(const Moe& m, const q4tc::Args& a, const void* map_hi, const void* map_lo,
+                        cudaStream_t st) {
+  auto k = q4tc::q4k_tc_gemm<MODE>;
+  cudaError_t e = set_smem_limit(k, q4tc::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  k<<<m.sm_count, q4tc::kThreads, q4tc::kSmemBytes, st>>>(
+      *reinterpret_cast<const CUtensorMap*>(map_hi), *reinterpret_cast<const CUtensorMap*>(map_lo),
+      a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                                  cudaStream_t st) {
+  const gb_moe_desc& d = m.desc;
+  cudaError_t e;
+  if ((e = launch_tile_table(m, g, q4tc::BN, eb, st)) != cudaSuccess) return e;
+  if ((e = launch_split_gather(m, g, x, eb, st)) != cudaSuccess) return e;
+  q4tc::Args a = q4tc_args(m, g, eb);
+  a.q = m.w.q4_gu;
+  a.wexp = m.w.q4_gu_exp;
+  a.K = d.hidden;
+  a.rows = 2 * d.inter;
+  a.m_tiles = (a.rows + q4tc::BM - 1) / q4tc::BM;
+  a.xscale = eb.xscale;
+  a.out_hi = eb.hh;
+  a.out_lo = eb.hl;
+  a.out_stride = d.inter;
+  return launch_q4tc<q4tc::GATE_UP>(m, a, eb.map_xh, eb.map_xl, st);
+}
+
+cudaError_t launch_q4k_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
+  const gb_moe_desc& d = m.desc;
+  q4tc::Args a = q4tc_args(m, g, eb);
+  a.q = m.w.q4_dn;
+  a.wexp = m.w.q4_dn_exp;
+  a.K = d.inter;
+  a.rows = d.hidden;
+  a.m_tiles = (a.rows + q4tc::BM - 1) / q4tc::BM;
+  a.out_y = eb.y;
+  a.out_rows = g.out_rows;
+  a.out_stride = d.hidden;
+  return launch_q4tc<q4tc::DOWN>(m, a, eb.map_hh, eb.map_hl, st);
+}
+
+}  // namespace gb

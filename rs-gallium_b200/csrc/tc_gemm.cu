@@ -605,17 +605,21 @@ cudaError_t launch_tile_table(const Moe& m, const Groups& g, int bn, ExpertBufs&
                     m.e_begin, m.e_end, bn, g.meta, eb.tile_expert, eb.tile_row0, eb.tile_rows);
 }
 
+cudaError_t launch_split_gather(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                                cudaStream_t st) {
+  const int positions = (int)g.rows;
+  if (positions <= 0) return cudaSuccess;
+  tc::split_gather_kernel<<<positions, 256, 0, st>>>(x, g.perm, g.perm_div, m.desc.hidden,
+                                                     positions, eb.xh, eb.xl, eb.xscale);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                               cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  const int positions = (int)g.rows;
   cudaError_t e;
   if ((e = launch_tile_table(m, g, tc::BN, eb, st)) != cudaSuccess) return e;
-  if (positions > 0) {
-    tc::split_gather_kernel<<<positions, 256, 0, st>>>(x, g.perm, g.perm_div, d.hidden, positions,
-                                                       eb.xh, eb.xl, eb.xscale);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  }
+  if ((e = launch_split_gather(m, g, x, eb, st)) != cudaSuccess) return e;
   tc::Args a = common_args(m, g, eb);
   a.blocks = m.w.gu_blocks;
   a.scales = m.w.gu_scales;

@@ -86,3 +86,21 @@ def test_q4k_ragged_rows_are_refused():
     with pytest.raises(GalliumError) as ei:
         Lfm2QMoEFFN.load(lay, device=0)
     assert "256-element" in str(ei.value)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64, 300])
+def test_lfm2_tensor_core_path_matches_oracle(layer, T):
+    # Q4_K weights decoded into f16 hi + lo for kind::f16 MMAs; AUTO takes
+    # this path above 32 rows per expert (T = 300 here), forced below
+    m = Lfm2QMoEFFN.load(layer, device=0, max_tokens=T)
+    try:
+        m.set_expert_path("tensor_cores")
+        x = synth.tokens(T, 2048, seed=1300 + T)
+        got = m.forward(_cuda(x)).cpu().numpy()
+        want, _, _ = oracle.OracleLfm2(layer).forward(x)
+        _parity(got, want, f"tensor cores T={T}")
+        m.set_expert_path("cuda_cores")
+        cc = m.forward(_cuda(x)).cpu().numpy()
+        _parity(got, cc.astype(np.float64), f"tensor vs CUDA cores T={T}")
+    finally:
+        m.close()
