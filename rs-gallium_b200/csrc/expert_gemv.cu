@@ -198,29 +198,50 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
   const int t = blockIdx.x;
   const int o4 = blockIdx.y * blockDim.x + threadIdx.x;
   if (o4 * 4 >= H) return;
-  int order[8];
-  for (int r = 0; r < K; ++r) order[r] = r;
+  // the token's k entries first (K <= 8), then all its y rows at once: one
+  // dependent round trip instead of one per rank
+  int e[8], order[8];
+  int64_t p[8];
+  float wv[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (r < K) {
+      e[r] = idx[(int64_t)t * K + r];
+      p[r] = inv[(int64_t)t * K + r];
+      wv[r] = wts[(int64_t)t * K + r];
+      order[r] = r;
+    }
+  }
   if (expert_order) {
     for (int a = 1; a < K; ++a) {
       const int cur = order[a];
       int b = a - 1;
-      while (b >= 0 && idx[(int64_t)t * K + order[b]] > idx[(int64_t)t * K + cur]) {
+      while (b >= 0 && e[order[b]] > e[cur]) {
         order[b + 1] = order[b];
         --b;
       }
       order[b + 1] = cur;
     }
   }
+  float4 v[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+    if (r < K) v[r] = reinterpret_cast<const float4*>(y + p[r] * H)[o4];
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int q = 0; q < K; ++q) {
     const int r = order[q];
-    const int64_t p = inv[(int64_t)t * K + r];
-    const float wv = wts[(int64_t)t * K + r];
-    const float4 v = reinterpret_cast<const float4*>(y + p * H)[o4];
-    acc.x = __fadd_rn(acc.x, __fmul_rn(v.x, wv));
-    acc.y = __fadd_rn(acc.y, __fmul_rn(v.y, wv));
-    acc.z = __fadd_rn(acc.z, __fmul_rn(v.z, wv));
-    acc.w = __fadd_rn(acc.w, __fmul_rn(v.w, wv));
+    float4 vr = v[0];
+    float w = wv[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i)
+      if (i == r) {
+        vr = v[i];
+        w = wv[i];
+      }
+    acc.x = __fadd_rn(acc.x, __fmul_rn(vr.x, w));
+    acc.y = __fadd_rn(acc.y, __fmul_rn(vr.y, w));
+    acc.z = __fadd_rn(acc.z, __fmul_rn(vr.z, w));
+    acc.w = __fadd_rn(acc.w, __fmul_rn(vr.w, w));
   }
   reinterpret_cast<float4*>(out + (int64_t)t * H)[o4] = acc;
 }

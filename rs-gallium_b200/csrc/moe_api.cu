@@ -639,15 +639,15 @@ int forward_dispatch(gb::Moe& m, const float* x, int64_t T, float* out, cudaStre
 
 namespace gb {
 
-// Q4_K experts: the tensor-core kernel for groups averaging more than 32 rows
+// Q4_K experts: the tensor-core kernel for groups averaging at least 8 rows
 // per local expert (or when the tensor cores are forced); the CUDA-core
-// kernel streams decode-sized groups faster.
+// kernel streams smaller groups faster.
 bool use_q4k_tc(const Moe& m, const Groups& g, const ExpertBufs& eb) {
   if (!q4k_tc_supported(m) || !eb.maps_ok || m.expert_path == GB_PATH_CUDA_CORES) return false;
   if (m.expert_path == GB_PATH_TENSOR_CORES || m.expert_path == GB_PATH_TENSOR_CORES_F16)
     return true;
   const int64_t nloc = std::max(1, m.e_end - m.e_begin);
-  return g.rows > 32 * nloc;
+  return g.rows >= 8 * nloc;
 }
 
 cudaError_t set_smem_limit_fn(const void* kern, size_t bytes) {

@@ -120,6 +120,22 @@ __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
     }
     __syncthreads();
 
+    if (c0 == 0) {
+      // pull every row pair's blocks toward L2 at once: the pairs below run
+      // one after the other, so without this each waits a full HBM round trip
+      for (int p = 1; p < PAIRS; ++p) {
+        const int row = wrow0 + 2 * p;
+        if (row >= a.rows) break;
+        for (int c = lane; c < NP; c += 32) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const uint8_t* blk = ebase + (int64_t)(row + r) * row_bytes + (c >> 2) * 144;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(blk));
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(blk + 128));
+          }
+        }
+      }
+    }
     for (int p = 0; p < PAIRS; ++p) {
       const int row = wrow0 + 2 * p;
       if (row >= a.rows) break;

@@ -1,5 +1,5 @@
 // q4k_tc.cu -- grouped Q4_K expert GEMMs on the tensor cores (LFM2.5 batches
-// of more than 32 rows per expert).
+// of at least 8 rows per expert).
 //
 // Reference math: lfm2moe_q.rs:279-296 (h = silu(x Wg^T) * (x Wu^T), y =
 // h Wd^T, no biases) over candle's Q4_K dequantiser (quantized.rs:162-177):
@@ -16,12 +16,14 @@
 //
 // Tiles and roles follow tc_gemm.cu: D[m, n] = sum_k W[m, k] X[n, k] with
 // M = 128 weight rows, N = 128 grouped positions of one expert, K stepped by
-// 64 (one Q4_K sub-block pair).  Warps 4-7 decode: thread r loads row r's
-// super-block header and 32 quant bytes straight from HBM (the next stage's
-// bytes are in flight while it decodes) and writes A hi / lo into shared
-// memory in the K-major 128-byte-swizzled layout; warp 8 copies B hi / lo by
-// TMA; warp 9 issues the MMAs; warps 0-3 run the epilogue (bias-free SiLU or
-// clamped SwiGLU into h hi / lo, or y).  Three 64 KB stages; two TMEM
+// 64 (one Q4_K sub-block pair).  Warps 4-11 decode: threads r and r + 128
+// load row r's super-block header and 32 quant bytes straight from HBM (the
+// next two stages' bytes are in flight while they decode), each decodes one
+// sub-block (the low or the high nibbles) and writes its half of A hi / lo
+// into shared memory in the K-major 128-byte-swizzled layout (decoding, not
+// the MMAs, bounds this kernel, hence eight warps); warp 12 copies B hi / lo
+// by TMA; warp 13 issues the MMAs; warps 0-3 run the epilogue (bias-free SiLU
+// or clamped SwiGLU into h hi / lo, or y).  Three 64 KB stages; two TMEM
 // accumulator pairs so the epilogue of one tile overlaps the next tile's MMAs.
 // Every mbarrier wait is bounded (timeout -> abort flag, error bit 2, TMEM
 // freed, return).
@@ -40,7 +42,8 @@ constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * B_BYTES;  // A hi, A lo, B hi, B lo
-constexpr int kThreads = 320;
+constexpr int kThreads = 448;
+constexpr int kDecoders = 256;  // two threads per weight row
 constexpr int kTmemCols = 4 * BN;  // two buffers x (hi, lo) accumulators
 constexpr size_t kSmemBytes = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 
@@ -110,40 +113,34 @@ __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   return it;
 }
 
-// The 64 values of one sub-block pair (low nibbles: sub-block 2c, high: 2c+1)
-// times 2^e, as f16 hi / lo pairs packed two per word in element order.
-__device__ __forceinline__ void decode_pair(const uint4& hdr, const uint4& qa, const uint4& qb,
-                                            int c, float scale, uint32_t (&hi)[32],
-                                            uint32_t (&lo)[32]) {
+// The 32 values of sub-block 2c + h of a super-block (h = 0: the low
+// nibbles of the pair's 32 quant bytes, 1: the high nibbles) times 2^e, as
+// f16 hi / lo pairs packed two per word in element order.
+__device__ __forceinline__ void decode_half(const uint4& hdr, const uint4& qa, const uint4& qb,
+                                            int c, int h, float scale, uint32_t (&hi)[16],
+                                            uint32_t (&lo)[16]) {
   const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
   const float d = f16_bits_to_f32((uint32_t)hb[0] | ((uint32_t)hb[1] << 8));
   const float dmin = f16_bits_to_f32((uint32_t)hb[2] | ((uint32_t)hb[3] << 8));
-  float d1[2], m1[2];
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    int sc, mn;
-    q4k_scale_min(2 * c + h, hb + 4, sc, mn);
-    d1[h] = __fmul_rn(d, (float)sc);
-    m1[h] = __fmul_rn(dmin, (float)mn);
-  }
+  int sc, mn;
+  q4k_scale_min(2 * c + h, hb + 4, sc, mn);
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
   const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+  const int shift = 4 * h;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
+  for (int i = 0; i < 16; ++i) {  // elements 2i, 2i + 1 of the sub-block
+    float v[2];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {  // elements 32h + 2i, 32h + 2i + 1
-      float v[2];
-#pragma unroll
-      for (int u = 0; u < 2; ++u) {
-        const int byte = 2 * i + u;
-        const uint32_t qv = (words[byte >> 2] >> (8 * (byte & 3) + 4 * h)) & 0xFu;
-        v[u] = __fmul_rn(__fsub_rn(__fmul_rn(d1[h], (float)qv), m1[h]), scale);
-      }
-      const __half2 vh = __floats2half2_rn(v[0], v[1]);
-      const float2 back = __half22float2(vh);
-      const __half2 vl = __floats2half2_rn(__fsub_rn(v[0], back.x), __fsub_rn(v[1], back.y));
-      hi[16 * h + i] = *reinterpret_cast<const uint32_t*>(&vh);
-      lo[16 * h + i] = *reinterpret_cast<const uint32_t*>(&vl);
+    for (int u = 0; u < 2; ++u) {
+      const int byte = 2 * i + u;
+      const uint32_t qv = (words[byte >> 2] >> (8 * (byte & 3) + shift)) & 0xFu;
+      v[u] = __fmul_rn(__fsub_rn(__fmul_rn(d1, (float)qv), m1), scale);
     }
+    const __half2 vh = __floats2half2_rn(v[0], v[1]);
+    const float2 back = __half22float2(vh);
+    const __half2 vl = __floats2half2_rn(__fsub_rn(v[0], back.x), __fsub_rn(v[1], back.y));
+    hi[i] = *reinterpret_cast<const uint32_t*>(&vh);
+    lo[i] = *reinterpret_cast<const uint32_t*>(&vl);
   }
 }
 
@@ -207,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&tma_full[s], 1);
-      mbar_init(&a_full[s], 128);
+      mbar_init(&a_full[s], kDecoders);
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -223,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ---------------- TMA producer: activation hi / lo -----------------------
     if (lane == 0) {
       int stage = 0;
@@ -252,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ---------------- MMA issuer ---------------------------------------------
     if (lane == 0) {
       int stage = 0;
@@ -301,8 +298,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- weight decode: thread r owns row r of the M tile -------
-    const int r = threadIdx.x - 128;
+    // ---------------- weight decode: threads r, r + 128 own row r -----------
+    const int r = (threadIdx.x - 128) & 127;
+    const int hsel = (threadIdx.x - 128) >> 7;  // 0: low nibbles, 1: high
     const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
     int stage = 0;
     uint32_t phase = 0;
@@ -320,13 +318,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
         qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
       };
-      uint4 hdr, qa, qb;
+      // two K steps of bytes in flight ahead of the one being decoded
+      uint4 hdr, qa, qb, h1 = {}, a1 = {}, b1 = {};
       load(0, hdr, qa, qb);
+      if (nk > 1) load(1, h1, a1, b1);
       for (int kc = 0; kc < nk; ++kc) {
-        uint4 nh = hdr, na = qa, nb = qb;
-        if (kc + 1 < nk) load(kc + 1, nh, na, nb);
-        uint32_t hi[32], lo[32];
-        decode_pair(hdr, qa, qb, kc & 3, scale, hi, lo);
+        uint4 h2 = h1, a2 = a1, b2 = b1;
+        if (kc + 2 < nk) load(kc + 2, h2, a2, b2);
+        uint32_t hi[16], lo[16];
+        decode_half(hdr, qa, qb, kc & 3, hsel, scale, hi, lo);
         if (!mbar_wait(&tma_full[stage], phase, abort_flag, a.err)) {
           ok = false;
           break;
@@ -334,12 +334,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sah = smem + stage * STAGE_BYTES;
         const int rb = (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int cc = 0; cc < 4; ++cc) {  // 16-byte chunks 4 hsel .. 4 hsel + 3 of the row
+          const int c = 4 * hsel + cc;
           const int off = rb + ((c ^ (r & 7)) << 4);
           *reinterpret_cast<uint4*>(sah + off) =
-              make_uint4(hi[4 * c], hi[4 * c + 1], hi[4 * c + 2], hi[4 * c + 3]);
+              make_uint4(hi[4 * cc], hi[4 * cc + 1], hi[4 * cc + 2], hi[4 * cc + 3]);
           *reinterpret_cast<uint4*>(sah + A_BYTES + off) =
-              make_uint4(lo[4 * c], lo[4 * c + 1], lo[4 * c + 2], lo[4 * c + 3]);
+              make_uint4(lo[4 * cc], lo[4 * cc + 1], lo[4 * cc + 2], lo[4 * cc + 3]);
         }
         fence_proxy_async_smem();
         mbar_arrive(&a_full[stage]);
@@ -347,9 +348,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           stage = 0;
           phase ^= 1;
         }
-        hdr = nh;
-        qa = na;
-        qb = nb;
+        hdr = h1;
+        qa = a1;
+        qb = b1;
+        h1 = h2;
+        a1 = a2;
+        b1 = b2;
       }
     }
   } else {

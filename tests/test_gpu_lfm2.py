@@ -91,7 +91,7 @@ def test_q4k_ragged_rows_are_refused():
 @pytest.mark.parametrize("T", [1, 8, 64, 300])
 def test_lfm2_tensor_core_path_matches_oracle(layer, T):
     # Q4_K weights decoded into f16 hi + lo for kind::f16 MMAs; AUTO takes
-    # this path above 32 rows per expert (T = 300 here), forced below
+    # this path from 8 rows per expert (T = 64, 300 here), forced below
     m = Lfm2QMoEFFN.load(layer, device=0, max_tokens=T)
     try:
         m.set_expert_path("tensor_cores")
