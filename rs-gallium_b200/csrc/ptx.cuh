@@ -35,14 +35,19 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t byte
                : "memory");
 }
 
+// A thread whose phase is not complete is suspended (not spinning, so it
+// takes no issue slots from the warps doing work) until the phase completes
+// or kMbarSuspendNs pass.
+constexpr uint32_t kMbarSuspendNs = 1000000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(b)), "r"(parity)
+      : "r"(smem_u32(b)), "r"(parity), "r"(kMbarSuspendNs)
       : "memory");
   return ok != 0;
 }
