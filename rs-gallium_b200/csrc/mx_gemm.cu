@@ -58,13 +58,14 @@
 
 #include "common.cuh"
 #include "moe_internal.h"
+#include "pieces.cuh"
 #include "ptx.cuh"
 #include "umma.cuh"
 
 namespace gb {
 namespace mx {
 
-constexpr int BM = 128, BK = 128, kPieces = 4;
+constexpr int BM = 128, BK = 128, kPieces = kActPieces;
 constexpr int DM = 256;  // weight rows per tile
 constexpr int SF_BYTES = 512;
 constexpr int kSmemLimit = 232448;
@@ -99,28 +100,6 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
                  "=r"(v[6]), "=r"(v[7])
                : "r"(taddr));
 }
-
-// E4M3 of one f32 (round to nearest even, saturating) and back.
-__device__ __forceinline__ uint32_t e4m3_of(float v) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(v));
-  return r & 0xffu;
-}
-
-__device__ __forceinline__ uint32_t e4m3x2_of(float hi, float lo) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-
-__device__ __forceinline__ float2 e4m3x2_value(uint32_t v) {
-  uint32_t h;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"((uint16_t)v));
-  const __half2 hv = *reinterpret_cast<const __half2*>(&h);
-  return __half22float2(hv);  // .x = low byte, .y = high byte
-}
-
-__device__ __forceinline__ float e4m3_value(uint32_t v) { return e4m3x2_value(v).x; }
 
 // Writes the pieces of hp (|hp| < 256) at dst, dst + step, ...
 __device__ __forceinline__ void store_pieces(float hp, uint8_t* dst, int64_t step) {
@@ -711,54 +690,6 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, D::TMEM_COLS);
-  }
-}
-
-// One activation row -> exponent s and four E4M3 pieces of x * 2^-s, written
-// [4][K] at each of the `ndst` destinations (a token routed to several
-// experts has one grouped position per expert).  128 threads.
-__device__ __forceinline__ void row_pieces(const float* __restrict__ xrow, int K,
-                                           uint8_t* __restrict__ q,
-                                           float* __restrict__ xscale, const int* dst_pos,
-                                           int ndst) {
-  const float4* src = reinterpret_cast<const float4*>(xrow);
-  const int n4 = K / 4;
-  __shared__ float red[4];
-  float mx = 0.0f;
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-    const float4 v = src[i];
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-  }
-#pragma unroll
-  for (int s = 16; s >= 1; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, s));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  // max |x'| in [128, 256); exponents kept where 2^-s stays a normal f32
-  int s = mx > 0.0f ? ilogbf(mx) - 7 : 0;
-  s = max(-120, min(120, s));
-  const float inv = pow2f(-s);
-  if (threadIdx.x < ndst) xscale[dst_pos[threadIdx.x]] = (float)s;
-  for (int i = threadIdx.x; i < n4; i += blockDim.x) {
-    const float4 v = src[i];
-    float r[4] = {__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv),
-                  __fmul_rn(v.w, inv)};
-    uint32_t w[kPieces];
-#pragma unroll
-    for (int p = 0; p < kPieces; ++p) {
-      const uint32_t lo = e4m3x2_of(r[1], r[0]), hi = e4m3x2_of(r[3], r[2]);
-      w[p] = lo | (hi << 16);
-      const float2 a = e4m3x2_value(lo), b = e4m3x2_value(hi);
-      r[0] = __fmul_rn(__fsub_rn(r[0], a.x), 16.0f);
-      r[1] = __fmul_rn(__fsub_rn(r[1], a.y), 16.0f);
-      r[2] = __fmul_rn(__fsub_rn(r[2], b.x), 16.0f);
-      r[3] = __fmul_rn(__fsub_rn(r[3], b.y), 16.0f);
-    }
-    for (int d = 0; d < ndst; ++d) {
-      uint32_t* dst = reinterpret_cast<uint32_t*>(q + (int64_t)dst_pos[d] * kPieces * K);
-#pragma unroll
-      for (int p = 0; p < kPieces; ++p) dst[p * n4 + i] = w[p];
-    }
   }
 }
 
