@@ -45,9 +45,12 @@
 // passes.  The four K steps of a stage rotate over ACCS accumulators so
 // consecutive MMAs do not wait on one another.
 //
-// Persistent grid (one or two CTAs per SM) over work items (N tile, M tile),
-// M fastest.  Warps: 0-3 epilogue (TMEM lanes 0-127), 4 and 6 TMA producers
-// (alternate stages), 5 MMA issuer.  Every mbarrier wait is bounded: on
+// Persistent grid (two CTAs per SM) over work items (N tile, M tile, K
+// split), M fastest; when the tiles cannot fill the grid, K is split and the
+// last split to finish adds the partial sums in split order.  Grouped decode
+// batches run gate_up and down as one launch (MODE 2, see the kernel).
+// Warps: 0-3 epilogue (TMEM lanes 0-127), 4 and 6 TMA producers (alternate
+// stages), 5 MMA issuer.  Every mbarrier wait is bounded: on
 // timeout the CTA raises an abort flag, records error bit 2, lets in-flight
 // copies land, frees its TMEM and returns.
 #include <cuda.h>
