@@ -592,52 +592,94 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       };
       const uint32_t base =
           tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * D::BUF);
-#pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const int row = it.m_tile * DM + h * BM + m;
-        const bool valid = row < A.rows;
-        const int64_t grow = (int64_t)it.le * A.rows + (valid ? row : 0);
-        const float bias = (valid && A.bias) ? A.bias[grow] : 0.0f;
-#pragma unroll 1
-        for (int n0p = 0; n0p < NT; n0p += 2 * D::PAIRS) {
-          // columns 4n .. 4n + 7 hold the pieces of positions n and n + 1
-          uint32_t v[D::PAIRS][D::ACCS][8];
+      // Sums of the pieces (and accumulators) of positions n0p .. n0p +
+      // 2 PAIRS - 1 of half h; columns 4n .. 4n + 7 hold positions n, n + 1.
+      auto load_sums = [&](int h, int n0p, float (&sums)[D::PAIRS][2]) {
+        uint32_t v[D::PAIRS][D::ACCS][8];
 #pragma unroll
-          for (int pp = 0; pp < D::PAIRS; ++pp)
+        for (int pp = 0; pp < D::PAIRS; ++pp)
 #pragma unroll
-            for (int q = 0; q < D::ACCS; ++q)
-              if (n0p + 2 * pp < NT)
-                tmem_ld8(base + (uint32_t)((h * D::ACCS + q) * D::N + kPieces * (n0p + 2 * pp)),
-                         v[pp][q]);
-          tmem_wait_ld();
+          for (int q = 0; q < D::ACCS; ++q)
+            if (n0p + 2 * pp < NT)
+              tmem_ld8(base + (uint32_t)((h * D::ACCS + q) * D::N + kPieces * (n0p + 2 * pp)),
+                       v[pp][q]);
+        tmem_wait_ld();
 #pragma unroll
-          for (int pp = 0; pp < D::PAIRS; ++pp) {
-            const int n = n0p + 2 * pp;
-            if (n >= NT) break;
-            float val[2];
+        for (int pp = 0; pp < D::PAIRS; ++pp)
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              float sum = 0.0f;
+          for (int u = 0; u < 2; ++u) {
+            float sum = 0.0f;
 #pragma unroll
-              for (int p = 0; p < kPieces; ++p) {
-                float t = __uint_as_float(v[pp][0][u * kPieces + p]);
+            for (int p = 0; p < kPieces; ++p) {
+              float t = __uint_as_float(v[pp][0][u * kPieces + p]);
 #pragma unroll
-                for (int q = 1; q < D::ACCS; ++q)
-                  t = __fadd_rn(t, __uint_as_float(v[pp][q][u * kPieces + p]));
-                sum = p == 0 ? t : __fadd_rn(sum, t);
+              for (int q = 1; q < D::ACCS; ++q)
+                t = __fadd_rn(t, __uint_as_float(v[pp][q][u * kPieces + p]));
+              sum = p == 0 ? t : __fadd_rn(sum, t);
+            }
+            sums[pp][u] = sum;
+          }
+      };
+      auto store_pair = [&](int h, int row, bool valid, float bias, int n, float (&val)[2]) {
+        if (split)
+          *reinterpret_cast<float2*>(part + (h * BM + m) * NT + n) = make_float2(val[0], val[1]);
+        else
+          finish(row, valid, bias, n, val);
+      };
+      if constexpr (D::NACC == 1) {
+        // One accumulator buffer (the widest tiles): the whole tile's sums
+        // (2 x NT per thread) come out of TMEM first and the buffer is handed
+        // back at once, so that the next item's MMAs run while this thread
+        // stores h or y.  The arrive is relaxed: the MMA warp reads none of
+        // the stores.
+        float acc[2][NT];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int n0p = 0; n0p < NT; n0p += 2 * D::PAIRS) {
+            float sums[D::PAIRS][2];
+            load_sums(h, n0p, sums);
+#pragma unroll
+            for (int pp = 0; pp < D::PAIRS; ++pp)
+              if (n0p + 2 * pp < NT) {
+                acc[h][n0p + 2 * pp] = sums[pp][0];
+                acc[h][n0p + 2 * pp + 1] = sums[pp][1];
               }
-              val[u] = sum;
-            }
-            if (split) {
-              *reinterpret_cast<float2*>(part + (h * BM + m) * NT + n) = make_float2(val[0], val[1]);
-            } else {
-              finish(row, valid, bias, n, val);
-            }
+          }
+        tc_fence_before();
+        mbar_arrive_relaxed(&acc_empty[b]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = it.m_tile * DM + h * BM + m;
+          const bool valid = row < A.rows;
+          const int64_t grow = (int64_t)it.le * A.rows + (valid ? row : 0);
+          const float bias = (valid && A.bias) ? A.bias[grow] : 0.0f;
+#pragma unroll
+          for (int n = 0; n < NT; n += 2) {
+            float val[2] = {acc[h][n], acc[h][n + 1]};
+            store_pair(h, row, valid, bias, n, val);
           }
         }
+      } else {
+        // Two buffers: the next item's MMAs already run in the other one.
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          const int row = it.m_tile * DM + h * BM + m;
+          const bool valid = row < A.rows;
+          const int64_t grow = (int64_t)it.le * A.rows + (valid ? row : 0);
+          const float bias = (valid && A.bias) ? A.bias[grow] : 0.0f;
+#pragma unroll 1
+          for (int n0p = 0; n0p < NT; n0p += 2 * D::PAIRS) {
+            float sums[D::PAIRS][2];
+            load_sums(h, n0p, sums);
+#pragma unroll
+            for (int pp = 0; pp < D::PAIRS; ++pp)
+              if (n0p + 2 * pp < NT) store_pair(h, row, valid, bias, n0p + 2 * pp, sums[pp]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[b]);
       }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
       if (!split) {
         if (MODE == 2 && ph == 0) publish_ready(a0, it, m);
       } else {
