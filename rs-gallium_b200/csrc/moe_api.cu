@@ -517,7 +517,7 @@ int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t 
   if (m.ep_size == 1 && m.desc.weight_format != GB_FMT_Q4_K && gb::mx_group_fits(m, T) &&
       pick_expert_kernel(m, m.ws.eb) == ExpertKernel::kMx) {
     gb::Groups g = local_groups(m, T);
-    const int kind = gb::mx_tile_kind(m, g);
+    const int kind = std::min(gb::mx_tile_kind(m, g), gb::kMxKind30);
     if ((rc = run_route_grouped(m, x, T, g, kind, st))) return rc;
     if (g.rows >= gb::kMxOneLaunchRows) {
       // gate_up and down in one launch: the "down" stage is empty

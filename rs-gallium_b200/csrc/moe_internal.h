@@ -130,8 +130,8 @@ struct ExpertBufs {
   alignas(64) unsigned char map_hl[128] = {};
   uint8_t* xq = nullptr;       // [rows][4][H] E4M3 pieces of the grouped activations
   uint8_t* hq = nullptr;       // [rows][4][I] E4M3 pieces of the SwiGLU output
-  alignas(64) unsigned char map_xq[5][128] = {};  // CUtensorMaps, tiles of 2, 4, 8, 16, 30
-  alignas(64) unsigned char map_hq[5][128] = {};  // positions (index: kind)
+  alignas(64) unsigned char map_xq[6][128] = {};  // CUtensorMaps, tiles of 2, 4, 8, 16, 30,
+  alignas(64) unsigned char map_hq[6][128] = {};  // 60 positions (index: kind)
   float* mx_partial = nullptr;  // split-K partial sums (2 x kMxPartialBytes: gate_up, down)
   int* mx_arrivals = nullptr;   // split-K tickets [2 x kMxSplitSlots], zero between forwards
   int* mx_ready = nullptr;      // one-launch expert kernel: [0] item counter, then
@@ -252,7 +252,9 @@ cudaError_t launch_q4k_dequant(const Moe& m, int which, int local_expert, float*
                                cudaStream_t st);
 
 // Block-scaled tensor-core expert path (mx_gemm.cu).
-constexpr int kMxTileKinds = 5;  // tiles of 2, 4, 8, 16, 30 positions
+constexpr int kMxTileKinds = 6;  // tiles of 2, 4, 8, 16, 30, 60 positions
+constexpr int kMxKind30 = 4;     // the widest tile of the one-launch mode
+constexpr int kMxKind60 = 5;     // gate_up / down launched alone, one CTA per SM
 constexpr size_t kMxPartialBytes = size_t(8) << 20;  // split-K partial sums
 constexpr int kMxSplitSlots = 4096;                  // split-K tiles x splits
 constexpr int kMxGroupEntries = 512;  // routing entries of the one-launch grouping

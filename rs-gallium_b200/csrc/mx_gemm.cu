@@ -179,13 +179,15 @@ __device__ __forceinline__ Item decode_item(const Args& a, int item) {
 }
 
 // Bias + clamped SwiGLU + pieces of h (GATE_UP) or bias + y (DOWN) for
-// positions n and n + 1 of the tile, val[u] being the sum of weight row
-// `row` for position n + u.  Every lane of the warp calls it (the gate/up
-// pair of rows 2i, 2i+1 is exchanged between neighbouring lanes: the even
-// lane finishes position n, the odd lane position n + 1).
+// positions pg + n and pg + n + 1 of the tile (pg: the epilogue group's first
+// position; lane n holds position pg + n's scale or output row), val[u]
+// being the sum of weight row `row` for position pg + n + u.  Every lane of
+// the warp calls it (the gate/up pair of rows 2i, 2i+1 is exchanged between
+// neighbouring lanes: the even lane finishes position pg + n, the odd lane
+// pg + n + 1).
 template <int MODE>
 __device__ __forceinline__ void finish_pair(const Args& a, const Item& it, int row, bool valid,
-                                            float bias, int n, float (&val)[2],
+                                            float bias, int pg, int n, float (&val)[2],
                                             float lane_scale, int64_t lane_orow, int m) {
   if (MODE == 0) {
 #pragma unroll
@@ -195,7 +197,7 @@ __device__ __forceinline__ void finish_pair(const Args& a, const Item& it, int r
     const float other = __shfl_xor_sync(kFullMask, odd ? val[0] : val[1], 1);
     const float gate = odd ? other : val[0];
     const float up = odd ? val[1] : other;
-    const int np = n + (odd ? 1 : 0);
+    const int np = pg + n + (odd ? 1 : 0);
     if (valid && np < it.nrows)
       store_pieces(__fmul_rn(act_gptoss(gate, up, a.limit), pow2f(-a.h_exp)),
                    a.out_q + ((int64_t)it.row0 + np) * (kPieces * a.out_stride) + (row >> 1),
@@ -205,7 +207,7 @@ __device__ __forceinline__ void finish_pair(const Args& a, const Item& it, int r
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int64_t orow = __shfl_sync(kFullMask, lane_orow, n + u);
-      if (valid && n + u < it.nrows)
+      if (valid && pg + n + u < it.nrows)
         a.out_y[orow * a.out_stride + row] = __fadd_rn(__fmul_rn(val[u], f), bias);
     }
   }
@@ -221,15 +223,27 @@ __device__ __forceinline__ void linger_2ms() {
 // share an SM: each issues its own copies (one CTA's copies stall near
 // 40 GB/s), and one CTA's epilogue overlaps the other's MMAs; each has at most
 // 256 TMEM columns and half the shared memory.
+// NT = 60 (large batches, gate_up or down launched alone): one CTA per SM
+// with all 512 TMEM columns, N = 240 per MMA, and two epilogue groups
+// (warps 0-3 positions 0-29, warps 8-11 positions 30-59).  Each MMA
+// instruction costs a fixed overhead besides its N-proportional time, so the
+// 240-column MMAs keep the tensor pipe busier than 120-column ones.
+// From NT = 30 a tile's MMAs are only as wide as its positions (N = 8
+// ceil(rows / 2)), so an expert's last, partial tile costs its own rows.
 // TMEM: NACC tile buffers of (2 halves x ACCS accumulators x N columns), then
-// the constant piece scales (4 columns) and one 8-column slot of weight
-// scales, rewritten by tcgen05.cp before each stage's MMAs (the tcgen05
-// pipeline runs a thread's copies and MMAs in issue order; a ring of slots
-// measured no faster and costs the widest tile 2 positions).
+// the constant piece scales (4 columns, 8 for N > 128) and one 8-column slot
+// of weight scales, rewritten by tcgen05.cp before each stage's MMAs (the
+// tcgen05 pipeline runs a thread's copies and MMAs in issue order; a ring of
+// slots measured no faster and costs the widest tile 2 positions).
 template <int NT>
 struct Tile {
   static constexpr int N = kPieces * NT;
-  static constexpr int CPS = 2;
+  static constexpr int GROUPS = NT > 32 ? 2 : 1;     // epilogue groups of 4 warps
+  static constexpr int EPT = NT / GROUPS;            // positions per epilogue group
+  static constexpr int THREADS = GROUPS == 1 ? kThreads : 384;
+  static constexpr int CPS = GROUPS == 1 ? 2 : 1;
+  static constexpr bool VARN = NT >= 30;             // MMA width follows the tile's rows
+  static constexpr int SFB_COLS = N > 128 ? 8 : 4;
   static constexpr int W_BYTES = DM * BK;            // 32 KB in shared memory, 16 KB packed
   static constexpr int X_BYTES = N * BK;             // NT positions x 4 pieces x 128 bytes
   static constexpr int SFW = 2 * SF_BYTES;           // scale atoms of the two halves
@@ -238,14 +252,16 @@ struct Tile {
   static constexpr int ACCS = N <= 16 ? 2 : 1;       // accumulators per half and tile
   static constexpr int BUF = 2 * ACCS * N;
   static constexpr int COLS_MAX = 512 / CPS;
-  static constexpr int NACC = 2 * BUF + 12 <= COLS_MAX ? 2 : 1;  // tile buffers
-  static constexpr int SFB_COL = NACC * BUF;         // constant piece scales, 4 columns
-  static constexpr int SFA_COL = SFB_COL + 4;        // weight scales, 8 columns
+  static constexpr int NACC = 2 * BUF + SFB_COLS + 8 <= COLS_MAX ? 2 : 1;  // tile buffers
+  static constexpr int SFB_COL = NACC * BUF;         // constant piece scales
+  static constexpr int SFA_COL = SFB_COL + SFB_COLS;  // weight scales, 8 columns
   static constexpr int USED = SFA_COL + 8;
   static constexpr int TMEM_COLS = USED <= 128 ? 128 : USED <= 256 ? 256 : 512;
-  static constexpr int PAIRS = NT >= 8 ? 4 : NT / 2;  // position pairs per epilogue batch
+  static constexpr int PAIRS = EPT >= 8 ? 4 : EPT / 2;  // position pairs per epilogue batch
   static constexpr size_t SMEM = (size_t)STAGES * STAGE + SF_BYTES + 1024 + 256;
-  static_assert(NT % 2 == 0 && NT <= 32, "positions are read in pairs, one lane each");
+  static_assert(NT % 2 == 0 && EPT % 2 == 0 && EPT <= 32,
+                "positions are read in pairs, one lane each per epilogue group");
+  static_assert(N <= 256, "MMA width");
   static_assert(STAGES >= 2, "pipeline depth");
   static_assert(TMEM_COLS <= COLS_MAX, "tensor memory");
   static_assert(SMEM * CPS <= (size_t)kSmemLimit, "shared memory");
@@ -304,12 +320,13 @@ __device__ __forceinline__ void publish_ready(const Args& a, const Item& it, int
 // that the producer keeps streaming weights.  Gate_up items wait on nothing,
 // so with every CTA resident (one grid of 2 CTAs per SM) the waits end.
 template <int MODE, int NT>
-__global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
+__global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
     mx_expert_gemm(const __grid_constant__ CUtensorMap tmap_w0,
                    const __grid_constant__ CUtensorMap tmap_x0,
                    const __grid_constant__ CUtensorMap tmap_w1,
                    const __grid_constant__ CUtensorMap tmap_x1, const Args a0, const Args a1) {
   using D = Tile<NT>;
+  static_assert(D::GROUPS == 1 || MODE != 2, "the one-launch mode runs tiles of at most 30");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -323,7 +340,6 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ int s_last;
   // MODE 2 schedule: producer warp 4 takes items from a0.next_item (the
   // first is blockIdx.x) and hands each to warp 6, the MMA warp and the
   // epilogue through this ring; -1 ends the list
@@ -331,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
   __shared__ __align__(8) uint64_t s_sched_full[kSchedRing], s_sched_empty[kSchedRing];
   pdl_trigger();
 
-  for (int i = threadIdx.x; i < SF_BYTES / 4; i += kThreads)
+  for (int i = threadIdx.x; i < SF_BYTES / 4; i += D::THREADS)
     reinterpret_cast<uint32_t*>(sfb_const)[i] = piece_scale_word(i);
   fence_proxy_async_smem();
   if (threadIdx.x == 0) {
@@ -341,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 128);
+      mbar_init(&acc_empty[b], 128 * D::GROUPS);
     }
     for (int r = 0; r < kSchedRing; ++r) {
       mbar_init(&s_sched_full[r], 1);
@@ -493,6 +509,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       const uint32_t sfb = tmem_base + (uint32_t)D::SFB_COL;
       const uint32_t sfa = tmem_base + (uint32_t)D::SFA_COL;
       tmem_cp_sf(sfb, rows16_desc(smem_u32(sfb_const)));
+      if (D::SFB_COLS > 4) tmem_cp_sf(sfb + 4, rows16_desc(smem_u32(sfb_const)));  // rows 128-255
       const uint64_t dconst = sw128_desc(0), rconst = rows16_desc(0);
       const uint32_t smem0 = smem_u32(smem);
       uint32_t s = 0, sph = 0, sw = smem0;
@@ -515,6 +532,11 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
         tc_fence_after();
         const uint32_t dbase = tmem_base + (uint32_t)(b * D::BUF);
         const Item it = decode_item(A, local_of(item));
+        // MMA width: the tile's positions rounded up to even (4 piece rows each)
+        const uint32_t idesc =
+            D::VARN ? (D::IDESC & ~(0x3Fu << 17)) |
+                          ((uint32_t)min(D::N, 8 * ((it.nrows + 1) >> 1)) >> 3 << 17)
+                    : D::IDESC;
         for (int kc = it.kc0; kc < it.kc1; ++kc) {
           if (!mbar_wait(&full[s], sph, abort_flag, A.err)) {
             ok = false;
@@ -535,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
             for (int h = 0; h < 2; ++h)
               mma_mx(dbase + (uint32_t)((h * D::ACCS + acc) * D::N),
                      da + (uint64_t)((h * BM * BK) >> 4) + (uint64_t)(2 * j), db + (uint64_t)(2 * j),
-                     D::IDESC | ((uint32_t)j << 29), (sfa + 4 * h) | ((uint32_t)j << 30), sfb, on);
+                     idesc | ((uint32_t)j << 29), (sfa + 4 * h) | ((uint32_t)j << 30), sfb, on);
           }
           mma_commit(&empty[s]);
           if (++s == (uint32_t)D::STAGES) {
@@ -550,13 +572,17 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       }
       if (!ok || *abort_flag) linger_2ms();
     }
-  } else if (warp < 4) {
+  } else if (warp < 4 || (D::GROUPS > 1 && warp >= 8)) {
     // ---------------- epilogue: thread m owns TMEM lane m -------------------
-    // Thread 0 takes the item and waits for its accumulator, then the 128
-    // threads agree on it at a named barrier (so that a wait that gave up
-    // ends every thread's loop at the same item).
-    const int m = threadIdx.x;
-    __shared__ int s_epi_item[2];
+    // Group grp (warps 0-3; warps 8-11 in 60-position tiles) finishes
+    // positions pg .. pg + EPT - 1.  Its thread 0 takes the item and waits
+    // for the accumulator, then the group's 128 threads agree on it at named
+    // barrier 1 + grp (so that a wait that gave up ends every thread's loop
+    // at the same item).
+    const int m = threadIdx.x & 127, grp = warp >> 3, pg = grp * D::EPT;
+    const uint32_t nbar = 1u + (uint32_t)grp;
+    __shared__ int s_epi_item[2][2];
+    __shared__ int s_last[2];
     int acc_iter = 0;
     for (int i = 0;; ++i, ++acc_iter) {
       const int b = acc_iter % D::NACC;
@@ -565,10 +591,10 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
         int item = MODE != 2 ? static_item(i) : read_item(i);
         if (MODE == 2 && item >= 0) mbar_arrive(&s_sched_empty[i % kSchedRing]);
         if (item >= 0 && !mbar_wait(&acc_full[b], acc_phase, abort_flag, a0.err)) item = -1;
-        s_epi_item[i & 1] = item;
+        s_epi_item[grp][i & 1] = item;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      const int item = *reinterpret_cast<volatile int*>(&s_epi_item[i & 1]);
+      asm volatile("bar.sync %0, 128;" ::"r"(nbar) : "memory");
+      const int item = *reinterpret_cast<volatile int*>(&s_epi_item[grp][i & 1]);
       if (item < 0) break;
       const int ph = phase_of(item);
       const Args& A = ph ? a1 : a0;
@@ -576,32 +602,34 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       const Item it = decode_item(A, local_of(item));
       const bool split = A.ksplit > 1;
       float* part = A.partial + ((int64_t)it.slot * A.ksplit + it.split) * (DM * NT);
-      // lane n holds position n's activation scale (gate_up) or output row (down)
+      // lane n holds position pg + n's activation scale (gate_up) or output
+      // row (down)
       float lane_scale = 0.0f;
       int64_t lane_orow = 0;
-      if (lane < it.nrows) {
-        const int64_t pos = (int64_t)it.row0 + lane;
+      if (lane < D::EPT && pg + lane < it.nrows) {
+        const int64_t pos = (int64_t)it.row0 + pg + lane;
         if (ph == 0) lane_scale = pow2f((int)A.xscale[pos]);
         else lane_orow = A.out_rows ? A.out_rows[pos] : pos;
       }
       auto finish = [&](int row, bool valid, float bias, int n, float (&val)[2]) {
         if (MODE != 1 && ph == 0)
-          finish_pair<0>(a0, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+          finish_pair<0>(a0, it, row, valid, bias, pg, n, val, lane_scale, lane_orow, m);
         else if (MODE != 0)
-          finish_pair<1>(a1, it, row, valid, bias, n, val, lane_scale, lane_orow, m);
+          finish_pair<1>(a1, it, row, valid, bias, pg, n, val, lane_scale, lane_orow, m);
       };
       const uint32_t base =
-          tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * D::BUF);
-      // Sums of the pieces (and accumulators) of positions n0p .. n0p +
-      // 2 PAIRS - 1 of half h; columns 4n .. 4n + 7 hold positions n, n + 1.
+          tmem_base + ((uint32_t)((warp & 3) * 32) << 16) + (uint32_t)(b * D::BUF);
+      // Sums of the pieces (and accumulators) of positions pg + n0p .. pg +
+      // n0p + 2 PAIRS - 1 of half h; columns 4n .. 4n + 7 hold positions n,
+      // n + 1.
       auto load_sums = [&](int h, int n0p, float (&sums)[D::PAIRS][2]) {
         uint32_t v[D::PAIRS][D::ACCS][8];
 #pragma unroll
         for (int pp = 0; pp < D::PAIRS; ++pp)
 #pragma unroll
           for (int q = 0; q < D::ACCS; ++q)
-            if (n0p + 2 * pp < NT)
-              tmem_ld8(base + (uint32_t)((h * D::ACCS + q) * D::N + kPieces * (n0p + 2 * pp)),
+            if (n0p + 2 * pp < D::EPT)
+              tmem_ld8(base + (uint32_t)((h * D::ACCS + q) * D::N + kPieces * (pg + n0p + 2 * pp)),
                        v[pp][q]);
         tmem_wait_ld();
 #pragma unroll
@@ -622,26 +650,27 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
       };
       auto store_pair = [&](int h, int row, bool valid, float bias, int n, float (&val)[2]) {
         if (split)
-          *reinterpret_cast<float2*>(part + (h * BM + m) * NT + n) = make_float2(val[0], val[1]);
+          *reinterpret_cast<float2*>(part + (h * BM + m) * NT + pg + n) =
+              make_float2(val[0], val[1]);
         else
           finish(row, valid, bias, n, val);
       };
       if constexpr (D::NACC == 1) {
-        // One accumulator buffer (the widest tiles): the whole tile's sums
-        // (2 x NT per thread) come out of TMEM first and the buffer is handed
-        // back at once, so that the next item's MMAs run while this thread
-        // stores h or y.  The arrive is relaxed: the MMA warp reads none of
-        // the stores.
-        float acc[2][NT];
+        // One accumulator buffer (the widest tiles): the group's sums
+        // (2 x EPT per thread) come out of TMEM first and the buffer is
+        // handed back at once, so that the next item's MMAs run while this
+        // thread stores h or y.  The arrive is relaxed: the MMA warp reads
+        // none of the stores.
+        float acc[2][D::EPT];
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
-          for (int n0p = 0; n0p < NT; n0p += 2 * D::PAIRS) {
+          for (int n0p = 0; n0p < D::EPT; n0p += 2 * D::PAIRS) {
             float sums[D::PAIRS][2];
             load_sums(h, n0p, sums);
 #pragma unroll
             for (int pp = 0; pp < D::PAIRS; ++pp)
-              if (n0p + 2 * pp < NT) {
+              if (n0p + 2 * pp < D::EPT) {
                 acc[h][n0p + 2 * pp] = sums[pp][0];
                 acc[h][n0p + 2 * pp + 1] = sums[pp][1];
               }
@@ -655,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
           const int64_t grow = (int64_t)it.le * A.rows + (valid ? row : 0);
           const float bias = (valid && A.bias) ? A.bias[grow] : 0.0f;
 #pragma unroll
-          for (int n = 0; n < NT; n += 2) {
+          for (int n = 0; n < D::EPT; n += 2) {
             float val[2] = {acc[h][n], acc[h][n + 1]};
             store_pair(h, row, valid, bias, n, val);
           }
@@ -669,12 +698,12 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
           const int64_t grow = (int64_t)it.le * A.rows + (valid ? row : 0);
           const float bias = (valid && A.bias) ? A.bias[grow] : 0.0f;
 #pragma unroll 1
-          for (int n0p = 0; n0p < NT; n0p += 2 * D::PAIRS) {
+          for (int n0p = 0; n0p < D::EPT; n0p += 2 * D::PAIRS) {
             float sums[D::PAIRS][2];
             load_sums(h, n0p, sums);
 #pragma unroll
             for (int pp = 0; pp < D::PAIRS; ++pp)
-              if (n0p + 2 * pp < NT) store_pair(h, row, valid, bias, n0p + 2 * pp, sums[pp]);
+              if (n0p + 2 * pp < D::EPT) store_pair(h, row, valid, bias, n0p + 2 * pp, sums[pp]);
           }
         }
         tc_fence_before();
@@ -684,12 +713,13 @@ __global__ void __launch_bounds__(kThreads, Tile<NT>::CPS)
         if (MODE == 2 && ph == 0) publish_ready(a0, it, m);
       } else {
         // the last of the tile's ksplit items adds the partial sums in split
-        // order and finishes the tile (no waiting: a ticket per tile)
+        // order and finishes the tile (no waiting: a ticket per tile; tiles of
+        // one epilogue group only, the host never splits 60-position tiles)
         __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (m == 0) s_last = atomicAdd(&A.arrivals[it.slot], 1) == A.ksplit - 1;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (s_last) {
+        asm volatile("bar.sync %0, 128;" ::"r"(nbar) : "memory");
+        if (m == 0) s_last[grp] = atomicAdd(&A.arrivals[it.slot], 1) == A.ksplit - 1;
+        asm volatile("bar.sync %0, 128;" ::"r"(nbar) : "memory");
+        if (s_last[grp]) {
           __threadfence();
           if (m == 0) A.arrivals[it.slot] = 0;  // ready for the next forward
           const float* p0 = A.partial + (int64_t)it.slot * A.ksplit * (DM * NT);
@@ -1030,17 +1060,22 @@ cudaError_t mx_make_maps(const Moe& m, ExpertBufs& eb) {
 
 size_t mx_piece_bytes(int64_t rows, int k) { return (size_t)(rows * k) * mx::kPieces; }
 
-int mx_tile_positions(int kind) { return kind < kMxTileKinds - 1 ? 2 << kind : 30; }
+int mx_tile_positions(int kind) {
+  return kind < kMxKind30 ? 2 << kind : kind == kMxKind30 ? 30 : 60;
+}
 
 int mx_tile_kind(const Moe& m, const Groups& g) {
   const int64_t nloc = std::max<int64_t>(1, m.e_end - m.e_begin);
   // positions per tile: the power of two at or above twice the mean rows per
   // local expert, at least 2; at most 16 (two CTAs per SM) while the mean is
-  // at most 8, else 30 (the widest tile whose accumulators fit half the TMEM)
-  if (g.rows > 8 * nloc) return kMxTileKinds - 1;
+  // at most 8, 30 (the widest tile whose accumulators fit half the TMEM) up
+  // to a mean of 30, else 60 (one CTA per SM; the one-launch mode caps the
+  // kind at 30)
+  if (g.rows > 30 * nloc) return kMxKind60;
+  if (g.rows > 8 * nloc) return kMxKind30;
   const int64_t target = (2 * g.rows + nloc - 1) / nloc;
   int i = 0;
-  while (i < kMxTileKinds - 2 && (int64_t(2) << i) < target) ++i;
+  while (i < kMxKind30 - 1 && (int64_t(2) << i) < target) ++i;
   return i;
 }
 
@@ -1051,11 +1086,12 @@ namespace {
 template <int MODE, int NT>
 cudaError_t launch_tiles(const Moe& m, const mx::Args& a0, const mx::Args& a1,
                          const ExpertBufs& eb, int kind, cudaStream_t st) {
+  using D = mx::Tile<NT>;
   auto k = mx::mx_expert_gemm<MODE, NT>;
-  const size_t smem = mx::Tile<NT>::SMEM;
+  const size_t smem = D::SMEM;
   cudaError_t e = set_smem_limit(k, smem);
   if (e != cudaSuccess) return e;
-  return launch_pdl(k, dim3(m.sm_count * mx::Tile<NT>::CPS), dim3(mx::kThreads), smem, st,
+  return launch_pdl(k, dim3(m.sm_count * D::CPS), dim3(D::THREADS), smem, st,
                     *reinterpret_cast<const CUtensorMap*>(m.mx.map_gu),
                     *reinterpret_cast<const CUtensorMap*>(eb.map_xq[kind]),
                     *reinterpret_cast<const CUtensorMap*>(m.mx.map_dn),
@@ -1070,7 +1106,10 @@ cudaError_t launch_mx(const Moe& m, const mx::Args& a0, const mx::Args& a1,
     case 1: return launch_tiles<MODE, 4>(m, a0, a1, eb, kind, st);
     case 2: return launch_tiles<MODE, 8>(m, a0, a1, eb, kind, st);
     case 3: return launch_tiles<MODE, 16>(m, a0, a1, eb, kind, st);
-    default: return launch_tiles<MODE, 30>(m, a0, a1, eb, kind, st);
+    case 4: return launch_tiles<MODE, 30>(m, a0, a1, eb, kind, st);
+    default:
+      if constexpr (MODE != 2) return launch_tiles<MODE, 60>(m, a0, a1, eb, kind, st);
+      return cudaErrorInvalidValue;
   }
 }
 
@@ -1116,6 +1155,7 @@ mx::Args mx_common(const Moe& m, const Groups& g, const ExpertBufs& eb, int rows
 // grouping of g.rows rows can make.
 void set_ksplit(const Moe& m, const Groups& g, int kind, mx::Args& a) {
   const int nt = mx_tile_positions(kind);
+  if (kind == kMxKind60) return;  // two epilogue groups per tile: never split
   const int64_t nloc = std::max<int64_t>(1, m.e_end - m.e_begin);
   const int64_t tiles = std::min<int64_t>(g.rows, nloc + g.rows / nt);
   a.ksplit = choose_ksplit(tiles * a.m_tiles, m.sm_count * 2, a.kchunks, nt);

@@ -328,11 +328,13 @@ def test_tensor_core_path_handles_large_and_tiny_activations(moe32, layer32, pat
         assert err.sum() / np.abs(want[r]).sum() <= MEAN_REL, r
 
 
-@pytest.mark.parametrize("T", [2, 16, 32, 64, 100])
+@pytest.mark.parametrize("T", [2, 16, 32, 64, 100, 300, 1000])
 def test_block_scaled_every_tile_width(moe32, layer32, T):
-    # 32 experts, top-4, mean T / 8 rows per expert: the tile holds 2, 4, 8,
-    # 16 or 32 positions (twice the mean, rounded up to a power of two, at
-    # most 16 while the mean is at most 8)
+    # 32 experts, top-4, mean T / 8 rows per expert: the tile holds 2, 4, 8
+    # or 16 positions (twice the mean, rounded up to a power of two, while
+    # the mean is at most 8), 30 up to a mean of 30, else 60 (T = 1000: two
+    # full 60-position tiles and a short one per expert, whose MMAs are only
+    # as wide as its rows)
     x = synth.tokens(T, 2880, seed=900 + T)
     want, _, _ = oracle.OracleMoe(layer32).forward(x)
     moe32.set_expert_path("tensor_cores")
