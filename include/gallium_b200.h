@@ -147,8 +147,8 @@ typedef struct gb_moe_info {
  * (gpt_oss_q.rs:135-163) and QMoEFFN::load (lfm2moe_q.rs:214-232). */
 int gb_moe_create(const gb_moe_desc* desc, gb_moe** out);
 
-/* Forward: x_dev [T, H] f32 row-major -> out_dev [T, H] f32.  Asynchronous on
- * `stream`.  Replaces the forward methods listed at the top of this file;
+/* Forward: x_dev [T, H] f32 row-major -> out_dev [T, H] f32, both 16-byte
+ * aligned (GB_ERR_INVALID_ARG otherwise).  Asynchronous on `stream`.  Replaces the forward methods listed at the top of this file;
  * the caller flattens (batch, seq) into T and adds the residual itself, as
  * gpt_oss.rs:385 and gpt_oss_q.rs:296 do.  T == 0 is a no-op. */
 int gb_moe_forward(gb_moe* m, const float* x_dev, int64_t T, float* out_dev, void* stream);
@@ -165,7 +165,8 @@ int gb_moe_forward_host(gb_moe* m, const float* x_host, int64_t T, float* out_ho
  *   counts_dev [E] i32, offsets_dev [E+1] i32 (exclusive prefix);
  *   perm_dev [T*k] i32, entry t*k+r at each sorted position (expert
  *   ascending, then token ascending).
- * Synchronises the stream. */
+ * x_dev is 16-byte aligned (GB_ERR_INVALID_ARG otherwise).  Synchronises the
+ * stream. */
 int gb_moe_route(gb_moe* m, const float* x_dev, int64_t T, int32_t* idx_dev, float* w_dev,
                  int32_t* counts_dev, int32_t* offsets_dev, int32_t* perm_dev, void* stream);
 

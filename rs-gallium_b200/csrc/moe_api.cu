@@ -861,6 +861,8 @@ int gb_moe_forward(gb_moe* h, const float* x_dev, int64_t T, float* out_dev, voi
   // With expert parallelism every rank joins the exchanges, even with no tokens.
   if (T == 0 && h->m.ep_size == 1) return GB_OK;
   if (T > 0 && (!x_dev || !out_dev)) return set_err(GB_ERR_INVALID_ARG, "x or out is null");
+  if (T > 0 && ((reinterpret_cast<uintptr_t>(x_dev) | reinterpret_cast<uintptr_t>(out_dev)) & 15))
+    return set_err(GB_ERR_INVALID_ARG, "x and out must be 16-byte aligned");
   if (T > (int64_t)1 << 24) return set_err(GB_ERR_UNSUPPORTED, "T = %lld too large", (long long)T);
   gb::Moe& m = h->m;
   DeviceScope ds(m.device);
@@ -873,33 +875,54 @@ int gb_moe_forward(gb_moe* h, const float* x_dev, int64_t T, float* out_dev, voi
 
 namespace {
 
-// Host buffers of at least 2 kHostChunkMin tokens go through in up to four
-// chunks: chunk i's copy in (h2d stream) overlaps the forward of chunk i - 1
-// and its copy out (d2h stream) the forward of chunk i + 1.  The forward of a
-// chunk is the forward of those tokens (routing and experts are per token),
-// so the result equals the one-chunk forward.  Expert-parallel forwards stay
-// one chunk: every rank must make the same collective calls.
+// Host buffers of at least 2 kHostChunkMin tokens go through in chunks:
+// chunk i's copy in (h2d stream) overlaps the forward of chunk i - 1 and its
+// copy out (d2h stream) the forward of chunk i + 1.  The first and last
+// chunks hold kHostChunkMin tokens (their copies are the ones nothing
+// hides); the rest is split into up to kHostChunks - 2 equal middle chunks
+// of about kHostChunkMid tokens, whose copies in take about as long as the
+// forward before them.  Every chunk holds at least kHostChunkMin tokens.
+// The forward of a chunk is the forward of those tokens (routing and
+// experts are per token; the expert tiles follow the chunk's rows per
+// expert, which at GPT-OSS shapes keeps the one accumulation order of the
+// 30- and 60-position tiles).  Expert-parallel forwards stay one chunk:
+// every rank must make the same collective calls.
 constexpr int64_t kHostChunkMin = 1024;
-constexpr int kHostChunks = 4;
+constexpr int64_t kHostChunkMid = 3072;
+constexpr int kHostChunks = gb::kHostChunksMax;
 
 int forward_host_pipelined(gb::Moe& m, const float* x_host, int64_t T, float* out_host,
                            cudaStream_t st) {
   const int64_t H = m.desc.hidden;
-  const int64_t chunk = std::max<int64_t>(kHostChunkMin, (T + kHostChunks - 1) / kHostChunks);
-  const int n = (int)((T + chunk - 1) / chunk);
+  const int64_t rest = T - 2 * kHostChunkMin;
+  int64_t bound[kHostChunks + 1];
+  int n;
+  if (rest < kHostChunkMin) {  // two halves
+    bound[0] = 0;
+    bound[1] = T / 2;
+    bound[2] = T;
+    n = 2;
+  } else {
+    const int nmid = (int)std::min<int64_t>(kHostChunks - 2,
+                                            (rest + kHostChunkMid - 1) / kHostChunkMid);
+    bound[0] = 0;
+    for (int i = 0; i <= nmid; ++i) bound[1 + i] = kHostChunkMin + rest * i / nmid;
+    bound[nmid + 2] = T;
+    n = nmid + 2;
+  }
   if (!m.h2d) GB_CUDA(cudaStreamCreateWithFlags(&m.h2d, cudaStreamNonBlocking), "copy stream");
   if (!m.d2h) GB_CUDA(cudaStreamCreateWithFlags(&m.d2h, cudaStreamNonBlocking), "copy stream");
   for (auto& e : m.host_ev)
     if (!e) GB_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "chunk event");
   cudaEvent_t start = m.host_ev[0], done = m.host_ev[1];
-  cudaEvent_t* in = m.host_ev + 2;   // [kHostChunks]
-  cudaEvent_t* fwd = m.host_ev + 6;  // [kHostChunks]
+  cudaEvent_t* in = m.host_ev + 2;                 // [kHostChunks]
+  cudaEvent_t* fwd = m.host_ev + 2 + kHostChunks;  // [kHostChunks]
   // the staging buffers may still be in use by work queued earlier on st
   GB_CUDA(cudaEventRecord(start, st), "record chunk event");
   GB_CUDA(cudaStreamWaitEvent(m.h2d, start, 0), "order copy stream");
   GB_CUDA(cudaStreamWaitEvent(m.d2h, start, 0), "order copy stream");
   for (int i = 0; i < n; ++i) {
-    const int64_t t0 = i * chunk, tn = std::min(chunk, T - t0);
+    const int64_t t0 = bound[i], tn = bound[i + 1] - bound[i];
     GB_CUDA(cudaMemcpyAsync(m.ws.x_stage + t0 * H, x_host + t0 * H, sizeof(float) * tn * H,
                             cudaMemcpyHostToDevice, m.h2d),
             "copy x in");
@@ -907,7 +930,7 @@ int forward_host_pipelined(gb::Moe& m, const float* x_host, int64_t T, float* ou
   }
   int rc;
   for (int i = 0; i < n; ++i) {
-    const int64_t t0 = i * chunk, tn = std::min(chunk, T - t0);
+    const int64_t t0 = bound[i], tn = bound[i + 1] - bound[i];
     GB_CUDA(cudaStreamWaitEvent(st, in[i], 0), "wait for chunk in");
     if ((rc = run_forward(m, m.ws.x_stage + t0 * H, tn, m.ws.out_stage + t0 * H, st))) return rc;
     GB_CUDA(cudaEventRecord(fwd[i], st), "record chunk event");
@@ -958,6 +981,8 @@ int gb_moe_route(gb_moe* h, const float* x_dev, int64_t T, int32_t* idx_dev, flo
   if (rc) return rc;
   if (T < 0) return set_err(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
   if (T > 0 && !x_dev) return set_err(GB_ERR_INVALID_ARG, "x is null");
+  if (T > 0 && (reinterpret_cast<uintptr_t>(x_dev) & 15))
+    return set_err(GB_ERR_INVALID_ARG, "x must be 16-byte aligned");
   gb::Moe& m = h->m;
   DeviceScope ds(m.device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);

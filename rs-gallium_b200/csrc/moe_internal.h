@@ -162,6 +162,8 @@ struct Workspace {
   ExpertBufs eb;               // single GPU: T*k positions
 };
 
+constexpr int kHostChunksMax = 8;  // host-buffer forward: chunks per call
+
 struct Moe {
   gb_moe_desc desc{};  // copy; host pointers inside are not kept valid
   int device = 0;
@@ -186,7 +188,7 @@ struct Moe {
   int expert_path = 0;  // gb_expert_path
   // gb_moe_forward_host pipelining: copy streams and chunk events (lazily made)
   cudaStream_t h2d = nullptr, d2h = nullptr;
-  cudaEvent_t host_ev[10] = {};
+  cudaEvent_t host_ev[2 + 2 * kHostChunksMax] = {};
   // Replayed forwards: one CUDA graph per (x, out, T), captured on `cap` the
   // second time a single-GPU forward of at most kGraphMaxTokens tokens meets
   // that triple (a triple seen once sits in `seen`); least recently used

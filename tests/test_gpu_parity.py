@@ -189,9 +189,10 @@ def test_host_path_equals_device_path(moe32):
 
 
 def test_chunked_host_path_equals_device_path(moe32):
-    # 4096 tokens through host buffers run as four overlapped chunks of 1024;
-    # every chunk keeps the widest tile (mean rows per expert > 8), so the
-    # result equals the one-launch device forward bit for bit
+    # 4096 tokens through host buffers run as overlapped chunks of 1024,
+    # 2048 and 1024; every chunk keeps tiles of 30 or 60 positions (mean rows
+    # per expert > 8, one accumulation order), so the result equals the
+    # one-launch device forward bit for bit
     torch = _torch()
     x = synth.tokens(4096, 2880, seed=19)
     dev = moe32.forward(_cuda(x)).cpu().numpy()
@@ -221,6 +222,20 @@ def test_wrong_hidden_is_an_error(moe32):
     torch = _torch()
     with pytest.raises(GalliumError):
         moe32.forward(torch.zeros((2, 100), device="cuda"))
+
+
+def test_misaligned_pointers_are_an_error(moe32):
+    # the kernels copy x rows in 16-byte units: a pointer off that grid is
+    # refused before any launch
+    torch = _torch()
+    buf = torch.zeros((4 * 2880 + 4,), device="cuda")
+    out = torch.empty((4 * 2880 + 4,), device="cuda")
+    with pytest.raises(GalliumError):
+        moe32.forward_raw(buf.data_ptr() + 4, 4, out.data_ptr())
+    with pytest.raises(GalliumError):
+        moe32.forward_raw(buf.data_ptr(), 4, out.data_ptr() + 4)
+    moe32.forward_raw(buf.data_ptr(), 4, out.data_ptr())  # aligned: runs
+    torch.cuda.synchronize()
 
 
 # ---- full-size properties (T = 4096, 20B shape) ------------------------------
