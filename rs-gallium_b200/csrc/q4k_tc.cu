@@ -71,16 +71,25 @@ struct Args {
   int* err;
 };
 
-// kind::f16, A = B = f16, D = f32, K-major, N = BN, M = BM.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// kind::f16, A = B = f16, D = f32, K-major, M = BM; N (bits 17-22) per tile:
+// the tile's positions rounded up to 16 (decode-sized batches fill a tile
+// with a few positions, and a full-width MMA would multiply empty ones).
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BM >> 4) << 24);
+
+__host__ __device__ constexpr uint32_t idesc_for(int rows) {
+  return kIdesc | ((uint32_t)(((rows < 1 ? 1 : rows < BN ? rows : BN) + 15) & ~15) >> 3 << 17);
+}
+static_assert(idesc_for(0) == idesc_for(16) && idesc_for(8) == (kIdesc | (2u << 17)) &&
+                  idesc_for(1000) == (kIdesc | ((uint32_t)(BN >> 3) << 17)),
+              "MMA width: 16..BN in steps of 16");
 
 __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                        uint32_t accumulate) {
+                                        uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -151,7 +160,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
   const bool valid = row < a.rows;
   const float row_f = pow2f(-a.wexp[it.le]);
 #pragma unroll 1
-  for (int c0 = 0; c0 < BN; c0 += 16) {
+  for (int c0 = 0; c0 < it.nrows; c0 += 16) {  // the columns the MMAs wrote
     uint32_t vh[16], vl[16];
     tmem_ld16(hi_addr + (uint32_t)c0, vh);
     tmem_ld16(lo_addr + (uint32_t)c0, vl);
@@ -263,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_hi = tmem_base + (uint32_t)(b * 2 * BN);
         const uint32_t d_lo = d_hi + (uint32_t)BN;
+        const uint32_t idesc = idesc_for(decode_item(a, item).nrows);
         for (int kc = 0; kc < nk; ++kc) {
           if (!mbar_wait(&a_full[stage], phase, abort_flag, a.err) ||
               !mbar_wait(&tma_full[stage], phase, abort_flag, a.err)) {
@@ -279,9 +289,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t dah = sw128_desc(sah + kk * 32), dal = sw128_desc(sal + kk * 32);
             const uint64_t dbh = sw128_desc(sbh + kk * 32), dbl = sw128_desc(sbl + kk * 32);
             const uint32_t acc = (kc | kk) != 0;
-            mma_f16(d_hi, dah, dbh, acc);
-            mma_f16(d_lo, dah, dbl, acc);
-            mma_f16(d_lo, dal, dbh, 1u);
+            mma_f16(d_hi, dah, dbh, idesc, acc);
+            mma_f16(d_lo, dah, dbl, idesc, acc);
+            mma_f16(d_lo, dal, dbh, idesc, 1u);
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
