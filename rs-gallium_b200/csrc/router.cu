@@ -259,6 +259,31 @@ __global__ void __launch_bounds__(256, 2)
     float* xs = sm + (c & 1) * kBuf;
     float* ws = xs + kTileTokens * kTileK;
     const int k0 = c * kTileK, q4 = min(kTileK, H - k0) / 4;
+    if (q4 == kTileK / 4) {
+      // full chunk: thread i copies column 4 (i % 64) of rows i / 64 + 4 n
+      // (256 threads, 64 16-byte pieces per row), no per-copy division
+      const int col = 4 * (threadIdx.x & 63), r0 = threadIdx.x >> 6;
+#pragma unroll
+      for (int n = 0; n < kTileTokens / 4; ++n) {
+        const int r = r0 + 4 * n;
+        const float* src = x + (int64_t)(t0 + (r < nt ? r : 0)) * H + k0 + col;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                         smem_u32(xs + r * kTileK + col)),
+                     "l"(src), "r"(r < nt ? 16 : 0)
+                     : "memory");
+      }
+#pragma unroll
+      for (int n = 0; n < kTileExperts / 4; ++n) {
+        const int r = r0 + 4 * n;
+        const float* src = rw + (int64_t)min(e0 + r, E - 1) * H + k0 + col;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                         smem_u32(ws + r * kTileK + col)),
+                     "l"(src)
+                     : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+      return;
+    }
     for (int i = threadIdx.x; i < (kTileTokens + kTileExperts) * q4; i += blockDim.x) {
       const int r = i / q4, col = 4 * (i - r * q4);
       const float* src;
