@@ -39,17 +39,18 @@
 //   D[m, 4n + p] = 16^-p sum_k w[m, k] q_p[n, k]
 // keeps each piece in its own accumulator column (adding the small pieces
 // into the large sum inside the tensor core would lose their low bits); the
-// epilogue thread of weight row m adds its position's 4 columns.  NT (2..30)
-// follows the batch: few positions per expert in decode, 30 in prefill,
-// where 4 pieces at the E4M3 rate cost the same tensor time as two f16
-// passes.  The four K steps of a stage rotate over ACCS accumulators so
+// epilogue thread of weight row m adds its position's 4 columns.  NT (2..60)
+// follows the batch: few positions per expert in decode, 30 or 60 in
+// prefill, where 4 pieces at the E4M3 rate cost the same tensor time as two
+// f16 passes.  The four K steps of a stage rotate over ACCS accumulators so
 // consecutive MMAs do not wait on one another.
 //
-// Persistent grid (two CTAs per SM) over work items (N tile, M tile, K
-// split), M fastest; when the tiles cannot fill the grid, K is split and the
-// last split to finish adds the partial sums in split order.  Grouped decode
-// batches run gate_up and down as one launch (MODE 2, see the kernel).
-// Warps: 0-3 epilogue (TMEM lanes 0-127), 4 and 6 TMA producers (alternate
+// Persistent grid (two CTAs per SM; one for 60-position tiles) over work
+// items (N tile, M tile, K split), M fastest; when the tiles cannot fill the
+// grid, K is split and the last split to finish adds the partial sums in
+// split order.  Grouped decode batches run gate_up and down as one launch
+// (MODE 2, see the kernel).  Warps: 0-3 epilogue (TMEM lanes 0-127; 8-11 a
+// second group for 60-position tiles), 4 and 6 TMA producers (alternate
 // stages), 5 MMA issuer.  Every mbarrier wait is bounded: on
 // timeout the CTA raises an abort flag, records error bit 2, lets in-flight
 // copies land, frees its TMEM and returns.
