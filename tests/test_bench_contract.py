@@ -1,0 +1,45 @@
+"""bench.py's JSON line contract, checked on the reference arm (host cores only).
+
+The reference arm times the oracle on a bounded sample of the workload and
+prints one JSON line with the same metric, unit and direction as the CUDA arm,
+plus its own cpu_baseline and a zero-copy e2e object.  A small batch keeps
+this a few seconds; the CUDA arm's line is exercised by the GPU runs.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _reference_line(*args):
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    out = subprocess.run(
+        [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", *args],
+        cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, out.stdout
+    return json.loads(lines[0])
+
+
+@pytest.mark.parametrize("model", ["gptoss", "lfm2"])
+def test_reference_arm_prints_one_contract_line(model):
+    d = _reference_line("--model", model, "--tokens", "64", "--steps", "1", "--warmup", "1")
+    for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config", "e2e",
+                "cpu_baseline"):
+        assert key in d, key
+    assert d["impl"] == "reference"
+    assert d["unit"] == "tokens/s" and d["higher_is_better"] is True
+    assert d["n_gpus"] == 1 and d["steps"] == 1 and d["warmup"] == 1
+    assert d["value"] > 0 and d["ms_per_step"] > 0
+    assert "workload" in d["config"] and "model" not in d["config"]
+    assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference")
+    assert cb["cores"] >= 1 and cb["sample"]
