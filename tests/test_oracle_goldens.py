@@ -268,6 +268,33 @@ def _numpy_block(layer, x):
     return out, logits
 
 
+@pytest.mark.parametrize("i", [0, 5, 33, 63])
+def test_one_hot_input_through_one_expert_by_hand(i):
+    # unit scales (E8M0 127), zero biases, x = e_i: gate_up row j is the E2M1
+    # value of its code at column i, so the expert's output follows from the
+    # code table alone (gpt_oss.rs:189-221)
+    layer = synth.gptoss_layer(n_experts=2, hidden=64, inter=32, top_k=1, seed=4)
+    layer.gu_scales[:] = 127
+    layer.dn_scales[:] = 127
+    layer.gu_bias[:] = 0
+    layer.dn_bias[:] = 0
+    H, I = layer.hidden, layer.inter
+
+    def code(blocks, row, col):
+        byte = blocks[row, col // 32, (col % 32) // 2]
+        return E2M1[(byte >> 4) if col % 2 else (byte & 0xF)]
+
+    gu = np.array([code(layer.gu_blocks[1], j, i) for j in range(2 * I)])
+    g, u = np.minimum(gu[0::2], 7.0), np.clip(gu[1::2], -7.0, 7.0)
+    h = g / (1.0 + np.exp(-1.702 * g)) * (u + 1.0)
+    w_dn = np.array([[code(layer.dn_blocks[1], r, c) for c in range(I)] for r in range(H)])
+    want = w_dn @ h
+    x = np.zeros((1, H), np.float32)
+    x[0, i] = 1.0
+    got = oracle.OracleMoe(layer).expert_ffn(1, x)[0]
+    assert np.abs(got - want).max() <= 1e-5 * max(1.0, np.abs(want).max())
+
+
 @pytest.mark.parametrize("skewed", [False, True])
 def test_oracle_block_matches_float64_restatement(skewed):
     layer = synth.gptoss_layer(n_experts=8, hidden=128, inter=96, top_k=2, seed=11, skewed=skewed)
