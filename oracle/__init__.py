@@ -177,8 +177,14 @@ def permute(idx: np.ndarray, n_experts: int):
 
 # ---- whole block ----------------------------------------------------------
 
-def _bf(bits):
-    return (np.ascontiguousarray(bits, np.uint16).astype(np.uint32) << 16).view(np.float32)
+def _bf(a):
+    """A router or bias array as float32: uint16 arrays are bf16 bits; float
+    arrays (as read from F32 / F16 checkpoint tensors) widen exactly."""
+    if a is None:
+        return None
+    if a.dtype == np.uint16:
+        return (np.ascontiguousarray(a).astype(np.uint32) << 16).view(np.float32)
+    return np.ascontiguousarray(a, np.float32)
 
 
 class OracleMoe:
@@ -211,7 +217,7 @@ class OracleMoe:
             keep["gb"] = _bf(gguf.gate_bias)
             keep["ub"] = _bf(gguf.up_bias)
             d.gate_bias, d.up_bias = _p(keep["gb"]), _p(keep["ub"])
-        keep["db"] = _bf(layer.dn_bias)
+        keep["db"] = _bf(layer.dn_bias if gguf is None else gguf.down_bias)
         d.dn_bias = _p(keep["db"])
         self.desc = d
         self._keep = keep

@@ -26,6 +26,25 @@ from ._lib import MoeDesc, MoeInfo, check, load_library
 from .synth import GptOssGgufLayer, GptOssLayer, Lfm2Layer, bf16_bits_to_f32
 
 
+def _as_f32(a: Optional[np.ndarray]) -> Optional[np.ndarray]:
+    """A router or bias array as float32: uint16 arrays are bf16 bits, float16
+    and float32 widen exactly."""
+    if a is None:
+        return None
+    if a.dtype == np.uint16:
+        return bf16_bits_to_f32(a)
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _float_pair(a: Optional[np.ndarray], b: Optional[np.ndarray]):
+    """(a, b, gb_dtype): kept as bf16 bits when every given array is bf16
+    bits (uint16), else both widened to float32."""
+    given = [x for x in (a, b) if x is not None]
+    if given and all(x.dtype == np.uint16 for x in given):
+        return a, b, _lib.GB_DTYPE_BF16
+    return _as_f32(a), _as_f32(b), _lib.GB_DTYPE_F32
+
+
 def _ptr(a: Optional[np.ndarray]) -> Optional[int]:
     if a is None:
         return None
@@ -204,13 +223,14 @@ class OssMoEFFN(MoEBlock):
         d.act_kind = _lib.GB_ACT_GPTOSS_CLAMP
         d.weight_format = _lib.GB_FMT_MXFP4_SPLIT
         d.swiglu_limit = layer.swiglu_limit
-        arrs = [np.ascontiguousarray(a) for a in (
-            layer.router_w, layer.router_b, layer.gu_blocks, layer.gu_scales, layer.dn_blocks,
-            layer.dn_scales, layer.gu_bias, layer.dn_bias)]
+        # Router and biases go over in their stored dtype: bf16 bits (uint16)
+        # as BF16, float32 / float16 as F32.
+        rw, rb, d.router_dtype = _float_pair(layer.router_w, layer.router_b)
+        gub, dnb, d.bias_dtype = _float_pair(layer.gu_bias, layer.dn_bias)
+        arrs = [None if a is None else np.ascontiguousarray(a) for a in (
+            rw, rb, layer.gu_blocks, layer.gu_scales, layer.dn_blocks, layer.dn_scales, gub, dnb)]
         (d.router_weight, d.router_bias, d.gate_up_blocks, d.gate_up_scales, d.down_blocks,
          d.down_scales, d.gate_up_bias, d.down_bias) = [_ptr(a) for a in arrs]
-        d.router_dtype = _lib.GB_DTYPE_BF16
-        d.bias_dtype = _lib.GB_DTYPE_BF16
         return cls(d, arrs + [getattr(d, "_nccl_id_buf", None)])
 
 
@@ -226,12 +246,10 @@ class GptOssQMoEFFN(MoEBlock):
         d.act_kind = _lib.GB_ACT_GPTOSS_CLAMP
         d.weight_format = _lib.GB_FMT_MXFP4_GGUF
         d.swiglu_limit = b.swiglu_limit
-        rw = bf16_bits_to_f32(b.router_w)
-        rb = bf16_bits_to_f32(b.router_b)
-        gb_ = bf16_bits_to_f32(layer.gate_bias)
-        ub = bf16_bits_to_f32(layer.up_bias)
-        db = bf16_bits_to_f32(layer.down_bias)
-        arrs = [np.ascontiguousarray(a) for a in (
+        # Router and biases as float32 (GGUF F32 tensors, or bf16 bits widened).
+        rw, rb = _as_f32(b.router_w), _as_f32(b.router_b)
+        gb_, ub, db = _as_f32(layer.gate_bias), _as_f32(layer.up_bias), _as_f32(layer.down_bias)
+        arrs = [None if a is None else np.ascontiguousarray(a) for a in (
             rw, rb, layer.gate_raw, layer.up_raw, layer.down_raw, gb_, ub, db)]
         (d.router_weight, d.router_bias, d.gate_raw, d.up_raw, d.down_raw, d.gate_bias,
          d.up_bias, d.down_bias) = [_ptr(a) for a in arrs]
@@ -251,8 +269,9 @@ class Lfm2QMoEFFN(MoEBlock):
         d.router_kind = _lib.GB_ROUTER_SIGMOID_TOPK
         d.act_kind = _lib.GB_ACT_SILU
         d.weight_format = _lib.GB_FMT_Q4_K
-        arrs = [np.ascontiguousarray(a) for a in (
-            layer.router_w, layer.sel_bias, layer.gate_raw, layer.up_raw, layer.down_raw)]
+        arrs = [None if a is None else np.ascontiguousarray(a) for a in (
+            _as_f32(layer.router_w), _as_f32(layer.sel_bias), layer.gate_raw, layer.up_raw,
+            layer.down_raw)]
         (d.router_weight, d.selection_bias, d.gate_raw, d.up_raw, d.down_raw) = [
             _ptr(a) for a in arrs]
         d.router_dtype = _lib.GB_DTYPE_F32
