@@ -3,8 +3,9 @@
 Public surface:
   OssMoEFFN, GptOssQMoEFFN, Lfm2QMoEFFN -- the reference's MoE blocks (load / forward)
   synth                     -- seeded synthetic layers and inputs
+  weights                   -- layers read from safetensors / GGUF checkpoint files
   GalliumError              -- raised for any non-OK gb_status
 """
 from ._lib import GalliumError, load_library  # noqa: F401
 from .moe import GptOssQMoEFFN, Lfm2QMoEFFN, MoEBlock, OssMoEFFN, nccl_unique_id  # noqa: F401
-from . import synth  # noqa: F401
+from . import synth, weights  # noqa: F401
