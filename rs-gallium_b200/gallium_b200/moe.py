@@ -48,7 +48,8 @@ def _float_pair(a: Optional[np.ndarray], b: Optional[np.ndarray]):
 def _ptr(a: Optional[np.ndarray]) -> Optional[int]:
     if a is None:
         return None
-    assert a.flags["C_CONTIGUOUS"]
+    if not a.flags["C_CONTIGUOUS"]:
+        raise _lib.GalliumError(_lib.GB_ERR_INVALID_ARG, "weight array is not C-contiguous")
     return a.ctypes.data
 
 
