@@ -236,7 +236,8 @@ int gb_moe_destroy(gb_moe* m);
  * cannot call cudaMalloc when they route -- a candle custom op whose device
  * buffers must all come from candle's allocator, or a serving process that
  * has reserved the device's memory up front.  The caller passes every input
- * and output as device pointers on the current device: x_dev [T, hidden] f32,
+ * and output as device pointers on the current device: x_dev [T, hidden] f32
+ * (hidden a multiple of 32, at most 4096, as for gb_moe_create),
  * router_weight_dev [n_experts, hidden] f32, router_bias_dev [n_experts] f32
  * (NULL = none), selection_bias_dev [n_experts] f32 (sigmoid router only,
  * NULL = zeros), idx_dev [T, top_k] i32, w_dev [T, top_k] f32.  Results equal

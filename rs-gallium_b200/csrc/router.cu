@@ -492,8 +492,10 @@ extern "C" int gb_route_noalloc(const float* x_dev, const float* router_weight_d
                                 void* stream) {
   using namespace gb;
   if (T < 0) return set_error(GB_ERR_INVALID_ARG, "T = %lld < 0", (long long)T);
-  if (hidden <= 0 || hidden % 32 != 0 || hidden > 8192)
-    return set_error(GB_ERR_INVALID_ARG, "hidden %d must be a positive multiple of 32, <= 8192",
+  // hidden <= 4096 as for gb_moe_create; it also keeps the 8-token tile of x
+  // (8 * hidden floats) inside one CTA's shared memory.
+  if (hidden <= 0 || hidden % 32 != 0 || hidden > 4096)
+    return set_error(GB_ERR_INVALID_ARG, "hidden %d must be a positive multiple of 32, <= 4096",
                      hidden);
   if (n_experts < 1 || n_experts > 256)
     return set_error(GB_ERR_INVALID_ARG, "n_experts %d not in 1..256", n_experts);

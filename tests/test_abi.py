@@ -127,6 +127,28 @@ def test_null_handle_calls_are_errors_not_crashes():
     assert lib.gb_moe_get_info(None, ctypes.byref(info)) == _lib.GB_ERR_INVALID_ARG
 
 
+def test_noalloc_routing_checks_arguments_before_any_device_call():
+    """gb_route_noalloc refuses bad sizes (and accepts T = 0) before it touches
+    the device, so these calls need no GPU; the pointers are never read."""
+    lib = _lib.load_library()
+    S = _lib.GB_ROUTER_SOFTMAX_TOPK
+
+    def call(T=8, hidden=2880, E=32, k=4, kind=S, ptr=P):
+        rc = lib.gb_route_noalloc(ptr, ptr, None, None, T, hidden, E, k, kind, ptr, ptr, None)
+        return rc, lib.gb_last_error().decode()
+
+    assert call(T=0)[0] == _lib.GB_OK
+    for kw, needle in ((dict(T=-1), "T = -1"), (dict(hidden=100), "multiple of 32"),
+                       (dict(hidden=4128), "<= 4096"), (dict(E=0), "n_experts"),
+                       (dict(E=300), "n_experts"), (dict(k=9), "top_k"),
+                       (dict(E=2, k=3), "top_k"), (dict(kind=7), "router_kind"),
+                       (dict(ptr=None), "null"), (dict(T=4097, E=8), "4096"),
+                       (dict(T=2049, E=32), "65536")):
+        rc, msg = call(**kw)
+        assert rc == _lib.GB_ERR_INVALID_ARG, (kw, rc, msg)
+        assert needle in msg, (kw, msg)
+
+
 def test_python_errors_carry_status_and_message():
     with pytest.raises(_lib.GalliumError) as ei:
         _lib.check(_create(_full(hidden=100))[0])
