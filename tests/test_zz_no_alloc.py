@@ -5,9 +5,9 @@ device buffers must all come from candle's allocator, or a serving process
 that has reserved the device's memory up front.  gb_route_noalloc serves them
 with its scratch (router logits, per-tile tickets) in a fixed array inside the
 library.  These tests call it through the C ABI and check it against the
-existing routing entry point, gb_moe_route, on two calls in a row (a larger
-batch, then a smaller one, so anything left in the shared scratch by the first
-call would show in the second).
+existing routing entry point, gb_moe_route, on calls in a row (larger
+batches first, then smaller ones, so anything left in the shared scratch by one
+call would show in the next).
 
 The file name sorts last so that, if it fails, a run that stops at the first
 failure has already run every other test.  It builds everything it needs, so
@@ -28,7 +28,7 @@ def setup():
     import torch
 
     layer = synth.gptoss_layer(n_experts=E, hidden=H, inter=64, top_k=K, seed=21)
-    moe = OssMoEFFN.load(layer, device=0, max_tokens=64)
+    moe = OssMoEFFN.load(layer, device=0, max_tokens=128)
     rw = torch.from_numpy(synth.bf16_bits_to_f32(layer.router_w)).cuda()
     rb = torch.from_numpy(synth.bf16_bits_to_f32(layer.router_b)).cuda()
     yield moe, rw, rb
@@ -53,7 +53,8 @@ def test_noalloc_routing_matches_gb_moe_route_on_two_calls_in_a_row(setup):
     import torch
 
     moe, rw, rb = setup
-    for T, seed in ((37, 1), (5, 2)):
+    # 100, 37 and 3 tokens take the three tile shapes (8, 4 and 1 tokens per CTA)
+    for T, seed in ((100, 3), (37, 1), (3, 2)):
         x = torch.from_numpy(synth.tokens(T, H, seed=seed)).cuda()
         ref = moe.route(x)
         idx, w = _noalloc(x, rw, rb, T)
