@@ -3,10 +3,15 @@
 1. The reference's own MXFP4 GGUF decoder goldens, ported one for one from
    crates/gallium-core/src/quantized.rs:917-1010.
 2. Known-answer cases the reference does not pin (safetensors nibble order,
-   Q4_K, activation clamps, router tie-break, grouping order).
+   Q4_K, activation clamps, router tie-break, grouping order), and the Q4_K
+   and GGUF MXFP4 decoders against gguf-py 0.19.0 (llama.cpp's Python
+   implementation of the GGML formats) on the committed fixture
+   tests/golden/ggml_decode_goldens.npz.
 3. The whole-block oracle against an independent float64 numpy restatement
    of gpt_oss.rs:166-231 at a small shape.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -164,6 +169,27 @@ def test_q4k_known_answer():
     for j in range(8):
         q = 3 if j % 2 == 0 else 5
         assert np.all(out[32 * j:32 * j + 32] == np.float32(sc[j] * q - 0.5 * mn[j])), j
+
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                      "ggml_decode_goldens.npz")
+
+
+def test_q4k_decoder_matches_gguf_py_goldens():
+    """Q4_K, pinned bit for bit against gguf-py's decode of the same blocks
+    (tests/golden/make_ggml_goldens.py): zero, subnormal, negative and large
+    f16 d / dmin included."""
+    z = np.load(GOLDEN)
+    got = oracle.q4k_dequant(z["q4k_blocks"].reshape(-1), z["q4k_values"].size)
+    assert np.array_equal(got.view(np.uint32), z["q4k_values"].view(np.uint32))
+
+
+def test_gguf_mxfp4_decoder_matches_gguf_py_goldens():
+    """GGUF MXFP4 for every E8M0 byte 0..255, bit for bit against gguf-py."""
+    z = np.load(GOLDEN)
+    with np.errstate(over="ignore"):
+        got = oracle.mxfp4_gguf_dequant(z["mxfp4_blocks"].reshape(-1), z["mxfp4_values"].size)
+    assert np.array_equal(got.view(np.uint32), z["mxfp4_values"].view(np.uint32))
 
 
 def test_q4k_ragged_is_an_error():

@@ -276,6 +276,59 @@ def test_gguf_version1_header(tmp_path):
     np.testing.assert_array_equal(f.floats("w", (2, 3)), data.reshape(2, 3))
 
 
+def test_gguf_container_agrees_with_gguf_py(tmp_path):
+    """The GGUF reader and writer against gguf-py (llama.cpp's Python GGUF
+    package) in both directions: MXFP4 and Q4_K expert tensors, F32 tensors,
+    metadata of several types."""
+    gguf = pytest.importorskip("gguf")
+    layer = synth.lfm2_layer(n_experts=2, hidden=256, inter=256, top_k=2, seed=9)
+    mx = synth.gptoss_gguf_from_split(
+        synth.gptoss_layer(n_experts=2, hidden=64, inter=64, top_k=2, seed=9))
+    Q4K, MXFP4 = gguf.GGMLQuantizationType.Q4_K, gguf.GGMLQuantizationType.MXFP4
+
+    # gguf-py writes, this module reads.
+    a = str(tmp_path / "by_gguf_py.gguf")
+    w = gguf.GGUFWriter(a, "lfm2moe")
+    w.add_uint32("lfm2moe.expert_count", 2)
+    w.add_uint32("lfm2moe.expert_used_count", 2)
+    w.add_float32("lfm2moe.rope.freq_base", 1e6)
+    w.add_array("lfm2moe.attention.head_count_kv", [0, 8])
+    # quantized tensors go in as their bytes; gguf-py derives the element shape
+    w.add_tensor("blk.0.ffn_gate_exps.weight", layer.gate_raw, raw_dtype=Q4K)
+    w.add_tensor("blk.0.ffn_up_exps.weight", layer.up_raw, raw_dtype=Q4K)
+    w.add_tensor("blk.0.ffn_down_exps.weight", layer.down_raw, raw_dtype=Q4K)
+    w.add_tensor("blk.0.ffn_gate_inp.weight", layer.router_w)
+    w.add_tensor("blk.1.ffn_gate_exps.weight", mx.gate_raw, raw_dtype=MXFP4)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    f = GgufFile(a)
+    assert f.architecture == "lfm2moe"
+    assert f.metadata["lfm2moe.rope.freq_base"] == np.float32(1e6)
+    assert f.metadata["lfm2moe.attention.head_count_kv"] == [0, 8]
+    got = lfm2_layer_from_gguf(f, 0)
+    for name in ("gate_raw", "up_raw", "down_raw", "router_w"):
+        np.testing.assert_array_equal(getattr(got, name), getattr(layer, name), err_msg=name)
+    np.testing.assert_array_equal(f.experts("blk.1.ffn_gate_exps.weight", GGML_MXFP4, (2, 64, 64)),
+                                  mx.gate_raw)
+
+    # This module writes, gguf-py reads.
+    b = str(tmp_path / "by_weights.gguf")
+    md, tensors = _gguf_lfm2(layer, 0, lead=0)
+    write_gguf(b, md, tensors, alignment=64)
+    r = gguf.GGUFReader(b)
+    assert r.alignment == 64
+    t = {x.name: x for x in r.tensors}
+    assert t["blk.0.ffn_gate_exps.weight"].tensor_type == Q4K
+    assert [int(v) for v in t["blk.0.ffn_down_exps.weight"].shape] == [256, 256, 2]  # innermost first
+    np.testing.assert_array_equal(np.asarray(t["blk.0.ffn_up_exps.weight"].data).reshape(-1),
+                                  layer.up_raw.reshape(-1))
+    np.testing.assert_array_equal(np.asarray(t["blk.0.ffn_gate_inp.weight"].data).reshape(2, 256),
+                                  layer.router_w)
+    assert int(r.get_field("lfm2moe.expert_used_count").contents()) == 2
+
+
 def _gguf_lfm2(layer, i, lead=1):
     E, H, I = layer.n_experts, layer.hidden, layer.inter
     p = f"blk.{i}."
