@@ -280,6 +280,34 @@ def test_full_size_rows_do_not_depend_on_the_batch(moe32, big_run):
     assert_parity(part, out[1000:1037], "sub-batch vs full batch")
 
 
+# ---- the 120B-shaped layer at its largest batch (E = 128, T = 8192) ------------
+
+def test_120b_shape_at_8192_tokens():
+    """The headline workload's shape: routing and grouping bit-exact on every
+    token, sampled rows against the oracle, two forwards bit-identical."""
+    torch = _torch()
+    T = 8192
+    layer = synth.gptoss_layer(n_experts=128, seed=0)
+    x = synth.tokens(T, 2880, seed=8192)
+    m = OssMoEFFN.load(layer, device=0, max_tokens=T)
+    try:
+        xc = _cuda(x)
+        out1 = m.forward(xc).cpu().numpy()
+        out2 = m.forward(xc).cpu().numpy()
+        r = m.route(xc)
+        torch.cuda.synchronize()
+    finally:
+        m.close()
+    _, idx, _, counts, _, perm = _route_oracle(layer, x)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx)
+    assert np.array_equal(r["counts"].cpu().numpy(), counts)
+    assert np.array_equal(r["perm"].cpu().numpy(), perm)
+    assert np.array_equal(out1, out2)
+    rows = np.random.default_rng(1).choice(T, 24, replace=False)
+    want, _, _ = oracle.OracleMoe(layer).forward(x[rows])
+    assert_parity(out1[rows], want, "E=128 T=8192 sampled rows")
+
+
 # ---- tensor-core expert path (tcgen05) ---------------------------------------
 
 # "tensor_cores": block-scaled MMA, MXFP4 weights as stored, E4M3 pieces;
