@@ -308,6 +308,32 @@ def test_120b_shape_at_8192_tokens():
     assert_parity(out1[rows], want, "E=128 T=8192 sampled rows")
 
 
+def test_skewed_routing_at_4096_tokens(layer32_skew):
+    """Zipf-skewed router bias (20B shape): the most popular experts take
+    thousands of rows.  Routing bit-exact on every token; sampled rows, half of
+    them routed to the most popular expert, against the oracle."""
+    T = 4096
+    x = synth.tokens(T, 2880, seed=4097)
+    m = OssMoEFFN.load(layer32_skew, device=0, max_tokens=T)
+    try:
+        xc = _cuda(x)
+        out = m.forward(xc).cpu().numpy()
+        r = m.route(xc)
+    finally:
+        m.close()
+    _, idx, _, counts, _, perm = _route_oracle(layer32_skew, x)
+    assert np.array_equal(r["idx"].cpu().numpy(), idx)
+    assert np.array_equal(r["counts"].cpu().numpy(), counts)
+    assert np.array_equal(r["perm"].cpu().numpy(), perm)
+    top = int(np.argmax(counts))
+    assert counts[top] > T // 4  # the skew is real
+    rng = np.random.default_rng(2)
+    hot = rng.choice(np.nonzero((idx == top).any(axis=1))[0], 12, replace=False)
+    rows = np.concatenate([hot, rng.choice(T, 12, replace=False)])
+    want, _, _ = oracle.OracleMoe(layer32_skew).forward(x[rows])
+    assert_parity(out[rows], want, "skewed T=4096 sampled rows")
+
+
 # ---- tensor-core expert path (tcgen05) ---------------------------------------
 
 # "tensor_cores": block-scaled MMA, MXFP4 weights as stored, E4M3 pieces;
