@@ -1,4 +1,4 @@
-"""Expert-parallel data movement, on CPU ranks (gloo, world size 2).
+"""Expert-parallel data movement, on CPU ranks (gloo, world sizes 2 and 4).
 
 Each rank routes its own tokens, sends every routed row to the rank that owns
 the expert, the owner groups what it received by local expert (expert
@@ -93,9 +93,9 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_plan_reproduces_one_device_bit_for_bit():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_plan_reproduces_one_device_bit_for_bit(world):
     with mp.get_context("spawn").Manager() as mgr:
         results = mgr.dict()
         mp.spawn(_worker, args=(world, _free_port(), results), nprocs=world, join=True)
-        assert dict(results) == {0: True, 1: True}
+        assert dict(results) == {r: True for r in range(world)}
