@@ -110,6 +110,7 @@ class MoEBlock:
         if shape[-1] != self.hidden:
             raise _lib.GalliumError(_lib.GB_ERR_SHAPE,
                                     f"last dim {shape[-1]} != hidden {self.hidden}")
+        self._check_device(x)
         xf = x.reshape(-1, self.hidden).to(torch.float32).contiguous()
         T = xf.shape[0]
         if x.is_cuda:
@@ -124,6 +125,14 @@ class MoEBlock:
         return out.reshape(shape).to(x.dtype)
 
     __call__ = forward
+
+    def _check_device(self, x) -> None:
+        """A CUDA input must live on the handle's device: the kernels would
+        otherwise be handed another GPU's addresses."""
+        if x.is_cuda and x.device.index != self.device:
+            raise _lib.GalliumError(
+                _lib.GB_ERR_INVALID_ARG,
+                f"x is on cuda:{x.device.index}, the block on cuda:{self.device}")
 
     def device_status(self, stream: int = 0) -> None:
         """Waits for `stream` and raises if a forward kernel recorded an error."""
@@ -160,6 +169,9 @@ class MoEBlock:
         """Routing of x (CUDA tensor [T, H] f32) as torch tensors on its device."""
         import torch
 
+        self._check_device(x)
+        if not x.is_cuda:
+            raise _lib.GalliumError(_lib.GB_ERR_INVALID_ARG, "route takes a CUDA tensor")
         xf = x.reshape(-1, self.hidden).to(torch.float32).contiguous()
         T = xf.shape[0]
         dev = xf.device

@@ -149,6 +149,25 @@ def test_noalloc_routing_checks_arguments_before_any_device_call():
         assert needle in msg, (kw, msg)
 
 
+def test_block_refuses_inputs_on_another_gpu():
+    """forward / route check the input's device before any kernel sees its
+    address (no handle or GPU needed: the check is on the host)."""
+    from gallium_b200.moe import MoEBlock
+
+    blk = MoEBlock.__new__(MoEBlock)
+    blk.device, blk.hidden = 0, 4
+
+    class OnGpu1:
+        is_cuda = True
+        device = type("dev", (), {"index": 1})()
+
+    with pytest.raises(_lib.GalliumError) as ei:
+        blk._check_device(OnGpu1())
+    assert ei.value.status == _lib.GB_ERR_INVALID_ARG and "cuda:1" in str(ei.value)
+    import torch
+    blk._check_device(torch.zeros(2, 4))  # host tensors go through gb_moe_forward_host
+
+
 def test_python_errors_carry_status_and_message():
     with pytest.raises(_lib.GalliumError) as ei:
         _lib.check(_create(_full(hidden=100))[0])
