@@ -131,11 +131,15 @@ def test_gptoss_block_at_hidden_2880_matches_transformers():
     _close(out, hf_out[0].numpy(), "GPT-OSS block, H = I = 2880", max_abs_bar=1e-2)
 
 
-def test_lfm2_block_matches_transformers_lfm2_moe():
+@pytest.mark.parametrize("E,H,I,K,max_abs_bar", [
+    (8, 256, 256, 4, MAX_ABS),
+    (4, 2048, 1792, 2, 1e-2),  # the LFM2.5 hidden and expert sizes
+])
+def test_lfm2_block_matches_transformers_lfm2_moe(E, H, I, K, max_abs_bar):
     from transformers.models.lfm2_moe.configuration_lfm2_moe import Lfm2MoeConfig
     from transformers.models.lfm2_moe.modeling_lfm2_moe import Lfm2MoeSparseMoeBlock
 
-    E, H, I, K, T = 8, 256, 256, 4, 24
+    T = 24
     layer = synth.lfm2_layer(n_experts=E, hidden=H, inter=I, top_k=K, seed=6)
     layer.sel_bias[:] = np.linspace(-0.02, 0.02, E, dtype=np.float32)
     cfg = Lfm2MoeConfig(hidden_size=H, moe_intermediate_size=I, num_experts=E,
@@ -162,4 +166,4 @@ def test_lfm2_block_matches_transformers_lfm2_moe():
     np.testing.assert_array_equal(idx, hf_idx.numpy())
     # transformers adds 1e-6 to the sum where the reference clamps it below at 1e-20
     np.testing.assert_allclose(w, hf_w.numpy(), rtol=2e-6, atol=1e-7)
-    _close(out, hf_out[0].numpy(), "LFM2.5 block")
+    _close(out, hf_out[0].numpy(), f"LFM2.5 block H={H} I={I}", max_abs_bar=max_abs_bar)
