@@ -50,6 +50,16 @@ class CheckpointError(ValueError):
     """A checkpoint file that cannot be read as the requested MoE layer."""
 
 
+def _block_indices(names: Iterable[str], prefix: str, suffix: str) -> List[int]:
+    out = set()
+    for n in names:
+        if n.startswith(prefix) and n.endswith(suffix):
+            mid = n[len(prefix):len(n) - len(suffix)]
+            if mid.isdigit():
+                out.add(int(mid))
+    return sorted(out)
+
+
 # ---- safetensors --------------------------------------------------------------
 
 _ST_DTYPES = {
@@ -148,6 +158,11 @@ class SafetensorsCheckpoint:
 
     def __contains__(self, name: str) -> bool:
         return name in self._where
+
+    def moe_layers(self) -> List[int]:
+        """Indices i of the layers whose MoE experts are in the checkpoint
+        (``model.layers.{i}.mlp.experts.gate_up_proj_blocks``), ascending."""
+        return _block_indices(self._where, "model.layers.", ".mlp.experts.gate_up_proj_blocks")
 
     def file_of(self, name: str) -> SafetensorsFile:
         try:
@@ -352,6 +367,11 @@ class GgufFile:
     # -- tensors ----------------------------------------------------------------
     def __contains__(self, name: str) -> bool:
         return name in self.tensors
+
+    def moe_blocks(self) -> List[int]:
+        """Indices i of the blocks with merged expert tensors
+        (``blk.{i}.ffn_gate_exps.weight``), ascending; dense blocks are absent."""
+        return _block_indices(self.tensors, "blk.", ".ffn_gate_exps.weight")
 
     def info(self, name: str) -> Tuple[Tuple[int, ...], int, int]:
         try:

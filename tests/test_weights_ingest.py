@@ -87,6 +87,21 @@ def test_safetensors_sharded_gptoss_layer_round_trip(tmp_path, small):
     _same_forward(small, got)
 
 
+def test_moe_layer_listing(tmp_path, small):
+    """Which layers of a file carry MoE experts, for loading a whole model."""
+    t = dict(_st_tensors(small, 3))
+    t.update(_st_tensors(small, 1))
+    t["model.layers.2.mlp.gate_proj.weight"] = ("F32", np.zeros((2, 2), np.float32))
+    p = str(tmp_path / "m.safetensors")
+    write_safetensors(p, t)
+    assert SafetensorsCheckpoint(p).moe_layers() == [1, 3]
+    md, tensors, _ = _gguf_gptoss(small, 5)
+    tensors["blk.0.ffn_gate.weight"] = (GGML_F32, (2, 2), np.zeros((2, 2), np.float32))
+    q = str(tmp_path / "m.gguf")
+    write_gguf(q, dict(md, **{"gpt-oss.block_count": 6}), tensors)
+    assert GgufFile(q).moe_blocks() == [5]
+
+
 def test_safetensors_f32_router_keeps_f32(tmp_path, small):
     p = str(tmp_path / "m.safetensors")
     write_safetensors(p, _st_tensors(small, 0, router_dtype="F32"))
