@@ -108,9 +108,12 @@ class SafetensorsFile:
 
     def _info(self, name: str) -> dict:
         try:
-            return self._infos[name]
+            info = self._infos[name]
         except KeyError:
             raise CheckpointError(f"{self.path}: no tensor {name!r}") from None
+        if not isinstance(info, dict) or not isinstance(info.get("shape", []), list):
+            raise CheckpointError(f"{self.path}: header entry of {name!r} is not a tensor record")
+        return info
 
     def tensor(self, name: str) -> np.ndarray:
         """The tensor as a read-only numpy view of the mapped file (BF16 as uint16 bits)."""

@@ -134,6 +134,13 @@ def test_safetensors_errors(tmp_path, small):
     open(r, "wb").write((1 << 40).to_bytes(8, "little") + b"{}")
     with pytest.raises(CheckpointError, match="header length"):
         SafetensorsCheckpoint(r)
+    # A header entry that is not a tensor record.
+    import struct
+    h = b'{"w": 5}'
+    bad = str(tmp_path / "rec.safetensors")
+    open(bad, "wb").write(struct.pack("<Q", len(h)) + h)
+    with pytest.raises(CheckpointError, match="not a tensor record"):
+        SafetensorsCheckpoint(bad).tensor("w")
     # The same tensor in two shards.
     with pytest.raises(CheckpointError, match="in both"):
         SafetensorsCheckpoint([p, p])
