@@ -37,6 +37,7 @@ tensor.
 from __future__ import annotations
 
 import json
+import math
 import os
 import struct
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple, Union
@@ -111,8 +112,14 @@ class SafetensorsFile:
             info = self._infos[name]
         except KeyError:
             raise CheckpointError(f"{self.path}: no tensor {name!r}") from None
-        if not isinstance(info, dict) or not isinstance(info.get("shape", []), list):
-            raise CheckpointError(f"{self.path}: header entry of {name!r} is not a tensor record")
+        ok = (isinstance(info, dict) and isinstance(info.get("dtype"), str)
+              and isinstance(info.get("shape"), list)
+              and all(isinstance(d, int) and d >= 0 for d in info["shape"])
+              and isinstance(info.get("data_offsets"), list) and len(info["data_offsets"]) == 2
+              and all(isinstance(v, int) for v in info["data_offsets"]))
+        if not ok:
+            raise CheckpointError(f"{self.path}: header entry of {name!r} is not a tensor record "
+                                  f"(dtype, shape, data_offsets)")
         return info
 
     def tensor(self, name: str) -> np.ndarray:
@@ -124,7 +131,7 @@ class SafetensorsFile:
                                   f"not one of {sorted(_ST_DTYPES)}")
         shape = tuple(int(d) for d in info.get("shape", []))
         begin, end = (int(v) for v in info.get("data_offsets", (-1, -1)))
-        nbytes = int(np.prod(shape, dtype=np.int64)) * np.dtype(dt).itemsize
+        nbytes = math.prod(shape) * np.dtype(dt).itemsize  # Python ints: no wrap-around
         if not (0 <= begin <= end <= self._data_len) or end - begin != nbytes:
             raise CheckpointError(f"{self.path}: tensor {name!r} data_offsets [{begin}, {end}) do "
                                   f"not hold {shape} {info['dtype']} inside {self._data_len} data "
@@ -398,7 +405,7 @@ class GgufFile:
             raise CheckpointError(f"{self.path}: tensor {name!r} rows of {inner} elements are not "
                                   f"whole {_GGML_NAMES[ttype]} blocks of {per_block}")
         row_bytes = inner // per_block * block_bytes
-        rows = int(np.prod(dims[:-1], dtype=np.int64)) if len(dims) > 1 else 1
+        rows = math.prod(dims[:-1])  # Python ints: no wrap-around on damaged dims
         begin = self.data_offset + off
         end = begin + rows * row_bytes
         if off % self.alignment or end > self.size:

@@ -489,3 +489,48 @@ def test_gpu_gguf_lfm2_layer_matches_oracle(tmp_path):
     want, widx, _ = oracle.OracleLfm2(layer).forward(x)
     np.testing.assert_array_equal(idx, widx)
     _parity(out, want, "GGUF Q4_K file")
+
+
+def test_damaged_gguf_files_raise_checkpoint_errors_only(tmp_path, small):
+    """Truncations at every 97th byte and 300 single-byte corruptions of the
+    header: each file either loads or raises CheckpointError (never another
+    exception, never a read outside the file)."""
+    md, tensors, _ = _gguf_gptoss(small, 0)
+    path = str(tmp_path / "m.gguf")
+    write_gguf(path, md, tensors)
+    raw = open(path, "rb").read()
+    head_len = GgufFile(path).data_offset
+    rng = np.random.default_rng(11)
+    cases = [raw[:cut] for cut in range(0, len(raw), 97)]
+    for _ in range(300):
+        b = bytearray(raw)
+        b[int(rng.integers(0, head_len))] = int(rng.integers(0, 256))
+        cases.append(bytes(b))
+    q = str(tmp_path / "damaged.gguf")
+    for data in cases:
+        open(q, "wb").write(data)
+        try:
+            gptoss_layer_from_gguf(GgufFile(q), 0)
+        except CheckpointError:
+            pass
+
+
+def test_damaged_safetensors_files_raise_checkpoint_errors_only(tmp_path, small):
+    """The same for safetensors: truncations and single-byte header damage."""
+    path = str(tmp_path / "m.safetensors")
+    write_safetensors(path, _st_tensors(small, 0))
+    raw = open(path, "rb").read()
+    head_len = 8 + int.from_bytes(raw[:8], "little")
+    rng = np.random.default_rng(12)
+    cases = [raw[:cut] for cut in range(0, len(raw), 89)]
+    for _ in range(300):
+        b = bytearray(raw)
+        b[int(rng.integers(0, head_len))] = int(rng.integers(0, 256))
+        cases.append(bytes(b))
+    q = str(tmp_path / "damaged.safetensors")
+    for data in cases:
+        open(q, "wb").write(data)
+        try:
+            gptoss_layer_from_safetensors(SafetensorsCheckpoint(q), _config(small), 0)
+        except CheckpointError:
+            pass
