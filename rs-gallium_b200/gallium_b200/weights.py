@@ -51,6 +51,13 @@ class CheckpointError(ValueError):
     """A checkpoint file that cannot be read as the requested MoE layer."""
 
 
+def _file_size(path: str) -> int:
+    try:
+        return os.path.getsize(path)
+    except OSError as e:
+        raise CheckpointError(f"{path}: cannot open ({e.strerror})") from None
+
+
 def _block_indices(names: Iterable[str], prefix: str, suffix: str) -> List[int]:
     out = set()
     for n in names:
@@ -79,7 +86,7 @@ class SafetensorsFile:
 
     def __init__(self, path: str):
         self.path = path
-        size = os.path.getsize(path)
+        size = _file_size(path)
         if size < 8:
             raise CheckpointError(f"{path}: {size} bytes, too short for a safetensors file")
         with open(path, "rb") as f:
@@ -161,8 +168,13 @@ class SafetensorsCheckpoint:
     @classmethod
     def from_index(cls, index_path: str) -> "SafetensorsCheckpoint":
         """Shards named by a ``model.safetensors.index.json`` weight_map."""
-        with open(index_path) as f:
-            wm = json.load(f).get("weight_map", {})
+        try:
+            with open(index_path) as f:
+                wm = json.load(f).get("weight_map", {})
+        except (OSError, ValueError, AttributeError) as e:
+            raise CheckpointError(f"{index_path}: not a safetensors index ({e})") from None
+        if not isinstance(wm, dict) or not wm:
+            raise CheckpointError(f"{index_path}: no weight_map")
         d = os.path.dirname(os.path.abspath(index_path))
         return cls([os.path.join(d, s) for s in dict.fromkeys(wm.values())])
 
@@ -303,7 +315,7 @@ class GgufFile:
 
     def __init__(self, path: str):
         self.path = path
-        size = os.path.getsize(path)
+        size = _file_size(path)
         if size < 16:
             raise CheckpointError(f"{path}: {size} bytes, too short for GGUF")
         self._mm = np.memmap(path, dtype=np.uint8, mode="r")

@@ -141,6 +141,18 @@ def test_safetensors_errors(tmp_path, small):
     open(bad, "wb").write(struct.pack("<Q", len(h)) + h)
     with pytest.raises(CheckpointError, match="not a tensor record"):
         SafetensorsCheckpoint(bad).tensor("w")
+    # Missing files and a broken index.
+    with pytest.raises(CheckpointError, match="cannot open"):
+        SafetensorsCheckpoint(str(tmp_path / "absent.safetensors"))
+    with pytest.raises(CheckpointError, match="cannot open"):
+        GgufFile(str(tmp_path / "absent.gguf"))
+    idx = tmp_path / "model.safetensors.index.json"
+    idx.write_text("[1, 2]")
+    with pytest.raises(CheckpointError, match="not a safetensors index"):
+        SafetensorsCheckpoint.from_index(str(idx))
+    idx.write_text('{"weight_map": {}}')
+    with pytest.raises(CheckpointError, match="no weight_map"):
+        SafetensorsCheckpoint.from_index(str(idx))
     # The same tensor in two shards.
     with pytest.raises(CheckpointError, match="in both"):
         SafetensorsCheckpoint([p, p])
