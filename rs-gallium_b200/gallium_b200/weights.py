@@ -26,10 +26,10 @@ accepted until a tensor of that type is read).  Tensors are numpy views of an
 ``np.memmap``, so ``OssMoEFFN.load`` and friends upload straight from the
 mapped file without a host copy.
 
-Every format problem (bad magic, truncated file, a tensor outside the file,
-a missing tensor, a shape that disagrees with the layer's sizes, a tensor
-type this library cannot take) raises ``CheckpointError`` naming the file and
-tensor.
+Every problem with the files (a file that cannot be opened, bad magic, a
+truncated or damaged header, a tensor outside the file, a missing tensor, a
+shape that disagrees with the layer's sizes, a tensor type this library
+cannot take) raises ``CheckpointError`` naming the file and tensor.
 
 ``write_safetensors`` / ``write_gguf`` produce files in the same formats
 (used to build test checkpoints; they are not on the forward path).
