@@ -236,8 +236,9 @@ int gb_moe_destroy(gb_moe* m);
  * cannot call cudaMalloc when they route -- a candle custom op whose device
  * buffers must all come from candle's allocator, or a serving process that
  * has reserved the device's memory up front.  The caller passes every input
- * and output as device pointers on the current device: x_dev [T, hidden] f32
- * (hidden a multiple of 32, at most 4096, as for gb_moe_create),
+ * and output as device pointers on the current device: x_dev [T, hidden] f32,
+ * 16-byte aligned (GB_ERR_INVALID_ARG otherwise; hidden a multiple of 32, at
+ * most 4096, as for gb_moe_create),
  * router_weight_dev [n_experts, hidden] f32, router_bias_dev [n_experts] f32
  * (NULL = none), selection_bias_dev [n_experts] f32 (sigmoid router only,
  * NULL = zeros), idx_dev [T, top_k] i32, w_dev [T, top_k] f32.  Results equal
@@ -247,7 +248,9 @@ int gb_moe_destroy(gb_moe* m);
  * exits; requests with T * n_experts > 65536 or T > 4096 are rejected with
  * GB_ERR_INVALID_ARG.  The first call on each device looks up that array's
  * device address (cudaGetSymbolAddress); make that first call before any
- * stream capture.  Every call shares the one array and each call overwrites
+ * stream capture.  The address is kept for the life of the process: after a
+ * cudaDeviceReset of a device, do not call this on that device again.
+ * Every call shares the one array and each call overwrites
  * it: calls that overlap on the GPU (other streams, other threads) race, so
  * serialise them.  Asynchronous on `stream`; calls no cudaMalloc or cudaFree. */
 int gb_route_noalloc(const float* x_dev, const float* router_weight_dev,

@@ -65,6 +65,7 @@ def lib() -> ctypes.CDLL:
             "or_expert_ffn": (c_int, [POINTER(OrDesc), c_int64, P, c_int64, P]),
             "or_act_gptoss": (c_float, [c_float, c_float, c_float]),
             "or_act_silu": (c_float, [c_float, c_float]),
+            "or_exp_rn": (c_float, [c_float]),
             "or_last_error": (c_char_p, []),
         }
         for name, (res, args) in sig.items():
@@ -129,6 +130,12 @@ def act_gptoss(g: float, u: float, limit: float = 7.0) -> float:
 
 def act_silu(g: float, u: float) -> float:
     return lib().or_act_silu(g, u)
+
+
+def exp_rn(x: float) -> float:
+    """exp(x) correctly rounded to f32 (the exp of the router's softmax and
+    sigmoid)."""
+    return lib().or_exp_rn(x)
 
 
 # ---- routing --------------------------------------------------------------

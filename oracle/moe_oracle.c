@@ -210,6 +210,16 @@ static void stable_sort_desc(keyed* v, int64_t n) {
   }
 }
 
+/* exp(x) rounded once to f32.  The reference calls the platform's expf (Rust's
+ * f32::exp); glibc's expf is not always the nearest f32 to exp(x) (on this
+ * machine's glibc it differs from it by one unit in the last place on 170,648
+ * of the 2,240,020,482 f32 arguments in [-104, 90]), so the oracle takes the
+ * correctly rounded value, from the x87 extended-precision expl: the
+ * platform-independent definition of the same arithmetic. */
+static float exp_rn(float x) { return (float)expl((long double)x); }
+
+float or_exp_rn(float x) { return exp_rn(x); }
+
 /* gpt_oss.rs:174-182 with candle's softmax_last_dim (max, exp(v - max), sum,
  * divide), then the weight w / max(total, 1e-9) evaluated in f64 and rounded
  * to f32 by the tensor scale at gpt_oss.rs:223. */
@@ -225,7 +235,7 @@ int or_route_softmax_topk(const float* logits, int64_t t, int64_t e, int64_t k, 
     for (int64_t j = 1; j < e; ++j) mx = l[j] > mx ? l[j] : mx;
     float sum = 0.0f;
     for (int64_t j = 0; j < e; ++j) {
-      p[j] = expf(l[j] - mx);
+      p[j] = exp_rn(l[j] - mx);
       sum += p[j];
     }
     for (int64_t j = 0; j < e; ++j) {
@@ -255,7 +265,7 @@ int or_route_sigmoid_topk(const float* logits, const float* sel_bias, int64_t t,
   float* p = (float*)malloc(sizeof(float) * (size_t)e);
   for (int64_t i = 0; i < t; ++i) {
     for (int64_t j = 0; j < e; ++j) {
-      p[j] = 1.0f / (1.0f + expf(-logits[i * e + j]));
+      p[j] = 1.0f / (exp_rn(-logits[i * e + j]) + 1.0f);
       v[j].idx = (int32_t)j;
       v[j].key = p[j] + (sel_bias ? sel_bias[j] : 0.0f);
     }

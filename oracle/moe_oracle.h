@@ -133,6 +133,10 @@ int64_t or_moe_expert_sample(const or_moe_desc* d, const float* x,
                              const int32_t* experts, const int32_t* ntok,
                              int64_t n_items, float* y_scratch, int n_threads);
 
+/* exp(x) correctly rounded to f32 (the router's exp), for known-answer and
+ * cross-checks. */
+float or_exp_rn(float x);
+
 /* The two expert activations, exposed for known-answer tests. */
 float or_act_gptoss(float gate, float up, float limit);
 float or_act_silu(float gate, float up);

@@ -11,11 +11,18 @@
 // Grid: (token tiles of TT, expert groups).  Each warp computes EPW experts'
 // logits for the TT tokens of its tile; the last CTA of a tile to finish
 // (threadfence + per-tile ticket, no waiting) runs the top-k for that tile.
+//
+// Selection follows the reference's arithmetic to the last bit: softmax over
+// all experts (max, exp, sum in expert order, divide), stable descending
+// sort of the probabilities (equal probabilities keep the lower index), the
+// first k, weights p / max(sum, 1e-9).  exp is the correctly rounded one of
+// exp_f32.h, on the host and on the GPU alike.
 #include <math.h>
 
 #include <mutex>
 
 #include "common.cuh"
+#include "exp_f32.h"
 #include "moe_internal.h"
 #include "ptx.cuh"
 
@@ -50,17 +57,52 @@ __device__ __forceinline__ void route_tail(int t0, int nt, const float* __restri
     float key[kMaxPerLane];
     float raw[kMaxPerLane];
     unsigned taken = 0;
+    if (kind == GB_ROUTER_SIGMOID_TOPK) {
+      // p = 1 / (exp(-l) + 1) (candle's sigmoid); selection by p + bias
 #pragma unroll
-    for (int q = 0; q < kMaxPerLane; ++q) {
-      const int e = lane + 32 * q;
-      float l = e < E ? __ldcg(lg + e) : -INFINITY;
-      raw[q] = l;
-      if (kind == GB_ROUTER_SIGMOID_TOPK && e < E) {
-        const float p = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l)));
-        raw[q] = p;
-        key[q] = __fadd_rn(p, sel_bias ? sel_bias[e] : 0.0f);
-      } else {
-        key[q] = l;
+      for (int q = 0; q < kMaxPerLane; ++q) {
+        const int e = lane + 32 * q;
+        raw[q] = 0.0f;
+        key[q] = -INFINITY;
+        if (e < E) {
+          const float p = __fdiv_rn(1.0f, __fadd_rn(exp_f32(-__ldcg(lg + e)), 1.0f));
+          raw[q] = p;
+          key[q] = __fadd_rn(p, sel_bias ? sel_bias[e] : 0.0f);
+        }
+      }
+    } else {
+      // softmax over all E experts as candle's softmax_last_dim evaluates a
+      // row (gpt_oss.rs:174): the row maximum, exp(l - max), their sum in
+      // expert order, then each exp divided by the sum.  Experts are ranked
+      // by these probabilities, so two logits whose probabilities round to
+      // the same f32 tie and go to the lower index, as in the reference.
+      float l[kMaxPerLane];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < kMaxPerLane; ++q) {
+        const int e = lane + 32 * q;
+        l[q] = e < E ? __ldcg(lg + e) : -INFINITY;
+        mx = fmaxf(mx, l[q]);
+      }
+#pragma unroll
+      for (int s = 16; s >= 1; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, s));
+#pragma unroll
+      for (int q = 0; q < kMaxPerLane; ++q)
+        raw[q] = lane + 32 * q < E ? exp_f32(__fsub_rn(l[q], mx)) : 0.0f;
+      float sum = 0.0f;  // every lane adds the E values in expert order
+#pragma unroll
+      for (int q = 0; q < kMaxPerLane; ++q) {
+        if (32 * q >= E) break;
+        for (int src = 0; src < 32; ++src) {
+          const float v = __shfl_sync(kFullMask, raw[q], src);
+          if (32 * q + src < E) sum = __fadd_rn(sum, v);
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kMaxPerLane; ++q) {
+        const bool in = lane + 32 * q < E;
+        raw[q] = in ? __fdiv_rn(raw[q], sum) : 0.0f;
+        key[q] = in ? raw[q] : -INFINITY;
       }
     }
     float sel_raw[8];
@@ -89,7 +131,7 @@ __device__ __forceinline__ void route_tail(int t0, int nt, const float* __restri
           braw = orw;
         }
       }
-      if (bi >= E) {  // only NaN keys left: take the lowest free index
+      if (bi >= E) {  // only NaN keys left: take the lowest free index, weight 0
         bi = 0;
         for (int e = 0; e < E; ++e) {
           bool used = false;
@@ -99,7 +141,7 @@ __device__ __forceinline__ void route_tail(int t0, int nt, const float* __restri
             break;
           }
         }
-        braw = kind == GB_ROUTER_SIGMOID_TOPK ? 0.0f : lg[bi];
+        braw = 0.0f;
       }
       if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
       sel_idx[r] = bi;
@@ -117,18 +159,15 @@ __device__ __forceinline__ void route_tail(int t0, int nt, const float* __restri
           wo[r] = __fdiv_rn(sel_raw[r], total);
         }
       } else {
-        // softmax over the k selected logits (docs/gpt-oss.md:88-93)
-        const float m = sel_raw[0];
-        float ex[8];
+        // w = p / max(sum of the k selected p, 1e-9), summed in rank order
+        // (gpt_oss.rs:180-182); the reference divides in f64 and rounds to
+        // f32, which equals the f32 division
         float total = 0.0f;
-        for (int r = 0; r < K; ++r) {
-          ex[r] = expf(__fsub_rn(sel_raw[r], m));
-          total = __fadd_rn(total, ex[r]);
-        }
+        for (int r = 0; r < K; ++r) total = __fadd_rn(total, sel_raw[r]);
         total = fmaxf(total, 1e-9f);
         for (int r = 0; r < K; ++r) {
           io[r] = sel_idx[r];
-          wo[r] = __fdiv_rn(ex[r], total);
+          wo[r] = __fdiv_rn(sel_raw[r], total);
         }
       }
     }
@@ -448,7 +487,10 @@ std::mutex g_route_scratch_mu;
 void* g_route_scratch_addr[kNoAllocMaxDevices] = {};
 
 // Device address of g_route_scratch on device `dev` (which must be current),
-// looked up once per device on its first use.
+// looked up once per device on its first use and kept for the life of the
+// process.  A cudaDeviceReset (or any teardown of the device's primary
+// context) invalidates that address; gb_route_noalloc must not be called on a
+// device after such a reset.
 int route_scratch_address(int dev, void** out) {
   if (dev < 0 || dev >= kNoAllocMaxDevices)
     return set_error(GB_ERR_UNSUPPORTED, "device ordinal %d >= %d", dev, kNoAllocMaxDevices);
@@ -506,6 +548,9 @@ extern "C" int gb_route_noalloc(const float* x_dev, const float* router_weight_d
   if (T == 0) return GB_OK;
   if (!x_dev || !router_weight_dev || !idx_dev || !w_dev)
     return set_error(GB_ERR_INVALID_ARG, "x, router_weight, idx and w must not be null");
+  // the kernel reads x rows as 16-byte vectors
+  if (reinterpret_cast<uintptr_t>(x_dev) & 15)
+    return set_error(GB_ERR_INVALID_ARG, "x must be 16-byte aligned");
   if (T * (int64_t)n_experts > kNoAllocMaxLogits || T > kNoAllocMaxTiles)
     return set_error(GB_ERR_INVALID_ARG,
                      "T * n_experts = %lld exceeds the fixed routing scratch of %lld logits "

@@ -143,7 +143,8 @@ def test_noalloc_routing_checks_arguments_before_any_device_call():
                        (dict(E=300), "n_experts"), (dict(k=9), "top_k"),
                        (dict(E=2, k=3), "top_k"), (dict(kind=7), "router_kind"),
                        (dict(ptr=None), "null"), (dict(T=4097, E=8), "4096"),
-                       (dict(T=2049, E=32), "65536")):
+                       (dict(T=2049, E=32), "65536"),
+                       (dict(ptr=P + 4), "16-byte aligned")):
         rc, msg = call(**kw)
         assert rc == _lib.GB_ERR_INVALID_ARG, (kw, rc, msg)
         assert needle in msg, (kw, msg)

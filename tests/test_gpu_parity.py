@@ -112,7 +112,9 @@ def test_routing_is_bit_exact(moe32, layer32, T):
     assert np.array_equal(r["counts"].cpu().numpy(), counts)
     assert np.array_equal(r["offsets"].cpu().numpy(), offsets)
     assert np.array_equal(r["perm"].cpu().numpy(), perm)
-    np.testing.assert_allclose(r["w"].cpu().numpy(), w, rtol=2e-6, atol=1e-7)
+    # the kernel's exp is the oracle's (correctly rounded) and the sums run in
+    # the same order, so the combine weights are bit-identical too
+    assert np.array_equal(r["w"].cpu().numpy(), w)
 
 
 def test_routing_skewed_and_128_experts(moe32_skew, layer32_skew):
@@ -122,6 +124,41 @@ def test_routing_skewed_and_128_experts(moe32_skew, layer32_skew):
     assert np.array_equal(r["idx"].cpu().numpy(), idx)
     assert np.array_equal(r["perm"].cpu().numpy(), perm)
     assert counts[0] > counts[-1]  # skew is visible
+
+
+def _one_hot_router_layer(E, k):
+    """A layer whose f32 router weight is the identity on the first E inputs
+    and has no bias, so a token's logits are exactly its first E inputs."""
+    layer = synth.gptoss_layer(n_experts=E, hidden=64, inter=64, top_k=k, seed=0)
+    rw = np.zeros((E, 64), np.float32)
+    rw[np.arange(E), np.arange(E)] = 1.0
+    layer.router_w, layer.router_b = rw, None
+    return layer
+
+
+def test_routing_near_ties_rank_by_probability():
+    """Logits one unit in the last place apart whose softmax probabilities are
+    equal (gpt_oss.rs:174-182 sorts probabilities, stably): the lower index
+    wins although its logit is the smaller.  One case ties in exp(l - max)
+    (the subtraction rounds both to the same value), one only after the
+    division by the row sum."""
+    import test_router_exp as tre
+
+    for lg in (tre.near_tie_logits(), tre.near_tie_division_logits()):
+        E = lg.shape[0]
+        layer = _one_hot_router_layer(E, 2)
+        x = np.zeros((3, 64), np.float32)
+        x[:, :E] = lg
+        m = OssMoEFFN.load(layer, device=0, max_tokens=4)
+        try:
+            r = m.route(_cuda(x))
+        finally:
+            m.close()
+        idx, w = oracle.route_softmax_topk(x[:, :E], 2)
+        assert np.array_equal(r["idx"].cpu().numpy(), idx), (lg, r["idx"], idx)
+        assert np.array_equal(r["w"].cpu().numpy(), w)
+        hi = int(np.argmax(np.where(np.arange(E) == idx[0, 0], -np.inf, lg)))
+        assert hi != idx[0, 1] and lg[hi] > lg[idx[0, 1]]  # a logit ranking would differ
 
 
 def test_routing_ties_take_the_lower_index():
