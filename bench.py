@@ -7,19 +7,34 @@ Workload (one step = one forward of the layer over one batch):
   with zero bias, bf16 biases ~ N(0, 0.01), clamped SwiGLU (limit 7),
   x ~ N(0, 1) f32, seed 0 -- synthetic weights and inputs (no checkpoint).
   Headline batch: --tokens (default 8192) tokens per GPU; --sweep adds the
-  other batch sizes of the workload (1, 32, 1024) as extra measurements.
+  other batch sizes of the workload as extra measurements.
+
+The same line carries, under "configs", the workload's other layers:
+  20b_balanced / 20b_skewed  the GPT-OSS-20B-shaped block (32 experts,
+                             balanced router, or a Zipf(1.2) router bias) at
+                             4096 tokens, one GPU only;
+  lfm2_q4k                   the LFM2.5-shaped block (hidden 2048, 1792
+                             intermediate, 32 experts, top-4, Q4_K experts,
+                             sigmoid router) at 1, 64 and 2048 tokens per GPU,
+                             expert parallel over the N GPUs when N > 1.
+Each with its own roofline and a parity check against the oracle.
 
 Arms:
   default            the CUDA path through the C ABI (gb_moe_forward on
                      device-resident inputs -> "value"; gb_moe_forward_host
                      with pinned host buffers, copies included -> "e2e").
-  --impl reference   the reference's CPU algorithm (the oracle restatement in
-                     oracle/, built from the reference's Rust sources' logic)
-                     on the host cores, one bounded sample per step.
+  --impl reference   the reference's grouped CPU forward restated in
+                     oracle/cpu_reference.py, on every host core, one whole
+                     batch per step (all tokens routed, every active expert
+                     run).
 
---model lfm2 measures the LFM2.5-shaped layer instead (hidden 2048,
-intermediate 1792, 32 experts, top-4, Q4_K experts, sigmoid router with a
-selection bias, SiLU; d = 2^-11, dmin = 7.5 d).  The default is GPT-OSS.
+Parity: after timing, every rank checks its own forward against the oracle:
+expert indices of every token bit for bit, and the output rows of a sample
+(rows of the busiest expert plus random rows) within max-abs 2e-2 and
+mean-rel 1e-3.  The line's "parity" object has the worst rank's figures; a
+failed check prints the line and exits with status 3.
+
+--model lfm2 measures the LFM2.5-shaped layer as the headline instead.
 
 Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): one process
 per GPU, expert parallel: rank r holds experts [r*E/N, (r+1)*E/N) and its own
@@ -47,28 +62,32 @@ import numpy as np  # noqa: E402
 
 TOPK = 4
 L2_BYTES = 126 * 1024 * 1024
+MAX_ABS, MEAN_REL = 2e-2, 1e-3
 
 
 class Model:
     """Shapes, loader and byte counts of one measured MoE layer."""
 
-    def __init__(self, name, experts):
+    def __init__(self, name, experts, skewed=False):
         self.name = name
+        self.skewed = skewed
         if name == "gptoss":
             self.H, self.I, self.E = 2880, 2880, experts or 128
             self.metric = "MoE-layer tokens/s (GPT-OSS-120B shape, MXFP4)"
-            self.shape = f"gpt-oss-120b-shaped MoE layer, E={self.E}, H=I=2880, top-{TOPK}, MXFP4"
+            size = "120b" if self.E == 128 else "20b" if self.E == 32 else f"E{self.E}"
+            self.shape = (f"gpt-oss-{size}-shaped MoE layer, E={self.E}, H=I=2880, top-{TOPK}, "
+                          f"MXFP4" + (", Zipf(1.2) router bias" if skewed else ""))
         else:
             self.H, self.I, self.E = 2048, 1792, experts or 32
             self.metric = "MoE-layer tokens/s (LFM2.5 shape, Q4_K)"
             self.shape = (f"lfm2.5-shaped MoE layer, E={self.E}, H=2048, I=1792, top-{TOPK}, "
                           f"Q4_K, sigmoid router")
 
-    def layer(self, args):
+    def layer(self, seed):
         from gallium_b200 import synth
         if self.name == "gptoss":
-            return synth.gptoss_layer(n_experts=self.E, seed=args.seed, skewed=args.skewed)
-        return synth.lfm2_layer(n_experts=self.E, seed=args.seed)
+            return synth.gptoss_layer(n_experts=self.E, seed=seed, skewed=self.skewed)
+        return synth.lfm2_layer(n_experts=self.E, seed=seed)
 
     def load(self, layer, device, max_tokens, ep):
         from gallium_b200 import Lfm2QMoEFFN, OssMoEFFN
@@ -82,17 +101,21 @@ class Model:
             return (2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 2, H * I // 2 + H * I // 32 + H * 2)
         return (2 * I * H // 256 * 144, H * I // 256 * 144)
 
+    def oracle(self, layer):
+        import oracle
+        return oracle.OracleMoe(layer) if self.name == "gptoss" else oracle.OracleLfm2(layer)
+
     def route(self, layer, x):
-        """Oracle routing of x: (idx [T, k], oracle object for the experts)."""
+        """Oracle routing of x: idx [T, k]."""
         import oracle
         if self.name == "gptoss":
             rw = (layer.router_w.astype(np.uint32) << 16).view(np.float32)
             rb = (layer.router_b.astype(np.uint32) << 16).view(np.float32)
             idx, _ = oracle.route_softmax_topk(oracle.router_logits(x, rw, rb), TOPK)
-            return idx, oracle.OracleMoe(layer)
+            return idx
         lg = oracle.router_logits(x, layer.router_w, None)
         idx, _ = oracle.route_sigmoid_topk(lg, layer.sel_bias, TOPK)
-        return idx, oracle.OracleLfm2(layer)
+        return idx
 
 
 def parse_args():
@@ -106,9 +129,13 @@ def parse_args():
     ap.add_argument("--experts", type=int, default=0, help="default 128 (gptoss) / 32 (lfm2)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--skewed", action="store_true", help="Zipf(1.2) router bias")
-    ap.add_argument("--sweep", default="1,32,1024",
+    ap.add_argument("--sweep", default="1,8,32,64,1024",
                     help="extra per-GPU batch sizes to measure ('' = none)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the 20B-shaped and LFM2.5-shaped layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--parity-rows", type=int, default=64)
     ap.add_argument("--expert-path", default="auto",
                     choices=["auto", "cuda_cores", "tensor_cores", "tensor_cores_f16"],
                     help="force one expert kernel (gb_moe_set_expert_path)")
@@ -221,14 +248,30 @@ def barrier(world):
         dist.barrier()
 
 
-def allmax(world, v: float) -> float:
+def allreduce(world, vals, op="max"):
+    """Element-wise max or sum of a list of floats over the ranks."""
     if world == 1:
-        return v
+        return list(vals)
     import torch
     import torch.distributed as dist
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    t = torch.tensor(list(vals), dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return [float(v) for v in t.cpu()]
+
+
+def allmax(world, v: float) -> float:
+    return allreduce(world, [v], "max")[0]
+
+
+def new_ep(world, rank):
+    """(rank, size, nccl_id) for a new expert-parallel handle, or None."""
+    if world == 1:
+        return None
+    import torch.distributed as dist
+    from gallium_b200 import nccl_unique_id
+    obj = [nccl_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(obj, src=0)
+    return (rank, world, obj[0])
 
 
 def gpu_uuid(local: int) -> str:
@@ -241,10 +284,6 @@ def gpu_uuid(local: int) -> str:
         return vis.split(",")[local] if vis else str(local)
 
 
-# ---------------------------------------------------------------------------
-# CPU baseline (the oracle restatement of the reference's CPU path)
-# ---------------------------------------------------------------------------
-
 def cpu_cores(requested: int) -> int:
     if requested > 0:
         return requested
@@ -254,66 +293,57 @@ def cpu_cores(requested: int) -> int:
         return os.cpu_count() or 1
 
 
-def cpu_sample(model, layer, x, counts, cores):
-    """Time the reference's per-expert work (dequantise once, f32 GEMMs, the
-    activation; gpt_oss_q.rs:194-246, lfm2moe_q.rs:279-296) for a bounded set
-    of experts with their real token counts, plus the routing of a bounded
-    token sample, and scale both to the whole batch.  Returns (tokens/s,
-    description)."""
-    T = x.shape[0]
-    tr = min(T, 256)
-    t0 = time.perf_counter()
-    _, om = model.route(layer, x[:tr])
-    t_route = time.perf_counter() - t0
-    active = [e for e in range(len(counts)) if counts[e] > 0]
-    m = min(len(active), max(1, cores))
-    sample = np.array(active[:m], np.int32)
-    ntok = np.array([counts[e] for e in sample], np.int32)
-    t0 = time.perf_counter()
-    om.expert_sample(x[: int(ntok.max())], sample, ntok, n_threads=cores)
-    t_exp = time.perf_counter() - t0
-    est = t_exp * len(active) / m + t_route * T / tr
-    desc = (f"{m} of {len(active)} active experts with their routed token counts "
-            f"({int(ntok.sum())} token-expert rows) + routing of {tr} of {T} tokens, "
-            f"scaled to the batch; {t_exp + t_route:.1f} s of CPU work")
-    return T / est, desc
-
-
 # ---------------------------------------------------------------------------
-# arms
+# the reference arm: the reference's grouped CPU forward on the host cores
 # ---------------------------------------------------------------------------
+
+def cpu_reference_steps(layer, x, cores, warmup, steps):
+    """Mean seconds per whole-batch forward of oracle/cpu_reference.py."""
+    from oracle.cpu_reference import CpuReference
+    ref = CpuReference(layer, n_threads=cores)
+    try:
+        times = []
+        for i in range(warmup + steps):
+            t0 = time.perf_counter()
+            ref.forward(x)
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+    finally:
+        ref.close()
+    return statistics.mean(times)
+
 
 def run_reference(args, world, rank):
     if rank != 0:
         return
     from gallium_b200 import synth
-    model = Model(args.model, args.experts)
-    layer = model.layer(args)
+    model = Model(args.model, args.experts, args.skewed)
+    layer = model.layer(args.seed)
     T = args.tokens
     x = synth.tokens(T, model.H, seed=args.seed)
     cores = cpu_cores(args.cpu_threads)
-    idx, _ = model.route(layer, x)
-    counts = np.bincount(idx.ravel(), minlength=model.E)
-    vals, desc = [], ""
-    for i in range(args.warmup + args.steps):
-        v, desc = cpu_sample(model, layer, x, counts, cores)
-        if i >= args.warmup:
-            vals.append(v)
-    value = statistics.mean(vals)
+    sec = cpu_reference_steps(layer, x, cores, args.warmup, args.steps)
+    value = T / sec
+    sample = (f"full batch every step: all {T} tokens routed and every active expert run "
+              f"(grouped forward of gpt_oss_q.rs / lfm2moe_q.rs, OpenBLAS f32 GEMMs)")
     line = {
         "impl": "reference", "metric": model.metric, "value": value, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * T / value, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": 1000.0 * sec, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"{model.shape}, T={T} tokens",
                    "tokens": T, "experts": model.E, "skewed": args.skewed},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": desc},
+                         "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
+
+# ---------------------------------------------------------------------------
+# the CUDA arm
+# ---------------------------------------------------------------------------
 
 def stage_profile(moe, xd, out, T, flush, reps=3):
     """Median per-stage ms over `reps` forwards (CUDA events inside the library)."""
@@ -330,7 +360,7 @@ def stage_profile(moe, xd, out, T, flush, reps=3):
     return {k: statistics.median(v) for k, v in acc.items()}
 
 
-def measured_traffic(T, E, stage, n_gpus):
+def measured_traffic(model, T, stage, n_gpus):
     """DRAM bytes per launch of `stage`'s GEMM from the committed ncu capture
     (profiles/roofline_traffic.json), or None when none matches."""
     path = os.path.join(ROOT, "profiles", "roofline_traffic.json")
@@ -340,8 +370,9 @@ def measured_traffic(T, E, stage, n_gpus):
     except (OSError, ValueError, KeyError):
         return None
     for e in entries:
-        if (e["tokens"] == T and e["experts"] == E and e["stage"] == stage
-                and e.get("n_gpus", 1) == n_gpus):
+        if (e["tokens"] == T and e["experts"] == model.E and e["stage"] == stage
+                and e.get("n_gpus", 1) == n_gpus and e.get("model", "gptoss") == model.name
+                and e.get("skewed", False) == model.skewed):
             return e["dram_read_bytes"] + e["dram_write_bytes"]
     return None
 
@@ -349,7 +380,7 @@ def measured_traffic(T, E, stage, n_gpus):
 def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
     """Roofline of the dominant expert kernel (gate_up or down, or both when
     one launch runs them: the library then records an empty down stage)."""
-    H, I, E, k = model.H, model.I, model.E, TOPK
+    H, I, k = model.H, model.I, TOPK
     rows = T * k
     gu_w, dn_w = model.stage_weight_bytes()
     stage_bytes = {
@@ -365,7 +396,7 @@ def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
         stage_ms["gate_up"] = stage_ms["down"] = 0.0
     dom = max(stage_ms.keys() & stage_bytes.keys(), key=lambda s: stage_ms[s])
     t = stage_ms[dom] / 1e3
-    traffic = measured_traffic(T, E, dom, n_gpus) if model.name == "gptoss" else None
+    traffic = measured_traffic(model, T, dom, n_gpus)
     if T <= 64:
         ach = stage_bytes[dom] / t / 1e9
         return {"kernel": dom, "bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"],
@@ -379,126 +410,200 @@ def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
             "launch_ms": stage_ms[dom], "traffic": traffic}
 
 
+class Arm:
+    """One loaded layer on this rank's GPU, with device buffers for the largest
+    batch it is timed at."""
+
+    def __init__(self, model, layer, local, rank, world, max_T, seed, expert_path="auto"):
+        import torch
+        from gallium_b200 import synth
+        self.model, self.layer, self.rank, self.world = model, layer, rank, world
+        self.moe = model.load(layer, local, max_T, new_ep(world, rank))
+        self.moe.set_expert_path(expert_path)
+        self.x = synth.tokens(max_T, model.H, seed=seed + 1000 * rank)
+        self.xd = torch.from_numpy(self.x).cuda()
+        self.out = torch.empty_like(self.xd)
+        self.stream = torch.cuda.current_stream()
+
+    def fwd(self, T):
+        self.moe.forward_raw(self.xd.data_ptr(), T, self.out.data_ptr(), self.stream.cuda_stream)
+
+    def timed(self, n, T, fwd, flush):
+        """Sum of n CUDA-event step times (ms), L2 flushed before each step."""
+        import torch
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(n)]
+        for s, e in ev:
+            flush()
+            s.record(self.stream)
+            fwd(T)
+            e.record(self.stream)
+        torch.cuda.synchronize()
+        return sum(s.elapsed_time(e) for s, e in ev)
+
+    def touched(self, T):
+        """Experts this rank's GPU runs for a batch of T tokens per rank:
+        routed by any rank's tokens, among its own."""
+        c = self.moe.route(self.xd[:T])["counts"].cpu().numpy().astype(np.int64)
+        if self.world > 1:
+            c = np.array(allreduce(self.world, c.tolist(), "sum"), np.int64)
+            E = self.model.E
+            lo, hi = self.rank * E // self.world, (self.rank + 1) * E // self.world
+            mine = np.zeros(E, np.int64)
+            mine[lo:hi] = c[lo:hi]
+            return int((mine > 0).sum()), c
+        return int((c > 0).sum()), c
+
+    def measure(self, T, steps, warmup, flush, peaks):
+        """Device-resident throughput, stages and roofline at T tokens per GPU."""
+        for _ in range(warmup):
+            self.fwd(T)
+        n_touched, _ = self.touched(T)
+        barrier(self.world)
+        ms = allmax(self.world, self.timed(steps, T, self.fwd, flush)) / steps
+        st = stage_profile(self.moe, self.xd, self.out, T, flush)
+        return {"tokens": T, "value": self.world * T / (ms / 1e3), "ms_per_step": ms,
+                "stages_ms": st,
+                "roofline": roofline_for(self.model, st, T, n_touched, peaks, self.world)}
+
+    def parity(self, T, n_rows, threads):
+        """This rank's forward of T tokens against the oracle; the worst
+        figures over the ranks.  Every rank takes the same collective steps."""
+        import torch
+        self.fwd(T)  # every rank: the expert-parallel forward is collective
+        torch.cuda.synchronize()
+        got_all = self.out[:T].cpu().numpy()
+        self.moe.device_status(self.stream.cuda_stream)
+        idx_gpu = self.moe.route(self.xd[:T])["idx"].cpu().numpy()
+        x = self.x[:T]
+        idx_or = self.model.route(self.layer, x)
+        mism = int((idx_gpu != idx_or).any(axis=1).sum())
+        _, counts = self.touched(T)
+        busiest = int(np.argmax(counts))
+        rng = np.random.default_rng(1234 + self.rank)
+        busy_rows = np.nonzero((idx_or == busiest).any(axis=1))[0][: max(1, n_rows // 4)]
+        rand_rows = rng.choice(T, size=min(T, n_rows), replace=False)
+        rows = np.unique(np.concatenate([busy_rows, rand_rows]))[:n_rows]
+        want, _, _ = self.model.oracle(self.layer).forward(x[rows], n_threads=threads)
+        got = got_all[rows].astype(np.float64)
+        finite = bool(np.all(np.isfinite(got)))
+        err = np.abs(got - want)
+        max_abs = float(err.max()) if finite else float("inf")
+        mean_rel = float(err.sum() / max(np.abs(want).sum(), 1e-30)) if finite else float("inf")
+        mx = allreduce(self.world, [max_abs, mean_rel], "max")
+        sm = allreduce(self.world, [mism, len(rows), T], "sum")
+        ok = sm[0] == 0 and mx[0] <= MAX_ABS and mx[1] <= MEAN_REL
+        return {"rows": int(sm[1]), "tokens_routed": int(sm[2]), "idx_bit_exact": sm[0] == 0,
+                "idx_mismatched_tokens": int(sm[0]), "max_abs": mx[0], "mean_rel": mx[1],
+                "busiest_expert": busiest, "bar": {"max_abs": MAX_ABS, "mean_rel": MEAN_REL},
+                "pass": bool(ok)}
+
+    def close(self):
+        self.moe.close()
+
+
+def run_config(model, seed, local, rank, world, tokens, args, flush, peaks, threads):
+    """Throughput, roofline and parity of one of the workload's other layers."""
+    layer = model.layer(seed)
+    arm = Arm(model, layer, local, rank, world, max(tokens), seed)
+    try:
+        out = []
+        for T in tokens:
+            m = arm.measure(T, args.steps, args.warmup, flush, peaks)
+            if not args.no_parity:
+                m["parity"] = arm.parity(T, min(T, 32), threads)
+            out.append(m)
+        return {"workload": f"{model.shape}, tokens per GPU as listed", "results": out}
+    finally:
+        arm.close()
+
+
 def run_ours(args, world, rank, local):
     import torch
-    from gallium_b200 import nccl_unique_id, synth
     from gallium_b200._lib import check, load_library
 
     lib = load_library()
     peaks = load_peaks()
-    model = Model(args.model, args.experts)
+    cores = cpu_cores(args.cpu_threads)
+    threads = max(1, cores // world)
+    model = Model(args.model, args.experts, args.skewed)
     H = model.H
     T = args.tokens
     sweep = [int(s) for s in args.sweep.split(",") if s.strip()] if args.sweep else []
-    layer = model.layer(args)
-    ep = None
-    if world > 1:
-        import torch.distributed as dist
-        obj = [nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        ep = (rank, world, obj[0])
-    moe = model.load(layer, local, max([T] + sweep), ep)
-    moe.set_expert_path(args.expert_path)
-    # buffers hold the largest batch of the run (T and every sweep size)
-    x = synth.tokens(max([T] + sweep), H, seed=args.seed + 1000 * rank)
-    xd = torch.from_numpy(x).cuda()
-    out = torch.empty_like(xd)
-    x = x[:T]
+    layer = model.layer(args.seed)
+    arm = Arm(model, layer, local, rank, world, max([T] + sweep), args.seed, args.expert_path)
     flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device="cuda")
 
     def flush():
         flush_buf.zero_()
 
-    stream = torch.cuda.current_stream()
-    sp = stream.cuda_stream
-
-    def timed(n, Tn, fwd):
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(n)]
-        for s, e in ev:
-            flush()
-            s.record(stream)
-            fwd(Tn)
-            e.record(stream)
-        torch.cuda.synchronize()
-        return sum(s.elapsed_time(e) for s, e in ev)
-
-    fwd_dev = lambda Tn: moe.forward_raw(xd.data_ptr(), Tn, out.data_ptr(), sp)
     for _ in range(args.warmup):
-        fwd_dev(T)
+        arm.fwd(T)
     torch.cuda.synchronize()
-    counts = moe.route(xd[:T])["counts"].cpu().numpy()
-    n_touched = int((counts > 0).sum())
-    if world > 1:
-        # experts this rank's GPU runs: touched by any rank's tokens, among its own
-        import torch.distributed as dist
-        ct = torch.from_numpy(counts.astype(np.int64)).cuda()
-        dist.all_reduce(ct)
-        lo, hi = rank * model.E // world, (rank + 1) * model.E // world
-        n_touched = int((ct[lo:hi] > 0).sum())
+    n_touched, _ = arm.touched(T)
 
     # ---- timed region: exactly K steps --------------------------------------
     clocks = ClockSampler(gpu_uuid(local))
     clocks.start()
     clocks.wait_first()
-    launches0 = moe.info()["kernel_launches"]
+    launches0 = arm.moe.info()["kernel_launches"]
     barrier(world)
     torch.cuda.synchronize()
-    total_ms = timed(args.steps, T, fwd_dev)
+    total_ms = arm.timed(args.steps, T, arm.fwd, flush)
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
-    launches = moe.info()["kernel_launches"] - launches0
+    launches = arm.moe.info()["kernel_launches"] - launches0
     total_ms = allmax(world, total_ms)
     ms_per_step = total_ms / args.steps
     value = world * T / (ms_per_step / 1e3)
 
     # ---- e2e through the public host-buffer entry point ----------------------
-    xh = torch.from_numpy(x).pin_memory()
+    xh = torch.from_numpy(arm.x[:T]).pin_memory()
     oh = torch.empty_like(xh).pin_memory()
 
     def fwd_host(Tn):
-        check(lib.gb_moe_forward_host(moe.handle, xh.data_ptr(), Tn, oh.data_ptr(), sp))
+        check(lib.gb_moe_forward_host(arm.moe.handle, xh.data_ptr(), Tn, oh.data_ptr(),
+                                      arm.stream.cuda_stream))
 
     fwd_host(T)
     barrier(world)
-    e2e_ms = allmax(world, timed(args.steps, T, fwd_host)) / args.steps
+    e2e_ms = allmax(world, arm.timed(args.steps, T, fwd_host, flush)) / args.steps
     e2e = {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
            "h2d_bytes_per_step": T * H * 4, "d2h_bytes_per_step": T * H * 4,
            "ms_per_step": e2e_ms}
 
     # ---- roofline of the dominant kernel ------------------------------------
-    stages = stage_profile(moe, xd, out, T, flush)
+    stages = stage_profile(arm.moe, arm.xd, arm.out, T, flush)
     roof = roofline_for(model, stages, T, n_touched, peaks, world)
 
     # ---- other batch sizes of the workload -----------------------------------
-    sweep_out = []
-    for Ts in sweep:
-        for _ in range(2):
-            fwd_dev(Ts)
-        c = moe.route(xd[:Ts])["counts"].cpu().numpy()
-        if world > 1:
-            import torch.distributed as dist
-            ct = torch.from_numpy(c.astype(np.int64)).cuda()
-            dist.all_reduce(ct)
-            lo, hi = rank * model.E // world, (rank + 1) * model.E // world
-            c = np.zeros(model.E, np.int64)
-            c[lo:hi] = ct[lo:hi].cpu().numpy()
-        barrier(world)
-        ms = allmax(world, timed(args.steps, Ts, fwd_dev)) / args.steps
-        st = stage_profile(moe, xd, out, Ts, flush)
-        sweep_out.append({"tokens": Ts, "value": world * Ts / (ms / 1e3), "ms_per_step": ms,
-                          "stages_ms": st,
-                          "roofline": roofline_for(model, st, Ts, int((c > 0).sum()), peaks,
-                                                   world)})
+    sweep_out = [arm.measure(Ts, args.steps, 2, flush, peaks) for Ts in sweep]
+
+    # ---- parity against the oracle (every rank, outside the timed region) ----
+    parity = None if args.no_parity else arm.parity(T, args.parity_rows, threads)
+    arm.close()
+
+    # ---- the workload's other layers ----------------------------------------
+    configs = {}
+    if not args.no_configs and args.model == "gptoss":
+        if world == 1:
+            for name, sk in (("20b_balanced", False), ("20b_skewed", True)):
+                configs[name] = run_config(Model("gptoss", 32, sk), args.seed, local, rank, world,
+                                           [4096], args, flush, peaks, threads)
+        configs["lfm2_q4k"] = run_config(Model("lfm2", 32), args.seed, local, rank, world,
+                                         [1, 64, 2048], args, flush, peaks, threads)
 
     # ---- CPU baseline (rank 0, one GPU only) ---------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cores = cpu_cores(args.cpu_threads)
-        v, desc = cpu_sample(model, layer, x, counts, cores)
-        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": desc}
+        sec = cpu_reference_steps(layer, arm.x[:T], cores, 1, 2)
+        cpu = {"value": T / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": (f"full batch: all {T} tokens routed and every active expert run "
+                          f"(oracle/cpu_reference.py), mean of 2 forwards after 1 warm-up")}
 
+    all_parity = [parity] + [r.get("parity") for c in configs.values() for r in c["results"]]
+    ok = all(p is None or p["pass"] for p in all_parity)
     if rank == 0:
         line = {
             "metric": model.metric, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -517,10 +622,12 @@ def run_ours(args, world, rank, local):
             "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": int(launches),
+            "parity": parity,
             "sweep": sweep_out,
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
-    moe.close()
+    return ok
 
 
 def main():
@@ -531,12 +638,16 @@ def main():
         run_reference(args, world, rank)
         return
     world, rank, local = dist_setup(args)
+    ok = True
     try:
-        run_ours(args, world, rank, local)
+        ok = run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
+    if not ok:
+        print("parity check against the oracle failed", file=sys.stderr)
+        sys.exit(3)
 
 
 if __name__ == "__main__":

@@ -66,6 +66,8 @@ def lib() -> ctypes.CDLL:
             "or_act_gptoss": (c_float, [c_float, c_float, c_float]),
             "or_act_silu": (c_float, [c_float, c_float]),
             "or_exp_rn": (c_float, [c_float]),
+            "or_dequant_expert_matrix": (c_int, [POINTER(OrDesc), c_int, c_int64, P, c_int]),
+            "or_act_rows": (None, [POINTER(OrDesc), P, P, c_int64, c_int64, P, c_int]),
             "or_last_error": (c_char_p, []),
         }
         for name, (res, args) in sig.items():

@@ -39,9 +39,15 @@ static const float kMxfp4Table[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,  
 
 float or_e2m1_value(int code) { return kMxfp4Table[code & 15]; }
 
-/* gpt_oss.rs:145-164: scale 2^(e-127) (2f32.powi), e == 0 -> 0.  ldexpf gives
- * the same power of two, including the subnormal 2^-127 and +inf at 2^128. */
-static float split_scale(uint8_t e) { return e == 0 ? 0.0f : ldexpf(1.0f, (int)e - 127); }
+/* gpt_oss.rs:145-164: scale 2^(e-127) (2f32.powi), e == 0 -> 0.  For e >= 1 the
+ * f32 with exponent field e and a zero mantissa is that power of two (e = 255
+ * gives +inf, as 2f32.powi(128) overflows to). */
+static float split_scale(uint8_t e) {
+  const uint32_t bits = (uint32_t)e << 23;
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
 
 int or_mxfp4_split_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int64_t k,
                            float* out) {
@@ -539,6 +545,44 @@ done:
   free(inv);
   free(y);
   return rc;
+}
+
+int or_dequant_expert_matrix(const or_moe_desc* d, int which, int64_t expert, float* out,
+                             int n_threads) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if (expert < 0 || expert >= d->n_experts) return fail(1, "expert %lld out of range", (long long)expert);
+  if (which < 0 || which > 2 || (which == 1 && d->weight_format == OR_FMT_MXFP4_SPLIT))
+    return fail(1, "which = %d not valid for this format", which);
+  const int64_t H = d->hidden, I = d->inter;
+  const int64_t rows = which == 2 ? H : (d->weight_format == OR_FMT_MXFP4_SPLIT ? 2 * I : I);
+  const int64_t kdim = which == 2 ? I : H;
+#ifdef _OPENMP
+  if (n_threads <= 0) n_threads = omp_get_max_threads();
+#else
+  (void)n_threads;
+#endif
+#pragma omp parallel for schedule(static) num_threads(n_threads)
+  for (int64_t o = 0; o < rows; ++o) dequant_row(d, which, expert, o, out + o * kdim);
+  return 0;
+}
+
+void or_act_rows(const or_moe_desc* d, const float* gate, const float* up, int64_t n,
+                 int64_t stride, float* h, int n_threads) {
+  const int64_t I = d->inter;
+#ifdef _OPENMP
+  if (n_threads <= 0) n_threads = omp_get_max_threads();
+#else
+  (void)n_threads;
+#endif
+#pragma omp parallel for schedule(static) num_threads(n_threads)
+  for (int64_t t = 0; t < n; ++t)
+    for (int64_t i = 0; i < I; ++i) {
+      const float g = gate[t * stride + i * (stride == 2 * I ? 2 : 1)];
+      const float u = up[t * stride + i * (stride == 2 * I ? 2 : 1)];
+      h[t * I + i] = d->act_kind == OR_ACT_GPTOSS_CLAMP ? act_gptoss(g, u, d->swiglu_limit)
+                                                         : act_silu(g, u);
+    }
 }
 
 int or_expert_ffn(const or_moe_desc* d, int64_t expert, const float* xs, int64_t n, float* ys) {

@@ -133,6 +133,20 @@ int64_t or_moe_expert_sample(const or_moe_desc* d, const float* x,
                              const int32_t* experts, const int32_t* ntok,
                              int64_t n_items, float* y_scratch, int n_threads);
 
+/* One expert's weight matrix dequantised to f32 row-major [rows, K] with
+ * n_threads OpenMP threads: which 0 = gate_up [2I, H] (interleaved rows,
+ * MXFP4_SPLIT) or gate [I, H] (GGUF / Q4_K), 1 = up [I, H] (GGUF / Q4_K),
+ * 2 = down [H, I].  The dequantise-once step of gpt_oss_q.rs:203-209. */
+int or_dequant_expert_matrix(const or_moe_desc* d, int which, int64_t expert, float* out,
+                             int n_threads);
+
+/* The expert activation over n rows: h[t, i] = act(gate[t*stride + i*s],
+ * up[t*stride + i*s]) with s = 2 when stride == 2I (the interleaved gate_up
+ * product of MXFP4_SPLIT, gate and up pointing at its columns 0 and 1), else
+ * s = 1 (separate gate and up products, stride I).  h is [n, I]. */
+void or_act_rows(const or_moe_desc* d, const float* gate, const float* up, int64_t n,
+                 int64_t stride, float* h, int n_threads);
+
 /* exp(x) correctly rounded to f32 (the router's exp), for known-answer and
  * cross-checks. */
 float or_exp_rn(float x);

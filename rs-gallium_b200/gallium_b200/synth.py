@@ -71,6 +71,14 @@ def zipf_router_bias(n_experts: int, s: float = 1.2) -> np.ndarray:
     return (2.0 * np.log(p)).astype(np.float32)
 
 
+def _uniform_bytes(rng, shape) -> np.ndarray:
+    """Bytes uniform over 0..255 (so both nibbles are uniform over the 16
+    E2M1 codes), writable, in the given shape."""
+    n = int(np.prod(shape))
+    words = rng.bit_generator.random_raw((n + 7) // 8)  # uint64, fresh and writable
+    return words.view(np.uint8)[:n].reshape(shape)
+
+
 def gptoss_layer(n_experts: int = 32, hidden: int = 2880, inter: int = 2880, top_k: int = 4,
                  seed: int = 0, skewed: bool = False, scale_lo: int = 119,
                  scale_hi: int = 125) -> GptOssLayer:
@@ -79,10 +87,10 @@ def gptoss_layer(n_experts: int = 32, hidden: int = 2880, inter: int = 2880, top
     router_w = f32_to_bf16_bits(rng.normal(0.0, 0.02, (E, H)).astype(np.float32))
     rb = zipf_router_bias(E) if skewed else np.zeros(E, np.float32)
     router_b = f32_to_bf16_bits(rb)
-    gu_blocks = rng.integers(0, 256, (E, 2 * I, H // 32, 16), dtype=np.uint8)
+    gu_blocks = _uniform_bytes(rng, (E, 2 * I, H // 32, 16))
     gu_scales = rng.integers(scale_lo, scale_hi + 1, (E, 2 * I, H // 32), dtype=np.uint8)
     gu_bias = f32_to_bf16_bits(rng.normal(0.0, 0.01, (E, 2 * I)).astype(np.float32))
-    dn_blocks = rng.integers(0, 256, (E, H, I // 32, 16), dtype=np.uint8)
+    dn_blocks = _uniform_bytes(rng, (E, H, I // 32, 16))
     dn_scales = rng.integers(scale_lo, scale_hi + 1, (E, H, I // 32), dtype=np.uint8)
     dn_bias = f32_to_bf16_bits(rng.normal(0.0, 0.01, (E, H)).astype(np.float32))
     return GptOssLayer(H, I, E, top_k, 7.0, router_w, router_b, gu_blocks, gu_scales, gu_bias,

@@ -1,9 +1,10 @@
 """bench.py's JSON line contract, checked on the reference arm (host cores only).
 
-The reference arm times the oracle on a bounded sample of the workload and
-prints one JSON line with the same metric, unit and direction as the CUDA arm,
-plus its own cpu_baseline and a zero-copy e2e object.  A small batch keeps
-this a few seconds; the CUDA arm's line is exercised by the GPU runs.
+The reference arm times the reference's grouped CPU forward (restated in
+oracle/cpu_reference.py) on whole batches and prints one JSON line with the
+same metric, unit and direction as the CUDA arm, plus its own cpu_baseline and
+a zero-copy e2e object.  A small layer and batch keep this a few seconds; the
+CUDA arm's line is exercised by the GPU runs.
 """
 import json
 import os
@@ -28,7 +29,8 @@ def _reference_line(*args):
 
 @pytest.mark.parametrize("model", ["gptoss", "lfm2"])
 def test_reference_arm_prints_one_contract_line(model):
-    d = _reference_line("--model", model, "--tokens", "64", "--steps", "1", "--warmup", "1")
+    d = _reference_line("--model", model, "--tokens", "64", "--experts", "8", "--steps", "1",
+                        "--warmup", "1")
     for key in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
                 "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config", "e2e",
                 "cpu_baseline"):
@@ -42,4 +44,4 @@ def test_reference_arm_prints_one_contract_line(model):
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference")
-    assert cb["cores"] >= 1 and cb["sample"]
+    assert cb["cores"] >= 1 and cb["sample"].startswith("full batch")
