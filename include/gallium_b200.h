@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define GB_ABI_VERSION 2
+#define GB_ABI_VERSION 3
 
 typedef enum gb_status {
   GB_OK = 0,
@@ -45,8 +45,9 @@ typedef enum gb_status {
   GB_ERR_NO_MEMORY = 7    /* host or device allocation failed                 */
 } gb_status;
 
-/* Router: GPT-OSS softmax over the top-k logits (gpt_oss.rs:172-182), or the
- * LFM2.5 sigmoid router whose selection bias steers selection only
+/* Router: GPT-OSS softmax over all experts, the k largest probabilities
+ * (equal ones by lower index) renormalised to sum 1 (gpt_oss.rs:172-182), or
+ * the LFM2.5 sigmoid router whose selection bias steers selection only
  * (lfm2moe_q.rs:241-258). */
 typedef enum { GB_ROUTER_SOFTMAX_TOPK = 0, GB_ROUTER_SIGMOID_TOPK = 1 } gb_router_kind;
 
@@ -126,6 +127,12 @@ typedef struct gb_moe_desc {
   int32_t ep_rank;
   int32_t ep_size;
   const uint8_t* nccl_id;
+  /* Expert parallel: how long a host or device wait for the other ranks may
+   * last, in milliseconds (0 = 60000).  A wait that runs out aborts the
+   * communicator and the call returns GB_ERR_TIMEOUT (host) or the device
+   * status reports it; the handle then refuses further forwards and must be
+   * destroyed on every rank. */
+  int32_t ep_timeout_ms;
 } gb_moe_desc;
 
 typedef struct gb_moe gb_moe;
@@ -150,7 +157,11 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out);
 /* Forward: x_dev [T, H] f32 row-major -> out_dev [T, H] f32, both 16-byte
  * aligned (GB_ERR_INVALID_ARG otherwise).  Asynchronous on `stream`.  Replaces the forward methods listed at the top of this file;
  * the caller flattens (batch, seq) into T and adds the residual itself, as
- * gpt_oss.rs:385 and gpt_oss_q.rs:296 do.  T == 0 is a no-op. */
+ * gpt_oss.rs:385 and gpt_oss_q.rs:296 do.  T == 0 is a no-op.
+ * Expert parallel (ep_size > 1): every rank calls the forward the same
+ * number of times (T may differ, 0 included); the call waits on the host
+ * for the other ranks' expert counts, then returns with the rest queued;
+ * T may not exceed the largest max_tokens the ranks gave at create. */
 int gb_moe_forward(gb_moe* m, const float* x_dev, int64_t T, float* out_dev, void* stream);
 
 /* Same with host buffers: copies x in, runs, copies out, and synchronises

@@ -207,7 +207,7 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
   for (int r = 0; r < 8; ++r) {
     if (r < K) {
       e[r] = idx[(int64_t)t * K + r];
-      p[r] = inv[(int64_t)t * K + r];
+      p[r] = inv ? inv[(int64_t)t * K + r] : (int64_t)t * K + r;
       wv[r] = wts[(int64_t)t * K + r];
       order[r] = r;
     }
@@ -305,12 +305,13 @@ cudaError_t launch_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStrea
 }
 
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
-                           cudaStream_t st) {
+                           cudaStream_t st, bool slots) {
   const int H = m.desc.hidden;
   const int threads = 256;
   dim3 grid((unsigned)T, (unsigned)((H / 4 + threads - 1) / threads));
   const int expert_order = m.desc.weight_format != GB_FMT_MXFP4_SPLIT;
-  return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, y, ws.inv, ws.wts, ws.idx, H,
+  return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, y,
+                    slots ? (const int32_t*)nullptr : (const int32_t*)ws.inv, ws.wts, ws.idx, H,
                     m.desc.top_k, expert_order, out);
 }
 

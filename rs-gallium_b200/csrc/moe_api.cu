@@ -208,8 +208,6 @@ int alloc_ws(gb::Moe& m, int64_t T) {
       {(void**)&ws.inv, sizeof(int32_t) * (size_t)(T * K)},
       {(void**)&ws.x_stage, sizeof(float) * (size_t)(T * H)},
       {(void**)&ws.out_stage, sizeof(float) * (size_t)(T * H)},
-      {(void**)&ws.y_back, ep ? sizeof(float) * (size_t)(T * K * H) : 0},
-      {(void**)&ws.send_x, ep ? sizeof(float) * (size_t)(T * K * H) : 0},
   };
   void* base = nullptr;
   size_t bytes = 0;
@@ -665,9 +663,10 @@ cudaError_t set_smem_limit_fn(const void* kern, size_t bytes) {
 }
 
 int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& eb,
-                cudaStream_t st) {
+                cudaStream_t st, bool* stored_return) {
   int rc;
   (void)T;
+  if (stored_return) *stored_return = false;
   if (m.desc.weight_format == GB_FMT_Q4_K && use_q4k_tc(m, g, eb)) {
     GB_CUDA(launch_q4k_tc_gate_up(m, g, x, eb, st), "Q4_K tensor-core gate_up launch");
     if ((rc = mark(m, 3, st))) return rc;
@@ -684,6 +683,8 @@ int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& 
       GB_CUDA(launch_mx_gate_up(m, g, x, eb, kind, st), "block-scaled gate_up launch");
       if ((rc = mark(m, 3, st))) return rc;
       GB_CUDA(launch_mx_down(m, g, eb, kind, st), "block-scaled down launch");
+      // the block-scaled down epilogue stores rows in their return slots
+      if (stored_return && g.ret_dst) *stored_return = true;
     } else {
       GB_CUDA(launch_tc_gate_up(m, g, x, eb, st), "tensor-core gate_up launch");
       if ((rc = mark(m, 3, st))) return rc;
@@ -885,31 +886,34 @@ namespace {
 // The forward of a chunk is the forward of those tokens (routing and
 // experts are per token; the expert tiles follow the chunk's rows per
 // expert, which at GPT-OSS shapes keeps the one accumulation order of the
-// 30- and 60-position tiles).  Expert-parallel forwards stay one chunk:
-// every rank must make the same collective calls.
+// 30- and 60-position tiles).  Expert-parallel ranks chunk by the largest
+// batch of any rank, so that all make the same number of forwards.
 constexpr int64_t kHostChunkMin = 1024;
 constexpr int64_t kHostChunkMid = 3072;
 constexpr int kHostChunks = gb::kHostChunksMax;
 
-int forward_host_pipelined(gb::Moe& m, const float* x_host, int64_t T, float* out_host,
-                           cudaStream_t st) {
-  const int64_t H = m.desc.hidden;
+// Chunk boundaries of a batch of T >= 2 kHostChunkMin tokens; returns the
+// chunk count.
+int host_chunks(int64_t T, int64_t (&bound)[kHostChunks + 1]) {
   const int64_t rest = T - 2 * kHostChunkMin;
-  int64_t bound[kHostChunks + 1];
-  int n;
   if (rest < kHostChunkMin) {  // two halves
     bound[0] = 0;
     bound[1] = T / 2;
     bound[2] = T;
-    n = 2;
-  } else {
-    const int nmid = (int)std::min<int64_t>(kHostChunks - 2,
-                                            (rest + kHostChunkMid - 1) / kHostChunkMid);
-    bound[0] = 0;
-    for (int i = 0; i <= nmid; ++i) bound[1 + i] = kHostChunkMin + rest * i / nmid;
-    bound[nmid + 2] = T;
-    n = nmid + 2;
+    return 2;
   }
+  const int nmid = (int)std::min<int64_t>(kHostChunks - 2,
+                                          (rest + kHostChunkMid - 1) / kHostChunkMid);
+  bound[0] = 0;
+  for (int i = 0; i <= nmid; ++i) bound[1 + i] = kHostChunkMin + rest * i / nmid;
+  bound[nmid + 2] = T;
+  return nmid + 2;
+}
+
+// The chunked host-buffer forward over chunks [bound[i], bound[i + 1]).
+int forward_host_pipelined(gb::Moe& m, const float* x_host, float* out_host, cudaStream_t st,
+                           const int64_t* bound, int n) {
+  const int64_t H = m.desc.hidden;
   if (!m.h2d) GB_CUDA(cudaStreamCreateWithFlags(&m.h2d, cudaStreamNonBlocking), "copy stream");
   if (!m.d2h) GB_CUDA(cudaStreamCreateWithFlags(&m.d2h, cudaStreamNonBlocking), "copy stream");
   for (auto& e : m.host_ev)
@@ -959,8 +963,16 @@ int gb_moe_forward_host(gb_moe* h, const float* x_host, int64_t T, float* out_ho
   DeviceScope ds(m.device);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if ((rc = ensure_ws(m, T, st))) return rc;
-  if (m.ep_size == 1 && T >= 2 * kHostChunkMin) {
-    if ((rc = forward_host_pipelined(m, x_host, T, out_host, st))) return rc;
+  // Expert parallel: every rank must run the same number of forwards, so
+  // the ranks first agree on the largest batch and all chunk like it (each
+  // rank's chunks in proportion to its own T).
+  int64_t t_chunks = T;
+  if (m.ep_size > 1 && (rc = gb::ep_agree_max(m, T, &t_chunks, st))) return rc;
+  if (t_chunks >= 2 * kHostChunkMin) {
+    int64_t bound[kHostChunks + 1];
+    const int n = host_chunks(t_chunks, bound);
+    for (int i = 0; i <= n; ++i) bound[i] = bound[i] * T / t_chunks;
+    if ((rc = forward_host_pipelined(m, x_host, out_host, st, bound, n))) return rc;
   } else {
     const size_t bytes = sizeof(float) * (size_t)(T * m.desc.hidden);
     if (bytes)

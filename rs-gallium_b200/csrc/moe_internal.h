@@ -107,6 +107,13 @@ struct Groups {
   int64_t max_per_expert = 0;         // bound on the rows of one expert
   const int32_t* out_rows = nullptr;  // output row of position p for DOWN (null: p)
   bool grouped = false;  // tile table and activation pieces already written (mx_group)
+  // Expert parallel: the output row of position p belongs in return slot
+  // (ret_dst[p] & 0xffffffff) of rank ret_dst[p] >> 32, at ret_base[rank] +
+  // slot * H (peer addresses).  A down kernel that stores there itself
+  // reports it through run_experts; otherwise rows stay in ExpertBufs::y.
+  const int64_t* ret_dst = nullptr;
+  float* ret_base[8] = {};
+  int64_t ret_slots = 0;  // slots per rank (bounds every store)
 };
 
 // Buffers indexed by grouped position, sized for rows_cap positions.
@@ -157,8 +164,6 @@ struct Workspace {
   int32_t* inv = nullptr;      // [T*k]
   float* x_stage = nullptr;    // [T, H] host-path staging
   float* out_stage = nullptr;  // [T, H]
-  float* y_back = nullptr;     // [T*k, H] expert outputs returned to this rank (expert parallel)
-  float* send_x = nullptr;     // [T*k, H] activation rows in grouped order (expert parallel)
   ExpertBufs eb;               // single GPU: T*k positions
 };
 
@@ -299,9 +304,10 @@ cudaError_t launch_tc_gate_up(const Moe& m, const Groups& g, const float* x, Exp
                               cudaStream_t st);
 cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
 
-// out[t] = sum_r w[t, r] * y[inv[t*k + r]] in the fixed order (expert_gemv.cu).
+// out[t] = sum_r w[t, r] * y[inv[t*k + r]] in the fixed order (expert_gemv.cu);
+// with `slots`, y is indexed by t*k + r directly (expert-parallel return slots).
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
-                           cudaStream_t st);
+                           cudaStream_t st, bool slots = false);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
                                   cudaStream_t st);
 cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,
@@ -316,6 +322,10 @@ int32_t* ep_meta(Moe& m);
 int ep_init(Moe& m, const uint8_t* nccl_id);
 void ep_destroy(Moe& m);
 int ep_forward(Moe& m, const float* x, int64_t T, float* out, cudaStream_t st);
+// Tokens per rank an expert-parallel forward may hold (0 without EP).
+int64_t ep_capacity(const Moe& m);
+// Largest v over the ranks (a collective: every rank calls it).
+int ep_agree_max(Moe& m, int64_t v, int64_t* out, cudaStream_t st);
 
 // Allocates the grouped-position buffers for `rows` positions (and their TMA
 // descriptors when the tensor-core path applies); frees the previous ones.
@@ -323,8 +333,10 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows);
 void free_expert_bufs(ExpertBufs& eb);
 
 // Runs the expert products for a grouped view, choosing the kernels for T
-// (local tokens) and the handle's expert path.  Returns a gb_status.
+// (local tokens) and the handle's expert path.  Returns a gb_status.  With
+// g.ret_dst set, *stored_return tells whether the down kernel stored the
+// output rows in their return slots itself.
 int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& eb,
-                cudaStream_t st);
+                cudaStream_t st, bool* stored_return = nullptr);
 
 }  // namespace gb

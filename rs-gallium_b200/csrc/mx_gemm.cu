@@ -142,6 +142,12 @@ struct Args {
   int out_stride;             // I (GATE_UP) or H (DOWN)
   float* out_y;               // DOWN: y [rows][H], row = out_rows[position] (or position)
   const int32_t* out_rows;
+  // DOWN, expert parallel: position p's row goes to return slot
+  // ret_dst[p] & 0xffffffff of rank ret_dst[p] >> 32, at ret_base[rank] +
+  // slot * H (peer memory); out_y is then unused
+  const int64_t* ret_dst;
+  float* ret_base[8];
+  int64_t ret_slots;
   int* err;                   // error bits (2: a wait timed out)
   // split K: each (N tile, M tile) runs as ksplit items over consecutive
   // ranges of K chunks; partial sums meet in `partial`, the last to arrive
@@ -207,9 +213,9 @@ __device__ __forceinline__ void finish_pair(const Args& a, const Item& it, int r
     const float f = pow2f(a.in_exp);
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const int64_t orow = __shfl_sync(kFullMask, lane_orow, n + u);
-      if (valid && pg + n + u < it.nrows)
-        a.out_y[orow * a.out_stride + row] = __fadd_rn(__fmul_rn(val[u], f), bias);
+      // lane_orow carries the address of the position's output row
+      float* orow = reinterpret_cast<float*>(__shfl_sync(kFullMask, lane_orow, n + u));
+      if (valid && pg + n + u < it.nrows && orow) orow[row] = __fadd_rn(__fmul_rn(val[u], f), bias);
     }
   }
 }
@@ -603,14 +609,31 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
       const Item it = decode_item(A, local_of(item));
       const bool split = A.ksplit > 1;
       float* part = A.partial + ((int64_t)it.slot * A.ksplit + it.split) * (DM * NT);
-      // lane n holds position pg + n's activation scale (gate_up) or output
-      // row (down)
+      // lane n holds position pg + n's activation scale (gate_up) or the
+      // address of its output row (down: local y, or the return slot on the
+      // token's own rank)
       float lane_scale = 0.0f;
       int64_t lane_orow = 0;
       if (lane < D::EPT && pg + lane < it.nrows) {
         const int64_t pos = (int64_t)it.row0 + pg + lane;
-        if (ph == 0) lane_scale = pow2f((int)A.xscale[pos]);
-        else lane_orow = A.out_rows ? A.out_rows[pos] : pos;
+        if (ph == 0) {
+          lane_scale = pow2f((int)A.xscale[pos]);
+        } else if (A.ret_dst) {
+          const int64_t dst = A.ret_dst[pos];
+          const int rk = (int)(dst >> 32);
+          const int64_t sl = dst & 0xffffffffll;
+          float* base = nullptr;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q == rk) base = A.ret_base[q];
+          if (dst >= 0 && base && sl < A.ret_slots)
+            lane_orow = reinterpret_cast<int64_t>(base + sl * A.out_stride);
+          else
+            atomicOr(A.err, 1);  // no valid slot: the row is dropped
+        } else {
+          lane_orow = reinterpret_cast<int64_t>(
+              A.out_y + (A.out_rows ? (int64_t)A.out_rows[pos] : pos) * A.out_stride);
+        }
       }
       auto finish = [&](int row, bool valid, float bias, int n, float (&val)[2]) {
         if (MODE != 1 && ph == 0)
@@ -759,6 +782,9 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
         }
       }
     }
+    // rows stored in peers' return slots are visible system-wide before this
+    // kernel ends (the return flags are released after it)
+    if (MODE != 0 && a1.ret_dst) __threadfence_system();
   }
 
   tc_fence_before();
@@ -1187,6 +1213,9 @@ mx::Args down_args(const Moe& m, const Groups& g, ExpertBufs& eb, int kind) {
   a.in_exp = m.mx.h_exp;
   a.out_y = eb.y;
   a.out_rows = g.out_rows;
+  a.ret_dst = g.ret_dst;
+  for (int q = 0; q < 8; ++q) a.ret_base[q] = g.ret_base[q];
+  a.ret_slots = g.ret_slots;
   a.out_stride = d.hidden;
   set_ksplit(m, g, kind, a);
   return a;

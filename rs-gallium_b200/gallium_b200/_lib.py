@@ -83,6 +83,7 @@ class MoeDesc(ctypes.Structure):
         ("ep_rank", c_int32),
         ("ep_size", c_int32),
         ("nccl_id", c_void_p),
+        ("ep_timeout_ms", c_int32),
     ]
 
 

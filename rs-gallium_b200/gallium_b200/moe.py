@@ -208,7 +208,9 @@ def nccl_unique_id() -> bytes:
 
 
 def _base_desc(hidden, inter, n_experts, top_k, device, max_tokens, ep=None) -> MoeDesc:
-    """ep: None (one GPU) or (rank, size, nccl_id bytes) for expert parallelism."""
+    """ep: None (one GPU) or (rank, size, nccl_id bytes[, timeout_ms]) for expert
+    parallelism; timeout_ms bounds every wait for the other ranks (default
+    60000)."""
     d = MoeDesc()
     d.struct_size = ctypes.sizeof(MoeDesc)
     d.hidden, d.inter, d.n_experts, d.top_k = hidden, inter, n_experts, top_k
@@ -216,8 +218,9 @@ def _base_desc(hidden, inter, n_experts, top_k, device, max_tokens, ep=None) -> 
     d.max_tokens = max_tokens
     d.ep_size = 1
     if ep is not None:
-        rank, size, nid = ep
+        rank, size, nid = ep[:3]
         d.ep_rank, d.ep_size = rank, size
+        d.ep_timeout_ms = int(ep[3]) if len(ep) > 3 else 0
         d._nccl_id_buf = (ctypes.c_uint8 * 128).from_buffer_copy(nid)
         d.nccl_id = ctypes.addressof(d._nccl_id_buf)
     return d
