@@ -158,7 +158,8 @@ struct Ep {
   int32_t* slot = nullptr;      // [Tc][size] row slot of token t at each destination, or -1
   int32_t* nrows = nullptr;     // [size] rows this rank sends to each destination
   unsigned* tickets = nullptr;  // [2] last-CTA tickets of the dispatch and return kernels
-  int32_t* host = nullptr;      // pinned: [E] received counts
+  int32_t* host = nullptr;      // mapped pinned: [max(E, 2)] received counts (or one int64)
+  int32_t* host_dev = nullptr;  // its device address
   int32_t* perm2 = nullptr;     // [r_cap] received row of each position
   int64_t* ret2 = nullptr;      // [r_cap] (source rank << 32) | return slot of each position
   int64_t r_cap = 0;
@@ -501,6 +502,23 @@ __global__ void __launch_bounds__(kDispatchThreads)
   if (threadIdx.x == 0) *ticket = 0;
 }
 
+// Small device <-> host transfers that must not queue behind bulk copies on
+// the copy engines: a kernel stores into mapped pinned host memory, or
+// writes a value passed as its argument.
+__global__ void ep_to_host_kernel(const int32_t* __restrict__ src, int n,
+                                  volatile int32_t* __restrict__ host) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) host[i] = src[i];
+  __threadfence_system();
+}
+
+__global__ void ep_set_i64_kernel(int64_t* __restrict__ dst, int64_t v) { *dst = v; }
+
+__global__ void ep_i64_to_host_kernel(const int64_t* __restrict__ src,
+                                      volatile int64_t* __restrict__ host) {
+  *host = *src;
+  __threadfence_system();
+}
+
 // Bounded wait for every rank's return flag of this epoch.
 __global__ void ep_wait_kernel(const int* __restrict__ flags, int N, int epoch,
                                uint64_t timeout_ns, int32_t* __restrict__ err) {
@@ -627,7 +645,9 @@ int ep_init(Moe& m, const uint8_t* id_bytes) {
   GB_CU(cudaMalloc(&ep->nrows, sizeof(int32_t) * std::max(N, 2)), "EP row counts");
   GB_CU(cudaMalloc(&ep->tickets, sizeof(unsigned) * 2), "EP tickets");
   GB_CU(cudaMemset(ep->tickets, 0, sizeof(unsigned) * 2), "EP tickets");
-  GB_CU(cudaMallocHost(&ep->host, sizeof(int32_t) * std::max(E, 2)), "EP pinned counts");
+  GB_CU(cudaHostAlloc(&ep->host, sizeof(int32_t) * std::max(E, 2), cudaHostAllocMapped),
+        "EP mapped counts");
+  GB_CU(cudaHostGetDevicePointer(&ep->host_dev, ep->host, 0), "EP mapped counts");
   GB_CU(cudaDeviceSynchronize(), "EP setup");
   return GB_OK;
 }
@@ -639,16 +659,16 @@ int ep_agree_max(Moe& m, int64_t v, int64_t* out, cudaStream_t st) {
   if (ep->broken)
     return set_error(GB_ERR_NCCL, "the expert-parallel communicator was aborted by an earlier "
                                   "failure; destroy and recreate the handle on every rank");
-  int64_t* h = reinterpret_cast<int64_t*>(ep->host);  // at least 2 ints of pinned space
-  h[0] = v;
   int64_t* dev = reinterpret_cast<int64_t*>(ep->nrows);  // free between forwards
-  GB_CU(cudaMemcpyAsync(dev, h, sizeof(int64_t), cudaMemcpyHostToDevice, st), "agree on T");
+  ep_set_i64_kernel<<<1, 1, 0, st>>>(dev, v);
+  GB_CU(cudaGetLastError(), "agree on T");
   int rc = nccl_settle(ep, g_nccl.AllReduce(dev, dev, 1, ncclInt64, ncclMax, ep->comm, st),
                        "agree on T");
   if (rc) return rc;
-  GB_CU(cudaMemcpyAsync(h, dev, sizeof(int64_t), cudaMemcpyDeviceToHost, st), "agree on T");
+  ep_i64_to_host_kernel<<<1, 1, 0, st>>>(dev, reinterpret_cast<int64_t*>(ep->host_dev));
+  GB_CU(cudaGetLastError(), "agree on T");
   if ((rc = stream_settle(ep, st, "agree on T"))) return rc;
-  *out = h[0];
+  *out = *reinterpret_cast<volatile int64_t*>(ep->host);
   return GB_OK;
 }
 
@@ -744,11 +764,11 @@ int ep_forward(Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
     }
   }
   if ((rc = nccl_settle(ep, g_nccl.GroupEnd(), "count exchange"))) return rc;
-  GB_CU(cudaMemcpyAsync(ep->host, ep->cnt_recv, sizeof(int32_t) * E, cudaMemcpyDeviceToHost, st),
-        "copy received counts");
+  ep_to_host_kernel<<<1, 256, 0, st>>>(ep->cnt_recv, E, ep->host_dev);
+  GB_CU(cudaGetLastError(), "read received counts");
   if ((rc = stream_settle(ep, st, "count exchange"))) return rc;
   int64_t R = 0;
-  for (int i = 0; i < N * e_per; ++i) R += ep->host[i];
+  for (int i = 0; i < N * e_per; ++i) R += reinterpret_cast<volatile int32_t*>(ep->host)[i];
   if ((rc = ensure_positions(m, std::max<int64_t>(R, 1), st))) return rc;
 
   // 2. dispatch: each token's row once per destination rank, by peer stores
