@@ -228,6 +228,17 @@ int gb_moe_set_expert_path(gb_moe* m, int32_t path);
  * has one CPU path. */
 int gb_moe_set_graphs(gb_moe* m, int32_t max_graphs);
 
+/* Failure-handling test hooks (no counterpart in the reference; its CPU path
+ * has no asynchronous waits).  wait_limit_us: how long each bounded wait of
+ * the block-scaled expert kernel may last before it gives up (0 = the
+ * default, 2 s).  withhold_ready != 0: the one-launch expert kernel (grouped
+ * batches of 16-512 positions) leaves the first gate_up tile's ready flag
+ * unset, so the down work that needs it waits until the limit; that forward's
+ * output is invalid and gb_moe_device_status reports GB_ERR_TIMEOUT.  Both
+ * apply to later forwards until reset with (0, 0); the next forward after a
+ * reset is complete again.  Clears the forward graph cache. */
+int gb_moe_set_test_hooks(gb_moe* m, int64_t wait_limit_us, int32_t withhold_ready);
+
 /* Stage timing for profiling (no counterpart in the reference, whose timing
  * is per generated token, crates/gallium-agent/src/llm_candle.rs:302-345).
  * When enabled, each forward records a CUDA event at every stage boundary on

@@ -654,6 +654,8 @@ int ep_init(Moe& m, const uint8_t* id_bytes) {
 
 int32_t* ep_meta(Moe& m) { return m.ep ? m.ep->meta2 : nullptr; }
 
+int* ep_arrivals(Moe& m) { return m.ep ? m.ep->eb.mx_arrivals : nullptr; }
+
 int ep_agree_max(Moe& m, int64_t v, int64_t* out, cudaStream_t st) {
   Ep* ep = m.ep;
   if (ep->broken)

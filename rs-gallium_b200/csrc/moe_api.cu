@@ -491,6 +491,17 @@ int read_device_status(gb::Moe& m, cudaStream_t st) {
   }
   GB_CUDA(cudaStreamSynchronize(st), "synchronise device status");
   bits |= b2;
+  if (bits) {
+    // a kernel that gave up may have left split-K tickets counted: clear them
+    // so that the next forward starts from zero
+    if (m.ws.eb.mx_arrivals)
+      GB_CUDA(cudaMemsetAsync(m.ws.eb.mx_arrivals, 0, 2 * sizeof(int) * (size_t)gb::kMxSplitSlots, st),
+              "clear split-K tickets");
+    if (int* a = gb::ep_arrivals(m))
+      GB_CUDA(cudaMemsetAsync(a, 0, 2 * sizeof(int) * (size_t)gb::kMxSplitSlots, st),
+              "clear split-K tickets");
+    GB_CUDA(cudaStreamSynchronize(st), "clear split-K tickets");
+  }
   if (bits & 2) return set_err(GB_ERR_TIMEOUT, "a tensor-core pipeline wait timed out on the device");
   if (bits & 1) return set_err(GB_ERR_INVALID_ARG, "routing produced an expert index out of range");
   return GB_OK;
@@ -1116,6 +1127,19 @@ int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
   DeviceScope ds(h->m.device);
   clear_graphs(h->m);
   h->m.expert_path = path;
+  return GB_OK;
+}
+
+int gb_moe_set_test_hooks(gb_moe* h, int64_t wait_limit_us, int32_t withhold_ready) {
+  int rc = check_handle(h);
+  if (rc) return rc;
+  if (wait_limit_us < 0 || wait_limit_us > 10000000)
+    return set_err(GB_ERR_INVALID_ARG, "wait_limit_us %lld outside [0, 1e7]",
+                   (long long)wait_limit_us);
+  DeviceScope ds(h->m.device);
+  clear_graphs(h->m);
+  h->m.test_wait_ns = (uint64_t)wait_limit_us * 1000ull;
+  h->m.test_withhold_ready = withhold_ready != 0;
   return GB_OK;
 }
 

@@ -191,6 +191,10 @@ struct Moe {
   cudaEvent_t ev[kStages + 1] = {};
   int64_t launches = 0;
   int expert_path = 0;  // gb_expert_path
+  // gb_moe_set_test_hooks: bounded-wait limit of the block-scaled kernels
+  // (0 = default) and the withheld ready flag of the one-launch kernel
+  uint64_t test_wait_ns = 0;
+  int test_withhold_ready = 0;
   // gb_moe_forward_host pipelining: copy streams and chunk events (lazily made)
   cudaStream_t h2d = nullptr, d2h = nullptr;
   cudaEvent_t host_ev[2 + 2 * kHostChunksMax] = {};
@@ -324,6 +328,8 @@ void ep_destroy(Moe& m);
 int ep_forward(Moe& m, const float* x, int64_t T, float* out, cudaStream_t st);
 // Tokens per rank an expert-parallel forward may hold (0 without EP).
 int64_t ep_capacity(const Moe& m);
+// Split-K tickets of the expert-parallel expert buffers (null without EP).
+int* ep_arrivals(Moe& m);
 // Largest v over the ranks (a collective: every rank calls it).
 int ep_agree_max(Moe& m, int64_t v, int64_t* out, cudaStream_t st);
 

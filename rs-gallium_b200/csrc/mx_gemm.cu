@@ -160,6 +160,11 @@ struct Args {
   int* ready;
   int ready_stride;
   int* next_item;             // one-launch mode: items handed out so far beyond the grid
+  // failure-handling tests: every bounded wait gives up after wait_ns (0 =
+  // kMbarWaitNs); withhold_ready keeps gate_up tile 0's first ready flag
+  // unpublished, so down items that need it wait until the limit
+  uint64_t wait_ns;
+  int withhold_ready;
 };
 
 struct Item {
@@ -286,12 +291,13 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 
 // Bounded wait for a ready flag; false if the CTA is aborting or it ran out.
-__device__ __forceinline__ bool wait_ready(const int* p, volatile int* abort_flag, int* err) {
+__device__ __forceinline__ bool wait_ready(const int* p, volatile int* abort_flag, int* err,
+                                           uint64_t limit_ns) {
   if (ld_acquire(p)) return true;
   const uint64_t t0 = globaltimer();
   while (!ld_acquire(p)) {
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kMbarWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicOr(err, 2);
       return false;
@@ -313,7 +319,7 @@ __device__ __forceinline__ void publish_ready(const Args& a, const Item& it, int
   __threadfence();
   fence_proxy_async_global();
   asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (m == 0) {
+  if (m == 0 && !(a.withhold_ready && it.tile == 0 && it.m_tile == 0)) {
     int* f = a.ready + (int64_t)it.tile * a.ready_stride + it.m_tile;
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(1) : "memory");
   }
@@ -386,6 +392,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint64_t wait_ns = a0.wait_ns ? a0.wait_ns : kMbarWaitNs;
   // Everything above touches only this CTA's shared memory and TMEM, so it
   // overlaps the tail of the grid before; global memory is read after the wait.
   pdl_wait();
@@ -402,7 +409,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
   };
   auto publish_item = [&](int i) -> int {
     const int r = i % kSchedRing;
-    if (!mbar_wait(&s_sched_empty[r], ((i / kSchedRing) & 1) ^ 1, abort_flag, a0.err)) return -1;
+    if (!mbar_wait(&s_sched_empty[r], ((i / kSchedRing) & 1) ^ 1, abort_flag, a0.err, wait_ns)) return -1;
     int item = i == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(a0.next_item, 1);
     if (item >= total_items) item = -1;
     s_sched[r] = item;
@@ -411,7 +418,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
   };
   auto read_item = [&](int i) -> int {
     const int r = i % kSchedRing;
-    if (!mbar_wait(&s_sched_full[r], (i / kSchedRing) & 1, abort_flag, a0.err)) return -1;
+    if (!mbar_wait(&s_sched_full[r], (i / kSchedRing) & 1, abort_flag, a0.err, wait_ns)) return -1;
     return *reinterpret_cast<volatile int*>(&s_sched[r]);
   };
 
@@ -440,7 +447,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
       // depend on gate_up items only, which wait on nothing.
       auto drain = [&]() {
         while (ok && qn > 0) {
-          if (!wait_ready(a1.ready + q_flag[qh], abort_flag, a1.err)) ok = false;
+          if (!wait_ready(a1.ready + q_flag[qh], abort_flag, a1.err, wait_ns)) ok = false;
           else issue_front();
         }
       };
@@ -474,12 +481,12 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
           if (MODE == 2) {
             // the stage that last used slot s needs its h copy before slot s frees
             while (ok && qn > 0 && (q_g[qh] + D::STAGES <= g || qn == QCAP)) {
-              if (!wait_ready(a1.ready + q_flag[qh], abort_flag, A.err)) ok = false;
+              if (!wait_ready(a1.ready + q_flag[qh], abort_flag, A.err, wait_ns)) ok = false;
               else issue_front();
             }
             if (!ok) break;
           }
-          if (!mbar_wait(&empty[s], sph ^ 1u, abort_flag, A.err)) {
+          if (!mbar_wait(&empty[s], sph ^ 1u, abort_flag, A.err, wait_ns)) {
             ok = false;
             break;
           }
@@ -535,7 +542,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
         const Args& A = ph ? a1 : a0;
         const int b = acc_iter % D::NACC;
         const uint32_t acc_phase = (uint32_t)(acc_iter / D::NACC) & 1u;
-        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1u, abort_flag, A.err)) break;
+        if (!mbar_wait(&acc_empty[b], acc_phase ^ 1u, abort_flag, A.err, wait_ns)) break;
         tc_fence_after();
         const uint32_t dbase = tmem_base + (uint32_t)(b * D::BUF);
         const Item it = decode_item(A, local_of(item));
@@ -545,7 +552,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
                           ((uint32_t)min(D::N, 8 * ((it.nrows + 1) >> 1)) >> 3 << 17)
                     : D::IDESC;
         for (int kc = it.kc0; kc < it.kc1; ++kc) {
-          if (!mbar_wait(&full[s], sph, abort_flag, A.err)) {
+          if (!mbar_wait(&full[s], sph, abort_flag, A.err, wait_ns)) {
             ok = false;
             break;
           }
@@ -597,7 +604,7 @@ __global__ void __launch_bounds__(Tile<NT>::THREADS, Tile<NT>::CPS)
       if (m == 0) {
         int item = MODE != 2 ? static_item(i) : read_item(i);
         if (MODE == 2 && item >= 0) mbar_arrive(&s_sched_empty[i % kSchedRing]);
-        if (item >= 0 && !mbar_wait(&acc_full[b], acc_phase, abort_flag, a0.err)) item = -1;
+        if (item >= 0 && !mbar_wait(&acc_full[b], acc_phase, abort_flag, a0.err, wait_ns)) item = -1;
         s_epi_item[grp][i & 1] = item;
       }
       asm volatile("bar.sync %0, 128;" ::"r"(nbar) : "memory");
@@ -1175,6 +1182,8 @@ mx::Args mx_common(const Moe& m, const Groups& g, const ExpertBufs& eb, int rows
   a.ksplit = 1;
   a.partial = eb.mx_partial;
   a.arrivals = eb.mx_arrivals;
+  a.wait_ns = m.test_wait_ns;
+  a.withhold_ready = m.test_withhold_ready;
   return a;
 }
 

@@ -59,14 +59,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait.  Returns false if the CTA is aborting or the wait ran out.
+// Bounded wait (limit_ns, default kMbarWaitNs).  Returns false if the CTA is
+// aborting or the wait ran out.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag,
-                                          int* err) {
+                                          int* err, uint64_t limit_ns = kMbarWaitNs) {
   if (mbar_try_wait(b, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(b, parity)) {
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kMbarWaitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicOr(err, 2);
       return false;

@@ -114,6 +114,7 @@ SIGNATURES = {
     "gb_moe_destroy": (c_int, [c_void_p]),
     "gb_moe_set_expert_path": (c_int, [c_void_p, c_int32]),
     "gb_moe_set_graphs": (c_int, [c_void_p, c_int32]),
+    "gb_moe_set_test_hooks": (c_int, [c_void_p, c_int64, c_int32]),
     "gb_moe_set_profiling": (c_int, [c_void_p, c_int]),
     "gb_moe_stage_times": (c_int, [c_void_p, POINTER(c_float), c_int32, POINTER(c_int32)]),
     "gb_moe_stage_name": (c_char_p, [c_int32]),

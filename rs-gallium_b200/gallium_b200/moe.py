@@ -155,6 +155,13 @@ class MoEBlock:
         directly (gb_moe_set_graphs)."""
         check(self._lib.gb_moe_set_graphs(self._h, int(max_graphs)))
 
+    def set_test_hooks(self, wait_limit_us: int = 0, withhold_ready: bool = False) -> None:
+        """Failure-handling test hooks (gb_moe_set_test_hooks): a shorter
+        bounded-wait limit and a withheld ready flag in the one-launch expert
+        kernel; (0, False) restores normal operation."""
+        check(self._lib.gb_moe_set_test_hooks(self._h, int(wait_limit_us),
+                                               1 if withhold_ready else 0))
+
     def set_profiling(self, enable: bool = True) -> None:
         check(self._lib.gb_moe_set_profiling(self._h, 1 if enable else 0))
 
