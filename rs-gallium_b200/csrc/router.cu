@@ -41,8 +41,9 @@ __device__ __forceinline__ void route_tail(int t0, int nt, const float* __restri
                                            int32_t* __restrict__ idx_out,
                                            float* __restrict__ w_out) {
   __shared__ unsigned s_ticket;
+  __shared__ float s_exp[kRouterWarps][256];  // per warp: exp(l - max) of a token's experts
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nwarps = blockDim.x >> 5;
+  const int nwarps = blockDim.x >> 5;  // both router kernels run kRouterWarps warps
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_ticket = atomicAdd(&tickets[blockIdx.x], 1u);
@@ -86,18 +87,22 @@ __device__ __forceinline__ void route_tail(int t0, int nt, const float* __restri
       }
 #pragma unroll
       for (int s = 16; s >= 1; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, s));
-#pragma unroll
-      for (int q = 0; q < kMaxPerLane; ++q)
-        raw[q] = lane + 32 * q < E ? exp_f32(__fsub_rn(l[q], mx)) : 0.0f;
-      float sum = 0.0f;  // every lane adds the E values in expert order
+      float* ex = s_exp[warp];
 #pragma unroll
       for (int q = 0; q < kMaxPerLane; ++q) {
-        if (32 * q >= E) break;
-        for (int src = 0; src < 32; ++src) {
-          const float v = __shfl_sync(kFullMask, raw[q], src);
-          if (32 * q + src < E) sum = __fadd_rn(sum, v);
+        raw[q] = 0.0f;
+        if (lane + 32 * q < E) {
+          raw[q] = exp_f32(__fsub_rn(l[q], mx));
+          ex[lane + 32 * q] = raw[q];
         }
       }
+      __syncwarp();
+      // every lane adds the E values in expert order (broadcast loads, so
+      // only the additions form a chain)
+      float sum = 0.0f;
+#pragma unroll 8
+      for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, ex[e]);
+      __syncwarp();  // the next token of this warp rewrites ex
 #pragma unroll
       for (int q = 0; q < kMaxPerLane; ++q) {
         const bool in = lane + 32 * q < E;
