@@ -16,7 +16,12 @@ The same line carries, under "configs", the workload's other layers:
   lfm2_q4k                   the LFM2.5-shaped block (hidden 2048, 1792
                              intermediate, 32 experts, top-4, Q4_K experts,
                              sigmoid router) at 1, 64 and 2048 tokens per GPU,
-                             expert parallel over the N GPUs when N > 1.
+                             expert parallel over the N GPUs when N > 1;
+  moeffn_dense               gallium-core's generic MoEFFN with dense bf16
+                             experts (a Qwen3-MoE-like shape: hidden 2048,
+                             128 experts, top-8, intermediate 768, SiLU) and a
+                             512-wide shared expert, at 1, 64 and 2048 tokens
+                             per GPU, expert parallel when N > 1.
 Each with its own roofline and a parity check against the oracle.
 
 Arms:
@@ -34,12 +39,14 @@ expert indices of every token bit for bit, and the output rows of a sample
 mean-rel 1e-3.  The line's "parity" object has the worst rank's figures; a
 failed check prints the line and exits with status 3.
 
---model lfm2 measures the LFM2.5-shaped layer as the headline instead.
+--model lfm2 / dense measures the LFM2.5-shaped or the generic dense layer as
+the headline instead.
 
 Multi-GPU (python -m torch.distributed.run ... bench.py --gpus N): one process
 per GPU, expert parallel: rank r holds experts [r*E/N, (r+1)*E/N) and its own
-batch of --tokens tokens; routed rows go to the owning rank and back by NCCL
-inside the library.  Timing = max over ranks, value = all ranks' tokens / that
+batch of --tokens tokens; inside the library the ranks exchange expert counts
+by NCCL and move activation rows to the owning rank, and output rows back, by
+NVLink peer stores.  Timing = max over ranks, value = all ranks' tokens / that
 time (weak scaling).
 """
 from __future__ import annotations
@@ -71,27 +78,36 @@ class Model:
     def __init__(self, name, experts, skewed=False):
         self.name = name
         self.skewed = skewed
+        self.k, self.Is = TOPK, 0
         if name == "gptoss":
             self.H, self.I, self.E = 2880, 2880, experts or 128
             self.metric = "MoE-layer tokens/s (GPT-OSS-120B shape, MXFP4)"
             size = "120b" if self.E == 128 else "20b" if self.E == 32 else f"E{self.E}"
             self.shape = (f"gpt-oss-{size}-shaped MoE layer, E={self.E}, H=I=2880, top-{TOPK}, "
                           f"MXFP4" + (", Zipf(1.2) router bias" if skewed else ""))
-        else:
+        elif name == "lfm2":
             self.H, self.I, self.E = 2048, 1792, experts or 32
             self.metric = "MoE-layer tokens/s (LFM2.5 shape, Q4_K)"
             self.shape = (f"lfm2.5-shaped MoE layer, E={self.E}, H=2048, I=1792, top-{TOPK}, "
                           f"Q4_K, sigmoid router")
+        else:  # the generic MoEFFN with dense bf16 experts and a shared expert
+            self.H, self.I, self.E, self.k, self.Is = 2048, 768, experts or 128, 8, 512
+            self.metric = "MoE-layer tokens/s (generic MoEFFN, dense bf16 experts)"
+            self.shape = (f"qwen3-moe-like generic MoEFFN layer, E={self.E}, H=2048, I=768, "
+                          f"top-8, SiLU, dense bf16 experts, shared expert 512")
 
     def layer(self, seed):
         from gallium_b200 import synth
         if self.name == "gptoss":
             return synth.gptoss_layer(n_experts=self.E, seed=seed, skewed=self.skewed)
-        return synth.lfm2_layer(n_experts=self.E, seed=seed)
+        if self.name == "lfm2":
+            return synth.lfm2_layer(n_experts=self.E, seed=seed)
+        return synth.dense_layer(n_experts=self.E, hidden=self.H, inter=self.I, top_k=self.k,
+                                 shared_inter=self.Is, seed=seed)
 
     def load(self, layer, device, max_tokens, ep):
-        from gallium_b200 import Lfm2QMoEFFN, OssMoEFFN
-        cls = OssMoEFFN if self.name == "gptoss" else Lfm2QMoEFFN
+        from gallium_b200 import Lfm2QMoEFFN, MoEFFN, OssMoEFFN
+        cls = {"gptoss": OssMoEFFN, "lfm2": Lfm2QMoEFFN, "dense": MoEFFN}[self.name]
         return cls.load(layer, device=device, max_tokens=max_tokens, ep=ep)
 
     def stage_weight_bytes(self):
@@ -99,11 +115,14 @@ class Model:
         H, I = self.H, self.I
         if self.name == "gptoss":
             return (2 * I * H // 2 + 2 * I * H // 32 + 2 * I * 2, H * I // 2 + H * I // 32 + H * 2)
-        return (2 * I * H // 256 * 144, H * I // 256 * 144)
+        if self.name == "lfm2":
+            return (2 * I * H // 256 * 144, H * I // 256 * 144)
+        return (2 * I * H * 2, H * I * 2)  # bf16
 
     def oracle(self, layer):
         import oracle
-        return oracle.OracleMoe(layer) if self.name == "gptoss" else oracle.OracleLfm2(layer)
+        return {"gptoss": oracle.OracleMoe, "lfm2": oracle.OracleLfm2,
+                "dense": oracle.OracleDense}[self.name](layer)
 
     def route(self, layer, x):
         """Oracle routing of x: idx [T, k]."""
@@ -112,6 +131,10 @@ class Model:
             rw = (layer.router_w.astype(np.uint32) << 16).view(np.float32)
             rb = (layer.router_b.astype(np.uint32) << 16).view(np.float32)
             idx, _ = oracle.route_softmax_topk(oracle.router_logits(x, rw, rb), TOPK)
+            return idx
+        if self.name == "dense":
+            rw = (layer.router_w.astype(np.uint32) << 16).view(np.float32)
+            idx, _ = oracle.route_softmax_topk(oracle.router_logits(x, rw, None), self.k)
             return idx
         lg = oracle.router_logits(x, layer.router_w, None)
         idx, _ = oracle.route_sigmoid_topk(lg, layer.sel_bias, TOPK)
@@ -125,7 +148,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--tokens", type=int, default=8192)
-    ap.add_argument("--model", choices=["gptoss", "lfm2"], default="gptoss")
+    ap.add_argument("--model", choices=["gptoss", "lfm2", "dense"], default="gptoss")
     ap.add_argument("--experts", type=int, default=0, help="default 128 (gptoss) / 32 (lfm2)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--skewed", action="store_true", help="Zipf(1.2) router bias")
@@ -380,7 +403,7 @@ def measured_traffic(model, T, stage, n_gpus):
 def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
     """Roofline of the dominant expert kernel (gate_up or down, or both when
     one launch runs them: the library then records an empty down stage)."""
-    H, I, k = model.H, model.I, TOPK
+    H, I, k = model.H, model.I, model.k
     rows = T * k
     gu_w, dn_w = model.stage_weight_bytes()
     stage_bytes = {
@@ -388,6 +411,9 @@ def roofline_for(model, stage_ms, T, n_touched, peaks, n_gpus=1):
         "down": n_touched * dn_w + rows * I * 4 + rows * H * 4,
     }
     stage_flops = {"gate_up": 2 * rows * 2 * I * H, "down": 2 * rows * H * I}
+    if model.Is:  # the shared expert runs in the gate_up stage's window
+        stage_bytes["gate_up"] += 3 * model.Is * H * 2 + T * (2 * H + model.Is) * 4
+        stage_flops["gate_up"] += 2 * T * 3 * H * model.Is
     stage_ms = dict(stage_ms)
     if stage_ms.get("down", 0.0) < 0.005:  # two adjacent events: no kernel between them
         stage_ms["gate_up+down"] = stage_ms["gate_up"]
@@ -593,6 +619,8 @@ def run_ours(args, world, rank, local):
                                            [4096], args, flush, peaks, threads)
         configs["lfm2_q4k"] = run_config(Model("lfm2", 32), args.seed, local, rank, world,
                                          [1, 64, 2048], args, flush, peaks, threads)
+        configs["moeffn_dense"] = run_config(Model("dense", 128), args.seed, local, rank, world,
+                                             [1, 64, 2048], args, flush, peaks, threads)
 
     # ---- CPU baseline (rank 0, one GPU only) ---------------------------------
     cpu = None

@@ -51,9 +51,19 @@ typedef enum gb_status {
  * (lfm2moe_q.rs:241-258). */
 typedef enum { GB_ROUTER_SOFTMAX_TOPK = 0, GB_ROUTER_SIGMOID_TOPK = 1 } gb_router_kind;
 
-/* Expert activation: GPT-OSS clamped SwiGLU (gpt_oss.rs:202-212) or plain
- * SiLU-gated (lfm2moe_q.rs:287-290, ffn.rs:56-66 without clamp). */
-typedef enum { GB_ACT_GPTOSS_CLAMP = 0, GB_ACT_SILU = 1 } gb_act_kind;
+/* Expert activation: GPT-OSS clamped SwiGLU (gpt_oss.rs:202-212), or a gated
+ * h = act(gate) * up with act one of gallium-core's Activation
+ * (ffn.rs:4-24): SiLU (also the LFM2.5 experts, lfm2moe_q.rs:287-290), GELU
+ * (erf), GELU (tanh), ReLU.  The gated kinds clamp act(gate) to
+ * [-act_clamp, act_clamp] when act_clamp > 0 (ffn.rs:56-66).  GELU, GELU_TANH
+ * and RELU apply to GB_FMT_DENSE experts. */
+typedef enum {
+  GB_ACT_GPTOSS_CLAMP = 0,
+  GB_ACT_SILU = 1,
+  GB_ACT_GELU = 2,
+  GB_ACT_GELU_TANH = 3,
+  GB_ACT_RELU = 4
+} gb_act_kind;
 
 /* Expert weight format as the caller holds it. */
 typedef enum {
@@ -69,7 +79,12 @@ typedef enum {
   /* GGML Q4_K (144-byte, 256-element super-blocks), separate gate/up/down
    * like GGUF (quantized.rs:139-178, the LFM2.5 experts of
    * lfm2moe_q.rs:203-232).  H and I multiples of 256. */
-  GB_FMT_Q4_K = 2
+  GB_FMT_Q4_K = 2,
+  /* Dense expert weights in weight_dtype (gallium-core MoEFFN's GatedFFN
+   * experts, ffn.rs:30-67, 72-166): gate_raw, up_raw [E, I, H], down_raw
+   * [E, H, I], no biases; router_weight [E, H], no bias; combine in rank
+   * order; optional shared expert.  Experts run on the CUDA cores. */
+  GB_FMT_DENSE = 3
 } gb_weight_format;
 
 typedef enum { GB_DTYPE_F32 = 0, GB_DTYPE_BF16 = 1 } gb_dtype;
@@ -133,6 +148,19 @@ typedef struct gb_moe_desc {
    * status reports it; the handle then refuses further forwards and must be
    * destroyed on every rank. */
   int32_t ep_timeout_ms;
+
+  /* GB_FMT_DENSE: dtype of gate_raw / up_raw / down_raw and of the shared
+   * expert's weights (gb_dtype). */
+  int32_t weight_dtype;
+  /* Gated activations: clamp of act(gate) to [-act_clamp, act_clamp]; 0 = none. */
+  float act_clamp;
+  /* GB_FMT_DENSE: shared expert over all tokens, added after the routed
+   * combine (ffn.rs:160-163); shared_inter 0 = none.  shared_gate,
+   * shared_up [shared_inter, H], shared_down [H, shared_inter], weight_dtype. */
+  int32_t shared_inter;
+  const void* shared_gate;
+  const void* shared_up;
+  const void* shared_down;
 } gb_moe_desc;
 
 typedef struct gb_moe gb_moe;

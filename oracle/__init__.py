@@ -17,8 +17,8 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "liboracle.so")
 
 OR_ROUTER_SOFTMAX_TOPK, OR_ROUTER_SIGMOID_TOPK = 0, 1
-OR_ACT_GPTOSS_CLAMP, OR_ACT_SILU = 0, 1
-OR_FMT_MXFP4_SPLIT, OR_FMT_MXFP4_GGUF, OR_FMT_Q4_K = 0, 1, 2
+OR_ACT_GPTOSS_CLAMP, OR_ACT_SILU, OR_ACT_GELU, OR_ACT_GELU_TANH, OR_ACT_RELU = 0, 1, 2, 3, 4
+OR_FMT_MXFP4_SPLIT, OR_FMT_MXFP4_GGUF, OR_FMT_Q4_K, OR_FMT_DENSE = 0, 1, 2, 3
 
 
 class OrDesc(ctypes.Structure):
@@ -32,6 +32,9 @@ class OrDesc(ctypes.Structure):
         ("gate_raw", c_void_p), ("up_raw", c_void_p), ("down_raw", c_void_p),
         ("gu_bias", c_void_p), ("gate_bias", c_void_p), ("up_bias", c_void_p),
         ("dn_bias", c_void_p),
+        ("dense_gate", c_void_p), ("dense_up", c_void_p), ("dense_down", c_void_p),
+        ("shared_inter", c_int64), ("sh_gate", c_void_p), ("sh_up", c_void_p),
+        ("sh_down", c_void_p), ("act_clamp", c_float),
     ]
 
 
@@ -272,6 +275,36 @@ class OracleLfm2:
                 for k in ("router_w", "sel_bias", "gate_raw", "up_raw", "down_raw")}
         d.router_w, d.sel_bias = _p(keep["router_w"]), _p(keep["sel_bias"])
         d.gate_raw, d.up_raw, d.down_raw = _p(keep["gate_raw"]), _p(keep["up_raw"]), _p(keep["down_raw"])
+        self.desc = d
+        self._keep = keep
+
+    forward = OracleMoe.forward
+    expert_ffn = OracleMoe.expert_ffn
+    expert_sample = OracleMoe.expert_sample
+
+
+class OracleDense:
+    """The oracle for one gallium-core MoEFFN layer (ffn.rs:72-166): dense
+    experts (bf16 bits widened exactly, or f32), generic activation with an
+    optional clamp, optional shared expert."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        d = OrDesc()
+        d.hidden, d.inter, d.n_experts, d.top_k = (layer.hidden, layer.inter, layer.n_experts,
+                                                   layer.top_k)
+        d.router_kind = OR_ROUTER_SOFTMAX_TOPK
+        d.act_kind = layer.act_kind
+        d.act_clamp = layer.act_clamp
+        d.weight_format = OR_FMT_DENSE
+        keep = {k: _bf(getattr(layer, k)) for k in ("router_w", "gate", "up", "down")}
+        d.router_w = _p(keep["router_w"])
+        d.dense_gate, d.dense_up, d.dense_down = _p(keep["gate"]), _p(keep["up"]), _p(keep["down"])
+        d.shared_inter = layer.shared_inter
+        if layer.shared_inter:
+            for k in ("sh_gate", "sh_up", "sh_down"):
+                keep[k] = _bf(getattr(layer, k))
+            d.sh_gate, d.sh_up, d.sh_down = _p(keep["sh_gate"]), _p(keep["sh_up"]), _p(keep["sh_down"])
         self.desc = d
         self._keep = keep
 

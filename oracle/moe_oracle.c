@@ -347,6 +347,35 @@ static float act_gptoss(float g, float u, float limit) {
 /* lfm2moe_q.rs:288-290: silu(g) * u with candle's silu v / (1 + exp(-v)). */
 static float act_silu(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
 
+/* gallium-core's gated activations (ffn.rs:16-24, 56-66): act(gate), clamped
+ * to [-clamp, clamp] when clamp > 0 (candle clamp: maximum, then minimum),
+ * times up.  GELU (erf) with erf evaluated in f64 as candle's gelu_erf does;
+ * GELU (tanh) as candle's gelu, 0.5 v (1 + tanh(sqrt(2/pi) v (1 + 0.044715 v^2))). */
+static float act_gated(int kind, float g, float u, float clamp) {
+  float a;
+  switch (kind) {
+    case OR_ACT_GELU:
+      a = (float)(0.5 * (double)g * (1.0 + erf((double)g / sqrt(2.0))));
+      break;
+    case OR_ACT_GELU_TANH:
+      a = 0.5f * g * (1.0f + tanhf(0.7978845608028654f * g * (1.0f + 0.044715f * g * g)));
+      break;
+    case OR_ACT_RELU:
+      a = g > 0.0f ? g : 0.0f;
+      break;
+    default:
+      a = g / (1.0f + expf(-g));
+  }
+  if (clamp > 0.0f) a = fminf(fmaxf(a, -clamp), clamp);
+  return a * u;
+}
+
+static float act_apply(const or_moe_desc* d, float g, float u) {
+  if (d->act_kind == OR_ACT_GPTOSS_CLAMP) return act_gptoss(g, u, d->swiglu_limit);
+  if (d->act_kind == OR_ACT_SILU && !(d->act_clamp > 0.0f)) return act_silu(g, u);
+  return act_gated(d->act_kind, g, u, d->act_clamp);
+}
+
 float or_act_gptoss(float g, float u, float limit) { return act_gptoss(g, u, limit); }
 float or_act_silu(float g, float u) { return act_silu(g, u); }
 
@@ -360,6 +389,11 @@ static void dequant_row(const or_moe_desc* d, int which, int64_t ex, int64_t row
   const int64_t H = d->hidden, I = d->inter;
   const int64_t rows = which == 2 ? H : (d->weight_format == OR_FMT_MXFP4_SPLIT ? 2 * I : I);
   const int64_t kdim = which == 2 ? I : H;
+  if (d->weight_format == OR_FMT_DENSE) {
+    const float* w = which == 0 ? d->dense_gate : which == 1 ? d->dense_up : d->dense_down;
+    memcpy(dst, w + (ex * rows + row) * kdim, sizeof(float) * (size_t)kdim);
+    return;
+  }
   if (d->weight_format == OR_FMT_MXFP4_SPLIT) {
     const uint8_t* blocks = which == 2 ? d->dn_blocks : d->gu_blocks;
     const uint8_t* scales = which == 2 ? d->dn_scales : d->gu_scales;
@@ -410,8 +444,7 @@ static void expert_ffn(const or_moe_desc* d, int64_t ex, const float* xs, int64_
       float u = dot_f32(xs + t * H, r1, H);
       if (has_gb) g = g + bg;
       if (has_ub) u = u + bu;
-      hbuf[t * I + i] = d->act_kind == OR_ACT_GPTOSS_CLAMP ? act_gptoss(g, u, d->swiglu_limit)
-                                                           : act_silu(g, u);
+      hbuf[t * I + i] = act_apply(d, g, u);
     }
   }
   for (int64_t o = 0; o < H; ++o) {
@@ -432,6 +465,10 @@ static int check_desc(const or_moe_desc* d) {
     return fail(1, "bad shape H=%lld I=%lld E=%lld k=%lld", (long long)d->hidden,
                 (long long)d->inter, (long long)d->n_experts, (long long)d->top_k);
   const int64_t blk = d->weight_format == OR_FMT_Q4_K ? 256 : 32;
+  if (d->weight_format == OR_FMT_DENSE && (!d->dense_gate || !d->dense_up || !d->dense_down))
+    return fail(1, "dense weights missing");
+  if (d->shared_inter > 0 && (!d->sh_gate || !d->sh_up || !d->sh_down))
+    return fail(1, "shared expert weights missing");
   if (d->hidden % blk || d->inter % blk)
     return fail(2, "H=%lld / I=%lld not multiples of the %lld-element block",
                 (long long)d->hidden, (long long)d->inter, (long long)blk);
@@ -513,7 +550,7 @@ int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out, 
   for (int64_t i = 0; i < t; ++i) {
     int order[64];
     for (int r = 0; r < K; ++r) order[r] = r;
-    if (d->weight_format != OR_FMT_MXFP4_SPLIT) {
+    if (d->weight_format == OR_FMT_MXFP4_GGUF || d->weight_format == OR_FMT_Q4_K) {
       for (int a = 1; a < K; ++a) {
         int cur = order[a], b = a - 1;
         while (b >= 0 && idx[i * K + order[b]] > idx[i * K + cur]) {
@@ -532,6 +569,35 @@ int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out, 
       }
       out[i * H + o] = acc;
     }
+  }
+  /* The shared expert over all tokens, added after the routed sum
+   * (ffn.rs:160-163): a GatedFFN with the experts' activation. */
+  if (d->shared_inter > 0) {
+    or_moe_desc sd = *d;
+    sd.weight_format = OR_FMT_DENSE;
+    sd.inter = d->shared_inter;
+    sd.n_experts = 1;
+    sd.dense_gate = d->sh_gate;
+    sd.dense_up = d->sh_up;
+    sd.dense_down = d->sh_down;
+    sd.gu_bias = sd.gate_bias = sd.up_bias = sd.dn_bias = NULL;
+    float* sy = (float*)malloc(sizeof(float) * (size_t)(t * H));
+    if (!sy) {
+      rc = fail(7, "out of host memory");
+      goto done;
+    }
+#pragma omp parallel num_threads(n_threads)
+    {
+      const int64_t Is = sd.inter, cap = (H > Is ? H : Is);
+      float* rowbuf = (float*)malloc(sizeof(float) * (size_t)(2 * cap));
+      float* hbuf = (float*)malloc(sizeof(float) * (size_t)Is);
+#pragma omp for schedule(dynamic, 1)
+      for (int64_t i = 0; i < t; ++i) expert_ffn(&sd, 0, x + i * H, 1, sy + i * H, hbuf, rowbuf);
+      free(rowbuf);
+      free(hbuf);
+    }
+    for (int64_t i = 0; i < t * H; ++i) out[i] = out[i] + sy[i];
+    free(sy);
   }
   if (idx_out) memcpy(idx_out, idx, sizeof(int32_t) * (size_t)(t * K));
   if (w_out) memcpy(w_out, w, sizeof(float) * (size_t)(t * K));

@@ -85,8 +85,13 @@ int or_permute(const int32_t* idx, int64_t t, int64_t e, int64_t k,
 /* ---- expert FFN and the whole block ------------------------------------ */
 
 enum { OR_ROUTER_SOFTMAX_TOPK = 0, OR_ROUTER_SIGMOID_TOPK = 1 };
-enum { OR_ACT_GPTOSS_CLAMP = 0, OR_ACT_SILU = 1 };
-enum { OR_FMT_MXFP4_SPLIT = 0, OR_FMT_MXFP4_GGUF = 1, OR_FMT_Q4_K = 2 };
+/* Activations: GPT-OSS clamped SwiGLU, or a gated act(gate) * up with act one
+ * of gallium-core's Activation (ffn.rs:4-24), act(gate) clamped to
+ * [-act_clamp, act_clamp] when act_clamp > 0 (ffn.rs:56-66). */
+enum { OR_ACT_GPTOSS_CLAMP = 0, OR_ACT_SILU = 1, OR_ACT_GELU = 2, OR_ACT_GELU_TANH = 3,
+       OR_ACT_RELU = 4 };
+/* OR_FMT_DENSE: gallium-core MoEFFN (ffn.rs:72-166), dense f32 experts. */
+enum { OR_FMT_MXFP4_SPLIT = 0, OR_FMT_MXFP4_GGUF = 1, OR_FMT_Q4_K = 2, OR_FMT_DENSE = 3 };
 
 typedef struct {
   int64_t hidden, inter, n_experts, top_k;
@@ -111,6 +116,16 @@ typedef struct {
   const float* gate_bias;
   const float* up_bias;
   const float* dn_bias;
+  /* DENSE: gate, up [E, I, H], down [E, H, I] f32; the shared expert
+   * (shared_inter > 0) sh_gate, sh_up [Is, H], sh_down [H, Is] f32. */
+  const float* dense_gate;
+  const float* dense_up;
+  const float* dense_down;
+  int64_t shared_inter;
+  const float* sh_gate;
+  const float* sh_up;
+  const float* sh_down;
+  float act_clamp;
 } or_moe_desc;
 
 /* Full block forward.  x [t, H] f32 -> out [t, H] f32.  Per active expert the

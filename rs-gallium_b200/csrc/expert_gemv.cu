@@ -192,7 +192,8 @@ cudaError_t launch_rows(const Moe& m, const Groups& g, const float* in, int K_in
 // (gpt_oss_q.rs:252-266, lfm2moe_q.rs:303-311) instead of rank order.
 __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv,
                                const float* __restrict__ wts, const int32_t* __restrict__ idx,
-                               int H, int K, int expert_order, float* __restrict__ out) {
+                               int H, int K, int expert_order, const float* __restrict__ add,
+                               float* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
@@ -242,6 +243,13 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
     acc.y = __fadd_rn(acc.y, __fmul_rn(vr.y, w));
     acc.z = __fadd_rn(acc.z, __fmul_rn(vr.z, w));
     acc.w = __fadd_rn(acc.w, __fmul_rn(vr.w, w));
+  }
+  if (add) {  // the shared expert's row, added after the routed sum (ffn.rs:160-163)
+    const float4 a = reinterpret_cast<const float4*>(add + (int64_t)t * H)[o4];
+    acc.x = __fadd_rn(acc.x, a.x);
+    acc.y = __fadd_rn(acc.y, a.y);
+    acc.z = __fadd_rn(acc.z, a.z);
+    acc.w = __fadd_rn(acc.w, a.w);
   }
   reinterpret_cast<float4*>(out + (int64_t)t * H)[o4] = acc;
 }
@@ -309,10 +317,14 @@ cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const f
   const int H = m.desc.hidden;
   const int threads = 256;
   dim3 grid((unsigned)T, (unsigned)((H / 4 + threads - 1) / threads));
-  const int expert_order = m.desc.weight_format != GB_FMT_MXFP4_SPLIT;
+  // rank order for the safetensors GPT-OSS and generic MoEFFN blocks
+  // (gpt_oss.rs:223, ffn.rs:153-156), expert order for the GGUF ones
+  const int expert_order =
+      m.desc.weight_format == GB_FMT_MXFP4_GGUF || m.desc.weight_format == GB_FMT_Q4_K;
+  const float* add = m.desc.shared_inter > 0 ? (const float*)ws.sh_y : nullptr;
   return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, y,
                     slots ? (const int32_t*)nullptr : (const int32_t*)ws.inv, ws.wts, ws.idx, H,
-                    m.desc.top_k, expert_order, out);
+                    m.desc.top_k, expert_order, add, out);
 }
 
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,

@@ -86,8 +86,23 @@ int validate(const gb_moe_desc* d) {
                    d->n_experts);
   if (d->router_kind != GB_ROUTER_SOFTMAX_TOPK && d->router_kind != GB_ROUTER_SIGMOID_TOPK)
     return set_err(GB_ERR_INVALID_ARG, "unknown router_kind %d", d->router_kind);
-  if (d->act_kind != GB_ACT_GPTOSS_CLAMP && d->act_kind != GB_ACT_SILU)
+  if (d->act_kind < GB_ACT_GPTOSS_CLAMP || d->act_kind > GB_ACT_RELU)
     return set_err(GB_ERR_INVALID_ARG, "unknown act_kind %d", d->act_kind);
+  if (d->act_kind > GB_ACT_SILU && d->weight_format != GB_FMT_DENSE)
+    return set_err(GB_ERR_UNSUPPORTED, "act_kind %d needs GB_FMT_DENSE experts", d->act_kind);
+  if (!(d->act_clamp >= 0.0f) || (d->act_clamp > 0.0f && d->act_kind == GB_ACT_GPTOSS_CLAMP))
+    return set_err(GB_ERR_INVALID_ARG,
+                   "act_clamp must be >= 0 (and 0 for the GPT-OSS activation, which uses "
+                   "swiglu_limit)");
+  if (d->shared_inter < 0 || (d->shared_inter > 0 && d->weight_format != GB_FMT_DENSE))
+    return set_err(GB_ERR_UNSUPPORTED, "a shared expert needs GB_FMT_DENSE experts");
+  if (d->shared_inter > 0 &&
+      (d->shared_inter % 32 != 0 || d->shared_inter > 4096 || !d->shared_gate ||
+       !d->shared_up || !d->shared_down))
+    return set_err(GB_ERR_INVALID_ARG,
+                   "shared expert: shared_inter %d must be a multiple of 32, <= 4096, with "
+                   "shared_gate, shared_up and shared_down",
+                   d->shared_inter);
   if (d->router_dtype != GB_DTYPE_F32 && d->router_dtype != GB_DTYPE_BF16)
     return set_err(GB_ERR_INVALID_ARG, "unknown router_dtype %d", d->router_dtype);
   if (d->bias_dtype != GB_DTYPE_F32 && d->bias_dtype != GB_DTYPE_BF16)
@@ -101,6 +116,14 @@ int validate(const gb_moe_desc* d) {
     case GB_FMT_MXFP4_GGUF:
       if (!d->gate_raw || !d->up_raw || !d->down_raw)
         return set_err(GB_ERR_INVALID_ARG, "MXFP4_GGUF needs gate_raw, up_raw and down_raw");
+      break;
+    case GB_FMT_DENSE:
+      if (!d->gate_raw || !d->up_raw || !d->down_raw)
+        return set_err(GB_ERR_INVALID_ARG, "DENSE needs gate_raw, up_raw and down_raw");
+      if (d->weight_dtype != GB_DTYPE_F32 && d->weight_dtype != GB_DTYPE_BF16)
+        return set_err(GB_ERR_INVALID_ARG, "unknown weight_dtype %d", d->weight_dtype);
+      if (d->act_kind == GB_ACT_GPTOSS_CLAMP)
+        return set_err(GB_ERR_UNSUPPORTED, "DENSE experts take a gated activation");
       break;
     case GB_FMT_Q4_K:
       if (!d->gate_raw || !d->up_raw || !d->down_raw)
@@ -206,6 +229,8 @@ int alloc_ws(gb::Moe& m, int64_t T) {
       {(void**)&ws.meta, sizeof(int32_t) * 4},
       {(void**)&ws.perm, sizeof(int32_t) * (size_t)(T * K)},
       {(void**)&ws.inv, sizeof(int32_t) * (size_t)(T * K)},
+      {(void**)&ws.sh_h, sizeof(float) * (size_t)(T * std::max(d.shared_inter, 0))},
+      {(void**)&ws.sh_y, d.shared_inter > 0 ? sizeof(float) * (size_t)(T * H) : 0},
       {(void**)&ws.x_stage, sizeof(float) * (size_t)(T * H)},
       {(void**)&ws.out_stage, sizeof(float) * (size_t)(T * H)},
   };
@@ -267,6 +292,9 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.q4_gu);
   cudaFree(m.w.q4_dn);
   cudaFree(m.w.q4_gu_exp);
+  for (void* p : {m.w.dense_gate, m.w.dense_up, m.w.dense_down, m.w.sh_gate, m.w.sh_up,
+                  m.w.sh_down})
+    cudaFree(p);
   gb::mx_release(m.mx);
   free_ws(m.ws);
   gb::ep_destroy(m);
@@ -302,9 +330,47 @@ int upload_q4k(gb::Moe& m) {
   return upload_router(m);
 }
 
+// Dense experts: the caller's rows as they are (bf16 or f32), local experts
+// only; the shared expert whole.
+int upload_dense(gb::Moe& m) {
+  const gb_moe_desc& d = m.desc;
+  const size_t es = d.weight_dtype == GB_DTYPE_BF16 ? 2 : 4;
+  const int64_t H = d.hidden, I = d.inter, nloc = m.e_end - m.e_begin;
+  m.w.dense_bf16 = d.weight_dtype == GB_DTYPE_BF16;
+  const size_t mat = (size_t)(I * H) * es;
+  int rc;
+  struct Part {
+    void** dst;
+    const void* src;
+    size_t bytes;
+    const char* what;
+  };
+  const size_t sh = (size_t)d.shared_inter * (size_t)H * es;
+  const Part parts[] = {
+      {&m.w.dense_gate, static_cast<const char*>((const void*)d.gate_raw) + m.e_begin * mat,
+       nloc * mat, "dense gate"},
+      {&m.w.dense_up, static_cast<const char*>((const void*)d.up_raw) + m.e_begin * mat,
+       nloc * mat, "dense up"},
+      {&m.w.dense_down, static_cast<const char*>((const void*)d.down_raw) + m.e_begin * mat,
+       nloc * mat, "dense down"},
+      {&m.w.sh_gate, d.shared_gate, sh, "shared gate"},
+      {&m.w.sh_up, d.shared_up, sh, "shared up"},
+      {&m.w.sh_down, d.shared_down, sh, "shared down"},
+  };
+  m.weight_bytes = 0;
+  for (const Part& p : parts) {
+    if (!p.bytes) continue;
+    if ((rc = dev_alloc((char**)p.dst, p.bytes, p.what))) return rc;
+    GB_CUDA(cudaMemcpy(*p.dst, p.src, p.bytes, cudaMemcpyHostToDevice), p.what);
+    m.weight_bytes += (int64_t)p.bytes;
+  }
+  return upload_router(m);
+}
+
 int upload_weights(gb::Moe& m) {
   const gb_moe_desc& d = m.desc;
   if (d.weight_format == GB_FMT_Q4_K) return upload_q4k(m);
+  if (d.weight_format == GB_FMT_DENSE) return upload_dense(m);
   const int64_t H = d.hidden, I = d.inter;
   const int64_t nloc = m.e_end - m.e_begin;
   const int64_t nbh = H / 32, nbi = I / 32;
@@ -552,6 +618,10 @@ int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t 
     GB_CUDA(cudaMemsetAsync(m.ws.counts, 0, sizeof(int32_t) * m.desc.n_experts, st),
             "clear counts");
   }
+  if (m.desc.shared_inter > 0 && T > 0) {  // shared expert over all tokens, added by combine
+    GB_CUDA(gb::launch_shared_expert(m, x, T, m.ws.sh_h, m.ws.sh_y, st), "shared expert launch");
+    m.launches += 2;
+  }
   if (m.ep_size > 1) {
     if ((rc = gb::ep_forward(m, x, T, out, st))) return rc;
     if ((rc = mark(m, 5, st))) return rc;
@@ -678,7 +748,12 @@ int run_experts(Moe& m, const Groups& g, const float* x, int64_t T, ExpertBufs& 
   int rc;
   (void)T;
   if (stored_return) *stored_return = false;
-  if (m.desc.weight_format == GB_FMT_Q4_K && use_q4k_tc(m, g, eb)) {
+  if (m.desc.weight_format == GB_FMT_DENSE) {
+    GB_CUDA(launch_dense_gate_up(m, g, x, eb, st), "dense gate_up launch");
+    if ((rc = mark(m, 3, st))) return rc;
+    GB_CUDA(launch_dense_down(m, g, eb, st), "dense down launch");
+    m.launches += 2;
+  } else if (m.desc.weight_format == GB_FMT_Q4_K && use_q4k_tc(m, g, eb)) {
     GB_CUDA(launch_q4k_tc_gate_up(m, g, x, eb, st), "Q4_K tensor-core gate_up launch");
     if ((rc = mark(m, 3, st))) return rc;
     GB_CUDA(launch_q4k_tc_down(m, g, eb, st), "Q4_K tensor-core down launch");
@@ -816,6 +891,19 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
   g_err[0] = 0;
   if (!out) return set_err(GB_ERR_INVALID_ARG, "out is null");
   *out = nullptr;
+  // A descriptor from an older header (shorter struct_size) reads as zeros in
+  // the fields it lacks.
+  gb_moe_desc dcopy;
+  memset(&dcopy, 0, sizeof dcopy);
+  if (desc && desc->struct_size >= offsetof(gb_moe_desc, ep_timeout_ms))
+    memcpy(&dcopy, desc, std::min<size_t>(desc->struct_size, sizeof dcopy));
+  else if (desc)
+    return set_err(GB_ERR_INVALID_ARG, "descriptor struct_size %u is too small (header mismatch)",
+                   desc->struct_size);
+  if (desc) {
+    dcopy.struct_size = sizeof dcopy;
+    desc = &dcopy;
+  }
   int rc = validate(desc);
   if (rc) return rc;
   int ndev = 0;

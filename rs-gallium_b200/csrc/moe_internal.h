@@ -71,6 +71,16 @@ struct ExpertWeights {
   // tensor-core Q4_K path: per local expert, weights decode as w * 2^exp
   int32_t* q4_gu_exp = nullptr;  // [E_loc] (one allocation with q4_dn_exp)
   int32_t* q4_dn_exp = nullptr;  // [E_loc]
+  // Dense experts (GB_FMT_DENSE), as stored (bf16 or f32): dense_gate,
+  // dense_up [E_loc][I][H], dense_down [E_loc][H][I]; the shared expert's
+  // sh_gate, sh_up [Is][H], sh_down [H][Is]
+  void* dense_gate = nullptr;
+  void* dense_up = nullptr;
+  void* dense_down = nullptr;
+  void* sh_gate = nullptr;
+  void* sh_up = nullptr;
+  void* sh_down = nullptr;
+  bool dense_bf16 = false;
 };
 
 // Weights in the block-scaled tensor-core layout (mx_gemm.cu), built from
@@ -162,6 +172,8 @@ struct Workspace {
   int32_t* meta = nullptr;     // [0] active count, [1] error flags, [2] N tiles
   int32_t* perm = nullptr;     // [T*k]
   int32_t* inv = nullptr;      // [T*k]
+  float* sh_h = nullptr;       // [T, Is] shared expert's activation (GB_FMT_DENSE)
+  float* sh_y = nullptr;       // [T, H] shared expert's output
   float* x_stage = nullptr;    // [T, H] host-path staging
   float* out_stage = nullptr;  // [T, H]
   ExpertBufs eb;               // single GPU: T*k positions
@@ -312,6 +324,14 @@ cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaSt
 // with `slots`, y is indexed by t*k + r directly (expert-parallel return slots).
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
                            cudaStream_t st, bool slots = false);
+
+// Dense experts on CUDA cores (dense_gemv.cu): the generic MoEFFN.
+cudaError_t launch_dense_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
+                                 cudaStream_t st);
+cudaError_t launch_dense_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+// The shared expert over all T tokens: h [T, Is], y [T, H] (ws.sh_h / sh_y).
+cudaError_t launch_shared_expert(const Moe& m, const float* x, int64_t T, float* h, float* y,
+                                 cudaStream_t st);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
                                   cudaStream_t st);
 cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,

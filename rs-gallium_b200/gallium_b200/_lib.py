@@ -31,9 +31,13 @@ GB_ROUTER_SOFTMAX_TOPK = 0
 GB_ROUTER_SIGMOID_TOPK = 1
 GB_ACT_GPTOSS_CLAMP = 0
 GB_ACT_SILU = 1
+GB_ACT_GELU = 2
+GB_ACT_GELU_TANH = 3
+GB_ACT_RELU = 4
 GB_FMT_MXFP4_SPLIT = 0
 GB_FMT_MXFP4_GGUF = 1
 GB_FMT_Q4_K = 2
+GB_FMT_DENSE = 3
 GB_PATH_AUTO = 0
 GB_PATH_CUDA_CORES = 1
 GB_PATH_TENSOR_CORES = 2
@@ -84,6 +88,12 @@ class MoeDesc(ctypes.Structure):
         ("ep_size", c_int32),
         ("nccl_id", c_void_p),
         ("ep_timeout_ms", c_int32),
+        ("weight_dtype", c_int32),
+        ("act_clamp", c_float),
+        ("shared_inter", c_int32),
+        ("shared_gate", c_void_p),
+        ("shared_up", c_void_p),
+        ("shared_down", c_void_p),
     ]
 
 

@@ -23,7 +23,7 @@ import numpy as np
 
 from . import _lib
 from ._lib import MoeDesc, MoeInfo, check, load_library
-from .synth import GptOssGgufLayer, GptOssLayer, Lfm2Layer, bf16_bits_to_f32
+from .synth import DenseMoeLayer, GptOssGgufLayer, GptOssLayer, Lfm2Layer, bf16_bits_to_f32
 
 
 def _as_f32(a: Optional[np.ndarray]) -> Optional[np.ndarray]:
@@ -300,3 +300,36 @@ class Lfm2QMoEFFN(MoEBlock):
         d.router_dtype = _lib.GB_DTYPE_F32
         d.bias_dtype = _lib.GB_DTYPE_F32
         return cls(d, arrs + [getattr(d, "_nccl_id_buf", None)])
+
+
+class MoEFFN(MoEBlock):
+    """gallium-core's generic MoE FFN (MoEFFN, crates/gallium-core/src/ffn.rs:72-166):
+    dense GatedFFN experts with a configurable activation and optional clamp,
+    softmax top-k routing, and an optional shared expert over all tokens
+    (the Qwen3.5 MoE layers, crates/gallium-models/src/qwen35.rs:222-233)."""
+
+    @classmethod
+    def load(cls, layer: DenseMoeLayer, device: int = 0, max_tokens: int = 64,
+             ep=None) -> "MoEFFN":
+        d = _base_desc(layer.hidden, layer.inter, layer.n_experts, layer.top_k, device,
+                       max_tokens, ep)
+        d.router_kind = _lib.GB_ROUTER_SOFTMAX_TOPK
+        d.act_kind = layer.act_kind
+        d.act_clamp = layer.act_clamp
+        d.weight_format = _lib.GB_FMT_DENSE
+        mats = [layer.gate, layer.up, layer.down]
+        if layer.shared_inter:
+            mats += [layer.sh_gate, layer.sh_up, layer.sh_down]
+        # weights go over as stored when they are all bf16 bits, else as f32
+        bf16 = all(a.dtype == np.uint16 for a in mats)
+        mats = [np.ascontiguousarray(a) if bf16 else np.ascontiguousarray(_as_f32(a))
+                for a in mats]
+        d.weight_dtype = _lib.GB_DTYPE_BF16 if bf16 else _lib.GB_DTYPE_F32
+        rw, _, d.router_dtype = _float_pair(layer.router_w, None)
+        rw = np.ascontiguousarray(rw)
+        d.router_weight = _ptr(rw)
+        d.gate_raw, d.up_raw, d.down_raw = [_ptr(a) for a in mats[:3]]
+        d.shared_inter = layer.shared_inter
+        if layer.shared_inter:
+            d.shared_gate, d.shared_up, d.shared_down = [_ptr(a) for a in mats[3:]]
+        return cls(d, mats + [rw, getattr(d, "_nccl_id_buf", None)])

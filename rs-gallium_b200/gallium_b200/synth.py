@@ -208,3 +208,49 @@ def lfm2_layer(n_experts: int = 32, hidden: int = 2048, inter: int = 1792, top_k
     down = np.stack([q4k_blocks(rng, H, I, d, dmin) for _ in range(E)])
     return Lfm2Layer(H, I, E, top_k, router_w, np.zeros(E, np.float32), gate, up, down,
                      meta={"seed": seed, "d": d, "dmin": dmin})
+
+
+# ---- gallium-core MoEFFN (dense experts, ffn.rs:72-166) --------------------
+
+@dataclass
+class DenseMoeLayer:
+    hidden: int
+    inter: int
+    n_experts: int
+    top_k: int
+    router_w: np.ndarray   # [E, H] bf16 bits (uint16) or f32
+    gate: np.ndarray       # [E, I, H]
+    up: np.ndarray         # [E, I, H]
+    down: np.ndarray       # [E, H, I]
+    act_kind: int = 1      # gb_act_kind: 1 SiLU, 2 GELU, 3 GELU (tanh), 4 ReLU
+    act_clamp: float = 0.0
+    shared_inter: int = 0
+    sh_gate: Optional[np.ndarray] = None  # [Is, H]
+    sh_up: Optional[np.ndarray] = None    # [Is, H]
+    sh_down: Optional[np.ndarray] = None  # [H, Is]
+    meta: dict = field(default_factory=dict)
+
+
+def dense_layer(n_experts: int = 128, hidden: int = 2048, inter: int = 768, top_k: int = 8,
+                shared_inter: int = 512, act_kind: int = 1, act_clamp: float = 0.0,
+                seed: int = 0, bf16: bool = True) -> DenseMoeLayer:
+    """A generic MoEFFN layer with random weights: router ~ N(0, 0.02), expert
+    and shared weights ~ N(0, 1/sqrt(fan_in)) so gate and up products are
+    O(1) for x ~ N(0, 1); bf16 bits (uint16) by default, as a bf16 checkpoint
+    holds them, else f32."""
+    rng = np.random.default_rng(seed)
+    E, H, I = n_experts, hidden, inter
+    cast = f32_to_bf16_bits if bf16 else (lambda a: a.astype(np.float32))
+
+    def normal(shape, std):
+        return cast(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+    layer = DenseMoeLayer(H, I, E, top_k, normal((E, H), 0.02), normal((E, I, H), H ** -0.5),
+                          normal((E, I, H), H ** -0.5), normal((E, H, I), I ** -0.5),
+                          act_kind=act_kind, act_clamp=act_clamp, shared_inter=shared_inter,
+                          meta={"seed": seed})
+    if shared_inter:
+        layer.sh_gate = normal((shared_inter, H), H ** -0.5)
+        layer.sh_up = normal((shared_inter, H), H ** -0.5)
+        layer.sh_down = normal((H, shared_inter), shared_inter ** -0.5)
+    return layer

@@ -5,7 +5,9 @@ the same tokens, and the ranks hold different token counts, so some run the
 decode-sized kernels and others the tensor-core path, and one rank may send
 rows it receives none back for.  Cases: the 20B-shaped block (32 experts), a
 128-expert layer (the 120B layer's routing and exchange shape at a smaller
-hidden size, so the oracle stays fast), and the LFM2.5 Q4_K block."""
+hidden size, so the oracle stays fast), the LFM2.5 Q4_K block, and a generic
+MoEFFN layer with dense experts and a shared expert (one rank with no tokens
+at all in the 4-rank case)."""
 import os
 import socket
 
@@ -14,7 +16,7 @@ import pytest
 import torch
 
 import oracle
-from gallium_b200 import Lfm2QMoEFFN, OssMoEFFN, nccl_unique_id, synth
+from gallium_b200 import Lfm2QMoEFFN, MoEFFN, OssMoEFFN, nccl_unique_id, synth
 
 pytestmark = [
     pytest.mark.gpu,
@@ -32,6 +34,9 @@ CASES = {
                     OssMoEFFN, oracle.OracleMoe, 128, 512, ([300, 64], [100, 37, 256, 3])),
     "lfm2-q4k": (lambda: synth.lfm2_layer(n_experts=32, seed=5), Lfm2QMoEFFN,
                  oracle.OracleLfm2, 32, 2048, ([5, 200], [64, 1, 300, 17])),
+    "dense-shared": (lambda: synth.dense_layer(n_experts=32, hidden=512, inter=256, top_k=4,
+                                               shared_inter=128, seed=6),
+                     MoEFFN, oracle.OracleDense, 32, 512, ([9, 150], [150, 9, 0, 33])),
 }
 
 
@@ -68,8 +73,8 @@ def _worker(rank, world, port, case, results):
         want, idx, _ = orc(layer).forward(x, n_threads=2)
         err = np.abs(out[0].astype(np.float64) - want)
         results[rank] = {
-            "max_abs": float(err.max()),
-            "mean_rel": float(err.sum() / np.abs(want).sum()),
+            "max_abs": float(err.max()) if err.size else 0.0,
+            "mean_rel": float(err.sum() / max(np.abs(want).sum(), 1e-30)),
             "repeat_equal": bool(np.array_equal(out[0], out[1])),
             "idx_equal": bool(np.array_equal(idx_gpu, idx)),
             "experts": (info["local_expert_begin"], info["local_expert_end"]),
