@@ -161,6 +161,24 @@ typedef struct gb_moe_desc {
   const void* shared_gate;
   const void* shared_up;
   const void* shared_down;
+
+  /* Gemma-4's routed experts (QGemmaMoe, gemma4_q.rs:187-330):
+   * gate_up_merged != 0 (GGUF MXFP4 / Q4_K): gate_raw holds the merged
+   *   [E, 2I, H] tensor, gate rows [0, I) then up rows [I, 2I); up_raw unused.
+   * expert_scale [E] f32: each expert's output row is multiplied by it
+   *   before the routing weight (ffn_down_exps.scale); NULL = none.
+   * input_norm 1: the router reads rms(x) * H^-0.5 * router_input_scale and
+   *   the experts read rms_norm(x) * expert_input_norm (both [H] f32), where
+   *   rms(x) = x / sqrt(mean(x^2) + rms_eps); 0 = both read x.
+   * output_norm [H] f32: the result is rms_norm(result) * output_norm
+   *   (post_ffw_norm_2); NULL = none. */
+  int32_t gate_up_merged;
+  const float* expert_scale;
+  int32_t input_norm;
+  const float* router_input_scale;
+  const float* expert_input_norm;
+  const float* output_norm;
+  float rms_eps;
 } gb_moe_desc;
 
 typedef struct gb_moe gb_moe;

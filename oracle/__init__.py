@@ -35,6 +35,9 @@ class OrDesc(ctypes.Structure):
         ("dense_gate", c_void_p), ("dense_up", c_void_p), ("dense_down", c_void_p),
         ("shared_inter", c_int64), ("sh_gate", c_void_p), ("sh_up", c_void_p),
         ("sh_down", c_void_p), ("act_clamp", c_float),
+        ("gate_up_merged", c_int32), ("expert_scale", c_void_p), ("input_norm", c_int32),
+        ("router_input_scale", c_void_p), ("expert_input_norm", c_void_p),
+        ("output_norm", c_void_p), ("rms_eps", c_float),
     ]
 
 
@@ -311,3 +314,35 @@ class OracleDense:
     forward = OracleMoe.forward
     expert_ffn = OracleMoe.expert_ffn
     expert_sample = OracleMoe.expert_sample
+
+
+class OracleGemma4:
+    """The oracle for Gemma-4's routed-experts block (QGemmaMoe::forward,
+    gemma4_q.rs:262-328): normed router input, normed expert input, merged
+    gate_up, GELU (tanh) gating, per-expert output scale, expert-order sum,
+    output norm."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        d = OrDesc()
+        d.hidden, d.inter, d.n_experts, d.top_k = (layer.hidden, layer.inter, layer.n_experts,
+                                                   layer.top_k)
+        d.router_kind = OR_ROUTER_SOFTMAX_TOPK
+        d.act_kind = OR_ACT_GELU_TANH
+        d.weight_format = layer.fmt
+        d.gate_up_merged = 1
+        keep = {k: np.ascontiguousarray(getattr(layer, k)) for k in (
+            "router_w", "router_scale", "expert_norm", "gate_up_raw", "down_raw", "output_norm")}
+        d.router_w = _p(keep["router_w"])
+        d.gate_raw, d.down_raw = _p(keep["gate_up_raw"]), _p(keep["down_raw"])
+        if layer.expert_scale is not None:
+            keep["expert_scale"] = np.ascontiguousarray(layer.expert_scale, np.float32)
+            d.expert_scale = _p(keep["expert_scale"])
+        d.input_norm = 1
+        d.router_input_scale, d.expert_input_norm = _p(keep["router_scale"]), _p(keep["expert_norm"])
+        d.output_norm = _p(keep["output_norm"])
+        d.rms_eps = layer.rms_eps
+        self.desc = d
+        self._keep = keep
+
+    forward = OracleMoe.forward

@@ -402,12 +402,18 @@ static void dequant_row(const or_moe_desc* d, int which, int64_t ex, int64_t row
                            1, kdim, dst);
   } else {
     const uint8_t* raw = which == 0 ? d->gate_raw : which == 1 ? d->up_raw : d->down_raw;
+    /* merged gate_up [E, 2I, H]: gate rows [0, I), up rows [I, 2I) (gemma4_q.rs:297-303) */
+    int64_t r = ex * rows + row;
+    if (which < 2 && d->gate_up_merged) {
+      raw = d->gate_raw;
+      r = ex * 2 * rows + (which == 1 ? rows : 0) + row;
+    }
     if (d->weight_format == OR_FMT_MXFP4_GGUF) {
       const int64_t rb = kdim / 32 * 17;
-      or_mxfp4_gguf_dequant(raw + (ex * rows + row) * rb, kdim, dst);
+      or_mxfp4_gguf_dequant(raw + r * rb, kdim, dst);
     } else {
       const int64_t rb = kdim / 256 * 144;
-      or_q4k_dequant(raw + (ex * rows + row) * rb, kdim, dst);
+      or_q4k_dequant(raw + r * rb, kdim, dst);
     }
   }
 }
@@ -476,8 +482,18 @@ static int check_desc(const or_moe_desc* d) {
   return 0;
 }
 
-int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out, int32_t* idx_out,
-                   float* w_out, int n_threads) {
+/* v / sqrt(mean(v^2) + eps), candle_nn::ops::rms_norm's arithmetic (the sum
+ * of squares in order). */
+static float rms_of(const float* v, int64_t n, float eps) {
+  float ss = 0.0f;
+  for (int64_t k = 0; k < n; ++k) ss += v[k] * v[k];
+  return sqrtf(ss / (float)n + eps);
+}
+
+/* The block from router logits to the combined output: the router reads
+ * x_route, the experts x. */
+static int moe_forward_core(const or_moe_desc* d, const float* x_route, const float* x, int64_t t,
+                            float* out, int32_t* idx_out, float* w_out, int n_threads) {
   int rc = check_desc(d);
   if (rc) return rc;
   const int64_t H = d->hidden, I = d->inter, E = d->n_experts, K = d->top_k;
@@ -494,7 +510,7 @@ int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out, 
     rc = fail(7, "out of host memory");
     goto done;
   }
-  rc = or_router_logits(x, d->router_w, d->router_b, t, H, E, logits);
+  rc = or_router_logits(x_route, d->router_w, d->router_b, t, H, E, logits);
   if (rc) goto done;
   rc = d->router_kind == OR_ROUTER_SOFTMAX_TOPK
            ? or_route_softmax_topk(logits, t, E, K, idx, w)
@@ -564,7 +580,10 @@ int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out, 
       float acc = 0.0f;
       for (int q = 0; q < K; ++q) {
         const int r = order[q];
-        const float term = y[(int64_t)inv[i * K + r] * H + o] * w[i * K + r];
+        float yv = y[(int64_t)inv[i * K + r] * H + o];
+        /* an expert's output scale comes before the routing weight (gemma4_q.rs:308-314) */
+        if (d->expert_scale) yv = yv * d->expert_scale[idx[i * K + r]];
+        const float term = yv * w[i * K + r];
         acc = acc + term;
       }
       out[i * H + o] = acc;
@@ -610,6 +629,46 @@ done:
   free(perm);
   free(inv);
   free(y);
+  return rc;
+}
+
+int or_moe_forward(const or_moe_desc* d, const float* x, int64_t t, float* out, int32_t* idx_out,
+                   float* w_out, int n_threads) {
+  int rc = check_desc(d);
+  if (rc) return rc;
+  if (d->input_norm != 1) {
+    rc = moe_forward_core(d, x, x, t, out, idx_out, w_out, n_threads);
+  } else {
+    /* Gemma-4: the router reads rms(x) * H^-0.5 * scale, the experts
+     * rms(x) * norm weight (gemma4_q.rs:267-276) */
+    const int64_t H = d->hidden;
+    float* xr = (float*)malloc(sizeof(float) * (size_t)(t * H) + 4);
+    float* xe = (float*)malloc(sizeof(float) * (size_t)(t * H) + 4);
+    if (!xr || !xe) {
+      free(xr);
+      free(xe);
+      return fail(7, "out of host memory");
+    }
+    const float inv_sqrt_h = (float)(1.0 / sqrt((double)H));
+    for (int64_t i = 0; i < t; ++i) {
+      const float m = rms_of(x + i * H, H, d->rms_eps);
+      for (int64_t k = 0; k < H; ++k) {
+        const float nv = x[i * H + k] / m;
+        xr[i * H + k] = nv * inv_sqrt_h * d->router_input_scale[k];
+        xe[i * H + k] = nv * d->expert_input_norm[k];
+      }
+    }
+    rc = moe_forward_core(d, xr, xe, t, out, idx_out, w_out, n_threads);
+    free(xr);
+    free(xe);
+  }
+  if (!rc && d->output_norm) { /* post_ffw_norm_2 (gemma4_q.rs:327) */
+    const int64_t H = d->hidden;
+    for (int64_t i = 0; i < t; ++i) {
+      const float m = rms_of(out + i * H, H, d->rms_eps);
+      for (int64_t k = 0; k < H; ++k) out[i * H + k] = out[i * H + k] / m * d->output_norm[k];
+    }
+  }
   return rc;
 }
 

@@ -126,6 +126,17 @@ typedef struct {
   const float* sh_up;
   const float* sh_down;
   float act_clamp;
+  /* Gemma-4 routed experts (gemma4_q.rs:187-330): merged gate_up (gate_raw
+   * [E, 2I, H], gate rows first); per-expert output scale [E]; input_norm 1:
+   * router on rms(x) * H^-0.5 * router_input_scale, experts on rms_norm(x) *
+   * expert_input_norm; output_norm [H] on the result. */
+  int32_t gate_up_merged;
+  const float* expert_scale;
+  int32_t input_norm;
+  const float* router_input_scale;
+  const float* expert_input_norm;
+  const float* output_norm;
+  float rms_eps;
 } or_moe_desc;
 
 /* Full block forward.  x [t, H] f32 -> out [t, H] f32.  Per active expert the

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/gallium_b200.h"
+
 namespace gb {
 
 constexpr unsigned kFullMask = 0xffffffffu;
@@ -89,6 +91,38 @@ __device__ __forceinline__ float act_gptoss(float g, float u, float limit) {
 __device__ __forceinline__ float act_silu(float g, float u) {
   const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
   return __fmul_rn(sg, u);
+}
+
+// gallium-core's Activation (ffn.rs:16-24) on the gate, clamped to
+// [-clamp, clamp] when clamp > 0 (ffn.rs:58-62): SiLU, GELU (erf, candle
+// gelu_erf), GELU (tanh, candle gelu; also Gemma-4's GEGLU,
+// gemma4_q.rs:305), ReLU.
+__device__ __forceinline__ float act_generic(int kind, float g, float clamp) {
+  float a;
+  switch (kind) {
+    case GB_ACT_GELU:
+      a = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, erff(__fmul_rn(g, 0.70710678118654752f))));
+      break;
+    case GB_ACT_GELU_TANH: {
+      const float inner = __fmul_rn(0.79788456080286536f,
+                                    __fadd_rn(g, __fmul_rn(0.044715f, __fmul_rn(g, __fmul_rn(g, g)))));
+      a = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(inner)));
+      break;
+    }
+    case GB_ACT_RELU:
+      a = fmaxf(g, 0.0f);
+      break;
+    default:
+      a = __fdiv_rn(g, __fadd_rn(expf(-g), 1.0f));
+  }
+  return clamp > 0.0f ? fminf(fmaxf(a, -clamp), clamp) : a;
+}
+
+// The expert activation h(gate, up) of every kind (gb_act_kind).
+__device__ __forceinline__ float act_apply(int kind, float g, float u, float limit, float clamp) {
+  if (kind == GB_ACT_GPTOSS_CLAMP) return act_gptoss(g, u, limit);
+  if (kind == GB_ACT_SILU && !(clamp > 0.0f)) return act_silu(g, u);
+  return __fmul_rn(act_generic(kind, g, clamp), u);
 }
 
 }  // namespace gb

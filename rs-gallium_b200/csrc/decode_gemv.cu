@@ -52,6 +52,7 @@ struct DecArgs {
   const int32_t* perm;
   int e_begin;
   int act_kind;
+  float clamp;  // act_clamp
   float limit;
   const int32_t* out_rows;  // DOWN: output row of each position (null: the position)
   float* out;
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) decode_rows_kernel(const DecAr
               u = __fadd_rn(u, a.bias[erow + row + 1]);
             }
             a.out[pos * a.out_stride + (row >> 1)] =
-                a.act_kind == GB_ACT_GPTOSS_CLAMP ? act_gptoss(g, u, a.limit) : act_silu(g, u);
+                act_apply(a.act_kind, g, u, a.limit, a.clamp);
           } else {
             float y0 = s0, y1 = s1;
             if (a.bias) {
@@ -230,6 +231,7 @@ DecArgs base_args(const Moe& m, const Groups& g) {
   a.perm = g.perm;
   a.e_begin = m.e_begin;
   a.act_kind = d.act_kind;
+  a.clamp = d.act_clamp;
   a.limit = d.swiglu_limit;
   return a;
 }

@@ -42,28 +42,6 @@ __device__ __forceinline__ void widen(const uint4& q, float (&v)[8], const float
   v[3] = __uint_as_float(q.w);
 }
 
-// The generic activation of ffn.rs:16-24 with the clamp of ffn.rs:58-62.
-__device__ __forceinline__ float act_generic(int kind, float g, float clamp) {
-  float a;
-  switch (kind) {
-    case GB_ACT_GELU:  // 0.5 x (1 + erf(x / sqrt 2)), candle gelu_erf
-      a = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, erff(__fmul_rn(g, 0.70710678118654752f))));
-      break;
-    case GB_ACT_GELU_TANH: {  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), candle gelu
-      const float inner = __fmul_rn(0.79788456080286536f,
-                                    __fadd_rn(g, __fmul_rn(0.044715f, __fmul_rn(g, __fmul_rn(g, g)))));
-      a = __fmul_rn(__fmul_rn(0.5f, g), __fadd_rn(1.0f, tanhf(inner)));
-      break;
-    }
-    case GB_ACT_RELU:
-      a = fmaxf(g, 0.0f);
-      break;
-    default:  // SiLU, candle silu: v / (exp(-v) + 1)
-      a = __fdiv_rn(g, __fadd_rn(expf(-g), 1.0f));
-  }
-  return clamp > 0.0f ? fminf(fmaxf(a, -clamp), clamp) : a;
-}
-
 // identity != 0: the shared expert: `identity` positions, position p = input
 // row p, weights at w0 / w1 directly (one expert).
 template <int MODE, int TC, typename W>

@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(kWarps * 32)
                        const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
                        const int32_t* __restrict__ active, const int32_t* __restrict__ meta,
                        const int32_t* __restrict__ perm, int e_begin, int act_kind, float limit,
-                       const int32_t* __restrict__ out_rows, float* __restrict__ out,
+                       float clamp, const int32_t* __restrict__ out_rows, float* __restrict__ out,
                        int out_stride) {
   extern __shared__ float xs[];  // [TC][33 * NB], element k at k + k/32
   const int slot = blockIdx.y;
@@ -137,8 +137,7 @@ __global__ void __launch_bounds__(kWarps * 32)
             g = __fadd_rn(g, bias[(int64_t)le * n_rows_total + row0]);
             u = __fadd_rn(u, bias[(int64_t)le * n_rows_total + row0 + 1]);
           }
-          out[pos * out_stride + pair] =
-              act_kind == GB_ACT_GPTOSS_CLAMP ? act_gptoss(g, u, limit) : act_silu(g, u);
+          out[pos * out_stride + pair] = act_apply(act_kind, g, u, limit, clamp);
         } else {
           float y0 = s0, y1 = s1;
           if (bias) {
@@ -174,7 +173,8 @@ cudaError_t launch_rows(const Moe& m, const Groups& g, const float* in, int K_in
     kern<<<grid, kWarps * 32, smem, st>>>(in, K_in, n_rows_total, g.perm_div, blocks, scales, sp, \
                                           bias, m.w.zero_scale, g.counts, g.offsets, g.active,   \
                                           g.meta, g.perm, m.e_begin, d.act_kind, d.swiglu_limit, \
-                                          MODE == DOWN ? g.out_rows : nullptr, out, out_stride); \
+                                          d.act_clamp, MODE == DOWN ? g.out_rows : nullptr, out,  \
+                                          out_stride);                                           \
   }
   switch (nbq) {
     case 1: GB_LAUNCH_NBQ(1) break;
@@ -192,8 +192,8 @@ cudaError_t launch_rows(const Moe& m, const Groups& g, const float* in, int K_in
 // (gpt_oss_q.rs:252-266, lfm2moe_q.rs:303-311) instead of rank order.
 __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv,
                                const float* __restrict__ wts, const int32_t* __restrict__ idx,
-                               int H, int K, int expert_order, const float* __restrict__ add,
-                               float* __restrict__ out) {
+                               int H, int K, int expert_order, const float* __restrict__ escale,
+                               const float* __restrict__ add, float* __restrict__ out) {
   pdl_trigger();
   pdl_wait();
   const int t = blockIdx.x;
@@ -233,12 +233,21 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
     const int r = order[q];
     float4 vr = v[0];
     float w = wv[0];
+    int er = e[0];
 #pragma unroll
     for (int i = 1; i < 8; ++i)
       if (i == r) {
         vr = v[i];
         w = wv[i];
+        er = e[i];
       }
+    if (escale) {  // the expert's output scale, before the routing weight (gemma4_q.rs:308-314)
+      const float s = escale[er];
+      vr.x = __fmul_rn(vr.x, s);
+      vr.y = __fmul_rn(vr.y, s);
+      vr.z = __fmul_rn(vr.z, s);
+      vr.w = __fmul_rn(vr.w, s);
+    }
     acc.x = __fadd_rn(acc.x, __fmul_rn(vr.x, w));
     acc.y = __fadd_rn(acc.y, __fmul_rn(vr.y, w));
     acc.z = __fadd_rn(acc.z, __fmul_rn(vr.z, w));
@@ -324,7 +333,7 @@ cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const f
   const float* add = m.desc.shared_inter > 0 ? (const float*)ws.sh_y : nullptr;
   return launch_pdl(combine_kernel, grid, dim3(threads), 0, st, y,
                     slots ? (const int32_t*)nullptr : (const int32_t*)ws.inv, ws.wts, ws.idx, H,
-                    m.desc.top_k, expert_order, add, out);
+                    m.desc.top_k, expert_order, (const float*)m.w.expert_scale, add, out);
 }
 
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,

@@ -88,12 +88,22 @@ int validate(const gb_moe_desc* d) {
     return set_err(GB_ERR_INVALID_ARG, "unknown router_kind %d", d->router_kind);
   if (d->act_kind < GB_ACT_GPTOSS_CLAMP || d->act_kind > GB_ACT_RELU)
     return set_err(GB_ERR_INVALID_ARG, "unknown act_kind %d", d->act_kind);
-  if (d->act_kind > GB_ACT_SILU && d->weight_format != GB_FMT_DENSE)
-    return set_err(GB_ERR_UNSUPPORTED, "act_kind %d needs GB_FMT_DENSE experts", d->act_kind);
+  if (d->act_kind > GB_ACT_SILU && d->weight_format == GB_FMT_MXFP4_SPLIT)
+    return set_err(GB_ERR_UNSUPPORTED, "act_kind %d does not apply to MXFP4_SPLIT experts",
+                   d->act_kind);
   if (!(d->act_clamp >= 0.0f) || (d->act_clamp > 0.0f && d->act_kind == GB_ACT_GPTOSS_CLAMP))
     return set_err(GB_ERR_INVALID_ARG,
                    "act_clamp must be >= 0 (and 0 for the GPT-OSS activation, which uses "
                    "swiglu_limit)");
+  if (d->gate_up_merged && d->weight_format != GB_FMT_MXFP4_GGUF && d->weight_format != GB_FMT_Q4_K)
+    return set_err(GB_ERR_INVALID_ARG, "gate_up_merged applies to GGUF MXFP4 and Q4_K experts");
+  if (d->input_norm != 0 && d->input_norm != 1)
+    return set_err(GB_ERR_INVALID_ARG, "unknown input_norm %d", d->input_norm);
+  if (d->input_norm == 1 && (!d->router_input_scale || !d->expert_input_norm))
+    return set_err(GB_ERR_INVALID_ARG,
+                   "input_norm 1 needs router_input_scale and expert_input_norm");
+  if ((d->input_norm || d->output_norm) && !(d->rms_eps >= 0.0f))
+    return set_err(GB_ERR_INVALID_ARG, "rms_eps must be >= 0");
   if (d->shared_inter < 0 || (d->shared_inter > 0 && d->weight_format != GB_FMT_DENSE))
     return set_err(GB_ERR_UNSUPPORTED, "a shared expert needs GB_FMT_DENSE experts");
   if (d->shared_inter > 0 &&
@@ -114,7 +124,7 @@ int validate(const gb_moe_desc* d) {
         return set_err(GB_ERR_INVALID_ARG, "MXFP4_SPLIT needs gate_up/down blocks and scales");
       break;
     case GB_FMT_MXFP4_GGUF:
-      if (!d->gate_raw || !d->up_raw || !d->down_raw)
+      if (!d->gate_raw || (!d->up_raw && !d->gate_up_merged) || !d->down_raw)
         return set_err(GB_ERR_INVALID_ARG, "MXFP4_GGUF needs gate_raw, up_raw and down_raw");
       break;
     case GB_FMT_DENSE:
@@ -126,7 +136,7 @@ int validate(const gb_moe_desc* d) {
         return set_err(GB_ERR_UNSUPPORTED, "DENSE experts take a gated activation");
       break;
     case GB_FMT_Q4_K:
-      if (!d->gate_raw || !d->up_raw || !d->down_raw)
+      if (!d->gate_raw || (!d->up_raw && !d->gate_up_merged) || !d->down_raw)
         return set_err(GB_ERR_INVALID_ARG, "Q4_K needs gate_raw, up_raw and down_raw");
       // QExperts::dequantize_expert (quantized.rs:162-177) refuses a ragged expert
       if (d->hidden % 256 != 0 || d->inter % 256 != 0)
@@ -229,6 +239,8 @@ int alloc_ws(gb::Moe& m, int64_t T) {
       {(void**)&ws.meta, sizeof(int32_t) * 4},
       {(void**)&ws.perm, sizeof(int32_t) * (size_t)(T * K)},
       {(void**)&ws.inv, sizeof(int32_t) * (size_t)(T * K)},
+      {(void**)&ws.x_route, d.input_norm ? sizeof(float) * (size_t)(T * H) : 0},
+      {(void**)&ws.x_expert, d.input_norm ? sizeof(float) * (size_t)(T * H) : 0},
       {(void**)&ws.sh_h, sizeof(float) * (size_t)(T * std::max(d.shared_inter, 0))},
       {(void**)&ws.sh_y, d.shared_inter > 0 ? sizeof(float) * (size_t)(T * H) : 0},
       {(void**)&ws.x_stage, sizeof(float) * (size_t)(T * H)},
@@ -293,7 +305,8 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.q4_dn);
   cudaFree(m.w.q4_gu_exp);
   for (void* p : {m.w.dense_gate, m.w.dense_up, m.w.dense_down, m.w.sh_gate, m.w.sh_up,
-                  m.w.sh_down})
+                  m.w.sh_down, (void*)m.w.expert_scale, (void*)m.w.router_in_scale,
+                  (void*)m.w.expert_in_norm, (void*)m.w.out_norm})
     cudaFree(p);
   gb::mx_release(m.mx);
   free_ws(m.ws);
@@ -317,11 +330,14 @@ int upload_q4k(gb::Moe& m) {
   for (int64_t le = 0; le < nloc; ++le) {
     const int64_t e = m.e_begin + le;
     uint8_t* dst = m.w.q4_gu + (size_t)(le * 2 * I) * rb_h;
-    GB_CUDA(cudaMemcpy2D(dst, 2 * rb_h, d.gate_raw + (size_t)(e * I) * rb_h, rb_h, rb_h, (size_t)I,
-                         cudaMemcpyHostToDevice),
+    // separate gate / up [E, I, H], or merged [E, 2I, H] with gate rows first
+    const uint8_t* gsrc = d.gate_up_merged ? d.gate_raw + (size_t)(e * 2 * I) * rb_h
+                                           : d.gate_raw + (size_t)(e * I) * rb_h;
+    const uint8_t* usrc = d.gate_up_merged ? gsrc + (size_t)I * rb_h
+                                           : d.up_raw + (size_t)(e * I) * rb_h;
+    GB_CUDA(cudaMemcpy2D(dst, 2 * rb_h, gsrc, rb_h, rb_h, (size_t)I, cudaMemcpyHostToDevice),
             "upload Q4_K gate");
-    GB_CUDA(cudaMemcpy2D(dst + rb_h, 2 * rb_h, d.up_raw + (size_t)(e * I) * rb_h, rb_h, rb_h,
-                         (size_t)I, cudaMemcpyHostToDevice),
+    GB_CUDA(cudaMemcpy2D(dst + rb_h, 2 * rb_h, usrc, rb_h, rb_h, (size_t)I, cudaMemcpyHostToDevice),
             "upload Q4_K up");
   }
   GB_CUDA(cudaMemcpy(m.w.q4_dn, d.down_raw + (size_t)(m.e_begin * H) * rb_i, dn_bytes,
@@ -413,9 +429,15 @@ int upload_weights(gb::Moe& m) {
     for (int64_t le = 0; le < nloc && rc == GB_OK; ++le) {
       const int64_t e = m.e_begin + le;
       for (int which = 0; which < 3 && rc == GB_OK; ++which) {
-        const uint8_t* src = which == 0 ? d.gate_raw : which == 1 ? d.up_raw : d.down_raw;
         const size_t bytes = which == 2 ? raw_down : raw_gate;
-        cudaError_t ce = cudaMemcpy(tmp, src + (size_t)e * bytes, bytes, cudaMemcpyHostToDevice);
+        const uint8_t* src;
+        if (which == 2)
+          src = d.down_raw + (size_t)e * bytes;
+        else if (d.gate_up_merged)  // [E, 2I, H]: gate rows, then up rows
+          src = d.gate_raw + (size_t)e * 2 * bytes + (size_t)which * bytes;
+        else
+          src = (which == 0 ? d.gate_raw : d.up_raw) + (size_t)e * bytes;
+        cudaError_t ce = cudaMemcpy(tmp, src, bytes, cudaMemcpyHostToDevice);
         if (ce == cudaSuccess) {
           if (which < 2) {
             // gate row i -> fused row 2i, up row i -> 2i+1
@@ -493,6 +515,22 @@ int upload_router(gb::Moe& m) {
     if ((rc = dev_alloc(&m.sel_bias, (size_t)E * 4, "selection bias"))) return rc;
     GB_CUDA(cudaMemcpy(m.sel_bias, d.selection_bias, (size_t)E * 4, cudaMemcpyHostToDevice),
             "upload selection bias");
+  }
+  // Gemma-4: expert output scales (all E: the combine reads them by global
+  // id) and the norm vectors
+  const struct {
+    float** dst;
+    const float* src;
+    int64_t n;
+  } vecs[] = {{&m.w.expert_scale, d.expert_scale, E},
+              {&m.w.router_in_scale, d.input_norm ? d.router_input_scale : nullptr, H},
+              {&m.w.expert_in_norm, d.input_norm ? d.expert_input_norm : nullptr, H},
+              {&m.w.out_norm, d.output_norm, H}};
+  for (const auto& v : vecs) {
+    if (!v.src) continue;
+    if ((rc = dev_alloc(v.dst, (size_t)v.n * 4, "Gemma-4 vector"))) return rc;
+    GB_CUDA(cudaMemcpy(*v.dst, v.src, (size_t)v.n * 4, cudaMemcpyHostToDevice),
+            "upload Gemma-4 vector");
   }
   return GB_OK;
 }
@@ -589,7 +627,8 @@ int run_route_grouped(gb::Moe& m, const float* x, int64_t T, gb::Groups& g, int 
 
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
   int rc;
-  if (m.ep_size == 1 && m.desc.weight_format != GB_FMT_Q4_K && gb::mx_group_fits(m, T) &&
+  if (m.ep_size == 1 && m.desc.weight_format != GB_FMT_Q4_K && !m.desc.input_norm &&
+      !m.w.out_norm && gb::mx_group_fits(m, T) &&
       pick_expert_kernel(m, m.ws.eb) == ExpertKernel::kMx) {
     gb::Groups g = local_groups(m, T);
     const int kind = std::min(gb::mx_tile_kind(m, g), gb::kMxKind30);
@@ -612,27 +651,39 @@ int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t 
     m.profiled_once = m.profiling;
     return GB_OK;
   }
+  // Gemma-4: the router and the experts read differently normed copies of x
+  const float* x_route = x;
+  const float* x_expert = x;
+  if (m.desc.input_norm && T > 0) {
+    GB_CUDA(gb::launch_input_norms(m, x, T, m.ws.x_route, m.ws.x_expert, st), "input norm launch");
+    x_route = m.ws.x_route;
+    x_expert = m.ws.x_expert;
+    m.launches += 1;
+  }
   if (T > 0) {
-    if ((rc = run_route(m, x, T, st))) return rc;
+    if ((rc = run_route(m, x_route, T, st))) return rc;
   } else {
     GB_CUDA(cudaMemsetAsync(m.ws.counts, 0, sizeof(int32_t) * m.desc.n_experts, st),
             "clear counts");
   }
   if (m.desc.shared_inter > 0 && T > 0) {  // shared expert over all tokens, added by combine
-    GB_CUDA(gb::launch_shared_expert(m, x, T, m.ws.sh_h, m.ws.sh_y, st), "shared expert launch");
+    GB_CUDA(gb::launch_shared_expert(m, x_expert, T, m.ws.sh_h, m.ws.sh_y, st),
+            "shared expert launch");
     m.launches += 2;
   }
   if (m.ep_size > 1) {
-    if ((rc = gb::ep_forward(m, x, T, out, st))) return rc;
-    if ((rc = mark(m, 5, st))) return rc;
-    m.profiled_once = m.profiling;
-    return GB_OK;
+    if ((rc = gb::ep_forward(m, x_expert, T, out, st))) return rc;
+  } else {
+    gb::Groups g = local_groups(m, T);
+    if ((rc = gb::run_experts(m, g, x_expert, T, m.ws.eb, st))) return rc;
+    if ((rc = mark(m, 4, st))) return rc;
+    GB_CUDA(gb::launch_combine(m, T, m.ws, m.ws.eb.y, out, st), "combine kernel launch");
+    m.launches += 1;
   }
-  gb::Groups g = local_groups(m, T);
-  if ((rc = gb::run_experts(m, g, x, T, m.ws.eb, st))) return rc;
-  if ((rc = mark(m, 4, st))) return rc;
-  GB_CUDA(gb::launch_combine(m, T, m.ws, m.ws.eb.y, out, st), "combine kernel launch");
-  m.launches += 1;
+  if (m.w.out_norm && T > 0) {  // post_ffw_norm_2 on the result
+    GB_CUDA(gb::launch_output_norm(m, out, T, st), "output norm launch");
+    m.launches += 1;
+  }
   if ((rc = mark(m, 5, st))) return rc;
   m.profiled_once = m.profiling;
   return GB_OK;

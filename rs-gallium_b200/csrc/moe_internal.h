@@ -81,6 +81,12 @@ struct ExpertWeights {
   void* sh_up = nullptr;
   void* sh_down = nullptr;
   bool dense_bf16 = false;
+  // Gemma-4: per-expert output scale [E] (all experts: the combine reads it),
+  // input / output norm vectors [H]
+  float* expert_scale = nullptr;
+  float* router_in_scale = nullptr;
+  float* expert_in_norm = nullptr;
+  float* out_norm = nullptr;
 };
 
 // Weights in the block-scaled tensor-core layout (mx_gemm.cu), built from
@@ -172,6 +178,8 @@ struct Workspace {
   int32_t* meta = nullptr;     // [0] active count, [1] error flags, [2] N tiles
   int32_t* perm = nullptr;     // [T*k]
   int32_t* inv = nullptr;      // [T*k]
+  float* x_route = nullptr;    // [T, H] the router's input (input_norm 1)
+  float* x_expert = nullptr;   // [T, H] the experts' input (input_norm 1)
   float* sh_h = nullptr;       // [T, Is] shared expert's activation (GB_FMT_DENSE)
   float* sh_y = nullptr;       // [T, H] shared expert's output
   float* x_stage = nullptr;    // [T, H] host-path staging
@@ -324,6 +332,12 @@ cudaError_t launch_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaSt
 // with `slots`, y is indexed by t*k + r directly (expert-parallel return slots).
 cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const float* y, float* out,
                            cudaStream_t st, bool slots = false);
+
+// Gemma-4 norms (norm.cu): the router's and the experts' inputs from x, and
+// the output norm in place.
+cudaError_t launch_input_norms(const Moe& m, const float* x, int64_t T, float* x_route,
+                               float* x_expert, cudaStream_t st);
+cudaError_t launch_output_norm(const Moe& m, float* out, int64_t T, cudaStream_t st);
 
 // Dense experts on CUDA cores (dense_gemv.cu): the generic MoEFFN.
 cudaError_t launch_dense_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,

@@ -38,6 +38,7 @@ struct QArgs {
   const int32_t* perm;
   int e_begin;
   int act_kind;
+  float clamp;  // act_clamp
   float limit;
   const int32_t* out_rows;
   float* out;
@@ -226,7 +227,7 @@ __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
           const int64_t pos = p0 + c0 + t;
           if (MODE == GATE_UP) {
             a.out[pos * a.out_stride + (row >> 1)] =
-                a.act_kind == GB_ACT_GPTOSS_CLAMP ? act_gptoss(s0, s1, a.limit) : act_silu(s0, s1);
+                act_apply(a.act_kind, s0, s1, a.limit, a.clamp);
           } else {
             const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
             a.out[orow * a.out_stride + row] = s0;
@@ -275,6 +276,7 @@ QArgs q_args(const Moe& m, const Groups& g) {
   a.perm = g.perm;
   a.e_begin = m.e_begin;
   a.act_kind = m.desc.act_kind;
+  a.clamp = m.desc.act_clamp;
   a.limit = m.desc.swiglu_limit;
   return a;
 }

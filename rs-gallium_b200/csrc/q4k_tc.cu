@@ -62,6 +62,7 @@ struct Args {
   const int32_t* tile_rows;
   const float* xscale;    // GATE_UP: exponent s of each position's row
   int act_kind;
+  float clamp;  // act_clamp
   float limit;
   __half* out_hi;         // GATE_UP: h hi [positions][I]
   __half* out_lo;
@@ -175,8 +176,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
         // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
         const float up = __shfl_down_sync(kFullMask, val, 1);
         if ((m & 1) == 0 && valid && n < it.nrows) {
-          const float h = a.act_kind == GB_ACT_GPTOSS_CLAMP ? act_gptoss(val, up, a.limit)
-                                                            : act_silu(val, up);
+          const float h = act_apply(a.act_kind, val, up, a.limit, a.clamp);
           const __half hi = __float2half_rn(h);
           const __half lo = __float2half_rn(__fsub_rn(h, __half2float(hi)));
           const int64_t o = pos * a.out_stride + (row >> 1);
@@ -458,6 +458,7 @@ q4tc::Args q4tc_args(const Moe& m, const Groups& g, ExpertBufs& eb) {
   a.tile_row0 = eb.tile_row0;
   a.tile_rows = eb.tile_rows;
   a.act_kind = m.desc.act_kind;
+  a.clamp = m.desc.act_clamp;
   a.limit = m.desc.swiglu_limit;
   a.err = g.meta + 1;
   return a;

@@ -94,6 +94,13 @@ class MoeDesc(ctypes.Structure):
         ("shared_gate", c_void_p),
         ("shared_up", c_void_p),
         ("shared_down", c_void_p),
+        ("gate_up_merged", c_int32),
+        ("expert_scale", c_void_p),
+        ("input_norm", c_int32),
+        ("router_input_scale", c_void_p),
+        ("expert_input_norm", c_void_p),
+        ("output_norm", c_void_p),
+        ("rms_eps", c_float),
     ]
 
 

@@ -23,7 +23,8 @@ import numpy as np
 
 from . import _lib
 from ._lib import MoeDesc, MoeInfo, check, load_library
-from .synth import DenseMoeLayer, GptOssGgufLayer, GptOssLayer, Lfm2Layer, bf16_bits_to_f32
+from .synth import (DenseMoeLayer, Gemma4MoeLayer, GptOssGgufLayer, GptOssLayer, Lfm2Layer,
+                    bf16_bits_to_f32)
 
 
 def _as_f32(a: Optional[np.ndarray]) -> Optional[np.ndarray]:
@@ -333,3 +334,36 @@ class MoEFFN(MoEBlock):
         if layer.shared_inter:
             d.shared_gate, d.shared_up, d.shared_down = [_ptr(a) for a in mats[3:]]
         return cls(d, mats + [rw, getattr(d, "_nccl_id_buf", None)])
+
+
+class QGemmaMoe(MoEBlock):
+    """Gemma-4's routed experts (QGemmaMoe, crates/gallium-models/src/gemma4_q.rs:187-330):
+    forward(attn_out) = post_ffw_norm_2(sum of the top-k experts' scaled
+    outputs), the router reading rms(x) / sqrt(H) * ffn_gate_inp.scale, the
+    experts reading pre_ffw_norm_2(x), merged gate_up (gate rows first), GELU
+    (tanh) gating, GGUF MXFP4 or Q4_K experts."""
+
+    @classmethod
+    def load(cls, layer: Gemma4MoeLayer, device: int = 0, max_tokens: int = 64,
+             ep=None) -> "QGemmaMoe":
+        d = _base_desc(layer.hidden, layer.inter, layer.n_experts, layer.top_k, device,
+                       max_tokens, ep)
+        d.router_kind = _lib.GB_ROUTER_SOFTMAX_TOPK
+        d.act_kind = _lib.GB_ACT_GELU_TANH
+        d.weight_format = layer.fmt
+        d.gate_up_merged = 1
+        arrs = [np.ascontiguousarray(a) for a in (
+            layer.router_w.astype(np.float32), layer.gate_up_raw, layer.down_raw,
+            layer.router_scale.astype(np.float32), layer.expert_norm.astype(np.float32),
+            layer.output_norm.astype(np.float32))]
+        (d.router_weight, d.gate_raw, d.down_raw, d.router_input_scale, d.expert_input_norm,
+         d.output_norm) = [_ptr(a) for a in arrs]
+        d.router_dtype = _lib.GB_DTYPE_F32
+        d.bias_dtype = _lib.GB_DTYPE_F32
+        d.input_norm = 1
+        d.rms_eps = layer.rms_eps
+        if layer.expert_scale is not None:
+            es = np.ascontiguousarray(layer.expert_scale, np.float32)
+            arrs.append(es)
+            d.expert_scale = _ptr(es)
+        return cls(d, arrs + [getattr(d, "_nccl_id_buf", None)])

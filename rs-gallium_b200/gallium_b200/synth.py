@@ -254,3 +254,51 @@ def dense_layer(n_experts: int = 128, hidden: int = 2048, inter: int = 768, top_
         layer.sh_up = normal((shared_inter, H), H ** -0.5)
         layer.sh_down = normal((H, shared_inter), shared_inter ** -0.5)
     return layer
+
+
+# ---- Gemma-4 routed experts (gemma4_q.rs:187-330) ---------------------------
+
+@dataclass
+class Gemma4MoeLayer:
+    hidden: int
+    inter: int               # n_ff_exp
+    n_experts: int
+    top_k: int
+    fmt: int                 # gb_weight_format: 1 GGUF MXFP4 or 2 Q4_K
+    router_w: np.ndarray     # [E, H] f32 (ffn_gate_inp, dequantised)
+    router_scale: np.ndarray  # [H] f32 (ffn_gate_inp.scale)
+    expert_norm: np.ndarray  # [H] f32 (pre_ffw_norm_2)
+    gate_up_raw: np.ndarray  # [E, 2I, row bytes]: gate rows, then up rows
+    down_raw: np.ndarray     # [E, H, row bytes]
+    expert_scale: Optional[np.ndarray]  # [E] f32 (ffn_down_exps.scale) or None
+    output_norm: np.ndarray  # [H] f32 (post_ffw_norm_2)
+    rms_eps: float = 1e-6
+    meta: dict = field(default_factory=dict)
+
+
+def gemma4_layer(n_experts: int = 128, hidden: int = 2816, inter: int = 704, top_k: int = 8,
+                 fmt: int = 1, seed: int = 0, expert_scale: bool = True) -> Gemma4MoeLayer:
+    """A Gemma-4-26B-A4B-like routed-experts block with random weights (the
+    default shape is the 26B-A4B one: hidden 2816, 128 experts, top-8, expert
+    intermediate 704).  Experts in GGUF MXFP4 (fmt 1: codes uniform, E8M0
+    exponents uniform in [-8, -2]) or Q4_K (fmt 2: H and I multiples of 256).
+    Router ~ N(0, 1) (its input is normed to ~ N(0, 1/H)); norm weights and
+    the router scale uniform in [0.5, 1.5]; expert scales uniform in
+    [0.5, 2]."""
+    rng = np.random.default_rng(seed)
+    E, H, I = n_experts, hidden, inter
+    if fmt == 1:
+        def mx(rows, k):
+            b = _uniform_bytes(rng, (E, rows, k // 32, 16))
+            sc = rng.integers(119, 126, (E, rows, k // 32), dtype=np.uint8)
+            return split_to_gguf_blocks(b, sc)
+        gu, dn = mx(2 * I, H), mx(H, I)
+    else:
+        d, dmin = 2.0 ** -11, 15 * 2.0 ** -12
+        gu = np.stack([q4k_blocks(rng, 2 * I, H, d, dmin) for _ in range(E)])
+        dn = np.stack([q4k_blocks(rng, H, I, d, dmin) for _ in range(E)])
+    u = lambda n: rng.uniform(0.5, 1.5, n).astype(np.float32)
+    return Gemma4MoeLayer(H, I, E, top_k, fmt, rng.standard_normal((E, H), dtype=np.float32),
+                          u(H), u(H), gu, dn,
+                          rng.uniform(0.5, 2.0, E).astype(np.float32) if expert_scale else None,
+                          u(H), meta={"seed": seed})
