@@ -231,6 +231,7 @@ int alloc_ws(gb::Moe& m, int64_t T) {
   Piece pieces[] = {
       {(void**)&ws.logits, sizeof(float) * (size_t)(T * E)},
       {(void**)&ws.tickets, sizeof(unsigned) * (size_t)T},
+      {(void**)&ws.grid_bar, sizeof(unsigned) * 2},
       {(void**)&ws.idx, sizeof(int32_t) * (size_t)(T * K)},
       {(void**)&ws.wts, sizeof(float) * (size_t)(T * K)},
       {(void**)&ws.counts, sizeof(int32_t) * (size_t)E},
@@ -604,6 +605,8 @@ int read_device_status(gb::Moe& m, cudaStream_t st) {
     if (int* a = gb::ep_arrivals(m))
       GB_CUDA(cudaMemsetAsync(a, 0, 2 * sizeof(int) * (size_t)gb::kMxSplitSlots, st),
               "clear split-K tickets");
+    if (m.ws.grid_bar)  // a grid barrier left mid-count
+      GB_CUDA(cudaMemsetAsync(m.ws.grid_bar, 0, sizeof(unsigned), st), "clear grid barrier");
     GB_CUDA(cudaStreamSynchronize(st), "clear split-K tickets");
   }
   if (bits & 2) return set_err(GB_ERR_TIMEOUT, "a tensor-core pipeline wait timed out on the device");
@@ -627,6 +630,18 @@ int run_route_grouped(gb::Moe& m, const float* x, int64_t T, gb::Groups& g, int 
 
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
   int rc;
+  if (m.expert_path == GB_PATH_AUTO && gb::fused_decode_fits(m, T)) {
+    // one launch: the router, grouping, expert and combine stages of the
+    // profile are empty except the expert stage, which holds the kernel
+    for (int i = 0; i < 3; ++i)
+      if ((rc = mark(m, i, st))) return rc;
+    GB_CUDA(gb::launch_fused_decode(m, x, T, out, st), "fused decode launch");
+    m.launches += 1;
+    for (int i = 3; i < 6; ++i)
+      if ((rc = mark(m, i, st))) return rc;
+    m.profiled_once = m.profiling;
+    return GB_OK;
+  }
   if (m.ep_size == 1 && m.desc.weight_format != GB_FMT_Q4_K && !m.desc.input_norm &&
       !m.w.out_norm && gb::mx_group_fits(m, T) &&
       pick_expert_kernel(m, m.ws.eb) == ExpertKernel::kMx) {
@@ -741,8 +756,10 @@ gb::Moe::Graph* find_slot(gb::Moe::Graph* slots, int n, const float* x, int64_t 
 // one from the host would dominate); other forwards launch their kernels
 // directly.
 int forward_dispatch(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
+  // the fused decode forward is one (cooperative) launch: nothing to replay
   if (m.ep_size > 1 || m.profiling || m.graph_slots <= 0 || T <= 0 ||
-      T > gb::Moe::kGraphMaxTokens)
+      T > gb::Moe::kGraphMaxTokens ||
+      (m.expert_path == GB_PATH_AUTO && gb::fused_decode_fits(m, T)))
     return run_forward(m, x, T, out, st);
   gb::Moe::Graph* victim = nullptr;
   gb::Moe::Graph* hit = find_slot(m.graphs, m.graph_slots, x, T, out, &victim);
@@ -992,6 +1009,10 @@ int gb_moe_create(const gb_moe_desc* desc, gb_moe** out) {
   if (!rc && gb::mx_supported(m)) {
     ce = gb::mx_prepare_weights(m);
     if (ce != cudaSuccess) rc = cuda_err(ce, "block-scaled weight layout");
+  }
+  if (!rc && (desc->weight_format == GB_FMT_MXFP4_SPLIT || desc->weight_format == GB_FMT_MXFP4_GGUF)) {
+    ce = gb::fused_decode_prepare(m);
+    if (ce != cudaSuccess) rc = cuda_err(ce, "fused decode kernel set-up");
   }
   if (!rc) rc = alloc_ws(m, std::max(1, desc->max_tokens));
   if (rc) {

@@ -170,6 +170,7 @@ struct Workspace {
   void* base = nullptr;
   float* logits = nullptr;     // [T, E] router logits
   unsigned* tickets = nullptr; // [T] per token tile, zero between forwards
+  unsigned* grid_bar = nullptr;  // [2] fused decode kernel's grid barrier (arrivals, generation)
   int32_t* idx = nullptr;      // [T*k]
   float* wts = nullptr;        // [T*k]
   int32_t* counts = nullptr;   // [E]
@@ -215,6 +216,7 @@ struct Moe {
   // (0 = default) and the withheld ready flag of the one-launch kernel
   uint64_t test_wait_ns = 0;
   int test_withhold_ready = 0;
+  int fused_ctas = 0;  // CTAs of the fused decode kernel's cooperative grid (0: unavailable)
   // gb_moe_forward_host pipelining: copy streams and chunk events (lazily made)
   cudaStream_t h2d = nullptr, d2h = nullptr;
   cudaEvent_t host_ev[2 + 2 * kHostChunksMax] = {};
@@ -338,6 +340,13 @@ cudaError_t launch_combine(const Moe& m, int64_t T, const Workspace& ws, const f
 cudaError_t launch_input_norms(const Moe& m, const float* x, int64_t T, float* x_route,
                                float* x_expert, cudaStream_t st);
 cudaError_t launch_output_norm(const Moe& m, float* out, int64_t T, cudaStream_t st);
+
+// The whole layer in one cooperative launch for decode-sized single-GPU
+// batches of MXFP4 experts (decode_fused.cu).
+bool fused_decode_fits(const Moe& m, int64_t T);
+cudaError_t fused_decode_prepare(Moe& m);
+cudaError_t launch_fused_decode(const Moe& m, const float* x, int64_t T, float* out,
+                                cudaStream_t st);
 
 // Dense experts on CUDA cores (dense_gemv.cu): the generic MoEFFN.
 cudaError_t launch_dense_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
