@@ -344,13 +344,12 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_decode_kernel(const FusedA
   }
 }
 
-size_t fused_smem(const Moe& m) {
-  const gb_moe_desc& d = m.desc;
-  const int sp = std::max(m.w.sp_h, m.w.sp_i);
-  const int slot = 2 * (kMaxNB * 16 + sp);
-  (void)d;
-  return (size_t)kMaxTok * kMaxNB * kPitch * sizeof(float) + (size_t)kFWarps * kRing * slot;
-}
+// One size for every handle (the kernel attribute is shared by all of them):
+// the largest rows (K = 3072: 96 blocks, 96 scale bytes).
+constexpr size_t kFusedSmem = (size_t)kMaxTok * kMaxNB * kPitch * sizeof(float) +
+                              (size_t)kFWarps * kRing * 2 * (kMaxNB * 16 + kMaxNB);
+
+size_t fused_smem(const Moe&) { return kFusedSmem; }
 
 }  // namespace
 
