@@ -246,7 +246,10 @@ int gb_moe_get_info(const gb_moe* m, gb_moe_info* info);
  * failure. */
 int gb_moe_device_status(gb_moe* m, void* stream);
 
-/* Which kernels run the expert products.  AUTO and TENSOR_CORES pick the
+/* Which kernels run the expert products.  AUTO runs a single-GPU MXFP4
+ * batch of at most 8 tokens (and 32 token-expert entries) as one fused
+ * cooperative launch (router, grouping, expert rows on the CUDA cores,
+ * combine) and otherwise does what TENSOR_CORES does.  AUTO and TENSOR_CORES pick the
  * block-scaled tcgen05 GEMM (MXFP4 weights as stored, activations as four
  * E4M3 pieces, tiles of 256 weight rows x 2-32 positions chosen from the
  * batch); CUDA_CORES forces the streaming MXFP4 rows with f32 FMA;
@@ -264,7 +267,9 @@ typedef enum {
 int gb_moe_set_expert_path(gb_moe* m, int32_t path);
 
 /* Forward graphs.  A single-GPU gb_moe_forward (and gb_moe_forward_host) of
- * at most 512 tokens is captured once per (x, out, T) into a CUDA graph and
+ * at most 512 tokens (except the batches of at most 8 tokens that the
+ * AUTO path runs as one fused launch) is captured once per (x, out, T) into a
+ * CUDA graph and
  * replayed on later calls with the same triple, which removes the host launch
  * cost of its kernels; the graph reads x and writes out at replay time, so
  * new contents of the same buffers are used.  Up to `max_graphs` (0..16,

@@ -470,9 +470,10 @@ def test_tensor_cores_on_odd_shapes():
 
 def test_graph_replay_equals_direct_launches(moe32, layer32):
     # the same buffers three times: launched directly, captured, replayed; new
-    # contents of x between calls are read by the replay
+    # contents of x between calls are read by the replay.  Batches of at most
+    # 8 tokens run as one fused launch and are never captured (checked last).
     torch = _torch()
-    for T in (1, 7, 64):
+    for T in (9, 13, 64):
         xs = [synth.tokens(T, 2880, seed=400 + 10 * T + i) for i in range(3)]
         xd = torch.empty((T, 2880), device="cuda")
         out = torch.empty_like(xd)
@@ -493,28 +494,38 @@ def test_graph_replay_equals_direct_launches(moe32, layer32):
         assert moe32.info()["graph_captures"] - c0 == 1
         want, _, _ = oracle.OracleMoe(layer32).forward(xs[2])
         assert_parity(direct[2], want, f"graph T={T}")
+    xd = _cuda(synth.tokens(8, 2880, seed=401))
+    out = torch.empty_like(xd)
+    c0 = moe32.info()["graph_captures"]
+    first = None
+    for _ in range(3):
+        moe32.forward_raw(xd.data_ptr(), 8, out.data_ptr())
+        moe32.device_status()
+        first = out.cpu().numpy() if first is None else first
+        assert np.array_equal(out.cpu().numpy(), first)
+    assert moe32.info()["graph_captures"] == c0
 
 
 def test_graph_cache_replaces_the_least_recently_used(moe32):
     torch = _torch()
     moe32.set_graphs(2)
     try:
-        xd = _cuda(synth.tokens(8, 2880, seed=77))
+        xd = _cuda(synth.tokens(16, 2880, seed=77))
         out = torch.empty_like(xd)
         ref = {}
         moe32.set_graphs(0)
-        for T in (2, 4, 8):
+        for T in (10, 12, 16):
             moe32.forward_raw(xd.data_ptr(), T, out.data_ptr())
             torch.cuda.synchronize()
             ref[T] = out[:T].cpu().numpy()
         moe32.set_graphs(2)
         c0 = moe32.info()["graph_captures"]
-        for T in (2, 2, 4, 4, 8, 8, 2, 2):
+        for T in (10, 10, 12, 12, 16, 16, 10, 10):
             out.zero_()
             moe32.forward_raw(xd.data_ptr(), T, out.data_ptr())
             torch.cuda.synchronize()
             assert np.array_equal(out[:T].cpu().numpy(), ref[T]), f"T={T}"
-        # 2, 4, 8 captured; 8 replaced 2, so 2 was seen again and captured again
+        # 10, 12, 16 captured; 16 replaced 10, so 10 was seen again and captured again
         assert moe32.info()["graph_captures"] - c0 == 4
     finally:
         moe32.set_graphs(16)
@@ -523,8 +534,11 @@ def test_graph_cache_replaces_the_least_recently_used(moe32):
 @pytest.mark.parametrize("T", [1, 5, 127, 128, 129])
 def test_one_launch_grouping_matches_oracle(layer32_skew, T):
     # up to 512 routing entries the grouping, tile table and activation pieces
-    # come from one launch; 129 tokens x top-4 take the separate kernels
+    # come from one launch; 129 tokens x top-4 take the separate kernels (the
+    # tensor-core path is forced: batches of <= 8 tokens would otherwise run
+    # the fused decode kernel)
     m = OssMoEFFN.load(layer32_skew, device=0, max_tokens=T)
+    m.set_expert_path("tensor_cores")
     try:
         x = synth.tokens(T, 2880, seed=500 + T)
         got = m.forward(_cuda(x)).cpu().numpy()
