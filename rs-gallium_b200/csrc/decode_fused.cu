@@ -9,18 +9,20 @@
 // starting up and waiting on each other; here one persistent grid (every CTA
 // resident, one per SM) runs five phases separated by grid barriers (a
 // counter and a generation word in global memory, every wait bounded):
-//   1. router logits: one warp per (token, expert), the router kernel's
-//      reduction order (lane-strided FMAs, butterfly, bias), so the logits
-//      are bit-identical to it;
+//   1. router logits: the token rows staged in shared memory, one warp per
+//      expert with its router row loaded into registers at once, the router
+//      kernel's reduction order (lane-strided FMAs, butterfly, bias), so the
+//      logits are bit-identical to it;
 //   2. (no barrier after) every CTA selects the top-k of every token from the
 //      logits with the router's select_topk and builds the same grouping
 //      (experts ascending, tokens ascending) in shared memory;
-//   3. gate_up: the active experts' 2I rows in tasks of kPairs row pairs, a
-//      contiguous range of tasks per CTA (so a CTA stages the inputs of one or
-//      two experts); each warp streams its row pairs through a shared-memory
-//      ring with 16-byte cp.async copies (MXFP4 blocks and E8M0 bytes), decodes
-//      them in registers and dots them with the expert's staged token rows;
-//      bias + activation -> h;
+//   3. gate_up: the active experts' 2I rows as row pairs, a contiguous range
+//      of pairs per CTA (so a CTA stages the inputs of one or two experts) and
+//      a contiguous run per warp; each warp streams its pairs through a
+//      shared-memory ring with 16-byte cp.async copies (MXFP4 blocks and E8M0
+//      bytes), decodes them in registers and dots them with the expert's
+//      staged token rows (the token count a template parameter, 1, 2, 4 or
+//      8, so the unrolled body stays small); bias + activation -> h;
 //   4. down: the same over the H rows with the staged h rows -> y (+ bias);
 //   5. combine: out[t] = sum over ranks of w * y, in the reference's order.
 // Phases 3 and 4 read each weight byte from HBM once; the grid barriers cost
@@ -40,7 +42,6 @@ constexpr int kFThreads = kFWarps * 32;
 constexpr int kMaxTok = 8;      // tokens of one forward
 constexpr int kMaxPos = 32;     // token-expert entries
 constexpr int kMaxK = 8;        // top-k
-constexpr int kPairs = 4;       // row pairs per warp task
 constexpr int kRing = 3;        // row-pair slots per warp (2 in flight)
 constexpr int kPitch = 36;      // floats per staged 32-element block (+4 pad)
 constexpr int kMaxNB = 96;      // 32-element blocks per row (K <= 3072)
@@ -116,133 +117,160 @@ __device__ bool grid_barrier(const FusedArgs& a, int* s_ok) {
   return *s_ok != 0;
 }
 
-// One phase of expert rows (MODE 0: gate_up over 2I rows with K = H; 1: down
-// over H rows with K = I).  Tasks (slot, kPairs row pairs) in a contiguous
-// range per CTA; per expert the CTA stages its positions' input rows.
+// The rows of one phase (MODE 0: gate_up, 2I rows, K = H; 1: down, H rows,
+// K = I) as this warp sees them.
+struct PhaseRows {
+  const uint8_t* blocks;
+  const uint8_t* scales;
+  const float* bias;
+  int K, rows, NB, sp, row_bytes, slot_bytes, xstride;
+};
+
+// This warp's contiguous run of row pairs [q0, q1) of local expert le,
+// streamed through its ring (kRing - 1 pairs in flight), dotted with the TC
+// (>= n) staged rows of xs; results to h (MODE 0) or y (MODE 1) at positions
+// p0 .. p0 + n - 1.  The token count is a template parameter so that the
+// unrolled body stays small (the usual decode expert has one token).
+template <int MODE, int TC>
+__device__ void stream_pairs(const FusedArgs& a, const PhaseRows& R, const float* xs,
+                             uint8_t* ring, int le, int q0, int q1, int p0, int n) {
+  const int lane = threadIdx.x & 31;
+  const int64_t erow = (int64_t)le * R.rows;
+  const int np = q1 - q0;
+  auto fetch = [&](int p) {
+    if (p < np) {
+      uint8_t* dst = ring + (p % kRing) * R.slot_bytes;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int64_t row = erow + 2 * (q0 + p) + r;
+        const uint8_t* rbp = R.blocks + row * R.row_bytes;
+        for (int c = lane; c < R.NB; c += 32) cp_async16(dst + r * R.row_bytes + c * 16, rbp + c * 16);
+        const uint8_t* rs = R.scales + row * R.sp;
+        for (int c = lane; c < (R.sp >> 4); c += 32)
+          cp_async16(dst + 2 * R.row_bytes + r * R.sp + c * 16, rs + c * 16);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int p = 0; p < kRing - 1; ++p) fetch(p);
+  for (int p = 0; p < np; ++p) {
+    fetch(p + kRing - 1);
+    cp_async_wait<kRing - 1>();
+    __syncwarp();
+    const uint8_t* sl = ring + (p % kRing) * R.slot_bytes;
+    float acc[2][TC];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int t = 0; t < TC; ++t) acc[r][t] = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+#pragma unroll
+      for (int i = 0; i < kMaxNB / 32; ++i) {
+        const int b = lane + 32 * i;
+        if (b >= R.NB) continue;
+        const uint4 q = *reinterpret_cast<const uint4*>(sl + r * R.row_bytes + b * 16);
+        const float sc = e8m0_scale(sl[2 * R.row_bytes + r * R.sp + b], a.zero_scale);
+        float v[32];
+        decode_block_f32(q, v);
+#pragma unroll
+        for (int t = 0; t < TC; ++t) {
+          if (TC == 1 || t < n) {
+            const float4* x4 = reinterpret_cast<const float4*>(xs + t * R.xstride + b * kPitch);
+            float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f, f3 = 0.0f;
+#pragma unroll
+            for (int q4 = 0; q4 < 8; ++q4) {
+              const float4 xv = x4[q4];
+              f0 = __fmaf_rn(xv.x, v[4 * q4], f0);
+              f1 = __fmaf_rn(xv.y, v[4 * q4 + 1], f1);
+              f2 = __fmaf_rn(xv.z, v[4 * q4 + 2], f2);
+              f3 = __fmaf_rn(xv.w, v[4 * q4 + 3], f3);
+            }
+            acc[r][t] = __fmaf_rn(__fadd_rn(__fadd_rn(f0, f1), __fadd_rn(f2, f3)), sc, acc[r][t]);
+          }
+        }
+      }
+    }
+    __syncwarp();  // the slot is refilled by a later fetch
+    const int row = 2 * (q0 + p);
+#pragma unroll
+    for (int t = 0; t < TC; ++t) {
+      if (TC > 1 && t >= n) break;
+      const float s0 = warp_sum_butterfly(acc[0][t]);
+      const float s1 = warp_sum_butterfly(acc[1][t]);
+      if (lane == 0) {
+        const int64_t pos = p0 + t;
+        if (MODE == 0) {
+          float g = s0, u = s1;
+          if (R.bias) {
+            g = __fadd_rn(g, R.bias[erow + row]);
+            u = __fadd_rn(u, R.bias[erow + row + 1]);
+          }
+          a.h[pos * a.I + (row >> 1)] = act_apply(a.act_kind, g, u, a.limit, a.clamp);
+        } else {
+          float y0 = s0, y1 = s1;
+          if (R.bias) {
+            y0 = __fadd_rn(y0, R.bias[erow + row]);
+            y1 = __fadd_rn(y1, R.bias[erow + row + 1]);
+          }
+          a.y[pos * a.H + row] = y0;
+          a.y[pos * a.H + row + 1] = y1;
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// One phase over the active experts' row pairs: a contiguous range of pairs
+// per CTA (so a CTA stages the inputs of one or two experts), split into a
+// contiguous run per warp inside each expert.
 template <int MODE>
 __device__ void expert_phase(const FusedArgs& a, uint8_t* smem, const int* s_act, const int* s_off,
                              const int* s_tok, int nact) {
-  const int K = MODE == 0 ? a.H : a.I;
-  const int rows = MODE == 0 ? 2 * a.I : a.H;
-  const int NB = K >> 5;
-  const int sp = MODE == 0 ? a.sp_h : a.sp_i;
-  const int row_bytes = NB * 16;
-  const int slot_bytes = 2 * (row_bytes + sp);
-  const int xstride = NB * kPitch;
-  const uint8_t* blocks = MODE == 0 ? a.gu_blocks : a.dn_blocks;
-  const uint8_t* scales = MODE == 0 ? a.gu_scales : a.dn_scales;
-  const float* bias = MODE == 0 ? a.gu_bias : a.dn_bias;
+  PhaseRows R;
+  R.K = MODE == 0 ? a.H : a.I;
+  R.rows = MODE == 0 ? 2 * a.I : a.H;
+  R.NB = R.K >> 5;
+  R.sp = MODE == 0 ? a.sp_h : a.sp_i;
+  R.row_bytes = R.NB * 16;
+  R.slot_bytes = 2 * (R.row_bytes + R.sp);
+  R.xstride = R.NB * kPitch;
+  R.blocks = MODE == 0 ? a.gu_blocks : a.dn_blocks;
+  R.scales = MODE == 0 ? a.gu_scales : a.dn_scales;
+  R.bias = MODE == 0 ? a.gu_bias : a.dn_bias;
   float* xs = reinterpret_cast<float*>(smem);  // [kMaxTok][NB][kPitch]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   uint8_t* ring = smem + (size_t)kMaxTok * kMaxNB * kPitch * sizeof(float) +
-                  (size_t)warp * kRing * slot_bytes;
-  const int tpe = (rows / 2 + kPairs - 1) / kPairs;  // tasks per expert
-  const int ntask = nact * tpe;
-  const int lo = (int)((int64_t)blockIdx.x * ntask / gridDim.x);
-  const int hi = (int)((int64_t)(blockIdx.x + 1) * ntask / gridDim.x);
-  for (int s = lo / tpe; s < nact && s * tpe < hi; ++s) {
-    const int t_lo = max(lo, s * tpe), t_hi = min(hi, (s + 1) * tpe);
-    const int le = s_act[s];
+                  (size_t)warp * kRing * R.slot_bytes;
+  const int ppe = R.rows / 2;  // row pairs per expert
+  const int total = nact * ppe;
+  const int lo = (int)((int64_t)blockIdx.x * total / gridDim.x);
+  const int hi = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
+  for (int s = lo / ppe; s < nact && s * ppe < hi; ++s) {
+    const int a_lo = max(lo, s * ppe) - s * ppe, a_hi = min(hi, (s + 1) * ppe) - s * ppe;
     const int p0 = s_off[s], n = s_off[s + 1] - s_off[s];  // n <= kMaxTok
     __syncthreads();  // the previous expert's rows are no longer read
     for (int j = 0; j < n; ++j) {
-      const float* src = MODE == 0 ? a.x + (int64_t)s_tok[p0 + j] * K : a.h + (int64_t)(p0 + j) * K;
-      for (int k4 = threadIdx.x; k4 < (K >> 2); k4 += blockDim.x) {
+      const float* src =
+          MODE == 0 ? a.x + (int64_t)s_tok[p0 + j] * R.K : a.h + (int64_t)(p0 + j) * R.K;
+      for (int k4 = threadIdx.x; k4 < (R.K >> 2); k4 += blockDim.x) {
         const int k = k4 << 2;
         const float4 v = MODE == 0 ? reinterpret_cast<const float4*>(src)[k4]
                                    : __ldcg(reinterpret_cast<const float4*>(src) + k4);
-        *reinterpret_cast<float4*>(xs + j * xstride + (k >> 5) * kPitch + (k & 31)) = v;
+        *reinterpret_cast<float4*>(xs + j * R.xstride + (k >> 5) * kPitch + (k & 31)) = v;
       }
     }
     __syncthreads();
-    const int64_t erow = (int64_t)le * rows;
-    for (int task = t_lo + warp; task < t_hi; task += kFWarps) {
-      const int pair0 = (task - s * tpe) * kPairs;
-      const int npairs = max(0, min(kPairs, rows / 2 - pair0));
-      auto fetch = [&](int p) {
-        if (p < npairs) {
-          uint8_t* dst = ring + (p % kRing) * slot_bytes;
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const int64_t row = erow + 2 * (pair0 + p) + r;
-            const uint8_t* rbp = blocks + row * row_bytes;
-            for (int c = lane; c < NB; c += 32) cp_async16(dst + r * row_bytes + c * 16, rbp + c * 16);
-            const uint8_t* rs = scales + row * sp;
-            for (int c = lane; c < (sp >> 4); c += 32)
-              cp_async16(dst + 2 * row_bytes + r * sp + c * 16, rs + c * 16);
-          }
-        }
-        cp_async_commit();
-      };
-#pragma unroll
-      for (int p = 0; p < kRing - 1; ++p) fetch(p);
-      for (int p = 0; p < npairs; ++p) {
-        fetch(p + kRing - 1);
-        cp_async_wait<kRing - 1>();
-        __syncwarp();
-        const uint8_t* sl = ring + (p % kRing) * slot_bytes;
-        float acc[2][kMaxTok];
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-#pragma unroll
-          for (int t = 0; t < kMaxTok; ++t) acc[r][t] = 0.0f;
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-#pragma unroll
-          for (int i = 0; i < kMaxNB / 32; ++i) {
-            const int b = lane + 32 * i;
-            if (b >= NB) continue;
-            const uint4 q = *reinterpret_cast<const uint4*>(sl + r * row_bytes + b * 16);
-            const float sc = e8m0_scale(sl[2 * row_bytes + r * sp + b], a.zero_scale);
-            float v[32];
-            decode_block_f32(q, v);
-#pragma unroll
-            for (int t = 0; t < kMaxTok; ++t) {
-              if (t < n) {
-                const float4* x4 = reinterpret_cast<const float4*>(xs + t * xstride + b * kPitch);
-                float f0 = 0.0f, f1 = 0.0f, f2 = 0.0f, f3 = 0.0f;
-#pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4) {
-                  const float4 xv = x4[q4];
-                  f0 = __fmaf_rn(xv.x, v[4 * q4], f0);
-                  f1 = __fmaf_rn(xv.y, v[4 * q4 + 1], f1);
-                  f2 = __fmaf_rn(xv.z, v[4 * q4 + 2], f2);
-                  f3 = __fmaf_rn(xv.w, v[4 * q4 + 3], f3);
-                }
-                acc[r][t] = __fmaf_rn(__fadd_rn(__fadd_rn(f0, f1), __fadd_rn(f2, f3)), sc, acc[r][t]);
-              }
-            }
-          }
-        }
-        __syncwarp();  // the slot is refilled by a later fetch
-        const int row = 2 * (pair0 + p);
-#pragma unroll
-        for (int t = 0; t < kMaxTok; ++t) {
-          if (t >= n) break;
-          const float s0 = warp_sum_butterfly(acc[0][t]);
-          const float s1 = warp_sum_butterfly(acc[1][t]);
-          if (lane == 0) {
-            const int64_t pos = p0 + t;
-            if (MODE == 0) {
-              float g = s0, u = s1;
-              if (bias) {
-                g = __fadd_rn(g, bias[erow + row]);
-                u = __fadd_rn(u, bias[erow + row + 1]);
-              }
-              a.h[pos * a.I + (row >> 1)] = act_apply(a.act_kind, g, u, a.limit, a.clamp);
-            } else {
-              float y0 = s0, y1 = s1;
-              if (bias) {
-                y0 = __fadd_rn(y0, bias[erow + row]);
-                y1 = __fadd_rn(y1, bias[erow + row + 1]);
-              }
-              a.y[pos * a.H + row] = y0;
-              a.y[pos * a.H + row + 1] = y1;
-            }
-          }
-        }
-      }
-      cp_async_wait<0>();
+    const int span = a_hi - a_lo;
+    const int q0 = a_lo + span * warp / kFWarps, q1 = a_lo + span * (warp + 1) / kFWarps;
+    if (q1 > q0) {
+      const int le = s_act[s];
+      if (n <= 1) stream_pairs<MODE, 1>(a, R, xs, ring, le, q0, q1, p0, n);
+      else if (n <= 2) stream_pairs<MODE, 2>(a, R, xs, ring, le, q0, q1, p0, n);
+      else if (n <= 4) stream_pairs<MODE, 4>(a, R, xs, ring, le, q0, q1, p0, n);
+      else stream_pairs<MODE, 8>(a, R, xs, ring, le, q0, q1, p0, n);
     }
   }
 }
@@ -258,15 +286,31 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_decode_kernel(const FusedA
   const int T = a.T, H = a.H, E = a.E, K = a.K;
   if (threadIdx.x == 0) s_ok = 1;
 
-  // 1. router logits, one warp per (token, expert), the router's order
-  for (int u = blockIdx.x * kFWarps + warp; u < T * E; u += gridDim.x * kFWarps) {
-    const int t = u / E, e = u - t * E;
-    const float* xr = a.x + (int64_t)t * H;
-    const float* wr = a.rw + (int64_t)e * H;
-    float acc = 0.0f;
-    for (int k = lane; k < H; k += 32) acc = __fmaf_rn(xr[k], __ldg(wr + k), acc);
-    acc = warp_sum_butterfly(acc);
-    if (lane == 0) a.logits[u] = a.rb ? __fadd_rn(acc, a.rb[e]) : acc;
+  // 1. router logits: the T token rows staged in shared memory; one warp per
+  // expert loads its whole router row into registers at once (one memory
+  // round trip), then accumulates every token in the router's order
+  // (lane-strided FMAs, butterfly, bias)
+  if ((int)blockIdx.x * kFWarps < E) {
+    float* xs = reinterpret_cast<float*>(smem);  // [T][H]
+    for (int i = threadIdx.x; i < T * (H >> 2); i += blockDim.x)
+      reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(a.x)[i];
+    __syncthreads();
+    for (int e = blockIdx.x * kFWarps + warp; e < E; e += gridDim.x * kFWarps) {
+      const float* wr = a.rw + (int64_t)e * H;
+      const int nb = H >> 5;
+      float wv[kMaxNB];
+#pragma unroll
+      for (int j = 0; j < kMaxNB; ++j)
+        if (j < nb) wv[j] = __ldg(wr + lane + (j << 5));
+      for (int t = 0; t < T; ++t) {
+        float acc = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxNB; ++j)
+          if (j < nb) acc = __fmaf_rn(xs[t * H + lane + (j << 5)], wv[j], acc);
+        acc = warp_sum_butterfly(acc);
+        if (lane == 0) a.logits[(int64_t)t * E + e] = a.rb ? __fadd_rn(acc, a.rb[e]) : acc;
+      }
+    }
   }
   if (!grid_barrier(a, &s_ok)) return;
 
