@@ -37,9 +37,10 @@
 namespace gb {
 namespace {
 
-constexpr int kFWarps = 8;
+constexpr int kFWarps = 16;
 constexpr int kFThreads = kFWarps * 32;
 constexpr int kMaxTok = 8;      // tokens of one forward
+constexpr int kStageTok = 4;    // input rows staged at a time per expert
 constexpr int kMaxPos = 32;     // token-expert entries
 constexpr int kMaxK = 8;        // top-k
 constexpr int kRing = 3;        // row-pair slots per warp (2 in flight)
@@ -240,9 +241,9 @@ __device__ void expert_phase(const FusedArgs& a, uint8_t* smem, const int* s_act
   R.blocks = MODE == 0 ? a.gu_blocks : a.dn_blocks;
   R.scales = MODE == 0 ? a.gu_scales : a.dn_scales;
   R.bias = MODE == 0 ? a.gu_bias : a.dn_bias;
-  float* xs = reinterpret_cast<float*>(smem);  // [kMaxTok][NB][kPitch]
+  float* xs = reinterpret_cast<float*>(smem);  // [kStageTok][NB][kPitch]
   const int warp = threadIdx.x >> 5;
-  uint8_t* ring = smem + (size_t)kMaxTok * kMaxNB * kPitch * sizeof(float) +
+  uint8_t* ring = smem + (size_t)kStageTok * kMaxNB * kPitch * sizeof(float) +
                   (size_t)warp * kRing * R.slot_bytes;
   const int ppe = R.rows / 2;  // row pairs per expert
   const int total = nact * ppe;
@@ -250,34 +251,38 @@ __device__ void expert_phase(const FusedArgs& a, uint8_t* smem, const int* s_act
   const int hi = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
   for (int s = lo / ppe; s < nact && s * ppe < hi; ++s) {
     const int a_lo = max(lo, s * ppe) - s * ppe, a_hi = min(hi, (s + 1) * ppe) - s * ppe;
-    const int p0 = s_off[s], n = s_off[s + 1] - s_off[s];  // n <= kMaxTok
-    __syncthreads();  // the previous expert's rows are no longer read
-    for (int j = 0; j < n; ++j) {
-      const float* src =
-          MODE == 0 ? a.x + (int64_t)s_tok[p0 + j] * R.K : a.h + (int64_t)(p0 + j) * R.K;
-      for (int k4 = threadIdx.x; k4 < (R.K >> 2); k4 += blockDim.x) {
-        const int k = k4 << 2;
-        const float4 v = MODE == 0 ? reinterpret_cast<const float4*>(src)[k4]
-                                   : __ldcg(reinterpret_cast<const float4*>(src) + k4);
-        *reinterpret_cast<float4*>(xs + j * R.xstride + (k >> 5) * kPitch + (k & 31)) = v;
+    const int pe = s_off[s], ne = s_off[s + 1] - s_off[s];  // ne <= kMaxTok
+    // positions in chunks of kStageTok (an expert with more than 4 of the
+    // batch's tokens streams its rows once per chunk)
+    for (int c0 = 0; c0 < ne; c0 += kStageTok) {
+      const int p0 = pe + c0, n = min(kStageTok, ne - c0);
+      __syncthreads();  // the previous rows are no longer read
+      for (int j = 0; j < n; ++j) {
+        const float* src =
+            MODE == 0 ? a.x + (int64_t)s_tok[p0 + j] * R.K : a.h + (int64_t)(p0 + j) * R.K;
+        for (int k4 = threadIdx.x; k4 < (R.K >> 2); k4 += blockDim.x) {
+          const int k = k4 << 2;
+          const float4 v = MODE == 0 ? reinterpret_cast<const float4*>(src)[k4]
+                                     : __ldcg(reinterpret_cast<const float4*>(src) + k4);
+          *reinterpret_cast<float4*>(xs + j * R.xstride + (k >> 5) * kPitch + (k & 31)) = v;
+        }
       }
-    }
-    __syncthreads();
-    const int span = a_hi - a_lo;
-    const int q0 = a_lo + span * warp / kFWarps, q1 = a_lo + span * (warp + 1) / kFWarps;
-    if (q1 > q0) {
-      const int le = s_act[s];
-      if (n <= 1) stream_pairs<MODE, 1>(a, R, xs, ring, le, q0, q1, p0, n);
-      else if (n <= 2) stream_pairs<MODE, 2>(a, R, xs, ring, le, q0, q1, p0, n);
-      else if (n <= 4) stream_pairs<MODE, 4>(a, R, xs, ring, le, q0, q1, p0, n);
-      else stream_pairs<MODE, 8>(a, R, xs, ring, le, q0, q1, p0, n);
+      __syncthreads();
+      const int span = a_hi - a_lo;
+      const int q0 = a_lo + span * warp / kFWarps, q1 = a_lo + span * (warp + 1) / kFWarps;
+      if (q1 > q0) {
+        const int le = s_act[s];
+        if (n <= 1) stream_pairs<MODE, 1>(a, R, xs, ring, le, q0, q1, p0, n);
+        else if (n <= 2) stream_pairs<MODE, 2>(a, R, xs, ring, le, q0, q1, p0, n);
+        else stream_pairs<MODE, 4>(a, R, xs, ring, le, q0, q1, p0, n);
+      }
     }
   }
 }
 
 __global__ void __launch_bounds__(kFThreads, 1) fused_decode_kernel(const FusedArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ float s_exp[kFWarps][256];
+  __shared__ float s_exp[kMaxTok][256];  // warps t < T select token t
   __shared__ int s_idx[kMaxTok * kMaxK];
   __shared__ float s_w[kMaxTok * kMaxK];
   __shared__ int s_act[kMaxPos], s_off[kMaxPos + 1], s_tok[kMaxPos], s_inv[kMaxTok * kMaxK];
@@ -389,9 +394,11 @@ __global__ void __launch_bounds__(kFThreads, 1) fused_decode_kernel(const FusedA
 }
 
 // One size for every handle (the kernel attribute is shared by all of them):
-// the largest rows (K = 3072: 96 blocks, 96 scale bytes).
-constexpr size_t kFusedSmem = (size_t)kMaxTok * kMaxNB * kPitch * sizeof(float) +
+// the largest rows (K = 3072: 96 blocks, 96 scale bytes).  Phase 1 uses the
+// same space for the T token rows (at most 8 x 3072 floats).
+constexpr size_t kFusedSmem = (size_t)kStageTok * kMaxNB * kPitch * sizeof(float) +
                               (size_t)kFWarps * kRing * 2 * (kMaxNB * 16 + kMaxNB);
+static_assert(kFusedSmem >= (size_t)kMaxTok * kMaxNB * 32 * sizeof(float), "phase 1 rows");
 
 size_t fused_smem(const Moe&) { return kFusedSmem; }
 
