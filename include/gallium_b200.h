@@ -246,10 +246,7 @@ int gb_moe_get_info(const gb_moe* m, gb_moe_info* info);
  * failure. */
 int gb_moe_device_status(gb_moe* m, void* stream);
 
-/* Which kernels run the expert products.  AUTO runs a single-GPU MXFP4
- * batch of at most 8 tokens (and 32 token-expert entries) as one fused
- * cooperative launch (router, grouping, expert rows on the CUDA cores,
- * combine) and otherwise does what TENSOR_CORES does.  AUTO and TENSOR_CORES pick the
+/* Which kernels run the expert products.  AUTO and TENSOR_CORES pick the
  * block-scaled tcgen05 GEMM (MXFP4 weights as stored, activations as four
  * E4M3 pieces, tiles of 256 weight rows x 2-32 positions chosen from the
  * batch); CUDA_CORES forces the streaming MXFP4 rows with f32 FMA;
@@ -262,14 +259,20 @@ typedef enum {
   GB_PATH_AUTO = 0,
   GB_PATH_CUDA_CORES = 1,
   GB_PATH_TENSOR_CORES = 2,
-  GB_PATH_TENSOR_CORES_F16 = 3
+  GB_PATH_TENSOR_CORES_F16 = 3,
+  /* A single-GPU MXFP4 batch of at most 8 tokens (32 token-expert entries)
+   * as one cooperative launch: router, grouping, expert rows streamed on the
+   * CUDA cores, combine, with bounded grid barriers between them; larger
+   * batches as TENSOR_CORES.  Measured slower than TENSOR_CORES at every
+   * size it takes (1 token: 77 vs 52 us at 128 experts), so AUTO does not
+   * choose it. */
+  GB_PATH_FUSED_DECODE = 4
 } gb_expert_path;
 int gb_moe_set_expert_path(gb_moe* m, int32_t path);
 
 /* Forward graphs.  A single-GPU gb_moe_forward (and gb_moe_forward_host) of
- * at most 512 tokens (except the batches of at most 8 tokens that the
- * AUTO path runs as one fused launch) is captured once per (x, out, T) into a
- * CUDA graph and
+ * at most 512 tokens (except the batches that GB_PATH_FUSED_DECODE runs
+ * as one launch) is captured once per (x, out, T) into a CUDA graph and
  * replayed on later calls with the same triple, which removes the host launch
  * cost of its kernels; the graph reads x and writes out at replay time, so
  * new contents of the same buffers are used.  Up to `max_graphs` (0..16,

@@ -42,6 +42,7 @@ pub const GB_PATH_AUTO: i32 = 0;
 pub const GB_PATH_CUDA_CORES: i32 = 1;
 pub const GB_PATH_TENSOR_CORES: i32 = 2;
 pub const GB_PATH_TENSOR_CORES_F16: i32 = 3;
+pub const GB_PATH_FUSED_DECODE: i32 = 4;
 
 #[repr(C)]
 #[derive(Clone, Copy)]

@@ -630,7 +630,7 @@ int run_route_grouped(gb::Moe& m, const float* x, int64_t T, gb::Groups& g, int 
 
 int run_forward(gb::Moe& m, const float* x, int64_t T, float* out, cudaStream_t st) {
   int rc;
-  if (m.expert_path == GB_PATH_AUTO && gb::fused_decode_fits(m, T)) {
+  if (m.expert_path == GB_PATH_FUSED_DECODE && gb::fused_decode_fits(m, T)) {
     // one launch: the router, grouping, expert and combine stages of the
     // profile are empty except the expert stage, which holds the kernel
     for (int i = 0; i < 3; ++i)
@@ -759,7 +759,7 @@ int forward_dispatch(gb::Moe& m, const float* x, int64_t T, float* out, cudaStre
   // the fused decode forward is one (cooperative) launch: nothing to replay
   if (m.ep_size > 1 || m.profiling || m.graph_slots <= 0 || T <= 0 ||
       T > gb::Moe::kGraphMaxTokens ||
-      (m.expert_path == GB_PATH_AUTO && gb::fused_decode_fits(m, T)))
+      (m.expert_path == GB_PATH_FUSED_DECODE && gb::fused_decode_fits(m, T)))
     return run_forward(m, x, T, out, st);
   gb::Moe::Graph* victim = nullptr;
   gb::Moe::Graph* hit = find_slot(m.graphs, m.graph_slots, x, T, out, &victim);
@@ -1278,10 +1278,10 @@ int gb_moe_destroy(gb_moe* h) {
 int gb_moe_set_expert_path(gb_moe* h, int32_t path) {
   int rc = check_handle(h);
   if (rc) return rc;
-  if (path < GB_PATH_AUTO || path > GB_PATH_TENSOR_CORES_F16)
+  if (path < GB_PATH_AUTO || path > GB_PATH_FUSED_DECODE)
     return set_err(GB_ERR_INVALID_ARG, "unknown expert path %d", path);
-  if (path >= GB_PATH_TENSOR_CORES && !gb::tc_supported(h->m) && !h->m.mx.ok &&
-      !gb::q4k_tc_supported(h->m))
+  if ((path == GB_PATH_TENSOR_CORES || path == GB_PATH_TENSOR_CORES_F16) &&
+      !gb::tc_supported(h->m) && !h->m.mx.ok && !gb::q4k_tc_supported(h->m))
     return set_err(GB_ERR_UNSUPPORTED,
                    "tensor-core expert path needs the GPT-OSS activation and H, I multiples of 64");
   DeviceScope ds(h->m.device);

@@ -294,7 +294,7 @@ constexpr int kMxGroupEntries = 512;  // routing entries of the one-launch group
 // Grouped forwards of at least this many positions run gate_up and down as
 // one launch; below it the two launches measured faster (the wait for h
 // chunks costs more than the second launch when each CTA has one item).
-constexpr int64_t kMxOneLaunchRows = 16;
+constexpr int64_t kMxOneLaunchRows = 24;
 bool mx_supported(const Moe& m);
 cudaError_t mx_prepare_weights(Moe& m);
 void mx_release(MxWeights& x);

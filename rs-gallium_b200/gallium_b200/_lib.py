@@ -42,6 +42,7 @@ GB_PATH_AUTO = 0
 GB_PATH_CUDA_CORES = 1
 GB_PATH_TENSOR_CORES = 2
 GB_PATH_TENSOR_CORES_F16 = 3
+GB_PATH_FUSED_DECODE = 4
 GB_DTYPE_F32 = 0
 GB_DTYPE_BF16 = 1
 

@@ -144,11 +144,12 @@ class MoEBlock:
         check(self._lib.gb_moe_forward(self._h, x_ptr, T, out_ptr, stream))
 
     def set_expert_path(self, path: str) -> None:
-        """'auto', 'cuda_cores', 'tensor_cores' or 'tensor_cores_f16'
-        (gb_moe_set_expert_path)."""
+        """'auto', 'cuda_cores', 'tensor_cores', 'tensor_cores_f16' or
+        'fused_decode' (gb_moe_set_expert_path)."""
         code = {"auto": _lib.GB_PATH_AUTO, "cuda_cores": _lib.GB_PATH_CUDA_CORES,
                 "tensor_cores": _lib.GB_PATH_TENSOR_CORES,
-                "tensor_cores_f16": _lib.GB_PATH_TENSOR_CORES_F16}[path]
+                "tensor_cores_f16": _lib.GB_PATH_TENSOR_CORES_F16,
+                "fused_decode": _lib.GB_PATH_FUSED_DECODE}[path]
         check(self._lib.gb_moe_set_expert_path(self._h, code))
 
     def set_graphs(self, max_graphs: int) -> None:

@@ -1,4 +1,5 @@
-"""The fused decode kernel (the whole layer in one cooperative launch, T <= 8)
+"""The fused decode path (GB_PATH_FUSED_DECODE: the whole layer in one
+cooperative launch, T <= 8)
 against the oracle and against the separate tensor-core kernels: expert
 indices bit for bit, outputs within max-abs 2e-2 and mean-rel 1e-3, at every
 batch size it takes (1-8 tokens), with 32 and 128 experts, safetensors and
@@ -35,7 +36,7 @@ def test_fused_decode_matches_oracle_and_the_tensor_core_path(E, gguf):
     try:
         for T in range(1, 9):
             x = torch.from_numpy(synth.tokens(T, 2880, seed=100 + T)).cuda()
-            moe.set_expert_path("auto")
+            moe.set_expert_path("fused_decode")
             fused = moe.forward(x).cpu().numpy()
             again = moe.forward(x).cpu().numpy()
             assert np.array_equal(fused, again), T
@@ -44,7 +45,6 @@ def test_fused_decode_matches_oracle_and_the_tensor_core_path(E, gguf):
             want, idx, _ = orc.forward(x.cpu().numpy())
             _check(fused, want)
             _check(tc, want)
-            moe.set_expert_path("auto")
             assert np.array_equal(moe.route(x)["idx"].cpu().numpy(), idx)
     finally:
         moe.close()

@@ -470,10 +470,10 @@ def test_tensor_cores_on_odd_shapes():
 
 def test_graph_replay_equals_direct_launches(moe32, layer32):
     # the same buffers three times: launched directly, captured, replayed; new
-    # contents of x between calls are read by the replay.  Batches of at most
-    # 8 tokens run as one fused launch and are never captured (checked last).
+    # contents of x between calls are read by the replay.  Batches that the
+    # fused decode path runs as one launch are never captured (checked last).
     torch = _torch()
-    for T in (9, 13, 64):
+    for T in (1, 7, 64):
         xs = [synth.tokens(T, 2880, seed=400 + 10 * T + i) for i in range(3)]
         xd = torch.empty((T, 2880), device="cuda")
         out = torch.empty_like(xd)
@@ -496,14 +496,18 @@ def test_graph_replay_equals_direct_launches(moe32, layer32):
         assert_parity(direct[2], want, f"graph T={T}")
     xd = _cuda(synth.tokens(8, 2880, seed=401))
     out = torch.empty_like(xd)
-    c0 = moe32.info()["graph_captures"]
-    first = None
-    for _ in range(3):
-        moe32.forward_raw(xd.data_ptr(), 8, out.data_ptr())
-        moe32.device_status()
-        first = out.cpu().numpy() if first is None else first
-        assert np.array_equal(out.cpu().numpy(), first)
-    assert moe32.info()["graph_captures"] == c0
+    moe32.set_expert_path("fused_decode")
+    try:
+        c0 = moe32.info()["graph_captures"]
+        first = None
+        for _ in range(3):
+            moe32.forward_raw(xd.data_ptr(), 8, out.data_ptr())
+            moe32.device_status()
+            first = out.cpu().numpy() if first is None else first
+            assert np.array_equal(out.cpu().numpy(), first)
+        assert moe32.info()["graph_captures"] == c0
+    finally:
+        moe32.set_expert_path("auto")
 
 
 def test_graph_cache_replaces_the_least_recently_used(moe32):
@@ -535,8 +539,7 @@ def test_graph_cache_replaces_the_least_recently_used(moe32):
 def test_one_launch_grouping_matches_oracle(layer32_skew, T):
     # up to 512 routing entries the grouping, tile table and activation pieces
     # come from one launch; 129 tokens x top-4 take the separate kernels (the
-    # tensor-core path is forced: batches of <= 8 tokens would otherwise run
-    # the fused decode kernel)
+    # tensor-core path is forced, as AUTO would choose here)
     m = OssMoEFFN.load(layer32_skew, device=0, max_tokens=T)
     m.set_expert_path("tensor_cores")
     try:
