@@ -8,13 +8,15 @@
 //   down:    y[p, o] = h_p . Wd[o]
 //
 // dense_rows_kernel<MODE, TC, W>: one CTA per (active expert, tile of rows); a
-// warp owns two weight rows (GATE_UP: gate row i and up row i; DOWN: rows 2p,
-// 2p + 1).  The expert's rows stream through shared memory TC at a time; lane
+// warp owns two weight rows (GATE_UP: gate row i and up row i, stored
+// interleaved as rows 2i and 2i + 1; DOWN: rows 2p, 2p + 1).  The expert's rows stream through shared memory TC at a time; lane
 // l reads 16-byte pieces l, l + 32, ... of both weight rows (bf16 or f32, as
 // stored; exact in f32) and accumulates f32 FMAs, folded by a butterfly.  For
 // decode-sized groups (one chunk) each weight byte is read from HBM once; more
 // chunks re-read the expert's rows from L2.
 #include <math.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "moe_internal.h"
@@ -43,11 +45,12 @@ __device__ __forceinline__ void widen(const uint4& q, float (&v)[8], const float
 }
 
 // identity != 0: the shared expert: `identity` positions, position p = input
-// row p, weights at w0 / w1 directly (one expert).
+// row p, weights at w0 directly (one expert).  GATE_UP: w0 holds 2 n_rows
+// interleaved gate / up rows per expert; DOWN: n_rows rows.
 template <int MODE, int TC, typename W>
 __global__ void __launch_bounds__(kWarps * 32)
     dense_rows_kernel(const float* __restrict__ in, int K_in, int n_rows, int top_k,
-                      const W* __restrict__ w0, const W* __restrict__ w1,
+                      const W* __restrict__ w0,
                       const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
                       const int32_t* __restrict__ active, const int32_t* __restrict__ meta,
                       const int32_t* __restrict__ perm, int e_begin, int act_kind, float clamp,
@@ -73,13 +76,20 @@ __global__ void __launch_bounds__(kWarps * 32)
   constexpr int EPQ = 16 / (int)sizeof(W);  // weights per 16-byte piece
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int pair = blockIdx.x * kWarps + warp;
-  // GATE_UP: gate row `pair` (w0) and up row `pair` (w1); DOWN: rows 2 pair, 2 pair + 1 (w0)
+  // GATE_UP: gate row `pair` and up row `pair` (stored rows 2 pair, 2 pair + 1
+  // of the expert's 2 n_rows); DOWN: rows 2 pair, 2 pair + 1
   const int64_t r0 = MODE == GATE_UP ? pair : 2 * pair;
   const bool valid = MODE == GATE_UP ? pair < n_rows : r0 < n_rows;
   const bool valid1 = MODE == GATE_UP ? valid : r0 + 1 < n_rows;
-  const W* row_a = w0 + ((int64_t)le * n_rows + (valid ? r0 : 0)) * K_in;
-  const W* row_b = MODE == GATE_UP ? w1 + ((int64_t)le * n_rows + (valid ? r0 : 0)) * K_in
-                                   : w0 + ((int64_t)le * n_rows + (valid1 ? r0 + 1 : 0)) * K_in;
+  const W* row_a;
+  const W* row_b;
+  if (MODE == GATE_UP) {
+    row_a = w0 + ((int64_t)le * 2 * n_rows + (valid ? 2 * r0 : 0)) * K_in;
+    row_b = row_a + K_in;
+  } else {
+    row_a = w0 + ((int64_t)le * n_rows + (valid ? r0 : 0)) * K_in;
+    row_b = w0 + ((int64_t)le * n_rows + (valid1 ? r0 + 1 : 0)) * K_in;
+  }
   const int npieces = K_in / EPQ;
 
   for (int c0 = 0; c0 < n; c0 += TC) {
@@ -137,8 +147,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 
 template <int MODE, typename W>
 cudaError_t launch_dense(const Moe& m, const Groups* g, int identity, const float* in, int K_in,
-                         int n_rows, const void* w0, const void* w1, float* out, int out_stride,
-                         int max_active, int64_t max_per_expert, cudaStream_t st) {
+                         int n_rows, const void* w0, float* out, int out_stride, int max_active,
+                         int64_t max_per_expert, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
   if (max_active <= 0) return cudaSuccess;
   const int units = MODE == GATE_UP ? n_rows : (n_rows + 1) / 2;
@@ -149,7 +159,7 @@ cudaError_t launch_dense(const Moe& m, const Groups* g, int identity, const floa
     cudaError_t err = set_smem_limit(kern, smem);
     if (err != cudaSuccess) return err;
     return launch_pdl(kern, grid, dim3(kWarps * 32), smem, st, in, K_in, n_rows,
-                      g ? g->perm_div : 1, static_cast<const W*>(w0), static_cast<const W*>(w1),
+                      g ? g->perm_div : 1, static_cast<const W*>(w0),
                       g ? g->counts : nullptr, g ? g->offsets : nullptr,
                       g ? g->active : nullptr, g ? (const int32_t*)g->meta : nullptr,
                       g ? g->perm : nullptr, m.e_begin, d.act_kind, d.act_clamp,
@@ -160,14 +170,29 @@ cudaError_t launch_dense(const Moe& m, const Groups* g, int identity, const floa
 
 template <int MODE>
 cudaError_t launch_dense_any(const Moe& m, const Groups* g, int identity, const float* in,
-                             int K_in, int n_rows, const void* w0, const void* w1, float* out,
-                             int out_stride, int max_active, int64_t max_per_expert,
-                             cudaStream_t st) {
+                             int K_in, int n_rows, const void* w0, float* out, int out_stride,
+                             int max_active, int64_t max_per_expert, cudaStream_t st) {
   if (m.w.dense_bf16)
-    return launch_dense<MODE, __nv_bfloat16>(m, g, identity, in, K_in, n_rows, w0, w1, out,
+    return launch_dense<MODE, __nv_bfloat16>(m, g, identity, in, K_in, n_rows, w0, out,
                                              out_stride, max_active, max_per_expert, st);
-  return launch_dense<MODE, float>(m, g, identity, in, K_in, n_rows, w0, w1, out, out_stride,
+  return launch_dense<MODE, float>(m, g, identity, in, K_in, n_rows, w0, out, out_stride,
                                    max_active, max_per_expert, st);
+}
+
+// Stored rows [row0 + i * step] (i < nrows) of K values -> f32 [nrows][K].
+template <typename W>
+__global__ void widen_rows_kernel(const W* __restrict__ w, int64_t row0, int step, int nrows,
+                                  int K, float* __restrict__ out) {
+  const int64_t n = (int64_t)nrows * K;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K, k = i - r * K;
+    const W v = w[(row0 + r * step) * K + k];
+    if constexpr (sizeof(W) == 2)
+      out[i] = __bfloat162float(v);
+    else
+      out[i] = v;
+  }
 }
 
 }  // namespace
@@ -175,14 +200,14 @@ cudaError_t launch_dense_any(const Moe& m, const Groups* g, int identity, const 
 cudaError_t launch_dense_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                  cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  return launch_dense_any<GATE_UP>(m, &g, 0, x, d.hidden, d.inter, m.w.dense_gate, m.w.dense_up,
-                                   eb.h, d.inter, g.max_active, g.max_per_expert, st);
+  return launch_dense_any<GATE_UP>(m, &g, 0, x, d.hidden, d.inter, m.w.dense_gu, eb.h, d.inter,
+                                   g.max_active, g.max_per_expert, st);
 }
 
 cudaError_t launch_dense_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  return launch_dense_any<DOWN>(m, &g, 0, eb.h, d.inter, d.hidden, m.w.dense_down, nullptr, eb.y,
-                                d.hidden, g.max_active, g.max_per_expert, st);
+  return launch_dense_any<DOWN>(m, &g, 0, eb.h, d.inter, d.hidden, m.w.dense_down, eb.y, d.hidden,
+                                g.max_active, g.max_per_expert, st);
 }
 
 cudaError_t launch_shared_expert(const Moe& m, const float* x, int64_t T, float* h, float* y,
@@ -190,10 +215,40 @@ cudaError_t launch_shared_expert(const Moe& m, const float* x, int64_t T, float*
   const gb_moe_desc& d = m.desc;
   if (T <= 0) return cudaSuccess;
   cudaError_t e = launch_dense_any<GATE_UP>(m, nullptr, (int)T, x, d.hidden, d.shared_inter,
-                                            m.w.sh_gate, m.w.sh_up, h, d.shared_inter, 1, T, st);
+                                            m.w.sh_gu, h, d.shared_inter, 1, T, st);
   if (e != cudaSuccess) return e;
-  return launch_dense_any<DOWN>(m, nullptr, (int)T, h, d.shared_inter, d.hidden, m.w.sh_down,
-                                nullptr, y, d.hidden, 1, T, st);
+  return launch_dense_any<DOWN>(m, nullptr, (int)T, h, d.shared_inter, d.hidden, m.w.sh_down, y,
+                                d.hidden, 1, T, st);
+}
+
+cudaError_t launch_dense_dequant(const Moe& m, int which, int local_expert, float* out,
+                                 cudaStream_t st) {
+  const gb_moe_desc& d = m.desc;
+  const int H = d.hidden, I = d.inter;
+  const void* w;
+  int64_t row0;
+  int step, nrows, K;
+  if (which == 2) {
+    w = m.w.dense_down;
+    row0 = (int64_t)local_expert * H;
+    step = 1;
+    nrows = H;
+    K = I;
+  } else {
+    w = m.w.dense_gu;
+    row0 = (int64_t)local_expert * 2 * I + which;
+    step = 2;
+    nrows = I;
+    K = H;
+  }
+  const unsigned blocks = (unsigned)std::min<int64_t>(((int64_t)nrows * K + 255) / 256, 4096);
+  if (m.w.dense_bf16)
+    widen_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(w), row0, step,
+                                              nrows, K, out);
+  else
+    widen_rows_kernel<<<blocks, 256, 0, st>>>(static_cast<const float*>(w), row0, step, nrows, K,
+                                              out);
+  return cudaGetLastError();
 }
 
 }  // namespace gb

@@ -1,6 +1,7 @@
 // moe_internal.h -- state of a gb_moe handle and the kernel launchers.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -71,16 +72,20 @@ struct ExpertWeights {
   // tensor-core Q4_K path: per local expert, weights decode as w * 2^exp
   int32_t* q4_gu_exp = nullptr;  // [E_loc] (one allocation with q4_dn_exp)
   int32_t* q4_dn_exp = nullptr;  // [E_loc]
-  // Dense experts (GB_FMT_DENSE), as stored (bf16 or f32): dense_gate,
-  // dense_up [E_loc][I][H], dense_down [E_loc][H][I]; the shared expert's
-  // sh_gate, sh_up [Is][H], sh_down [H][Is]
-  void* dense_gate = nullptr;
-  void* dense_up = nullptr;
+  // Dense experts (GB_FMT_DENSE), values as stored (bf16 or f32), gate and
+  // up rows interleaved: dense_gu [E_loc][2I][H] (row 2i = gate i, 2i + 1 =
+  // up i), dense_down [E_loc][H][I]; the shared expert's sh_gu [2Is][H],
+  // sh_down [H][Is]
+  void* dense_gu = nullptr;
   void* dense_down = nullptr;
-  void* sh_gate = nullptr;
-  void* sh_up = nullptr;
+  void* sh_gu = nullptr;
   void* sh_down = nullptr;
   bool dense_bf16 = false;
+  // CUtensorMaps of the bf16 dense weights (dense_tc.cu): 128-row boxes
+  alignas(64) unsigned char map_dense_gu[128] = {};
+  alignas(64) unsigned char map_dense_dn[128] = {};
+  alignas(64) unsigned char map_sh_gu[128] = {};
+  alignas(64) unsigned char map_sh_dn[128] = {};
   // Gemma-4: per-expert output scale [E] (all experts: the combine reads it),
   // input / output norm vectors [H]
   float* expert_scale = nullptr;
@@ -183,6 +188,16 @@ struct Workspace {
   float* x_expert = nullptr;   // [T, H] the experts' input (input_norm 1)
   float* sh_h = nullptr;       // [T, Is] shared expert's activation (GB_FMT_DENSE)
   float* sh_y = nullptr;       // [T, H] shared expert's output
+  // shared expert on the tensor cores (bf16 dense weights): x and h as bf16
+  // hi / lo, [T, H] and [T, Is], with their CUtensorMaps
+  __nv_bfloat16* sh_xh = nullptr;
+  __nv_bfloat16* sh_xl = nullptr;
+  __nv_bfloat16* sh_hh = nullptr;
+  __nv_bfloat16* sh_hl = nullptr;
+  alignas(64) unsigned char map_sh_xh[128] = {};
+  alignas(64) unsigned char map_sh_xl[128] = {};
+  alignas(64) unsigned char map_sh_hh[128] = {};
+  alignas(64) unsigned char map_sh_hl[128] = {};
   float* x_stage = nullptr;    // [T, H] host-path staging
   float* out_stage = nullptr;  // [T, H]
   ExpertBufs eb;               // single GPU: T*k positions
@@ -355,6 +370,27 @@ cudaError_t launch_dense_down(const Moe& m, const Groups& g, ExpertBufs& eb, cud
 // The shared expert over all T tokens: h [T, Is], y [T, H] (ws.sh_h / sh_y).
 cudaError_t launch_shared_expert(const Moe& m, const float* x, int64_t T, float* h, float* y,
                                  cudaStream_t st);
+// Stored dense weights of one local expert widened to f32 (which: 0 gate,
+// 1 up, 2 down), for gb_moe_dequant_expert.
+cudaError_t launch_dense_dequant(const Moe& m, int which, int local_expert, float* out,
+                                 cudaStream_t st);
+
+// Dense bf16 experts on the tensor cores (dense_tc.cu): kind::f16 with the
+// activations split into bf16 hi + lo.  The routed experts use the grouped
+// buffers of ExpertBufs (xh / xl / hh / hl hold bf16 there) and the tile
+// table; the shared expert the workspace's sh_x* / sh_h* buffers.
+bool dense_tc_supported(const Moe& m);
+bool dense_tc_shared_supported(const Moe& m);
+cudaError_t dense_tc_prepare(Moe& m);
+cudaError_t dense_tc_make_maps(const Moe& m, ExpertBufs& eb);
+cudaError_t dense_tc_make_ws_maps(const Moe& m, Workspace& ws);
+cudaError_t launch_dense_tc_gate_up(const Moe& m, const Groups& g, const float* x,
+                                    ExpertBufs& eb, cudaStream_t st);
+cudaError_t launch_dense_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+cudaError_t launch_shared_expert_tc(const Moe& m, const float* x, int64_t T, float* y,
+                                    cudaStream_t st);
+// Whether the shared expert of a T-token forward runs on the tensor cores.
+bool use_dense_tc_shared(const Moe& m, int64_t T);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
                                   cudaStream_t st);
 cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,
