@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define GB_ABI_VERSION 3
+#define GB_ABI_VERSION 4
 
 typedef enum gb_status {
   GB_OK = 0,
@@ -83,7 +83,9 @@ typedef enum {
   /* Dense expert weights in weight_dtype (gallium-core MoEFFN's GatedFFN
    * experts, ffn.rs:30-67, 72-166): gate_raw, up_raw [E, I, H], down_raw
    * [E, H, I], no biases; router_weight [E, H], no bias; combine in rank
-   * order; optional shared expert.  Experts run on the CUDA cores. */
+   * order; optional shared expert.  bf16 weights run on the tensor cores
+   * (from one grouped position per two local experts, and H, I multiples of
+   * 64), f32 weights on the CUDA cores. */
   GB_FMT_DENSE = 3
 } gb_weight_format;
 
@@ -333,6 +335,102 @@ int gb_route_noalloc(const float* x_dev, const float* router_weight_dev,
                      const float* router_bias_dev, const float* selection_bias_dev, int64_t T,
                      int32_t hidden, int32_t n_experts, int32_t top_k, int32_t router_kind,
                      int32_t* idx_dev, float* w_dev, void* stream);
+
+/* ---- GPT-OSS decode stack ------------------------------------------------
+ * The GGUF GPT-OSS model around the MoE block (crates/gallium-models/src/
+ * gpt_oss_q.rs:15-107 attention, :270-297 block, :437-472 forward): per
+ * layer, RMSNorm -> attention (q/k/v projections with biases, RoPE, grouped
+ * queries, learned per-head sink logits, a sliding window on the layers
+ * marked so) -> residual add -> RMSNorm -> the MoE block -> residual add;
+ * then the final RMSNorm, the LM head on each sequence's last token and the
+ * greedy token (the largest logit, ties to the highest token id, as
+ * sampling.rs:85-92 takes Iterator::max_by's last maximum).  Activations,
+ * the KV cache and all arithmetic are f32; attention and LM-head weights
+ * are bf16 (widened exactly).  B sequences run in lockstep: every forward
+ * gives each of them T tokens at the same positions pos .. pos + T - 1, as
+ * the reference's (batch, seq_len) token tensor does. */
+
+typedef struct gb_decoder gb_decoder;
+
+typedef struct gb_decoder_layer {
+  const float* attn_norm;        /* [hidden] RMSNorm weight before attention */
+  const float* post_attn_norm;   /* [hidden] RMSNorm weight before the MoE block */
+  const uint16_t* wq;            /* [n_heads * head_dim][hidden] bf16 bits */
+  const uint16_t* wk;            /* [n_kv_heads * head_dim][hidden] */
+  const uint16_t* wv;            /* [n_kv_heads * head_dim][hidden] */
+  const uint16_t* wo;            /* [hidden][n_heads * head_dim] */
+  const float* bq;               /* biases, each nullable: [n_heads * head_dim] */
+  const float* bk;               /* [n_kv_heads * head_dim] */
+  const float* bv;               /* [n_kv_heads * head_dim] */
+  const float* bo;               /* [hidden] */
+  const float* sinks;            /* [n_heads] sink logits */
+  int32_t sliding;               /* 1: sliding-window attention, 0: full causal */
+  const gb_moe_desc* moe;        /* the layer's MoE block (device, max_tokens and the
+                                    expert-parallel fields are set by the decoder) */
+} gb_decoder_layer;
+
+typedef struct gb_decoder_desc {
+  uint32_t struct_size;          /* sizeof(gb_decoder_desc) */
+  int32_t n_layers;
+  int32_t hidden;
+  int32_t n_heads;               /* query heads, a multiple of n_kv_heads */
+  int32_t n_kv_heads;
+  int32_t head_dim;              /* even, <= 256 */
+  int32_t vocab;
+  int32_t sliding_window;        /* keys visible to a sliding layer, the query's own included */
+  int32_t max_seq_len;           /* KV cache positions per sequence */
+  int32_t max_batch;             /* sequences per forward */
+  int32_t max_tokens;            /* tokens per sequence per forward */
+  float rope_theta;
+  float rope_scaling_factor;     /* > 1: YaRN frequencies (pos_enc.rs:113-137) */
+  int32_t rope_orig_ctx;         /* YaRN original context length */
+  float rope_beta_fast;          /* YaRN betas (0: 32 and 1) */
+  float rope_beta_slow;
+  float rms_eps;
+  int32_t device;
+  const uint16_t* embed;         /* [vocab][hidden] bf16 token embeddings */
+  const uint16_t* lm_head;       /* [vocab][hidden] bf16, NULL: tied to embed */
+  const float* final_norm;       /* [hidden] */
+  const gb_decoder_layer* layers; /* [n_layers] */
+} gb_decoder_desc;
+
+/* Uploads every weight (the MoE blocks through gb_moe_create) and sizes the
+ * KV cache for max_batch x max_seq_len positions.  Host pointers are read
+ * during the call only. */
+int gb_decoder_create(const gb_decoder_desc* desc, gb_decoder** out);
+
+/* One forward of B sequences x T tokens at positions pos .. pos + T - 1
+ * (tokens_dev: device int32 [B][T]).  pos must equal the positions already
+ * cached (0 after create or reset) and B the batch of the cached positions;
+ * pos + T <= max_seq_len.  logits_dev (nullable): device f32 [B][vocab], the
+ * logits of each sequence's last token; next_dev (nullable): device int32
+ * [B], its greedy token.  Asynchronous on `stream`. */
+int gb_decoder_forward(gb_decoder* d, const int32_t* tokens_dev, int32_t B, int32_t T,
+                       int64_t pos, float* logits_dev, int32_t* next_dev, void* stream);
+
+/* n_steps greedy decode steps of B sequences, each feeding the previous
+ * step's greedy token: step 0 feeds tokens_dev [B] at position pos.  Writes
+ * the n_steps x B tokens produced to out_dev (device int32 [n_steps][B]).
+ * Each step replays one CUDA graph (captured on the first call for each B).
+ * Asynchronous on `stream`. */
+int gb_decoder_generate(gb_decoder* d, const int32_t* tokens_dev, int32_t B, int64_t pos,
+                        int32_t n_steps, int32_t* out_dev, void* stream);
+
+/* Forget the cached positions (the next forward starts at pos 0). */
+int gb_decoder_reset(gb_decoder* d);
+
+/* Stage timing of the following forwards (CUDA events): when enabled,
+ * gb_decoder_stage_times returns the milliseconds of the last eager forward
+ * spent in attention (norms, projections, RoPE, attention, residual), in
+ * the MoE blocks (norms, MoE, residual) and in the head (final norm, LM head,
+ * greedy token).  Synchronises `stream`. */
+int gb_decoder_set_profiling(gb_decoder* d, int32_t enable);
+int gb_decoder_stage_times(gb_decoder* d, float ms_out[3], void* stream);
+
+/* Device error words of every layer's MoE block (gb_moe_device_status). */
+int gb_decoder_device_status(gb_decoder* d, void* stream);
+
+int gb_decoder_destroy(gb_decoder* d);
 
 /* Expert parallel: a fresh 128-byte ncclUniqueId (rank 0 calls this and
  * shares the bytes with the other ranks). */

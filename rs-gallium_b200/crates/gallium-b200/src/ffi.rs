@@ -1,10 +1,10 @@
-//! Raw bindings of include/gallium_b200.h (ABI version 3).  Field order and
+//! Raw bindings of include/gallium_b200.h (ABI version 4).  Field order and
 //! types follow the header exactly; tests/test_rust_binding.py checks them.
 #![allow(non_camel_case_types)]
 
 use std::os::raw::{c_char, c_int, c_void};
 
-pub const GB_ABI_VERSION: c_int = 3;
+pub const GB_ABI_VERSION: c_int = 4;
 
 // gb_status
 pub const GB_OK: c_int = 0;
@@ -124,6 +124,68 @@ pub struct gb_moe {
     _private: [u8; 0],
 }
 
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct gb_decoder_layer {
+    pub attn_norm: *const f32,
+    pub post_attn_norm: *const f32,
+    pub wq: *const u16,
+    pub wk: *const u16,
+    pub wv: *const u16,
+    pub wo: *const u16,
+    pub bq: *const f32,
+    pub bk: *const f32,
+    pub bv: *const f32,
+    pub bo: *const f32,
+    pub sinks: *const f32,
+    pub sliding: i32,
+    pub moe: *const gb_moe_desc,
+}
+
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct gb_decoder_desc {
+    pub struct_size: u32,
+    pub n_layers: i32,
+    pub hidden: i32,
+    pub n_heads: i32,
+    pub n_kv_heads: i32,
+    pub head_dim: i32,
+    pub vocab: i32,
+    pub sliding_window: i32,
+    pub max_seq_len: i32,
+    pub max_batch: i32,
+    pub max_tokens: i32,
+    pub rope_theta: f32,
+    pub rope_scaling_factor: f32,
+    pub rope_orig_ctx: i32,
+    pub rope_beta_fast: f32,
+    pub rope_beta_slow: f32,
+    pub rms_eps: f32,
+    pub device: i32,
+    pub embed: *const u16,
+    pub lm_head: *const u16,
+    pub final_norm: *const f32,
+    pub layers: *const gb_decoder_layer,
+}
+
+impl Default for gb_decoder_desc {
+    /// Zeroed, with struct_size set, as the header asks.
+    fn default() -> Self {
+        // SAFETY: every field is an integer, a float or a raw pointer, for
+        // which all-zero bytes are valid (null pointers).
+        let mut d: Self = unsafe { std::mem::zeroed() };
+        d.struct_size = std::mem::size_of::<Self>() as u32;
+        d
+    }
+}
+
+/// Opaque decoder handle.
+#[repr(C)]
+pub struct gb_decoder {
+    _private: [u8; 0],
+}
+
 extern "C" {
     pub fn gb_moe_create(desc: *const gb_moe_desc, out: *mut *mut gb_moe) -> c_int;
     pub fn gb_moe_forward(m: *mut gb_moe, x_dev: *const f32, t: i64, out_dev: *mut f32,
@@ -150,6 +212,18 @@ extern "C" {
                             router_bias_dev: *const f32, selection_bias_dev: *const f32, t: i64,
                             hidden: i32, n_experts: i32, top_k: i32, router_kind: i32,
                             idx_dev: *mut i32, w_dev: *mut f32, stream: *mut c_void) -> c_int;
+    pub fn gb_decoder_create(desc: *const gb_decoder_desc, out: *mut *mut gb_decoder) -> c_int;
+    pub fn gb_decoder_forward(d: *mut gb_decoder, tokens_dev: *const i32, b: i32, t: i32,
+                              pos: i64, logits_dev: *mut f32, next_dev: *mut i32,
+                              stream: *mut c_void) -> c_int;
+    pub fn gb_decoder_generate(d: *mut gb_decoder, tokens_dev: *const i32, b: i32, pos: i64,
+                               n_steps: i32, out_dev: *mut i32, stream: *mut c_void) -> c_int;
+    pub fn gb_decoder_reset(d: *mut gb_decoder) -> c_int;
+    pub fn gb_decoder_set_profiling(d: *mut gb_decoder, enable: i32) -> c_int;
+    pub fn gb_decoder_stage_times(d: *mut gb_decoder, ms_out: *mut f32, stream: *mut c_void)
+        -> c_int;
+    pub fn gb_decoder_device_status(d: *mut gb_decoder, stream: *mut c_void) -> c_int;
+    pub fn gb_decoder_destroy(d: *mut gb_decoder) -> c_int;
     pub fn gb_nccl_unique_id(out: *mut u8) -> c_int;
     pub fn gb_last_error() -> *const c_char;
     pub fn gb_abi_version() -> c_int;

@@ -65,6 +65,8 @@ struct Args {
   float* out_y;              // DOWN: y [rows][out_stride], row = out_rows[position] (or position)
   const int32_t* out_rows;
   int out_stride;
+  const float* bias;         // DOWN: + bias[row] (nullable)
+  int add_out;               // DOWN: y = y + (acc + bias) instead of y = acc + bias
   int* err;                  // error flags (bit 1: wait timed out)
   uint64_t wait_ns;          // bound of every mbarrier wait
 };
@@ -145,7 +147,10 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
         }
       } else if (valid && n < it.nrows) {
         const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
-        a.out_y[orow * a.out_stride + row] = val;
+        float* o = a.out_y + orow * a.out_stride + row;
+        float v = a.bias ? __fadd_rn(val, a.bias[row]) : val;
+        if (a.add_out) v = __fadd_rn(*o, v);
+        *o = v;
       }
     }
   }
@@ -324,8 +329,6 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, const int32_t* __
 
 }  // namespace dtc
 
-namespace {
-
 // bf16 [rows][K] row-major, one box = box_rows rows x 64 elements, 128-byte
 // swizzle (the canonical K-major layout of the MMA descriptors).
 cudaError_t make_bf16_map(void* map, const void* base, uint64_t K, uint64_t rows,
@@ -343,13 +346,15 @@ cudaError_t make_bf16_map(void* map, const void* base, uint64_t K, uint64_t rows
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+namespace {
+
 template <int MODE>
-cudaError_t launch_gemm(const Moe& m, const dtc::Args& a, const void* map_w, const void* map_hi,
+cudaError_t launch_gemm(int sm_count, const dtc::Args& a, const void* map_w, const void* map_hi,
                         const void* map_lo, cudaStream_t st) {
   auto k = dtc::dense_tc_gemm<MODE>;
   cudaError_t e = set_smem_limit(k, dtc::kSmemBytes);
   if (e != cudaSuccess) return e;
-  k<<<m.sm_count, dtc::kThreads, dtc::kSmemBytes, st>>>(
+  k<<<sm_count, dtc::kThreads, dtc::kSmemBytes, st>>>(
       *reinterpret_cast<const CUtensorMap*>(map_w), *reinterpret_cast<const CUtensorMap*>(map_hi),
       *reinterpret_cast<const CUtensorMap*>(map_lo), a);
   return cudaGetLastError();
@@ -365,6 +370,8 @@ dtc::Args base_args(const Moe& m, int* err) {
   return a;
 }
 
+}  // namespace
+
 cudaError_t split_rows(const float* x, const int32_t* perm, int perm_div, int H, int64_t positions,
                        __nv_bfloat16* xh, __nv_bfloat16* xl, cudaStream_t st) {
   if (positions <= 0) return cudaSuccess;
@@ -373,7 +380,24 @@ cudaError_t split_rows(const float* x, const int32_t* perm, int perm_div, int H,
   return cudaGetLastError();
 }
 
-}  // namespace
+cudaError_t launch_linear_tc(int sm_count, const void* map_w, const void* map_xh,
+                             const void* map_xl, int K, int rows, int n_pos, const float* bias,
+                             float* out, int out_stride, bool add_out, int* err,
+                             cudaStream_t st) {
+  if (n_pos <= 0) return cudaSuccess;
+  dtc::Args a{};
+  a.err = err;
+  a.wait_ns = kMbarWaitNs;
+  a.uniform_rows = n_pos;
+  a.K = K;
+  a.rows = rows;
+  a.m_tiles = (rows + dtc::BM - 1) / dtc::BM;
+  a.out_y = out;
+  a.out_stride = out_stride;
+  a.bias = bias;
+  a.add_out = add_out ? 1 : 0;
+  return launch_gemm<dtc::DOWN>(sm_count, a, map_w, map_xh, map_xl, st);
+}
 
 bool dense_tc_supported(const Moe& m) {
   const gb_moe_desc& d = m.desc;
@@ -442,7 +466,7 @@ cudaError_t launch_dense_tc_gate_up(const Moe& m, const Groups& g, const float* 
   a.out_hi = reinterpret_cast<__nv_bfloat16*>(eb.hh);
   a.out_lo = reinterpret_cast<__nv_bfloat16*>(eb.hl);
   a.out_stride = d.inter;
-  return launch_gemm<dtc::GATE_UP>(m, a, m.w.map_dense_gu, eb.map_xh, eb.map_xl, st);
+  return launch_gemm<dtc::GATE_UP>(m.sm_count, a, m.w.map_dense_gu, eb.map_xh, eb.map_xl, st);
 }
 
 cudaError_t launch_dense_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
@@ -458,7 +482,7 @@ cudaError_t launch_dense_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, 
   a.out_y = eb.y;
   a.out_rows = g.out_rows;
   a.out_stride = d.hidden;
-  return launch_gemm<dtc::DOWN>(m, a, m.w.map_dense_dn, eb.map_hh, eb.map_hl, st);
+  return launch_gemm<dtc::DOWN>(m.sm_count, a, m.w.map_dense_dn, eb.map_hh, eb.map_hl, st);
 }
 
 cudaError_t launch_shared_expert_tc(const Moe& m, const float* x, int64_t T, float* y,
@@ -477,7 +501,7 @@ cudaError_t launch_shared_expert_tc(const Moe& m, const float* x, int64_t T, flo
   a.out_hi = ws.sh_hh;
   a.out_lo = ws.sh_hl;
   a.out_stride = d.shared_inter;
-  if ((e = launch_gemm<dtc::GATE_UP>(m, a, m.w.map_sh_gu, ws.map_sh_xh, ws.map_sh_xl, st)) !=
+  if ((e = launch_gemm<dtc::GATE_UP>(m.sm_count, a, m.w.map_sh_gu, ws.map_sh_xh, ws.map_sh_xl, st)) !=
       cudaSuccess)
     return e;
   dtc::Args b = base_args(m, ws.meta + 1);
@@ -487,7 +511,7 @@ cudaError_t launch_shared_expert_tc(const Moe& m, const float* x, int64_t T, flo
   b.m_tiles = (b.rows + dtc::BM - 1) / dtc::BM;
   b.out_y = y;
   b.out_stride = d.hidden;
-  return launch_gemm<dtc::DOWN>(m, b, m.w.map_sh_dn, ws.map_sh_hh, ws.map_sh_hl, st);
+  return launch_gemm<dtc::DOWN>(m.sm_count, b, m.w.map_sh_dn, ws.map_sh_hh, ws.map_sh_hl, st);
 }
 
 }  // namespace gb

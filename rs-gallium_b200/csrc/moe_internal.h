@@ -391,6 +391,23 @@ cudaError_t launch_shared_expert_tc(const Moe& m, const float* x, int64_t T, flo
                                     cudaStream_t st);
 // Whether the shared expert of a T-token forward runs on the tensor cores.
 bool use_dense_tc_shared(const Moe& m, int64_t T);
+
+// Plain bf16-weight linear layers on the same tensor-core kernel (the GPT-OSS
+// decode stack's projections and LM head, decoder.cu).
+// make_bf16_map: CUtensorMap of a bf16 [rows][K] matrix, boxes of box_rows
+// rows x 64 columns, 128-byte swizzle (K a multiple of 64).
+cudaError_t make_bf16_map(void* map, const void* base, uint64_t K, uint64_t rows,
+                          uint32_t box_rows);
+constexpr int kLinearBoxRows = 128;  // weight rows and activation rows per tile
+// f32 rows (through perm / perm_div when perm is set) -> bf16 hi / lo [positions][H].
+cudaError_t split_rows(const float* x, const int32_t* perm, int perm_div, int H, int64_t positions,
+                       __nv_bfloat16* xh, __nv_bfloat16* xl, cudaStream_t st);
+// out[p][r] = (add_out ? out[p][r] : 0) + (W[r] . x[p] + bias[r]) for p < n_pos,
+// r < rows: map_w of W [rows][K], map_xh / map_xl of the split activations.
+cudaError_t launch_linear_tc(int sm_count, const void* map_w, const void* map_xh,
+                             const void* map_xl, int K, int rows, int n_pos, const float* bias,
+                             float* out, int out_stride, bool add_out, int* err,
+                             cudaStream_t st);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
                                   cudaStream_t st);
 cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,

@@ -119,6 +119,51 @@ class MoeInfo(ctypes.Structure):
     ]
 
 
+class DecoderLayer(ctypes.Structure):
+    _fields_ = [
+        ("attn_norm", c_void_p),
+        ("post_attn_norm", c_void_p),
+        ("wq", c_void_p),
+        ("wk", c_void_p),
+        ("wv", c_void_p),
+        ("wo", c_void_p),
+        ("bq", c_void_p),
+        ("bk", c_void_p),
+        ("bv", c_void_p),
+        ("bo", c_void_p),
+        ("sinks", c_void_p),
+        ("sliding", c_int32),
+        ("moe", POINTER(MoeDesc)),
+    ]
+
+
+class DecoderDesc(ctypes.Structure):
+    _fields_ = [
+        ("struct_size", c_uint32),
+        ("n_layers", c_int32),
+        ("hidden", c_int32),
+        ("n_heads", c_int32),
+        ("n_kv_heads", c_int32),
+        ("head_dim", c_int32),
+        ("vocab", c_int32),
+        ("sliding_window", c_int32),
+        ("max_seq_len", c_int32),
+        ("max_batch", c_int32),
+        ("max_tokens", c_int32),
+        ("rope_theta", c_float),
+        ("rope_scaling_factor", c_float),
+        ("rope_orig_ctx", c_int32),
+        ("rope_beta_fast", c_float),
+        ("rope_beta_slow", c_float),
+        ("rms_eps", c_float),
+        ("device", c_int32),
+        ("embed", c_void_p),
+        ("lm_head", c_void_p),
+        ("final_norm", c_void_p),
+        ("layers", POINTER(DecoderLayer)),
+    ]
+
+
 # name -> (restype, argtypes); every symbol the header declares.
 SIGNATURES = {
     "gb_moe_create": (c_int, [POINTER(MoeDesc), POINTER(c_void_p)]),
@@ -138,6 +183,16 @@ SIGNATURES = {
     "gb_moe_stage_name": (c_char_p, [c_int32]),
     "gb_route_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32,
                                  c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "gb_decoder_create": (c_int, [POINTER(DecoderDesc), POINTER(c_void_p)]),
+    "gb_decoder_forward": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p,
+                                   c_void_p, c_void_p]),
+    "gb_decoder_generate": (c_int, [c_void_p, c_void_p, c_int32, c_int64, c_int32, c_void_p,
+                                    c_void_p]),
+    "gb_decoder_reset": (c_int, [c_void_p]),
+    "gb_decoder_set_profiling": (c_int, [c_void_p, c_int32]),
+    "gb_decoder_stage_times": (c_int, [c_void_p, POINTER(c_float), c_void_p]),
+    "gb_decoder_device_status": (c_int, [c_void_p, c_void_p]),
+    "gb_decoder_destroy": (c_int, [c_void_p]),
     "gb_nccl_unique_id": (c_int, [POINTER(c_uint8)]),
     "gb_last_error": (c_char_p, []),
     "gb_abi_version": (c_int, []),

@@ -302,3 +302,94 @@ def gemma4_layer(n_experts: int = 128, hidden: int = 2816, inter: int = 704, top
                           u(H), u(H), gu, dn,
                           rng.uniform(0.5, 2.0, E).astype(np.float32) if expert_scale else None,
                           u(H), meta={"seed": seed})
+
+
+# ---- GPT-OSS decode stack (gpt_oss_q.rs:15-107, 270-472) --------------------
+
+@dataclass
+class DecoderLayerWeights:
+    attn_norm: np.ndarray        # [H] f32
+    post_attn_norm: np.ndarray   # [H] f32
+    wq: np.ndarray               # [nh * hd, H] bf16 bits
+    wk: np.ndarray               # [nkv * hd, H]
+    wv: np.ndarray               # [nkv * hd, H]
+    wo: np.ndarray               # [H, nh * hd]
+    bq: Optional[np.ndarray]     # f32 biases or None
+    bk: Optional[np.ndarray]
+    bv: Optional[np.ndarray]
+    bo: Optional[np.ndarray]
+    sinks: np.ndarray            # [nh] f32
+    sliding: int                 # 1: sliding-window attention
+    moe: GptOssGgufLayer         # the layer's MoE block (GGUF MXFP4, gpt_oss_q.rs:119-269)
+
+
+@dataclass
+class GptOssDecoderWeights:
+    hidden: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    sliding_window: int
+    rope_theta: float
+    rope_scaling_factor: float
+    rope_orig_ctx: int
+    rms_eps: float
+    embed: np.ndarray            # [vocab, H] bf16 bits
+    lm_head: Optional[np.ndarray]  # [vocab, H] bf16 bits, None: tied
+    final_norm: np.ndarray       # [H] f32
+    layers: list
+    meta: dict = field(default_factory=dict)
+
+    @property
+    def n_layers(self) -> int:
+        return len(self.layers)
+
+
+def gptoss_decoder(n_layers: int = 24, hidden: int = 2880, n_heads: int = 64,
+                   n_kv_heads: int = 8, head_dim: int = 64, vocab: int = 201088,
+                   n_experts: int = 32, inter: int = 2880, top_k: int = 4,
+                   sliding_window: int = 128, rope_theta: float = 150000.0,
+                   rope_scaling_factor: float = 32.0, rope_orig_ctx: int = 4096,
+                   rms_eps: float = 1e-5, seed: int = 0,
+                   share_experts: bool = False) -> GptOssDecoderWeights:
+    """A GPT-OSS-shaped decode stack with random weights (defaults: the
+    20B shape).  Attention and LM-head weights bf16 ~ N(0, 1/sqrt(fan_in)),
+    biases ~ N(0, 0.01), norm weights 1 + N(0, 0.02), sink logits ~ N(0, 1),
+    embeddings ~ N(0, 1); even layers sliding-window, odd layers full
+    (gpt_oss_q.rs:360-375).  Each layer's MoE block is the GGUF view of
+    gptoss_layer(n_experts, hidden, inter, top_k); share_experts reuses one
+    block's host arrays for every layer (each layer still gets its own copy on
+    the device)."""
+    rng = np.random.default_rng([seed, 0xDEC0])
+    H, qn, kn = hidden, n_heads * head_dim, n_kv_heads * head_dim
+
+    def w(shape, fan_in):
+        return f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32) *
+                                np.float32(fan_in ** -0.5))
+
+    def vec(n, std, mean=0.0):
+        return (np.float32(mean) + rng.standard_normal(n, dtype=np.float32) *
+                np.float32(std)).astype(np.float32)
+
+    shared = None
+    layers = []
+    for i in range(n_layers):
+        if share_experts and shared is not None:
+            moe = shared
+        else:
+            moe = gptoss_gguf_from_split(gptoss_layer(n_experts=n_experts, hidden=hidden,
+                                                      inter=inter, top_k=top_k,
+                                                      seed=seed * 1000 + i))
+            shared = moe
+        layers.append(DecoderLayerWeights(
+            attn_norm=vec(H, 0.02, 1.0), post_attn_norm=vec(H, 0.02, 1.0),
+            wq=w((qn, H), H), wk=w((kn, H), H), wv=w((kn, H), H), wo=w((H, qn), qn),
+            bq=vec(qn, 0.01), bk=vec(kn, 0.01), bv=vec(kn, 0.01), bo=vec(H, 0.01),
+            sinks=vec(n_heads, 1.0), sliding=1 if i % 2 == 0 else 0, moe=moe))
+    embed = f32_to_bf16_bits(rng.standard_normal((vocab, H), dtype=np.float32))
+    lm_head = w((vocab, H), H)
+    return GptOssDecoderWeights(H, n_heads, n_kv_heads, head_dim, vocab, sliding_window,
+                                rope_theta, rope_scaling_factor, rope_orig_ctx, rms_eps, embed,
+                                lm_head, vec(H, 0.02, 1.0), layers,
+                                meta={"seed": seed, "share_experts": share_experts})

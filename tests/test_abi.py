@@ -29,7 +29,7 @@ def test_library_exports_every_declared_symbol():
     for n in names:
         assert hasattr(lib, n), f"{n} declared in the header but not exported"
         assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
-    assert lib.gb_abi_version() == 3
+    assert lib.gb_abi_version() == 4
 
 
 def test_struct_layouts_match_the_header(tmp_path):

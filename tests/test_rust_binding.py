@@ -12,6 +12,8 @@ FFI = os.path.join(ROOT, "rs-gallium_b200", "crates", "gallium-b200", "src", "ff
 C_TO_RUST = {
     "uint32_t": "u32", "int32_t": "i32", "int64_t": "i64", "float": "f32",
     "const void*": "*const c_void", "const uint8_t*": "*const u8", "const float*": "*const f32",
+    "const uint16_t*": "*const u16", "const gb_moe_desc*": "*const gb_moe_desc",
+    "const gb_decoder_layer*": "*const gb_decoder_layer",
 }
 
 
@@ -38,7 +40,7 @@ def _rust_struct(src, name):
 
 def test_structs_match_the_header_field_for_field():
     h, r = open(HEADER).read(), open(FFI).read()
-    for name in ("gb_moe_desc", "gb_moe_info"):
+    for name in ("gb_moe_desc", "gb_moe_info", "gb_decoder_layer", "gb_decoder_desc"):
         assert _rust_struct(r, name) == _c_struct(h, name), name
 
 
