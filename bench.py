@@ -21,7 +21,13 @@ The same line carries, under "configs", the workload's other layers:
                              experts (a Qwen3-MoE-like shape: hidden 2048,
                              128 experts, top-8, intermediate 768, SiLU) and a
                              512-wide shared expert, at 1, 64 and 2048 tokens
-                             per GPU, expert parallel when N > 1.
+                             per GPU, expert parallel when N > 1;
+  gptoss20b_decode           the GPT-OSS-20B-shaped decode stack around the
+                             MoE block (24 layers, attention with sinks and a
+                             128-token sliding window on even layers, vocab
+                             201088): greedy decode of 256 tokens from random
+                             128-token prompts at batch 1 and 32, tokens/s and
+                             the MoE block's share of a step, one GPU only.
 Each with its own roofline and a parity check against the oracle.
 
 Arms:
@@ -156,6 +162,9 @@ def parse_args():
                     help="extra per-GPU batch sizes to measure ('' = none)")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the 20B-shaped and LFM2.5-shaped layers")
+    ap.add_argument("--configs", default="all",
+                    help="comma list of the extra layers to run (20b_balanced, 20b_skewed, "
+                         "lfm2_q4k, moeffn_dense, gptoss20b_decode), or all")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--parity-rows", type=int, default=64)
@@ -544,6 +553,117 @@ def run_config(model, seed, local, rank, world, tokens, args, flush, peaks, thre
         arm.close()
 
 
+DEC_PROMPT, DEC_STEPS, DEC_CONTEXT = 128, 256, 4096
+
+
+def run_decode_config(args, local, peaks, threads, batches=(1, 32)):
+    """The GPT-OSS-20B-shaped decode stack (24 layers, 64 query / 8 KV heads
+    of 64, sliding window 128 on even layers, vocab 201088, bf16 attention
+    and LM head, the 32-expert MXFP4 MoE block in every layer): for each
+    batch, a prompt of DEC_PROMPT random ids per sequence, then DEC_STEPS
+    greedy steps timed on the device (each step one replayed CUDA graph).
+    The MoE share comes from one profiled eager step.  Parity: the logits
+    of a 4-token prompt against the oracle of the whole stack."""
+    import torch
+    from gallium_b200 import GptOssQ, synth
+
+    w = synth.gptoss_decoder(n_layers=24, seed=args.seed, share_experts=True)
+    Bmax = max(batches)
+    out = {"workload": ("gpt-oss-20b-shaped decode stack: 24 layers, H=2880, 64/8 heads of 64, "
+                        "sliding window 128 on even layers, vocab 201088, bf16 attention and LM "
+                        "head, 32-expert MXFP4 MoE (top-4) per layer; KV cache context "
+                        f"{DEC_CONTEXT}; prompt {DEC_PROMPT} random ids, {DEC_STEPS} greedy "
+                        "steps timed"),
+           "weights": "random; every layer's experts drawn from one seed (own device copy each)",
+           "results": []}
+    m = GptOssQ.load(w, device=local, max_batch=Bmax, max_tokens=DEC_PROMPT,
+                     max_seq_len=DEC_CONTEXT)
+    try:
+        stream = torch.cuda.current_stream()
+        H, L, V = w.hidden, w.n_layers, w.vocab
+        # bf16 q/k/v rows [(nh + 2 nkv) hd][H] and o rows [H][nh hd]
+        attn_bytes = L * 2 * H * ((w.n_heads + 2 * w.n_kv_heads) * w.head_dim +
+                                  w.n_heads * w.head_dim)
+        expert_bytes = w.layers[0].moe.base.expert_bytes + w.layers[0].moe.base.expert_bias_bytes
+        for B in batches:
+            rng = np.random.default_rng(args.seed + B)
+            prompt = torch.from_numpy(rng.integers(0, V, (B, DEC_PROMPT)).astype(np.int32)).cuda()
+
+            def prefill():
+                m.reset()
+                m.forward(prompt, 0, check_status=False)
+                return m.last_next.clone()
+
+            first = prefill()
+            m.generate(first, DEC_PROMPT, 4)          # captures the step graph for B
+            first = prefill()
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            toks = m.generate(first, DEC_PROMPT, DEC_STEPS, check_status=False)
+            e.record(stream)
+            torch.cuda.synchronize()
+            ms = s.elapsed_time(e)
+            m._lib.gb_decoder_device_status(m._h, stream.cuda_stream)
+            ms_step = ms / DEC_STEPS
+            # MoE share: one profiled eager step after the same prefill
+            first = prefill()
+            m.set_profiling(True)
+            m.generate(first, DEC_PROMPT, 2, check_status=False)
+            st = m.stage_times()
+            m.set_profiling(False)
+            total = sum(st.values())
+            # bytes one step must read: attention and LM-head weights, the
+            # experts the step touches (expected for uniform routing), the KV
+            # cache at the mean context of the timed steps
+            ctx = DEC_PROMPT + DEC_STEPS / 2
+            kv = B * w.n_kv_heads * w.head_dim * 4 * 2 * (
+                (L // 2) * ctx + (L - L // 2) * min(ctx, w.sliding_window))
+            E, k = 32, 4
+            touched = E * (1 - (1 - k / E) ** B)
+            bytes_step = attn_bytes + V * H * 2 + L * touched * expert_bytes + kv
+            achieved = bytes_step / (ms_step / 1e3) / 1e9
+            peak = peaks["hbm_gbs"]
+            out["results"].append({
+                "batch": B, "value": B * DEC_STEPS / (ms / 1e3), "unit": "tokens/s",
+                "ms_per_step": ms_step,
+                "stage_ms_eager_step": st,
+                "moe_share": st["moe"] / total if total > 0 else None,
+                "roofline": {"kernel": "whole decode step", "bound": "hbm",
+                             "achieved": achieved, "peak": peak, "unit": "GB/s",
+                             "frac": achieved / peak, "peak_source": peaks["source"],
+                             "algorithmic_bytes": int(bytes_step),
+                             "experts_touched_per_layer": touched, "traffic": None},
+                "tokens_sample": toks[:4, :min(B, 4)].cpu().numpy().tolist(),
+            })
+        if not args.no_parity:
+            out["parity"] = decode_parity(w, m, threads)
+    finally:
+        m.close()
+    return out
+
+
+def decode_parity(w, m, threads):
+    """Logits of a 4-token prompt (batch 1) against the oracle of the whole
+    stack, and the greedy token."""
+    import torch
+    from oracle import decoder_oracle as dor
+
+    toks = np.random.default_rng(77).integers(0, w.vocab, (1, 4)).astype(np.int32)
+    m.reset()
+    got = m.forward(torch.from_numpy(toks).cuda(), 0).cpu().numpy()
+    orc = dor.OracleDecoder(w, max_seq_len=8)
+    want = orc.forward(toks, 0)
+    err = np.abs(got.astype(np.float64) - want)
+    max_abs, mean_rel = float(err.max()), float(err.sum() / np.abs(want).sum())
+    g, o = int(dor.greedy(got)[0]), int(dor.greedy(want)[0])
+    gap = abs(float(want[0, g]) - float(want[0, o]))
+    ok = max_abs <= MAX_ABS and mean_rel <= MEAN_REL and (g == o or gap < 5e-3)
+    return {"prompt_tokens": 4, "max_abs": max_abs, "mean_rel": mean_rel,
+            "greedy_equal": g == o, "bar": {"max_abs": MAX_ABS, "mean_rel": MEAN_REL},
+            "pass": bool(ok)}
+
+
 def run_ours(args, world, rank, local):
     import torch
     from gallium_b200._lib import check, load_library
@@ -612,15 +732,26 @@ def run_ours(args, world, rank, local):
 
     # ---- the workload's other layers ----------------------------------------
     configs = {}
+    want = set(args.configs.split(",")) if args.configs != "all" else None
+
+    def on(name):
+        return want is None or name in want
+
     if not args.no_configs and args.model == "gptoss":
         if world == 1:
             for name, sk in (("20b_balanced", False), ("20b_skewed", True)):
-                configs[name] = run_config(Model("gptoss", 32, sk), args.seed, local, rank, world,
-                                           [4096], args, flush, peaks, threads)
-        configs["lfm2_q4k"] = run_config(Model("lfm2", 32), args.seed, local, rank, world,
-                                         [1, 64, 2048], args, flush, peaks, threads)
-        configs["moeffn_dense"] = run_config(Model("dense", 128), args.seed, local, rank, world,
+                if on(name):
+                    configs[name] = run_config(Model("gptoss", 32, sk), args.seed, local, rank,
+                                               world, [4096], args, flush, peaks, threads)
+        if on("lfm2_q4k"):
+            configs["lfm2_q4k"] = run_config(Model("lfm2", 32), args.seed, local, rank, world,
                                              [1, 64, 2048], args, flush, peaks, threads)
+        if on("moeffn_dense"):
+            configs["moeffn_dense"] = run_config(Model("dense", 128), args.seed, local, rank,
+                                                 world, [1, 64, 2048], args, flush, peaks,
+                                                 threads)
+        if world == 1 and on("gptoss20b_decode"):
+            configs["gptoss20b_decode"] = run_decode_config(args, local, peaks, threads)
 
     # ---- CPU baseline (rank 0, one GPU only) ---------------------------------
     cpu = None
@@ -630,7 +761,8 @@ def run_ours(args, world, rank, local):
                "sample": (f"full batch: all {T} tokens routed and every active expert run "
                           f"(oracle/cpu_reference.py), mean of 2 forwards after 1 warm-up")}
 
-    all_parity = [parity] + [r.get("parity") for c in configs.values() for r in c["results"]]
+    all_parity = ([parity] + [r.get("parity") for c in configs.values() for r in c["results"]] +
+                  [c.get("parity") for c in configs.values()])
     ok = all(p is None or p["pass"] for p in all_parity)
     if rank == 0:
         line = {

@@ -364,9 +364,18 @@ def gptoss_decoder(n_layers: int = 24, hidden: int = 2880, n_heads: int = 64,
     rng = np.random.default_rng([seed, 0xDEC0])
     H, qn, kn = hidden, n_heads * head_dim, n_kv_heads * head_dim
 
-    def w(shape, fan_in):
-        return f32_to_bf16_bits(rng.standard_normal(shape, dtype=np.float32) *
-                                np.float32(fan_in ** -0.5))
+    def w(shape, fan_in, std=None):
+        # in chunks of rows, so the f32 and bf16 temporaries stay small
+        out = np.empty(shape, np.uint16)
+        scale = np.float32(fan_in ** -0.5 if std is None else std)
+        step = max(1, (1 << 22) // shape[1])
+        for r0 in range(0, shape[0], step):
+            r1 = min(shape[0], r0 + step)
+            u = (rng.standard_normal((r1 - r0, shape[1]), dtype=np.float32) * scale).view(
+                np.uint32)
+            # round to nearest even in 32-bit arithmetic (finite values only)
+            out[r0:r1] = ((u + (((u >> 16) & 1) + 0x7FFF)) >> 16).astype(np.uint16)
+        return out
 
     def vec(n, std, mean=0.0):
         return (np.float32(mean) + rng.standard_normal(n, dtype=np.float32) *
@@ -387,7 +396,7 @@ def gptoss_decoder(n_layers: int = 24, hidden: int = 2880, n_heads: int = 64,
             wq=w((qn, H), H), wk=w((kn, H), H), wv=w((kn, H), H), wo=w((H, qn), qn),
             bq=vec(qn, 0.01), bk=vec(kn, 0.01), bv=vec(kn, 0.01), bo=vec(H, 0.01),
             sinks=vec(n_heads, 1.0), sliding=1 if i % 2 == 0 else 0, moe=moe))
-    embed = f32_to_bf16_bits(rng.standard_normal((vocab, H), dtype=np.float32))
+    embed = w((vocab, H), H, std=1.0)
     lm_head = w((vocab, H), H)
     return GptOssDecoderWeights(H, n_heads, n_kv_heads, head_dim, vocab, sliding_window,
                                 rope_theta, rope_scaling_factor, rope_orig_ctx, rms_eps, embed,
