@@ -165,6 +165,10 @@ def parse_args():
     ap.add_argument("--configs", default="all",
                     help="comma list of the extra layers to run (20b_balanced, 20b_skewed, "
                          "lfm2_q4k, moeffn_dense, gptoss20b_decode), or all")
+    ap.add_argument("--decode-batches", default="1,32",
+                    help="batches of the gptoss20b_decode config")
+    ap.add_argument("--decode-steps", type=int, default=256,
+                    help="greedy steps timed in the gptoss20b_decode config")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--parity-rows", type=int, default=64)
@@ -553,26 +557,28 @@ def run_config(model, seed, local, rank, world, tokens, args, flush, peaks, thre
         arm.close()
 
 
-DEC_PROMPT, DEC_STEPS, DEC_CONTEXT = 128, 256, 4096
+DEC_PROMPT, DEC_CONTEXT = 128, 4096
 
 
-def run_decode_config(args, local, peaks, threads, batches=(1, 32)):
+def run_decode_config(args, local, peaks, threads):
     """The GPT-OSS-20B-shaped decode stack (24 layers, 64 query / 8 KV heads
     of 64, sliding window 128 on even layers, vocab 201088, bf16 attention
     and LM head, the 32-expert MXFP4 MoE block in every layer): for each
-    batch, a prompt of DEC_PROMPT random ids per sequence, then DEC_STEPS
+    batch, a prompt of DEC_PROMPT random ids per sequence, then --decode-steps
     greedy steps timed on the device (each step one replayed CUDA graph).
     The MoE share comes from one profiled eager step.  Parity: the logits
     of a 4-token prompt against the oracle of the whole stack."""
     import torch
     from gallium_b200 import GptOssQ, synth
 
+    batches = [int(b) for b in args.decode_batches.split(",") if b.strip()]
+    steps = args.decode_steps
     w = synth.gptoss_decoder(n_layers=24, seed=args.seed, share_experts=True)
     Bmax = max(batches)
     out = {"workload": ("gpt-oss-20b-shaped decode stack: 24 layers, H=2880, 64/8 heads of 64, "
                         "sliding window 128 on even layers, vocab 201088, bf16 attention and LM "
                         "head, 32-expert MXFP4 MoE (top-4) per layer; KV cache context "
-                        f"{DEC_CONTEXT}; prompt {DEC_PROMPT} random ids, {DEC_STEPS} greedy "
+                        f"{DEC_CONTEXT}; prompt {DEC_PROMPT} random ids, {steps} greedy "
                         "steps timed"),
            "weights": "random; every layer's experts drawn from one seed (own device copy each)",
            "results": []}
@@ -600,12 +606,12 @@ def run_decode_config(args, local, peaks, threads, batches=(1, 32)):
             torch.cuda.synchronize()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record(stream)
-            toks = m.generate(first, DEC_PROMPT, DEC_STEPS, check_status=False)
+            toks = m.generate(first, DEC_PROMPT, steps, check_status=False)
             e.record(stream)
             torch.cuda.synchronize()
             ms = s.elapsed_time(e)
             m._lib.gb_decoder_device_status(m._h, stream.cuda_stream)
-            ms_step = ms / DEC_STEPS
+            ms_step = ms / steps
             # MoE share: one profiled eager step after the same prefill
             first = prefill()
             m.set_profiling(True)
@@ -616,7 +622,7 @@ def run_decode_config(args, local, peaks, threads, batches=(1, 32)):
             # bytes one step must read: attention and LM-head weights, the
             # experts the step touches (expected for uniform routing), the KV
             # cache at the mean context of the timed steps
-            ctx = DEC_PROMPT + DEC_STEPS / 2
+            ctx = DEC_PROMPT + steps / 2
             kv = B * w.n_kv_heads * w.head_dim * 4 * 2 * (
                 (L // 2) * ctx + (L - L // 2) * min(ctx, w.sliding_window))
             E, k = 32, 4
@@ -625,7 +631,7 @@ def run_decode_config(args, local, peaks, threads, batches=(1, 32)):
             achieved = bytes_step / (ms_step / 1e3) / 1e9
             peak = peaks["hbm_gbs"]
             out["results"].append({
-                "batch": B, "value": B * DEC_STEPS / (ms / 1e3), "unit": "tokens/s",
+                "batch": B, "value": B * steps / (ms / 1e3), "unit": "tokens/s",
                 "ms_per_step": ms_step,
                 "stage_ms_eager_step": st,
                 "moe_share": st["moe"] / total if total > 0 else None,

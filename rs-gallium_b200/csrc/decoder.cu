@@ -60,35 +60,72 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint16_t*
 // after adding `delta` into the residual stream when delta is set
 // (h = h + delta; the reference's `h + h_moe`).  Row r of the input is row
 // src_row(r) = r * src_stride + src_off, so the final norm can take each
-// sequence's last token.  One CTA per output row.
-__global__ void add_rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ delta,
-                                   const float* __restrict__ w, int H, float eps, int src_stride,
-                                   int src_off, float* __restrict__ out) {
+// sequence's last token.  One CTA of kNormThreads per output row; each
+// thread keeps its float4s of the row in registers, so the row is read once
+// and every load is issued before the first is used (H <= 4 * 4 * 1024).
+constexpr int kNormThreads = 1024;
+constexpr int kNormVec = 4;  // float4s per thread
+__global__ void __launch_bounds__(kNormThreads)
+    add_rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ delta,
+                       const float* __restrict__ w, int H, float eps, int src_stride, int src_off,
+                       float* __restrict__ out) {
   __shared__ float red[32];
   const int r = blockIdx.x;
-  float* x = h + (int64_t)(r * src_stride + src_off) * H;
-  const float* dx = delta ? delta + (int64_t)(r * src_stride + src_off) * H : nullptr;
-  float ss = 0.0f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = x[i];
-    if (dx) {
-      v = __fadd_rn(v, dx[i]);
-      x[i] = v;
+  const int64_t src = (int64_t)(r * src_stride + src_off) * H;
+  float4* x4 = reinterpret_cast<float4*>(h + src);
+  const float4* d4 = delta ? reinterpret_cast<const float4*>(delta + src) : nullptr;
+  const int n4 = H / 4;
+  float4 v[kNormVec];
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    v[j] = i < n4 ? x4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (d4) {
+#pragma unroll
+    for (int j = 0; j < kNormVec; ++j) {
+      const int i = threadIdx.x + j * kNormThreads;
+      if (i < n4) {
+        const float4 dv = d4[i];
+        v[j].x = __fadd_rn(v[j].x, dv.x);
+        v[j].y = __fadd_rn(v[j].y, dv.y);
+        v[j].z = __fadd_rn(v[j].z, dv.z);
+        v[j].w = __fadd_rn(v[j].w, dv.w);
+        x4[i] = v[j];
+      }
     }
-    ss = __fmaf_rn(v, v, ss);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    ss = __fmaf_rn(v[j].x, v[j].x, ss);
+    ss = __fmaf_rn(v[j].y, v[j].y, ss);
+    ss = __fmaf_rn(v[j].z, v[j].z, ss);
+    ss = __fmaf_rn(v[j].w, v[j].w, ss);
   }
   ss = warp_sum_butterfly(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-    v = warp_sum_butterfly(v);
-    if (threadIdx.x == 0) red[0] = v;
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    t = warp_sum_butterfly(t);
+    if (threadIdx.x == 0) red[0] = t;
   }
   __syncthreads();
   const float m = sqrtf(__fadd_rn(__fdiv_rn(red[0], (float)H), eps));
-  for (int i = threadIdx.x; i < H; i += blockDim.x)
-    out[(int64_t)r * H + i] = __fmul_rn(__fdiv_rn(x[i], m), w[i]);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* o4 = reinterpret_cast<float4*>(out + (int64_t)r * H);
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int i = threadIdx.x + j * kNormThreads;
+    if (i < n4) {
+      const float4 wv = w4[i];
+      o4[i] = make_float4(__fmul_rn(__fdiv_rn(v[j].x, m), wv.x),
+                          __fmul_rn(__fdiv_rn(v[j].y, m), wv.y),
+                          __fmul_rn(__fdiv_rn(v[j].z, m), wv.z),
+                          __fmul_rn(__fdiv_rn(v[j].w, m), wv.w));
+    }
+  }
 }
 
 // ---- linear layers on the CUDA cores (fewer than 16 rows) ------------------
@@ -117,9 +154,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     float acc[2][kGemvRows];
 #pragma unroll
     for (int j = 0; j < kGemvRows; ++j) acc[0][j] = acc[1][j] = 0.0f;
+#pragma unroll 4
     for (int q = lane; q < npieces; q += 32) {
-      const uint4 a = ld_stream_u4(w0 + (int64_t)q * 8);
-      const uint4 b = ld_stream_u4(w1 + (int64_t)q * 8);
+      const uint4 a = __ldg(reinterpret_cast<const uint4*>(w0) + q);
+      const uint4 b = __ldg(reinterpret_cast<const uint4*>(w1) + q);
       const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int j = 0; j < kGemvRows; ++j) {
@@ -156,41 +194,105 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   }
 }
 
+// The same product for up to kGemvRows rows of x, a warp per output row:
+// each lane requests all its 16-byte pieces of the row (KP per pass of 32 KP
+// pieces) before the first multiply, so a warp keeps up to 8 KB of weights
+// in flight.  Used when x has at most kGemvRows rows.
+template <int KP>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    gemv_rows_kernel(const float* __restrict__ x, int n_x, int K,
+                     const uint16_t* __restrict__ W, int n_out, const float* __restrict__ bias,
+                     float* __restrict__ out, int out_stride, int add) {
+  extern __shared__ float xs[];  // [n_x][K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const int n4 = n_x * K / 4;
+    const float4* src = reinterpret_cast<const float4*>(x);
+    float4* dst = reinterpret_cast<float4*>(xs);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  const int o = blockIdx.x * kGemvWarps + warp;
+  if (o >= n_out) return;
+  const uint4* wr = reinterpret_cast<const uint4*>(W + (int64_t)o * K);
+  const int npieces = K / 8;
+  float acc[kGemvRows];
+#pragma unroll
+  for (int j = 0; j < kGemvRows; ++j) acc[j] = 0.0f;
+  for (int base = 0; base < npieces; base += 32 * KP) {
+    uint4 wv[KP];
+#pragma unroll
+    for (int u = 0; u < KP; ++u) {
+      const int q = base + lane + 32 * u;
+      wv[u] = q < npieces ? __ldg(wr + q) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < KP; ++u) {
+      const int q = base + lane + 32 * u;
+      if (q < npieces) {
+        const uint32_t ww[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+        for (int j = 0; j < kGemvRows; ++j) {
+          if (j < n_x) {
+            const float* xj = xs + j * K + q * 8;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              acc[j] = __fmaf_rn(xj[2 * e], __uint_as_float(ww[e] << 16), acc[j]);
+              acc[j] = __fmaf_rn(xj[2 * e + 1], __uint_as_float(ww[e] & 0xffff0000u), acc[j]);
+            }
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kGemvRows; ++j) {
+    if (j >= n_x) break;
+    const float sum = warp_sum_butterfly(acc[j]);
+    if (lane == 0) {
+      float* dst = out + (int64_t)j * out_stride + o;
+      float r = bias ? __fadd_rn(sum, bias[o]) : sum;
+      if (add) r = __fadd_rn(*dst, r);
+      *dst = r;
+    }
+  }
+}
+
 // ---- RoPE and the KV cache --------------------------------------------------
 
 // Rotates the q and k heads of row (b, t) at position pos + t in place
 // (candle_nn::rotary_emb::rope, halves layout: x1' = x1 cos - x2 sin,
 // x2' = x1 sin + x2 cos, each product rounded, pos_enc.rs:199-217) and
-// stores k and v at that position of sequence b's cache.  One CTA per row.
+// stores k and v at that position of sequence b's cache.  Grid (rows,
+// heads nh + 2 nkv); one thread per rotated pair (hd / 2 threads).
 __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int nh, int nkv, int hd,
                                    const float* __restrict__ cos_t,
                                    const float* __restrict__ sin_t, const int* __restrict__ d_pos,
                                    int S, float* __restrict__ kcache, float* __restrict__ vcache) {
-  const int r = blockIdx.x;
+  const int r = blockIdx.x, hh = blockIdx.y, j = threadIdx.x;
   const int b = r / T, t = r - b * T;
   const int p = *d_pos + t;
   const int half = hd / 2;
-  const int qkv_w = (nh + 2 * nkv) * hd;
-  float* row = qkv + (int64_t)r * qkv_w;
-  const float* c = cos_t + (int64_t)p * half;
-  const float* s = sin_t + (int64_t)p * half;
-  // q and k heads: nh + nkv heads of hd, rotated in place
-  for (int i = threadIdx.x; i < (nh + nkv) * half; i += blockDim.x) {
-    const int hh = i / half, j = i - hh * half;
-    float* x = row + hh * hd;
-    const float x1 = x[j], x2 = x[j + half];
-    x[j] = __fsub_rn(__fmul_rn(x1, c[j]), __fmul_rn(x2, s[j]));
-    x[j + half] = __fadd_rn(__fmul_rn(x1, s[j]), __fmul_rn(x2, c[j]));
+  float* x = qkv + (int64_t)r * (nh + 2 * nkv) * hd + hh * hd;
+  float x1 = x[j], x2 = x[j + half];
+  if (hh < nh + nkv) {  // q and k heads rotate
+    const float c = cos_t[(int64_t)p * half + j], s = sin_t[(int64_t)p * half + j];
+    const float y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+    const float y2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+    x1 = y1;
+    x2 = y2;
+    if (hh < nh) {
+      x[j] = x1;
+      x[j + half] = x2;
+      return;
+    }
   }
-  __syncthreads();
-  const float* k = row + nh * hd;
-  const float* v = row + (nh + nkv) * hd;
-  for (int i = threadIdx.x; i < nkv * hd; i += blockDim.x) {
-    const int g = i / hd, d = i - g * hd;
-    const int64_t at = (((int64_t)b * nkv + g) * S + p) * hd + d;
-    kcache[at] = k[i];
-    vcache[at] = v[i];
-  }
+  const bool is_k = hh < nh + nkv;
+  const int g = is_k ? hh - nh : hh - nh - nkv;
+  float* dst = (is_k ? kcache : vcache) + (((int64_t)b * nkv + g) * S + p) * hd;
+  dst[j] = x1;
+  dst[j + half] = x2;
 }
 
 // ---- attention --------------------------------------------------------------
@@ -237,10 +339,38 @@ __global__ void __launch_bounds__(kMaxRep * 32)
     const int j0 = lo + c * kChunk;
     const int nj = min(kChunk, qp + 1 - j0);
     __syncthreads();
-    for (int i = threadIdx.x; i < nj * hd; i += blockDim.x) {
-      const int j = i / hd, d = i - j * hd;
-      ks[j * kpitch + d] = kbase[(int64_t)(j0 + j) * hd + d];
-      vs[j * hd + d] = vbase[(int64_t)(j0 + j) * hd + d];
+    {
+      // float4 loads, all of a thread's issued before any is stored
+      const int n4 = nj * hd / 4, hd4 = hd / 4;
+      const float4* k4 = reinterpret_cast<const float4*>(kbase + (int64_t)j0 * hd);
+      const float4* v4 = reinterpret_cast<const float4*>(vbase + (int64_t)j0 * hd);
+      constexpr int kU = kChunk * kMaxHeadDim / 4 / (kMaxRep * 32) > 8
+                             ? 8
+                             : kChunk * kMaxHeadDim / 4 / (kMaxRep * 32);
+      for (int i0 = threadIdx.x; i0 < n4; i0 += kU * blockDim.x) {
+        float4 kv[kU], vv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * blockDim.x;
+          if (i < n4) {
+            kv[u] = k4[i];
+            vv[u] = v4[i];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + u * blockDim.x;
+          if (i < n4) {
+            const int j = i / hd4, d = (i - j * hd4) * 4;
+            float* kd = ks + j * kpitch + d;
+            kd[0] = kv[u].x;
+            kd[1] = kv[u].y;
+            kd[2] = kv[u].z;
+            kd[3] = kv[u].w;
+            *reinterpret_cast<float4*>(vs + j * hd + d) = vv[u];
+          }
+        }
+      }
     }
     __syncthreads();
     if (warp < rep) {
@@ -525,12 +655,13 @@ int validate(const gb_decoder_desc* d) {
   if (d->struct_size != sizeof(gb_decoder_desc))
     return set_error(GB_ERR_INVALID_ARG, "gb_decoder_desc.struct_size %u != %zu", d->struct_size,
                      sizeof(gb_decoder_desc));
-  if (d->n_layers < 1 || d->hidden < 32 || d->hidden % 32 || d->n_heads < 1 ||
+  if (d->n_layers < 1 || d->hidden < 32 || d->hidden % 32 ||
+      d->hidden > 4 * dec::kNormVec * dec::kNormThreads || d->n_heads < 1 ||
       d->n_kv_heads < 1 || d->n_heads % d->n_kv_heads || d->n_heads / d->n_kv_heads > dec::kMaxRep)
     return set_error(GB_ERR_INVALID_ARG,
-                     "need n_layers >= 1, hidden a multiple of 32, n_heads a multiple of "
-                     "n_kv_heads with at most %d query heads per KV head",
-                     dec::kMaxRep);
+                     "need n_layers >= 1, hidden a multiple of 32 up to %d, n_heads a multiple "
+                     "of n_kv_heads with at most %d query heads per KV head",
+                     4 * dec::kNormVec * dec::kNormThreads, dec::kMaxRep);
   if (d->head_dim < 32 || d->head_dim % 32 || d->head_dim > dec::kMaxHeadDim)
     return set_error(GB_ERR_UNSUPPORTED, "head_dim %d: a multiple of 32 up to %d", d->head_dim,
                      dec::kMaxHeadDim);
@@ -684,8 +815,27 @@ int linear(Decoder& D, const float* x, int n, int K, const uint16_t* W, const vo
              "tensor-core linear launch");
     return GB_OK;
   }
-  const size_t smem = (size_t)dec::kGemvRows * K * 4;
-  DEC_CUDA(set_smem_limit(dec::linear_rows_kernel, smem), "linear kernel shared memory");
+  if (n <= dec::kGemvRows) {
+    // a warp per output row, every piece of the row requested up front
+    const size_t smem = (size_t)n * K * 4;
+    const unsigned grid = (unsigned)((n_out + dec::kGemvWarps - 1) / dec::kGemvWarps);
+    const int per_lane = (K / 8 + 31) / 32;
+    auto go = [&](auto kern) -> int {
+      DEC_CUDA(set_smem_limit(kern, (size_t)dec::kGemvRows * K * 4), "GEMV shared memory");
+      kern<<<grid, dec::kGemvWarps * 32, smem, st>>>(x, n, K, W, n_out, bias, out, out_stride,
+                                                     add ? 1 : 0);
+      DEC_CUDA(cudaGetLastError(), "GEMV launch");
+      return GB_OK;
+    };
+    if (per_lane <= 4) return go(dec::gemv_rows_kernel<4>);
+    if (per_lane <= 8) return go(dec::gemv_rows_kernel<8>);
+    if (per_lane <= 12) return go(dec::gemv_rows_kernel<12>);
+    return go(dec::gemv_rows_kernel<16>);
+  }
+  // shared memory for the rows staged at once
+  const size_t smem = (size_t)std::min(n, dec::kGemvRows) * K * 4;
+  DEC_CUDA(set_smem_limit(dec::linear_rows_kernel, (size_t)dec::kGemvRows * K * 4),
+           "linear kernel shared memory");
   const unsigned grid = (unsigned)((n_out + 2 * dec::kGemvWarps - 1) / (2 * dec::kGemvWarps));
   dec::linear_rows_kernel<<<grid, dec::kGemvWarps * 32, smem, st>>>(x, n, K, W, n_out, bias, out,
                                                                     out_stride, add ? 1 : 0);
@@ -720,16 +870,16 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
     DecLayer& L = D.layers[l];
     if (l > 0 && (rc = record(D, 2 * l, st))) return rc;
     // RMSNorm (after the previous layer's MoE residual), q/k/v, RoPE + cache
-    dec::add_rmsnorm_kernel<<<rows, 256, 0, st>>>(D.h, l ? D.moe_out : nullptr, L.attn_norm, H,
-                                                  d.rms_eps, 1, 0, D.xn);
+    dec::add_rmsnorm_kernel<<<rows, dec::kNormThreads, 0, st>>>(
+        D.h, l ? D.moe_out : nullptr, L.attn_norm, H, d.rms_eps, 1, 0, D.xn);
     DEC_CUDA(cudaGetLastError(), "norm launch");
     if ((rc = linear(D, D.xn, rows, H, L.wqkv, D.tc ? L.map_qkv : nullptr, D.qkv_w, L.bqkv, D.qkv,
                      D.qkv_w, false, st)))
       return rc;
     float* kc = D.kcache + (size_t)l * layer_kv;
     float* vc = D.vcache + (size_t)l * layer_kv;
-    dec::rope_append_kernel<<<rows, 256, 0, st>>>(D.qkv, T, nh, nkv, hd, D.rope_cos, D.rope_sin,
-                                                  D.d_pos, (int)S, kc, vc);
+    dec::rope_append_kernel<<<dim3(rows, nh + 2 * nkv), hd / 2, 0, st>>>(
+        D.qkv, T, nh, nkv, hd, D.rope_cos, D.rope_sin, D.d_pos, (int)S, kc, vc);
     DEC_CUDA(cudaGetLastError(), "RoPE launch");
     for (int r0 = 0; r0 < rows; r0 += kAttnRowsPerLaunch) {
       const int nr = std::min(kAttnRowsPerLaunch, rows - r0);
@@ -746,8 +896,8 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
     if ((rc = linear(D, D.att, rows, D.att_w, L.wo, D.tc ? L.map_o : nullptr, H, L.bo, D.h, H,
                      true, st)))
       return rc;
-    dec::add_rmsnorm_kernel<<<rows, 256, 0, st>>>(D.h, nullptr, L.post_norm, H, d.rms_eps, 1, 0,
-                                                  D.xn);
+    dec::add_rmsnorm_kernel<<<rows, dec::kNormThreads, 0, st>>>(D.h, nullptr, L.post_norm, H,
+                                                                d.rms_eps, 1, 0, D.xn);
     DEC_CUDA(cudaGetLastError(), "norm launch");
     if ((rc = record(D, 2 * l + 1, st))) return rc;
     if ((rc = gb_moe_forward(L.moe, D.xn, rows, D.moe_out, st))) return rc;
@@ -755,8 +905,8 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
   const size_t head_ev = 2 * (size_t)d.n_layers;
   if ((rc = record(D, head_ev, st))) return rc;
   // last layer's MoE residual + final norm on each sequence's last token
-  dec::add_rmsnorm_kernel<<<B, 256, 0, st>>>(D.h, D.moe_out, D.final_norm, H, d.rms_eps, T, T - 1,
-                                             D.last);
+  dec::add_rmsnorm_kernel<<<B, dec::kNormThreads, 0, st>>>(D.h, D.moe_out, D.final_norm, H,
+                                                           d.rms_eps, T, T - 1, D.last);
   DEC_CUDA(cudaGetLastError(), "final norm launch");
   if ((rc = linear(D, D.last, B, H, D.lm_head, D.tc ? D.map_lm : nullptr, d.vocab, nullptr,
                    logits, d.vocab, false, st)))
