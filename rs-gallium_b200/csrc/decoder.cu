@@ -456,47 +456,62 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, int rows, in
 
 // next[b] = the index of the largest logit of row b, the highest index among
 // equal maxima (Iterator::max_by keeps the last maximum, sampling.rs:85-92);
-// a NaN never wins.  One CTA per row; also stores the token at
-// out_tokens[b] when set.
-__global__ void argmax_kernel(const float* __restrict__ logits, int vocab,
-                              int32_t* __restrict__ next, int32_t* __restrict__ out_tokens) {
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  const int b = blockIdx.x;
+// a NaN never wins.  Grid (chunks, B): each CTA reduces kArgmaxPerThread x
+// blockDim logits to one key (the value's bits made orderable in the high
+// half, the index in the low half, so the largest key is the largest value
+// and, among equal values, the highest index), atomicMax into slot[b]; the
+// CTA that finishes last for row b publishes the token and clears the slot
+// and its ticket for the next step.
+constexpr int kArgmaxThreads = 1024;
+constexpr int kArgmaxPerThread = 8;
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+  uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);  // -0 and +0 compare equal
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (uint32_t)i;
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads)
+    argmax_kernel(const float* __restrict__ logits, int vocab,
+                  unsigned long long* __restrict__ slot, unsigned* __restrict__ ticket,
+                  int32_t* __restrict__ next, int32_t* __restrict__ out_tokens) {
+  __shared__ unsigned long long red[32];
+  __shared__ bool last;
+  const int b = blockIdx.y;
   const float* row = logits + (int64_t)b * vocab;
-  float best = -INFINITY;
-  int bi = -1;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-    const float v = row[i];
-    if (v >= best || bi < 0) {  // later indices win ties
-      if (!(v != v)) {
-        best = v;
-        bi = i;
-      }
-    }
+  const int base = blockIdx.x * kArgmaxThreads * kArgmaxPerThread + threadIdx.x;
+  float v[kArgmaxPerThread];
+#pragma unroll
+  for (int j = 0; j < kArgmaxPerThread; ++j) {
+    const int i = base + j * kArgmaxThreads;
+    v[j] = i < vocab ? row[i] : __int_as_float(0x7fc00000);  // NaN: skipped
   }
+  unsigned long long best = 0;
+#pragma unroll
+  for (int j = 0; j < kArgmaxPerThread; ++j)
+    if (!(v[j] != v[j])) {
+      const unsigned long long k = argmax_key(v[j], base + j * kArgmaxThreads);
+      best = k > best ? k : best;
+    }
 #pragma unroll
   for (int o = 16; o >= 1; o >>= 1) {
-    const float ov = __shfl_xor_sync(kFullMask, best, o);
-    const int oi = __shfl_xor_sync(kFullMask, bi, o);
-    if (oi >= 0 && (bi < 0 || ov > best || (ov == best && oi > bi))) {
-      best = ov;
-      bi = oi;
-    }
+    const unsigned long long other = __shfl_xor_sync(kFullMask, best, o);
+    best = other > best ? other : best;
   }
-  if ((threadIdx.x & 31) == 0) {
-    sv[threadIdx.x >> 5] = best;
-    si[threadIdx.x >> 5] = bi;
-  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) {
-      if (si[w] >= 0 && (bi < 0 || sv[w] > best || (sv[w] == best && si[w] > bi))) {
-        best = sv[w];
-        bi = si[w];
-      }
-    }
-    const int tok = bi < 0 ? 0 : bi;
+    for (int w = 1; w < kArgmaxThreads / 32; ++w) best = red[w] > best ? red[w] : best;
+    if (best) atomicMax(&slot[b], best);
+    __threadfence();
+    last = atomicAdd(&ticket[b], 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (last && threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long k = atomicExch(&slot[b], 0ull);
+    ticket[b] = 0;
+    const int tok = (int)(uint32_t)(k & 0xffffffffull);  // 0 when every logit was NaN
     next[b] = tok;
     if (out_tokens) out_tokens[b] = tok;
   }
@@ -559,6 +574,8 @@ struct Decoder {
   float *last = nullptr, *logits = nullptr, *part = nullptr;
   __nv_bfloat16 *xh = nullptr, *xl = nullptr;  // [rows_cap][max(H, nh hd)]
   int32_t *next = nullptr, *tok_buf = nullptr, *d_pos = nullptr, *err = nullptr;
+  unsigned long long* am_slot = nullptr;  // [max_batch] greedy-token reduction, zero between steps
+  unsigned* am_ticket = nullptr;          // [max_batch]
   alignas(64) unsigned char map_xh_h[128] = {};  // split activations, K = H
   alignas(64) unsigned char map_xl_h[128] = {};
   alignas(64) unsigned char map_xh_a[128] = {};  // K = nh hd
@@ -781,6 +798,8 @@ int alloc_activations(Decoder& D) {
       {(void**)&D.tok_buf, B * 4},
       {(void**)&D.d_pos, 4},
       {(void**)&D.err, 4},
+      {(void**)&D.am_slot, B * 8},
+      {(void**)&D.am_ticket, B * 4},
   };
   size_t total = 0;
   for (const Piece& p : pieces) total += (p.bytes + 255) & ~(size_t)255;
@@ -792,6 +811,8 @@ int alloc_activations(Decoder& D) {
     at += (p.bytes + 255) & ~(size_t)255;
   }
   DEC_CUDA(cudaMemset(D.err, 0, 4), "decoder error word");
+  DEC_CUDA(cudaMemset(D.am_slot, 0, B * 8), "greedy-token slots");
+  DEC_CUDA(cudaMemset(D.am_ticket, 0, B * 4), "greedy-token tickets");
   if (D.tc) {
     DEC_CUDA(make_bf16_map(D.map_xh_h, D.xh, H, R, kLinearBoxRows), "activation map");
     DEC_CUDA(make_bf16_map(D.map_xl_h, D.xl, H, R, kLinearBoxRows), "activation map");
@@ -911,7 +932,11 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
   if ((rc = linear(D, D.last, B, H, D.lm_head, D.tc ? D.map_lm : nullptr, d.vocab, nullptr,
                    logits, d.vocab, false, st)))
     return rc;
-  dec::argmax_kernel<<<B, 1024, 0, st>>>(logits, d.vocab, next, out_tokens);
+  {
+    const int per_cta = dec::kArgmaxThreads * dec::kArgmaxPerThread;
+    dec::argmax_kernel<<<dim3((d.vocab + per_cta - 1) / per_cta, B), dec::kArgmaxThreads, 0, st>>>(
+        logits, d.vocab, D.am_slot, D.am_ticket, next, out_tokens);
+  }
   DEC_CUDA(cudaGetLastError(), "greedy token launch");
   return record(D, head_ev + 1, st);
 }

@@ -60,6 +60,14 @@ __device__ __forceinline__ float half_bits_to_f32(uint16_t h) {
   return __half2float(*reinterpret_cast<const __half*>(&h));
 }
 
+// 1 + q / 16 as an f32 (exact) for the nibble q at bit `lo` of `word`: the
+// nibble becomes the top four mantissa bits of 1.0.  Two integer operations,
+// where an int-to-float conversion is a quarter-rate instruction.
+__device__ __forceinline__ float nibble_float(uint32_t word, int lo) {
+  const uint32_t m = lo <= 19 ? (word << (19 - lo)) : (word >> (lo - 19));
+  return __uint_as_float((m & (0xFu << 19)) | 0x3F800000u);
+}
+
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
   return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
@@ -71,7 +79,9 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int i) {
 // once.  TT tokens are staged in shared memory with their 32-element sums;
 // a task adds d1 * sum(x q) - m1 * sum(x) per sub-block for the two rows of
 // a pair and every staged token, each nibble converted once for all tokens;
-// a butterfly folds the lanes.
+// a butterfly folds the lanes.  The nibbles enter the products as
+// 1 + q / 16 (nibble_float) and the sub-block's x sum takes the offset out:
+// sum x q = 16 (sum x (1 + q / 16) - sum x).
 template <int MODE, int TT, int PAIRS>
 __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
   extern __shared__ float qsm[];
@@ -186,8 +196,8 @@ __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
             const uint32_t word = w < 4 ? word_of(qa[r], w) : word_of(qb[r], w - 4);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              qv[r][0][i] = (float)((word >> (8 * i)) & 0xF);
-              qv[r][1][i] = (float)((word >> (8 * i + 4)) & 0xF);
+              qv[r][0][i] = nibble_float(word, 8 * i);
+              qv[r][1][i] = nibble_float(word, 8 * i + 4);
             }
           }
 #pragma unroll
@@ -212,8 +222,11 @@ __global__ void __launch_bounds__(kQWarps * 32) q4k_rows_kernel(const QArgs a) {
           const float xa = xsum[t * NB + 2 * c], xb = xsum[t * NB + 2 * c + 1];
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
-            const float pa = __fsub_rn(__fmul_rn(d1[r][0], s[r][0][t]), __fmul_rn(m1[r][0], xa));
-            const float pb = __fsub_rn(__fmul_rn(d1[r][1], s[r][1][t]), __fmul_rn(m1[r][1], xb));
+            // s = sum x (1 + q / 16) = sum x + (sum x q) / 16
+            const float sqa = __fmul_rn(16.0f, __fsub_rn(s[r][0][t], xa));
+            const float sqb = __fmul_rn(16.0f, __fsub_rn(s[r][1][t], xb));
+            const float pa = __fsub_rn(__fmul_rn(d1[r][0], sqa), __fmul_rn(m1[r][0], xa));
+            const float pb = __fsub_rn(__fmul_rn(d1[r][1], sqb), __fmul_rn(m1[r][1], xb));
             acc[r][t] = __fadd_rn(acc[r][t], __fadd_rn(pa, pb));
           }
         }
@@ -253,15 +266,17 @@ cudaError_t launch_q_shape(const Groups& g, const QArgs& a, cudaStream_t st) {
 }
 
 // Tokens staged per pass from the mean rows per local expert (an expert with
-// more rows takes several passes over its weights, from L2); each warp owns
-// four row pairs, so that a staged token serves 64 rows.
+// more rows takes several passes over its weights, from L2).  From three rows
+// per expert each warp owns four row pairs, so that a staged token serves 64
+// rows; at one or two, a warp owns one pair (four times the CTAs, and no warp
+// waits for one pair's bytes after another's).
 template <int MODE>
 cudaError_t launch_q(const Moe& m, const Groups& g, const QArgs& a, cudaStream_t st) {
   if (g.max_active <= 0) return cudaSuccess;
   const int64_t nloc = std::max(1, m.e_end - m.e_begin);
   const int64_t mean = (g.rows + nloc - 1) / nloc;
-  if (mean <= 1) return launch_q_shape<MODE, 1, 4>(g, a, st);
-  if (mean <= 2) return launch_q_shape<MODE, 2, 4>(g, a, st);
+  if (mean <= 1) return launch_q_shape<MODE, 1, 1>(g, a, st);
+  if (mean <= 2) return launch_q_shape<MODE, 2, 1>(g, a, st);
   if (mean <= 4) return launch_q_shape<MODE, 4, 4>(g, a, st);
   return launch_q_shape<MODE, 8, 4>(g, a, st);
 }

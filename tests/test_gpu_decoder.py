@@ -119,3 +119,19 @@ def test_argument_checks():
         with pytest.raises(GalliumError) as e:
             m.forward(bad, 0)
         assert e.value.status == _lib.GB_ERR_INVALID_ARG
+
+
+def test_greedy_token_ties_go_to_the_highest_id():
+    """The greedy-token reduction on planted ties: an LM head whose rows are
+    all equal gives equal logits, and an all-zero one gives +0 everywhere;
+    either way the highest token id wins (sampling.rs:85-92)."""
+    import torch
+
+    w = _weights(seed=11, layers=1)
+    toks = np.array([[3, 4, 5], [7, 8, 9]], np.int32)
+    for head in (np.repeat(w.lm_head[17:18], w.vocab, axis=0), np.zeros_like(w.lm_head)):
+        w.lm_head = np.ascontiguousarray(head)
+        with GptOssQ.load(w, device=0, max_batch=2, max_tokens=3, max_seq_len=8) as m:
+            got = m.forward(torch.from_numpy(toks).cuda(), 0).cpu().numpy()
+            assert (got == got[:, :1]).all()
+            assert list(m.last_next.cpu().numpy()) == [w.vocab - 1, w.vocab - 1]
