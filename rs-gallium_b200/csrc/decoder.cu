@@ -75,7 +75,13 @@ __global__ void __launch_bounds__(kNormThreads)
   float4* x4 = reinterpret_cast<float4*>(h + src);
   const float4* d4 = delta ? reinterpret_cast<const float4*>(delta + src) : nullptr;
   const int n4 = H / 4;
-  float4 v[kNormVec];
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 v[kNormVec], wv[kNormVec];
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {  // the weights with the row, not after the reduction
+    const int i = threadIdx.x + j * kNormThreads;
+    wv[j] = i < n4 ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
 #pragma unroll
   for (int j = 0; j < kNormVec; ++j) {
     const int i = threadIdx.x + j * kNormThreads;
@@ -113,18 +119,15 @@ __global__ void __launch_bounds__(kNormThreads)
   }
   __syncthreads();
   const float m = sqrtf(__fadd_rn(__fdiv_rn(red[0], (float)H), eps));
-  const float4* w4 = reinterpret_cast<const float4*>(w);
   float4* o4 = reinterpret_cast<float4*>(out + (int64_t)r * H);
 #pragma unroll
   for (int j = 0; j < kNormVec; ++j) {
     const int i = threadIdx.x + j * kNormThreads;
-    if (i < n4) {
-      const float4 wv = w4[i];
-      o4[i] = make_float4(__fmul_rn(__fdiv_rn(v[j].x, m), wv.x),
-                          __fmul_rn(__fdiv_rn(v[j].y, m), wv.y),
-                          __fmul_rn(__fdiv_rn(v[j].z, m), wv.z),
-                          __fmul_rn(__fdiv_rn(v[j].w, m), wv.w));
-    }
+    if (i < n4)
+      o4[i] = make_float4(__fmul_rn(__fdiv_rn(v[j].x, m), wv[j].x),
+                          __fmul_rn(__fdiv_rn(v[j].y, m), wv[j].y),
+                          __fmul_rn(__fdiv_rn(v[j].z, m), wv[j].z),
+                          __fmul_rn(__fdiv_rn(v[j].w, m), wv[j].w));
   }
 }
 
@@ -532,6 +535,7 @@ namespace gb {
 namespace {
 
 constexpr int kTcMinRows = 16;     // linear layers with this many rows use the tensor cores
+constexpr int64_t kLinearPartFloats = int64_t(4) << 20;  // split-K partial sums (16 MB)
 constexpr int kAttnRowsPerLaunch = 256;  // query rows per attention launch (partials buffer)
 
 struct DecLayer {
@@ -572,6 +576,7 @@ struct Decoder {
   void* act_base = nullptr;     // one allocation for the buffers below
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *moe_out = nullptr;
   float *last = nullptr, *logits = nullptr, *part = nullptr;
+  float* lin_part = nullptr;  // [kLinearPartFloats] split-K partials of the linear layers
   __nv_bfloat16 *xh = nullptr, *xl = nullptr;  // [rows_cap][max(H, nh hd)]
   int32_t *next = nullptr, *tok_buf = nullptr, *d_pos = nullptr, *err = nullptr;
   unsigned long long* am_slot = nullptr;  // [max_batch] greedy-token reduction, zero between steps
@@ -794,6 +799,7 @@ int alloc_activations(Decoder& D) {
       {(void**)&D.part, attn_rows * d.n_heads * dec::kSlots * (d.head_dim + 2) * 4},
       {(void**)&D.xh, D.tc ? R * kmax * 2 : 0},
       {(void**)&D.xl, D.tc ? R * kmax * 2 : 0},
+      {(void**)&D.lin_part, D.tc ? (size_t)kLinearPartFloats * 4 : 0},
       {(void**)&D.next, B * 4},
       {(void**)&D.tok_buf, B * 4},
       {(void**)&D.d_pos, 4},
@@ -832,7 +838,7 @@ int linear(Decoder& D, const float* x, int n, int K, const uint16_t* W, const vo
     DEC_CUDA(split_rows(x, nullptr, 1, K, n, D.xh, D.xl, st), "split activations");
     DEC_CUDA(launch_linear_tc(D.sm_count, map_w, kh ? D.map_xh_h : D.map_xh_a,
                               kh ? D.map_xl_h : D.map_xl_a, K, n_out, n, bias, out, out_stride,
-                              add, D.err, st),
+                              add, D.err, D.lin_part, kLinearPartFloats, st),
              "tensor-core linear launch");
     return GB_OK;
   }

@@ -28,6 +28,7 @@
 // abort flag, records an error bit, lets in-flight copies and MMAs finish,
 // frees its TMEM and returns.
 #include <cuda.h>
+#include <algorithm>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -67,6 +68,8 @@ struct Args {
   int out_stride;
   const float* bias;         // DOWN: + bias[row] (nullable)
   int add_out;               // DOWN: y = y + (acc + bias) instead of y = acc + bias
+  int ksplit;                // uniform DOWN only: K split into ksplit ranges (1 = none)
+  float* part;               // ksplit > 1: raw sums [ksplit][uniform_rows][rows]
   int* err;                  // error flags (bit 1: wait timed out)
   uint64_t wait_ns;          // bound of every mbarrier wait
 };
@@ -89,7 +92,7 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
 }
 
 struct Item {
-  int le, m_tile, row0, nrows;
+  int le, m_tile, row0, nrows, ks, k0, k1;  // k0 .. k1: the item's K steps
 };
 
 __device__ __forceinline__ int n_tiles(const Args& a) {
@@ -98,6 +101,11 @@ __device__ __forceinline__ int n_tiles(const Args& a) {
 
 __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   Item it;
+  const int nk = a.K / BK;
+  it.ks = item % a.ksplit;
+  item /= a.ksplit;
+  it.k0 = it.ks * nk / a.ksplit;
+  it.k1 = (it.ks + 1) * nk / a.ksplit;
   const int j = item / a.m_tiles;
   it.m_tile = item - j * a.m_tiles;
   if (a.tile_expert) {
@@ -145,6 +153,8 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
           a.out_hi[o] = hi;
           a.out_lo[o] = lo;
         }
+      } else if (valid && n < it.nrows && a.ksplit > 1) {
+        a.part[((int64_t)it.ks * a.uniform_rows + pos) * a.rows + row] = val;
       } else if (valid && n < it.nrows) {
         const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
         float* o = a.out_y + orow * a.out_stride + row;
@@ -172,8 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_items = n_tiles(a) * a.m_tiles;
-  const int nk = a.K / BK;
+  const int total_items = n_tiles(a) * a.m_tiles * a.ksplit;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -202,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
         const Item it = decode_item(a, item);
         const int wrow = it.le * a.rows + it.m_tile * BM;
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int kc = it.k0; kc < it.k1; ++kc) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, a.wait_ns)) {
             ok = false;
             break;
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_hi = tmem_base + (uint32_t)(b * 2 * BN);
         const uint32_t d_lo = d_hi + (uint32_t)BN;
-        for (int kc = 0; kc < nk; ++kc) {
+        for (int kc = it.k0; kc < it.k1; ++kc) {
           if (!mbar_wait(&full[stage], phase, abort_flag, a.err, a.wait_ns)) {
             ok = false;
             break;
@@ -255,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             const uint64_t da = sw128_desc(sa + kk * 32);
-            const uint32_t acc = (kc | kk) != 0;
+            const uint32_t acc = (kc != it.k0 || kk != 0) ? 1u : 0u;
             mma_bf16(d_hi, da, sw128_desc(sh + kk * 32), idesc, acc);
             mma_bf16(d_lo, da, sw128_desc(sl + kk * 32), idesc, acc);
           }
@@ -327,6 +336,23 @@ __global__ void split_bf16_kernel(const float* __restrict__ x, const int32_t* __
   }
 }
 
+// out[p][r] = (add_out ? out[p][r] : 0) + ((sum over s of part[s][p][r], s
+// ascending) + bias[r]): the split-K sums of the plain-GEMM form, folded in
+// one fixed order.
+__global__ void split_reduce_kernel(const float* __restrict__ part, int ksplit, int n_pos,
+                                    int rows, const float* __restrict__ bias, float* __restrict__ out,
+                                    int out_stride, int add_out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)n_pos * rows) return;
+  const int p = (int)(i / rows), r = (int)(i - (int64_t)p * rows);
+  float v = part[i];
+  for (int s = 1; s < ksplit; ++s) v = __fadd_rn(v, part[(int64_t)s * n_pos * rows + i]);
+  if (bias) v = __fadd_rn(v, bias[r]);
+  float* o = out + (int64_t)p * out_stride + r;
+  if (add_out) v = __fadd_rn(*o, v);
+  *o = v;
+}
+
 }  // namespace dtc
 
 // bf16 [rows][K] row-major, one box = box_rows rows x 64 elements, 128-byte
@@ -362,6 +388,7 @@ cudaError_t launch_gemm(int sm_count, const dtc::Args& a, const void* map_w, con
 
 dtc::Args base_args(const Moe& m, int* err) {
   dtc::Args a{};
+  a.ksplit = 1;
   a.e_begin = m.e_begin;
   a.act_kind = m.desc.act_kind;
   a.clamp = m.desc.act_clamp;
@@ -382,8 +409,8 @@ cudaError_t split_rows(const float* x, const int32_t* perm, int perm_div, int H,
 
 cudaError_t launch_linear_tc(int sm_count, const void* map_w, const void* map_xh,
                              const void* map_xl, int K, int rows, int n_pos, const float* bias,
-                             float* out, int out_stride, bool add_out, int* err,
-                             cudaStream_t st) {
+                             float* out, int out_stride, bool add_out, int* err, float* part,
+                             int64_t part_floats, cudaStream_t st) {
   if (n_pos <= 0) return cudaSuccess;
   dtc::Args a{};
   a.err = err;
@@ -396,7 +423,22 @@ cudaError_t launch_linear_tc(int sm_count, const void* map_w, const void* map_xh
   a.out_stride = out_stride;
   a.bias = bias;
   a.add_out = add_out ? 1 : 0;
-  return launch_gemm<dtc::DOWN>(sm_count, a, map_w, map_xh, map_xl, st);
+  // split K when the tiles alone would leave SMs idle: up to one item per
+  // SM, at least four K steps per item, as the partial buffer allows
+  const int tiles = a.m_tiles * ((n_pos + dtc::BN - 1) / dtc::BN);
+  int ks = std::min((sm_count + tiles - 1) / tiles, std::max(1, (K / dtc::BK) / 4));
+  if (part && part_floats > 0)
+    ks = (int)std::min<int64_t>(ks, part_floats / ((int64_t)n_pos * rows));
+  else
+    ks = 1;
+  a.ksplit = std::max(1, ks);
+  a.part = part;
+  cudaError_t e = launch_gemm<dtc::DOWN>(sm_count, a, map_w, map_xh, map_xl, st);
+  if (e != cudaSuccess || a.ksplit == 1) return e;
+  const int64_t n = (int64_t)n_pos * rows;
+  dtc::split_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+      part, a.ksplit, n_pos, rows, bias, out, out_stride, add_out ? 1 : 0);
+  return cudaGetLastError();
 }
 
 bool dense_tc_supported(const Moe& m) {

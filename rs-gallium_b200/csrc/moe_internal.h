@@ -404,10 +404,13 @@ cudaError_t split_rows(const float* x, const int32_t* perm, int perm_div, int H,
                        __nv_bfloat16* xh, __nv_bfloat16* xl, cudaStream_t st);
 // out[p][r] = (add_out ? out[p][r] : 0) + (W[r] . x[p] + bias[r]) for p < n_pos,
 // r < rows: map_w of W [rows][K], map_xh / map_xl of the split activations.
+// When the tiles would leave SMs idle, K is split and the partial sums (in
+// `part`, up to part_floats floats) are folded in a fixed order by a second
+// kernel.
 cudaError_t launch_linear_tc(int sm_count, const void* map_w, const void* map_xh,
                              const void* map_xl, int K, int rows, int n_pos, const float* bias,
-                             float* out, int out_stride, bool add_out, int* err,
-                             cudaStream_t st);
+                             float* out, int out_stride, bool add_out, int* err, float* part,
+                             int64_t part_floats, cudaStream_t st);
 cudaError_t launch_dequant_expert(const Moe& m, int which, int local_expert, float* out,
                                   cudaStream_t st);
 cudaError_t launch_gguf_to_split(const uint8_t* raw_dev, int64_t rows, int k, uint8_t* blocks_dev,
