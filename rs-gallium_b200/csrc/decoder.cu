@@ -65,10 +65,20 @@ __global__ void embed_kernel(const int32_t* __restrict__ tokens, const uint16_t*
 // and every load is issued before the first is used (H <= 4 * 4 * 1024).
 constexpr int kNormThreads = 1024;
 constexpr int kNormVec = 4;  // float4s per thread
+// oh / ol (nullable): the output also as bf16 hi / lo (hi = bf16(v),
+// lo = bf16(v - hi)), the input a tensor-core linear layer takes.
+__device__ __forceinline__ void split_store(__nv_bfloat16* oh, __nv_bfloat16* ol, int64_t i,
+                                            float v) {
+  const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+  oh[i] = hi;
+  ol[i] = __float2bfloat16_rn(__fsub_rn(v, __bfloat162float(hi)));
+}
+
 __global__ void __launch_bounds__(kNormThreads)
     add_rmsnorm_kernel(float* __restrict__ h, const float* __restrict__ delta,
                        const float* __restrict__ w, int H, float eps, int src_stride, int src_off,
-                       float* __restrict__ out) {
+                       float* __restrict__ out, __nv_bfloat16* __restrict__ oh,
+                       __nv_bfloat16* __restrict__ ol) {
   __shared__ float red[32];
   const int r = blockIdx.x;
   const int64_t src = (int64_t)(r * src_stride + src_off) * H;
@@ -123,11 +133,20 @@ __global__ void __launch_bounds__(kNormThreads)
 #pragma unroll
   for (int j = 0; j < kNormVec; ++j) {
     const int i = threadIdx.x + j * kNormThreads;
-    if (i < n4)
-      o4[i] = make_float4(__fmul_rn(__fdiv_rn(v[j].x, m), wv[j].x),
-                          __fmul_rn(__fdiv_rn(v[j].y, m), wv[j].y),
-                          __fmul_rn(__fdiv_rn(v[j].z, m), wv[j].z),
-                          __fmul_rn(__fdiv_rn(v[j].w, m), wv[j].w));
+    if (i < n4) {
+      const float4 y = make_float4(__fmul_rn(__fdiv_rn(v[j].x, m), wv[j].x),
+                                   __fmul_rn(__fdiv_rn(v[j].y, m), wv[j].y),
+                                   __fmul_rn(__fdiv_rn(v[j].z, m), wv[j].z),
+                                   __fmul_rn(__fdiv_rn(v[j].w, m), wv[j].w));
+      o4[i] = y;
+      if (oh) {
+        const int64_t b = (int64_t)r * H + 4 * i;
+        split_store(oh, ol, b, y.x);
+        split_store(oh, ol, b + 1, y.y);
+        split_store(oh, ol, b + 2, y.z);
+        split_store(oh, ol, b + 3, y.w);
+      }
+    }
   }
 }
 
@@ -304,8 +323,9 @@ __global__ void rope_append_kernel(float* __restrict__ qkv, int T, int nh, int n
 // query head of the group (warp w = head g * rep + w): scores (q . k) * scale
 // over the visible keys (causal; the last `window` positions on sliding
 // layers), a running max and sum, and sum_j p_j v_j.  The visible keys are
-// split into kChunk-key chunks; CTA slot c takes chunks c, c + kSlots, ...
-// and writes (max, sum, acc[hd]) for its chunks.  Keys and values of a chunk
+// split into kChunk-key chunks; CTA slot c of gridDim.x (at most kSlots)
+// takes chunks c, c + gridDim.x, ... and writes (max, sum, acc[hd]) for its
+// chunks.  Keys and values of a chunk
 // are staged in shared memory once for the group.
 // Query rows row0 + blockIdx.z; partials indexed by blockIdx.z.
 __global__ void __launch_bounds__(kMaxRep * 32)
@@ -338,7 +358,7 @@ __global__ void __launch_bounds__(kMaxRep * 32)
 #pragma unroll
   for (int i = 0; i < kMaxHeadDim / 32; ++i) acc[i] = 0.0f;
   const int dpl = hd / 32;  // dims per lane (hd a multiple of 32)
-  for (int c = slot; c < nchunks; c += kSlots) {
+  for (int c = slot; c < nchunks; c += gridDim.x) {
     const int j0 = lo + c * kChunk;
     const int nj = min(kChunk, qp + 1 - j0);
     __syncthreads();
@@ -428,30 +448,35 @@ __global__ void __launch_bounds__(kMaxRep * 32)
 // Merges the slots of each (row, head) with the head's sink logit
 // (gpt_oss_q.rs:92-101: softmax over the scores and the sink, the sink's
 // column dropped): out = sum_c acc_c e^(m_c - M) / (e^(sink - M) + sum_c s_c
-// e^(m_c - M)), M the largest of the sink and the slots' maxima.  One warp
-// per (row, head); partial row i is output row row0 + i.
+// e^(m_c - M)), M the largest of the sink and the slots' maxima (the first
+// nslots slots are used).  One warp per (row, head); partial row i is output
+// row row0 + i.
 __global__ void attn_combine_kernel(const float* __restrict__ part, int rows, int row0, int nh,
-                                    int hd, const float* __restrict__ sinks,
-                                    float* __restrict__ out) {
+                                    int hd, int nslots, const float* __restrict__ sinks,
+                                    float* __restrict__ out, __nv_bfloat16* __restrict__ oh,
+                                    __nv_bfloat16* __restrict__ ol) {
   const int wid = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (wid >= rows * nh) return;
   const int r = row0 + wid / nh, hq = wid % nh;
   const float* pp = part + (int64_t)wid * kSlots * (hd + 2);
   const float sink = sinks[hq];
   float M = sink;
-  for (int c = 0; c < kSlots; ++c) M = fmaxf(M, pp[c * (hd + 2)]);
+  for (int c = 0; c < nslots; ++c) M = fmaxf(M, pp[c * (hd + 2)]);
   float S = exp_f32(__fsub_rn(sink, M));
   float f[kSlots];
-  for (int c = 0; c < kSlots; ++c) {
+  for (int c = 0; c < nslots; ++c) {
     const float mc = pp[c * (hd + 2)];
     f[c] = mc == -INFINITY ? 0.0f : exp_f32(__fsub_rn(mc, M));
     S = __fadd_rn(S, __fmul_rn(pp[c * (hd + 2) + 1], f[c]));
   }
   for (int d = lane; d < hd; d += 32) {
     float a = 0.0f;
-    for (int c = 0; c < kSlots; ++c)
+    for (int c = 0; c < nslots; ++c)
       if (f[c] != 0.0f) a = __fmaf_rn(pp[c * (hd + 2) + 2 + d], f[c], a);
-    out[(int64_t)r * nh * hd + hq * hd + d] = __fdiv_rn(a, S);
+    const int64_t o = (int64_t)r * nh * hd + hq * hd + d;
+    const float y = __fdiv_rn(a, S);
+    out[o] = y;
+    if (oh) split_store(oh, ol, o, y);
   }
 }
 
@@ -830,12 +855,19 @@ int alloc_activations(Decoder& D) {
 
 // out[p] (+)= W x[p] + bias for p < n: the tensor cores from kTcMinRows rows,
 // else the CUDA-core kernel.
+// Whether a linear layer of n rows runs on the tensor cores (its input then
+// needs the bf16 hi / lo copies in D.xh / D.xl).
+bool linear_tc(const Decoder& D, int n) { return D.tc && n >= kTcMinRows; }
+
+// presplit: the producer of x already wrote its hi / lo copies.
 int linear(Decoder& D, const float* x, int n, int K, const uint16_t* W, const void* map_w,
-           int n_out, const float* bias, float* out, int out_stride, bool add, cudaStream_t st) {
+           int n_out, const float* bias, float* out, int out_stride, bool add, cudaStream_t st,
+           bool presplit = false) {
   if (n <= 0) return GB_OK;
   if (D.tc && map_w && n >= kTcMinRows) {
     const bool kh = K == D.d.hidden;
-    DEC_CUDA(split_rows(x, nullptr, 1, K, n, D.xh, D.xl, st), "split activations");
+    if (!presplit)
+      DEC_CUDA(split_rows(x, nullptr, 1, K, n, D.xh, D.xl, st), "split activations");
     DEC_CUDA(launch_linear_tc(D.sm_count, map_w, kh ? D.map_xh_h : D.map_xh_a,
                               kh ? D.map_xl_h : D.map_xl_a, K, n_out, n, bias, out, out_stride,
                               add, D.err, D.lin_part, kLinearPartFloats, st),
@@ -897,34 +929,40 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
     DecLayer& L = D.layers[l];
     if (l > 0 && (rc = record(D, 2 * l, st))) return rc;
     // RMSNorm (after the previous layer's MoE residual), q/k/v, RoPE + cache
+    const bool split = linear_tc(D, rows);  // producers write the hi / lo copies
     dec::add_rmsnorm_kernel<<<rows, dec::kNormThreads, 0, st>>>(
-        D.h, l ? D.moe_out : nullptr, L.attn_norm, H, d.rms_eps, 1, 0, D.xn);
+        D.h, l ? D.moe_out : nullptr, L.attn_norm, H, d.rms_eps, 1, 0, D.xn,
+        split ? D.xh : nullptr, split ? D.xl : nullptr);
     DEC_CUDA(cudaGetLastError(), "norm launch");
     if ((rc = linear(D, D.xn, rows, H, L.wqkv, D.tc ? L.map_qkv : nullptr, D.qkv_w, L.bqkv, D.qkv,
-                     D.qkv_w, false, st)))
+                     D.qkv_w, false, st, split)))
       return rc;
     float* kc = D.kcache + (size_t)l * layer_kv;
     float* vc = D.vcache + (size_t)l * layer_kv;
     dec::rope_append_kernel<<<dim3(rows, nh + 2 * nkv), hd / 2, 0, st>>>(
         D.qkv, T, nh, nkv, hd, D.rope_cos, D.rope_sin, D.d_pos, (int)S, kc, vc);
     DEC_CUDA(cudaGetLastError(), "RoPE launch");
+    // key slots per query: every slot for a lone row; from 16 rows the rows
+    // fill the GPU and two slots keep CTAs busy with several chunks each
+    const int slots = rows >= 16 ? 2 : rows >= 4 ? 4 : dec::kSlots;
     for (int r0 = 0; r0 < rows; r0 += kAttnRowsPerLaunch) {
       const int nr = std::min(kAttnRowsPerLaunch, rows - r0);
-      dec::attn_partial_kernel<<<dim3(dec::kSlots, nkv, nr), rep * 32, attn_smem, st>>>(
+      dec::attn_partial_kernel<<<dim3(slots, nkv, nr), rep * 32, attn_smem, st>>>(
           D.qkv, r0, T, nh, nkv, hd, D.d_pos, L.sliding, d.sliding_window, scale, (int)S, kc, vc,
           D.part);
       DEC_CUDA(cudaGetLastError(), "attention launch");
       const int warps = nr * nh;
-      dec::attn_combine_kernel<<<(warps + 7) / 8, 256, 0, st>>>(D.part, nr, r0, nh, hd, L.sinks,
-                                                                D.att);
+      dec::attn_combine_kernel<<<(warps + 7) / 8, 256, 0, st>>>(
+          D.part, nr, r0, nh, hd, slots, L.sinks, D.att, split ? D.xh : nullptr,
+          split ? D.xl : nullptr);
       DEC_CUDA(cudaGetLastError(), "attention combine launch");
     }
     // o projection + residual, RMSNorm, MoE block (its residual joins the next norm)
     if ((rc = linear(D, D.att, rows, D.att_w, L.wo, D.tc ? L.map_o : nullptr, H, L.bo, D.h, H,
-                     true, st)))
+                     true, st, split)))
       return rc;
-    dec::add_rmsnorm_kernel<<<rows, dec::kNormThreads, 0, st>>>(D.h, nullptr, L.post_norm, H,
-                                                                d.rms_eps, 1, 0, D.xn);
+    dec::add_rmsnorm_kernel<<<rows, dec::kNormThreads, 0, st>>>(
+        D.h, nullptr, L.post_norm, H, d.rms_eps, 1, 0, D.xn, nullptr, nullptr);
     DEC_CUDA(cudaGetLastError(), "norm launch");
     if ((rc = record(D, 2 * l + 1, st))) return rc;
     if ((rc = gb_moe_forward(L.moe, D.xn, rows, D.moe_out, st))) return rc;
@@ -932,11 +970,13 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
   const size_t head_ev = 2 * (size_t)d.n_layers;
   if ((rc = record(D, head_ev, st))) return rc;
   // last layer's MoE residual + final norm on each sequence's last token
-  dec::add_rmsnorm_kernel<<<B, dec::kNormThreads, 0, st>>>(D.h, D.moe_out, D.final_norm, H,
-                                                           d.rms_eps, T, T - 1, D.last);
+  const bool split_head = linear_tc(D, B);
+  dec::add_rmsnorm_kernel<<<B, dec::kNormThreads, 0, st>>>(
+      D.h, D.moe_out, D.final_norm, H, d.rms_eps, T, T - 1, D.last,
+      split_head ? D.xh : nullptr, split_head ? D.xl : nullptr);
   DEC_CUDA(cudaGetLastError(), "final norm launch");
   if ((rc = linear(D, D.last, B, H, D.lm_head, D.tc ? D.map_lm : nullptr, d.vocab, nullptr,
-                   logits, d.vocab, false, st)))
+                   logits, d.vocab, false, st, split_head)))
     return rc;
   {
     const int per_cta = dec::kArgmaxThreads * dec::kArgmaxPerThread;

@@ -826,8 +826,11 @@ __global__ void __launch_bounds__(128) split_pieces_kernel(
 // its entries and the pieces of x[t] at each of its positions.
 constexpr int kGroupEntries = kMxGroupEntries;
 constexpr int kGroupExperts = 256;
+// Threads of the grouping kernel: its pass over the token's row (max, then
+// the pieces) takes two float4 per thread at H = 2880 instead of six.
+constexpr int kGroupThreads = 512;
 
-__global__ void __launch_bounds__(128) group_pieces_kernel(
+__global__ void __launch_bounds__(kGroupThreads) group_pieces_kernel(
     const float* __restrict__ x, const int32_t* __restrict__ idx, int T, int E, int topk,
     int H, int e_begin, int e_end, int bn, int32_t* __restrict__ counts,
     int32_t* __restrict__ offsets, int32_t* __restrict__ active, int32_t* __restrict__ meta,
@@ -926,8 +929,8 @@ __global__ void __launch_bounds__(128) group_pieces_kernel(
     for (int i = tid; i < s_tiles * ready_per_tile; i += blockDim.x) ready[i] = 0;
     if (tid == 0) *next_item = 0;
   }
-  // positions of this token's entries: warp w takes rank w, w + 4, ...
-  for (int r = warp; r < topk; r += 4) {
+  // positions of this token's entries: warp w takes rank w, w + nwarps, ...
+  for (int r = warp; r < topk; r += (int)(blockDim.x >> 5)) {
     const int i = t * topk + r;
     const int e = s_idx[i];
     int before = 0;
@@ -1243,7 +1246,7 @@ bool mx_group_fits(const Moe& m, int64_t T) {
 cudaError_t launch_mx_group(const Moe& m, const float* x, int64_t T, Workspace& ws, int kind,
                             cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
-  return launch_pdl(mx::group_pieces_kernel, dim3((unsigned)T), dim3(128), 0, st, x,
+  return launch_pdl(mx::group_pieces_kernel, dim3((unsigned)T), dim3(mx::kGroupThreads), 0, st, x,
                     (const int32_t*)ws.idx, (int)T, d.n_experts, d.top_k, d.hidden, m.e_begin,
                     m.e_end, mx_tile_positions(kind), ws.counts, ws.offsets, ws.active, ws.meta,
                     ws.perm, ws.inv, ws.eb.tile_expert, ws.eb.tile_row0, ws.eb.tile_rows,

@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(kRouterWarps * 32)
   const int t0 = blockIdx.x * TT;
   const int nt = min(TT, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e0 = (blockIdx.y * kRouterWarps + warp) * EPW;
+  const int e0 = (blockIdx.y * (int)(blockDim.x >> 5) + warp) * EPW;
   const int nb = H >> 5;
   // Decode-sized batches: few warps read the router weight, so each lane
   // issues all of its weight loads first, then the x loads, and only then
@@ -298,17 +298,20 @@ __global__ void __launch_bounds__(256, 2)
   route_tail(t0, nt, logits, tickets, E, K, kind, sel_bias, idx_out, w_out);
 }
 
+// warps: experts per CTA (EPW each); fewer warps spread a small batch's
+// router rows over more SMs.  A warp computes its experts' dot products
+// whole, so the logits do not depend on it.
 template <int TT, int EPW>
 cudaError_t launch(const Moe& m, const float* x, int64_t T, int32_t* idx, float* wts,
-                   cudaStream_t st) {
+                   cudaStream_t st, int warps = kRouterWarps) {
   const gb_moe_desc& d = m.desc;
   const int H = d.hidden, E = d.n_experts;
-  dim3 grid((unsigned)((T + TT - 1) / TT), (unsigned)((E + kRouterWarps * EPW - 1) / (kRouterWarps * EPW)));
+  dim3 grid((unsigned)((T + TT - 1) / TT), (unsigned)((E + warps * EPW - 1) / (warps * EPW)));
   const size_t smem = (size_t)TT * H * sizeof(float);
   auto kern = router_kernel<TT, EPW>;
   cudaError_t err = set_smem_limit(kern, smem);
   if (err != cudaSuccess) return err;
-  return launch_pdl(kern, grid, dim3(kRouterWarps * 32), smem, st, x, (int)T, H, m.router_w,
+  return launch_pdl(kern, grid, dim3(warps * 32), smem, st, x, (int)T, H, m.router_w,
                     m.router_b, E, d.top_k, d.router_kind, m.sel_bias, m.ws.logits, m.ws.tickets,
                     idx, wts);
 }
@@ -320,7 +323,9 @@ cudaError_t launch_router_topk(const Moe& m, const float* x, int64_t T, int32_t*
   if (T <= 0) return cudaSuccess;
   // measured on 128 experts x 2880: one token per CTA is fastest to 16
   // tokens, two to 64 (more tokens per warp lengthen its dependent chains);
-  // the tiled kernel needs more than a few hundred tokens to fill the GPU
+  // the tiled kernel needs more than a few hundred tokens to fill the GPU.
+  // (Two warps per CTA at one token, E / 2 CTAs, measured slower: 15.1 vs
+  // 13.5 us.)
   if (T <= 16) return launch<1, 1>(m, x, T, idx, wts, st);
   if (T <= 256) return launch<2, 1>(m, x, T, idx, wts, st);
   const gb_moe_desc& d = m.desc;
