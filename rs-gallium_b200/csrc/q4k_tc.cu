@@ -134,7 +134,12 @@ __device__ __forceinline__ void decode_half(const uint4& hdr, const uint4& qa, c
   const float dmin = f16_bits_to_f32((uint32_t)hb[2] | ((uint32_t)hb[3] << 8));
   int sc, mn;
   q4k_scale_min(2 * c + h, hb + 4, sc, mn);
-  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mn);
+  // (d1 q - m1) 2^e computed as (16 d1 2^e)(q / 16) - m1 2^e: multiplying by
+  // powers of two is exact and commutes with each rounding, and q / 16 comes
+  // exactly from the bits of 1 + q / 16, so every value is bit-identical to
+  // the reference's d1 * q - m1, times 2^e (no int-to-float conversion)
+  const float d16 = __fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc), 16.0f), scale);
+  const float m1 = __fmul_rn(__fmul_rn(dmin, (float)mn), scale);
   const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
   const int shift = 4 * h;
 #pragma unroll
@@ -143,8 +148,11 @@ __device__ __forceinline__ void decode_half(const uint4& hdr, const uint4& qa, c
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int byte = 2 * i + u;
-      const uint32_t qv = (words[byte >> 2] >> (8 * (byte & 3) + shift)) & 0xFu;
-      v[u] = __fmul_rn(__fsub_rn(__fmul_rn(d1, (float)qv), m1), scale);
+      const int lo_bit = 8 * (byte & 3) + shift;  // the nibble's bit in its word
+      const uint32_t wd = words[byte >> 2];
+      const uint32_t m = lo_bit <= 19 ? (wd << (19 - lo_bit)) : (wd >> (lo_bit - 19));
+      const float q16 = __fsub_rn(__uint_as_float((m & (0xFu << 19)) | 0x3F800000u), 1.0f);
+      v[u] = __fsub_rn(__fmul_rn(d16, q16), m1);
     }
     const __half2 vh = __floats2half2_rn(v[0], v[1]);
     const float2 back = __half22float2(vh);
