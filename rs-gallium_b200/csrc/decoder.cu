@@ -204,11 +204,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
       if (lane == 0) {
         float* o = out + (int64_t)(p0 + j) * out_stride + o0;
         float r0 = bias ? __fadd_rn(s0, bias[o0]) : s0;
-        if (add) r0 = __fadd_rn(o[0], r0);
+        if (add) r0 = __fadd_rn(__ldcg(o), r0);
         o[0] = r0;
         if (v1) {
           float r1 = bias ? __fadd_rn(s1, bias[o0 + 1]) : s1;
-          if (add) r1 = __fadd_rn(o[1], r1);
+          if (add) r1 = __fadd_rn(__ldcg(o + 1), r1);
           o[1] = r1;
         }
       }
@@ -275,7 +275,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
     if (lane == 0) {
       float* dst = out + (int64_t)j * out_stride + o;
       float r = bias ? __fadd_rn(sum, bias[o]) : sum;
-      if (add) r = __fadd_rn(*dst, r);
+      if (add) r = __fadd_rn(__ldcg(dst), r);
       *dst = r;
     }
   }

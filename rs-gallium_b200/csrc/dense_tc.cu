@@ -126,7 +126,18 @@ __device__ __forceinline__ int mma_cols(int nrows) { return (nrows + 15) & ~15; 
 // tile); hi_addr / lo_addr are this warp's lane-adjusted accumulator
 // addresses.  GATE_UP: gate (even lane) and up (odd lane) -> h as bf16 hi /
 // lo; DOWN: y.
-template <int MODE>
+// The gate_up activation, fixed per kernel (SiLU without a clamp, the common
+// case, or any gallium-core activation), so the unrolled epilogue holds one
+// variant.
+enum Act { ACT_SILU = 0, ACT_GENERIC = 1 };
+
+template <int ACT>
+__device__ __forceinline__ float activation(const Args& a, float g) {
+  if (ACT == ACT_SILU) return __fdiv_rn(g, __fadd_rn(expf(-g), 1.0f));
+  return act_generic(a.act_kind, g, a.clamp);
+}
+
+template <int MODE, int ACT>
 __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uint32_t hi_addr,
                                               uint32_t lo_addr, int m) {
   const int row = it.m_tile * BM + m;
@@ -146,7 +157,7 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
       if (MODE == GATE_UP) {
         const float up = __shfl_down_sync(kFullMask, val, 1);
         if ((m & 1) == 0 && valid && n < it.nrows) {
-          const float h = __fmul_rn(act_generic(a.act_kind, val, a.clamp), up);
+          const float h = __fmul_rn(activation<ACT>(a, val), up);
           const __nv_bfloat16 hi = __float2bfloat16_rn(h);
           const __nv_bfloat16 lo = __float2bfloat16_rn(__fsub_rn(h, __bfloat162float(hi)));
           const int64_t o = pos * a.out_stride + (row >> 1);
@@ -159,14 +170,17 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
         const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
         float* o = a.out_y + orow * a.out_stride + row;
         float v = a.bias ? __fadd_rn(val, a.bias[row]) : val;
-        if (a.add_out) v = __fadd_rn(*o, v);
+        // the old value is read only when it is added to: a plain load here
+        // may be hoisted above the branch (the store below makes it legal),
+        // which reads all of y on every forward
+        if (a.add_out) v = __fadd_rn(__ldcg(o), v);
         *o = v;
       }
     }
   }
 }
 
-template <int MODE>
+template <int MODE, int ACT>
 __global__ void __launch_bounds__(kThreads, 1)
     dense_tc_gemm(const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_hi,
@@ -295,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item it = decode_item(a, item);
       const uint32_t hi_addr =
           tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 2 * BN);
-      epilogue_tile<MODE>(a, it, hi_addr, hi_addr + (uint32_t)BN, m);
+      epilogue_tile<MODE, ACT>(a, it, hi_addr, hi_addr + (uint32_t)BN, m);
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
@@ -349,7 +363,7 @@ __global__ void split_reduce_kernel(const float* __restrict__ part, int ksplit, 
   for (int s = 1; s < ksplit; ++s) v = __fadd_rn(v, part[(int64_t)s * n_pos * rows + i]);
   if (bias) v = __fadd_rn(v, bias[r]);
   float* o = out + (int64_t)p * out_stride + r;
-  if (add_out) v = __fadd_rn(*o, v);
+  if (add_out) v = __fadd_rn(__ldcg(o), v);
   *o = v;
 }
 
@@ -374,16 +388,24 @@ cudaError_t make_bf16_map(void* map, const void* base, uint64_t K, uint64_t rows
 
 namespace {
 
-template <int MODE>
-cudaError_t launch_gemm(int sm_count, const dtc::Args& a, const void* map_w, const void* map_hi,
-                        const void* map_lo, cudaStream_t st) {
-  auto k = dtc::dense_tc_gemm<MODE>;
+template <int MODE, int ACT>
+cudaError_t launch_gemm_act(int sm_count, const dtc::Args& a, const void* map_w,
+                            const void* map_hi, const void* map_lo, cudaStream_t st) {
+  auto k = dtc::dense_tc_gemm<MODE, ACT>;
   cudaError_t e = set_smem_limit(k, dtc::kSmemBytes);
   if (e != cudaSuccess) return e;
   k<<<sm_count, dtc::kThreads, dtc::kSmemBytes, st>>>(
       *reinterpret_cast<const CUtensorMap*>(map_w), *reinterpret_cast<const CUtensorMap*>(map_hi),
       *reinterpret_cast<const CUtensorMap*>(map_lo), a);
   return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_gemm(int sm_count, const dtc::Args& a, const void* map_w, const void* map_hi,
+                        const void* map_lo, cudaStream_t st) {
+  if (MODE == dtc::GATE_UP && !(a.act_kind == GB_ACT_SILU && !(a.clamp > 0.0f)))
+    return launch_gemm_act<MODE, dtc::ACT_GENERIC>(sm_count, a, map_w, map_hi, map_lo, st);
+  return launch_gemm_act<MODE, dtc::ACT_SILU>(sm_count, a, map_w, map_hi, map_lo, st);
 }
 
 dtc::Args base_args(const Moe& m, int* err) {
