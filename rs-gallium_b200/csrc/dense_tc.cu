@@ -91,6 +91,16 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// The gate_up activation, fixed per kernel (SiLU without a clamp, the common
+// case, or any gallium-core activation), so the unrolled epilogue holds one
+// variant.
+enum Act { ACT_SILU = 0, ACT_GENERIC = 1 };
+// The down epilogue, fixed per kernel: the grouped expert rows (a plain
+// store), or the plain-GEMM form of a linear layer (bias, residual add,
+// split-K partials).  The down GEMM's tiles have few K steps, so its
+// epilogue is on the critical path and carries no branch it does not need.
+enum Epi { EPI_GROUPED = 0, EPI_LINEAR = 1 };
+
 struct Item {
   int le, m_tile, row0, nrows, ks, k0, k1;  // k0 .. k1: the item's K steps
 };
@@ -99,13 +109,22 @@ __device__ __forceinline__ int n_tiles(const Args& a) {
   return a.tile_expert ? a.meta[2] : (a.uniform_rows + BN - 1) / BN;
 }
 
+// SPLIT: the item index also carries a K range (the linear-layer form);
+// otherwise every item covers all of K.
+template <bool SPLIT>
 __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   Item it;
   const int nk = a.K / BK;
-  it.ks = item % a.ksplit;
-  item /= a.ksplit;
-  it.k0 = it.ks * nk / a.ksplit;
-  it.k1 = (it.ks + 1) * nk / a.ksplit;
+  if (SPLIT) {
+    it.ks = item % a.ksplit;
+    item /= a.ksplit;
+    it.k0 = it.ks * nk / a.ksplit;
+    it.k1 = (it.ks + 1) * nk / a.ksplit;
+  } else {
+    it.ks = 0;
+    it.k0 = 0;
+    it.k1 = nk;
+  }
   const int j = item / a.m_tiles;
   it.m_tile = item - j * a.m_tiles;
   if (a.tile_expert) {
@@ -122,14 +141,6 @@ __device__ __forceinline__ Item decode_item(const Args& a, int item) {
 
 __device__ __forceinline__ int mma_cols(int nrows) { return (nrows + 15) & ~15; }
 
-// Epilogue of one tile: thread m owns TMEM lane m (weight row m of the M
-// tile); hi_addr / lo_addr are this warp's lane-adjusted accumulator
-// addresses.  GATE_UP: gate (even lane) and up (odd lane) -> h as bf16 hi /
-// lo; DOWN: y.
-// The gate_up activation, fixed per kernel (SiLU without a clamp, the common
-// case, or any gallium-core activation), so the unrolled epilogue holds one
-// variant.
-enum Act { ACT_SILU = 0, ACT_GENERIC = 1 };
 
 template <int ACT>
 __device__ __forceinline__ float activation(const Args& a, float g) {
@@ -137,12 +148,17 @@ __device__ __forceinline__ float activation(const Args& a, float g) {
   return act_generic(a.act_kind, g, a.clamp);
 }
 
-template <int MODE, int ACT>
+// Epilogue of one tile: thread m owns TMEM lane m (weight row m of the M
+// tile); hi_addr / lo_addr are this warp's lane-adjusted accumulator
+// addresses.  GATE_UP: gate (even lane) and up (odd lane) -> h as bf16 hi /
+// lo; DOWN: y.
+template <int MODE, int ACT, int EPI>
 __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uint32_t hi_addr,
                                               uint32_t lo_addr, int m) {
   const int row = it.m_tile * BM + m;
   const bool valid = row < a.rows;
   const int ncols = mma_cols(it.nrows);
+  const float bias = (EPI == EPI_LINEAR && MODE == DOWN && a.bias && valid) ? a.bias[row] : 0.0f;
 #pragma unroll 1
   for (int c0 = 0; c0 < ncols; c0 += 16) {
     uint32_t vh[16], vl[16];
@@ -164,23 +180,27 @@ __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uin
           a.out_hi[o] = hi;
           a.out_lo[o] = lo;
         }
-      } else if (valid && n < it.nrows && a.ksplit > 1) {
-        a.part[((int64_t)it.ks * a.uniform_rows + pos) * a.rows + row] = val;
+      } else if (EPI == EPI_GROUPED) {
+        if (valid && n < it.nrows) {
+          const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
+          a.out_y[orow * a.out_stride + row] = val;
+        }
       } else if (valid && n < it.nrows) {
-        const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
-        float* o = a.out_y + orow * a.out_stride + row;
-        float v = a.bias ? __fadd_rn(val, a.bias[row]) : val;
-        // the old value is read only when it is added to: a plain load here
-        // may be hoisted above the branch (the store below makes it legal),
-        // which reads all of y on every forward
-        if (a.add_out) v = __fadd_rn(__ldcg(o), v);
-        *o = v;
+        if (a.ksplit > 1) {
+          a.part[((int64_t)it.ks * a.uniform_rows + pos) * a.rows + row] = val;
+        } else {
+          float* o = a.out_y + pos * a.out_stride + row;
+          float v = a.bias ? __fadd_rn(val, bias) : val;
+          // the old value is read only when it is added to
+          if (a.add_out) v = __fadd_rn(__ldcg(o), v);
+          *o = v;
+        }
       }
     }
   }
 }
 
-template <int MODE, int ACT>
+template <int MODE, int ACT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     dense_tc_gemm(const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_hi,
@@ -196,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int total_items = n_tiles(a) * a.m_tiles * a.ksplit;
+  const int total_items = n_tiles(a) * a.m_tiles * (EPI == EPI_LINEAR ? a.ksplit : 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -223,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
-        const Item it = decode_item(a, item);
+        const Item it = decode_item<EPI == EPI_LINEAR>(a, item);
         const int wrow = it.le * a.rows + it.m_tile * BM;
         for (int kc = it.k0; kc < it.k1; ++kc) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err, a.wait_ns)) {
@@ -258,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int acc_iter = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x, ++acc_iter) {
-        const Item it = decode_item(a, item);
+        const Item it = decode_item<EPI == EPI_LINEAR>(a, item);
         const uint32_t idesc = idesc_bf16(mma_cols(it.nrows));
         const int b = acc_iter & 1;
         const uint32_t acc_phase = (acc_iter >> 1) & 1;
@@ -306,10 +326,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_phase = (acc_iter >> 1) & 1;
       if (!mbar_wait(&acc_full[b], acc_phase, abort_flag, a.err, a.wait_ns)) break;
       tc_fence_after();
-      const Item it = decode_item(a, item);
+      const Item it = decode_item<EPI == EPI_LINEAR>(a, item);
       const uint32_t hi_addr =
           tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 2 * BN);
-      epilogue_tile<MODE, ACT>(a, it, hi_addr, hi_addr + (uint32_t)BN, m);
+      epilogue_tile<MODE, ACT, EPI>(a, it, hi_addr, hi_addr + (uint32_t)BN, m);
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
     }
@@ -388,10 +408,10 @@ cudaError_t make_bf16_map(void* map, const void* base, uint64_t K, uint64_t rows
 
 namespace {
 
-template <int MODE, int ACT>
+template <int MODE, int ACT, int EPI = dtc::EPI_GROUPED>
 cudaError_t launch_gemm_act(int sm_count, const dtc::Args& a, const void* map_w,
                             const void* map_hi, const void* map_lo, cudaStream_t st) {
-  auto k = dtc::dense_tc_gemm<MODE, ACT>;
+  auto k = dtc::dense_tc_gemm<MODE, ACT, EPI>;
   cudaError_t e = set_smem_limit(k, dtc::kSmemBytes);
   if (e != cudaSuccess) return e;
   k<<<sm_count, dtc::kThreads, dtc::kSmemBytes, st>>>(
@@ -455,7 +475,8 @@ cudaError_t launch_linear_tc(int sm_count, const void* map_w, const void* map_xh
     ks = 1;
   a.ksplit = std::max(1, ks);
   a.part = part;
-  cudaError_t e = launch_gemm<dtc::DOWN>(sm_count, a, map_w, map_xh, map_xl, st);
+  cudaError_t e = launch_gemm_act<dtc::DOWN, dtc::ACT_SILU, dtc::EPI_LINEAR>(sm_count, a, map_w,
+                                                                             map_xh, map_xl, st);
   if (e != cudaSuccess || a.ksplit == 1) return e;
   const int64_t n = (int64_t)n_pos * rows;
   dtc::split_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
