@@ -181,3 +181,91 @@ def test_gguf_repack_helper_round_trips_values():
     gg = synth.gptoss_gguf_from_split(layer)
     assert gg.gate_raw.shape == (1, 32, 2 * 17)
     assert gg.down_raw.shape == (1, 64, 1 * 17)
+
+
+def test_decoder_struct_layouts_match_the_header(tmp_path):
+    from gallium_b200._lib import DecoderDesc, DecoderLayer
+    src = ['#include <stdio.h>', '#include <stddef.h>', f'#include "{HEADER}"', 'int main(void){']
+    want = []
+    for name, cls in (("gb_decoder_layer", DecoderLayer), ("gb_decoder_desc", DecoderDesc)):
+        src.append(f'printf("%zu\\n", sizeof({name}));')
+        want.append(ctypes.sizeof(cls))
+        for f, _ in cls._fields_:
+            src.append(f'printf("%zu\\n", offsetof({name}, {f}));')
+            want.append(getattr(cls, f).offset)
+    src.append("return 0;}")
+    c = tmp_path / "dlayout.c"
+    c.write_text("\n".join(src))
+    exe = tmp_path / "dlayout"
+    subprocess.run(["gcc", str(c), "-o", str(exe)], check=True)
+    vals = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                           check=True).stdout.split()]
+    assert vals == want
+
+
+def _decoder_desc(layers=1, **kw):
+    """A decoder descriptor whose pointers are all set (to a dummy host
+    buffer): validation only, nothing reaches the device."""
+    from gallium_b200._lib import DecoderDesc, DecoderLayer
+    buf = np.zeros(16, np.float32)
+    p = buf.ctypes.data
+    moe = _desc()
+    L = (DecoderLayer * layers)()
+    for i in range(layers):
+        for f, _ in DecoderLayer._fields_:
+            if f not in ("sliding", "moe"):
+                setattr(L[i], f, p)
+        L[i].moe = ctypes.pointer(moe)
+    d = DecoderDesc()
+    d.struct_size = ctypes.sizeof(DecoderDesc)
+    d.n_layers, d.hidden, d.n_heads, d.n_kv_heads, d.head_dim = layers, 64, 4, 2, 32
+    d.vocab, d.sliding_window, d.max_seq_len, d.max_batch, d.max_tokens = 10, 4, 16, 1, 4
+    d.rope_theta, d.rms_eps = 10000.0, 1e-5
+    d.embed = d.final_norm = p
+    d.layers = L
+    for k, v in kw.items():
+        setattr(d, k, v)
+    return d, (buf, moe, L)
+
+
+@pytest.mark.parametrize("kw,status,needle", [
+    ({"struct_size": 8}, _lib.GB_ERR_INVALID_ARG, "struct_size"),
+    ({"n_heads": 3}, _lib.GB_ERR_INVALID_ARG, "multiple"),
+    ({"n_heads": 40, "n_kv_heads": 2}, _lib.GB_ERR_INVALID_ARG, "query heads"),
+    ({"head_dim": 48}, _lib.GB_ERR_UNSUPPORTED, "head_dim"),
+    ({"hidden": 40}, _lib.GB_ERR_INVALID_ARG, "hidden"),
+    ({"vocab": 0}, _lib.GB_ERR_INVALID_ARG, "vocab"),
+    ({"rope_scaling_factor": 32.0, "rope_orig_ctx": 0}, _lib.GB_ERR_INVALID_ARG, "YaRN"),
+    ({"embed": None}, _lib.GB_ERR_INVALID_ARG, "embed"),
+])
+def test_decoder_create_rejects_bad_descriptors(kw, status, needle):
+    lib = _lib.load_library()
+    d, keep = _decoder_desc(**kw)
+    h = ctypes.c_void_p()
+    rc = lib.gb_decoder_create(ctypes.byref(d), ctypes.byref(h))
+    assert rc == status, lib.gb_last_error()
+    assert needle in lib.gb_last_error().decode()
+    assert not h.value
+
+
+def test_decoder_layer_checks():
+    lib = _lib.load_library()
+    d, keep = _decoder_desc(layers=2)
+    keep[2][1].wk = None
+    h = ctypes.c_void_p()
+    assert lib.gb_decoder_create(ctypes.byref(d), ctypes.byref(h)) == _lib.GB_ERR_INVALID_ARG
+    assert b"layer 1" in lib.gb_last_error()
+    d, keep = _decoder_desc(layers=1)
+    keep[1].hidden = 128  # the MoE block's hidden differs from the model's
+    assert lib.gb_decoder_create(ctypes.byref(d), ctypes.byref(h)) == _lib.GB_ERR_INVALID_ARG
+    assert b"hidden" in lib.gb_last_error()
+
+
+def test_decoder_null_handle_calls_are_errors():
+    lib = _lib.load_library()
+    assert lib.gb_decoder_forward(None, None, 1, 1, 0, None, None, None) == _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_decoder_generate(None, None, 1, 0, 1, None, None) == _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_decoder_reset(None) == _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_decoder_set_profiling(None, 1) == _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_decoder_device_status(None, None) == _lib.GB_ERR_INVALID_ARG
+    assert lib.gb_decoder_destroy(None) == _lib.GB_OK
