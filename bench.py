@@ -173,7 +173,8 @@ def parse_args():
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--parity-rows", type=int, default=64)
     ap.add_argument("--expert-path", default="auto",
-                    choices=["auto", "cuda_cores", "tensor_cores", "tensor_cores_f16"],
+                    choices=["auto", "cuda_cores", "tensor_cores", "tensor_cores_f16",
+                             "fused_decode"],
                     help="force one expert kernel (gb_moe_set_expert_path)")
     ap.add_argument("--cpu-threads", type=int, default=0)
     return ap.parse_args()
