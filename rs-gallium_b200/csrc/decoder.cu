@@ -281,6 +281,106 @@ __global__ void __launch_bounds__(kGemvWarps * 32)
   }
 }
 
+// q/k/v projection of up to kGemvRows rows with RoPE and the KV-cache store
+// folded in: a warp owns output rows j and j + hd / 2 of one head (the pair
+// one rotation mixes), requests KP pieces of each row per pass before the
+// first multiply, and lane 0 adds the biases, rotates q and k as
+// rope_append_kernel does (same roundings) and stores q into qkv, k and v
+// into sequence b's cache at position pos + t.
+template <int KP>
+__global__ void __launch_bounds__(kGemvWarps * 32)
+    qkv_rope_gemv_kernel(const float* __restrict__ x, int n_x, int K,
+                         const uint16_t* __restrict__ W, const float* __restrict__ bias, int nh,
+                         int nkv, int hd, int T, const float* __restrict__ cos_t,
+                         const float* __restrict__ sin_t, const int* __restrict__ d_pos, int S,
+                         float* __restrict__ qkv, float* __restrict__ kcache,
+                         float* __restrict__ vcache) {
+  extern __shared__ float xs[];  // [n_x][K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {
+    const int n4 = n_x * K / 4;
+    const float4* src = reinterpret_cast<const float4*>(x);
+    float4* dst = reinterpret_cast<float4*>(xs);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  const int half = hd / 2;
+  const int pidx = blockIdx.x * kGemvWarps + warp;
+  if (pidx >= (nh + 2 * nkv) * half) return;
+  const int hh = pidx / half, j = pidx - hh * half;
+  const int r1 = hh * hd + j, r2 = r1 + half;
+  const uint4* w1 = reinterpret_cast<const uint4*>(W + (int64_t)r1 * K);
+  const uint4* w2 = reinterpret_cast<const uint4*>(W + (int64_t)r2 * K);
+  const int npieces = K / 8;
+  float a1[kGemvRows], a2[kGemvRows];
+#pragma unroll
+  for (int t = 0; t < kGemvRows; ++t) a1[t] = a2[t] = 0.0f;
+  for (int base = 0; base < npieces; base += 32 * KP) {
+    uint4 v1[KP], v2[KP];
+#pragma unroll
+    for (int u = 0; u < KP; ++u) {
+      const int q = base + lane + 32 * u;
+      v1[u] = q < npieces ? __ldg(w1 + q) : make_uint4(0u, 0u, 0u, 0u);
+      v2[u] = q < npieces ? __ldg(w2 + q) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < KP; ++u) {
+      const int q = base + lane + 32 * u;
+      if (q < npieces) {
+        const uint32_t b1[4] = {v1[u].x, v1[u].y, v1[u].z, v1[u].w};
+        const uint32_t b2[4] = {v2[u].x, v2[u].y, v2[u].z, v2[u].w};
+#pragma unroll
+        for (int t = 0; t < kGemvRows; ++t) {
+          if (t < n_x) {
+            const float* xt = xs + t * K + q * 8;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float xa = xt[2 * e], xb = xt[2 * e + 1];
+              a1[t] = __fmaf_rn(xa, __uint_as_float(b1[e] << 16), a1[t]);
+              a1[t] = __fmaf_rn(xb, __uint_as_float(b1[e] & 0xffff0000u), a1[t]);
+              a2[t] = __fmaf_rn(xa, __uint_as_float(b2[e] << 16), a2[t]);
+              a2[t] = __fmaf_rn(xb, __uint_as_float(b2[e] & 0xffff0000u), a2[t]);
+            }
+          }
+        }
+      }
+    }
+  }
+  const int qkv_w = (nh + 2 * nkv) * hd;
+#pragma unroll
+  for (int t = 0; t < kGemvRows; ++t) {
+    if (t >= n_x) break;
+    float s1 = warp_sum_butterfly(a1[t]);
+    float s2 = warp_sum_butterfly(a2[t]);
+    if (lane == 0) {
+      if (bias) {
+        s1 = __fadd_rn(s1, bias[r1]);
+        s2 = __fadd_rn(s2, bias[r2]);
+      }
+      const int b = t / T, tt = t - b * T;
+      const int p = *d_pos + tt;
+      if (hh < nh + nkv) {  // q and k heads rotate
+        const float c = cos_t[(int64_t)p * half + j], sn = sin_t[(int64_t)p * half + j];
+        const float y1 = __fsub_rn(__fmul_rn(s1, c), __fmul_rn(s2, sn));
+        const float y2 = __fadd_rn(__fmul_rn(s1, sn), __fmul_rn(s2, c));
+        s1 = y1;
+        s2 = y2;
+      }
+      if (hh < nh) {
+        qkv[(int64_t)t * qkv_w + r1] = s1;
+        qkv[(int64_t)t * qkv_w + r2] = s2;
+      } else {
+        const bool is_k = hh < nh + nkv;
+        const int g = is_k ? hh - nh : hh - nh - nkv;
+        float* dst = (is_k ? kcache : vcache) + (((int64_t)b * nkv + g) * S + p) * hd;
+        dst[j] = s1;
+        dst[j + half] = s2;
+      }
+    }
+  }
+}
+
 // ---- RoPE and the KV cache --------------------------------------------------
 
 // Rotates the q and k heads of row (b, t) at position pos + t in place
@@ -934,14 +1034,27 @@ int run_step(Decoder& D, const int32_t* tokens, int B, int T, float* logits, int
         D.h, l ? D.moe_out : nullptr, L.attn_norm, H, d.rms_eps, 1, 0, D.xn,
         split ? D.xh : nullptr, split ? D.xl : nullptr);
     DEC_CUDA(cudaGetLastError(), "norm launch");
-    if ((rc = linear(D, D.xn, rows, H, L.wqkv, D.tc ? L.map_qkv : nullptr, D.qkv_w, L.bqkv, D.qkv,
-                     D.qkv_w, false, st, split)))
-      return rc;
     float* kc = D.kcache + (size_t)l * layer_kv;
     float* vc = D.vcache + (size_t)l * layer_kv;
-    dec::rope_append_kernel<<<dim3(rows, nh + 2 * nkv), hd / 2, 0, st>>>(
-        D.qkv, T, nh, nkv, hd, D.rope_cos, D.rope_sin, D.d_pos, (int)S, kc, vc);
-    DEC_CUDA(cudaGetLastError(), "RoPE launch");
+    if (!split && rows <= dec::kGemvRows) {
+      // q/k/v, RoPE and the cache store in one launch
+      const size_t smem = (size_t)rows * H * 4;
+      const int pairs = (nh + 2 * nkv) * (hd / 2);
+      DEC_CUDA(set_smem_limit(dec::qkv_rope_gemv_kernel<8>, (size_t)dec::kGemvRows * H * 4),
+               "q/k/v kernel shared memory");
+      dec::qkv_rope_gemv_kernel<8><<<(pairs + dec::kGemvWarps - 1) / dec::kGemvWarps,
+                                     dec::kGemvWarps * 32, smem, st>>>(
+          D.xn, rows, H, L.wqkv, L.bqkv, nh, nkv, hd, T, D.rope_cos, D.rope_sin, D.d_pos, (int)S,
+          D.qkv, kc, vc);
+      DEC_CUDA(cudaGetLastError(), "q/k/v launch");
+    } else {
+      if ((rc = linear(D, D.xn, rows, H, L.wqkv, D.tc ? L.map_qkv : nullptr, D.qkv_w, L.bqkv,
+                       D.qkv, D.qkv_w, false, st, split)))
+        return rc;
+      dec::rope_append_kernel<<<dim3(rows, nh + 2 * nkv), hd / 2, 0, st>>>(
+          D.qkv, T, nh, nkv, hd, D.rope_cos, D.rope_sin, D.d_pos, (int)S, kc, vc);
+      DEC_CUDA(cudaGetLastError(), "RoPE launch");
+    }
     // key slots per query: every slot for a lone row; from 16 rows the rows
     // fill the GPU and two slots keep CTAs busy with several chunks each
     const int slots = rows >= 16 ? 2 : rows >= 4 ? 4 : dec::kSlots;
