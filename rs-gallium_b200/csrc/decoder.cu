@@ -9,7 +9,7 @@
 //   qkv [rows][(nh + 2 nkv) hd]      q heads, then k heads, then v heads
 //   att [rows][nh hd]                attention output (head-major, as the
 //                                    reference's transpose + reshape leaves it)
-//   kv [layer][2][B][nkv][S][hd]     K (after RoPE) and V per position
+//   kcache, vcache [layer][max_batch][nkv][S][hd]  K (after RoPE) and V per position
 //   part [rows][nh][kSlots][hd + 2]  attention partials (max, sum, acc) per slot
 //   bf16 hi / lo copies of a linear layer's input for the tensor-core GEMMs.
 // Weights: wqkv [(nh + 2 nkv) hd][H] bf16 (q, k, v rows concatenated), wo
