@@ -151,6 +151,10 @@ __global__ void __launch_bounds__(kNormThreads)
 }
 
 // ---- linear layers on the CUDA cores (fewer than 16 rows) ------------------
+// Up to four rows: gemv_rows_kernel (and qkv_rope_gemv_kernel for the q/k/v
+// projection), a warp per output row with all its weight loads in flight.
+// Five to fifteen rows: linear_rows_kernel, a warp per pair of output rows.
+// From sixteen rows the projections run on the tensor cores (dense_tc.cu).
 
 // out[p][o] = (add ? out[p][o] : 0) + (x[p] . W[o] + bias[o]), W bf16 [n_out][K].
 // A warp owns two output rows; x rows are staged kGemvRows at a time.
