@@ -18,12 +18,13 @@
 // M = 128 weight rows, N = 128 grouped positions of one expert, K stepped by
 // 64 (one Q4_K sub-block pair).  Warps 4-11 decode: threads r and r + 128
 // load row r's super-block header and 32 quant bytes straight from HBM (the
-// next two stages' bytes are in flight while they decode), each decodes one
-// sub-block (the low or the high nibbles) and writes its half of A hi / lo
-// into shared memory in the K-major 128-byte-swizzled layout (decoding, not
-// the MMAs, bounds this kernel, hence eight warps); warp 12 copies B hi / lo
-// by TMA; warp 13 issues the MMAs; warps 0-3 run the epilogue (bias-free SiLU
-// or clamped SwiGLU into h hi / lo, or y).  Three 64 KB stages; two TMEM
+// next three K steps' bytes in flight while they decode, in a register ring
+// walked with compile-time slots), each decodes one sub-block (the low or
+// the high nibbles) and, once the MMAs have released the stage, writes its
+// half of A hi / lo into shared memory in the K-major 128-byte-swizzled
+// layout (decoding, not the MMAs, bounds this kernel, hence eight warps);
+// warp 12 copies B hi / lo by TMA; warp 13 issues the MMAs; warps 0-3 run
+// the epilogue (bias-free SiLU or clamped SwiGLU into h hi / lo, or y).  Three 64 KB stages; two TMEM
 // accumulator pairs so the epilogue of one tile overlaps the next tile's MMAs.
 // Every mbarrier wait is bounded (timeout -> abort flag, error bit 2, TMEM
 // freed, return).
@@ -94,16 +95,6 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
-__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t* s, int& sc, int& m) {
-  if (j < 4) {
-    sc = s[j] & 63;
-    m = s[j + 4] & 63;
-  } else {
-    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
-    m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
-  }
-}
-
 __device__ __forceinline__ float f16_bits_to_f32(uint32_t h) {
   const uint16_t b = (uint16_t)h;
   return __half2float(*reinterpret_cast<const __half*>(&b));
@@ -123,32 +114,51 @@ __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   return it;
 }
 
+// Scale and min of sub-block j = 2c + h of a super-block (candle's
+// get_scale_min_k4), read from the header words by shifts: the twelve scale
+// bytes are header bytes 4..15 (words y, z, w), so no byte array is indexed
+// at run time (which would put the header in local memory).  c is a
+// constant wherever the caller's loop is unrolled.
+__device__ __forceinline__ void q4k_scale_min_hdr(const uint4& hdr, int c, int h, int& sc,
+                                                  int& mn) {
+  const int sh = 8 * ((2 * c + h) & 3);
+  if (c < 2) {  // j < 4: sc = s[j] & 63, m = s[j + 4] & 63
+    sc = (int)((hdr.y >> sh) & 63u);
+    mn = (int)((hdr.z >> sh) & 63u);
+  } else {  // j >= 4: from s[j + 4] (word w), s[j - 4] (word y) and s[j] (word z)
+    const uint32_t b8 = (hdr.w >> sh) & 0xFFu, b0 = (hdr.y >> sh) & 0xFFu;
+    const uint32_t b4 = (hdr.z >> sh) & 0xFFu;
+    sc = (int)((b8 & 0xFu) | ((b0 >> 6) << 4));
+    mn = (int)((b8 >> 4) | ((b4 >> 6) << 4));
+  }
+}
+
 // The 32 values of sub-block 2c + h of a super-block (h = 0: the low
 // nibbles of the pair's 32 quant bytes, 1: the high nibbles) times 2^e, as
 // f16 hi / lo pairs packed two per word in element order.
 __device__ __forceinline__ void decode_half(const uint4& hdr, const uint4& qa, const uint4& qb,
                                             int c, int h, float scale, uint32_t (&hi)[16],
                                             uint32_t (&lo)[16]) {
-  const uint8_t* hb = reinterpret_cast<const uint8_t*>(&hdr);
-  const float d = f16_bits_to_f32((uint32_t)hb[0] | ((uint32_t)hb[1] << 8));
-  const float dmin = f16_bits_to_f32((uint32_t)hb[2] | ((uint32_t)hb[3] << 8));
+  const float d = f16_bits_to_f32(hdr.x & 0xFFFFu);
+  const float dmin = f16_bits_to_f32(hdr.x >> 16);
   int sc, mn;
-  q4k_scale_min(2 * c + h, hb + 4, sc, mn);
+  q4k_scale_min_hdr(hdr, c, h, sc, mn);
   // (d1 q - m1) 2^e computed as (16 d1 2^e)(q / 16) - m1 2^e: multiplying by
   // powers of two is exact and commutes with each rounding, and q / 16 comes
   // exactly from the bits of 1 + q / 16, so every value is bit-identical to
   // the reference's d1 * q - m1, times 2^e (no int-to-float conversion)
   const float d16 = __fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc), 16.0f), scale);
   const float m1 = __fmul_rn(__fmul_rn(dmin, (float)mn), scale);
-  const uint32_t words[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-  const int shift = 4 * h;
+  const int shift = 4 * h;  // the wanted nibble of each byte moved to its low half
+  const uint32_t words[8] = {qa.x >> shift, qa.y >> shift, qa.z >> shift, qa.w >> shift,
+                             qb.x >> shift, qb.y >> shift, qb.z >> shift, qb.w >> shift};
 #pragma unroll
   for (int i = 0; i < 16; ++i) {  // elements 2i, 2i + 1 of the sub-block
     float v[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int byte = 2 * i + u;
-      const int lo_bit = 8 * (byte & 3) + shift;  // the nibble's bit in its word
+      const int lo_bit = 8 * (byte & 3);  // the nibble's bit in its (shifted) word
       const uint32_t wd = words[byte >> 2];
       const uint32_t m = lo_bit <= 19 ? (wd << (19 - lo_bit)) : (wd >> (lo_bit - 19));
       const float q16 = __fsub_rn(__uint_as_float((m & (0xFu << 19)) | 0x3F800000u), 1.0f);
@@ -349,42 +359,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
         qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
       };
-      // two K steps of bytes in flight ahead of the one being decoded
-      uint4 hdr, qa, qb, h1 = {}, a1 = {}, b1 = {};
-      load(0, hdr, qa, qb);
-      if (nk > 1) load(1, h1, a1, b1);
-      for (int kc = 0; kc < nk; ++kc) {
-        uint4 h2 = h1, a2 = a1, b2 = b1;
-        if (kc + 2 < nk) load(kc + 2, h2, a2, b2);
-        uint32_t hi[16], lo[16];
-        decode_half(hdr, qa, qb, kc & 3, hsel, scale, hi, lo);
-        if (!mbar_wait(&tma_full[stage], phase, abort_flag, a.err)) {
-          ok = false;
-          break;
-        }
-        uint8_t* sah = smem + stage * STAGE_BYTES;
-        const int rb = (r >> 3) * 1024 + (r & 7) * 128;
+      // A ring of four K steps of bytes, three in flight ahead of the one
+      // being decoded.  The loop walks the ring with compile-time slots (four
+      // K steps per pass; nk is a multiple of four since K % 256 == 0), so no
+      // register copy has to wait for a load still in flight.
+      uint4 hdr[4], qa[4], qb[4];
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {  // 16-byte chunks 4 hsel .. 4 hsel + 3 of the row
-          const int c = 4 * hsel + cc;
-          const int off = rb + ((c ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(sah + off) =
-              make_uint4(hi[4 * cc], hi[4 * cc + 1], hi[4 * cc + 2], hi[4 * cc + 3]);
-          *reinterpret_cast<uint4*>(sah + A_BYTES + off) =
-              make_uint4(lo[4 * cc], lo[4 * cc + 1], lo[4 * cc + 2], lo[4 * cc + 3]);
+      for (int u = 0; u < 3; ++u)
+        if (u < nk) load(u, hdr[u], qa[u], qb[u]);
+      for (int kc0 = 0; kc0 < nk && ok; kc0 += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int kc = kc0 + u;
+          if (kc + 3 < nk) load(kc + 3, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
+          uint32_t hi[16], lo[16];
+          decode_half(hdr[u], qa[u], qb[u], u, hsel, scale, hi, lo);  // pair kc % 4 == u
+          // the slot is free once the MMAs that read it have completed
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sah = smem + stage * STAGE_BYTES;
+          const int rb = (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {  // 16-byte chunks 4 hsel .. 4 hsel + 3 of the row
+            const int c = 4 * hsel + cc;
+            const int off = rb + ((c ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(sah + off) =
+                make_uint4(hi[4 * cc], hi[4 * cc + 1], hi[4 * cc + 2], hi[4 * cc + 3]);
+            *reinterpret_cast<uint4*>(sah + A_BYTES + off) =
+                make_uint4(lo[4 * cc], lo[4 * cc + 1], lo[4 * cc + 2], lo[4 * cc + 3]);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&a_full[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&a_full[stage]);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1;
-        }
-        hdr = h1;
-        qa = a1;
-        qb = b1;
-        h1 = h2;
-        a1 = a2;
-        b1 = b2;
       }
     }
   } else {
