@@ -185,38 +185,66 @@ __device__ __forceinline__ float activation(const Args& a, float g, float u) {
   return __fmul_rn(act_generic(a.act_kind, g, a.clamp), u);
 }
 
+// Thread m holds TMEM lane m (weight row m of the tile) for the tile's
+// columns (positions).  The per-column factors (2^s of each position, or its
+// output row) are read for sixteen columns at a time before that chunk's
+// stores.  For gate_up, rows 2i (gate) and 2i + 1 (up) sit in neighbouring
+// lanes; the pair swaps one value per two columns so that the even lane
+// finishes column j and the odd lane column j + 1, each lane computing the
+// activation of half the columns (the same values and roundings as one lane
+// doing them all).
 template <int MODE, int ACT>
 __device__ __forceinline__ void epilogue_tile(const Args& a, const Item& it, uint32_t hi_addr,
                                               uint32_t lo_addr, int m) {
   const int row = it.m_tile * BM + m;
   const bool valid = row < a.rows;
   const float row_f = pow2f(-a.wexp[it.le]);
+  const int odd = m & 1;
 #pragma unroll 1
   for (int c0 = 0; c0 < it.nrows; c0 += 16) {  // the columns the MMAs wrote
     uint32_t vh[16], vl[16];
     tmem_ld16(hi_addr + (uint32_t)c0, vh);
     tmem_ld16(lo_addr + (uint32_t)c0, vl);
-    tmem_wait_ld();
+    float colf[16];
+    int64_t orow[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const int n = c0 + j;
       const int64_t pos = (int64_t)it.row0 + n;
-      float val = __fmul_rn(__fadd_rn(__uint_as_float(vh[j]), __uint_as_float(vl[j])), row_f);
       if (MODE == GATE_UP) {
-        if (n < it.nrows) val = __fmul_rn(val, pow2f((int)a.xscale[pos]));
-        // rows 2i (gate) and 2i+1 (up) sit in neighbouring lanes
-        const float up = __shfl_down_sync(kFullMask, val, 1);
-        if ((m & 1) == 0 && valid && n < it.nrows) {
-          const float h = activation<ACT>(a, val, up);
+        colf[j] = n < it.nrows ? pow2f((int)__ldg(a.xscale + pos)) : 1.0f;
+      } else {
+        orow[j] = n < it.nrows ? (a.out_rows ? (int64_t)__ldg(a.out_rows + pos) : pos) : 0;
+      }
+    }
+    tmem_wait_ld();
+    if (MODE == GATE_UP) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        const float v0 = __fmul_rn(
+            __fmul_rn(__fadd_rn(__uint_as_float(vh[j]), __uint_as_float(vl[j])), row_f), colf[j]);
+        const float v1 = __fmul_rn(
+            __fmul_rn(__fadd_rn(__uint_as_float(vh[j + 1]), __uint_as_float(vl[j + 1])), row_f),
+            colf[j + 1]);
+        const float recv = __shfl_xor_sync(kFullMask, odd ? v0 : v1, 1);
+        const float g = odd ? recv : v0;
+        const float u = odd ? v1 : recv;
+        const int n = c0 + j + odd;
+        if (valid && n < it.nrows) {
+          const float h = activation<ACT>(a, g, u);
           const __half hi = __float2half_rn(h);
           const __half lo = __float2half_rn(__fsub_rn(h, __half2float(hi)));
-          const int64_t o = pos * a.out_stride + (row >> 1);
+          const int64_t o = ((int64_t)it.row0 + n) * a.out_stride + (row >> 1);
           a.out_hi[o] = hi;
           a.out_lo[o] = lo;
         }
-      } else if (valid && n < it.nrows) {
-        const int64_t orow = a.out_rows ? a.out_rows[pos] : pos;
-        a.out_y[orow * a.out_stride + row] = val;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float val =
+            __fmul_rn(__fadd_rn(__uint_as_float(vh[j]), __uint_as_float(vl[j])), row_f);
+        if (valid && c0 + j < it.nrows) a.out_y[orow[j] * a.out_stride + row] = val;
       }
     }
   }
