@@ -133,9 +133,40 @@ __device__ __forceinline__ void q4k_scale_min_hdr(const uint4& hdr, int c, int h
   }
 }
 
+// Two f32 lanes in one 64-bit register, and the sm_100 paired f32 ops on
+// them (each lane rounded to nearest like its scalar op).
+__device__ __forceinline__ uint64_t f2_pack(float x, float y) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t x, uint64_t y) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t x, uint64_t y) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(x), "l"(y));
+  return r;
+}
+
 // The 32 values of sub-block 2c + h of a super-block (h = 0: the low
 // nibbles of the pair's 32 quant bytes, 1: the high nibbles) times 2^e, as
 // f16 hi / lo pairs packed two per word in element order.
+//
+// Each nibble q, sitting at bit 8k of its word (k = 0, 1, 2), becomes the
+// float 2^23 + q 2^8k by OR-ing in the exponent of 2^23 (one logic op, no
+// int-to-float conversion); subtracting 2^23 leaves q 2^8k exactly, and
+// multiplying by d1 2^(e - 8k) gives the correctly rounded d1 q 2^e.  So every
+// value is bit-identical to the reference's d1 * q - m1 (each product rounded
+// to f32), times 2^e: powers of two are exact and commute with the roundings.
+// Two elements go through each paired op.
 __device__ __forceinline__ void decode_half(const uint4& hdr, const uint4& qa, const uint4& qb,
                                             int c, int h, float scale, uint32_t (&hi)[16],
                                             uint32_t (&lo)[16]) {
@@ -143,30 +174,34 @@ __device__ __forceinline__ void decode_half(const uint4& hdr, const uint4& qa, c
   const float dmin = f16_bits_to_f32(hdr.x >> 16);
   int sc, mn;
   q4k_scale_min_hdr(hdr, c, h, sc, mn);
-  // (d1 q - m1) 2^e computed as (16 d1 2^e)(q / 16) - m1 2^e: multiplying by
-  // powers of two is exact and commutes with each rounding, and q / 16 comes
-  // exactly from the bits of 1 + q / 16, so every value is bit-identical to
-  // the reference's d1 * q - m1, times 2^e (no int-to-float conversion)
-  const float d16 = __fmul_rn(__fmul_rn(__fmul_rn(d, (float)sc), 16.0f), scale);
+  const float d0 = __fmul_rn(__fmul_rn(d, (float)sc), scale);  // d1 2^e
   const float m1 = __fmul_rn(__fmul_rn(dmin, (float)mn), scale);
+  const uint64_t d_lo = f2_pack(d0, __fmul_rn(d0, 0x1p-8f));  // bytes 0, 1 of a word
+  const float d16 = __fmul_rn(d0, 0x1p-16f);
+  const uint64_t d_hi = f2_pack(d16, d16);  // bytes 2, 3 (byte 3 moved down to bit 16)
+  const uint64_t mm = f2_pack(m1, m1);
+  const uint64_t two23 = f2_pack(0x1p23f, 0x1p23f);
   const int shift = 4 * h;  // the wanted nibble of each byte moved to its low half
   const uint32_t words[8] = {qa.x >> shift, qa.y >> shift, qa.z >> shift, qa.w >> shift,
                              qb.x >> shift, qb.y >> shift, qb.z >> shift, qb.w >> shift};
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {  // elements 2i, 2i + 1 of the sub-block
-    float v[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int byte = 2 * i + u;
-      const int lo_bit = 8 * (byte & 3);  // the nibble's bit in its (shifted) word
-      const uint32_t wd = words[byte >> 2];
-      const uint32_t m = lo_bit <= 19 ? (wd << (19 - lo_bit)) : (wd >> (lo_bit - 19));
-      const float q16 = __fsub_rn(__uint_as_float((m & (0xFu << 19)) | 0x3F800000u), 1.0f);
-      v[u] = __fsub_rn(__fmul_rn(d16, q16), m1);
+  for (int i = 0; i < 16; ++i) {  // elements 2i, 2i + 1 of the sub-block: bytes 2i, 2i + 1
+    const uint32_t w = words[i >> 1];
+    uint32_t b0, b1;
+    if ((i & 1) == 0) {
+      b0 = (w & 0xFu) | 0x4B000000u;
+      b1 = (w & 0xF00u) | 0x4B000000u;
+    } else {
+      b0 = (w & 0xF0000u) | 0x4B000000u;
+      b1 = ((w >> 8) & 0xF0000u) | 0x4B000000u;
     }
-    const __half2 vh = __floats2half2_rn(v[0], v[1]);
+    const uint64_t q = f2_sub(f2_pack(__uint_as_float(b0), __uint_as_float(b1)), two23);
+    const uint64_t v = f2_sub(f2_mul(q, (i & 1) ? d_hi : d_lo), mm);
+    const float2 vf = f2_unpack(v);
+    const __half2 vh = __floats2half2_rn(vf.x, vf.y);
     const float2 back = __half22float2(vh);
-    const __half2 vl = __floats2half2_rn(__fsub_rn(v[0], back.x), __fsub_rn(v[1], back.y));
+    const float2 rf = f2_unpack(f2_sub(v, f2_pack(back.x, back.y)));
+    const __half2 vl = __floats2half2_rn(rf.x, rf.y);
     hi[i] = *reinterpret_cast<const uint32_t*>(&vh);
     lo[i] = *reinterpret_cast<const uint32_t*>(&vl);
   }
