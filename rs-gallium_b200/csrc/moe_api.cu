@@ -967,6 +967,7 @@ int alloc_expert_bufs(const Moe& m, ExpertBufs& eb, int64_t rows) {
       {(void**)&nb.xscale, (tc || m.mx.ok) ? sizeof(float) * (size_t)rows : 0},
       {(void**)&nb.hh, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
       {(void**)&nb.hl, tc ? sizeof(__half) * (size_t)(rows * I) : 0},
+      {(void**)&nb.xsum, q4k_tc_supported(m) ? sizeof(float) * (size_t)(rows * (std::max(H, I) / 32)) : 0},
       {(void**)&nb.xq, m.mx.ok ? mx_piece_bytes(rows, (int)H) : 0},
       {(void**)&nb.hq, m.mx.ok ? mx_piece_bytes(rows, (int)I) : 0},
       {(void**)&nb.mx_partial, m.mx.ok ? 2 * kMxPartialBytes : 0},

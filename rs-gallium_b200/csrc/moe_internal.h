@@ -137,6 +137,9 @@ struct Groups {
   int64_t ret_slots = 0;  // slots per rank (bounds every store)
 };
 
+// Positions per tile of the small-batch Q4_K tensor-core kernel (q4k_tc.cu).
+constexpr int kQ4SmallBN = 32;
+
 // Buffers indexed by grouped position, sized for rows_cap positions.
 struct ExpertBufs {
   int64_t rows_cap = 0;
@@ -156,6 +159,12 @@ struct ExpertBufs {
   alignas(64) unsigned char map_xl[128] = {};
   alignas(64) unsigned char map_hh[128] = {};
   alignas(64) unsigned char map_hl[128] = {};
+  // the same four as tiles of kQ4SmallBN rows (small-batch Q4_K kernel)
+  alignas(64) unsigned char map_xh_s[128] = {};
+  alignas(64) unsigned char map_xl_s[128] = {};
+  alignas(64) unsigned char map_hh_s[128] = {};
+  alignas(64) unsigned char map_hl_s[128] = {};
+  float* xsum = nullptr;       // [rows][max(H, I) / 32] sub-block sums of x or h (Q4_K)
   uint8_t* xq = nullptr;       // [rows][4][H] E4M3 pieces of the grouped activations
   uint8_t* hq = nullptr;       // [rows][4][I] E4M3 pieces of the SwiGLU output
   alignas(64) unsigned char map_xq[6][128] = {};  // CUtensorMaps, tiles of 2, 4, 8, 16, 30,
@@ -287,6 +296,9 @@ cudaError_t q4k_tc_prepare(Moe& m);
 cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                   cudaStream_t st);
 cudaError_t launch_q4k_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st);
+// Whether this batch runs the small-batch Q4_K kernel (weights as exact
+// integers, at most kQ4SmallBN positions per tile) rather than the f16 hi + lo one.
+bool use_q4k_small(const Moe& m, const Groups& g);
 // Activation rows (through perm) -> f16 hi / lo with a per-row power of two
 // (tc_gemm.cu), the B operand of the kind::f16 kernels.
 cudaError_t launch_split_gather(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,

@@ -71,6 +71,7 @@ struct Args {
   const int32_t* out_rows;
   int out_stride;
   int* err;
+  const float* xsum;      // small-batch kernel: [positions][K / 32] sub-block sums of B
 };
 
 // kind::f16, A = B = f16, D = f32, K-major, M = BM; N (bits 17-22) per tile:
@@ -488,6 +489,376 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Small batches (at most kSmallBN positions per tile): the weights go onto
+// the tensor cores as the exact integers sc * q, one f16 each.
+//
+// Over one super-block (256 K) the weight of row r at k is
+// d * (sc_s q_k) - dmin * m_s (s = k's sub-block), so
+//   y[r][p] = sum_sb ( d_sb * A_sb[r][p] - dmin_sb * sum_s m_s * S[p][s] )
+// with A_sb = sum over the super-block of (sc q) x (tcgen05, kind::f16, x as
+// f16 hi + lo into two accumulators) and S[p][s] the sub-block sums of
+// x = hi + lo.  sc q <= 945 is exact in f16, so each weight costs one byte
+// permute, one logic op and half a paired f16 FMA, where the f16 hi + lo
+// decode of the kernel above costs about four times that; the MMAs read one
+// A operand instead of two.  The epilogue warps read each super-block's
+// accumulators out of TMEM and fold them into registers (one per position),
+// so the tile is at most 32 positions wide.  The sums are the reference's
+// dequantise-then-multiply regrouped (exact weights, x as hi + lo as in the
+// kernel above); they differ from it by f32 rounding only.
+//
+// Roles as above: warps 4-11 decode, 12 copies B by TMA, 13 issues the MMAs,
+// 0-3 fold the super-blocks and finish the tile.  Six 24 KB stages; two TMEM
+// buffers of (hi, lo) accumulators so that one super-block's MMAs run while
+// the previous one is folded.
+constexpr int kSmallBN = 32;
+constexpr int kSmallStages = 6;
+constexpr int SA_BYTES = BM * BK * 2;
+constexpr int SB_BYTES = kSmallBN * BK * 2;
+constexpr int SSTAGE_BYTES = SA_BYTES + 2 * SB_BYTES;  // A, B hi, B lo
+constexpr int kSmallTmemCols = 4 * kSmallBN;           // 2 buffers x (hi, lo)
+
+__host__ __device__ constexpr size_t small_smem_bytes(int K) {
+  // stages, the tile's sub-block sums [kSmallBN][K / 32], barriers
+  return (size_t)kSmallStages * SSTAGE_BYTES + (size_t)kSmallBN * (K / 32) * 4 + 1024 + 256;
+}
+
+// The 32 values sc * q of sub-block 2c + h of a super-block as f16, packed
+// two per word in element order: byte b's nibble goes to a half of
+// 0x6400 | q (the f16 1024 + q) and one paired FMA (1024 + q) sc - 1024 sc
+// leaves sc q exactly (every intermediate is an integer below 2^16).
+__device__ __forceinline__ void decode_int_half(const uint4& hdr, const uint4& qa, const uint4& qb,
+                                                int c, int h, uint32_t (&v)[16]) {
+  int sc, mn;
+  q4k_scale_min_hdr(hdr, c, h, sc, mn);
+  const __half2 s2 = __float2half2_rn((float)sc);
+  const __half2 o2 = __float2half2_rn(-1024.0f * (float)sc);
+  const int shift = 4 * h;
+  const uint32_t words[8] = {qa.x >> shift, qa.y >> shift, qa.z >> shift, qa.w >> shift,
+                             qb.x >> shift, qb.y >> shift, qb.z >> shift, qb.w >> shift};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {  // elements 2i, 2i + 1: bytes 2i, 2i + 1
+    const uint32_t w = words[i >> 1];
+    // bytes (0, 1) or (2, 3) of the word to bits 0-7 and 16-23
+    const uint32_t r = __byte_perm(w, 0u, (i & 1) ? 0x4342u : 0x4140u);
+    const uint32_t f = (r & 0x000F000Fu) | 0x64006400u;
+    const __half2 x = __hfma2(*reinterpret_cast<const __half2*>(&f), s2, o2);
+    v[i] = *reinterpret_cast<const uint32_t*>(&x);
+  }
+}
+
+// Sixteen columns of one super-block folded into y: y[j] += d A[j] -
+// dmin sum_s m_s S[j][s], A = hi + lo read from TMEM, S from shared memory.
+template <int J0>
+__device__ __forceinline__ void fold16(uint32_t hi_addr, uint32_t lo_addr, float d, float dmin,
+                                       const float (&mf)[8], const float* xs, int nsub, int sb,
+                                       int ncols, float (&y)[kSmallBN]) {
+  uint32_t vh[16], vl[16];
+  tmem_ld16(hi_addr + (uint32_t)J0, vh);
+  tmem_ld16(lo_addr + (uint32_t)J0, vl);
+  tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (J0 + j < ncols) {
+      const float4* sp = reinterpret_cast<const float4*>(xs + (J0 + j) * nsub + sb * 8);
+      const float4 s0 = sp[0], s1 = sp[1];
+      float t = mf[0] * s0.x;
+      t = fmaf(mf[1], s0.y, t);
+      t = fmaf(mf[2], s0.z, t);
+      t = fmaf(mf[3], s0.w, t);
+      t = fmaf(mf[4], s1.x, t);
+      t = fmaf(mf[5], s1.y, t);
+      t = fmaf(mf[6], s1.z, t);
+      t = fmaf(mf[7], s1.w, t);
+      const float acc = __uint_as_float(vh[j]) + __uint_as_float(vl[j]);
+      y[J0 + j] += fmaf(d, acc, -dmin * t);
+    }
+  }
+}
+
+// The mins m_0 .. m_7 of a super-block from its header (get_scale_min_k4).
+__device__ __forceinline__ void q4k_mins(const uint4& hdr, float (&mf)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int sh = 8 * (j & 3);
+    uint32_t mv;
+    if (j < 4) {
+      mv = (hdr.z >> sh) & 63u;
+    } else {
+      mv = ((hdr.w >> sh) >> 4 & 0xFu) | (((hdr.z >> sh) >> 6 & 3u) << 4);
+    }
+    mf[j] = (float)mv;
+  }
+}
+
+template <int MODE, int ACT>
+__global__ void __launch_bounds__(kThreads, 1)
+    q4k_tc_small(const __grid_constant__ CUtensorMap tmap_hi,
+                 const __grid_constant__ CUtensorMap tmap_lo, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int nsub = a.K / 32;
+  float* xs = reinterpret_cast<float*>(smem + kSmallStages * SSTAGE_BYTES);  // [kSmallBN][nsub]
+  uint64_t* tma_full = reinterpret_cast<uint64_t*>(xs + kSmallBN * nsub);
+  uint64_t* a_full = tma_full + kSmallStages;
+  uint64_t* empty = a_full + kSmallStages;
+  uint64_t* acc_full = empty + kSmallStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_items = a.meta[2] * a.m_tiles;
+  const int nk = a.K / BK;
+  const int nsb = a.K / 256;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSmallStages; ++s) {
+      mbar_init(&tma_full[s], 1);
+      mbar_init(&a_full[s], kDecoders);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) tmem_alloc(tmem_slot, kSmallTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 12) {
+    // ---------------- TMA producer: B hi / lo ---------------------------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+        const Item it = decode_item(a, item);
+        for (int kc = 0; kc < nk; ++kc) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sb = smem + stage * SSTAGE_BYTES + SA_BYTES;
+          mbar_arrive_expect_tx(&tma_full[stage], 2 * SB_BYTES);
+          tma_load_2d(sb, &tmap_hi, kc * BK, it.row0, &tma_full[stage]);
+          tma_load_2d(sb + SB_BYTES, &tmap_lo, kc * BK, it.row0, &tma_full[stage]);
+          if (++stage == kSmallStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == 13) {
+    // ---------------- MMA issuer: one accumulator pair per super-block --------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int sbi = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+        const uint32_t idesc = idesc_for(decode_item(a, item).nrows);
+        for (int sb = 0; sb < nsb && ok; ++sb, ++sbi) {
+          const int b = sbi & 1;
+          if (!mbar_wait(&acc_empty[b], ((sbi >> 1) & 1) ^ 1, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_hi = tmem_base + (uint32_t)(b * 2 * kSmallBN);
+          const uint32_t d_lo = d_hi + (uint32_t)kSmallBN;
+          for (int kq = 0; kq < 4; ++kq) {
+            if (!mbar_wait(&a_full[stage], phase, abort_flag, a.err) ||
+                !mbar_wait(&tma_full[stage], phase, abort_flag, a.err)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(smem + stage * SSTAGE_BYTES);
+            const uint32_t sbh = sa + SA_BYTES;
+            const uint32_t sbl = sbh + SB_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t da = sw128_desc(sa + kk * 32);
+              const uint32_t acc = (kq | kk) != 0;
+              mma_f16(d_hi, da, sw128_desc(sbh + kk * 32), idesc, acc);
+              mma_f16(d_lo, da, sw128_desc(sbl + kk * 32), idesc, acc);
+            }
+            mma_commit(&empty[stage]);
+            if (++stage == kSmallStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (ok) mma_commit(&acc_full[b]);
+        }
+      }
+      if (!ok || *abort_flag) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- weight decode: threads r, r + 128 own row r -----------
+    const int r = (threadIdx.x - 128) & 127;
+    const int hsel = (threadIdx.x - 128) >> 7;  // 0: low nibbles, 1: high
+    const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
+      const Item it = decode_item(a, item);
+      const int row = it.m_tile * BM + r;
+      const bool valid = row < a.rows;
+      const uint8_t* rowp = a.q + ((int64_t)it.le * a.rows + (valid ? row : 0)) * row_bytes;
+      auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) {
+        const uint8_t* blk = rowp + (kc >> 2) * 144;
+        hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+        qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
+        qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
+      };
+      // the register ring of the kernel above: three K steps in flight
+      uint4 hdr[4], qa[4], qb[4];
+#pragma unroll
+      for (int u = 0; u < 3; ++u)
+        if (u < nk) load(u, hdr[u], qa[u], qb[u]);
+      for (int kc0 = 0; kc0 < nk && ok; kc0 += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int kc = kc0 + u;
+          if (kc + 3 < nk) load(kc + 3, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
+          uint32_t v[16];
+          decode_int_half(hdr[u], qa[u], qb[u], u, hsel, v);
+          if (!valid) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = 0u;
+          }
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * SSTAGE_BYTES;
+          const int rb = (r >> 3) * 1024 + (r & 7) * 128;
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * hsel + cc;
+            *reinterpret_cast<uint4*>(sa + rb + ((c ^ (r & 7)) << 4)) =
+                make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(&a_full[stage]);
+          if (++stage == kSmallStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: thread = TMEM lane = weight row ---------------
+    const int m = threadIdx.x;
+    const int odd = m & 1;
+    const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
+    int sbi = 0;
+    bool ok = true;
+    // every epilogue thread runs every item (the named barriers below need
+    // all 128); after a failed wait a thread only walks the loops
+    for (int item = blockIdx.x; item < total_items; item += gridDim.x) {
+      const Item it = decode_item(a, item);
+      const int row = it.m_tile * BM + m;
+      const bool valid = row < a.rows;
+      const int ncols = it.nrows < kSmallBN ? it.nrows : kSmallBN;
+      // the tile's sub-block sums into shared memory (after every epilogue
+      // thread has finished with the previous tile's)
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      {
+        const float4* src = reinterpret_cast<const float4*>(a.xsum + (int64_t)it.row0 * nsub);
+        float4* dst = reinterpret_cast<float4*>(xs);
+        const int n4 = ncols * nsub / 4;
+        for (int i = m; i < n4; i += 128) dst[i] = __ldg(src + i);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const uint8_t* hp = a.q + ((int64_t)it.le * a.rows + (valid ? row : 0)) * row_bytes;
+      float y[kSmallBN];
+#pragma unroll
+      for (int j = 0; j < kSmallBN; ++j) y[j] = 0.0f;
+      uint4 hnext = __ldg(reinterpret_cast<const uint4*>(hp));
+      for (int sb = 0; sb < nsb; ++sb, ++sbi) {
+        const uint4 hdr = hnext;
+        if (sb + 1 < nsb) hnext = __ldg(reinterpret_cast<const uint4*>(hp + (sb + 1) * 144));
+        const int b = sbi & 1;
+        if (ok && !mbar_wait(&acc_full[b], (sbi >> 1) & 1, abort_flag, a.err)) ok = false;
+        if (!ok) continue;
+        tc_fence_after();
+        const float d = f16_bits_to_f32(hdr.x & 0xFFFFu);
+        const float dmin = f16_bits_to_f32(hdr.x >> 16);
+        float mf[8];
+        q4k_mins(hdr, mf);
+        const uint32_t hi_addr =
+            tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 2 * kSmallBN);
+        const uint32_t lo_addr = hi_addr + (uint32_t)kSmallBN;
+        fold16<0>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, ncols, y);
+        if (ncols > 16) fold16<16>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, ncols, y);
+        tc_fence_before();
+        mbar_arrive(&acc_empty[b]);
+      }
+      if (!ok) continue;
+      if (MODE == GATE_UP) {
+        // rows 2i (gate) and 2i + 1 (up) in neighbouring lanes: the even lane
+        // finishes column j, the odd lane column j + 1
+#pragma unroll
+        for (int j = 0; j < kSmallBN; j += 2) {
+          if (j >= ncols) break;
+          const int64_t p0 = (int64_t)it.row0 + j;
+          const float v0 = j < ncols ? __fmul_rn(y[j], pow2f((int)__ldg(a.xscale + p0))) : 0.0f;
+          const float v1 =
+              j + 1 < ncols ? __fmul_rn(y[j + 1], pow2f((int)__ldg(a.xscale + p0 + 1))) : 0.0f;
+          const float recv = __shfl_xor_sync(kFullMask, odd ? v0 : v1, 1);
+          const float g = odd ? recv : v0;
+          const float u = odd ? v1 : recv;
+          const int n = j + odd;
+          if (valid && n < ncols) {
+            const float h = activation<ACT>(a, g, u);
+            const __half hi = __float2half_rn(h);
+            const __half lo = __float2half_rn(__fsub_rn(h, __half2float(hi)));
+            const int64_t o = ((int64_t)it.row0 + n) * a.out_stride + (row >> 1);
+            a.out_hi[o] = hi;
+            a.out_lo[o] = lo;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kSmallBN; ++j) {
+          if (j >= ncols) break;
+          const int64_t pos = (int64_t)it.row0 + j;
+          const int64_t orow = a.out_rows ? (int64_t)__ldg(a.out_rows + pos) : pos;
+          if (valid) a.out_y[orow * a.out_stride + row] = y[j];
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kSmallTmemCols);
+  }
+}
+
 // Decode exponent e of one local expert's matrix: the largest |d| * 63 * 15 +
 // |dmin| * 63 over its super-blocks bounds |w|; e puts that bound at or below
 // 2^14.  One CTA per local expert.
@@ -520,6 +891,35 @@ __global__ void wexp_kernel(const uint8_t* __restrict__ q, int64_t blocks_per_ex
     wexp[le] = max(-60, min(60, e));
   }
 }
+
+// Sub-block sums of the split rows: out[p][s] = sum over i < 32 of
+// (hi + lo)[p][32 s + i], in order, in f32 (hi + lo is exact in f32).
+__global__ void sub_sums_kernel(const __half* __restrict__ hi, const __half* __restrict__ lo,
+                                int K, int64_t n, float* __restrict__ out) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  const int nsub = K / 32;
+  const int64_t p = t / nsub;
+  const int sub = (int)(t - p * nsub);
+  const uint4* h4 = reinterpret_cast<const uint4*>(hi + p * K + sub * 32);
+  const uint4* l4 = reinterpret_cast<const uint4*>(lo + p * K + sub * 32);
+  float acc = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 hv = __ldg(h4 + c), lv = __ldg(l4 + c);
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w}, lw[4] = {lv.x, lv.y, lv.z, lv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&hw[e]));
+      const float2 lf = __half22float2(*reinterpret_cast<const __half2*>(&lw[e]));
+      acc = __fadd_rn(acc, __fadd_rn(hf.x, lf.x));
+      acc = __fadd_rn(acc, __fadd_rn(hf.y, lf.y));
+    }
+  }
+  out[t] = acc;
+}
+
+static_assert(kSmallBN == kQ4SmallBN, "small-batch tile width");
 
 }  // namespace q4tc
 
@@ -572,6 +972,36 @@ cudaError_t launch_q4tc_act(const Moe& m, const q4tc::Args& a, const void* map_h
   return cudaGetLastError();
 }
 
+template <int MODE, int ACT>
+cudaError_t launch_q4tc_small_act(const Moe& m, const q4tc::Args& a, const void* map_hi,
+                                  const void* map_lo, cudaStream_t st) {
+  auto k = q4tc::q4k_tc_small<MODE, ACT>;
+  const size_t smem = q4tc::small_smem_bytes(a.K);
+  cudaError_t e = set_smem_limit(k, smem);
+  if (e != cudaSuccess) return e;
+  k<<<m.sm_count, q4tc::kThreads, smem, st>>>(*reinterpret_cast<const CUtensorMap*>(map_hi),
+                                              *reinterpret_cast<const CUtensorMap*>(map_lo), a);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_q4tc_small(const Moe& m, const q4tc::Args& a, const void* map_hi,
+                              const void* map_lo, cudaStream_t st) {
+  if (MODE != q4tc::GATE_UP || a.act_kind == GB_ACT_GPTOSS_CLAMP)
+    return launch_q4tc_small_act<MODE, q4tc::ACT_GPTOSS>(m, a, map_hi, map_lo, st);
+  if (a.act_kind == GB_ACT_SILU && !(a.clamp > 0.0f))
+    return launch_q4tc_small_act<MODE, q4tc::ACT_SILU>(m, a, map_hi, map_lo, st);
+  return launch_q4tc_small_act<MODE, q4tc::ACT_GENERIC>(m, a, map_hi, map_lo, st);
+}
+
+cudaError_t launch_sub_sums(const __half* hi, const __half* lo, int K, int64_t positions,
+                            float* out, cudaStream_t st) {
+  const int64_t n = positions * (K / 32);
+  if (n <= 0) return cudaSuccess;
+  q4tc::sub_sums_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(hi, lo, K, n, out);
+  return cudaGetLastError();
+}
+
 template <int MODE>
 cudaError_t launch_q4tc(const Moe& m, const q4tc::Args& a, const void* map_hi, const void* map_lo,
                         cudaStream_t st) {
@@ -584,11 +1014,25 @@ cudaError_t launch_q4tc(const Moe& m, const q4tc::Args& a, const void* map_hi, c
 
 }  // namespace
 
+bool use_q4k_small(const Moe& m, const Groups& g) {
+  const gb_moe_desc& d = m.desc;
+  if (m.expert_path == GB_PATH_TENSOR_CORES_F16) return false;
+  if (q4tc::small_smem_bytes(std::max(d.hidden, d.inter)) > (size_t)227 * 1024) return false;
+  // up to 16 rows per expert on average: folding 32-column accumulators
+  // every super-block costs more than the f16 decode saves (measured at 32
+  // rows per expert: 430 vs 344 us per layer; at 2 and 4 rows 289 vs 326 and
+  // 314 vs 331 us)
+  const int64_t nloc = std::max(1, m.e_end - m.e_begin);
+  return g.rows <= (int64_t)(q4tc::kSmallBN / 2) * nloc;
+}
+
 cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,
                                   cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
+  const bool small = use_q4k_small(m, g);
   cudaError_t e;
-  if ((e = launch_tile_table(m, g, q4tc::BN, eb, st)) != cudaSuccess) return e;
+  if ((e = launch_tile_table(m, g, small ? q4tc::kSmallBN : q4tc::BN, eb, st)) != cudaSuccess)
+    return e;
   if ((e = launch_split_gather(m, g, x, eb, st)) != cudaSuccess) return e;
   q4tc::Args a = q4tc_args(m, g, eb);
   a.q = m.w.q4_gu;
@@ -600,6 +1044,12 @@ cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x,
   a.out_hi = eb.hh;
   a.out_lo = eb.hl;
   a.out_stride = d.inter;
+  if (small) {
+    if ((e = launch_sub_sums(eb.xh, eb.xl, d.hidden, g.rows, eb.xsum, st)) != cudaSuccess)
+      return e;
+    a.xsum = eb.xsum;
+    return launch_q4tc_small<q4tc::GATE_UP>(m, a, eb.map_xh_s, eb.map_xl_s, st);
+  }
   return launch_q4tc<q4tc::GATE_UP>(m, a, eb.map_xh, eb.map_xl, st);
 }
 
@@ -614,6 +1064,12 @@ cudaError_t launch_q4k_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cu
   a.out_y = eb.y;
   a.out_rows = g.out_rows;
   a.out_stride = d.hidden;
+  if (use_q4k_small(m, g)) {
+    cudaError_t e = launch_sub_sums(eb.hh, eb.hl, d.inter, g.rows, eb.xsum, st);
+    if (e != cudaSuccess) return e;
+    a.xsum = eb.xsum;
+    return launch_q4tc_small<q4tc::DOWN>(m, a, eb.map_hh_s, eb.map_hl_s, st);
+  }
   return launch_q4tc<q4tc::DOWN>(m, a, eb.map_hh, eb.map_hl, st);
 }
 

@@ -89,19 +89,45 @@ def test_q4k_ragged_rows_are_refused():
     assert "256-element" in str(ei.value)
 
 
+@pytest.mark.parametrize("path", ["tensor_cores", "tensor_cores_f16"])
 @pytest.mark.parametrize("T", [1, 8, 64, 300])
-def test_lfm2_tensor_core_path_matches_oracle(layer, T):
-    # Q4_K weights decoded into f16 hi + lo for kind::f16 MMAs; AUTO takes
-    # this path from 8 rows per expert (T = 64, 300 here), forced below
+def test_lfm2_tensor_core_path_matches_oracle(layer, T, path):
+    # Two kind::f16 kernels: "tensor_cores" runs the weights as the exact
+    # integers sc * q with the super-block scales applied to the partial sums
+    # while the batch averages at most 16 rows per expert (T = 1, 8, 64 here)
+    # and the f16 hi + lo decode above that (T = 300); "tensor_cores_f16"
+    # forces the hi + lo decode.  AUTO takes the tensor cores from 8 rows per
+    # expert.
     m = Lfm2QMoEFFN.load(layer, device=0, max_tokens=T)
     try:
-        m.set_expert_path("tensor_cores")
+        m.set_expert_path(path)
         x = synth.tokens(T, 2048, seed=1300 + T)
         got = m.forward(_cuda(x)).cpu().numpy()
         want, _, _ = oracle.OracleLfm2(layer).forward(x)
-        _parity(got, want, f"tensor cores T={T}")
+        _parity(got, want, f"{path} T={T}")
         m.set_expert_path("cuda_cores")
         cc = m.forward(_cuda(x)).cpu().numpy()
-        _parity(got, cc.astype(np.float64), f"tensor vs CUDA cores T={T}")
+        _parity(got, cc.astype(np.float64), f"{path} vs CUDA cores T={T}")
+    finally:
+        m.close()
+
+
+def test_lfm2_small_batch_kernel_splits_a_crowded_expert(layer):
+    # every token picks expert 0 (selection bias), so it gets 64 rows: two
+    # tiles of 32 in the small-batch kernel while the batch averages 8 rows
+    # per expert
+    import copy
+    lay = copy.deepcopy(layer)
+    lay.sel_bias[:] = 0.0
+    lay.sel_bias[0] = 30.0
+    T = 64
+    m = Lfm2QMoEFFN.load(lay, device=0, max_tokens=T)
+    try:
+        m.set_expert_path("tensor_cores")
+        x = synth.tokens(T, 2048, seed=1777)
+        got = m.forward(_cuda(x)).cpu().numpy()
+        want, idx, _ = oracle.OracleLfm2(lay).forward(x)
+        assert (np.asarray(idx) == 0).any(axis=1).all()
+        _parity(got, want, "crowded expert")
     finally:
         m.close()
