@@ -616,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kSmallStages; ++s) {
       mbar_init(&tma_full[s], 1);
-      mbar_init(&a_full[s], kDecoders);
+      mbar_init(&a_full[s], kDecoders / 2);  // one decoder group per stage
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -712,11 +712,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- weight decode: threads r, r + 128 own row r -----------
+    // ---------------- weight decode --------------------------------------------
+    // Group g = 0, 1 (warps 4-7, 8-11) takes the K steps of parity g; thread
+    // r of a group decodes both sub-blocks of row r in its steps.  Its ring
+    // of four steps of bytes then reaches six K steps ahead of the MMAs.
     const int r = (threadIdx.x - 128) & 127;
-    const int hsel = (threadIdx.x - 128) >> 7;  // 0: low nibbles, 1: high
+    const int grp = (threadIdx.x - 128) >> 7;
     const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
-    int stage = 0;
+    const int nks = nk / 2;  // K steps per group (nk is a multiple of four)
+    int stage = grp;         // global step index gs = grp (mod 2), stage = gs % 6
     uint32_t phase = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
@@ -730,39 +734,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
         qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
       };
-      // the register ring of the kernel above: three K steps in flight
       uint4 hdr[4], qa[4], qb[4];
 #pragma unroll
       for (int u = 0; u < 3; ++u)
-        if (u < nk) load(u, hdr[u], qa[u], qb[u]);
-      for (int kc0 = 0; kc0 < nk && ok; kc0 += 4) {
+        if (u < nks) load(grp + 2 * u, hdr[u], qa[u], qb[u]);
+      for (int j0 = 0; j0 < nks && ok; j0 += 4) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int kc = kc0 + u;
-          if (kc + 3 < nk) load(kc + 3, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
-          uint32_t v[16];
-          decode_int_half(hdr[u], qa[u], qb[u], u, hsel, v);
-          if (!valid) {
+          const int j = j0 + u;
+          if (j < nks) {
+            const int kc = grp + 2 * j;
+            if (j + 3 < nks)
+              load(kc + 6, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
+              ok = false;
+              break;
+            }
+            uint8_t* sa = smem + stage * SSTAGE_BYTES + (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] = 0u;
-          }
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sa = smem + stage * SSTAGE_BYTES;
-          const int rb = (r >> 3) * 1024 + (r & 7) * 128;
+            for (int h = 0; h < 2; ++h) {  // sub-block 2c + h: chunks 4h .. 4h + 3 of the row
+              uint32_t v[16];
+              decode_int_half(hdr[u], qa[u], qb[u], kc & 3, h, v);
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const int c = 4 * hsel + cc;
-            *reinterpret_cast<uint4*>(sa + rb + ((c ^ (r & 7)) << 4)) =
-                make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(&a_full[stage]);
-          if (++stage == kSmallStages) {
-            stage = 0;
-            phase ^= 1;
+              for (int cc = 0; cc < 4; ++cc)
+                *reinterpret_cast<uint4*>(sa + (((4 * h + cc) ^ (r & 7)) << 4)) =
+                    valid ? make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3])
+                          : make_uint4(0u, 0u, 0u, 0u);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&a_full[stage]);
+            stage += 2;
+            if (stage >= kSmallStages) {
+              stage -= kSmallStages;
+              phase ^= 1;
+            }
           }
         }
       }
@@ -920,6 +925,7 @@ __global__ void sub_sums_kernel(const __half* __restrict__ hi, const __half* __r
 }
 
 static_assert(kSmallBN == kQ4SmallBN, "small-batch tile width");
+static_assert(kSmallStages % 2 == 0, "each decoder group keeps to its own stages");
 
 }  // namespace q4tc
 
