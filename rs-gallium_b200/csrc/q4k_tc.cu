@@ -513,6 +513,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // the previous one is folded.
 constexpr int kSmallBN = 32;
 constexpr int kSmallStages = 6;
+// K steps of weight bytes in each decoder thread's register ring (six
+// spilled registers and ran slower)
+constexpr int kSmallRing = 4;
 constexpr int SA_BYTES = BM * BK * 2;
 constexpr int SB_BYTES = kSmallBN * BK * 2;
 constexpr int SSTAGE_BYTES = SA_BYTES + 2 * SB_BYTES;  // A, B hi, B lo
@@ -715,7 +718,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- weight decode --------------------------------------------
     // Group g = 0, 1 (warps 4-7, 8-11) takes the K steps of parity g; thread
     // r of a group decodes both sub-blocks of row r in its steps.  Its ring
-    // of four steps of bytes then reaches six K steps ahead of the MMAs.
+    // of kSmallRing steps of bytes then reaches 2 (kSmallRing - 1) K steps
+    // ahead of the MMAs.
     const int r = (threadIdx.x - 128) & 127;
     const int grp = (threadIdx.x - 128) >> 7;
     const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
@@ -734,18 +738,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
         qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
       };
-      uint4 hdr[4], qa[4], qb[4];
+      uint4 hdr[kSmallRing], qa[kSmallRing], qb[kSmallRing];
 #pragma unroll
-      for (int u = 0; u < 3; ++u)
+      for (int u = 0; u < kSmallRing - 1; ++u)
         if (u < nks) load(grp + 2 * u, hdr[u], qa[u], qb[u]);
-      for (int j0 = 0; j0 < nks && ok; j0 += 4) {
+      for (int j0 = 0; j0 < nks && ok; j0 += kSmallRing) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kSmallRing; ++u) {
           const int j = j0 + u;
           if (j < nks) {
             const int kc = grp + 2 * j;
-            if (j + 3 < nks)
-              load(kc + 6, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
+            constexpr int n = kSmallRing - 1;  // steps in flight ahead of this one
+            if (j + n < nks)
+              load(kc + 2 * n, hdr[(u + n) % kSmallRing], qa[(u + n) % kSmallRing],
+                   qb[(u + n) % kSmallRing]);
             if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
               ok = false;
               break;
