@@ -16,13 +16,14 @@
 //
 // Tiles and roles follow tc_gemm.cu: D[m, n] = sum_k W[m, k] X[n, k] with
 // M = 128 weight rows, N = 128 grouped positions of one expert, K stepped by
-// 64 (one Q4_K sub-block pair).  Warps 4-11 decode: threads r and r + 128
-// load row r's super-block header and 32 quant bytes straight from HBM (the
-// next three K steps' bytes in flight while they decode, in a register ring
-// walked with compile-time slots), each decodes one sub-block (the low or
-// the high nibbles) and, once the MMAs have released the stage, writes its
-// half of A hi / lo into shared memory in the K-major 128-byte-swizzled
-// layout (decoding, not the MMAs, bounds this kernel, hence eight warps);
+// 64 (one Q4_K sub-block pair).  Warps 4-11 decode, as two groups taking
+// alternate K steps: thread r of a group loads row r's super-block header
+// and 32 quant bytes straight from HBM (its next three steps' bytes in
+// flight, six K steps ahead, in a register ring walked with compile-time
+// slots) and, once the MMAs have released the stage, decodes both
+// sub-blocks into A hi / lo in shared memory in the K-major
+// 128-byte-swizzled layout (decoding, not the MMAs, bounds this kernel,
+// hence eight warps);
 // warp 12 copies B hi / lo by TMA; warp 13 issues the MMAs; warps 0-3 run
 // the epilogue (bias-free SiLU or clamped SwiGLU into h hi / lo, or y).  Three 64 KB stages; two TMEM
 // accumulator pairs so the epilogue of one tile overlaps the next tile's MMAs.
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&tma_full[s], 1);
-      mbar_init(&a_full[s], kDecoders);
+      mbar_init(&a_full[s], kDecoders / 2);  // one decoder group per stage
       mbar_init(&empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -403,11 +404,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- weight decode: threads r, r + 128 own row r -----------
+    // ---------------- weight decode --------------------------------------------
+    // Group g = 0, 1 (warps 4-7, 8-11) takes the K steps of parity g; thread
+    // r of a group decodes both sub-blocks of row r in its steps, so its ring
+    // of four steps of bytes reaches six K steps ahead of the MMAs.  The ring
+    // is walked with compile-time slots, so no register copy waits for a
+    // load still in flight.
     const int r = (threadIdx.x - 128) & 127;
-    const int hsel = (threadIdx.x - 128) >> 7;  // 0: low nibbles, 1: high
+    const int grp = (threadIdx.x - 128) >> 7;
     const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
-    int stage = 0;
+    const int nks = nk / 2;  // K steps per group (nk is a multiple of four)
+    int stage = grp;         // global step index gs = grp (mod 2), stage = gs % STAGES
     uint32_t phase = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
@@ -423,42 +430,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
         qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
       };
-      // A ring of four K steps of bytes, three in flight ahead of the one
-      // being decoded.  The loop walks the ring with compile-time slots (four
-      // K steps per pass; nk is a multiple of four since K % 256 == 0), so no
-      // register copy has to wait for a load still in flight.
       uint4 hdr[4], qa[4], qb[4];
 #pragma unroll
       for (int u = 0; u < 3; ++u)
-        if (u < nk) load(u, hdr[u], qa[u], qb[u]);
-      for (int kc0 = 0; kc0 < nk && ok; kc0 += 4) {
+        if (u < nks) load(grp + 2 * u, hdr[u], qa[u], qb[u]);
+      for (int j0 = 0; j0 < nks && ok; j0 += 4) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const int kc = kc0 + u;
-          if (kc + 3 < nk) load(kc + 3, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
-          uint32_t hi[16], lo[16];
-          decode_half(hdr[u], qa[u], qb[u], u, hsel, scale, hi, lo);  // pair kc % 4 == u
-          // the slot is free once the MMAs that read it have completed
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
-            ok = false;
-            break;
-          }
-          uint8_t* sah = smem + stage * STAGE_BYTES;
-          const int rb = (r >> 3) * 1024 + (r & 7) * 128;
+          const int j = j0 + u;
+          if (j < nks) {
+            const int kc = grp + 2 * j;
+            if (j + 3 < nks) load(kc + 6, hdr[(u + 3) & 3], qa[(u + 3) & 3], qb[(u + 3) & 3]);
+            // the slot is free once the MMAs that read it have completed
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, a.err)) {
+              ok = false;
+              break;
+            }
+            uint8_t* sah = smem + stage * STAGE_BYTES;
+            const int rb = (r >> 3) * 1024 + (r & 7) * 128;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {  // 16-byte chunks 4 hsel .. 4 hsel + 3 of the row
-            const int c = 4 * hsel + cc;
-            const int off = rb + ((c ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(sah + off) =
-                make_uint4(hi[4 * cc], hi[4 * cc + 1], hi[4 * cc + 2], hi[4 * cc + 3]);
-            *reinterpret_cast<uint4*>(sah + A_BYTES + off) =
-                make_uint4(lo[4 * cc], lo[4 * cc + 1], lo[4 * cc + 2], lo[4 * cc + 3]);
-          }
-          fence_proxy_async_smem();
-          mbar_arrive(&a_full[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+            for (int h = 0; h < 2; ++h) {  // sub-block 2c + h: chunks 4h .. 4h + 3 of the row
+              uint32_t hi[16], lo[16];
+              decode_half(hdr[u], qa[u], qb[u], kc & 3, h, scale, hi, lo);
+#pragma unroll
+              for (int cc = 0; cc < 4; ++cc) {
+                const int off = rb + (((4 * h + cc) ^ (r & 7)) << 4);
+                *reinterpret_cast<uint4*>(sah + off) =
+                    make_uint4(hi[4 * cc], hi[4 * cc + 1], hi[4 * cc + 2], hi[4 * cc + 3]);
+                *reinterpret_cast<uint4*>(sah + A_BYTES + off) =
+                    make_uint4(lo[4 * cc], lo[4 * cc + 1], lo[4 * cc + 2], lo[4 * cc + 3]);
+              }
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&a_full[stage]);
+            stage += 2;  // STAGES > 2: one wrap at most
+            if (stage >= STAGES) {
+              stage -= STAGES;
+              phase ^= 1;
+            }
           }
         }
       }
