@@ -139,6 +139,9 @@ struct Groups {
 
 // Positions per tile of the small-batch Q4_K tensor-core kernel (q4k_tc.cu).
 constexpr int kQ4SmallBN = 32;
+// Rows per TMA box of that kernel's activation maps (a tile's f16 hi and lo
+// rows are loaded back to back, 16 rows at a time).
+constexpr int kQ4SmallBox = 16;
 
 // Buffers indexed by grouped position, sized for rows_cap positions.
 struct ExpertBufs {
@@ -159,7 +162,7 @@ struct ExpertBufs {
   alignas(64) unsigned char map_xl[128] = {};
   alignas(64) unsigned char map_hh[128] = {};
   alignas(64) unsigned char map_hl[128] = {};
-  // the same four as tiles of kQ4SmallBN rows (small-batch Q4_K kernel)
+  // the same four in boxes of kQ4SmallBox rows (small-batch Q4_K kernel)
   alignas(64) unsigned char map_xh_s[128] = {};
   alignas(64) unsigned char map_xl_s[128] = {};
   alignas(64) unsigned char map_hh_s[128] = {};

@@ -567,10 +567,10 @@ cudaError_t tc_make_maps(const Moe& m, ExpertBufs& eb) {
   if ((e = make(eb.map_hh, eb.hh, d.inter, tc::BN)) != cudaSuccess) return e;
   if ((e = make(eb.map_hl, eb.hl, d.inter, tc::BN)) != cudaSuccess) return e;
   if (d.weight_format != GB_FMT_Q4_K) return cudaSuccess;
-  if ((e = make(eb.map_xh_s, eb.xh, d.hidden, kQ4SmallBN)) != cudaSuccess) return e;
-  if ((e = make(eb.map_xl_s, eb.xl, d.hidden, kQ4SmallBN)) != cudaSuccess) return e;
-  if ((e = make(eb.map_hh_s, eb.hh, d.inter, kQ4SmallBN)) != cudaSuccess) return e;
-  return make(eb.map_hl_s, eb.hl, d.inter, kQ4SmallBN);
+  if ((e = make(eb.map_xh_s, eb.xh, d.hidden, kQ4SmallBox)) != cudaSuccess) return e;
+  if ((e = make(eb.map_xl_s, eb.xl, d.hidden, kQ4SmallBox)) != cudaSuccess) return e;
+  if ((e = make(eb.map_hh_s, eb.hh, d.inter, kQ4SmallBox)) != cudaSuccess) return e;
+  return make(eb.map_hl_s, eb.hl, d.inter, kQ4SmallBox);
 }
 
 namespace {
