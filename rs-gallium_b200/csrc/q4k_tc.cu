@@ -1047,12 +1047,12 @@ bool use_q4k_small(const Moe& m, const Groups& g) {
   const gb_moe_desc& d = m.desc;
   if (m.expert_path == GB_PATH_TENSOR_CORES_F16) return false;
   if (q4tc::small_smem_bytes(std::max(d.hidden, d.inter)) > (size_t)227 * 1024) return false;
-  // up to 16 rows per expert on average: folding 32-column accumulators
-  // every super-block costs more than the f16 decode saves (measured at 32
-  // rows per expert: 430 vs 344 us per layer; at 2 and 4 rows 289 vs 326 and
-  // 314 vs 331 us)
+  // up to 24 rows per expert on average: beyond that, folding 32-column
+  // accumulators every super-block costs more than the f16 decode saves
+  // (LFM2.5 layer: 273 vs 333 us at 20 rows per expert, 292 vs 333 at 24,
+  // 365 vs 340 at 32)
   const int64_t nloc = std::max(1, m.e_end - m.e_begin);
-  return g.rows <= (int64_t)(q4tc::kSmallBN / 2) * nloc;
+  return g.rows <= (int64_t)(q4tc::kSmallBN * 3 / 4) * nloc;
 }
 
 cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x, ExpertBufs& eb,

@@ -94,7 +94,7 @@ def test_q4k_ragged_rows_are_refused():
 def test_lfm2_tensor_core_path_matches_oracle(layer, T, path):
     # Two kind::f16 kernels: "tensor_cores" runs the weights as the exact
     # integers sc * q with the super-block scales applied to the partial sums
-    # while the batch averages at most 16 rows per expert (T = 1, 8, 64 here)
+    # while the batch averages at most 24 rows per expert (T = 1, 8, 64 here)
     # and the f16 hi + lo decode above that (T = 300); "tensor_cores_f16"
     # forces the hi + lo decode.  AUTO takes the tensor cores from 8 rows per
     # expert.
