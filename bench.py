@@ -335,19 +335,32 @@ def cpu_cores(requested: int) -> int:
 # ---------------------------------------------------------------------------
 
 def cpu_reference_steps(layer, x, cores, warmup, steps):
-    """Mean seconds per whole-batch forward of oracle/cpu_reference.py."""
+    """Mean seconds per whole-batch forward of oracle/cpu_reference.py, and
+    the last forward's output (every row of the batch)."""
     from oracle.cpu_reference import CpuReference
     ref = CpuReference(layer, n_threads=cores)
     try:
         times = []
         for i in range(warmup + steps):
             t0 = time.perf_counter()
-            ref.forward(x)
+            y = ref.forward(x)
             if i >= warmup:
                 times.append(time.perf_counter() - t0)
     finally:
         ref.close()
-    return statistics.mean(times)
+    return statistics.mean(times), y
+
+
+def rows_parity(got, want):
+    """Every row of a forward against the CPU forward's rows, on the bar."""
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    finite = bool(np.all(np.isfinite(got)))
+    err = np.abs(got - want)
+    max_abs = float(err.max()) if finite else float("inf")
+    mean_rel = float(err.sum() / max(np.abs(want).sum(), 1e-30)) if finite else float("inf")
+    return {"rows": int(got.shape[0]), "max_abs": max_abs, "mean_rel": mean_rel,
+            "pass": bool(max_abs <= MAX_ABS and mean_rel <= MEAN_REL)}
 
 
 def run_reference(args, world, rank):
@@ -359,7 +372,7 @@ def run_reference(args, world, rank):
     T = args.tokens
     x = synth.tokens(T, model.H, seed=args.seed)
     cores = cpu_cores(args.cpu_threads)
-    sec = cpu_reference_steps(layer, x, cores, args.warmup, args.steps)
+    sec, _ = cpu_reference_steps(layer, x, cores, args.warmup, args.steps)
     value = T / sec
     sample = (f"full batch every step: all {T} tokens routed and every active expert run "
               f"(grouped forward of gpt_oss_q.rs / lfm2moe_q.rs, OpenBLAS f32 GEMMs)")
@@ -513,6 +526,7 @@ class Arm:
         self.fwd(T)  # every rank: the expert-parallel forward is collective
         torch.cuda.synchronize()
         got_all = self.out[:T].cpu().numpy()
+        self.last_out = got_all
         self.moe.device_status(self.stream.cuda_stream)
         idx_gpu = self.moe.route(self.xd[:T])["idx"].cpu().numpy()
         x = self.x[:T]
@@ -735,6 +749,7 @@ def run_ours(args, world, rank, local):
 
     # ---- parity against the oracle (every rank, outside the timed region) ----
     parity = None if args.no_parity else arm.parity(T, args.parity_rows, threads)
+    got_rows = getattr(arm, "last_out", None)
     arm.close()
 
     # ---- the workload's other layers ----------------------------------------
@@ -763,10 +778,15 @@ def run_ours(args, world, rank, local):
     # ---- CPU baseline (rank 0, one GPU only) ---------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        sec = cpu_reference_steps(layer, arm.x[:T], cores, 1, 2)
+        sec, y_cpu = cpu_reference_steps(layer, arm.x[:T], cores, 1, 2)
         cpu = {"value": T / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": (f"full batch: all {T} tokens routed and every active expert run "
                           f"(oracle/cpu_reference.py), mean of 2 forwards after 1 warm-up")}
+        # the CPU forward's output covers the whole batch: check every row of
+        # the GPU forward against it, beside the oracle's sampled rows
+        if parity is not None and got_rows is not None:
+            parity["every_row_vs_cpu_forward"] = rows_parity(got_rows, y_cpu)
+            parity["pass"] = bool(parity["pass"] and parity["every_row_vs_cpu_forward"]["pass"])
 
     all_parity = ([parity] + [r.get("parity") for c in configs.values() for r in c["results"]] +
                   [c.get("parity") for c in configs.values()])

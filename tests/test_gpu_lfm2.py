@@ -79,6 +79,14 @@ def test_lfm2_full_size_sampled_rows_and_determinism(moe, layer):
     rows = np.random.default_rng(3).choice(T, 16, replace=False)
     want, _, _ = oracle.OracleLfm2(layer).forward(x[rows])
     _parity(a[rows], want, "T=2048 sampled rows")
+    # every row against the grouped CPU forward (oracle/cpu_reference.py,
+    # checked against the oracle by tests/test_cpu_reference.py)
+    from oracle.cpu_reference import CpuReference
+    ref = CpuReference(layer)
+    try:
+        _parity(a, ref.forward(x), "T=2048 every row")
+    finally:
+        ref.close()
 
 
 def test_q4k_ragged_rows_are_refused():

@@ -72,6 +72,18 @@ def _cuda(a):
     return _torch().from_numpy(np.ascontiguousarray(a)).cuda()
 
 
+def _cpu_grouped_forward(layer, x):
+    """Every row of a large batch on the CPU: the grouped forward of
+    oracle/cpu_reference.py (BLAS GEMMs), which tests/test_cpu_reference.py
+    checks against the oracle."""
+    from oracle.cpu_reference import CpuReference
+    ref = CpuReference(layer)
+    try:
+        return ref.forward(x)
+    finally:
+        ref.close()
+
+
 # ---- decoders ---------------------------------------------------------------
 
 @pytest.mark.parametrize("expert", [0, 17, 31])
@@ -321,7 +333,9 @@ def test_full_size_rows_do_not_depend_on_the_batch(moe32, big_run):
 
 def test_120b_shape_at_8192_tokens():
     """The headline workload's shape: routing and grouping bit-exact on every
-    token, sampled rows against the oracle, two forwards bit-identical."""
+    token, sampled rows against the oracle, every row against the grouped
+    CPU forward (oracle/cpu_reference.py, itself checked against the oracle),
+    two forwards bit-identical."""
     torch = _torch()
     T = 8192
     layer = synth.gptoss_layer(n_experts=128, seed=0)
@@ -343,6 +357,7 @@ def test_120b_shape_at_8192_tokens():
     rows = np.random.default_rng(1).choice(T, 24, replace=False)
     want, _, _ = oracle.OracleMoe(layer).forward(x[rows])
     assert_parity(out1[rows], want, "E=128 T=8192 sampled rows")
+    assert_parity(out1, _cpu_grouped_forward(layer, x), "E=128 T=8192 every row")
 
 
 def test_skewed_routing_at_4096_tokens(layer32_skew):
