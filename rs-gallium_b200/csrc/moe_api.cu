@@ -317,6 +317,8 @@ void release_moe(gb::Moe& m) {
   cudaFree(m.w.q4_gu);
   cudaFree(m.w.q4_dn);
   cudaFree(m.w.q4_gu_exp);
+  cudaFree(m.w.q4_gu_t);
+  cudaFree(m.w.q4_dn_t);
   for (void* p : {m.w.dense_gu, m.w.dense_down, m.w.sh_gu, m.w.sh_down,
                   (void*)m.w.expert_scale, (void*)m.w.router_in_scale,
                   (void*)m.w.expert_in_norm, (void*)m.w.out_norm})

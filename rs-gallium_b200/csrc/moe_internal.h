@@ -72,6 +72,10 @@ struct ExpertWeights {
   // tensor-core Q4_K path: per local expert, weights decode as w * 2^exp
   int32_t* q4_gu_exp = nullptr;  // [E_loc] (one allocation with q4_dn_exp)
   int32_t* q4_dn_exp = nullptr;  // [E_loc]
+  // the same bytes tile-interleaved for the tensor-core decoders (q4k_tc.cu
+  // q4tc::tile_q4k_kernel): [E_loc][128-row tile][super-block][18432 B]
+  uint8_t* q4_gu_t = nullptr;
+  uint8_t* q4_dn_t = nullptr;
   // Dense experts (GB_FMT_DENSE), values as stored (bf16 or f32), gate and
   // up rows interleaved: dense_gu [E_loc][2I][H] (row 2i = gate i, 2i + 1 =
   // up i), dense_down [E_loc][H][I]; the shared expert's sh_gu [2Is][H],

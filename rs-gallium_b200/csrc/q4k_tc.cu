@@ -52,7 +52,7 @@ constexpr size_t kSmemBytes = (size_t)STAGES * STAGE_BYTES + 1024 + 256;
 enum Mode { GATE_UP = 0, DOWN = 1 };
 
 struct Args {
-  const uint8_t* q;       // [E_loc][rows][K/256][144]
+  const uint8_t* q;       // tiled copy: [E_loc][m_tiles][K/256][128 * 144] (tiled_row)
   const int32_t* wexp;    // [E_loc] decode scale exponent e
   int K;
   int rows;               // 2I (gate/up interleaved) or H
@@ -114,6 +114,33 @@ __device__ __forceinline__ Item decode_item(const Args& a, int item) {
   it.row0 = a.tile_row0[j];
   it.nrows = a.tile_rows[j];
   return it;
+}
+
+// The decoders read a tile-interleaved copy of each Q4_K matrix, made once at
+// load (tile_q4k_kernel): per (local expert, 128-row tile, super-block) one
+// block of 128 * 144 bytes holding the 16-byte headers of the tile's rows
+// (row r at 16 r), then for each sub-block pair c its first and its second
+// 16 quant bytes of every row (at 2048 + 4096 c and 4096 + 4096 c, row r at
+// 16 r).  Decoder thread r loads row r, so each warp-wide 16-byte load reads
+// 512 consecutive bytes, where rows of the GGUF layout lie a whole row of
+// super-blocks apart (32 separate lines per warp load).  Rows past the
+// matrix in the last tile are zero.
+constexpr int kTileBlock = BM * 144;
+
+// Row r of an item's tile at super-block 0 in the tiled copy.
+__device__ __forceinline__ const uint8_t* tiled_row(const Args& a, const Item& it, int r,
+                                                    int nsb) {
+  return a.q + ((int64_t)it.le * a.m_tiles + it.m_tile) * nsb * kTileBlock + r * 16;
+}
+
+// K step kc's bytes of a row: the header of super-block kc / 4 and the 32
+// quant bytes of sub-block pair kc % 4.
+__device__ __forceinline__ void load_step(const uint8_t* tr, int kc, uint4& hdr, uint4& qa,
+                                          uint4& qb) {
+  const uint8_t* blk = tr + (int64_t)(kc >> 2) * kTileBlock;
+  hdr = __ldg(reinterpret_cast<const uint4*>(blk));
+  qa = __ldg(reinterpret_cast<const uint4*>(blk + 2048 + 4096 * (kc & 3)));
+  qb = __ldg(reinterpret_cast<const uint4*>(blk + 4096 + 4096 * (kc & 3)));
 }
 
 // Scale and min of sub-block j = 2c + h of a super-block (candle's
@@ -414,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // load still in flight.
     const int r = (threadIdx.x - 128) & 127;
     const int grp = (threadIdx.x - 128) >> 7;
-    const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
+    const int nsb = a.K >> 8;  // super-blocks per row
     const int nks = nk / 2;  // K steps per group (nk is a multiple of four)
     int stage = grp;         // global step index gs = grp (mod 2), stage = gs % STAGES
     uint32_t phase = 0;
@@ -423,15 +450,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item it = decode_item(a, item);
       const int row = it.m_tile * BM + r;
       const bool valid = row < a.rows;
-      const uint8_t* rowp = a.q + ((int64_t)it.le * a.rows + (valid ? row : 0)) * row_bytes;
+      const uint8_t* tr = tiled_row(a, it, r, nsb);
       const float scale = valid ? pow2f(a.wexp[it.le]) : 0.0f;
-      // bytes of K step kc: header of super-block kc / 4, quants of pair kc % 4
-      auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) {
-        const uint8_t* blk = rowp + (kc >> 2) * 144;
-        hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-        qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
-        qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
-      };
+      auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) { load_step(tr, kc, hdr, qa, qb); };
       uint4 hdr[4], qa[4], qb[4];
 #pragma unroll
       for (int u = 0; u < 3; ++u)
@@ -739,7 +760,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ahead of the MMAs.
     const int r = (threadIdx.x - 128) & 127;
     const int grp = (threadIdx.x - 128) >> 7;
-    const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
     const int nks = nk / 2;  // K steps per group (nk is a multiple of four)
     int stage = grp;         // global step index gs = grp (mod 2), stage = gs % 6
     uint32_t phase = 0;
@@ -748,13 +768,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item it = decode_item(a, item);
       const int row = it.m_tile * BM + r;
       const bool valid = row < a.rows;
-      const uint8_t* rowp = a.q + ((int64_t)it.le * a.rows + (valid ? row : 0)) * row_bytes;
-      auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) {
-        const uint8_t* blk = rowp + (kc >> 2) * 144;
-        hdr = __ldg(reinterpret_cast<const uint4*>(blk));
-        qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (kc & 3)));
-        qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (kc & 3)));
-      };
+      const uint8_t* tr = tiled_row(a, it, r, nsb);
+      auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) { load_step(tr, kc, hdr, qa, qb); };
       uint4 hdr[kSmallRing], qa[kSmallRing], qb[kSmallRing];
 #pragma unroll
       for (int u = 0; u < kSmallRing - 1; ++u)
@@ -799,7 +814,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue: thread = TMEM lane = weight row ---------------
     const int m = threadIdx.x;
     const int odd = m & 1;
-    const int64_t row_bytes = (int64_t)(a.K >> 8) * 144;
     int sbi = 0;
     bool ok = true;
     // every epilogue thread runs every item (the named barriers below need
@@ -819,14 +833,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = m; i < n4; i += 128) dst[i] = __ldg(src + i);
       }
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      const uint8_t* hp = a.q + ((int64_t)it.le * a.rows + (valid ? row : 0)) * row_bytes;
+      const uint8_t* hp = tiled_row(a, it, m, nsb);  // super-block headers, kTileBlock apart
       float y[kSmallBN];
 #pragma unroll
       for (int j = 0; j < kSmallBN; ++j) y[j] = 0.0f;
       uint4 hnext = __ldg(reinterpret_cast<const uint4*>(hp));
       for (int sb = 0; sb < nsb; ++sb, ++sbi) {
         const uint4 hdr = hnext;
-        if (sb + 1 < nsb) hnext = __ldg(reinterpret_cast<const uint4*>(hp + (sb + 1) * 144));
+        if (sb + 1 < nsb)
+          hnext = __ldg(reinterpret_cast<const uint4*>(hp + (int64_t)(sb + 1) * kTileBlock));
         const int b = sbi & 1;
         if (ok && !mbar_wait(&acc_full[b], (sbi >> 1) & 1, abort_flag, a.err)) ok = false;
         if (!ok) continue;
@@ -920,6 +935,25 @@ __global__ void wexp_kernel(const uint8_t* __restrict__ q, int64_t blocks_per_ex
   }
 }
 
+// The tiled copy of one Q4_K matrix set ([n_exp][rows][nsb][144] in, layout
+// at tiled_row out; the output is cleared beforehand for the padding rows):
+// one thread per (expert, row, super-block) moves its nine 16-byte pieces.
+__global__ void tile_q4k_kernel(const uint8_t* __restrict__ src, int rows, int nsb, int m_tiles,
+                                int64_t n, uint8_t* __restrict__ dst) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  const int64_t er = t / nsb;  // expert * rows + row
+  const int sb = (int)(t - er * nsb);
+  const int64_t le = er / rows;
+  const int row = (int)(er - le * rows);
+  const uint4* s = reinterpret_cast<const uint4*>(src + t * 144);
+  uint8_t* blk = dst + ((le * m_tiles + row / BM) * nsb + sb) * kTileBlock + (row % BM) * 16;
+  *reinterpret_cast<uint4*>(blk) = __ldg(s);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)  // quant bytes 16 j .. 16 j + 15: pair j / 2, half j % 2
+    *reinterpret_cast<uint4*>(blk + 2048 + 2048 * j) = __ldg(s + 1 + j);
+}
+
 // Sub-block sums of the split rows: out[p][s] = sum over i < 32 of
 // (hi + lo)[p][32 s + i], in order, in f32 (hi + lo is exact in f32).
 __global__ void sub_sums_kernel(const __half* __restrict__ hi, const __half* __restrict__ lo,
@@ -955,8 +989,25 @@ static_assert(kSmallStages % 2 == 0, "each decoder group keeps to its own stages
 bool q4k_tc_supported(const Moe& m) {
   const gb_moe_desc& d = m.desc;
   return d.weight_format == GB_FMT_Q4_K && d.hidden % 256 == 0 && d.inter % 256 == 0 &&
-         m.w.q4_gu_exp != nullptr;
+         m.w.q4_gu_exp != nullptr && m.w.q4_gu_t != nullptr && m.w.q4_dn_t != nullptr;
 }
+
+namespace {
+
+// The tiled copy of one matrix set (q4tc::tile_q4k_kernel).
+cudaError_t make_tiled(const uint8_t* src, int nloc, int rows, int K, uint8_t** out) {
+  const int nsb = K / 256;
+  const int m_tiles = (rows + q4tc::BM - 1) / q4tc::BM;
+  const size_t bytes = (size_t)nloc * m_tiles * nsb * q4tc::kTileBlock;
+  cudaError_t e = cudaMalloc(out, bytes);
+  if (e != cudaSuccess) return e;
+  if ((e = cudaMemset(*out, 0, bytes)) != cudaSuccess) return e;
+  const int64_t n = (int64_t)nloc * rows * nsb;
+  q4tc::tile_q4k_kernel<<<(unsigned)((n + 255) / 256), 256>>>(src, rows, nsb, m_tiles, n, *out);
+  return cudaGetLastError();
+}
+
+}  // namespace
 
 cudaError_t q4k_tc_prepare(Moe& m) {
   const gb_moe_desc& d = m.desc;
@@ -970,6 +1021,12 @@ cudaError_t q4k_tc_prepare(Moe& m) {
   q4tc::wexp_kernel<<<nloc, 256>>>(m.w.q4_dn, (int64_t)d.hidden * (d.inter / 256),
                                    m.w.q4_dn_exp);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  if (d.hidden % 256 == 0 && d.inter % 256 == 0) {
+    if ((e = make_tiled(m.w.q4_gu, nloc, 2 * d.inter, d.hidden, &m.w.q4_gu_t)) != cudaSuccess)
+      return e;
+    if ((e = make_tiled(m.w.q4_dn, nloc, d.hidden, d.inter, &m.w.q4_dn_t)) != cudaSuccess)
+      return e;
+  }
   return cudaDeviceSynchronize();
 }
 
@@ -1064,7 +1121,7 @@ cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x,
     return e;
   if ((e = launch_split_gather(m, g, x, eb, st)) != cudaSuccess) return e;
   q4tc::Args a = q4tc_args(m, g, eb);
-  a.q = m.w.q4_gu;
+  a.q = m.w.q4_gu_t;
   a.wexp = m.w.q4_gu_exp;
   a.K = d.hidden;
   a.rows = 2 * d.inter;
@@ -1085,7 +1142,7 @@ cudaError_t launch_q4k_tc_gate_up(const Moe& m, const Groups& g, const float* x,
 cudaError_t launch_q4k_tc_down(const Moe& m, const Groups& g, ExpertBufs& eb, cudaStream_t st) {
   const gb_moe_desc& d = m.desc;
   q4tc::Args a = q4tc_args(m, g, eb);
-  a.q = m.w.q4_dn;
+  a.q = m.w.q4_dn_t;
   a.wexp = m.w.q4_dn_exp;
   a.K = d.inter;
   a.rows = d.hidden;
