@@ -821,9 +821,11 @@ int forward_dispatch(gb::Moe& m, const float* x, int64_t T, float* out, cudaStre
 
 namespace gb {
 
-// Q4_K experts: the tensor-core kernel for groups averaging at least 8 rows
+// Q4_K experts: the tensor-core kernels for groups averaging at least 2 rows
 // per local expert (or when the tensor cores are forced); the CUDA-core
-// kernel streams smaller groups faster.
+// kernel streams smaller groups faster (LFM2.5 layer, 32 experts: 16 tokens
+// 192 us on the tensor cores against 221 on the CUDA cores, 24 tokens 209
+// against 287; the two about even near 1.5 rows per expert).
 // Dense bf16 experts: the tensor cores from one grouped position per two
 // local experts (measured on 128 experts x 2048 x 768, top-8: T = 8 took
 // 178 us on the tensor cores against 249 on the CUDA cores, T = 4 142
@@ -850,7 +852,7 @@ bool use_q4k_tc(const Moe& m, const Groups& g, const ExpertBufs& eb) {
   if (m.expert_path == GB_PATH_TENSOR_CORES || m.expert_path == GB_PATH_TENSOR_CORES_F16)
     return true;
   const int64_t nloc = std::max(1, m.e_end - m.e_begin);
-  return g.rows >= 8 * nloc;
+  return g.rows >= 2 * nloc;
 }
 
 cudaError_t set_smem_limit_fn(const void* kern, size_t bytes) {

@@ -1,5 +1,5 @@
 // q4k_tc.cu -- grouped Q4_K expert GEMMs on the tensor cores (LFM2.5 batches
-// of at least 8 rows per expert).
+// of at least 2 rows per expert).
 //
 // Reference math: lfm2moe_q.rs:279-296 (h = silu(x Wg^T) * (x Wu^T), y =
 // h Wd^T, no biases) over candle's Q4_K dequantiser (quantized.rs:162-177):

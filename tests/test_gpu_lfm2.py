@@ -61,7 +61,9 @@ def test_sigmoid_routing_is_bit_exact(moe, layer, T):
     assert np.array_equal(r["w"].cpu().numpy(), w)
 
 
-@pytest.mark.parametrize("T", [1, 8, 64])
+# AUTO kernel choice at 32 experts: CUDA cores below 2 rows per expert
+# (T = 1, 8), the small-batch tensor-core kernel from there (T = 16, 24, 64)
+@pytest.mark.parametrize("T", [1, 8, 16, 24, 64])
 def test_lfm2_forward_matches_oracle(moe, layer, T):
     x = synth.tokens(T, 2048, seed=900 + T)
     got = moe.forward(_cuda(x)).cpu().numpy()
@@ -104,7 +106,7 @@ def test_lfm2_tensor_core_path_matches_oracle(layer, T, path):
     # integers sc * q with the super-block scales applied to the partial sums
     # while the batch averages at most 24 rows per expert (T = 1, 8, 64 here)
     # and the f16 hi + lo decode above that (T = 300); "tensor_cores_f16"
-    # forces the hi + lo decode.  AUTO takes the tensor cores from 8 rows per
+    # forces the hi + lo decode.  AUTO takes the tensor cores from 2 rows per
     # expert.
     m = Lfm2QMoEFFN.load(layer, device=0, max_tokens=T)
     try:
