@@ -588,19 +588,23 @@ __device__ __forceinline__ void decode_int_half(const uint4& hdr, const uint4& q
   }
 }
 
-// Sixteen columns of one super-block folded into y: y[j] += d A[j] -
-// dmin sum_s m_s S[j][s], A = hi + lo read from TMEM, S from shared memory.
-template <int J0>
+// Columns J0 .. J0 + NJ - 1 of one super-block folded into y: y[j] += d A[j]
+// - dmin sum_s m_s S[j][s], A = hi + lo read from TMEM, S from shared memory.
+// NJ is fixed at compile time and every column is folded: columns past the
+// tile's positions compute values nobody stores (their S entries are stale
+// shared memory), which costs less than a test per column.
+template <int J0, int NJ>
 __device__ __forceinline__ void fold16(uint32_t hi_addr, uint32_t lo_addr, float d, float dmin,
                                        const float (&mf)[8], const float* xs, int nsub, int sb,
-                                       int ncols, float (&y)[kSmallBN]) {
+                                       float (&y)[kSmallBN]) {
+  static_assert(NJ == 8 || NJ == 16, "8 or 16 columns per fold");
   uint32_t vh[16], vl[16];
   tmem_ld16(hi_addr + (uint32_t)J0, vh);
   tmem_ld16(lo_addr + (uint32_t)J0, vl);
   tmem_wait_ld();
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    if (J0 + j < ncols) {
+  for (int j = 0; j < NJ; ++j) {
+    {
       const float4* sp = reinterpret_cast<const float4*>(xs + (J0 + j) * nsub + sb * 8);
       const float4 s0 = sp[0], s1 = sp[1];
       float t = mf[0] * s0.x;
@@ -766,8 +770,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int item = blockIdx.x; item < total_items && ok; item += gridDim.x) {
       const Item it = decode_item(a, item);
-      const int row = it.m_tile * BM + r;
-      const bool valid = row < a.rows;
       const uint8_t* tr = tiled_row(a, it, r, nsb);
       auto load = [&](int kc, uint4& hdr, uint4& qa, uint4& qb) { load_step(tr, kc, hdr, qa, qb); };
       uint4 hdr[kSmallRing], qa[kSmallRing], qb[kSmallRing];
@@ -794,10 +796,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t v[16];
               decode_int_half(hdr[u], qa[u], qb[u], kc & 3, h, v);
 #pragma unroll
+              // rows past the matrix are zero bytes in the tiled copy, so
+              // they decode to zero (sc = 0) without a select here
               for (int cc = 0; cc < 4; ++cc)
                 *reinterpret_cast<uint4*>(sa + (((4 * h + cc) ^ (r & 7)) << 4)) =
-                    valid ? make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3])
-                          : make_uint4(0u, 0u, 0u, 0u);
+                    make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
             }
             fence_proxy_async_smem();
             mbar_arrive(&a_full[stage]);
@@ -853,8 +856,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t hi_addr =
             tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(b * 2 * kSmallBN);
         const uint32_t lo_addr = hi_addr + (uint32_t)small_nh(it.nrows);
-        fold16<0>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, ncols, y);
-        if (ncols > 16) fold16<16>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, ncols, y);
+        if (ncols <= 8) {
+          fold16<0, 8>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, y);
+        } else {
+          fold16<0, 16>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, y);
+          if (ncols > 16) fold16<16, 16>(hi_addr, lo_addr, d, dmin, mf, xs, nsub, sb, y);
+        }
         tc_fence_before();
         mbar_arrive(&acc_empty[b]);
       }
