@@ -189,7 +189,9 @@ typedef struct gb_moe gb_moe;
 typedef struct gb_moe_info {
   uint32_t struct_size;
   int32_t local_expert_begin, local_expert_end;
-  int64_t weight_bytes;    /* device bytes of the repacked expert weights  */
+  int64_t weight_bytes;    /* device bytes of the expert weights in every
+                              layout the kernels read (row layout, plus the
+                              block-scaled MXFP4 or tiled Q4_K copy)        */
   int64_t workspace_bytes; /* device bytes of the current workspace        */
   int32_t workspace_tokens;
   int32_t sm_count;

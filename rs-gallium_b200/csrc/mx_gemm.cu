@@ -1041,6 +1041,7 @@ cudaError_t mx_prepare_weights(Moe& m) {
   if ((e = cudaMalloc(&x.dn_nib, (size_t)dn_units * 16)) != cudaSuccess) return e;
   if ((e = cudaMalloc(&x.gu_sfa, gu_sf)) != cudaSuccess) return e;
   if ((e = cudaMalloc(&x.dn_sfa, dn_sf)) != cudaSuccess) return e;
+  m.weight_bytes += (gu_units + dn_units) * 16 + (int64_t)(gu_sf + dn_sf);
   const int split_zero = d.weight_format == GB_FMT_MXFP4_SPLIT ? 1 : 0;
   const int nbh = H / 32, nbi = I / 32;
   mx::pack_nibbles_kernel<<<(unsigned)((gu_units + 255) / 256), 256>>>(

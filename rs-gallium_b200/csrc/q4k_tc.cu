@@ -1001,13 +1001,15 @@ bool q4k_tc_supported(const Moe& m) {
 
 namespace {
 
-// The tiled copy of one matrix set (q4tc::tile_q4k_kernel).
-cudaError_t make_tiled(const uint8_t* src, int nloc, int rows, int K, uint8_t** out) {
+// The tiled copy of one matrix set (q4tc::tile_q4k_kernel), counted in the
+// handle's weight bytes.
+cudaError_t make_tiled(Moe& m, const uint8_t* src, int nloc, int rows, int K, uint8_t** out) {
   const int nsb = K / 256;
   const int m_tiles = (rows + q4tc::BM - 1) / q4tc::BM;
   const size_t bytes = (size_t)nloc * m_tiles * nsb * q4tc::kTileBlock;
   cudaError_t e = cudaMalloc(out, bytes);
   if (e != cudaSuccess) return e;
+  m.weight_bytes += (int64_t)bytes;
   if ((e = cudaMemset(*out, 0, bytes)) != cudaSuccess) return e;
   const int64_t n = (int64_t)nloc * rows * nsb;
   q4tc::tile_q4k_kernel<<<(unsigned)((n + 255) / 256), 256>>>(src, rows, nsb, m_tiles, n, *out);
@@ -1029,9 +1031,9 @@ cudaError_t q4k_tc_prepare(Moe& m) {
                                    m.w.q4_dn_exp);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   if (d.hidden % 256 == 0 && d.inter % 256 == 0) {
-    if ((e = make_tiled(m.w.q4_gu, nloc, 2 * d.inter, d.hidden, &m.w.q4_gu_t)) != cudaSuccess)
+    if ((e = make_tiled(m, m.w.q4_gu, nloc, 2 * d.inter, d.hidden, &m.w.q4_gu_t)) != cudaSuccess)
       return e;
-    if ((e = make_tiled(m.w.q4_dn, nloc, d.hidden, d.inter, &m.w.q4_dn_t)) != cudaSuccess)
+    if ((e = make_tiled(m, m.w.q4_dn, nloc, d.hidden, d.inter, &m.w.q4_dn_t)) != cudaSuccess)
       return e;
   }
   return cudaDeviceSynchronize();
