@@ -18,6 +18,13 @@ skewed routing still uses every core.  The matrix products run in OpenBLAS's
 f32 GEMM through numpy (one BLAS thread per task), standing in for candle's
 CPU matmul (the `gemm` crate, a blocked f32 GEMM of the same kind);
 dequantisation, activation and top-k run in the oracle's C code.
+
+gallium-core's generic MoEFFN (crates/gallium-core/src/ffn.rs:125-166: dense
+gated experts, softmax top-k renormalised, an optional shared expert over
+all tokens added after the routed sum) takes the same grouped form here.
+The reference itself runs that block token by token (ffn.rs:139-157), so
+this restatement times faster than the reference would: a conservative
+baseline.
 """
 from __future__ import annotations
 
@@ -29,7 +36,8 @@ from concurrent.futures import ThreadPoolExecutor
 
 import numpy as np
 
-from . import OracleLfm2, OracleMoe, _p, lib, permute, route_sigmoid_topk, route_softmax_topk
+from . import (OracleDense, OracleLfm2, OracleMoe, OrDesc, _p, lib, permute, route_sigmoid_topk,
+               route_softmax_topk)
 
 CHUNK_ROWS = 512
 
@@ -43,20 +51,29 @@ def host_threads() -> int:
 
 class CpuReference:
     """Runs the grouped CPU forward of one layer (GPT-OSS MXFP4 in the
-    safetensors layout, or LFM2.5 Q4_K) on `n_threads` host threads."""
+    safetensors layout, LFM2.5 Q4_K, or the generic MoEFFN with dense
+    experts) on `n_threads` host threads."""
 
     def __init__(self, layer, n_threads: int = 0):
         self.lfm2 = hasattr(layer, "sel_bias")
-        self.orc = OracleLfm2(layer) if self.lfm2 else OracleMoe(layer)
+        self.dense = hasattr(layer, "shared_inter")
+        self.orc = (OracleLfm2(layer) if self.lfm2 else
+                    OracleDense(layer) if self.dense else OracleMoe(layer))
         self.layer = layer
         self.n_threads = n_threads if n_threads > 0 else host_threads()
         d = self.orc.desc
         self.H, self.I, self.E, self.k = d.hidden, d.inter, d.n_experts, d.top_k
         keep = self.orc._keep
-        self.rw = np.ascontiguousarray(keep["router_w"] if self.lfm2 else keep["rw"], np.float32)
-        self.rb = None if self.lfm2 else keep["rb"]
-        self.gub = None if self.lfm2 else keep.get("gub")
-        self.dnb = None if self.lfm2 else keep.get("db")
+        plain = self.lfm2 or self.dense  # no router or expert biases
+        self.rw = np.ascontiguousarray(keep["router_w"] if plain else keep["rw"], np.float32)
+        self.rb = None if plain else keep["rb"]
+        self.gub = None if plain else keep.get("gub")
+        self.dnb = None if plain else keep.get("db")
+        self.Is = layer.shared_inter if self.dense else 0
+        if self.Is:
+            # the shared expert's activation: the experts' kind, its own width
+            self.sh_desc = OrDesc.from_buffer_copy(d)
+            self.sh_desc.inter = self.Is
         self.sel_bias = layer.sel_bias if self.lfm2 else None
         self._tls = threading.local()
         self._pool = ThreadPoolExecutor(self.n_threads)
@@ -86,7 +103,13 @@ class CpuReference:
         xe = x[ent // k]
         h = np.empty((xe.shape[0], I), np.float32)
         desc = ctypes.byref(self.orc.desc)
-        if self.lfm2:
+        if self.dense:
+            kp = self.orc._keep
+            g = xe @ kp["gate"][e].T
+            u = xe @ kp["up"][e].T
+            lib().or_act_rows(desc, _p(g), _p(u), g.shape[0], I, _p(h), 1)
+            wd = kp["down"][e]
+        elif self.lfm2:
             wg, wu, wd = self._buffers()
             self._dequant(0, e, wg)
             self._dequant(1, e, wu)
@@ -108,6 +131,14 @@ class CpuReference:
             ye += self.dnb[e]
         ye *= wflat[ent][:, None]
         y[a:b] = ye
+
+    def _shared_task(self, a, b, x, sh):
+        kp = self.orc._keep
+        g = x[a:b] @ kp["sh_gate"].T
+        u = x[a:b] @ kp["sh_up"].T
+        h = np.empty((b - a, self.Is), np.float32)
+        lib().or_act_rows(ctypes.byref(self.sh_desc), _p(g), _p(u), b - a, self.Is, _p(h), 1)
+        sh[a:b] = h @ kp["sh_down"].T
 
     def forward(self, x: np.ndarray, timings: dict | None = None) -> np.ndarray:
         """x [T, H] f32 -> out [T, H] f32.  `timings` (optional) receives the
@@ -134,9 +165,13 @@ class CpuReference:
             a, b = int(offsets[e]), int(offsets[e + 1])
             for c in range(a, b, CHUNK_ROWS):
                 tasks.append((int(e), c, min(b, c + CHUNK_ROWS)))
+        sh = np.empty((T, H), np.float32) if self.Is else None
         with threadpool_limits(1, user_api="blas"):
             futs = [self._pool.submit(self._task, e, a, b, x, perm, wflat, y)
                     for e, a, b in tasks]
+            if sh is not None:  # the shared expert over every token
+                futs += [self._pool.submit(self._shared_task, c, min(T, c + CHUNK_ROWS), x, sh)
+                         for c in range(0, T, CHUNK_ROWS)]
             for f in futs:
                 f.result()
         t2 = time.perf_counter()
@@ -148,6 +183,8 @@ class CpuReference:
         out = y[rows[:, 0]].copy()
         for r in range(1, k):
             out += y[rows[:, r]]
+        if sh is not None:  # after the routed sum (ffn.rs:160-163)
+            out += sh
         t3 = time.perf_counter()
         if timings is not None:
             timings.update(route=t1 - t0, experts=t2 - t1, combine=t3 - t2,

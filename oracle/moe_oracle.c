@@ -705,8 +705,7 @@ void or_act_rows(const or_moe_desc* d, const float* gate, const float* up, int64
     for (int64_t i = 0; i < I; ++i) {
       const float g = gate[t * stride + i * (stride == 2 * I ? 2 : 1)];
       const float u = up[t * stride + i * (stride == 2 * I ? 2 : 1)];
-      h[t * I + i] = d->act_kind == OR_ACT_GPTOSS_CLAMP ? act_gptoss(g, u, d->swiglu_limit)
-                                                         : act_silu(g, u);
+      h[t * I + i] = act_apply(d, g, u);
     }
 }
 

@@ -169,7 +169,9 @@ int or_dequant_expert_matrix(const or_moe_desc* d, int which, int64_t expert, fl
 /* The expert activation over n rows: h[t, i] = act(gate[t*stride + i*s],
  * up[t*stride + i*s]) with s = 2 when stride == 2I (the interleaved gate_up
  * product of MXFP4_SPLIT, gate and up pointing at its columns 0 and 1), else
- * s = 1 (separate gate and up products, stride I).  h is [n, I]. */
+ * s = 1 (separate gate and up products, stride I).  h is [n, I].  act is the
+ * descriptor's activation as the experts apply it (clamped SwiGLU, SiLU, or
+ * gallium-core's gated kinds with their clamp). */
 void or_act_rows(const or_moe_desc* d, const float* gate, const float* up, int64_t n,
                  int64_t stride, float* h, int n_threads);
 

@@ -44,3 +44,21 @@ def test_lfm2_grouped_forward_matches_oracle():
         ref.close()
     want, _, _ = oracle.OracleLfm2(layer).forward(x)
     _check(got, want)
+
+
+@pytest.mark.parametrize("act_kind, clamp, shared", [(1, 0.0, 128), (3, 6.0, 128), (4, 0.0, 0)])
+def test_dense_moeffn_grouped_forward_matches_oracle(act_kind, clamp, shared, monkeypatch):
+    # gallium-core's generic MoEFFN: dense experts, SiLU / GELU-tanh with a
+    # clamp / ReLU, with and without the shared expert; small chunks so that
+    # experts and the shared expert are split across tasks
+    monkeypatch.setattr(cpu_reference, "CHUNK_ROWS", 16)
+    layer = synth.dense_layer(n_experts=8, hidden=256, inter=192, top_k=2,
+                              shared_inter=shared, act_kind=act_kind, act_clamp=clamp, seed=5)
+    x = synth.tokens(70, 256, seed=6)
+    ref = cpu_reference.CpuReference(layer, n_threads=3)
+    try:
+        got = ref.forward(x)
+    finally:
+        ref.close()
+    want, _, _ = oracle.OracleDense(layer).forward(x)
+    _check(got, want)
