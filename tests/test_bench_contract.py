@@ -27,7 +27,7 @@ def _reference_line(*args):
     return json.loads(lines[0])
 
 
-@pytest.mark.parametrize("model", ["gptoss", "lfm2"])
+@pytest.mark.parametrize("model", ["gptoss", "lfm2", "dense"])
 def test_reference_arm_prints_one_contract_line(model):
     d = _reference_line("--model", model, "--tokens", "64", "--experts", "8", "--steps", "1",
                         "--warmup", "1")
