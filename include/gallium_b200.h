@@ -257,8 +257,14 @@ int gb_moe_device_status(gb_moe* m, void* stream);
  * TENSOR_CORES_F16 the kind::f16 GEMM that decodes the weights to f16 in
  * shared memory (activations as f16 hi + lo, 128-position tiles).  The
  * tensor-core kernels need the GPT-OSS activation and H, I multiples of 64;
- * without them every path uses the CUDA cores.  Q4_K experts always run on
- * the CUDA cores.  No counterpart in the reference, which has one CPU path. */
+ * without them every path uses the CUDA cores.  Q4_K experts: AUTO runs the
+ * CUDA cores below 2 grouped rows per local expert on average and kind::f16
+ * tcgen05 from there (weights as the exact integers sc * q up to 24 rows per
+ * expert, as f16 hi + lo above); TENSOR_CORES takes the tensor cores at any
+ * size, TENSOR_CORES_F16 the hi + lo kernel.  Dense bf16 experts: AUTO runs
+ * kind::f16 tcgen05 from one grouped row per two local experts, the CUDA
+ * cores below that and for f32 weights.  No counterpart in the reference,
+ * which has one CPU path. */
 typedef enum {
   GB_PATH_AUTO = 0,
   GB_PATH_CUDA_CORES = 1,
