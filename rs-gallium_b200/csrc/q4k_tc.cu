@@ -795,9 +795,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int h = 0; h < 2; ++h) {  // sub-block 2c + h: chunks 4h .. 4h + 3 of the row
               uint32_t v[16];
               decode_int_half(hdr[u], qa[u], qb[u], kc & 3, h, v);
-#pragma unroll
               // rows past the matrix are zero bytes in the tiled copy, so
               // they decode to zero (sc = 0) without a select here
+#pragma unroll
               for (int cc = 0; cc < 4; ++cc)
                 *reinterpret_cast<uint4*>(sa + (((4 * h + cc) ^ (r & 7)) << 4)) =
                     make_uint4(v[4 * cc], v[4 * cc + 1], v[4 * cc + 2], v[4 * cc + 3]);
