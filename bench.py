@@ -15,7 +15,7 @@ The same line carries, under "configs", the workload's other layers:
                              4096 tokens, one GPU only;
   lfm2_q4k                   the LFM2.5-shaped block (hidden 2048, 1792
                              intermediate, 32 experts, top-4, Q4_K experts,
-                             sigmoid router) at 1, 64 and 2048 tokens per GPU,
+                             sigmoid router) at 1, 16, 64 and 2048 tokens per GPU,
                              expert parallel over the N GPUs when N > 1;
   moeffn_dense               gallium-core's generic MoEFFN with dense bf16
                              experts (a Qwen3-MoE-like shape: hidden 2048,
@@ -42,8 +42,10 @@ Arms:
 Parity: after timing, every rank checks its own forward against the oracle:
 expert indices of every token bit for bit, and the output rows of a sample
 (rows of the busiest expert plus random rows) within max-abs 2e-2 and
-mean-rel 1e-3.  The line's "parity" object has the worst rank's figures; a
-failed check prints the line and exits with status 3.
+mean-rel 1e-3.  On one GPU the headline batch is also checked row by row
+against the CPU baseline's own output of the same batch
+("every_row_vs_cpu_forward").  The line's "parity" object has the worst
+rank's figures; a failed check prints the line and exits with status 3.
 
 --model lfm2 / dense measures the LFM2.5-shaped or the generic dense layer as
 the headline instead.
@@ -767,7 +769,7 @@ def run_ours(args, world, rank, local):
                                                world, [4096], args, flush, peaks, threads)
         if on("lfm2_q4k"):
             configs["lfm2_q4k"] = run_config(Model("lfm2", 32), args.seed, local, rank, world,
-                                             [1, 64, 2048], args, flush, peaks, threads)
+                                             [1, 16, 64, 2048], args, flush, peaks, threads)
         if on("moeffn_dense"):
             configs["moeffn_dense"] = run_config(Model("dense", 128), args.seed, local, rank,
                                                  world, [1, 64, 2048], args, flush, peaks,
