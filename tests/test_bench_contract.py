@@ -11,6 +11,7 @@ import os
 import subprocess
 import sys
 
+import numpy as np
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -45,3 +46,19 @@ def test_reference_arm_prints_one_contract_line(model):
     cb = d["cpu_baseline"]
     assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference")
     assert cb["cores"] >= 1 and cb["sample"].startswith("full batch")
+
+
+def test_every_row_parity_helper():
+    # bench.rows_parity judges the GPU forward's rows against the CPU
+    # forward's on the path's bar; a non-finite row fails it
+    sys.path.insert(0, ROOT)
+    import bench
+    want = np.linspace(-3.0, 3.0, 40, dtype=np.float32).reshape(4, 10)
+    ok = bench.rows_parity(want + 1e-3, want)
+    assert ok["pass"] and ok["rows"] == 4 and abs(ok["max_abs"] - 1e-3) < 1e-6
+    bad = bench.rows_parity(want + 0.05, want)
+    assert not bad["pass"] and bad["max_abs"] > bench.MAX_ABS
+    nan = want.copy()
+    nan[2, 3] = np.nan
+    r = bench.rows_parity(nan, want)
+    assert not r["pass"] and r["max_abs"] == float("inf")
